@@ -1,0 +1,158 @@
+/*
+ * qma_cuda.h -- C ABI of the B200 (sm_100a) engine for qma's qwen35moe
+ * model-engine hot path.
+ *
+ * Plain C: pointers, sizes and int status codes; no CUDA or C++ types in any
+ * signature (a CUDA stream is passed as void*, NULL = the legacy default
+ * stream).  Every entry point returns QMA_CUDA_OK (0) or a negative
+ * qma_cuda_status; qma_cuda_last_error() describes the last failure on the
+ * calling thread.  Nothing here ever calls exit().
+ *
+ * Pointer conventions: arguments documented "device" are CUDA device
+ * pointers; "host" are ordinary host pointers.  Weight type ids are GGML's
+ * (qma.h:67-69): 12 = Q4_K, 14 = Q6_K, plus 8 = Q8_0.
+ *
+ * Each entry point names the reference interface it replaces (qma sources,
+ * file:line).
+ */
+#ifndef QMA_CUDA_H
+#define QMA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMA_CUDA_ABI_VERSION 1
+
+typedef enum {
+    QMA_CUDA_OK = 0,
+    QMA_CUDA_ERR_INVALID = -1,     /* bad argument (null pointer, size, type) */
+    QMA_CUDA_ERR_NOMEM = -2,       /* device or host allocation failed        */
+    QMA_CUDA_ERR_CUDA = -3,        /* a CUDA runtime call failed              */
+    QMA_CUDA_ERR_UNSUPPORTED = -4, /* shape or type the engine does not handle */
+    QMA_CUDA_ERR_STATE = -5,       /* call out of order (e.g. no weights)     */
+    QMA_CUDA_ERR_TIMEOUT = -6      /* a bounded device-side wait gave up      */
+} qma_cuda_status;
+
+#define QMA_TYPE_F32  0
+#define QMA_TYPE_Q8_0 8
+#define QMA_TYPE_Q4_K 12
+#define QMA_TYPE_Q6_K 14
+
+/* ---- library ---------------------------------------------------------- */
+int         qma_cuda_abi_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char *qma_cuda_last_error(void);
+/* Select the CUDA device for this thread and check it is sm_100. */
+int         qma_cuda_init(int device);
+
+/* ---- Q8_K activation quantization --------------------------------------
+ * Replaces qma_q8k_quant (qma.h:359, q8k.c:280; kernel quantize_row_q8k,
+ * q8k.c:34-85).  x: device float [rows][n], n a multiple of 256.  Outputs
+ * (device): xq int8 [rows][n], xd float [rows][n/256], xsum int16
+ * [rows][n/16].  Bit-identical to the reference. */
+int qma_cuda_q8k_quant(const float *x, int rows, int n, int8_t *xq, float *xd,
+                       int16_t *xsum, void *stream);
+
+/* ---- weight layout ------------------------------------------------------
+ * The engine keeps Q4_K weights in GGUF block order (144 B blocks are
+ * 16-byte aligned).  Q6_K (210 B blocks) and Q8_0 (34 B blocks) are not
+ * 16-byte aligned, so they are repacked once, at load time, into planes per
+ * matrix: Q6_K -> [ql rows*n/2][qh rows*n/4][scales rows*n/16][d rows*n/256
+ * fp16]; Q8_0 -> [q rows*n][d rows*n/32 fp16].  Byte-for-byte the same
+ * values; only their order changes (the reference's own load-time repack is
+ * qma_align_model, gguf.c:674).  qma_cuda_packed_bytes() gives the size of a
+ * packed matrix (equal to the GGUF size, rounded up to 16 per plane). */
+size_t qma_cuda_packed_bytes(int wtype, int rows, int n);
+/* src: device GGUF-layout matrix [rows][n]; dst: device packed buffer of
+ * qma_cuda_packed_bytes() bytes (for Q4_K a plain copy). */
+int qma_cuda_repack(int wtype, const void *src, int rows, int n, void *dst,
+                    void *stream);
+
+/* ---- super-block GEMV / small-batch GEMM --------------------------------
+ * Replaces matmul / mm_worker (nn.c:261-345) and the row dot dispatch
+ * qma_q8k_dot (qma.h:360, q8k.c:305-316) for Q4_K (dot_q4_K_q8k,
+ * q8k.c:89-131), Q6_K (dot_q6_K_q8k, q8k.c:210-262) and Q8_0 (no reference
+ * kernel; the reference rejects Q8_0 weights, gguf.c:272-287).
+ *   out[t][r] = <dequant(W[r]), x_t>,  t < T, r < n_out
+ * W: device packed weights (see above), n_out rows of n_in; the activation
+ * is the Q8_K quantization of T rows (xq [T][n_in], xd [T][n_in/256], xsum
+ * [T][n_in/16], device); out: device float [T][n_out].  n_in a multiple of
+ * 256; any T >= 1.  fp32 results agree with the reference to ~1e-6
+ * relative (the integer super-block partials are exact; only the fp32
+ * summation order differs). */
+int qma_cuda_matvec(int wtype, const void *W, int n_in, int n_out, int T,
+                    const int8_t *xq, const float *xd, const int16_t *xsum,
+                    float *out, void *stream);
+
+/* Debug/parity: the exact int32 partial sums behind one token's row dots.
+ * Q4_K / Q8_0: per 32-lane block, sum(q * xq) -> isum [n_out][n_in/32];
+ * Q6_K: per super-block, sum_g scale_g * sum16((q - 32) * xq) -> isum
+ * [n_out][n_in/256].  Matches the oracle's integer partials bit for bit. */
+int qma_cuda_dot_partials(int wtype, const void *W, int n_in, int n_out,
+                          const int8_t *xq, int32_t *isum, void *stream);
+
+/* ---- synthetic weights ----------------------------------------------------
+ * Random-init weights generated on the device, in GGUF block order: element
+ * i of tensor `name` is a seeded Irwin-Hall(4) normal (a pure function of
+ * seed, name and i; N(0, 0.02) for projections, 1 + N(0, 0.05) for norms,
+ * negative for ssm_a), then quantized to `type` by the engine's quantizer.
+ * Byte-identical to the CPU generator the parity tests use.  No reference
+ * counterpart: the reference loads a GGUF file (qma_load, gguf.c:104). */
+int qma_cuda_synth_tensor(const char *name, int type, uint64_t nelem, uint64_t seed,
+                          void *dst, void *stream);
+
+/* ---- MoE FFN block ------------------------------------------------------
+ * Replaces moe_ffn (nn.c:509-649) with its q8k expert kernels
+ * (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473, the
+ * (token, expert) task loop moe_xpar_worker nn.c:652-707) and the residual
+ * around it in qma_eval (nn.c:2246-2252):
+ *   xn    = rms_norm(x2) * post_attention_norm
+ *   top-8 = router(xn)  (fp32 logits, softmax, top-8, renormalise)
+ *   x_out = x2 + sum_k w_k * down_k(q8k(silu(gate_k.xn) * up_k.xn))
+ *              + sigmoid(shexp_gate . q8k(xn)) * down_sh(...)
+ * Routing is bit-exact with the reference: every logit is known to within a
+ * proven bound of the reference's sequential fp32 sum, and any expert whose
+ * rank that bound cannot settle is recomputed in exactly the reference's
+ * order.  All pointers are device pointers.  gate/up expert tensors are in
+ * GGUF order ([256][512 rows][2048], Q4_K); down_exps holds one packed
+ * [2048 rows][512] matrix per expert (qma_cuda_packed_bytes(down_type,
+ * 2048, 512) bytes each, see qma_cuda_repack). */
+typedef struct {
+    const float *post_norm;        /* blk.N.post_attention_norm.weight [2048] */
+    const float *gate_inp;         /* blk.N.ffn_gate_inp.weight [256][2048]    */
+    const void  *gate_exps;        /* blk.N.ffn_gate_exps.weight, Q4_K         */
+    const void  *up_exps;          /* blk.N.ffn_up_exps.weight, Q4_K           */
+    const void  *down_exps;        /* blk.N.ffn_down_exps.weight, packed       */
+    const float *gate_inp_shexp;   /* blk.N.ffn_gate_inp_shexp.weight [2048]   */
+    const void  *gate_shexp;       /* blk.N.ffn_gate_shexp.weight, Q4_K        */
+    const void  *up_shexp;         /* blk.N.ffn_up_shexp.weight, Q4_K          */
+    const void  *down_shexp;       /* blk.N.ffn_down_shexp.weight, packed      */
+    int down_type;                 /* QMA_TYPE_Q6_K or QMA_TYPE_Q4_K           */
+    int down_shexp_type;
+} qma_cuda_moe_weights;
+
+/* Device scratch bytes qma_cuda_moe_layer needs for T tokens. */
+size_t qma_cuda_moe_scratch_bytes(int T);
+
+/* x2: device [T][2048] residual stream after attention; x_out: device
+ * [T][2048] (may alias x2).  sel (int32 [T][8]) and wts (float [T][8]),
+ * optional device outputs, receive the routing in selection order.  scratch:
+ * device buffer of qma_cuda_moe_scratch_bytes(T) bytes, owned by the caller;
+ * calls that share a scratch buffer must not overlap on the GPU. */
+int qma_cuda_moe_layer(const qma_cuda_moe_weights *w, const float *x2, int T,
+                       float *x_out, int32_t *sel, float *wts, void *scratch,
+                       size_t scratch_bytes, void *stream);
+
+/* Diagnostics of the last routing on a scratch buffer: how many tokens
+ * needed the exact sequential recompute (host int, read after the stream
+ * is synchronised). */
+int qma_cuda_moe_exact_fallbacks(const void *scratch, int T, int *count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QMA_CUDA_H */

@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
         L.qo_model_new.restype = vp
         L.qo_model_free.argtypes = [vp]
         L.qo_moe_ffn.argtypes = [vp, i32, vp, i32, vp, vp, vp]
+        L.qo_moe_block.argtypes = [vp, i32, vp, i32, vp, vp, vp]
         L.qo_router_logits.argtypes = [vp, vp, vp]
         L.qo_state_new.argtypes = [i32]
         L.qo_state_new.restype = vp
@@ -129,6 +130,7 @@ def ref() -> C.CDLL:
         R.qr_eval.restype = i32
         R.qr_moe_ffn.argtypes = [vp, i32, vp, i32, vp, vp]
         R.qr_gdn_layer.argtypes = [vp, vp, i32, vp, i32, vp]
+        R.qr_matmul.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32]
         R.qr_state_conv.argtypes = [vp, i32]
         R.qr_state_conv.restype = C.POINTER(C.c_float)
         R.qr_state_ssm.argtypes = [vp, i32]
@@ -226,6 +228,23 @@ def synth_layout(n_vocab=N_VOCAB, embd_type=Q8_0, out_type=Q8_0, down_type=Q6_K,
 
 def tensor_index(arr, n) -> dict:
     return {arr[i].name.decode(): i for i in range(n)}
+
+
+def synth_matrix(name: str, wtype: int, rows: int, n: int, seed: int = 0,
+                 threads=None) -> np.ndarray:
+    """GGUF-layout bytes [rows][row_bytes] of one synthetic weight matrix,
+    values a seeded function of (seed, name, index), N(0, 0.02) before
+    quantization (F32 matrices are returned as raw float bytes)."""
+    t = Tensor()
+    t.name = name.encode()
+    t.type = wtype
+    t.ne[0], t.ne[1], t.ne[2] = n, rows, 1
+    t.off = 0
+    rb = row_bytes(wtype, n)
+    t.nbytes = rb * rows
+    out = np.zeros((rows, rb), np.uint8)
+    lib().qo_synth_tensor(C.byref(t), _ptr(out), seed, threads or min(os.cpu_count() or 1, 32))
+    return out
 
 
 def synth_blob(arr, n, size, seed, names=None, threads=None) -> np.ndarray:

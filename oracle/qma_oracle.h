@@ -168,6 +168,10 @@ void      qo_model_free(qo_model *m);
  * optional) receive the routing in selection order. */
 void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
                 int *sel, float *w);
+/* FFN half of a layer (nn.c:2246-2252): out = x2 + moe_ffn(rms_norm(x2) *
+ * post_attention_norm). */
+void qo_moe_block(const qo_model *m, int il, const float *x2, int T, float *out,
+                  int *sel, float *w);
 /* router only: logits (256) of one token in the reference's sequential
  * fp32 order (nn.c:513-523) */
 void qo_router_logits(const float *gate_inp, const float *x, float *logits);

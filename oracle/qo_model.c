@@ -303,6 +303,20 @@ static void mm_rows(void *arg, int r0, int r1)
     }
 }
 
+/* The FFN half of a layer in qma_eval (nn.c:2246-2252):
+ * xn = rms_norm(x2) * post_norm; out = moe_ffn(xn) + x2. */
+void qo_moe_block(const qo_model *m, int il, const float *x2, int T, float *out,
+                  int *sel, float *w)
+{
+    float *xn = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    float *ra = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    rms_norm_m(xn, x2, m->L[il].post_norm, QO_EMBD, T);
+    qo_moe_ffn(m, il, xn, T, ra, sel, w);
+    for (size_t i = 0; i < (size_t)QO_EMBD * T; i++) out[i] = ra[i] + x2[i];
+    free(xn);
+    free(ra);
+}
+
 /* parallel matmul (rows independent; same per-element arithmetic) */
 static void matmul_p(const float *x, const uint8_t *W, int n_in, int n_out, int T,
                      int wtype, float *out)

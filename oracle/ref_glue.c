@@ -123,6 +123,14 @@ int qr_eval(qma_t *m, runstate_t *rs, const int *tokens, int n, float *logits,
     return qma_eval(m, rs, tokens, n, logits, n_threads, 0, logits_all);
 }
 
+/* the reference's quantized matmul (nn.c:307-345) on n_threads pool workers */
+void qr_matmul(const float *x, const uint8_t *W, int n_in, int n_out, int T, int wtype,
+               float *out, int n_threads)
+{
+    pool_init(n_threads);
+    matmul(x, W, n_in, n_out, T, wtype, out);
+}
+
 /* one MoE FFN (nn.c:509-649); sel8 (optional) gets the last token's
    routing from the history the reference keeps (nn.c:549-550) */
 void qr_moe_ffn(qma_t *m, int il, const float *x, int T, float *out, int *sel8)

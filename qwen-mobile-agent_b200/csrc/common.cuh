@@ -1,0 +1,163 @@
+// common.cuh -- shared device/host helpers of the qma B200 engine (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "qma_cuda.h"
+
+namespace qma {
+
+// ------------------------------------------------------------ error plumbing
+// Thread-local message behind qma_cuda_last_error(); every C entry point
+// returns a status and never exits the process.
+void set_error(const char *fmt, ...);
+void clear_error();
+
+#define QMA_CHECK_CUDA(call)                                                   \
+    do {                                                                       \
+        cudaError_t e_ = (call);                                               \
+        if (e_ != cudaSuccess) {                                               \
+            ::qma::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call,        \
+                             cudaGetErrorString(e_));                          \
+            return QMA_CUDA_ERR_CUDA;                                          \
+        }                                                                      \
+    } while (0)
+
+#define QMA_CHECK_LAUNCH()                                                     \
+    do {                                                                       \
+        cudaError_t e_ = cudaGetLastError();                                   \
+        if (e_ != cudaSuccess) {                                               \
+            ::qma::set_error("%s:%d kernel launch: %s", __FILE__, __LINE__,    \
+                             cudaGetErrorString(e_));                          \
+            return QMA_CUDA_ERR_CUDA;                                          \
+        }                                                                      \
+    } while (0)
+
+#define QMA_REQUIRE(cond, ...)                                                 \
+    do {                                                                       \
+        if (!(cond)) {                                                         \
+            ::qma::set_error(__VA_ARGS__);                                     \
+            return QMA_CUDA_ERR_INVALID;                                       \
+        }                                                                      \
+    } while (0)
+
+static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------ block formats
+constexpr int QK = 256;            // super-block lanes (QK_K, qma.h:74)
+constexpr int Q4K_BYTES = 144;     // block_q4_K, qma.h:77-82
+constexpr int Q6K_BYTES = 210;     // block_q6_K, qma.h:85-90
+constexpr int Q80_BYTES = 34;      // block_q8_0, qma.h:92-94
+
+// Packed (planar) layouts of Q6_K and Q8_0 matrices; see qma_cuda.h.
+struct Q6Planes {
+    const uint8_t *ql, *qh;
+    const int8_t *sc;
+    const __half *d;
+};
+struct Q8Planes {
+    const int8_t *q;
+    const __half *d;
+};
+static inline size_t pad16(size_t x) { return (x + 15) & ~size_t(15); }
+__host__ __device__ inline size_t q6_plane_ql(int rows, int n) { return size_t(rows) * n / 2; }
+__host__ __device__ inline size_t q6_plane_qh(int rows, int n) { return size_t(rows) * n / 4; }
+__host__ __device__ inline size_t q6_plane_sc(int rows, int n) { return size_t(rows) * n / 16; }
+__host__ __device__ inline size_t q6_plane_d(int rows, int n) { return size_t(rows) * (n / 256) * 2; }
+
+inline Q6Planes q6_planes(const void *base, int rows, int n) {
+    const uint8_t *p = static_cast<const uint8_t *>(base);
+    Q6Planes P;
+    P.ql = p;
+    p += pad16(q6_plane_ql(rows, n));
+    P.qh = p;
+    p += pad16(q6_plane_qh(rows, n));
+    P.sc = reinterpret_cast<const int8_t *>(p);
+    p += pad16(q6_plane_sc(rows, n));
+    P.d = reinterpret_cast<const __half *>(p);
+    return P;
+}
+inline Q8Planes q8_planes(const void *base, int rows, int n) {
+    const uint8_t *p = static_cast<const uint8_t *>(base);
+    Q8Planes P;
+    P.q = reinterpret_cast<const int8_t *>(p);
+    P.d = reinterpret_cast<const __half *>(p + pad16(size_t(rows) * n));
+    return P;
+}
+size_t packed_bytes(int wtype, int rows, int n);
+
+// ------------------------------------------------------------ device helpers
+// Streaming 16-byte load of weights: read once per step, keep out of L1.
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_stream8(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(v.x), "=r"(v.y)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_stream4(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ld_stream2(const void *p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// Sum over aligned groups of `width` lanes (width a power of two <= 32).
+__device__ __forceinline__ float group_sum(float v, int width) {
+    for (int o = width >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int group_sum_i(int v, int width) {
+    for (int o = width >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Programmatic dependent launch: wait for the upstream grid's writes, and
+// let the downstream grid start its prologue.  No-ops without PDL.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,
+// quants.c:18-26 / q8k.c:22-30).
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *s, int &d, int &m) {
+    if (j < 4) {
+        d = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        d = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+}  // namespace qma

@@ -1,0 +1,235 @@
+// gemv.cu -- standalone Q8_K quantization and quantized GEMV entry points
+// (qma_cuda_q8k_quant, qma_cuda_matvec, qma_cuda_dot_partials).
+#include "common.cuh"
+#include "gemv.cuh"
+#include "quant.cuh"
+
+namespace qma {
+
+// ------------------------------------------------------------------ Q8_K --
+__global__ void __launch_bounds__(256) q8k_quant_kernel(const float *__restrict__ x, int rows,
+                                                        int n, int8_t *xq, float *xd,
+                                                        int16_t *xsum) {
+    const int lane = threadIdx.x & 31;
+    const long warp = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long nwarps = (long(gridDim.x) * blockDim.x) >> 5;
+    const int nb = n / 256;
+    for (long b = warp; b < long(rows) * nb; b += nwarps) {
+        const long r = b / nb, j = b % nb;
+        const float4 *p = reinterpret_cast<const float4 *>(x + r * n + j * 256 + lane * 8);
+        const float4 a = p[0], c = p[1];
+        const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        q8k_block_warp(v, lane, xq + r * n + j * 256, xd + r * nb + j, xsum + r * (n / 16) + j * 16);
+    }
+}
+
+// ---------------------------------------------------------------- GEMV ----
+template <class F, int T, int LPR, int UPL, int RU>
+__global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, int n_out,
+                                                   const int8_t *xq, const float *xd,
+                                                   const int16_t *xsum, float *out, int out_ld) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    gemv_warp_rows<F, T, LPR, UPL, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, warp, nwarps,
+                                       lane);
+}
+
+static int g_num_sms = 0;
+int num_sms() {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+// One full wave: as many 256-thread CTAs as fit on every SM at once (from
+// the kernel's own register use), capped by the rows there are to do.
+template <class F, int T, int LPR, int UPL, int RU>
+static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
+                       const float *xd, const int16_t *xsum, float *out, int out_ld,
+                       cudaStream_t st) {
+    constexpr int RPW = 32 / LPR;
+    static int per_sm = 0;
+    if (!per_sm) {
+        QMA_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, gemv_kernel<F, T, LPR, UPL, RU>, 256, 0));
+        if (per_sm < 1) per_sm = 1;
+    }
+    const long warps_needed = (n_out + RPW * RU - 1) / (RPW * RU);
+    long blocks = (warps_needed + 7) / 8;
+    const long wave = long(num_sms()) * per_sm;
+    if (blocks > wave) blocks = wave;
+    gemv_kernel<F, T, LPR, UPL, RU><<<int(blocks), 256, 0, st>>>(W, n_in, n_out, xq, xd, xsum,
+                                                                 out, out_ld);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+// Shape dispatch: units per row U = n_in / F::UNIT.  Single-token passes
+// keep two row groups of loads in flight per warp.
+template <class F, int T, int RU = (T == 1 ? 2 : 1)>
+static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
+                          const float *xd, const int16_t *xsum, float *out, int out_ld,
+                          cudaStream_t st) {
+    const int U = n_in / F::UNIT;
+    switch (U) {
+    case 2: return launch_gemv<F, T, 2, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 4: return launch_gemv<F, T, 4, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 8: return launch_gemv<F, T, 8, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 16: return launch_gemv<F, T, 16, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 32: return launch_gemv<F, T, 32, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 64: return launch_gemv<F, T, 32, 2, (RU > 1 ? RU / 2 : 1)>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    default:
+        set_error("matvec: n_in %d unsupported for this weight type", n_in);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+}
+
+template <class F, int TMAX>
+static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, const int8_t *xq,
+                       const float *xd, const int16_t *xsum, float *out, cudaStream_t st) {
+    int t0 = 0;
+    while (t0 < T) {
+        const int rem = T - t0;
+        const int8_t *q = xq + size_t(t0) * n_in;
+        const float *d = xd + size_t(t0) * (n_in / 256);
+        const int16_t *s = xsum + size_t(t0) * (n_in / 16);
+        float *o = out + size_t(t0) * n_out;
+        int rc, tn;
+        if constexpr (TMAX >= 4) {
+            if (rem >= 4) {
+                rc = dispatch_shape<F, 4>(W, n_in, n_out, q, d, s, o, n_out, st);
+                tn = 4;
+                if (rc) return rc;
+                t0 += tn;
+                continue;
+            }
+        }
+        if (rem >= 2) {
+            rc = dispatch_shape<F, 2>(W, n_in, n_out, q, d, s, o, n_out, st);
+            tn = 2;
+        } else {
+            rc = dispatch_shape<F, 1>(W, n_in, n_out, q, d, s, o, n_out, st);
+            tn = 1;
+        }
+        if (rc) return rc;
+        t0 += tn;
+    }
+    return QMA_CUDA_OK;
+}
+
+int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
+           const float *xd, const int16_t *xsum, float *out, cudaStream_t st) {
+    switch (wtype) {
+    case QMA_TYPE_Q4_K:
+        return gemv_tokens<FmtQ4K, 4>(static_cast<const uint8_t *>(W), n_in, n_out, T, xq, xd,
+                                      xsum, out, st);
+    case QMA_TYPE_Q6_K:
+        return gemv_tokens<FmtQ6K, 2>(q6_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
+                                      out, st);
+    case QMA_TYPE_Q8_0:
+        return gemv_tokens<FmtQ80, 4>(q8_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
+                                      out, st);
+    default:
+        set_error("matvec: unsupported weight type %d", wtype);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+}
+
+// --------------------------------------------------------- int partials ---
+// One thread per (row, unit), with the GEMV's own unit arithmetic.
+template <class F>
+__global__ void partials_kernel_safe(typename F::Ptr W, int n_in, int n_out, const int8_t *xq,
+                                     const float *xd, const int16_t *xsum, int32_t *isum) {
+    const int U = n_in / F::UNIT;
+    const long total = long(n_out) * U;
+    for (long i = blockIdx.x * long(blockDim.x) + threadIdx.x; i < total;
+         i += long(gridDim.x) * blockDim.x) {
+        const int r = int(i / U), u = int(i % U);
+        typename F::Act a;
+        F::load_act(a, xq, xd, xsum, u);
+        typename F::Wt w;
+        F::load_w(w, W, r, n_in, u);
+        if constexpr (F::UNIT == 128) {
+            atomicAdd(isum + size_t(r) * (n_in / 256) + (u >> 1), F::isum(w, a));
+        } else {
+            int p0, p1;
+            F::isums(w, a, p0, p1);
+            isum[size_t(r) * (n_in / 32) + 2 * u] = p0;
+            isum[size_t(r) * (n_in / 32) + 2 * u + 1] = p1;
+        }
+    }
+}
+}  // namespace qma
+
+extern "C" {
+
+int qma_cuda_q8k_quant(const float *x, int rows, int n, int8_t *xq, float *xd, int16_t *xsum,
+                       void *stream) {
+    qma::clear_error();
+    QMA_REQUIRE(x && xq && xd && xsum && rows > 0 && n > 0 && n % 256 == 0,
+                "qma_cuda_q8k_quant: bad arguments (rows %d, n %d)", rows, n);
+    const long warps = long(rows) * (n / 256);
+    long blocks = (warps + 7) / 8;
+    if (blocks > 4096) blocks = 4096;
+    qma::q8k_quant_kernel<<<int(blocks), 256, 0, qma::as_stream(stream)>>>(x, rows, n, xq, xd, xsum);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
+                    const float *xd, const int16_t *xsum, float *out, void *stream) {
+    qma::clear_error();
+    QMA_REQUIRE(W && xq && xd && xsum && out && n_in > 0 && n_in % 256 == 0 && n_out > 0 && T > 0,
+                "qma_cuda_matvec: bad arguments (n_in %d, n_out %d, T %d)", n_in, n_out, T);
+    return qma::matvec(wtype, W, n_in, n_out, T, xq, xd, xsum, out, qma::as_stream(stream));
+}
+
+int qma_cuda_dot_partials(int wtype, const void *W, int n_in, int n_out, const int8_t *xq,
+                          int32_t *isum, void *stream) {
+    qma::clear_error();
+    QMA_REQUIRE(W && xq && isum && n_in > 0 && n_in % 256 == 0 && n_out > 0,
+                "qma_cuda_dot_partials: bad arguments");
+    cudaStream_t st = qma::as_stream(stream);
+    // xd / xsum do not enter the integer partials; give the loaders a
+    // harmless zero buffer of the right size.
+    static float *dummy_xd = nullptr;
+    static int16_t *dummy_xs = nullptr;
+    static int dummy_n = 0;
+    if (dummy_n < n_in) {
+        cudaFree(dummy_xd);
+        cudaFree(dummy_xs);
+        QMA_CHECK_CUDA(cudaMalloc(&dummy_xd, sizeof(float) * (n_in / 256)));
+        QMA_CHECK_CUDA(cudaMalloc(&dummy_xs, sizeof(int16_t) * (n_in / 16)));
+        QMA_CHECK_CUDA(cudaMemset(dummy_xd, 0, sizeof(float) * (n_in / 256)));
+        QMA_CHECK_CUDA(cudaMemset(dummy_xs, 0, sizeof(int16_t) * (n_in / 16)));
+        dummy_n = n_in;
+    }
+    const int grid = 1024;
+    switch (wtype) {
+    case QMA_TYPE_Q4_K:
+        qma::partials_kernel_safe<qma::FmtQ4K><<<grid, 256, 0, st>>>(
+            static_cast<const uint8_t *>(W), n_in, n_out, xq, dummy_xd, dummy_xs, isum);
+        break;
+    case QMA_TYPE_Q6_K:
+        QMA_CHECK_CUDA(cudaMemsetAsync(isum, 0, sizeof(int32_t) * size_t(n_out) * (n_in / 256), st));
+        qma::partials_kernel_safe<qma::FmtQ6K><<<grid, 256, 0, st>>>(
+            qma::q6_planes(W, n_out, n_in), n_in, n_out, xq, dummy_xd, dummy_xs, isum);
+        break;
+    case QMA_TYPE_Q8_0:
+        qma::partials_kernel_safe<qma::FmtQ80><<<grid, 256, 0, st>>>(
+            qma::q8_planes(W, n_out, n_in), n_in, n_out, xq, dummy_xd, dummy_xs, isum);
+        break;
+    default:
+        qma::set_error("qma_cuda_dot_partials: unsupported weight type %d", wtype);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+}  // extern "C"

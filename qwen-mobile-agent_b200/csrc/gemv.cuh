@@ -1,0 +1,250 @@
+// gemv.cuh -- super-block dot "units" for Q4_K / Q6_K / Q8_0 weights against
+// Q8_K activations, and the warp-cooperative GEMV built on them.
+//
+// A unit is the slice of one weight row a lane owns: 64 weights of a Q4_K
+// super-block (one (scale, min) pair of 32-lane sub-blocks), 128 weights
+// (one half) of a Q6_K super-block, or 64 weights (two blocks) of Q8_0.
+// Consecutive lanes own consecutive units, so a warp streams contiguous row
+// bytes with 16-byte loads; the activation slice of a unit stays in
+// registers and is reused for every row the warp visits.
+//
+// Integer work is exact (__dp4a): per-sub-block int32 sums equal the
+// reference's SDOT partials (q8k.c:89-262).  Only the fp32 combination of
+// those integers with the fp16 scales is ordered differently.
+#pragma once
+#include "common.cuh"
+
+namespace qma {
+
+__device__ __forceinline__ int hdr_byte(const uint4 &h, int k) {
+    const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
+    return (w >> ((k & 3) * 8)) & 0xff;
+}
+
+// ------------------------------------------------------------------ Q4_K --
+struct FmtQ4K {
+    static constexpr int UNIT = 64;
+    static constexpr int XW = 16;           // activation words per unit
+    using Ptr = const uint8_t *;
+    struct Act { int x[16]; float xd; int xs01, xs23; };
+    struct Wt { uint4 h, q0, q1; };
+
+    __device__ static void load_act(Act &a, const int8_t *xq, const float *xd,
+                                    const int16_t *xsum, int u) {
+        const int sb = u >> 2, g = u & 3;
+        const int4 *p = reinterpret_cast<const int4 *>(xq + sb * 256 + g * 64);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int4 v = p[k];
+            a.x[4 * k] = v.x; a.x[4 * k + 1] = v.y; a.x[4 * k + 2] = v.z; a.x[4 * k + 3] = v.w;
+        }
+        a.xd = xd[sb];
+        const int16_t *s = xsum + sb * 16 + g * 4;
+        a.xs01 = int(s[0]) + int(s[1]);
+        a.xs23 = int(s[2]) + int(s[3]);
+    }
+    __device__ static void load_w(Wt &w, Ptr W, int row, int n_in, int u) {
+        const uint8_t *b = W + size_t(row) * (n_in / 256) * 144 + (u >> 2) * 144;
+        w.h = ld_stream16(b);
+        w.q0 = ld_stream16(b + 16 + (u & 3) * 32);
+        w.q1 = ld_stream16(b + 32 + (u & 3) * 32);
+    }
+    // exact integer sub-block sums (low nibbles -> sub-block 2g, high -> 2g+1)
+    __device__ static void isums(const Wt &w, const Act &a, int &lo, int &hi) {
+        const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
+        int s0 = 0, s1 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            s0 = __dp4a(int(q[k] & 0x0F0F0F0Fu), a.x[k], s0);
+            s1 = __dp4a(int((q[k] >> 4) & 0x0F0F0F0Fu), a.x[8 + k], s1);
+        }
+        lo = s0;
+        hi = s1;
+    }
+    __device__ static float dot(const Wt &w, const Act &a, int u) {
+        int lo, hi;
+        isums(w, a, lo, hi);
+        const int g = u & 3;
+        int sc0, m0, sc1, m1;
+        {
+            const int j0 = 2 * g, j1 = 2 * g + 1;
+            // get_scale_min_k4 (quants.c:18-26) on the 12 header bytes
+            if (j0 < 4) {
+                sc0 = hdr_byte(w.h, j0) & 63; m0 = hdr_byte(w.h, j0 + 4) & 63;
+                sc1 = hdr_byte(w.h, j1) & 63; m1 = hdr_byte(w.h, j1 + 4) & 63;
+            } else {
+                sc0 = (hdr_byte(w.h, j0 + 4) & 0xF) | ((hdr_byte(w.h, j0 - 4) >> 6) << 4);
+                m0 = (hdr_byte(w.h, j0 + 4) >> 4) | ((hdr_byte(w.h, j0) >> 6) << 4);
+                sc1 = (hdr_byte(w.h, j1 + 4) & 0xF) | ((hdr_byte(w.h, j1 - 4) >> 6) << 4);
+                m1 = (hdr_byte(w.h, j1 + 4) >> 4) | ((hdr_byte(w.h, j1) >> 6) << 4);
+            }
+        }
+        const int I1 = sc0 * lo + sc1 * hi;
+        const int I2 = m0 * a.xs01 + m1 * a.xs23;
+        const float d = h2f(uint16_t(w.h.x & 0xffff));
+        const float dmin = h2f(uint16_t(w.h.x >> 16));
+        return a.xd * (d * float(I1) - dmin * float(I2));
+    }
+};
+
+// ------------------------------------------------------------------ Q6_K --
+struct FmtQ6K {
+    static constexpr int UNIT = 128;
+    static constexpr int XW = 32;
+    using Ptr = Q6Planes;
+    struct Act { int x[32]; float xd; };
+    struct Wt { uint4 l0, l1, l2, l3, h0, h1; uint2 sc; uint16_t d; };
+
+    __device__ static void load_act(Act &a, const int8_t *xq, const float *xd,
+                                    const int16_t *, int u) {
+        const int4 *p = reinterpret_cast<const int4 *>(xq + u * 128);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int4 v = p[k];
+            a.x[4 * k] = v.x; a.x[4 * k + 1] = v.y; a.x[4 * k + 2] = v.z; a.x[4 * k + 3] = v.w;
+        }
+        a.xd = xd[u >> 1];
+    }
+    __device__ static void load_w(Wt &w, const Ptr &P, int row, int n_in, int u) {
+        const int sb = u >> 1, j = u & 1;
+        const uint8_t *ql = P.ql + size_t(row) * (n_in / 2) + sb * 128 + j * 64;
+        const uint8_t *qh = P.qh + size_t(row) * (n_in / 4) + sb * 64 + j * 32;
+        w.l0 = ld_stream16(ql);
+        w.l1 = ld_stream16(ql + 16);
+        w.l2 = ld_stream16(ql + 32);
+        w.l3 = ld_stream16(ql + 48);
+        w.h0 = ld_stream16(qh);
+        w.h1 = ld_stream16(qh + 16);
+        w.sc = ld_stream8(P.sc + size_t(row) * (n_in / 16) + sb * 16 + j * 8);
+        w.d = ld_stream2(P.d + size_t(row) * (n_in / 256) + sb);
+    }
+    // exact sum over the 8 sixteen-lane groups of scale_g * sum((q-32)*xq)
+    __device__ static int isum(const Wt &w, const Act &a) {
+        const uint32_t QL[16] = {w.l0.x, w.l0.y, w.l0.z, w.l0.w, w.l1.x, w.l1.y, w.l1.z, w.l1.w,
+                                 w.l2.x, w.l2.y, w.l2.z, w.l2.w, w.l3.x, w.l3.y, w.l3.z, w.l3.w};
+        const uint32_t QH[8] = {w.h0.x, w.h0.y, w.h0.z, w.h0.w, w.h1.x, w.h1.y, w.h1.z, w.h1.w};
+        int I = 0;
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            int p = 0;
+#pragma unroll
+            for (int i4 = 0; i4 < 4; i4++) {
+                const int i = 4 * g + i4;              // quad of lanes 4i..4i+3
+                const int hi = i >> 4;
+                const int shift = 2 * (((i >> 3) & 1) + 2 * hi);
+                const uint32_t lo4 = (QL[i & 15] >> (4 * hi)) & 0x0F0F0F0Fu;
+                const uint32_t h2 = ((QH[i & 7] >> shift) & 0x03030303u) << 4;
+                const int v = int(__vsub4(lo4 | h2, 0x20202020u));
+                p = __dp4a(v, a.x[i], p);
+            }
+            const uint32_t sw = g < 4 ? w.sc.x : w.sc.y;
+            const int sc = int(int8_t((sw >> ((g & 3) * 8)) & 0xff));
+            I += sc * p;
+        }
+        return I;
+    }
+    __device__ static float dot(const Wt &w, const Act &a, int) {
+        const int I = isum(w, a);
+        return h2f(w.d) * a.xd * float(I);
+    }
+};
+
+// ------------------------------------------------------------------ Q8_0 --
+struct FmtQ80 {
+    static constexpr int UNIT = 64;
+    static constexpr int XW = 16;
+    using Ptr = Q8Planes;
+    struct Act { int x[16]; float xd; };
+    struct Wt { uint4 q0, q1, q2, q3; uint32_t d2; };
+
+    __device__ static void load_act(Act &a, const int8_t *xq, const float *xd,
+                                    const int16_t *, int u) {
+        const int4 *p = reinterpret_cast<const int4 *>(xq + u * 64);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int4 v = p[k];
+            a.x[4 * k] = v.x; a.x[4 * k + 1] = v.y; a.x[4 * k + 2] = v.z; a.x[4 * k + 3] = v.w;
+        }
+        a.xd = xd[u >> 2];
+    }
+    __device__ static void load_w(Wt &w, const Ptr &P, int row, int n_in, int u) {
+        const int8_t *q = P.q + size_t(row) * n_in + u * 64;
+        w.q0 = ld_stream16(q);
+        w.q1 = ld_stream16(q + 16);
+        w.q2 = ld_stream16(q + 32);
+        w.q3 = ld_stream16(q + 48);
+        w.d2 = ld_stream4(P.d + size_t(row) * (n_in / 32) + u * 2);
+    }
+    __device__ static void isums(const Wt &w, const Act &a, int &i0, int &i1) {
+        const uint32_t q[16] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w,
+                                w.q2.x, w.q2.y, w.q2.z, w.q2.w, w.q3.x, w.q3.y, w.q3.z, w.q3.w};
+        int s0 = 0, s1 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            s0 = __dp4a(int(q[k]), a.x[k], s0);
+            s1 = __dp4a(int(q[8 + k]), a.x[8 + k], s1);
+        }
+        i0 = s0;
+        i1 = s1;
+    }
+    __device__ static float dot(const Wt &w, const Act &a, int) {
+        int i0, i1;
+        isums(w, a, i0, i1);
+        const float d0 = h2f(uint16_t(w.d2 & 0xffff)), d1 = h2f(uint16_t(w.d2 >> 16));
+        return (float(i0) * d0 + float(i1) * d1) * a.xd;
+    }
+};
+
+// ---------------------------------------------------------------- GEMV ----
+// LPR lanes cooperate on one row (LPR = units per row when a row has fewer
+// than 32 units, else 32); each lane owns UPL units of the row; T tokens
+// are processed per pass with their activation slices in registers.  A warp
+// issues the loads of RU row groups before computing any of them, so every
+// lane keeps RU*UPL units of weights in flight.
+template <class F, int T, int LPR, int UPL, int RU>
+__device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_in, int n_out,
+                                               const int8_t *xq, const float *xd,
+                                               const int16_t *xsum, float *out, int out_ld,
+                                               int warp, int nwarps, int lane) {
+    constexpr int RPW = 32 / LPR;
+    const int lir = lane % LPR, slot = lane / LPR;
+    typename F::Act act[UPL][T];
+#pragma unroll
+    for (int k = 0; k < UPL; k++)
+#pragma unroll
+        for (int t = 0; t < T; t++)
+            F::load_act(act[k][t], xq + size_t(t) * n_in, xd + size_t(t) * (n_in / 256),
+                        xsum + size_t(t) * (n_in / 16), lir + k * LPR);
+    for (int rb = warp * RPW * RU; rb < n_out; rb += nwarps * RPW * RU) {
+        typename F::Wt w[RU][UPL];
+#pragma unroll
+        for (int ru = 0; ru < RU; ru++) {
+            const int r = rb + ru * RPW + slot;
+            if (r < n_out) {
+#pragma unroll
+                for (int k = 0; k < UPL; k++) F::load_w(w[ru][k], W, r, n_in, lir + k * LPR);
+            }
+        }
+#pragma unroll
+        for (int ru = 0; ru < RU; ru++) {
+            const int r = rb + ru * RPW + slot;
+            float acc[T];
+#pragma unroll
+            for (int t = 0; t < T; t++) acc[t] = 0.0f;
+            if (r < n_out) {
+#pragma unroll
+                for (int k = 0; k < UPL; k++)
+#pragma unroll
+                    for (int t = 0; t < T; t++) acc[t] += F::dot(w[ru][k], act[k][t], lir + k * LPR);
+            }
+#pragma unroll
+            for (int t = 0; t < T; t++) acc[t] = group_sum(acc[t], LPR);
+            if (lir == 0 && r < n_out) {
+#pragma unroll
+                for (int t = 0; t < T; t++) out[size_t(t) * out_ld + r] = acc[t];
+            }
+        }
+    }
+}
+
+}  // namespace qma

@@ -1,0 +1,310 @@
+// layers.cu -- embedding, RMSNorm + Q8_K, causal conv1d and the gated delta
+// net recurrence of the qwen35moe forward, for T tokens per launch.
+#include <math.h>
+
+#include "common.cuh"
+#include "layers.cuh"
+#include "quant.cuh"
+
+namespace qma {
+
+// ------------------------------------------------------------- embedding --
+// embed_row (nn.c:2044-2054): dequantize one token_embd row -- Q4_K in
+// GGUF order (dequantize_row_q4_K, quants.c:29-47), Q6_K and Q8_0 in the
+// engine's planar layout.  One CTA per token, 8 contiguous elements a thread;
+// the token comes from a device array, or from the step parameters (decode).
+__global__ void __launch_bounds__(256) embed_q8_kernel(const int8_t *q, const __half *d,
+                                                       const int *tokens, const StepParams *sp,
+                                                       float *x) {
+    const int t = blockIdx.x;
+    pdl_wait();
+    const int tok = tokens ? tokens[t] : sp->token;
+    const int i0 = threadIdx.x * 8;
+    const int8_t *qr = q + size_t(tok) * EMBD + i0;
+    const float dd = __half2float(d[size_t(tok) * (EMBD / 32) + i0 / 32]);
+    const int2 v = *reinterpret_cast<const int2 *>(qr);
+    const int8_t *b = reinterpret_cast<const int8_t *>(&v);
+    float *o = x + size_t(t) * EMBD + i0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) o[k] = __fmul_rn(dd, float(b[k]));
+}
+
+__global__ void __launch_bounds__(256) embed_q4k_kernel(const uint8_t *W, const int *tokens,
+                                                        const StepParams *sp, float *x) {
+    const int t = blockIdx.x;
+    pdl_wait();
+    const int tok = tokens ? tokens[t] : sp->token;
+    const int i0 = threadIdx.x * 8;
+    const uint8_t *b = W + size_t(tok) * (EMBD / 256) * Q4K_BYTES + (i0 / 256) * Q4K_BYTES;
+    const float d = h2f(uint16_t(b[0] | (b[1] << 8))), mn = h2f(uint16_t(b[2] | (b[3] << 8)));
+    const int w = i0 % 256, g = w / 64, hi = (w % 64) / 32, l0 = w % 32;
+    int sc, m;
+    q4k_scale_min(2 * g + hi, b + 4, sc, m);
+    const float d1 = __fmul_rn(d, float(sc)), m1 = __fmul_rn(mn, float(m));
+    float *o = x + size_t(t) * EMBD + i0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint8_t qb = b[16 + 32 * g + l0 + k];
+        const int q = hi ? (qb >> 4) : (qb & 0xF);
+        o[k] = __fsub_rn(__fmul_rn(d1, float(q)), m1);
+    }
+}
+
+// Q6_K planes (dequantize_row_q6_K, quants.c:50-75: y = d * sc * q)
+__global__ void __launch_bounds__(256) embed_q6k_kernel(Q6Planes P, const int *tokens,
+                                                        const StepParams *sp, float *x) {
+    const int t = blockIdx.x;
+    pdl_wait();
+    const int tok = tokens ? tokens[t] : sp->token;
+    const int i0 = threadIdx.x * 8;
+    const int sb = i0 / 256, half = (i0 % 256) / 128;
+    const uint8_t *ql = P.ql + size_t(tok) * (EMBD / 2) + sb * 128 + half * 64;
+    const uint8_t *qh = P.qh + size_t(tok) * (EMBD / 4) + sb * 64 + half * 32;
+    const int8_t *sc = P.sc + size_t(tok) * (EMBD / 16) + sb * 16 + half * 8;
+    const float d = __half2float(P.d[size_t(tok) * (EMBD / 256) + sb]);
+    float *o = x + size_t(t) * EMBD + i0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int w = (i0 % 128) + k;
+        const int L = w & 63, hi = w >> 6;
+        const int lo4 = hi ? (ql[L] >> 4) : (ql[L] & 0xF);
+        const int h2 = (qh[L & 31] >> (2 * ((L >> 5) + 2 * hi))) & 3;
+        const int q = (lo4 | (h2 << 4)) - 32;
+        o[k] = __fmul_rn(__fmul_rn(d, float(sc[w / 16])), float(q));
+    }
+}
+
+int launch_embed(const void *embd, int type, int n_vocab, const int *tokens,
+                 const StepParams *sp, int T, float *x, cudaStream_t st) {
+    if (type == QMA_TYPE_Q8_0) {
+        const Q8Planes P = q8_planes(embd, n_vocab, EMBD);
+        embed_q8_kernel<<<T, 256, 0, st>>>(P.q, P.d, tokens, sp, x);
+    } else if (type == QMA_TYPE_Q6_K) {
+        embed_q6k_kernel<<<T, 256, 0, st>>>(q6_planes(embd, n_vocab, EMBD), tokens, sp, x);
+    } else if (type == QMA_TYPE_Q4_K) {
+        embed_q4k_kernel<<<T, 256, 0, st>>>(static_cast<const uint8_t *>(embd), tokens, sp, x);
+    } else {
+        set_error("embed: unsupported token_embd type %d", type);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+// ----------------------------------------------------- RMSNorm + Q8_K ------
+// rms_norm_m (nn.c:348-357) followed by the Q8_K quantization the next
+// matmul applies (nn.c:318-324): y = (x * r) * w, r = 1 / sqrtf(mean(x^2) +
+// eps) with a double accumulator.  One CTA per token, one warp per block.
+__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restrict__ x,
+                                                            const float *__restrict__ w,
+                                                            int8_t *xq, float *xd, int16_t *xs) {
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ double red[8];
+    pdl_wait();
+    const float4 *p = reinterpret_cast<const float4 *>(x + size_t(t) * EMBD + tid * 8);
+    const float4 a = p[0], b = p[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) ss += double(v[k]) * double(v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    const double tot = ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
+    const float r = 1.0f / sqrtf(float(tot / EMBD) + 1e-6f);
+    const float4 *wp = reinterpret_cast<const float4 *>(w + tid * 8);
+    const float4 wa = wp[0], wb = wp[1];
+    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], r), wv[k]);
+    q8k_block_warp(v, lane, xq + size_t(t) * EMBD + warp * 256, xd + size_t(t) * 8 + warp,
+                   xs + size_t(t) * 128 + warp * 16);
+}
+
+int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *xq, float *xd,
+                         int16_t *xs, cudaStream_t st) {
+    if (n != EMBD) {
+        set_error("rmsnorm_quant: n %d != %d", n, EMBD);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    rmsnorm_quant_kernel<<<T, 256, 0, st>>>(x, w, xq, xd, xs);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+// --------------------------------------------------------------- conv1d ---
+// conv1d_layer (nn.c:717-741) + SiLU (nn.c:2196): width-4 causal conv per
+// channel over [3 state samples | T new samples], state <- last 3 samples.
+// One thread per channel (so each state row has exactly one writer).
+__global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ qkv, int ld,
+                                                     const float *__restrict__ w, float *state,
+                                                     int T, float *out) {
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();
+    if (ch >= CONV_DIM) return;
+    const float4 wc = *reinterpret_cast<const float4 *>(w + size_t(ch) * 4);
+    float s0 = state[ch * 3 + 0], s1 = state[ch * 3 + 1], s2 = state[ch * 3 + 2];
+    for (int t = 0; t < T; t++) {
+        const float xin = qkv[size_t(t) * ld + ch];
+        float sum = __fmul_rn(s0, wc.x);
+        sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
+        sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
+        sum = __fadd_rn(sum, __fmul_rn(xin, wc.w));
+        out[size_t(t) * CONV_DIM + ch] = sum / (1.0f + expf(-sum));
+        s0 = s1;
+        s1 = s2;
+        s2 = xin;
+    }
+    state[ch * 3 + 0] = s0;
+    state[ch * 3 + 1] = s1;
+    state[ch * 3 + 2] = s2;
+}
+
+int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
+                  cudaStream_t st) {
+    conv1d_kernel<<<CONV_DIM / 256, 256, 0, st>>>(qkv, ld, w, state, T, out);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+// ---------------------------------------------------- gated delta net -----
+// gdn_worker (nn.c:784-833) with the per-head L2 norms of q/k (l2norm_skv,
+// nn.c:744-761), the 16 -> 32 head expansion h % 16 (nn.c:2204), beta =
+// sigmoid(.) (nn.c:2170) and g = softplus(alpha + dt) * a (nn.c:2172-2180).
+// The state M[h] (rows j, M[j][i] = S[i][j]) is 128 x 128 fp32; every row
+// updates independently given q, k, v_j, g, beta, so a head is split over 4
+// CTAs of 32 rows; 8 threads own a row (16 elements each), the rows stay in
+// registers across the T tokens.
+__global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv_out,
+                                                  const float *__restrict__ proj, int proj_ld,
+                                                  int beta_off, int alpha_off,
+                                                  const float *__restrict__ dt,
+                                                  const float *__restrict__ av, float *ssm, int T,
+                                                  float *o) {
+    const int rb = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qh = h % KHEADS;
+    const int j = rb * 32 + (tid >> 3);          // state row
+    const int part = tid & 7;                    // 16-element slice of the row
+    __shared__ __align__(16) float qs[2][SSTATE], ks[2][SSTATE];
+    __shared__ double red[2][8];
+    __shared__ float kqred[2][4];
+    float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
+    pdl_wait();
+    float M[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float4 v = reinterpret_cast<const float4 *>(Mrow)[k];
+        M[4 * k] = v.x; M[4 * k + 1] = v.y; M[4 * k + 2] = v.z; M[4 * k + 3] = v.w;
+    }
+    const float scale = 1.0f / sqrtf(float(SSTATE));
+    const float dth = dt[h], ah = av[h];
+    for (int t = 0; t < T; t++) {
+        const int buf = t & 1;
+        const float *co = conv_out + size_t(t) * CONV_DIM;
+        // q (threads 0..127) and k (128..255) with their L2 norms
+        const float val = tid < SSTATE ? co[qh * SSTATE + tid] : co[KEY_DIM + qh * SSTATE + tid - SSTATE];
+        double sq = double(val) * double(val);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        if (lane == 0) red[buf][warp] = sq;
+        __syncthreads();
+        const int base = tid < SSTATE ? 0 : 4;
+        const double tot = (red[buf][base] + red[buf][base + 1]) + (red[buf][base + 2] + red[buf][base + 3]);
+        const float r = 1.0f / fmaxf(sqrtf(float(tot)), 1e-6f);
+        const float nv = __fmul_rn(val, r);
+        if (tid < SSTATE) qs[buf][tid] = nv;
+        else ks[buf][tid - SSTATE] = nv;
+        __syncthreads();
+        // k . q over the 128 lanes (warps 0..3)
+        if (warp < 4) {
+            float kq = __fmul_rn(ks[buf][tid], qs[buf][tid]);
+            kq = warp_sum(kq);
+            if (lane == 0) kqred[buf][warp] = kq;
+        }
+        const float braw = proj[size_t(t) * proj_ld + beta_off + h];
+        const float b = 1.0f / (1.0f + expf(-braw));
+        const float a = proj[size_t(t) * proj_ld + alpha_off + h] + dth;
+        const float sp = a > 20.0f ? a : log1pf(expf(a));
+        const float g = __fmul_rn(sp, ah);
+        const float expg = expf(g);
+        float dq = 0.0f, dk = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            dq = __fadd_rn(dq, __fmul_rn(M[i], qs[buf][part * 16 + i]));
+            dk = __fadd_rn(dk, __fmul_rn(M[i], ks[buf][part * 16 + i]));
+        }
+#pragma unroll
+        for (int off = 4; off > 0; off >>= 1) {
+            dq += __shfl_xor_sync(0xffffffffu, dq, off);
+            dk += __shfl_xor_sync(0xffffffffu, dk, off);
+        }
+        __syncthreads();
+        const float kq = (kqred[buf][0] + kqred[buf][1]) + (kqred[buf][2] + kqred[buf][3]);
+        const float vj = co[2 * KEY_DIM + h * SSTATE + j];
+        const float delta = __fmul_rn(__fsub_rn(vj, __fmul_rn(expg, dk)), b);
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            M[i] = __fadd_rn(__fmul_rn(expg, M[i]), __fmul_rn(ks[buf][part * 16 + i], delta));
+        if (part == 0)
+            o[size_t(t) * VAL_DIM + h * SSTATE + j] =
+                __fmul_rn(__fadd_rn(__fmul_rn(expg, dq), __fmul_rn(delta, kq)), scale);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
+}
+
+int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
+               const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st) {
+    gdn_kernel<<<dim3(4, VHEADS), 256, 0, st>>>(conv_out, proj, proj_ld, beta_off, alpha_off, dt, a,
+                                               ssm, T, o);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+// ------------------------------------------------ gated RMSNorm + Q8_K -----
+// rms_norm_head(ssm_norm) (nn.c:360-372) then * silu(z) (nn.c:2238-2242),
+// quantized for ssm_out: one CTA (32 warps) per token, one warp per head.
+__global__ void __launch_bounds__(1024) gated_norm_quant_kernel(const float *__restrict__ o,
+                                                                const float *__restrict__ z,
+                                                                int z_ld,
+                                                                const float *__restrict__ w,
+                                                                int8_t *xq, float *xd, int16_t *xs) {
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
+    __shared__ __align__(16) float y[VAL_DIM];
+    pdl_wait();
+    const float4 v4 = *reinterpret_cast<const float4 *>(o + size_t(t) * VAL_DIM + h * SSTATE + lane * 4);
+    float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) ss += double(v[k]) * double(v[k]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float r = 1.0f / sqrtf(float(ss / SSTATE) + 1e-6f);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int i = lane * 4 + k;
+        const float zz = z[size_t(t) * z_ld + h * SSTATE + i];
+        const float normed = __fmul_rn(v[k], __fmul_rn(r, w[i]));
+        y[h * SSTATE + i] = __fmul_rn(normed, zz / (1.0f + expf(-zz)));
+    }
+    __syncthreads();
+    if (h < VAL_DIM / 256) {
+        const float4 a = *reinterpret_cast<const float4 *>(y + h * 256 + lane * 8);
+        const float4 b = *reinterpret_cast<const float4 *>(y + h * 256 + lane * 8 + 4);
+        const float vv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        q8k_block_warp(vv, lane, xq + size_t(t) * VAL_DIM + h * 256, xd + size_t(t) * 16 + h,
+                       xs + size_t(t) * 256 + h * 16);
+    }
+}
+
+int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
+                            int8_t *xq, float *xd, int16_t *xs, cudaStream_t st) {
+    gated_norm_quant_kernel<<<T, 1024, 0, st>>>(o, z, z_ld, w, xq, xd, xs);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+}  // namespace qma

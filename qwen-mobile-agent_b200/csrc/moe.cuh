@@ -1,0 +1,40 @@
+// moe.cuh -- constants and scratch layout of the MoE FFN block (moe.cu).
+#pragma once
+#include "common.cuh"
+
+namespace qma {
+
+constexpr int MOE_EMBD = 2048;        // N_EMBD (qma.h:28)
+constexpr int MOE_NEXP = 256;         // N_EXPERT (qma.h:57)
+constexpr int MOE_TOPK = 8;           // N_EXPERT_USED (qma.h:58)
+constexpr int MOE_FF = 512;           // N_FF_EXP / N_FF_SHEXP (qma.h:59-60)
+constexpr int MOE_NSLOT = MOE_TOPK + 1;   // routed experts + the shared expert
+constexpr int MOE_GU_ROWS = 32;       // gate/up row pairs per CTA
+constexpr int MOE_GU_CHUNKS = MOE_FF / MOE_GU_ROWS;
+constexpr int MOE_DOWN_CHUNK = 128;   // down-projection output rows per CTA
+constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
+
+// Per-call device scratch of the MoE block for T tokens (moe_scratch_layout
+// carves one caller-provided buffer).  The two counter arrays must be zero
+// when a call starts; every call leaves them zero again.
+struct MoeScratch {
+    unsigned *rcount;      // [T] router CTAs finished
+    unsigned *dcount;      // [T][16] down CTAs finished per output chunk
+    double *S, *B;         // [T][256] exact logit, bound on the fp32 logit
+    int *fallback;         // [T] 1 if the exact sequential recompute ran
+    int *sel;              // [T][8] selected experts, selection order
+    float *w;              // [T][8] renormalised weights
+    int8_t *xq;            // [T][2048] Q8_K of the normed FFN input
+    float *xd;             // [T][8]
+    int16_t *xs;           // [T][128]
+    float *gs;             // [T] shared-expert gate sigmoid
+    float *h;              // [T][9][512] silu(gate) * up per slot
+    float *part;           // [T][9][2048] down projections per slot
+};
+
+size_t moe_scratch_bytes(int T);
+MoeScratch moe_scratch_layout(void *base, int T);
+int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
+              float *wts, void *scratch, cudaStream_t st);
+
+}  // namespace qma

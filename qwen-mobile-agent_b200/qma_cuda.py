@@ -1,0 +1,113 @@
+"""ctypes binding of libqma_cuda.so, the engine's C ABI (include/qma_cuda.h).
+
+This is the host-side mirror a Python caller (tests, bench) uses; C callers
+(qma's own nn.c) link the library directly.  Device memory is passed as raw
+pointers: torch tensors are used only as allocators (``t.data_ptr()``).
+
+The library must exist: there is no fallback of any kind.  Build it with
+``make -C qwen-mobile-agent_b200`` (``__graft_entry__.build()`` does).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqma_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "qma_cuda.h")
+
+OK = 0
+ERR_INVALID, ERR_NOMEM, ERR_CUDA, ERR_UNSUPPORTED, ERR_STATE, ERR_TIMEOUT = -1, -2, -3, -4, -5, -6
+F32, Q8_0, Q4_K, Q6_K = 0, 8, 12, 14
+
+_vp, _i32, _f32, _u64, _sz = C.c_void_p, C.c_int, C.c_float, C.c_uint64, C.c_size_t
+
+# name -> (restype, argtypes); every function declared in the header
+_SIGS = {
+    "qma_cuda_abi_version": (_i32, []),
+    "qma_cuda_last_error": (C.c_char_p, []),
+    "qma_cuda_init": (_i32, [_i32]),
+    "qma_cuda_q8k_quant": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "qma_cuda_packed_bytes": (_sz, [_i32, _i32, _i32]),
+    "qma_cuda_repack": (_i32, [_i32, _vp, _i32, _i32, _vp, _vp]),
+    "qma_cuda_matvec": (_i32, [_i32, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "qma_cuda_dot_partials": (_i32, [_i32, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "qma_cuda_synth_tensor": (_i32, [C.c_char_p, _i32, _u64, _u64, _vp, _vp]),
+    "qma_cuda_moe_scratch_bytes": (_sz, [_i32]),
+    "qma_cuda_moe_layer": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "qma_cuda_moe_exact_fallbacks": (_i32, [_vp, _i32, C.POINTER(C.c_int)]),
+}
+
+
+class MoeWeights(C.Structure):
+    """qma_cuda_moe_weights: device pointers of one layer's MoE tensors."""
+
+    _fields_ = [("post_norm", _vp), ("gate_inp", _vp), ("gate_exps", _vp), ("up_exps", _vp),
+                ("down_exps", _vp), ("gate_inp_shexp", _vp), ("gate_shexp", _vp),
+                ("up_shexp", _vp), ("down_shexp", _vp), ("down_type", _i32),
+                ("down_shexp_type", _i32)]
+
+
+class QmaError(RuntimeError):
+    """A qma_cuda_* call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn} -> {status}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build the CUDA engine (make -C {HERE}); "
+                "there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def declared_functions() -> list[str]:
+    """Every qma_cuda_* function declared in include/qma_cuda.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(qma_cuda_[a-z0-9_]+)\s*\(", text)))
+
+
+def last_error() -> str:
+    return lib().qma_cuda_last_error().decode()
+
+
+def call(name: str, *args) -> int:
+    """Call a status-returning entry point; raise QmaError on failure."""
+    rc = getattr(lib(), name)(*args)
+    if rc != OK:
+        raise QmaError(name, rc, last_error())
+    return rc
+
+
+def ptr(t) -> int:
+    """Raw device (or host) address of a torch tensor / numpy array / int."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    return t.ctypes.data
+
+
+def init(device: int = 0) -> None:
+    call("qma_cuda_init", device)
+
+
+def packed_bytes(wtype: int, rows: int, n: int) -> int:
+    return int(lib().qma_cuda_packed_bytes(wtype, rows, n))

@@ -1,0 +1,35 @@
+"""The C-ABI library loads on a CPU-only machine, exports every function the
+header declares, and rejects bad arguments with a status (no GPU needed)."""
+import ctypes as C
+
+import qma_cuda as Q
+
+
+def test_library_exports_every_declared_symbol():
+    lib = Q.lib()
+    declared = Q.declared_functions()
+    assert len(declared) >= 8
+    missing = [f for f in declared if not hasattr(lib, f)]
+    assert not missing, f"declared in qma_cuda.h but not exported: {missing}"
+    unbound = [f for f in declared if f not in Q._SIGS]
+    assert not unbound, f"no ctypes signature for {unbound}"
+
+
+def test_abi_version():
+    assert Q.lib().qma_cuda_abi_version() == 1
+
+
+def test_bad_arguments_return_invalid_without_touching_the_device():
+    lib = Q.lib()
+    assert lib.qma_cuda_matvec(Q.Q4_K, None, 2048, 8, 1, None, None, None, None, None) == Q.ERR_INVALID
+    assert "qma_cuda_matvec" in Q.last_error()
+    assert lib.qma_cuda_matvec(Q.Q4_K, 1, 100, 8, 1, 1, 1, 1, 1, None) == Q.ERR_INVALID  # n_in % 256
+    assert lib.qma_cuda_q8k_quant(None, 1, 256, None, None, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_repack(Q.Q6_K, None, 4, 512, None, None) == Q.ERR_INVALID
+
+
+def test_packed_sizes():
+    # Q4_K stays in GGUF order; Q6_K / Q8_0 planes hold exactly the GGUF bytes
+    assert Q.packed_bytes(Q.Q4_K, 512, 2048) == 512 * 8 * 144
+    assert Q.packed_bytes(Q.Q6_K, 2048, 512) == 2048 * 2 * 210
+    assert Q.packed_bytes(Q.Q8_0, 151936, 2048) == 151936 * 64 * 34

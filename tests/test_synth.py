@@ -1,0 +1,30 @@
+"""CPU checks of the synthetic generator: deterministic, and the
+distributions the configs name (projections ~N(0, 0.02) before quantization,
+norms near 1, ssm_a negative)."""
+import numpy as np
+
+import oracle as O
+
+
+def test_generator_is_deterministic_and_seeded():
+    a = O.synth_matrix("blk.1.attn_q.weight", O.Q4_K, 8, 2048, seed=1)
+    b = O.synth_matrix("blk.1.attn_q.weight", O.Q4_K, 8, 2048, seed=1)
+    c = O.synth_matrix("blk.1.attn_q.weight", O.Q4_K, 8, 2048, seed=2)
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+
+
+def test_distributions():
+    W = O.synth_matrix("blk.0.ffn_gate_inp.weight", O.F32, 256, 2048).view(np.float32)
+    assert abs(W.std() - 0.02) < 0.001 and abs(W.mean()) < 0.001
+    q = O.synth_matrix("blk.0.attn_q.weight", O.Q4_K, 64, 2048)
+    deq = np.zeros(2048, np.float32)
+    vals = []
+    for r in range(64):
+        O.lib().qo_dequant_row(O._ptr(q[r]), O.Q4_K, O._ptr(deq), 2048)
+        vals.append(deq.copy())
+    v = np.concatenate(vals)
+    assert abs(v.std() - 0.02) < 0.002
+    n = O.synth_matrix("blk.0.attn_norm.weight", O.F32, 1, 2048).view(np.float32)
+    assert abs(n.mean() - 1.0) < 0.01
+    a = O.synth_matrix("blk.0.ssm_a", O.F32, 1, 32).view(np.float32)
+    assert (a < 0).all()
