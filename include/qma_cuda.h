@@ -147,6 +147,23 @@ int qma_cuda_moe_layer(const qma_cuda_moe_weights *w, const float *x2, int T,
                        float *x_out, int32_t *sel, float *wts, void *scratch,
                        size_t scratch_bytes, void *stream);
 
+/* MoE FFN block that allocates nothing, for callers that cannot allocate
+ * device memory: a host that has reserved the device's memory for its own
+ * pools and lets no library allocate, or a step loop that cannot afford
+ * cudaMalloc's implicit synchronisation.  This entry point has no
+ * counterpart in the reference (the reference's moe_ffn mallocs host
+ * buffers per call, nn.c:604).  Same computation and arguments as
+ * qma_cuda_moe_layer minus the scratch, which lives in a fixed device array
+ * inside the library (512 KB, held on every device that loads the library
+ * until the process exits).  At most QMA_CUDA_MOE_NOALLOC_MAX_T tokens per
+ * call; larger T is rejected with QMA_CUDA_ERR_INVALID.  The first call on
+ * each device looks up that device's copy of the array (make it before any
+ * stream capture on the device).  All calls share the array: calls that
+ * overlap on the GPU race and must not be issued. */
+#define QMA_CUDA_MOE_NOALLOC_MAX_T 4
+int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const float *x2, int T,
+                               float *x_out, int32_t *sel, float *wts, void *stream);
+
 /* Diagnostics of the last routing on a scratch buffer: how many tokens
  * needed the exact sequential recompute (host int, read after the stream
  * is synchronised). */

@@ -37,6 +37,7 @@ _SIGS = {
     "qma_cuda_moe_scratch_bytes": (_sz, [_i32]),
     "qma_cuda_moe_layer": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "qma_cuda_moe_exact_fallbacks": (_i32, [_vp, _i32, C.POINTER(C.c_int)]),
+    "qma_cuda_moe_layer_noalloc": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
 }
 
 
