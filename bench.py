@@ -1,16 +1,23 @@
 #!/usr/bin/env python3
-"""Benchmark of the qma B200 engine (one JSON line on rank 0).
+"""Benchmark of the qma B200 engine; rank 0 prints one JSON line.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode|gemv]
 
-Workload (single GPU; N > 1 runs one independent replica per GPU, weak
-scaling): the configs[1] quantized GEMV microbench at the LM-head shape,
-Q4_K 151936x2048 at batch 1 -- fp32 activation ~N(0,1) quantized to Q8_K on
-the GPU, then the GEMV.  A step is one quantize + GEMV; the 175 MB weight
-matrix exceeds L2 and L2 is also flushed (256 MB write) between timed steps.
+decode (default; configs[3]): the full 40-layer random-init qwen35moe
+(hidden 2048, 3 GDN + 1 gated attention x 10, 256 experts top-8 + shared,
+vocab 151936, Q4_K projections and experts, Q6_K down, Q8_0 embeddings and
+LM head) generated on the GPU; an 8192-token prompt of seeded uniform token
+ids is prefilled (untimed), then K greedy decode steps at batch 1 are timed
+with CUDA events on the engine's stream.  A step streams ~2 GB of weights
+(> L2), so no L2 flush is needed.  `e2e` times the same steps through
+qma_cuda_eval with the token from and the logits to host memory.
 
---impl reference times the reference's own CPU matmul (nn.c:307-345, built
-from its sources in oracle/_ref) on the host cores for the same shape.
+gemv: Q4_K 151936x2048 GEMV at batch 1 (quantize + GEMV).
+
+N > 1 runs one independent replica per GPU (weak scaling, no collective).
+--impl reference times the reference's own CPU code (oracle/_ref, built
+from its sources) on the host cores for the same workload.
 """
 import argparse
 import json
@@ -26,24 +33,21 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 for sub in ("qwen-mobile-agent_b200", "oracle"):
     sys.path.insert(0, os.path.join(ROOT, sub))
 
-METRIC = "Q4_K GEMV HBM GB/s vs peak (part of: qwen35moe decode tok/s (bs1, 1 GPU) & Q4_K GEMV HBM GB/s vs peak; EP tok/s @2/4/8)"
-N_OUT, N_IN = 151936, 2048
-Q4_K = 12
+BASE_METRIC = "qwen35moe decode tok/s (bs1, 1 GPU) & Q4_K GEMV HBM GB/s vs peak; EP tok/s @2/4/8"
+DECODE_METRIC = "qwen35moe decode tok/s (bs1, 1 GPU)"
+GEMV_METRIC = "Q4_K GEMV HBM GB/s vs peak"
+F32, Q8_0, Q4_K, Q6_K = 0, 8, 12, 14
+N_VOCAB = 151936
+PROMPT = 8192
+N_CTX = 65536
+SEED = 0
 
 
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return float(d["hbm_gbs"]), "measured"
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
-
-
-def algorithmic_bytes(T=1):
-    w = N_OUT * (N_IN // 256) * 144
-    act = T * (N_IN * 4 + N_IN + (N_IN // 256) * 4 + (N_IN // 16) * 2)   # x read, Q8_K written+read
-    out = T * N_OUT * 4
-    return w + act + out, w
 
 
 # ------------------------------------------------------------------ clocks --
@@ -55,9 +59,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.gpu, self.proc, self.lines = gpu_index, None, []
 
     def __enter__(self):
         try:
@@ -65,8 +67,7 @@ class ClockSampler:
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-i", str(self.gpu), "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except OSError:
             self.proc = None
         return self
@@ -103,7 +104,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- distributed --
-def dist_setup(args):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -112,7 +113,7 @@ def dist_setup(args):
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -133,190 +134,307 @@ def dist_barrier(world):
         dist.barrier()
 
 
-# -------------------------------------------------------------- CPU legs ---
-def make_weight(seed=0):
+# --------------------------------------------------------------- decode ----
+def model_layout(lm_type):
     import oracle as O
-    return O.synth_matrix("bench.lm_head", Q4_K, N_OUT, N_IN, seed=seed)
+    return O.synth_layout(embd_type=lm_type, out_type=lm_type, down_type=Q6_K, proj_type=Q4_K)
 
 
-def cpu_reference_rate(W, x, seconds=10.0, min_steps=3, threads=None):
-    """Reference CPU matmul (oracle/_ref, nn.c:307) GB/s over a bounded sample."""
+def decode_bytes_per_token(arr, n, live_positions):
+    """Algorithmic bytes one decode token moves: every non-expert tensor once
+    (projections, norms, router, LM head), one token_embd row, 8 routed + 1
+    shared expert per layer, GDN/conv state read+write, and the KV records the
+    attention reads (q4 records of K and V for both KV heads)."""
     import oracle as O
-    R = O.ref()
+    total = 0
+    for i in range(n):
+        t = arr[i]
+        name = t.name.decode()
+        if name == "token_embd.weight":
+            total += O.row_bytes(int(t.type), int(t.ne[0]))
+        elif "_exps." in name:
+            total += t.nbytes // int(t.ne[2]) * 8
+        else:
+            total += t.nbytes
+    gdn_layers = 30
+    total += gdn_layers * 2 * (32 * 128 * 128 * 4 + 8192 * 3 * 4)
+    total += 10 * live_positions * 4 * 160
+    return int(total)
+
+
+def run_decode_ours(args, world, rank, local):
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    Q.init(local)
+    arr, n, size = model_layout(Q8_0)
+    tp = C.cast(arr, C.POINTER(Q.Tensor))
+    t0 = time.time()
+    model = Q.Model(tp, n, seed=SEED, device=local)
+    torch.cuda.synchronize()
+    t_model = time.time() - t0
+    st = Q.State(model, N_CTX)
+    stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(st.h), device=local)
+    rng = np.random.default_rng(SEED + rank)
+    prompt = rng.integers(0, N_VOCAB, PROMPT).astype(np.int32)
+    t0 = time.time()
+    logits = st.eval(prompt)
+    t_prefill = time.time() - t0
+    tok = int(np.argmax(logits))
+    toks, logits = st.decode_greedy(tok, max(args.warmup, 3))
+    tok = int(np.argmax(logits))
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        toks, logits = st.decode_greedy(tok, args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist_barrier(world)
+    ms = dist_max(e0.elapsed_time(e1), world)
+    tok = int(np.argmax(logits))
+    nk_pos = st.n_pos
+    kernels, sbytes = C.c_int(0), C.c_uint64(0)
+    Q.call("qma_cuda_state_stats", st.h, C.byref(kernels), C.byref(sbytes))
+
+    # end to end: one qma_cuda_eval per token, token H2D and logits D2H
+    e2e_steps = min(args.steps, 64)
+    e2e_ms = 0.0
+    for _ in range(e2e_steps):
+        e0.record(stream)
+        logits = st.eval(np.array([tok], np.int32))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms += e0.elapsed_time(e1)
+        tok = int(np.argmax(logits))
+    e2e_ms = dist_max(e2e_ms, world)
+
+    value = world * args.steps / (ms / 1e3)
+    e2e_value = world * e2e_steps / (e2e_ms / 1e3)
+    live = min(nk_pos, 4 + 4096 + 2048) + 64
+    bpt = decode_bytes_per_token(arr, n, live)
+    peak, peak_kind = load_peaks()
+    achieved = bpt * (args.steps / (ms / 1e3)) / 1e9
+    st.close()
+    model.close()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_decode_baseline(seconds=20.0)
+    line = {
+        "metric": DECODE_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4",
+        "data": "synthetic: random-init weights (seeded N(0,0.02), engine quantizers) and uniform random prompt ids",
+        "config": {"workload": "configs[3] full qwen35moe decode bs1: 40 layers (3 GDN + 1 attn) x10, "
+                               "256 experts top-8 + shared, vocab 151936, Q4_K experts/projections, "
+                               "Q6_K down, Q8_0 embeddings + LM head; 8192-token prompt (prefill untimed), "
+                               "then greedy decode; KV ring n_ctx 65536 with 4/2-bit tiers (sink 4, hot 4096)",
+                   "model": "qwen35moe-random-init", "global_batch": 1, "seq_len": PROMPT,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "each step streams ~2 GB of weights (> 126 MB L2)",
+                   "prefill_s": round(t_prefill, 2), "model_synth_s": round(t_model, 2),
+                   "base_metric": BASE_METRIC},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "whole decode step (one CUDA graph)",
+                     "algorithmic_bytes_per_launch": bpt},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": N_VOCAB * 4},
+        "gpu_launches": int(kernels.value) * args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def host_blob_for_reference(threads):
+    """The same random-init model for the reference, with Q6_K embeddings and
+    LM head (the reference has no Q8_0 weight kernels, gguf.c:272-287)."""
+    import oracle as O
+    arr, n, size = model_layout(Q6_K)
+    blob = O.synth_blob(arr, n, size, seed=SEED, threads=threads)
+    return arr, n, size, blob
+
+
+def cpu_decode_baseline(seconds=20.0, threads=None, prompt_len=16):
+    """The reference's qma_eval (oracle/_ref) decoding on the host cores over
+    a bounded sample: a short prompt, then greedy steps for ~`seconds`."""
+    import oracle as O
+    if not O.ref_available():
+        return None
     th = threads or min(os.cpu_count() or 1, 16)
+    arr, n, size, blob = host_blob_for_reference(os.cpu_count() or 1)
+    R = O.ref()
     R.qr_init(th)
-    out = np.zeros((1, N_OUT), np.float32)
-    R.qr_matmul(O._ptr(x), O._ptr(W), N_IN, N_OUT, 1, Q4_K, O._ptr(out), th)   # warm
+    rm = R.qr_model_new(arr, n, O._ptr(blob), size)
+    rs = R.qr_state_new(4096)
+    logits = np.zeros(N_VOCAB, np.float32)
+    prompt = np.random.default_rng(SEED).integers(0, N_VOCAB, prompt_len).astype(np.int32)
+    R.qr_eval(rm, rs, O._ptr(prompt), prompt_len, O._ptr(logits), th, 0)
     steps, t0 = 0, time.perf_counter()
     while True:
-        R.qr_matmul(O._ptr(x), O._ptr(W), N_IN, N_OUT, 1, Q4_K, O._ptr(out), th)
+        one = np.array([int(np.argmax(logits))], np.int32)
+        R.qr_eval(rm, rs, O._ptr(one), 1, O._ptr(logits), th, 0)
         steps += 1
         el = time.perf_counter() - t0
-        if steps >= min_steps and el >= seconds:
+        if steps >= 3 and el >= seconds:
             break
-    b, _ = algorithmic_bytes()
-    return b * steps / el / 1e9, th, steps, el
+    R.qr_state_free(rs)
+    R.qr_model_free(rm)
+    return {"value": round(steps / el, 4), "unit": "tok/s", "cores": th, "kind": "reference",
+            "sample": f"{steps} greedy decode tokens after a {prompt_len}-token prompt, {el:.1f} s, "
+                      f"reference qma_eval (nn.c:2056) with {th} pool threads; Q6_K LM head "
+                      f"(the reference has no Q8_0 kernels)"}
 
 
-def run_reference(args, world, rank):
+def run_decode_reference(args, world, rank):
     if rank != 0:
         return
     import oracle as O
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent at build time)"}))
         return
-    W = make_weight()
-    x = np.random.default_rng(0).standard_normal((1, N_IN)).astype(np.float32)
     th = min(os.cpu_count() or 1, 16)
+    arr, n, size, blob = host_blob_for_reference(os.cpu_count() or 1)
     R = O.ref()
     R.qr_init(th)
-    out = np.zeros((1, N_OUT), np.float32)
+    rm = R.qr_model_new(arr, n, O._ptr(blob), size)
+    rs = R.qr_state_new(4096)
+    logits = np.zeros(N_VOCAB, np.float32)
+    prompt = np.random.default_rng(SEED).integers(0, N_VOCAB, 16).astype(np.int32)
+    R.qr_eval(rm, rs, O._ptr(prompt), len(prompt), O._ptr(logits), th, 0)
     for _ in range(args.warmup):
-        R.qr_matmul(O._ptr(x), O._ptr(W), N_IN, N_OUT, 1, Q4_K, O._ptr(out), th)
+        one = np.array([int(np.argmax(logits))], np.int32)
+        R.qr_eval(rm, rs, O._ptr(one), 1, O._ptr(logits), th, 0)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        R.qr_matmul(O._ptr(x), O._ptr(W), N_IN, N_OUT, 1, Q4_K, O._ptr(out), th)
+        one = np.array([int(np.argmax(logits))], np.int32)
+        R.qr_eval(rm, rs, O._ptr(one), 1, O._ptr(logits), th, 0)
     el = time.perf_counter() - t0
-    b, _ = algorithmic_bytes()
-    v = b * args.steps / el / 1e9
+    v = args.steps / el
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
+        "impl": "reference", "metric": DECODE_METRIC, "value": round(v, 4), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4", "data": "synthetic",
-        "config": {"workload": "configs[1] Q4_K GEMV 151936x2048 batch 1 (reference CPU matmul, nn.c:307)"},
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": th, "kind": "reference",
-                         "sample": f"{args.steps} steps of the full 151936x2048 matmul"},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xq4", "data": "synthetic",
+        "config": {"workload": "configs[3] qwen35moe decode bs1 on the reference's CPU qma_eval "
+                               "(16-token prompt, Q6_K LM head: the reference has no Q8_0 kernels)",
+                   "model": "qwen35moe-random-init", "global_batch": 1},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": th, "kind": "reference",
+                         "sample": f"{args.steps} greedy decode steps after a 16-token prompt"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
-# ----------------------------------------------------------------- GPU leg --
-def run_ours(args, world, rank, local):
+# ------------------------------------------------------------------ gemv ---
+GN_OUT, GN_IN = 151936, 2048
+
+
+def gemv_bytes():
+    w = GN_OUT * (GN_IN // 256) * 144
+    return w + GN_IN * 4 + GN_IN + (GN_IN // 256) * 4 + (GN_IN // 16) * 2 + GN_OUT * 4
+
+
+def run_gemv_ours(args, world, rank, local):
     import torch
+    import oracle as O
     import qma_cuda as Q
     Q.init(local)
     dev = torch.device("cuda", local)
-    W = make_weight()
-    rng = np.random.default_rng(rank)
-    x = rng.standard_normal((1, N_IN)).astype(np.float32)
-
-    dW = torch.from_numpy(W).to(dev)
-    dx = torch.from_numpy(x).to(dev)
-    dq = torch.empty((1, N_IN), dtype=torch.int8, device=dev)
-    dd = torch.empty((1, N_IN // 256), dtype=torch.float32, device=dev)
-    ds = torch.empty((1, N_IN // 16), dtype=torch.int16, device=dev)
-    out = torch.empty((1, N_OUT), dtype=torch.float32, device=dev)
+    W = O.synth_matrix("bench.lm_head", Q4_K, GN_OUT, GN_IN, seed=0)
+    x = np.random.default_rng(rank).standard_normal((1, GN_IN)).astype(np.float32)
+    dW, dx = torch.from_numpy(W).to(dev), torch.from_numpy(x).to(dev)
+    dq = torch.empty((1, GN_IN), dtype=torch.int8, device=dev)
+    dd = torch.empty((1, GN_IN // 256), dtype=torch.float32, device=dev)
+    ds = torch.empty((1, GN_IN // 16), dtype=torch.int16, device=dev)
+    out = torch.empty((1, GN_OUT), dtype=torch.float32, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
-    def step():
-        Q.call("qma_cuda_q8k_quant", Q.ptr(dx), 1, N_IN, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds), sp)
-        Q.call("qma_cuda_matvec", Q4_K, Q.ptr(dW), N_IN, N_OUT, 1, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
+    def quant():
+        Q.call("qma_cuda_q8k_quant", Q.ptr(dx), 1, GN_IN, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds), sp)
+
+    def gemv():
+        Q.call("qma_cuda_matvec", Q4_K, Q.ptr(dW), GN_IN, GN_OUT, 1, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
                Q.ptr(out), sp)
 
     for _ in range(max(args.warmup, 3)):
-        step()
-        flush.zero_()
+        quant(); gemv(); flush.zero_()
     torch.cuda.synchronize()
-
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     with ClockSampler(local) as clk:
-        # keep the GPU busy ~0.5 s before the timed region so the sampler sees it
         t_end = time.time() + 0.5
         while time.time() < t_end:
-            step()
-            flush.zero_()
+            quant(); gemv(); flush.zero_()
         torch.cuda.synchronize()
         dist_barrier(world)
         torch.cuda.synchronize()
         for i in range(args.steps):
-            ev[i][0].record(stream)
-            Q.call("qma_cuda_q8k_quant", Q.ptr(dx), 1, N_IN, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds), sp)
-            ev[i][1].record(stream)
-            Q.call("qma_cuda_matvec", Q4_K, Q.ptr(dW), N_IN, N_OUT, 1, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
-                   Q.ptr(out), sp)
-            ev[i][2].record(stream)
+            ev[i][0].record(stream); quant(); ev[i][1].record(stream); gemv(); ev[i][2].record(stream)
             flush.zero_()
         torch.cuda.synchronize()
         dist_barrier(world)
-        torch.cuda.synchronize()
-    step_ms = sum(e[0].elapsed_time(e[2]) for e in ev)
+    step_ms = dist_max(sum(e[0].elapsed_time(e[2]) for e in ev), world)
     gemv_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
-    step_ms = dist_max(step_ms, world)
-
-    # end to end through the C ABI with host buffers: H2D of x, quantize,
-    # GEMV, D2H of the logits row, every step
     hx = torch.from_numpy(x).pin_memory()
-    hout = torch.empty((1, N_OUT), dtype=torch.float32).pin_memory()
-    for _ in range(3):
-        dx.copy_(hx, non_blocking=True); step(); hout.copy_(out, non_blocking=True)
-    torch.cuda.synchronize()
+    hout = torch.empty((1, GN_OUT), dtype=torch.float32).pin_memory()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_ms = 0.0
     for _ in range(args.steps):
         flush.zero_()
         e0.record(stream)
-        dx.copy_(hx, non_blocking=True)
-        step()
-        hout.copy_(out, non_blocking=True)
+        dx.copy_(hx, non_blocking=True); quant(); gemv(); hout.copy_(out, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms += e0.elapsed_time(e1)
     e2e_ms = dist_max(e2e_ms, world)
-
-    b, wbytes = algorithmic_bytes()
-    value = world * b * args.steps / (step_ms / 1e3) / 1e9
-    e2e_value = world * b * args.steps / (e2e_ms / 1e3) / 1e9
+    b = gemv_bytes()
     peak, peak_kind = load_peaks()
     achieved = b / (gemv_ms / args.steps / 1e3) / 1e9
-
     if rank != 0:
         return
-    cpu = None
-    if world == 1 and not args.no_cpu:
-        import oracle as O
-        if O.ref_available():
-            v, th, n, el = cpu_reference_rate(W, x)
-            cpu = {"value": round(v, 3), "unit": "GB/s", "cores": th, "kind": "reference",
-                   "sample": f"{n} full 151936x2048 Q4_K matmuls in {el:.1f} s (reference nn.c:307, {th} pool threads)"}
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms / args.steps, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4",
-        "data": "synthetic",
-        "config": {"workload": "configs[1] Q4_K GEMV 151936x2048 (LM-head shape), batch 1; "
-                               "weights N(0,0.02) quantized by the engine's Q4_K quantizer",
-                   "l2": "weights 175 MB > L2; 256 MB L2 flush between timed steps",
-                   "parallelism": f"replicas x{world}"},
+    print(json.dumps({
+        "metric": GEMV_METRIC, "value": round(world * b * args.steps / (step_ms / 1e3) / 1e9, 2),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xq4", "data": "synthetic",
+        "config": {"workload": "configs[1] Q4_K GEMV 151936x2048, batch 1",
+                   "l2": "256 MB L2 flush between timed steps", "base_metric": BASE_METRIC},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
-                     "peak_kind": peak_kind, "kernel": "gemv_kernel<FmtQ4K,1,32,1>",
-                     "algorithmic_bytes_per_launch": b},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": N_IN * 4,
-                "d2h_bytes_per_step": N_OUT * 4},
-        "gpu_launches": 2 * args.steps,
-        "clocks": clk.summary(),
-        "cpu_baseline": cpu,
-    }
-    print(json.dumps(line))
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "gemv_kernel<FmtQ4K,1,32,1,2>", "algorithmic_bytes_per_launch": b},
+        "e2e": {"value": round(world * b * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": GN_IN * 4, "d2h_bytes_per_step": GN_OUT * 4},
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
+    }), flush=True)
 
 
+# ------------------------------------------------------------------ main ---
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
-    world, rank, local = dist_setup(args)
+    world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
-            run_reference(args, world, rank)
+            if args.workload == "decode":
+                run_decode_reference(args, world, rank)
+            else:
+                print(json.dumps({"impl": "reference", "unavailable": "gemv reference arm: use --workload decode"}))
+        elif args.workload == "decode":
+            run_decode_ours(args, world, rank, local)
         else:
-            run_ours(args, world, rank, local)
+            run_gemv_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

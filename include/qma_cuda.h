@@ -105,6 +105,74 @@ int qma_cuda_dot_partials(int wtype, const void *W, int n_in, int n_out,
 int qma_cuda_synth_tensor(const char *name, int type, uint64_t nelem, uint64_t seed,
                           void *dst, void *stream);
 
+/* ---- model and sequence state (the qma_eval boundary) ---------------------
+ * One tensor of a GGUF data section, the layout of tensor_t (qma.h:155-161):
+ * ne[0] is the row length, ne[1] the rows, ne[2] the experts; `off` is the
+ * byte offset in the data section.  Names are the reference's GGUF names
+ * (gguf.c:308-345); types F32 / Q4_K / Q6_K / Q8_0. */
+typedef struct {
+    char     name[64];
+    uint32_t type;
+    int64_t  ne[3];
+    uint64_t off;
+    uint64_t nbytes;
+} qma_cuda_tensor;
+
+typedef struct qma_cuda_model qma_cuda_model;   /* device-resident weights */
+typedef struct qma_cuda_state qma_cuda_state;   /* one sequence's state    */
+
+/* Replaces qma_load (gguf.c:104-513) for the weights: uploads every tensor
+ * the forward uses from a host data section (e.g. an mmapped GGUF) into HBM
+ * in the engine's layout.  The hyper-parameters are qwen35moe's (qma.h:28-64);
+ * n_vocab comes from token_embd.weight. */
+int qma_cuda_model_load(int device, const qma_cuda_tensor *tensors, uint32_t n,
+                        const void *host_data, uint64_t data_size, qma_cuda_model **out);
+/* Same model with random-init weights generated on the device
+ * (qma_cuda_synth_tensor per tensor): no host copy of the weights. */
+int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n,
+                         uint64_t seed, qma_cuda_model **out);
+int qma_cuda_model_free(qma_cuda_model *m);
+int qma_cuda_model_n_vocab(const qma_cuda_model *m);
+/* Replaces qma_ecache_get (ecache.h:95, ecache.c:414-498): the expert
+ * record of (layer, expert) is HBM-resident; returns device pointers to its
+ * gate / up (Q4_K rows) and down (packed) matrices.  Never fails for valid
+ * ids; there is nothing to hint or prefetch (qma_ecache_hint/prefetch have
+ * no work to do when every expert is resident). */
+int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const void **gate,
+                        const void **up, const void **down);
+
+/* Replaces runstate_init_kv (nn.c:1878-1979) plus the HCM statics
+ * (nn.c:912-937): KV ring of n_ctx slots (4-bit + 2-bit records, 240 B per
+ * head and position), conv/ssm state, salience and heavy-hitter arena, all in
+ * HBM, zero-initialised. */
+int qma_cuda_state_create(qma_cuda_model *m, int n_ctx, qma_cuda_state **out);
+int qma_cuda_state_free(qma_cuda_state *s);
+int qma_cuda_state_n_pos(const qma_cuda_state *s);
+
+/* Replaces qma_eval (qma.h:327-328, nn.c:2056-2308): runs n_tokens host
+ * token ids through the model in chunks of up to 512, appending to the KV
+ * ring and recurrent state; writes the last token's logits (n_vocab floats,
+ * host) or, with logits_all, every token's (n_tokens * n_vocab).  logits may
+ * be NULL. */
+int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n_tokens,
+                  float *logits, int logits_all);
+
+/* Greedy decode kept on the device: feeds `token`, then each step's argmax
+ * (lowest id on ties), for n_steps steps; step i's input token goes to
+ * tokens_out[i] (host, optional) and the last step's logits to logits
+ * (host, optional).  Each step is one replay of a captured CUDA graph; the
+ * host intervenes only when the HCM live index is rebuilt (every 128
+ * positions, nn.c:2074-2088). */
+int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,
+                           int *tokens_out, float *logits);
+
+/* The CUDA stream (cudaStream_t as void*) every call on this state runs on,
+ * for callers that time or order work against it. */
+void *qma_cuda_state_stream(const qma_cuda_state *s);
+/* Kernel launches in one captured decode step (0 before the first capture),
+ * and the bytes of device memory the state holds. */
+int qma_cuda_state_stats(const qma_cuda_state *s, int *graph_kernels, uint64_t *state_bytes);
+
 /* ---- MoE FFN block ------------------------------------------------------
  * Replaces moe_ffn (nn.c:509-649) with its q8k expert kernels
  * (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473, the

@@ -102,7 +102,7 @@ def lib() -> C.CDLL:
             getattr(L, fn).restype = f32
         for fn in ("qo_kvq4_vacc", "qo_kvq2_vacc"):
             getattr(L, fn).argtypes = [vp, f32, vp]
-        L.qo_set_threads(min(os.cpu_count() or 1, 16))
+        L.qo_set_threads(min(os.cpu_count() or 1, 64))
         _lib = L
     return _lib
 

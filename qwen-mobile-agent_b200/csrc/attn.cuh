@@ -1,0 +1,37 @@
+// attn.cuh -- launch interface of the quantized-KV attention kernels (attn.cu).
+#pragma once
+#include "common.cuh"
+#include "layers.cuh"
+
+namespace qma {
+
+struct AttnArgs {
+    const float *qr;          // [T][16][256] normed, rotated queries
+    const uint8_t *kv;        // layer KV slab [4 heads][n_ctx][240]
+    const uint8_t *arena;     // layer heavy-hitter arena [4 heads][2048][240]
+    const int *live;          // live index (device)
+    const StepParams *sp;
+    int T;
+    int nk_max;               // attended positions of the last query
+    int pv_chunk;             // positions per softmax.V CTA
+    float *scores;            // [T][16][nk_max]
+    float *cmax;              // [T][16][ceil(nk_max/64)]
+    float *opart;             // [T][16][nchunk][256]
+    float *lpart;             // [T][16][nchunk]
+    float *ml;                // [T][16][2] max, sum of p
+    const float *z;           // [T][4096] gate
+    int8_t *xq;               // [T][4096] Q8_K of the gated output
+    float *xd;
+    int16_t *xs;
+    float *sal;               // this layer's ring salience [n_ctx]
+    float *pin_sal;           // this layer's arena salience [2048]
+};
+
+int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const float *kn,
+                          const float *rope, const StepParams *sp, int T, float *qr, float *z,
+                          uint8_t *kv, float *qf, float *sal, cudaStream_t st);
+int launch_attention(const AttnArgs &a, cudaStream_t st);
+int launch_arena_copy(const int2 *pairs, int n, uint8_t *const *kv, uint8_t *const *arena,
+                      const float *sal, float *pin_sal, int n_ctx, cudaStream_t st);
+
+}  // namespace qma

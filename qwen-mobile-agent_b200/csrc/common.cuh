@@ -88,6 +88,8 @@ inline Q8Planes q8_planes(const void *base, int rows, int n) {
     return P;
 }
 size_t packed_bytes(int wtype, int rows, int n);
+// GGUF-order device matrix -> packed layout (api.cu)
+int repack(int wtype, const void *src, int rows, int n, void *dst, cudaStream_t st);
 
 // ------------------------------------------------------------ device helpers
 // Streaming 16-byte load of weights: read once per step, keep out of L1.

@@ -1,0 +1,919 @@
+// engine.cu -- the qma_eval replacement: device-resident qwen35moe weights,
+// per-sequence state (KV ring, recurrent state, HCM tiers) and the forward
+// loop, for prefill chunks and CUDA-graph decode steps.
+//
+// Reference: qma_eval (nn.c:2056-2308), runstate_init_kv (nn.c:1878-1979),
+// hcm_rebuild (nn.c:981-1150), embed_row (nn.c:2044-2054), qma_load's tensor
+// resolution (gguf.c:302-345).
+#include <math.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "attn.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "layers.cuh"
+#include "moe.cuh"
+#include "synth.cuh"
+
+namespace qma {
+
+constexpr int HCM_W_HOT = 4096, HCM_W_GIST = 32768, HCM_REBUILD = 128;   // nn.c:894-901
+constexpr float HCM_QF_BIAS = 2.0f;
+
+struct LayerW {
+    const float *attn_norm = nullptr, *post_norm = nullptr;
+    void *in_proj = nullptr;       // GDN: qkv | gate | beta | alpha ; attn: q | k | v
+    int in_type = 0, in_rows = 0;
+    void *out_proj = nullptr;      // ssm_out / attn_output, 4096 -> 2048
+    int out_type = 0;
+    const float *conv1d = nullptr, *dt = nullptr, *a = nullptr, *ssm_norm = nullptr;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+    qma_cuda_moe_weights moe{};
+};
+
+}  // namespace qma
+
+struct qma_cuda_model {
+    int device = 0;
+    int n_vocab = 0;
+    std::vector<void *> allocs;
+    void *embd = nullptr;
+    int embd_type = 0;
+    void *out = nullptr;
+    int out_type = 0;
+    const float *out_norm = nullptr;
+    qma::LayerW L[qma::NLAYER];
+    size_t weight_bytes = 0;
+};
+
+struct qma_cuda_state {
+    qma_cuda_model *m = nullptr;
+    int n_ctx = 0, n_pos = 0;
+    cudaStream_t st = nullptr;
+    std::vector<void *> allocs;
+    // device state
+    float *conv[qma::NLAYER] = {};
+    float *ssm[qma::NLAYER] = {};
+    uint8_t *kv[qma::NATTN] = {};
+    uint8_t *arena[qma::NATTN] = {};
+    uint8_t **kv_dev = nullptr, **arena_dev = nullptr;
+    float *sal = nullptr;       // [10][n_ctx]
+    float *pin_sal = nullptr;   // [10][2048]
+    float *qf = nullptr;        // [n_ctx]
+    int *live_dev = nullptr;    // [n_ctx]
+    float *rope = nullptr;      // [n_ctx][32 cos | 32 sin]
+    qma::StepParams *sp_dev = nullptr, *sp_host = nullptr;
+    // activations, sized for MAX_CHUNK tokens
+    int *tokens_dev = nullptr;
+    float *x = nullptr, *x2 = nullptr, *proj = nullptr, *conv_out = nullptr, *gdo = nullptr;
+    float *qr = nullptr, *z = nullptr;
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int16_t *xs = nullptr;
+    void *moe_scratch = nullptr;
+    size_t moe_scratch_bytes = 0;
+    float *logits = nullptr;    // [MAX_CHUNK][n_vocab] (logits_all) or [1][n_vocab]
+    int logits_rows = 0;
+    int *argmax_dev = nullptr;
+    // attention scratch, grown on demand
+    float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr, *ml = nullptr;
+    size_t scores_cap = 0, cmax_cap = 0, opart_cap = 0, lpart_cap = 0;
+    int2 *pairs_dev = nullptr;
+    // host mirror of the HCM bookkeeping (nn.c:912-937)
+    std::vector<int> live;
+    std::vector<uint8_t> tier;
+    std::vector<int> pin_pos;
+    int live_n = 0, n4 = 0, n_ring_q4 = 0, rebuilt_at = 0, next_rebuild = HCM_REBUILD_INIT;
+    std::vector<float> h_sal, h_qf, h_pin_sal;
+    // decode graph
+    cudaGraphExec_t graph = nullptr;
+    int graph_nk = -1;
+    int graph_kernels = 0;
+    size_t state_bytes = 0;
+    static constexpr int HCM_REBUILD_INIT = 128;
+};
+
+namespace qma {
+
+// ------------------------------------------------------------------ model --
+static const qma_cuda_tensor *find_tensor(const qma_cuda_tensor *t, uint32_t n, const char *name) {
+    for (uint32_t i = 0; i < n; i++)
+        if (strncmp(t[i].name, name, sizeof(t[i].name)) == 0) return &t[i];
+    return nullptr;
+}
+
+static size_t gguf_row_bytes(int type, int64_t n) {
+    switch (type) {
+    case QMA_TYPE_Q4_K: return size_t(n / 256) * Q4K_BYTES;
+    case QMA_TYPE_Q6_K: return size_t(n / 256) * Q6K_BYTES;
+    case QMA_TYPE_Q8_0: return size_t(n / 32) * Q80_BYTES;
+    case QMA_TYPE_F32: return size_t(n) * 4;
+    default: return 0;
+    }
+}
+
+struct Loader {
+    qma_cuda_model *m;
+    const qma_cuda_tensor *t;
+    uint32_t n;
+    const uint8_t *host;
+    uint64_t host_size;
+    bool synth;
+    uint64_t seed;
+    cudaStream_t st;
+    uint8_t *tmp = nullptr;
+    size_t tmp_cap = 0;
+
+    int dalloc(void **p, size_t bytes) {
+        QMA_CHECK_CUDA(cudaMalloc(p, bytes ? bytes : 16));
+        m->allocs.push_back(*p);
+        m->weight_bytes += bytes;
+        return QMA_CUDA_OK;
+    }
+    // GGUF bytes of a tensor into device memory at dst (H2D or generated)
+    int fetch(const qma_cuda_tensor *x, void *dst) {
+        const uint64_t nel = uint64_t(x->ne[0]) * uint64_t(x->ne[1] ? x->ne[1] : 1) *
+                             uint64_t(x->ne[2] ? x->ne[2] : 1);
+        const size_t bytes = gguf_row_bytes(x->type, x->ne[0]) * (nel / uint64_t(x->ne[0]));
+        if (synth) return synth_tensor_gguf(x->name, int(x->type), nel, seed, dst, st);
+        if (x->off + bytes > host_size) {
+            set_error("model_load: tensor %s out of the data section", x->name);
+            return QMA_CUDA_ERR_INVALID;
+        }
+        QMA_CHECK_CUDA(cudaMemcpyAsync(dst, host + x->off, bytes, cudaMemcpyHostToDevice, st));
+        return QMA_CUDA_OK;
+    }
+    const qma_cuda_tensor *need(const char *name, int *rc) {
+        const qma_cuda_tensor *x = find_tensor(t, n, name);
+        if (!x) {
+            set_error("model_load: missing tensor %s", name);
+            *rc = QMA_CUDA_ERR_INVALID;
+        }
+        return x;
+    }
+    int ensure_tmp(size_t bytes) {
+        if (bytes <= tmp_cap) return QMA_CUDA_OK;
+        if (tmp) {
+            QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+            cudaFree(tmp);
+        }
+        QMA_CHECK_CUDA(cudaMalloc(&tmp, bytes));
+        tmp_cap = bytes;
+        return QMA_CUDA_OK;
+    }
+    // F32 vector / matrix, kept as is
+    int f32(const char *name, const float **out) {
+        int rc = 0;
+        const qma_cuda_tensor *x = need(name, &rc);
+        if (rc) return rc;
+        if (x->type != QMA_TYPE_F32) {
+            set_error("model_load: %s must be F32", name);
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
+        void *d;
+        const size_t bytes = size_t(x->ne[0]) * (x->ne[1] ? x->ne[1] : 1) * 4;
+        if ((rc = dalloc(&d, bytes))) return rc;
+        if ((rc = fetch(x, d))) return rc;
+        *out = static_cast<const float *>(d);
+        return QMA_CUDA_OK;
+    }
+    // quantized matrices stacked along rows (all of one type), packed
+    int stacked(const std::vector<std::string> &names, void **out, int *type, int *rows_out) {
+        int rc = 0;
+        std::vector<const qma_cuda_tensor *> xs;
+        int64_t rows = 0, ncols = -1;
+        int ty = -1;
+        for (auto &nm : names) {
+            const qma_cuda_tensor *x = need(nm.c_str(), &rc);
+            if (rc) return rc;
+            if (ty < 0) { ty = int(x->type); ncols = x->ne[0]; }
+            if (int(x->type) != ty || x->ne[0] != ncols) {
+                set_error("model_load: %s differs in type/width from %s", nm.c_str(), names[0].c_str());
+                return QMA_CUDA_ERR_UNSUPPORTED;
+            }
+            rows += x->ne[1];
+            xs.push_back(x);
+        }
+        const size_t rb = gguf_row_bytes(ty, ncols);
+        if ((rc = ensure_tmp(rb * size_t(rows)))) return rc;
+        size_t o = 0;
+        for (auto *x : xs) {
+            if ((rc = fetch(x, tmp + o))) return rc;
+            o += rb * size_t(x->ne[1]);
+        }
+        void *d;
+        if ((rc = dalloc(&d, packed_bytes(ty, int(rows), int(ncols))))) return rc;
+        if ((rc = repack(ty, tmp, int(rows), int(ncols), d, st))) return rc;
+        *out = d;
+        *type = ty;
+        if (rows_out) *rows_out = int(rows);
+        return QMA_CUDA_OK;
+    }
+    // 3-D expert tensor [ne2 experts][ne1 rows][ne0]: one packed matrix each
+    int experts(const char *name, void **out, int *type) {
+        int rc = 0;
+        const qma_cuda_tensor *x = need(name, &rc);
+        if (rc) return rc;
+        const int rows = int(x->ne[1]), cols = int(x->ne[0]), ne = int(x->ne[2]);
+        const size_t gb = gguf_row_bytes(int(x->type), cols) * rows;
+        const size_t pb = packed_bytes(int(x->type), rows, cols);
+        if ((rc = ensure_tmp(gb * ne))) return rc;
+        if ((rc = fetch(x, tmp))) return rc;
+        void *d;
+        if ((rc = dalloc(&d, pb * ne))) return rc;
+        for (int e = 0; e < ne; e++)
+            if ((rc = repack(int(x->type), tmp + gb * e, rows, cols, static_cast<uint8_t *>(d) + pb * e, st)))
+                return rc;
+        *out = d;
+        *type = int(x->type);
+        return QMA_CUDA_OK;
+    }
+};
+
+static int build_model(int device, const qma_cuda_tensor *t, uint32_t n, const void *host,
+                       uint64_t host_size, bool synth, uint64_t seed, qma_cuda_model **out) {
+    QMA_REQUIRE(t && n > 0 && out && (synth || host), "model: bad arguments");
+    QMA_CHECK_CUDA(cudaSetDevice(device));
+    qma_cuda_model *m = new qma_cuda_model();
+    m->device = device;
+    cudaStream_t st;
+    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    Loader ld{m, t, n, static_cast<const uint8_t *>(host), host_size, synth, seed, st};
+    int rc = 0;
+    char nm[96];
+    auto fail = [&](int code) {
+        cudaStreamSynchronize(st);
+        if (ld.tmp) cudaFree(ld.tmp);
+        cudaStreamDestroy(st);
+        for (void *p : m->allocs) cudaFree(p);
+        delete m;
+        return code;
+    };
+    const qma_cuda_tensor *te = find_tensor(t, n, "token_embd.weight");
+    if (!te || te->ne[0] != EMBD) {
+        set_error("model: token_embd.weight missing or not %d wide", EMBD);
+        return fail(QMA_CUDA_ERR_INVALID);
+    }
+    m->n_vocab = int(te->ne[1]);
+    int rows;
+    if ((rc = ld.stacked({"token_embd.weight"}, &m->embd, &m->embd_type, &rows))) return fail(rc);
+    if ((rc = ld.stacked({"output.weight"}, &m->out, &m->out_type, &rows))) return fail(rc);
+    if ((rc = ld.f32("output_norm.weight", &m->out_norm))) return fail(rc);
+    for (int il = 0; il < NLAYER; il++) {
+        LayerW &L = m->L[il];
+        auto N = [&](const char *s) { snprintf(nm, sizeof(nm), "blk.%d.%s", il, s); return std::string(nm); };
+        if ((rc = ld.f32(N("attn_norm.weight").c_str(), &L.attn_norm))) return fail(rc);
+        if ((rc = ld.f32(N("post_attention_norm.weight").c_str(), &L.post_norm))) return fail(rc);
+        if (is_attn(il)) {
+            if ((rc = ld.stacked({N("attn_q.weight"), N("attn_k.weight"), N("attn_v.weight")},
+                                 &L.in_proj, &L.in_type, &L.in_rows))) return fail(rc);
+            if ((rc = ld.stacked({N("attn_output.weight")}, &L.out_proj, &L.out_type, &rows))) return fail(rc);
+            if ((rc = ld.f32(N("attn_q_norm.weight").c_str(), &L.q_norm))) return fail(rc);
+            if ((rc = ld.f32(N("attn_k_norm.weight").c_str(), &L.k_norm))) return fail(rc);
+        } else {
+            if ((rc = ld.stacked({N("attn_qkv.weight"), N("attn_gate.weight"), N("ssm_beta.weight"),
+                                  N("ssm_alpha.weight")}, &L.in_proj, &L.in_type, &L.in_rows))) return fail(rc);
+            if ((rc = ld.stacked({N("ssm_out.weight")}, &L.out_proj, &L.out_type, &rows))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_conv1d.weight").c_str(), &L.conv1d))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_dt.bias").c_str(), &L.dt))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_a").c_str(), &L.a))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_norm.weight").c_str(), &L.ssm_norm))) return fail(rc);
+        }
+        qma_cuda_moe_weights &w = L.moe;
+        w.post_norm = L.post_norm;
+        if ((rc = ld.f32(N("ffn_gate_inp.weight").c_str(), &w.gate_inp))) return fail(rc);
+        if ((rc = ld.f32(N("ffn_gate_inp_shexp.weight").c_str(), &w.gate_inp_shexp))) return fail(rc);
+        int ty;
+        void *p;
+        if ((rc = ld.experts(N("ffn_gate_exps.weight").c_str(), &p, &ty))) return fail(rc);
+        w.gate_exps = p;
+        if ((rc = ld.experts(N("ffn_up_exps.weight").c_str(), &p, &ty))) return fail(rc);
+        w.up_exps = p;
+        if (ty != QMA_TYPE_Q4_K) { set_error("model: expert gate/up must be Q4_K"); return fail(QMA_CUDA_ERR_UNSUPPORTED); }
+        if ((rc = ld.experts(N("ffn_down_exps.weight").c_str(), &p, &w.down_type))) return fail(rc);
+        w.down_exps = p;
+        if ((rc = ld.stacked({N("ffn_gate_shexp.weight")}, &p, &ty, &rows))) return fail(rc);
+        w.gate_shexp = p;
+        if ((rc = ld.stacked({N("ffn_up_shexp.weight")}, &p, &ty, &rows))) return fail(rc);
+        w.up_shexp = p;
+        if ((rc = ld.stacked({N("ffn_down_shexp.weight")}, &p, &w.down_shexp_type, &rows))) return fail(rc);
+        w.down_shexp = p;
+    }
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if (ld.tmp) cudaFree(ld.tmp);
+    cudaStreamDestroy(st);
+    *out = m;
+    return QMA_CUDA_OK;
+}
+
+// ------------------------------------------------------------------ state --
+static int salloc(qma_cuda_state *s, void **p, size_t bytes, cudaStream_t st) {
+    QMA_CHECK_CUDA(cudaMalloc(p, bytes ? bytes : 16));
+    s->allocs.push_back(*p);
+    s->state_bytes += bytes;
+    QMA_CHECK_CUDA(cudaMemsetAsync(*p, 0, bytes ? bytes : 16, st));
+    return QMA_CUDA_OK;
+}
+
+template <class T>
+static int salloc_t(qma_cuda_state *s, T **p, size_t count, cudaStream_t st) {
+    void *v;
+    const int rc = salloc(s, &v, sizeof(T) * count, st);
+    *p = static_cast<T *>(v);
+    return rc;
+}
+
+static int grow(float **p, size_t *cap, size_t need) {
+    if (need <= *cap) return QMA_CUDA_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    QMA_CHECK_CUDA(cudaMalloc(p, need * sizeof(float)));
+    *cap = need;
+    return QMA_CUDA_OK;
+}
+
+static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
+    QMA_REQUIRE(m && out && n_ctx > HCM_SINK + 1, "state: bad arguments (n_ctx %d)", n_ctx);
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    qma_cuda_state *s = new qma_cuda_state();
+    s->m = m;
+    s->n_ctx = n_ctx;
+    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    cudaStream_t st = s->st;
+    int rc = 0;
+#define TRY(x) do { if ((rc = (x))) return rc; } while (0)
+    for (int il = 0; il < NLAYER; il++) {
+        if (is_attn(il)) {
+            TRY(salloc_t(s, &s->kv[il / 4], size_t(2) * NHEAD_KV * n_ctx * KVQ_SLOT, st));
+            TRY(salloc_t(s, &s->arena[il / 4], size_t(2) * NHEAD_KV * HCM_H_PIN * KVQ_SLOT, st));
+        } else {
+            TRY(salloc_t(s, &s->conv[il], size_t(CONV_DIM) * 3, st));
+            TRY(salloc_t(s, &s->ssm[il], size_t(VHEADS) * SSTATE * SSTATE, st));
+        }
+    }
+    TRY(salloc_t(s, &s->kv_dev, NATTN, st));
+    TRY(salloc_t(s, &s->arena_dev, NATTN, st));
+    QMA_CHECK_CUDA(cudaMemcpyAsync(s->kv_dev, s->kv, sizeof(s->kv), cudaMemcpyHostToDevice, st));
+    QMA_CHECK_CUDA(cudaMemcpyAsync(s->arena_dev, s->arena, sizeof(s->arena), cudaMemcpyHostToDevice, st));
+    TRY(salloc_t(s, &s->sal, size_t(NATTN) * n_ctx, st));
+    TRY(salloc_t(s, &s->pin_sal, size_t(NATTN) * HCM_H_PIN, st));
+    TRY(salloc_t(s, &s->qf, size_t(n_ctx), st));
+    TRY(salloc_t(s, &s->live_dev, size_t(n_ctx), st));
+    TRY(salloc_t(s, &s->pairs_dev, size_t(HCM_H_PIN), st));
+    // IMROPE table (rope_imrope, nn.c:841-861), computed with the host libm
+    // exactly as the reference does: theta_0 = p, theta_{j+1} = theta_j * s
+    {
+        std::vector<float> tab(size_t(n_ctx) * NROT);
+        const float theta_scale = powf(10000000.0f, -2.0f / NROT);
+        for (int p = 0; p < n_ctx; p++) {
+            float theta = float(p);
+            for (int j = 0; j < NROT / 2; j++) {
+                tab[size_t(p) * NROT + j] = cosf(theta);
+                tab[size_t(p) * NROT + NROT / 2 + j] = sinf(theta);
+                theta *= theta_scale;
+            }
+        }
+        TRY(salloc_t(s, &s->rope, tab.size(), st));
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st));
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    }
+    TRY(salloc_t(s, &s->sp_dev, 1, st));
+    QMA_CHECK_CUDA(cudaMallocHost(&s->sp_host, sizeof(StepParams)));
+    const int TM = MAX_CHUNK;
+    TRY(salloc_t(s, &s->tokens_dev, TM, st));
+    TRY(salloc_t(s, &s->x, size_t(TM) * EMBD, st));
+    TRY(salloc_t(s, &s->x2, size_t(TM) * EMBD, st));
+    TRY(salloc_t(s, &s->proj, size_t(TM) * (CONV_DIM + VAL_DIM + 2 * VHEADS), st));
+    TRY(salloc_t(s, &s->conv_out, size_t(TM) * CONV_DIM, st));
+    TRY(salloc_t(s, &s->gdo, size_t(TM) * VAL_DIM, st));
+    TRY(salloc_t(s, &s->qr, size_t(TM) * NHEAD * HEAD_DIM, st));
+    TRY(salloc_t(s, &s->z, size_t(TM) * WO_DIM, st));
+    TRY(salloc_t(s, &s->xq, size_t(TM) * VAL_DIM, st));
+    TRY(salloc_t(s, &s->xd, size_t(TM) * VAL_DIM / 256, st));
+    TRY(salloc_t(s, &s->xs, size_t(TM) * VAL_DIM / 16, st));
+    s->moe_scratch_bytes = moe_scratch_bytes(TM);
+    TRY(salloc(s, &s->moe_scratch, s->moe_scratch_bytes, st));
+    TRY(salloc_t(s, &s->ml, size_t(TM) * NHEAD * 2, st));
+    TRY(salloc_t(s, &s->argmax_dev, 4, st));
+    s->logits_rows = 1;
+    TRY(salloc_t(s, &s->logits, size_t(m->n_vocab), st));
+#undef TRY
+    s->live.assign(n_ctx, 0);
+    s->tier.assign(n_ctx, 0);
+    s->pin_pos.assign(HCM_H_PIN, -1);
+    s->next_rebuild = qma_cuda_state::HCM_REBUILD_INIT;
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    *out = s;
+    return QMA_CUDA_OK;
+}
+
+// ------------------------------------------------------------ HCM rebuild --
+// hcm_rebuild (nn.c:981-1150), host side, in the reference's exact order:
+// the live index is [sink + hot ring q4 | arena q4 | gist ring q2]; the
+// heavy-hitter heap keeps the top HCM_H_PIN of (ring middle positions scored
+// sum_l sal * (1 - 2 qf), existing arena occupants scored sum_l pin_sal);
+// fresh winners are copied ring -> arena on the device.
+struct HEnt { float sc; int pos; int is_arena; };
+
+static void heap_push(std::vector<HEnt> &heap, int &hn, float sc, int pos, int is_a) {
+    if (hn < HCM_H_PIN) {
+        int i = hn++;
+        heap[i] = {sc, pos, is_a};
+        while (i > 0) {
+            const int par = (i - 1) / 2;
+            if (heap[par].sc <= heap[i].sc) break;
+            std::swap(heap[par], heap[i]);
+            i = par;
+        }
+    } else if (sc > heap[0].sc) {
+        heap[0] = {sc, pos, is_a};
+        int i = 0;
+        for (;;) {
+            const int lc = 2 * i + 1, rc = 2 * i + 2;
+            int sm = i;
+            if (lc < hn && heap[lc].sc < heap[sm].sc) sm = lc;
+            if (rc < hn && heap[rc].sc < heap[sm].sc) sm = rc;
+            if (sm == i) break;
+            std::swap(heap[sm], heap[i]);
+            i = sm;
+        }
+    }
+}
+
+static int hcm_rebuild(qma_cuda_state *s, int n_pos) {
+    const int cap = s->n_ctx, ring = cap - HCM_SINK, oldest = n_pos - ring;
+    cudaStream_t st = s->st;
+    if (n_pos <= HCM_SINK + HCM_W_HOT) {
+        for (int p = 0; p < n_pos; p++) {
+            s->live[p] = hcm_slot(p, cap);
+            s->tier[hcm_slot(p, cap)] = 2;
+        }
+        s->live_n = s->n4 = s->n_ring_q4 = n_pos;
+    } else {
+        s->h_sal.resize(size_t(NATTN) * cap);
+        s->h_qf.resize(cap);
+        s->h_pin_sal.resize(size_t(NATTN) * HCM_H_PIN);
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_sal.data(), s->sal, s->h_sal.size() * 4, cudaMemcpyDeviceToHost, st));
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_qf.data(), s->qf, s->h_qf.size() * 4, cudaMemcpyDeviceToHost, st));
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_pin_sal.data(), s->pin_sal, s->h_pin_sal.size() * 4,
+                                       cudaMemcpyDeviceToHost, st));
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+        int n = 0;
+        int hot_lo = n_pos - HCM_W_HOT;
+        if (hot_lo < oldest) hot_lo = oldest;
+        for (int p = 0; p < HCM_SINK && p < hot_lo; p++) {
+            s->live[n++] = hcm_slot(p, cap);
+            s->tier[hcm_slot(p, cap)] = 2;
+        }
+        for (int p = hot_lo; p < n_pos; p++) {
+            s->live[n++] = hcm_slot(p, cap);
+            s->tier[hcm_slot(p, cap)] = 2;
+        }
+        int cand_lo = HCM_SINK;
+        if (oldest > cand_lo) cand_lo = oldest;
+        std::vector<HEnt> heap(HCM_H_PIN);
+        int hn = 0;
+        for (int p = cand_lo; p < hot_lo; p++) {
+            const int sl = hcm_slot(p, cap);
+            float sc = 0.0f;
+            for (int l = 0; l < NATTN; l++) sc += s->h_sal[size_t(l) * cap + sl];
+            const float qf = s->h_qf[sl] > 0 ? s->h_qf[sl] : 0.05f;
+            sc = sc * (1.0f - HCM_QF_BIAS * qf);
+            heap_push(heap, hn, sc, p, 0);
+        }
+        for (int a = 0; a < HCM_H_PIN; a++) {
+            if (s->pin_pos[a] < 0) continue;
+            float sc = 0.0f;
+            for (int l = 0; l < NATTN; l++) sc += s->h_pin_sal[size_t(l) * HCM_H_PIN + a];
+            heap_push(heap, hn, sc, a, 1);
+        }
+        std::vector<int> new_arena(HCM_H_PIN, -1);
+        for (int i = 0; i < hn; i++) new_arena[i] = heap[i].is_arena ? heap[i].pos : -1;
+        std::vector<int2> pairs;
+        for (int i = 0; i < hn; i++) {
+            if (heap[i].is_arena) continue;
+            const int src = hcm_slot(heap[i].pos, cap);
+            int slot = -1;
+            for (int a = 0; a < HCM_H_PIN; a++) if (s->pin_pos[a] < 0) { slot = a; break; }
+            if (slot < 0) {
+                float worst = 1e30f;
+                int wi = -1;
+                for (int a = 0; a < HCM_H_PIN; a++) {
+                    if (s->pin_pos[a] < 0) continue;
+                    bool kept = false;
+                    for (int k = 0; k < hn; k++) if (new_arena[k] == a) { kept = true; break; }
+                    if (kept) continue;
+                    float sc = 0.0f;
+                    for (int l = 0; l < NATTN; l++) sc += s->h_pin_sal[size_t(l) * HCM_H_PIN + a];
+                    if (sc < worst) { worst = sc; wi = a; }
+                }
+                slot = wi;
+            }
+            if (slot < 0) continue;
+            new_arena[i] = slot;
+            pairs.push_back(make_int2(src, slot));
+            for (int l = 0; l < NATTN; l++)
+                s->h_pin_sal[size_t(l) * HCM_H_PIN + slot] = s->h_sal[size_t(l) * cap + src];
+            s->pin_pos[slot] = heap[i].pos;
+        }
+        const int n_ring_q4 = n;
+        for (int i = 0; i < hn; i++)
+            if (new_arena[i] >= 0) s->live[n++] = HCM_ARENA_BASE + new_arena[i];
+        int gist_lo = hot_lo - HCM_W_GIST;
+        if (gist_lo < cand_lo) gist_lo = cand_lo;
+        for (int p = gist_lo; p < hot_lo; p++) {
+            const int sl = hcm_slot(p, cap);
+            if (s->tier[sl] == 2) continue;
+            s->live[n++] = sl;
+            s->tier[sl] = 1;
+        }
+        for (int p = cand_lo; p < gist_lo; p++) {
+            const int sl = hcm_slot(p, cap);
+            if (s->tier[sl] != 2) s->tier[sl] = 0;
+        }
+        s->live_n = n;
+        s->n4 = n_ring_q4 + hn;
+        s->n_ring_q4 = n_ring_q4;
+        if (!pairs.empty()) {
+            QMA_CHECK_CUDA(cudaMemcpyAsync(s->pairs_dev, pairs.data(), pairs.size() * sizeof(int2),
+                                           cudaMemcpyHostToDevice, st));
+            int rc = launch_arena_copy(s->pairs_dev, int(pairs.size()), s->kv_dev, s->arena_dev, s->sal,
+                                       s->pin_sal, cap, st);
+            if (rc) return rc;
+            QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+        }
+    }
+    if (s->live_n > 0)
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->live_dev, s->live.data(), size_t(s->live_n) * 4,
+                                       cudaMemcpyHostToDevice, st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    return QMA_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- forward --
+static int nk_upper(const qma_cuda_state *s, int pos_now, int T, bool graph) {
+    if (graph) {
+        // a decode graph serves positions [pos_now, next_rebuild)
+        const int last = s->next_rebuild - 1;
+        return s->live_n > 0 ? s->live_n + (last - s->rebuilt_at + 1) : last + 1;
+    }
+    return s->live_n > 0 ? s->live_n + (pos_now + T - 1 - s->rebuilt_at + 1) : pos_now + T;
+}
+
+static int ensure_attn_scratch(qma_cuda_state *s, int T, int nk, int pv_chunk) {
+    const size_t nsc = size_t((nk + 63) / 64), npv = size_t((nk + pv_chunk - 1) / pv_chunk);
+    const bool moves = size_t(T) * NHEAD * nk > s->scores_cap || size_t(T) * NHEAD * nsc > s->cmax_cap ||
+                       size_t(T) * NHEAD * npv * HEAD_DIM > s->opart_cap ||
+                       size_t(T) * NHEAD * npv > s->lpart_cap;
+    if (moves && s->graph) {
+        // a captured decode graph holds the old buffers
+        QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    int rc;
+    if ((rc = grow(&s->scores, &s->scores_cap, size_t(T) * NHEAD * nk))) return rc;
+    if ((rc = grow(&s->cmax, &s->cmax_cap, size_t(T) * NHEAD * nsc))) return rc;
+    if ((rc = grow(&s->opart, &s->opart_cap, size_t(T) * NHEAD * npv * HEAD_DIM))) return rc;
+    if ((rc = grow(&s->lpart, &s->lpart_cap, size_t(T) * NHEAD * npv))) return rc;
+    return QMA_CUDA_OK;
+}
+
+__global__ void argmax_kernel(const float *__restrict__ logits, int n, StepParams *sp, int *out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = logits[i];
+        if (x > v) { v = x; idx = i; }     // ascending i: keeps the first maximum
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = v; bi[threadIdx.x >> 5] = idx; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < blockDim.x / 32 ? bv[threadIdx.x] : -INFINITY;
+        idx = threadIdx.x < blockDim.x / 32 ? bi[threadIdx.x] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+        }
+        if (threadIdx.x == 0) {
+            *out = idx;
+            if (sp) {            // next decode step: this token at the next position
+                sp->token = idx;
+                sp->n_pos += 1;
+            }
+        }
+    }
+}
+
+// The forward of T tokens at the positions in *sp_dev (host copy hs):
+// embedding -> 40 layers -> (optionally) final norm + LM head.
+static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
+                   int logits_mode /*0 none, 1 last, 2 all*/) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    const int T = hs.T;
+    int rc;
+#define TRY(x) do { if ((rc = (x))) return rc; } while (0)
+    TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, tokens_dev, s->sp_dev, T, s->x, st));
+    const int pv_chunk = T == 1 ? 64 : 256;
+    for (int il = 0; il < NLAYER; il++) {
+        const LayerW &L = m->L[il];
+        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st));
+        TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st));
+        if (is_attn(il)) {
+            const int lay = il / 4;
+            TRY(launch_qk_prep_append(s->proj, L.in_rows, L.q_norm, L.k_norm, s->rope, s->sp_dev, T,
+                                      s->qr, s->z, s->kv[lay], s->qf, s->sal, st));
+            AttnArgs a;
+            a.qr = s->qr; a.kv = s->kv[lay]; a.arena = s->arena[lay]; a.live = s->live_dev;
+            a.sp = s->sp_dev; a.T = T; a.nk_max = nk_cap; a.pv_chunk = pv_chunk;
+            a.scores = s->scores; a.cmax = s->cmax; a.opart = s->opart; a.lpart = s->lpart;
+            a.ml = s->ml; a.z = s->z; a.xq = s->xq; a.xd = s->xd; a.xs = s->xs;
+            a.sal = s->sal + size_t(lay) * s->n_ctx;
+            a.pin_sal = s->pin_sal + size_t(lay) * HCM_H_PIN;
+            TRY(launch_attention(a, st));
+            TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
+        } else {
+            const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
+            TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
+            TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
+                           L.dt, L.a, s->ssm[il], T, s->gdo, st));
+            TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
+                                        s->xs, st));
+            TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
+        }
+        // x = x2 + moe(rms_norm(x2) * post_norm)
+        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st));
+    }
+    if (logits_mode) {
+        const int rows = logits_mode == 2 ? T : 1;
+        const float *xin = logits_mode == 2 ? s->x : s->x + size_t(T - 1) * EMBD;
+        TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
+        TRY(matvec(m->out_type, m->out, EMBD, m->n_vocab, rows, s->xq, s->xd, s->xs, s->logits, st));
+    }
+#undef TRY
+    return QMA_CUDA_OK;
+}
+
+static void fill_params(qma_cuda_state *s, StepParams &p, int pos_now, int T, int token) {
+    p.n_pos = pos_now;
+    p.T = T;
+    p.n_live = s->live_n;
+    p.n_ring_q4 = s->n_ring_q4;
+    p.n4 = s->n4;
+    p.rebuilt_at = s->rebuilt_at;
+    p.n_ctx = s->n_ctx;
+    p.token = token;
+}
+
+static int maybe_rebuild(qma_cuda_state *s, int pos_now) {
+    if (pos_now >= s->next_rebuild) {
+        const int rc = hcm_rebuild(s, pos_now);
+        if (rc) return rc;
+        s->rebuilt_at = pos_now;
+        s->next_rebuild = pos_now + HCM_REBUILD;
+        if (s->graph) {
+            cudaGraphExecDestroy(s->graph);
+            s->graph = nullptr;
+        }
+    }
+    return QMA_CUDA_OK;
+}
+
+static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logits, int logits_all) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    if (s->n_pos + n_tokens > s->n_ctx - HCM_SINK) {
+        set_error("eval: %d + %d positions exceed this state's ring of %d (no wrap-around)", s->n_pos,
+                  n_tokens, s->n_ctx);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    if (logits_all && MAX_CHUNK > s->logits_rows) {
+        void *p;
+        QMA_CHECK_CUDA(cudaMalloc(&p, sizeof(float) * size_t(MAX_CHUNK) * m->n_vocab));
+        s->allocs.push_back(p);
+        s->logits = static_cast<float *>(p);
+        s->logits_rows = MAX_CHUNK;
+    }
+    int done = 0, rc;
+    while (done < n_tokens) {
+        const int T = n_tokens - done < MAX_CHUNK ? n_tokens - done : MAX_CHUNK;
+        const int pos_now = s->n_pos + done;
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->tokens_dev, tokens + done, sizeof(int) * T,
+                                       cudaMemcpyHostToDevice, st));
+        if ((rc = maybe_rebuild(s, pos_now))) return rc;
+        for (int t = 0; t < T; t++) s->tier[hcm_slot(pos_now + t, s->n_ctx)] = 2;   // kv_append
+        fill_params(s, *s->sp_host, pos_now, T, tokens[done + T - 1]);
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->sp_dev, s->sp_host, sizeof(StepParams),
+                                       cudaMemcpyHostToDevice, st));
+        const int nk = nk_upper(s, pos_now, T, false);
+        if ((rc = ensure_attn_scratch(s, T, nk, T == 1 ? 64 : 256))) return rc;
+        const bool last = done + T == n_tokens;
+        const int mode = logits_all ? 2 : (last && logits ? 1 : 0);
+        if ((rc = forward(s, *s->sp_host, s->tokens_dev, nk, mode))) return rc;
+        if (mode == 2 && logits)
+            QMA_CHECK_CUDA(cudaMemcpyAsync(logits + size_t(done) * m->n_vocab, s->logits,
+                                           sizeof(float) * size_t(T) * m->n_vocab,
+                                           cudaMemcpyDeviceToHost, st));
+        else if (mode == 1)
+            QMA_CHECK_CUDA(cudaMemcpyAsync(logits, s->logits, sizeof(float) * m->n_vocab,
+                                           cudaMemcpyDeviceToHost, st));
+        // sp_host is reused by the next chunk: let this chunk consume it
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+        done += T;
+    }
+    s->n_pos += n_tokens;
+    return QMA_CUDA_OK;
+}
+
+// Capture one decode step (T = 1, token and position read from sp_dev,
+// argmax writes the next token and advances the position) as a graph.
+static int capture_decode(qma_cuda_state *s) {
+    cudaStream_t st = s->st;
+    const int nk = nk_upper(s, s->n_pos, 1, true);
+    int rc = ensure_attn_scratch(s, 1, nk, 64);
+    if (rc) return rc;
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    cudaGraph_t g;
+    QMA_CHECK_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    StepParams hs;
+    fill_params(s, hs, s->n_pos, 1, 0);
+    rc = forward(s, hs, nullptr, nk, 1);
+    if (!rc) {
+        argmax_kernel<<<1, 1024, 0, st>>>(s->logits, s->m->n_vocab, s->sp_dev, s->argmax_dev);
+        if (cudaGetLastError() != cudaSuccess) rc = QMA_CUDA_ERR_CUDA;
+    }
+    const cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc) return rc;
+    if (e != cudaSuccess) {
+        set_error("decode capture: %s", cudaGetErrorString(e));
+        return QMA_CUDA_ERR_CUDA;
+    }
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (nn) cudaGraphGetNodes(g, nodes.data(), &nn);
+    int kernels = 0;
+    for (size_t i = 0; i < nn; i++) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) kernels++;
+    }
+    s->graph_kernels = kernels;
+    const cudaError_t e2 = cudaGraphInstantiate(&s->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e2 != cudaSuccess) {
+        set_error("decode instantiate: %s", cudaGetErrorString(e2));
+        return QMA_CUDA_ERR_CUDA;
+    }
+    s->graph_nk = nk;
+    return QMA_CUDA_OK;
+}
+
+static int decode_greedy(qma_cuda_state *s, int token, int n_steps, int *tokens_out, float *logits) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    if (s->n_pos + n_steps > s->n_ctx - HCM_SINK) {
+        set_error("decode: %d + %d positions exceed this state's ring of %d", s->n_pos, n_steps, s->n_ctx);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    int rc;
+    int cur = token;
+    for (int i = 0; i < n_steps; i++) {
+        const int pos = s->n_pos;
+        const bool rebuild = pos >= s->next_rebuild;
+        if (rebuild || !s->graph || i == 0) {
+            // host state is current only after the device caught up
+            QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+            if (i > 0) {
+                int dev_tok;
+                QMA_CHECK_CUDA(cudaMemcpy(&dev_tok, s->argmax_dev, sizeof(int), cudaMemcpyDeviceToHost));
+                cur = dev_tok;
+            }
+            if ((rc = maybe_rebuild(s, pos))) return rc;
+            fill_params(s, *s->sp_host, pos, 1, cur);
+            QMA_CHECK_CUDA(cudaMemcpyAsync(s->sp_dev, s->sp_host, sizeof(StepParams),
+                                           cudaMemcpyHostToDevice, st));
+            if (!s->graph && (rc = capture_decode(s))) return rc;
+        }
+        s->tier[hcm_slot(pos, s->n_ctx)] = 2;
+        QMA_CHECK_CUDA(cudaGraphLaunch(s->graph, st));
+        if (tokens_out) {
+            if (i == 0) tokens_out[0] = cur;
+            if (i + 1 < n_steps)
+                QMA_CHECK_CUDA(cudaMemcpyAsync(tokens_out + i + 1, s->argmax_dev, sizeof(int),
+                                               cudaMemcpyDeviceToHost, st));
+        }
+        s->n_pos += 1;
+    }
+    if (logits)
+        QMA_CHECK_CUDA(cudaMemcpyAsync(logits, s->logits, sizeof(float) * m->n_vocab,
+                                       cudaMemcpyDeviceToHost, st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    return QMA_CUDA_OK;
+}
+
+}  // namespace qma
+
+// ------------------------------------------------------------------- C ABI --
+extern "C" {
+
+int qma_cuda_model_load(int device, const qma_cuda_tensor *tensors, uint32_t n,
+                        const void *host_data, uint64_t data_size, qma_cuda_model **out) {
+    qma::clear_error();
+    return qma::build_model(device, tensors, n, host_data, data_size, false, 0, out);
+}
+
+int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n, uint64_t seed,
+                         qma_cuda_model **out) {
+    qma::clear_error();
+    return qma::build_model(device, tensors, n, nullptr, 0, true, seed, out);
+}
+
+int qma_cuda_model_free(qma_cuda_model *m) {
+    qma::clear_error();
+    if (!m) return QMA_CUDA_OK;
+    cudaSetDevice(m->device);
+    for (void *p : m->allocs) cudaFree(p);
+    delete m;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_model_n_vocab(const qma_cuda_model *m) { return m ? m->n_vocab : 0; }
+
+int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const void **gate,
+                        const void **up, const void **down) {
+    qma::clear_error();
+    QMA_REQUIRE(m && layer >= 0 && layer < qma::NLAYER && expert >= 0 && expert < qma::MOE_NEXP,
+                "qma_cuda_ecache_get: bad (layer %d, expert %d)", layer, expert);
+    const qma_cuda_moe_weights &w = m->L[layer].moe;
+    const size_t gu = size_t(qma::MOE_FF) * (qma::MOE_EMBD / 256) * qma::Q4K_BYTES;
+    const size_t dn = qma::packed_bytes(w.down_type, qma::MOE_EMBD, qma::MOE_FF);
+    if (gate) *gate = static_cast<const uint8_t *>(w.gate_exps) + gu * expert;
+    if (up) *up = static_cast<const uint8_t *>(w.up_exps) + gu * expert;
+    if (down) *down = static_cast<const uint8_t *>(w.down_exps) + dn * expert;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_state_create(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
+    qma::clear_error();
+    return qma::create_state(m, n_ctx, out);
+}
+
+int qma_cuda_state_free(qma_cuda_state *s) {
+    qma::clear_error();
+    if (!s) return QMA_CUDA_OK;
+    cudaSetDevice(s->m->device);
+    cudaStreamSynchronize(s->st);
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    for (void *p : s->allocs) cudaFree(p);
+    for (float *p : {s->scores, s->cmax, s->opart, s->lpart}) if (p) cudaFree(p);
+    if (s->sp_host) cudaFreeHost(s->sp_host);
+    cudaStreamDestroy(s->st);
+    delete s;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_state_n_pos(const qma_cuda_state *s) { return s ? s->n_pos : -1; }
+
+void *qma_cuda_state_stream(const qma_cuda_state *s) { return s ? static_cast<void *>(s->st) : nullptr; }
+
+int qma_cuda_state_stats(const qma_cuda_state *s, int *graph_kernels, uint64_t *state_bytes) {
+    qma::clear_error();
+    QMA_REQUIRE(s, "qma_cuda_state_stats: null state");
+    if (graph_kernels) *graph_kernels = s->graph_kernels;
+    if (state_bytes) *state_bytes = s->state_bytes;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n_tokens,
+                  float *logits, int logits_all) {
+    qma::clear_error();
+    QMA_REQUIRE(m && s && s->m == m && tokens && n_tokens > 0, "qma_cuda_eval: bad arguments");
+    for (int i = 0; i < n_tokens; i++)
+        QMA_REQUIRE(tokens[i] >= 0 && tokens[i] < m->n_vocab, "qma_cuda_eval: token %d out of range",
+                    tokens[i]);
+    return qma::eval(s, tokens, n_tokens, logits, logits_all);
+}
+
+int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,
+                           int *tokens_out, float *logits) {
+    qma::clear_error();
+    QMA_REQUIRE(m && s && s->m == m && n_steps > 0 && token >= 0 && token < m->n_vocab,
+                "qma_cuda_decode_greedy: bad arguments");
+    return qma::decode_greedy(s, token, n_steps, tokens_out, logits);
+}
+
+}  // extern "C"

@@ -27,12 +27,13 @@ __global__ void __launch_bounds__(256) q8k_quant_kernel(const float *__restrict_
 template <class F, int T, int LPR, int UPL, int RU>
 __global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, int n_out,
                                                    const int8_t *xq, const float *xd,
-                                                   const int16_t *xsum, float *out, int out_ld) {
+                                                   const int16_t *xsum, float *out, int out_ld,
+                                                   const float *resid) {
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     gemv_warp_rows<F, T, LPR, UPL, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, warp, nwarps,
-                                       lane);
+                                       lane, resid);
 }
 
 static int g_num_sms = 0;
@@ -51,7 +52,7 @@ int num_sms() {
 template <class F, int T, int LPR, int UPL, int RU>
 static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
                        const float *xd, const int16_t *xsum, float *out, int out_ld,
-                       cudaStream_t st) {
+                       const float *resid, cudaStream_t st) {
     constexpr int RPW = 32 / LPR;
     static int per_sm = 0;
     if (!per_sm) {
@@ -64,7 +65,7 @@ static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8
     const long wave = long(num_sms()) * per_sm;
     if (blocks > wave) blocks = wave;
     gemv_kernel<F, T, LPR, UPL, RU><<<int(blocks), 256, 0, st>>>(W, n_in, n_out, xq, xd, xsum,
-                                                                 out, out_ld);
+                                                                 out, out_ld, resid);
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -74,15 +75,15 @@ static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8
 template <class F, int T, int RU = (T == 1 ? 2 : 1)>
 static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
                           const float *xd, const int16_t *xsum, float *out, int out_ld,
-                          cudaStream_t st) {
+                          const float *resid, cudaStream_t st) {
     const int U = n_in / F::UNIT;
     switch (U) {
-    case 2: return launch_gemv<F, T, 2, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
-    case 4: return launch_gemv<F, T, 4, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
-    case 8: return launch_gemv<F, T, 8, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
-    case 16: return launch_gemv<F, T, 16, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
-    case 32: return launch_gemv<F, T, 32, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
-    case 64: return launch_gemv<F, T, 32, 2, (RU > 1 ? RU / 2 : 1)>(W, n_in, n_out, xq, xd, xsum, out, out_ld, st);
+    case 2: return launch_gemv<F, T, 2, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
+    case 4: return launch_gemv<F, T, 4, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
+    case 8: return launch_gemv<F, T, 8, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
+    case 16: return launch_gemv<F, T, 16, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
+    case 32: return launch_gemv<F, T, 32, 1, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
+    case 64: return launch_gemv<F, T, 32, 2, (RU > 1 ? RU / 2 : 1)>(W, n_in, n_out, xq, xd, xsum, out, out_ld, resid, st);
     default:
         set_error("matvec: n_in %d unsupported for this weight type", n_in);
         return QMA_CUDA_ERR_UNSUPPORTED;
@@ -91,7 +92,8 @@ static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const i
 
 template <class F, int TMAX>
 static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, const int8_t *xq,
-                       const float *xd, const int16_t *xsum, float *out, cudaStream_t st) {
+                       const float *xd, const int16_t *xsum, float *out, const float *resid,
+                       cudaStream_t st) {
     int t0 = 0;
     while (t0 < T) {
         const int rem = T - t0;
@@ -99,10 +101,11 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
         const float *d = xd + size_t(t0) * (n_in / 256);
         const int16_t *s = xsum + size_t(t0) * (n_in / 16);
         float *o = out + size_t(t0) * n_out;
+        const float *rs = resid ? resid + size_t(t0) * n_out : nullptr;
         int rc, tn;
         if constexpr (TMAX >= 4) {
             if (rem >= 4) {
-                rc = dispatch_shape<F, 4>(W, n_in, n_out, q, d, s, o, n_out, st);
+                rc = dispatch_shape<F, 4>(W, n_in, n_out, q, d, s, o, n_out, rs, st);
                 tn = 4;
                 if (rc) return rc;
                 t0 += tn;
@@ -110,10 +113,10 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
             }
         }
         if (rem >= 2) {
-            rc = dispatch_shape<F, 2>(W, n_in, n_out, q, d, s, o, n_out, st);
+            rc = dispatch_shape<F, 2>(W, n_in, n_out, q, d, s, o, n_out, rs, st);
             tn = 2;
         } else {
-            rc = dispatch_shape<F, 1>(W, n_in, n_out, q, d, s, o, n_out, st);
+            rc = dispatch_shape<F, 1>(W, n_in, n_out, q, d, s, o, n_out, rs, st);
             tn = 1;
         }
         if (rc) return rc;
@@ -123,17 +126,18 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
 }
 
 int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
-           const float *xd, const int16_t *xsum, float *out, cudaStream_t st) {
+           const float *xd, const int16_t *xsum, float *out, cudaStream_t st,
+           const float *resid) {
     switch (wtype) {
     case QMA_TYPE_Q4_K:
         return gemv_tokens<FmtQ4K, 4>(static_cast<const uint8_t *>(W), n_in, n_out, T, xq, xd,
-                                      xsum, out, st);
+                                      xsum, out, resid, st);
     case QMA_TYPE_Q6_K:
         return gemv_tokens<FmtQ6K, 2>(q6_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
-                                      out, st);
+                                      out, resid, st);
     case QMA_TYPE_Q8_0:
         return gemv_tokens<FmtQ80, 4>(q8_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
-                                      out, st);
+                                      out, resid, st);
     default:
         set_error("matvec: unsupported weight type %d", wtype);
         return QMA_CUDA_ERR_UNSUPPORTED;

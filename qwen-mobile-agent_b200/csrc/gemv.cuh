@@ -205,7 +205,8 @@ template <class F, int T, int LPR, int UPL, int RU>
 __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_in, int n_out,
                                                const int8_t *xq, const float *xd,
                                                const int16_t *xsum, float *out, int out_ld,
-                                               int warp, int nwarps, int lane) {
+                                               int warp, int nwarps, int lane,
+                                               const float *resid = nullptr) {
     constexpr int RPW = 32 / LPR;
     const int lir = lane % LPR, slot = lane / LPR;
     typename F::Act act[UPL][T];
@@ -240,11 +241,21 @@ __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_i
 #pragma unroll
             for (int t = 0; t < T; t++) acc[t] = group_sum(acc[t], LPR);
             if (lir == 0 && r < n_out) {
+                // optional residual: out = dot + resid (add_m, nn.c:375)
 #pragma unroll
-                for (int t = 0; t < T; t++) out[size_t(t) * out_ld + r] = acc[t];
+                for (int t = 0; t < T; t++)
+                    out[size_t(t) * out_ld + r] =
+                        resid ? __fadd_rn(acc[t], resid[size_t(t) * out_ld + r]) : acc[t];
             }
         }
     }
 }
+
+// Host launcher (gemv.cu): out[t][r] = <W[r], x_t> (+ resid[t][r]).  W is
+// the packed matrix; T tokens are processed in passes of 4/2/1.
+int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
+           const float *xd, const int16_t *xsum, float *out, cudaStream_t st,
+           const float *resid = nullptr);
+int num_sms();
 
 }  // namespace qma

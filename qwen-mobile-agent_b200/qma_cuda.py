@@ -41,6 +41,81 @@ _SIGS = {
 }
 
 
+class Tensor(C.Structure):
+    """qma_cuda_tensor: one GGUF-style tensor (the layout of tensor_t, qma.h:155-161)."""
+
+    _fields_ = [("name", C.c_char * 64), ("type", C.c_uint32), ("ne", C.c_int64 * 3),
+                ("off", C.c_uint64), ("nbytes", C.c_uint64)]
+
+
+_TP = C.POINTER(Tensor)
+_SIGS.update({
+    "qma_cuda_model_load": (_i32, [_i32, _TP, C.c_uint32, _vp, _u64, C.POINTER(_vp)]),
+    "qma_cuda_model_synth": (_i32, [_i32, _TP, C.c_uint32, _u64, C.POINTER(_vp)]),
+    "qma_cuda_model_free": (_i32, [_vp]),
+    "qma_cuda_model_n_vocab": (_i32, [_vp]),
+    "qma_cuda_ecache_get": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "qma_cuda_state_create": (_i32, [_vp, _i32, C.POINTER(_vp)]),
+    "qma_cuda_state_free": (_i32, [_vp]),
+    "qma_cuda_state_n_pos": (_i32, [_vp]),
+    "qma_cuda_eval": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32]),
+    "qma_cuda_decode_greedy": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
+    "qma_cuda_state_stream": (_vp, [_vp]),
+    "qma_cuda_state_stats": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_u64)]),
+})
+
+
+class Model:
+    """Device-resident qwen35moe weights (qma_cuda_model)."""
+
+    def __init__(self, tensors, n, host_blob=None, seed=None, device=0):
+        h = _vp()
+        if host_blob is not None:
+            call("qma_cuda_model_load", device, tensors, n, ptr(host_blob), host_blob.nbytes, C.byref(h))
+        else:
+            call("qma_cuda_model_synth", device, tensors, n, seed, C.byref(h))
+        self.h = h
+        self.n_vocab = lib().qma_cuda_model_n_vocab(h)
+
+    def close(self):
+        if self.h:
+            call("qma_cuda_model_free", self.h)
+            self.h = None
+
+
+class State:
+    """One sequence (qma_cuda_state): KV ring, recurrent state, HCM tiers."""
+
+    def __init__(self, model: Model, n_ctx: int):
+        h = _vp()
+        call("qma_cuda_state_create", model.h, n_ctx, C.byref(h))
+        self.h, self.model = h, model
+
+    @property
+    def n_pos(self) -> int:
+        return lib().qma_cuda_state_n_pos(self.h)
+
+    def eval(self, tokens, logits_all=False):
+        import numpy as np
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        rows = len(toks) if logits_all else 1
+        out = np.zeros((rows, self.model.n_vocab), np.float32)
+        call("qma_cuda_eval", self.model.h, self.h, ptr(toks), len(toks), ptr(out), int(logits_all))
+        return out if logits_all else out[0]
+
+    def decode_greedy(self, token: int, n_steps: int):
+        import numpy as np
+        toks = np.zeros(n_steps, np.int32)
+        logits = np.zeros(self.model.n_vocab, np.float32)
+        call("qma_cuda_decode_greedy", self.model.h, self.h, token, n_steps, ptr(toks), ptr(logits))
+        return toks, logits
+
+    def close(self):
+        if self.h:
+            call("qma_cuda_state_free", self.h)
+            self.h = None
+
+
 class MoeWeights(C.Structure):
     """qma_cuda_moe_weights: device pointers of one layer's MoE tensors."""
 
