@@ -166,6 +166,21 @@ int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n
 int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,
                            int *tokens_out, float *logits);
 
+/* Parity entry point: like qma_cuda_eval but runs only the first n_layers
+ * layers (0..40; 0 = the embedding rows) and writes the hidden state after
+ * them (T x 2048 floats, host); n_layers < 0 runs |n_layers| layers but
+ * stops the last one after its mixer (GDN or attention) and residual,
+ * before the MoE block.  The state advances as in qma_cuda_eval.  No reference
+ * counterpart (the reference's closest hook is its QMA_DUMP_L1 debug dump,
+ * nn.c:2253-2266). */
+int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens,
+                         int n_tokens, int n_layers, float *hidden);
+
+/* Copies the 240-byte KV slot (q4 record + q2 record, kvq.h:22-29) of
+ * attention layer `lay` (0..9, model layer 4*lay+3), head `head` (0, 1 = K
+ * heads, 2, 3 = V heads) and ring slot `slot` to host `out`. */
+int qma_cuda_state_kv_slot(const qma_cuda_state *s, int lay, int head, int slot, uint8_t *out);
+
 /* The CUDA stream (cudaStream_t as void*) every call on this state runs on,
  * for callers that time or order work against it. */
 void *qma_cuda_state_stream(const qma_cuda_state *s);

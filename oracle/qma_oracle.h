@@ -181,10 +181,22 @@ typedef struct qo_state qo_state;
 qo_state *qo_state_new(int n_ctx);
 void      qo_state_free(qo_state *s);
 int       qo_state_n_pos(const qo_state *s);
+/* 240-byte KV slot of attention layer lay, head (0,1 K; 2,3 V), ring slot */
+const uint8_t *qo_state_kv_slot(const qo_state *s, int lay, int head, int slot);
 /* qma_eval (nn.c:2056-2308), single-threaded, q8k path, quantized KV + HCM.
  * Writes the last token's logits (n_vocab) or all (T*n_vocab). */
 int qo_eval(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
             float *logits, int logits_all);
+
+/* qo_eval through the first n_layers layers; hidden [n_tokens][2048] gets
+ * the residual stream after them (parity aid). */
+int qo_eval_hidden(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
+                   int n_layers, float *hidden);
+
+/* One full layer (mixer + residual + MoE block + residual, nn.c:2105-2252)
+ * from x_in [T][2048] to x_out, tokens at positions n_pos.. (parity aid). */
+void qo_layer_forward(const qo_model *m, qo_state *s, int il, const float *x_in, int T,
+                      int n_pos, float *x_out);
 
 /* ---- per-layer pieces, for layer-level parity ------------------------------ */
 /* GDN (recurrent) layer core from the post-norm input xn [T][2048] to the

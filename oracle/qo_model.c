@@ -387,6 +387,10 @@ void qo_state_free(qo_state *s)
 }
 
 int qo_state_n_pos(const qo_state *s) { return s->n_pos; }
+const uint8_t *qo_state_kv_slot(const qo_state *s, int lay, int head, int slot)
+{
+    return s->kv[lay] + ((size_t)head * s->n_ctx + slot) * QO_KVQ_SLOT;
+}
 float *qo_state_conv(qo_state *s, int il) { return s->conv[il]; }
 float *qo_state_ssm(qo_state *s, int il) { return s->ssm[il]; }
 
@@ -1003,8 +1007,47 @@ static void attn_layer(const qo_model *m, qo_state *s, int il, const float *xn, 
 }
 
 /* ------------------------------------------------------------ qma_eval -- */
+static int eval_impl(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
+                     float *logits, int logits_all, int n_layers, float *hidden);
+
+/* One layer of qma_eval's loop body (nn.c:2105-2252) on T tokens at
+ * positions n_pos.., from the residual x_in to the residual x_out, using
+ * and updating that layer's state in s (no HCM rebuild: call with a state
+ * whose live index is current).  Parity aid: lets a caller feed each layer
+ * the engine's own input so differences cannot compound across layers. */
+void qo_layer_forward(const qo_model *m, qo_state *s, int il, const float *x_in, int T,
+                      int n_pos, float *x_out)
+{
+    const qo_layer *L = &m->L[il];
+    float *xn = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    float *ra = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    float *x2 = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    rms_norm_m(xn, x_in, L->attn_norm, QO_EMBD, T);
+    if (QO_IS_ATTN(il)) attn_layer(m, s, il, xn, T, n_pos, ra);
+    else qo_gdn_layer(m, s, il, xn, T, ra);
+    for (size_t i = 0; i < (size_t)QO_EMBD * T; i++) x2[i] = ra[i] + x_in[i];
+    qo_moe_block(m, il, x2, T, x_out, NULL, NULL);
+    free(xn);
+    free(ra);
+    free(x2);
+}
+
 int qo_eval(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
             float *logits, int logits_all)
+{
+    return eval_impl(m, s, tokens, n_tokens, logits, logits_all, QO_LAYER, NULL);
+}
+
+/* qo_eval through the first n_layers layers only; the hidden state after
+ * them goes to hidden [n_tokens][2048] (parity aid, no logits). */
+int qo_eval_hidden(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
+                   int n_layers, float *hidden)
+{
+    return eval_impl(m, s, tokens, n_tokens, NULL, 0, n_layers, hidden);
+}
+
+static int eval_impl(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
+                     float *logits, int logits_all, int n_layers, float *hidden)
 {
     const int TM = QO_MAX_CHUNK;
     float *x = malloc(sizeof(float) * (size_t)TM * QO_EMBD);
@@ -1024,16 +1067,23 @@ int qo_eval(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,
             s->rebuilt_at = pos_now;
             s->next_rebuild = pos_now + QO_HCM_REBUILD;
         }
-        for (int il = 0; il < QO_LAYER; il++) {
+        const int nl = n_layers < 0 ? -n_layers : n_layers;
+        for (int il = 0; il < nl; il++) {
             const qo_layer *L = &m->L[il];
             rms_norm_m(xn, x, L->attn_norm, QO_EMBD, T);
             if (QO_IS_ATTN(il)) attn_layer(m, s, il, xn, T, pos_now, ra);
             else qo_gdn_layer(m, s, il, xn, T, ra);
             for (size_t i = 0; i < (size_t)QO_EMBD * T; i++) x2[i] = ra[i] + x[i];
+            if (n_layers < 0 && il == nl - 1) {   /* stop after this layer's mixer */
+                memcpy(x, x2, sizeof(float) * (size_t)QO_EMBD * T);
+                break;
+            }
             rms_norm_m(xn, x2, L->post_norm, QO_EMBD, T);
             qo_moe_ffn(m, il, xn, T, ra, NULL, NULL);
             for (size_t i = 0; i < (size_t)QO_EMBD * T; i++) x[i] = ra[i] + x2[i];
         }
+        if (hidden) memcpy(hidden + (size_t)done * QO_EMBD, x, sizeof(float) * (size_t)QO_EMBD * T);
+        if (n_layers < QO_LAYER) { done += T; continue; }
         rms_norm_m(xn, x, m->output_norm, QO_EMBD, T);
         if (logits_all) {
             if (logits)

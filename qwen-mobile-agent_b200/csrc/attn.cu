@@ -136,12 +136,16 @@ __global__ void __launch_bounds__(256) qk_prep_append_kernel(
         const float qk = __fadd_rn(qfv[0], qfv[1]), qv = __fadd_rn(qfv[2], qfv[3]);
         qf[slot] = __fadd_rn(qk, qv) / (2.0f * NHEAD_KV);
     }
-    // new records: warp w < 4 writes record w (K0, K1, V0, V1)
+    // new records: warp w < 4 writes record w (K0, K1, V0, V1).  Every
+    // 20-byte sub-block is {fp16 d, fp16 m, 16 payload bytes}: the header and
+    // the payload are packed in registers and stored as aligned 32-bit words
+    // (slot, record and sub-block offsets are multiples of 4 bytes).
     if (warp < 4) {
         const int kh = warp & 1;
         uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
         const float *x = hv[NHEAD + warp];
-        // q4: 8 sub-blocks of 32 lanes, q = rint((x - mn) / d) in [0, 15]
+        // q4: 8 sub-blocks of 32 lanes, q = rint((x - mn) / d) in [0, 15];
+        // value i is nibble (i & 1) of payload byte i / 2 (kvq.c:25-46)
         for (int sb = 0; sb < 8; sb++) {
             const float v = x[sb * 32 + lane];
             float mn = v, mx = v;
@@ -154,15 +158,16 @@ __global__ void __launch_bounds__(256) qk_prep_append_kernel(
             if (!(d > 0)) d = 1.0f;
             int q = __float2int_rn(__fsub_rn(v, mn) / d);
             q = q < 0 ? 0 : (q > 15 ? 15 : q);
-            const int qn1 = __shfl_down_sync(0xffffffffu, q, 1);
-            if ((lane & 1) == 0) rec[sb * 20 + 4 + lane / 2] = uint8_t(q | (qn1 << 4));
-            if (lane == 0) {
-                const uint16_t dh = f2h(d), mh = f2h(mn);
-                rec[sb * 20 + 0] = uint8_t(dh & 0xff); rec[sb * 20 + 1] = uint8_t(dh >> 8);
-                rec[sb * 20 + 2] = uint8_t(mh & 0xff); rec[sb * 20 + 3] = uint8_t(mh >> 8);
-            }
+            // payload word k holds values 8k .. 8k+7
+            uint32_t w = uint32_t(q) << (4 * (lane & 7));
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) w |= __shfl_xor_sync(0xffffffffu, w, o);
+            uint32_t *blk = reinterpret_cast<uint32_t *>(rec + sb * 20);
+            if ((lane & 7) == 0) blk[1 + lane / 8] = w;
+            if (lane == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
         }
-        // q2: 4 sub-blocks of 64, OR-ed into the existing bytes (kvq.c:67)
+        // q2: 4 sub-blocks of 64, value i at bits 2 (i & 3) of payload byte
+        // i / 4, OR-ed into the existing payload (kvq.c:50-70)
         for (int sb = 0; sb < 4; sb++) {
             const float v0 = x[sb * 64 + lane], v1 = x[sb * 64 + 32 + lane];
             float mn = fminf(v0, v1), mx = fmaxf(v0, v1);
@@ -176,21 +181,19 @@ __global__ void __launch_bounds__(256) qk_prep_append_kernel(
             int q0 = __float2int_rn(__fsub_rn(v0, mn) / d), q1 = __float2int_rn(__fsub_rn(v1, mn) / d);
             q0 = q0 < 0 ? 0 : (q0 > 3 ? 3 : q0);
             q1 = q1 < 0 ? 0 : (q1 > 3 ? 3 : q1);
-            int b0 = q0 << (2 * (lane & 3)), b1 = q1 << (2 * (lane & 3));
-            b0 |= __shfl_down_sync(0xffffffffu, b0, 1);
-            b0 |= __shfl_down_sync(0xffffffffu, b0, 2);
-            b1 |= __shfl_down_sync(0xffffffffu, b1, 1);
-            b1 |= __shfl_down_sync(0xffffffffu, b1, 2);
-            uint8_t *q2 = rec + KVQ2_OFF + sb * 20;
-            if ((lane & 3) == 0) {
-                q2[4 + lane / 4] |= uint8_t(b0);
-                q2[4 + 8 + lane / 4] |= uint8_t(b1);
+            // payload word k holds values 16k .. 16k+15: v0 -> words 0, 1; v1 -> 2, 3
+            uint32_t w0 = uint32_t(q0) << (2 * (lane & 15)), w1 = uint32_t(q1) << (2 * (lane & 15));
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+                w0 |= __shfl_xor_sync(0xffffffffu, w0, o);
+                w1 |= __shfl_xor_sync(0xffffffffu, w1, o);
             }
-            if (lane == 0) {
-                const uint16_t dh = f2h(d), mh = f2h(mn);
-                q2[0] = uint8_t(dh & 0xff); q2[1] = uint8_t(dh >> 8);
-                q2[2] = uint8_t(mh & 0xff); q2[3] = uint8_t(mh >> 8);
+            uint32_t *blk = reinterpret_cast<uint32_t *>(rec + KVQ2_OFF + sb * 20);
+            if ((lane & 15) == 0) {
+                blk[1 + lane / 16] |= w0;
+                blk[3 + lane / 16] |= w1;
             }
+            if (lane == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
         }
     }
     if (tid < NATTN) sal[size_t(tid) * sp.n_ctx + slot] = 0.0f;

@@ -93,6 +93,7 @@ struct qma_cuda_state {
     int graph_nk = -1;
     int graph_kernels = 0;
     size_t state_bytes = 0;
+    bool stop_before_moe = false;   // qma_cuda_eval_hidden with n_layers < 0
     static constexpr int HCM_REBUILD_INIT = 128;
 };
 
@@ -619,7 +620,7 @@ __global__ void argmax_kernel(const float *__restrict__ logits, int n, StepParam
 // The forward of T tokens at the positions in *sp_dev (host copy hs):
 // embedding -> 40 layers -> (optionally) final norm + LM head.
 static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
-                   int logits_mode /*0 none, 1 last, 2 all*/) {
+                   int logits_mode /*0 none, 1 last, 2 all*/, int n_layers = NLAYER) {
     qma_cuda_model *m = s->m;
     cudaStream_t st = s->st;
     const int T = hs.T;
@@ -627,7 +628,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
 #define TRY(x) do { if ((rc = (x))) return rc; } while (0)
     TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, tokens_dev, s->sp_dev, T, s->x, st));
     const int pv_chunk = T == 1 ? 64 : 256;
-    for (int il = 0; il < NLAYER; il++) {
+    for (int il = 0; il < n_layers; il++) {
         const LayerW &L = m->L[il];
         TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st));
         TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st));
@@ -652,6 +653,12 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
                                         s->xs, st));
             TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
+        }
+        if (il == n_layers - 1 && s->stop_before_moe) {
+            // parity aid: return the residual after the mixer of this layer
+            QMA_CHECK_CUDA(cudaMemcpyAsync(s->x, s->x2, sizeof(float) * size_t(T) * EMBD,
+                                           cudaMemcpyDeviceToDevice, st));
+            break;
         }
         // x = x2 + moe(rms_norm(x2) * post_norm)
         TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st));
@@ -691,7 +698,8 @@ static int maybe_rebuild(qma_cuda_state *s, int pos_now) {
     return QMA_CUDA_OK;
 }
 
-static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logits, int logits_all) {
+static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logits, int logits_all,
+                int n_layers = NLAYER, float *hidden = nullptr) {
     qma_cuda_model *m = s->m;
     cudaStream_t st = s->st;
     QMA_CHECK_CUDA(cudaSetDevice(m->device));
@@ -721,8 +729,11 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
         const int nk = nk_upper(s, pos_now, T, false);
         if ((rc = ensure_attn_scratch(s, T, nk, T == 1 ? 64 : 256))) return rc;
         const bool last = done + T == n_tokens;
-        const int mode = logits_all ? 2 : (last && logits ? 1 : 0);
-        if ((rc = forward(s, *s->sp_host, s->tokens_dev, nk, mode))) return rc;
+        const int mode = n_layers < NLAYER ? 0 : (logits_all ? 2 : (last && logits ? 1 : 0));
+        if ((rc = forward(s, *s->sp_host, s->tokens_dev, nk, mode, n_layers))) return rc;
+        if (hidden)
+            QMA_CHECK_CUDA(cudaMemcpyAsync(hidden + size_t(done) * EMBD, s->x, sizeof(float) * size_t(T) * EMBD,
+                                           cudaMemcpyDeviceToHost, st));
         if (mode == 2 && logits)
             QMA_CHECK_CUDA(cudaMemcpyAsync(logits + size_t(done) * m->n_vocab, s->logits,
                                            sizeof(float) * size_t(T) * m->n_vocab,
@@ -890,6 +901,17 @@ int qma_cuda_state_n_pos(const qma_cuda_state *s) { return s ? s->n_pos : -1; }
 
 void *qma_cuda_state_stream(const qma_cuda_state *s) { return s ? static_cast<void *>(s->st) : nullptr; }
 
+int qma_cuda_state_kv_slot(const qma_cuda_state *s, int lay, int head, int slot, uint8_t *out) {
+    qma::clear_error();
+    QMA_REQUIRE(s && out && lay >= 0 && lay < qma::NATTN && head >= 0 && head < 2 * qma::NHEAD_KV &&
+                    slot >= 0 && slot < s->n_ctx,
+                "qma_cuda_state_kv_slot: bad arguments");
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+    QMA_CHECK_CUDA(cudaMemcpy(out, s->kv[lay] + (size_t(head) * s->n_ctx + slot) * qma::KVQ_SLOT,
+                              qma::KVQ_SLOT, cudaMemcpyDeviceToHost));
+    return QMA_CUDA_OK;
+}
+
 int qma_cuda_state_stats(const qma_cuda_state *s, int *graph_kernels, uint64_t *state_bytes) {
     qma::clear_error();
     QMA_REQUIRE(s, "qma_cuda_state_stats: null state");
@@ -906,6 +928,18 @@ int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n
         QMA_REQUIRE(tokens[i] >= 0 && tokens[i] < m->n_vocab, "qma_cuda_eval: token %d out of range",
                     tokens[i]);
     return qma::eval(s, tokens, n_tokens, logits, logits_all);
+}
+
+int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n_tokens,
+                         int n_layers, float *hidden) {
+    qma::clear_error();
+    QMA_REQUIRE(m && s && s->m == m && tokens && n_tokens > 0 && hidden && n_layers >= -qma::NLAYER &&
+                    n_layers <= qma::NLAYER,
+                "qma_cuda_eval_hidden: bad arguments");
+    s->stop_before_moe = n_layers < 0;
+    const int rc = qma::eval(s, tokens, n_tokens, nullptr, 0, n_layers < 0 ? -n_layers : n_layers, hidden);
+    s->stop_before_moe = false;
+    return rc;
 }
 
 int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,

@@ -60,7 +60,9 @@ _SIGS.update({
     "qma_cuda_state_n_pos": (_i32, [_vp]),
     "qma_cuda_eval": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32]),
     "qma_cuda_decode_greedy": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
+    "qma_cuda_eval_hidden": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "qma_cuda_state_stream": (_vp, [_vp]),
+    "qma_cuda_state_kv_slot": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "qma_cuda_state_stats": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_u64)]),
 })
 
@@ -102,6 +104,13 @@ class State:
         out = np.zeros((rows, self.model.n_vocab), np.float32)
         call("qma_cuda_eval", self.model.h, self.h, ptr(toks), len(toks), ptr(out), int(logits_all))
         return out if logits_all else out[0]
+
+    def eval_hidden(self, tokens, n_layers: int):
+        import numpy as np
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros((len(toks), 2048), np.float32)
+        call("qma_cuda_eval_hidden", self.model.h, self.h, ptr(toks), len(toks), n_layers, ptr(out))
+        return out
 
     def decode_greedy(self, token: int, n_steps: int):
         import numpy as np

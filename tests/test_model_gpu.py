@@ -71,6 +71,25 @@ def oracle_run(om, prompt, decode_tokens):
     return out
 
 
+@pytest.mark.parametrize("n_layers", [1, 3, 4, 8, 40])
+def test_hidden_state_after_n_layers(full, n_layers):
+    """Residual stream after the first n layers (GDN layers 0-2, attention
+    layer 3, ...) for a 5-token prompt then one decode token."""
+    prompt = np.array([11, 22, 33, 44, 55], np.int32)
+    st = Q.State(full["model"], N_CTX)
+    L = O.lib()
+    os_ = L.qo_state_new(N_CTX)
+    try:
+        for toks in (prompt, np.array([66], np.int32)):
+            got = st.eval_hidden(toks, n_layers)
+            want = np.zeros_like(got)
+            L.qo_eval_hidden(full["om"], os_, O._ptr(toks), len(toks), n_layers, O._ptr(want))
+            assert_close(got, want, RTOL, f"hidden after {n_layers} layers, T={len(toks)}")
+    finally:
+        st.close()
+        L.qo_state_free(os_)
+
+
 def test_prompt_and_greedy_decode_match_reference_and_oracle(full):
     g = np.load(GOLDEN) if os.path.exists(GOLDEN) else None
     rng = np.random.default_rng(SEED)
