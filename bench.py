@@ -176,7 +176,7 @@ def run_decode_ours(args, world, rank, local):
     st = Q.State(model, N_CTX)
     stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(st.h), device=local)
     rng = np.random.default_rng(SEED + rank)
-    prompt = rng.integers(0, N_VOCAB, PROMPT).astype(np.int32)
+    prompt = rng.integers(0, N_VOCAB, args.prompt).astype(np.int32)
     t0 = time.time()
     logits = st.eval(prompt)
     t_prefill = time.time() - t0
@@ -188,10 +188,12 @@ def run_decode_ours(args, world, rank, local):
     with ClockSampler(local) as clk:
         dist_barrier(world)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")
         e0.record(stream)
         toks, logits = st.decode_greedy(tok, args.steps)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         dist_barrier(world)
     ms = dist_max(e0.elapsed_time(e1), world)
     tok = int(np.argmax(logits))
@@ -231,9 +233,9 @@ def run_decode_ours(args, world, rank, local):
         "data": "synthetic: random-init weights (seeded N(0,0.02), engine quantizers) and uniform random prompt ids",
         "config": {"workload": "configs[3] full qwen35moe decode bs1: 40 layers (3 GDN + 1 attn) x10, "
                                "256 experts top-8 + shared, vocab 151936, Q4_K experts/projections, "
-                               "Q6_K down, Q8_0 embeddings + LM head; 8192-token prompt (prefill untimed), "
+                               f"Q6_K down, Q8_0 embeddings + LM head; {args.prompt}-token prompt (prefill untimed), "
                                "then greedy decode; KV ring n_ctx 65536 with 4/2-bit tiers (sink 4, hot 4096)",
-                   "model": "qwen35moe-random-init", "global_batch": 1, "seq_len": PROMPT,
+                   "model": "qwen35moe-random-init", "global_batch": 1, "seq_len": args.prompt,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "each step streams ~2 GB of weights (> 126 MB L2)",
                    "prefill_s": round(t_prefill, 2), "model_synth_s": round(t_model, 2),
@@ -423,6 +425,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--prompt", type=int, default=PROMPT,
+                    help="decode: prompt tokens prefilled before the timed steps")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:

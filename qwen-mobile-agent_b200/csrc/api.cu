@@ -18,6 +18,8 @@ void set_error(const char *fmt, ...) {
 
 void clear_error() { g_err[0] = 0; }
 
+bool pdl_enabled() { return true; }
+
 size_t packed_bytes(int wtype, int rows, int n) {
     switch (wtype) {
     case QMA_TYPE_Q4_K: return size_t(rows) * (n / QK) * Q4K_BYTES;

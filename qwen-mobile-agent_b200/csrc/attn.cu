@@ -47,82 +47,105 @@ __device__ __forceinline__ const uint8_t *rec_of(const StepParams &sp, const int
 }
 
 // ------------------------------------------------------ q/k prep + append --
-// One CTA (256 threads) per token: q_norm / k_norm (nn.c:2116-2137, v *=
-// r * w with a double accumulator), IMROPE on dims (j, j+32), j < 32
-// (rope_imrope, nn.c:841-861; cos/sin come from a host-built table so they
-// equal the reference's libm values), the gate copy to z, and the append of
-// K and V as q4 + q2 records into the ring slot (kv_append): the Q-Hitter
-// score of the slot's previous contents first (kvq4_qf, kvq.c:84-100), then
-// the new records (kvq4_quant / kvq2_quant, kvq.c:25-70), then the slot's
-// salience in every layer reset to 0.
-__global__ void __launch_bounds__(256) qk_prep_append_kernel(
+// Grid (T, 5), 128 threads; each warp owns one 256-wide head vector, lane l
+// holding elements 8l .. 8l+7.  CTAs y = 0..3 handle query heads 4y .. 4y+3:
+// q_norm (v *= r * w, r from a double sum of squares, nn.c:2116-2137), the
+// IMROPE rotation of dims (j, j+32), j < 32 (rope_imrope, nn.c:841-861; the
+// cos/sin table is built on the host with the reference's libm calls), and
+// the copy of the head's gate half to z.  CTA y = 4 appends the token to the
+// KV ring (kv_append, nn.c:1455-1509): warps 0, 1 normalise and rotate K
+// heads 0, 1, warps 2, 3 take V heads 0, 1 raw; each warp scores its slot's
+// old q4 record against the new vector (kvq4_qf, kvq.c:84-100), then writes
+// the q4 and q2 records (kvq4_quant / kvq2_quant, kvq.c:25-70), and the
+// slot's salience in every layer is reset to 0.
+__device__ __forceinline__ void head_norm(float (&x)[8], const float *w, int lane) {
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) ss += double(x[k]) * double(x[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = 1.0f / sqrtf(float(ss / HEAD_DIM) + 1e-6f);
+    const float4 w0 = *reinterpret_cast<const float4 *>(w + lane * 8);
+    const float4 w1 = *reinterpret_cast<const float4 *>(w + lane * 8 + 4);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = __fmul_rn(x[k], __fmul_rn(r, wv[k]));
+}
+
+// rotate pairs (j, j+32), j < 32: lanes 0..3 hold j, lanes 4..7 hold j+32
+__device__ __forceinline__ void head_rope(float (&x)[8], const float *cs, int lane) {
+    float y[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) y[k] = __shfl_xor_sync(0xffffffffu, x[k], 4);
+    if (lane < 8) {
+        const int j0 = (lane & 3) * 8;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float c = cs[j0 + k], sn = cs[NROT / 2 + j0 + k];
+            if (lane < 4) x[k] = __fsub_rn(__fmul_rn(x[k], c), __fmul_rn(y[k], sn));
+            else x[k] = __fadd_rn(__fmul_rn(y[k], sn), __fmul_rn(x[k], c));
+        }
+    }
+}
+
+__device__ __forceinline__ void ld8(float (&x)[8], const float *p) {
+    const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ void st8(float *p, const float (&x)[8]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<float4 *>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+__global__ void __launch_bounds__(128) qk_prep_append_kernel(
     const float *__restrict__ proj, int proj_ld, const float *__restrict__ qn,
     const float *__restrict__ kn, const float *__restrict__ rope, const StepParams *spp,
     float *qr, float *z, uint8_t *kv, float *qf, float *sal) {
-    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ __align__(16) float hv[NHEAD + 2 * NHEAD_KV][HEAD_DIM];   // q heads, k heads, v heads
+    const int t = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float qfv[4];
+    pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
     const int pos = sp.n_pos + t;
     const int slot = hcm_slot(pos, sp.n_ctx);
     const float *row = proj + size_t(t) * proj_ld;
-    // norms: warp w handles vectors w, w + 8, w + 16 (16 q heads, 2 k heads)
-    for (int v = warp; v < NHEAD + NHEAD_KV; v += 8) {
-        const bool isq = v < NHEAD;
-        const float *src = isq ? row + v * (2 * HEAD_DIM) : row + WQ_DIM + (v - NHEAD) * HEAD_DIM;
-        const float *w = isq ? qn : kn;
-        float x[8];
-        double ss = 0.0;
+    const float *cs = rope + size_t(pos) * NROT;     // [32 cos][32 sin]
+    float x[8];
+    if (part < 4) {
+        const int h = part * 4 + warp;
+        ld8(x, row + h * (2 * HEAD_DIM) + lane * 8);
+        head_norm(x, qn, lane);
+        head_rope(x, cs, lane);
+        st8(qr + (size_t(t) * NHEAD + h) * HEAD_DIM + lane * 8, x);
+        float g[8];
+        ld8(g, row + h * (2 * HEAD_DIM) + HEAD_DIM + lane * 8);
+        st8(z + size_t(t) * WO_DIM + h * HEAD_DIM + lane * 8, g);
+        return;
+    }
+    // warp w: record w = K0, K1, V0, V1
+    const int kh = warp & 1;
+    if (warp < 2) {
+        ld8(x, row + WQ_DIM + kh * HEAD_DIM + lane * 8);
+        head_norm(x, kn, lane);
+        head_rope(x, cs, lane);
+    } else {
+        ld8(x, row + WQ_DIM + WKV_DIM + kh * HEAD_DIM + lane * 8);
+    }
+    uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
+    {   // Q-Hitter score of the slot's current q4 record against x (lane:
+        // elements 8l .. 8l+7, sub-block l / 4)
+        const uint32_t *sbw = reinterpret_cast<const uint32_t *>(rec + (lane >> 2) * 20);
+        const uint32_t hdr = sbw[0];
+        const uint32_t nw = sbw[1 + (lane & 3)];
+        const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
+        double se = 0.0, sx = 0.0;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            x[k] = src[lane * 8 + k];
-            ss += double(x[k]) * double(x[k]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float r = 1.0f / sqrtf(float(ss / HEAD_DIM) + 1e-6f);
-#pragma unroll
-        for (int k = 0; k < 8; k++) hv[v][lane * 8 + k] = __fmul_rn(x[k], __fmul_rn(r, w[lane * 8 + k]));
-        if (isq) {
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                z[size_t(t) * WO_DIM + v * HEAD_DIM + lane * 8 + k] = row[v * (2 * HEAD_DIM) + HEAD_DIM + lane * 8 + k];
-        }
-    }
-    // V heads (raw)
-    for (int i = tid; i < NHEAD_KV * HEAD_DIM; i += 256)
-        hv[NHEAD + NHEAD_KV + i / HEAD_DIM][i % HEAD_DIM] = row[WQ_DIM + WKV_DIM + i];
-    __syncthreads();
-    // IMROPE: 18 rotated vectors x 32 pairs
-    const float *cs = rope + size_t(pos) * NROT;     // [32 cos][32 sin]
-    for (int i = tid; i < (NHEAD + NHEAD_KV) * (NROT / 2); i += 256) {
-        const int v = i / (NROT / 2), j = i % (NROT / 2);
-        const float c = cs[j], s = cs[NROT / 2 + j];
-        const float x0 = hv[v][j], x1 = hv[v][j + NROT / 2];
-        hv[v][j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        hv[v][j + NROT / 2] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    }
-    __syncthreads();
-    for (int i = tid; i < NHEAD * HEAD_DIM; i += 256)
-        qr[size_t(t) * NHEAD * HEAD_DIM + i] = hv[i / HEAD_DIM][i % HEAD_DIM];
-    // Q-Hitter score of the slot's current q4 records vs the new K/V
-    // (warps 0..3: K head 0, K head 1, V head 0, V head 1)
-    if (warp < 4) {
-        const int kh = warp & 1;
-        const uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
-        const float *x = hv[NHEAD + warp];   // K0, K1, V0, V1 in that order
-        double se = 0.0, sx = 0.0;
-        for (int i = lane; i < HEAD_DIM; i += 32) {
-            const int sb = i / 32, l = i % 32;
-            const float d = h2f(uint16_t(rec[sb * 20] | (rec[sb * 20 + 1] << 8)));
-            const float m = h2f(uint16_t(rec[sb * 20 + 2] | (rec[sb * 20 + 3] << 8)));
-            const uint8_t b = rec[sb * 20 + 4 + l / 2];
-            const int q = (l & 1) ? (b >> 4) : (b & 0xF);
+            const int q = (nw >> (4 * k)) & 0xF;
             const float v = __fadd_rn(__fmul_rn(float(q), d), m);
-            const float e = __fsub_rn(v, x[i]);
+            const float e = __fsub_rn(v, x[k]);
             se += double(e) * double(e);
-            sx += double(x[i]) * double(x[i]);
+            sx += double(x[k]) * double(x[k]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -131,256 +154,296 @@ __global__ void __launch_bounds__(256) qk_prep_append_kernel(
         }
         if (lane == 0) qfv[warp] = sx <= 0 ? 0.0f : float(sqrt(se / sx));
     }
+    // Every 20-byte sub-block is {fp16 d, fp16 m, 16 payload bytes}, packed
+    // in registers and stored as aligned 32-bit words.
+    // q4: 8 sub-blocks of 32; value i is nibble (i & 1) of payload byte i / 2.
+    // Lane l holds values 8l .. 8l+7 = sub-block l / 4, payload word l % 4.
+    {
+        float mn = x[0], mx = x[0];
+#pragma unroll
+        for (int k = 1; k < 8; k++) { mn = fminf(mn, x[k]); mx = fmaxf(mx, x[k]); }
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        float d = __fsub_rn(mx, mn) / 15.0f;
+        if (!(d > 0)) d = 1.0f;
+        uint32_t w = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            int q = __float2int_rn(__fsub_rn(x[k], mn) / d);
+            q = q < 0 ? 0 : (q > 15 ? 15 : q);
+            w |= uint32_t(q) << (4 * k);
+        }
+        uint32_t *blk = reinterpret_cast<uint32_t *>(rec + (lane >> 2) * 20);
+        blk[1 + (lane & 3)] = w;
+        if ((lane & 3) == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
+    }
+    // q2: 4 sub-blocks of 64; value i at bits 2 (i & 3) of payload byte i / 4,
+    // OR-ed into the existing payload.  Lane l: sub-block l / 8, values
+    // 8 (l % 8) .. +7 = payload bytes 2 (l % 8), 2 (l % 8) + 1 = the half
+    // (l % 2) of payload word (l % 8) / 2.
+    {
+        float mn = x[0], mx = x[0];
+#pragma unroll
+        for (int k = 1; k < 8; k++) { mn = fminf(mn, x[k]); mx = fmaxf(mx, x[k]); }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        float d = __fsub_rn(mx, mn) / 3.0f;
+        if (!(d > 0)) d = 1.0f;
+        uint32_t w = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            int q = __float2int_rn(__fsub_rn(x[k], mn) / d);
+            q = q < 0 ? 0 : (q > 3 ? 3 : q);
+            w |= uint32_t(q) << (2 * k);
+        }
+        w <<= 16 * (lane & 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        uint32_t *blk = reinterpret_cast<uint32_t *>(rec + KVQ2_OFF + (lane >> 3) * 20);
+        if ((lane & 1) == 0) blk[1 + ((lane & 7) >> 1)] |= w;
+        if ((lane & 7) == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
+    }
     __syncthreads();
     if (tid == 0) {
         const float qk = __fadd_rn(qfv[0], qfv[1]), qv = __fadd_rn(qfv[2], qfv[3]);
         qf[slot] = __fadd_rn(qk, qv) / (2.0f * NHEAD_KV);
     }
-    // new records: warp w < 4 writes record w (K0, K1, V0, V1).  Every
-    // 20-byte sub-block is {fp16 d, fp16 m, 16 payload bytes}: the header and
-    // the payload are packed in registers and stored as aligned 32-bit words
-    // (slot, record and sub-block offsets are multiples of 4 bytes).
-    if (warp < 4) {
-        const int kh = warp & 1;
-        uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
-        const float *x = hv[NHEAD + warp];
-        // q4: 8 sub-blocks of 32 lanes, q = rint((x - mn) / d) in [0, 15];
-        // value i is nibble (i & 1) of payload byte i / 2 (kvq.c:25-46)
-        for (int sb = 0; sb < 8; sb++) {
-            const float v = x[sb * 32 + lane];
-            float mn = v, mx = v;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            }
-            float d = __fsub_rn(mx, mn) / 15.0f;
-            if (!(d > 0)) d = 1.0f;
-            int q = __float2int_rn(__fsub_rn(v, mn) / d);
-            q = q < 0 ? 0 : (q > 15 ? 15 : q);
-            // payload word k holds values 8k .. 8k+7
-            uint32_t w = uint32_t(q) << (4 * (lane & 7));
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) w |= __shfl_xor_sync(0xffffffffu, w, o);
-            uint32_t *blk = reinterpret_cast<uint32_t *>(rec + sb * 20);
-            if ((lane & 7) == 0) blk[1 + lane / 8] = w;
-            if (lane == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
-        }
-        // q2: 4 sub-blocks of 64, value i at bits 2 (i & 3) of payload byte
-        // i / 4, OR-ed into the existing payload (kvq.c:50-70)
-        for (int sb = 0; sb < 4; sb++) {
-            const float v0 = x[sb * 64 + lane], v1 = x[sb * 64 + 32 + lane];
-            float mn = fminf(v0, v1), mx = fmaxf(v0, v1);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            }
-            float d = __fsub_rn(mx, mn) / 3.0f;
-            if (!(d > 0)) d = 1.0f;
-            int q0 = __float2int_rn(__fsub_rn(v0, mn) / d), q1 = __float2int_rn(__fsub_rn(v1, mn) / d);
-            q0 = q0 < 0 ? 0 : (q0 > 3 ? 3 : q0);
-            q1 = q1 < 0 ? 0 : (q1 > 3 ? 3 : q1);
-            // payload word k holds values 16k .. 16k+15: v0 -> words 0, 1; v1 -> 2, 3
-            uint32_t w0 = uint32_t(q0) << (2 * (lane & 15)), w1 = uint32_t(q1) << (2 * (lane & 15));
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) {
-                w0 |= __shfl_xor_sync(0xffffffffu, w0, o);
-                w1 |= __shfl_xor_sync(0xffffffffu, w1, o);
-            }
-            uint32_t *blk = reinterpret_cast<uint32_t *>(rec + KVQ2_OFF + sb * 20);
-            if ((lane & 15) == 0) {
-                blk[1 + lane / 16] |= w0;
-                blk[3 + lane / 16] |= w1;
-            }
-            if (lane == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
-        }
-    }
     if (tid < NATTN) sal[size_t(tid) * sp.n_ctx + slot] = 0.0f;
 }
 
-// --------------------------------------------------------------- scores --
-// Q.K of every attended position for the 8 query heads of one KV head
-// (GQA: kv head = q head / 8): one thread per (position, pair of heads),
-// the record dequantized on the fly (kvq4_dot / kvq2_dot, kvq.c:183-213,
-// keeping their 4-lane partial sums and pairwise reduction).
-constexpr int SC_POS = 64;          // positions per scores CTA
+// ---------------------------------------------------- chunked attention ----
+// Grid (ceil(nk_max / span), KV head, query t), 256 threads.  A CTA covers
+// `span` attended positions of one KV head for its 8 query heads (GQA: KV
+// head = query head / 8) in sub-chunks of 64: the sub-chunk's K and V
+// records (q4: 160 B, q2: 80 B) are staged in shared memory with 16-byte
+// loads; thread (position i, head pair hp) computes two scores with the
+// record kernels' own order (kvq4_dot / kvq2_dot, kvq.c:183-213: four lane
+// partial sums per sub-block, pairwise reduced); warp h keeps the running max
+// and sum of p = expf(s - max) for head h; thread d accumulates
+// sum p * V[d] for the 8 heads (kvq4_vacc / kvq2_vacc, kvq.c:215-241),
+// rescaled when the running max grows.  Outputs: the raw scores (for the
+// salience update) and per-CTA (max, sum, partial output).
+constexpr int SUB = 64;
+constexpr int QS_LD = HEAD_DIM + 4;      // padded query rows: conflict-free float4 reads
 
-__device__ __forceinline__ float rec_dot(const uint8_t *rec, bool q2, const float *q) {
-    float acc = 0.0f;
+__device__ __forceinline__ float q4_val(uint32_t nw, int k, float d, float m) {
+    return __fadd_rn(m, __fmul_rn(float((nw >> (4 * k)) & 0xF), d));
+}
+
+// two scores (heads qa, qb) of a staged record
+__device__ __forceinline__ void rec_dot2(const uint32_t *w, bool q2, const float *qa,
+                                         const float *qb, float &sa, float &sb_) {
+    float acc_a = 0.0f, acc_b = 0.0f;
     if (!q2) {
+#pragma unroll 1
         for (int sb = 0; sb < 8; sb++) {
-            const uint8_t *b = rec + sb * 20;
-            const float d = h2f(uint16_t(b[0] | (b[1] << 8))), m = h2f(uint16_t(b[2] | (b[3] << 8)));
-            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t hdr = w[5 * sb];
+            const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f}, b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int k = 0; k < 8; k++)
+            for (int wi = 0; wi < 4; wi++) {
+                const uint32_t nw = w[5 * sb + 1 + wi];       // values 8 wi .. 8 wi + 7
 #pragma unroll
-                for (int l = 0; l < 4; l++) {
-                    const int i = 4 * k + l;
-                    const uint8_t byte = b[4 + i / 2];
-                    const int qv = (i & 1) ? (byte >> 4) : (byte & 0xF);
-                    const float e = __fadd_rn(m, __fmul_rn(float(qv), d));
-                    a[l] = __fadd_rn(a[l], __fmul_rn(e, q[sb * 32 + i]));
+                for (int half = 0; half < 2; half++) {
+                    const int i0 = sb * 32 + wi * 8 + half * 4;
+                    const float4 xa = *reinterpret_cast<const float4 *>(qa + i0);
+                    const float4 xb = *reinterpret_cast<const float4 *>(qb + i0);
+                    const float e0 = q4_val(nw, 4 * half + 0, d, m), e1 = q4_val(nw, 4 * half + 1, d, m);
+                    const float e2 = q4_val(nw, 4 * half + 2, d, m), e3 = q4_val(nw, 4 * half + 3, d, m);
+                    a[0] = __fadd_rn(a[0], __fmul_rn(e0, xa.x)); b[0] = __fadd_rn(b[0], __fmul_rn(e0, xb.x));
+                    a[1] = __fadd_rn(a[1], __fmul_rn(e1, xa.y)); b[1] = __fadd_rn(b[1], __fmul_rn(e1, xb.y));
+                    a[2] = __fadd_rn(a[2], __fmul_rn(e2, xa.z)); b[2] = __fadd_rn(b[2], __fmul_rn(e2, xb.z));
+                    a[3] = __fadd_rn(a[3], __fmul_rn(e3, xa.w)); b[3] = __fadd_rn(b[3], __fmul_rn(e3, xb.w));
                 }
-            acc = __fadd_rn(acc, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
+            }
+            acc_a = __fadd_rn(acc_a, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
+            acc_b = __fadd_rn(acc_b, __fadd_rn(__fadd_rn(b[0], b[1]), __fadd_rn(b[2], b[3])));
         }
     } else {
+#pragma unroll 1
         for (int sb = 0; sb < 4; sb++) {
-            const uint8_t *b = rec + sb * 20;
-            const float d = h2f(uint16_t(b[0] | (b[1] << 8))), m = h2f(uint16_t(b[2] | (b[3] << 8)));
-            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t hdr = w[5 * sb];
+            const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f}, b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int k = 0; k < 16; k++)
+            for (int wi = 0; wi < 4; wi++) {
+                const uint32_t pw = w[5 * sb + 1 + wi];       // values 16 wi .. 16 wi + 15
 #pragma unroll
-                for (int l = 0; l < 4; l++) {
-                    const int i = 4 * k + l;
-                    const int qv = (b[4 + i / 4] >> (2 * (i & 3))) & 3;
-                    const float e = __fadd_rn(m, __fmul_rn(float(qv), d));
-                    a[l] = __fadd_rn(a[l], __fmul_rn(e, q[sb * 64 + i]));
+                for (int qd = 0; qd < 4; qd++) {
+                    const int i0 = sb * 64 + wi * 16 + qd * 4;
+                    const float4 xa = *reinterpret_cast<const float4 *>(qa + i0);
+                    const float4 xb = *reinterpret_cast<const float4 *>(qb + i0);
+                    const uint32_t by = pw >> (8 * qd);
+                    float e[4];
+#pragma unroll
+                    for (int l = 0; l < 4; l++) e[l] = __fadd_rn(m, __fmul_rn(float((by >> (2 * l)) & 3), d));
+                    a[0] = __fadd_rn(a[0], __fmul_rn(e[0], xa.x)); b[0] = __fadd_rn(b[0], __fmul_rn(e[0], xb.x));
+                    a[1] = __fadd_rn(a[1], __fmul_rn(e[1], xa.y)); b[1] = __fadd_rn(b[1], __fmul_rn(e[1], xb.y));
+                    a[2] = __fadd_rn(a[2], __fmul_rn(e[2], xa.z)); b[2] = __fadd_rn(b[2], __fmul_rn(e[2], xb.z));
+                    a[3] = __fadd_rn(a[3], __fmul_rn(e[3], xa.w)); b[3] = __fadd_rn(b[3], __fmul_rn(e[3], xb.w));
                 }
-            acc = __fadd_rn(acc, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
+            }
+            acc_a = __fadd_rn(acc_a, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
+            acc_b = __fadd_rn(acc_b, __fadd_rn(__fadd_rn(b[0], b[1]), __fadd_rn(b[2], b[3])));
         }
     }
-    return acc;
+    sa = acc_a;
+    sb_ = acc_b;
 }
 
-__global__ void __launch_bounds__(256) attn_scores_kernel(const float *__restrict__ qr,
-                                                          const uint8_t *__restrict__ kv,
-                                                          const uint8_t *__restrict__ arena,
-                                                          const int *__restrict__ live,
-                                                          const StepParams *spp, float *scores,
-                                                          int nk_max, float *cmax, int nchunk) {
-    const int chunk = blockIdx.x, kh = blockIdx.y, t = blockIdx.z;
-    const int tid = threadIdx.x, pi = tid >> 2, hp = tid & 3;
-    __shared__ __align__(16) float qs[8][HEAD_DIM];
-    __shared__ float mred[SC_POS][8];
-    pdl_wait();
-    const StepParams sp = *spp;
-    for (int i = tid; i < 8 * HEAD_DIM; i += 256)
-        qs[i / HEAD_DIM][i % HEAD_DIM] = qr[(size_t(t) * NHEAD + kh * 8) * HEAD_DIM + i];
-    __syncthreads();
-    const int nk = nk_of(sp, t);
-    const int jj = chunk * SC_POS + pi;
-    float s0 = -INFINITY, s1 = -INFINITY;
-    if (jj < nk) {
-        bool q2;
-        const uint8_t *rec = rec_of(sp, live, kv + size_t(kh) * sp.n_ctx * KVQ_SLOT,
-                                    arena + size_t(kh) * HCM_H_PIN * KVQ_SLOT, jj, q2);
-        const float scale = 1.0f / sqrtf(float(HEAD_DIM));
-        s0 = __fmul_rn(rec_dot(rec, q2, qs[2 * hp]), scale);
-        s1 = __fmul_rn(rec_dot(rec, q2, qs[2 * hp + 1]), scale);
-        float *srow = scores + (size_t(t) * NHEAD + kh * 8 + 2 * hp) * nk_max;
-        srow[jj] = s0;
-        srow[nk_max + jj] = s1;
-    }
-    mred[pi][2 * hp] = s0;
-    mred[pi][2 * hp + 1] = s1;
-    __syncthreads();
-    if (tid < 8) {
-        float m = -INFINITY;
-        for (int p = 0; p < SC_POS; p++) m = fmaxf(m, mred[p][tid]);
-        cmax[(size_t(t) * NHEAD + kh * 8 + tid) * nchunk + chunk] = m;
-    }
-}
-
-// -------------------------------------------------------- softmax . V -----
-// Per (position chunk, KV head, query): p = expf(s - max) with the global
-// max of the head, the chunk's sum of p, and the chunk's sum of p * V
-// (kvq4_vacc / kvq2_vacc, kvq.c:215-241) for its 8 heads; one thread per
-// output dimension.
-__global__ void __launch_bounds__(256) attn_pv_kernel(const float *__restrict__ scores,
-                                                      int nk_max, const float *__restrict__ cmax,
-                                                      int nchunk_sc, const uint8_t *__restrict__ kv,
-                                                      const uint8_t *__restrict__ arena,
-                                                      const int *__restrict__ live,
-                                                      const StepParams *spp, int chunk_pos,
-                                                      float *opart, float *lpart, int nchunk) {
+__global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict__ qr,
+                                                         const uint8_t *__restrict__ kv,
+                                                         const uint8_t *__restrict__ arena,
+                                                         const int *__restrict__ live,
+                                                         const StepParams *spp, int nk_max,
+                                                         int span, int nchunk, float *scores,
+                                                         float *mpart, float *lpart, float *opart) {
     const int chunk = blockIdx.x, kh = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float M[8], pj[8][64];
+    __shared__ __align__(16) float qs[8 * QS_LD];
+    __shared__ __align__(16) uint4 kst[SUB][10];
+    __shared__ __align__(16) uint4 vst[SUB][10];
+    __shared__ const uint8_t *kp[SUB], *vp[SUB];
+    __shared__ int isq2[SUB];
+    __shared__ float ps[8][SUB];
+    __shared__ float scl[8];
+    pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
     const int nk = nk_of(sp, t);
-    {   // warp h: global max of head kh*8 + h
-        const float *cm = cmax + (size_t(t) * NHEAD + kh * 8 + warp) * nchunk_sc;
-        float m = -INFINITY;
-        for (int c = lane; c < nchunk_sc; c += 32) m = fmaxf(m, cm[c]);
-        m = warp_max(m);
-        if (lane == 0) M[warp] = m;
-    }
-    __syncthreads();
-    const int j0 = chunk * chunk_pos, j1 = min(nk, j0 + chunk_pos);
-    float acc[8], lsum = 0.0f;
+    const int j0 = chunk * span;
+    if (j0 >= nk) return;
+    const int j1 = min(nk, j0 + span);
+    for (int i = tid; i < 8 * HEAD_DIM; i += 256)
+        qs[(i / HEAD_DIM) * QS_LD + i % HEAD_DIM] = qr[(size_t(t) * NHEAD + kh * 8) * HEAD_DIM + i];
+    const uint8_t *kring = kv + size_t(kh) * sp.n_ctx * KVQ_SLOT;
+    const uint8_t *vring = kv + size_t(NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT;
+    const uint8_t *kar = arena + size_t(kh) * HCM_H_PIN * KVQ_SLOT;
+    const uint8_t *var = arena + size_t(NHEAD_KV + kh) * HCM_H_PIN * KVQ_SLOT;
+    float m_run = -INFINITY, l_run = 0.0f;     // warp h: head h (lane-uniform)
+    float acc[8];
 #pragma unroll
     for (int h = 0; h < 8; h++) acc[h] = 0.0f;
-    const uint8_t *ring = kv + size_t(NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT;
-    const uint8_t *ar = arena + size_t(NHEAD_KV + kh) * HCM_H_PIN * KVQ_SLOT;
     const int d = tid;
-    for (int b0 = j0; b0 < j1; b0 += 64) {
-        const int bn = min(64, j1 - b0);
-        __syncthreads();
-        for (int i = tid; i < 8 * 64; i += 256) {
-            const int h = i / 64, jj = i % 64;
-            pj[h][jj] = jj < bn ? expf(scores[(size_t(t) * NHEAD + kh * 8 + h) * nk_max + b0 + jj] - M[h]) : 0.0f;
+    for (int b0 = j0; b0 < j1; b0 += SUB) {
+        const int bn = min(SUB, j1 - b0);
+        __syncthreads();     // previous sub-chunk fully consumed
+        if (tid < bn) {
+            bool q2;
+            kp[tid] = rec_of(sp, live, kring, kar, b0 + tid, q2);
+            bool q2v;
+            vp[tid] = rec_of(sp, live, vring, var, b0 + tid, q2v);
+            isq2[tid] = q2;
         }
         __syncthreads();
-        if (warp == 0) {
-            // sum of p over this block, per head (lane h)
-            for (int h = 0; h < 8; h++) {
-                float s = pj[h][lane] + pj[h][lane + 32];
-                s = warp_sum(s);
-                if (lane == h) lsum += s;
+        for (int idx = tid; idx < bn * 10; idx += 256) {
+            const int i = idx / 10, wq = idx % 10;
+            if (wq < (isq2[i] ? 5 : 10)) {
+                kst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(kp[i]) + wq);
+                vst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(vp[i]) + wq);
             }
         }
-        for (int jj = 0; jj < bn; jj++) {
-            bool q2;
-            const uint8_t *rec = rec_of(sp, live, ring, ar, b0 + jj, q2);
+        __syncthreads();
+        {   // scores: thread (i, hp)
+            const int i = tid >> 2, hp = tid & 3;
+            float sa = -INFINITY, sb = -INFINITY;
+            if (i < bn) {
+                rec_dot2(reinterpret_cast<const uint32_t *>(kst[i]), isq2[i] != 0, qs + (2 * hp) * QS_LD,
+                         qs + (2 * hp + 1) * QS_LD, sa, sb);
+                sa = __fmul_rn(sa, 0.0625f);       // 1 / sqrtf(256)
+                sb = __fmul_rn(sb, 0.0625f);
+                float *srow = scores + (size_t(t) * NHEAD + kh * 8 + 2 * hp) * nk_max + b0 + i;
+                srow[0] = sa;
+                srow[nk_max] = sb;
+            }
+            ps[2 * hp][i] = sa;
+            ps[2 * hp + 1][i] = sb;
+        }
+        __syncthreads();
+        {   // warp h: running max / sum of head h, p of this sub-chunk
+            const int h = warp;
+            const float s0 = ps[h][lane], s1 = ps[h][lane + 32];
+            const float mloc = warp_max(fmaxf(s0, s1));
+            const float m_new = fmaxf(m_run, mloc);
+            const float p0 = lane < bn ? expf(s0 - m_new) : 0.0f;
+            const float p1 = lane + 32 < bn ? expf(s1 - m_new) : 0.0f;
+            const float c = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+            l_run = __fadd_rn(__fmul_rn(l_run, c), warp_sum(p0 + p1));
+            m_run = m_new;
+            __syncwarp();
+            ps[h][lane] = p0;
+            ps[h][lane + 32] = p1;
+            if (lane == 0) scl[h] = c;
+        }
+        __syncthreads();
+        // p . V for output dim d
+#pragma unroll
+        for (int h = 0; h < 8; h++) acc[h] = __fmul_rn(acc[h], scl[h]);
+        for (int i = 0; i < bn; i++) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(vst[i]);
             float v;
-            if (!q2) {
-                const uint8_t *b = rec + (d / 32) * 20;
-                const float dd = h2f(uint16_t(b[0] | (b[1] << 8))), m = h2f(uint16_t(b[2] | (b[3] << 8)));
-                const uint8_t byte = b[4 + (d % 32) / 2];
-                const int qv = (d & 1) ? (byte >> 4) : (byte & 0xF);
-                v = __fadd_rn(m, __fmul_rn(float(qv), dd));
+            if (!isq2[i]) {
+                const int sb = d >> 5, l = d & 31;
+                const uint32_t hdr = w[5 * sb];
+                const uint32_t nw = w[5 * sb + 1 + (l >> 3)];
+                v = __fadd_rn(h2f(uint16_t(hdr >> 16)),
+                              __fmul_rn(float((nw >> (4 * (l & 7))) & 0xF), h2f(uint16_t(hdr & 0xffff))));
             } else {
-                const uint8_t *b = rec + (d / 64) * 20;
-                const float dd = h2f(uint16_t(b[0] | (b[1] << 8))), m = h2f(uint16_t(b[2] | (b[3] << 8)));
-                const int qv = (b[4 + (d % 64) / 4] >> (2 * (d & 3))) & 3;
-                v = __fadd_rn(m, __fmul_rn(float(qv), dd));
+                const int sb = d >> 6, l = d & 63;
+                const uint32_t hdr = w[5 * sb];
+                const uint32_t pw = w[5 * sb + 1 + (l >> 4)];
+                v = __fadd_rn(h2f(uint16_t(hdr >> 16)),
+                              __fmul_rn(float((pw >> (2 * (l & 15))) & 3), h2f(uint16_t(hdr & 0xffff))));
             }
 #pragma unroll
-            for (int h = 0; h < 8; h++) acc[h] = __fadd_rn(acc[h], __fmul_rn(pj[h][jj], v));
+            for (int h = 0; h < 8; h++) acc[h] = __fadd_rn(acc[h], __fmul_rn(ps[h][i], v));
         }
     }
+    const size_t base = (size_t(t) * NHEAD + kh * 8) * nchunk + chunk;
 #pragma unroll
-    for (int h = 0; h < 8; h++)
-        opart[((size_t(t) * NHEAD + kh * 8 + h) * nchunk + chunk) * HEAD_DIM + d] = acc[h];
-    if (warp == 0 && lane < 8) lpart[(size_t(t) * NHEAD + kh * 8 + lane) * nchunk + chunk] = lsum;
+    for (int h = 0; h < 8; h++) opart[(base + size_t(h) * nchunk) * HEAD_DIM + d] = acc[h];
+    if (lane == 0) {
+        mpart[base + size_t(warp) * nchunk] = m_run;
+        lpart[base + size_t(warp) * nchunk] = l_run;
+    }
 }
 
 // -------------------------------------- combine + sigmoid gate + Q8_K ----
-// o = (sum of chunk partials) * (1 / sum of p) (nn.c:1410-1412), aout = o *
-// sigmoid(gate) (nn.c:2157-2159), quantized for attn_output; also keeps the
-// per-head max and sum of p for the salience update.
+// Per query t: for head h, M = max of the CTA maxima, f_c = expf(m_c - M),
+// L = sum f_c l_c, o = (sum_c f_c o_c) * (1 / L) (the softmax of attn_worker,
+// nn.c:1340-1412), aout = o * sigmoid(gate) (nn.c:2157-2159), quantized to
+// Q8_K for attn_output; (M, L) per head are kept for the salience update.
 __global__ void __launch_bounds__(1024) attn_combine_kernel(const float *__restrict__ opart,
+                                                            const float *__restrict__ mpart,
                                                             const float *__restrict__ lpart,
-                                                            const float *__restrict__ cmax,
-                                                            int nchunk_sc, int nchunk,
-                                                            const float *__restrict__ z,
+                                                            const StepParams *spp, int span,
+                                                            int nchunk, const float *__restrict__ z,
                                                             float *ml, int8_t *xq, float *xd,
                                                             int16_t *xs) {
+    extern __shared__ float fsh[];              // [16][nchunk] chunk factors
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float inv[NHEAD];
     __shared__ __align__(16) float y[WO_DIM];
+    pdl_trigger();
     pdl_wait();
+    const StepParams sp = *spp;
+    const int nc = (nk_of(sp, t) + span - 1) / span;
     if (warp < NHEAD) {
-        const float *cm = cmax + (size_t(t) * NHEAD + warp) * nchunk_sc;
-        const float *lp = lpart + (size_t(t) * NHEAD + warp) * nchunk;
-        float m = -INFINITY, l = 0.0f;
-        for (int c = lane; c < nchunk_sc; c += 32) m = fmaxf(m, cm[c]);
-        for (int c = lane; c < nchunk; c += 32) l += lp[c];
+        const size_t base = (size_t(t) * NHEAD + warp) * nchunk;
+        float m = -INFINITY;
+        for (int c = lane; c < nc; c += 32) m = fmaxf(m, mpart[base + c]);
         m = warp_max(m);
+        float l = 0.0f;
+        for (int c = lane; c < nc; c += 32) {
+            const float f = expf(mpart[base + c] - m);
+            fsh[warp * nchunk + c] = f;
+            l = __fadd_rn(l, __fmul_rn(f, lpart[base + c]));
+        }
         l = warp_sum(l);
         if (lane == 0) {
             inv[warp] = 1.0f / l;
@@ -392,8 +455,9 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float *__restr
     for (int i = tid; i < WO_DIM; i += 1024) {
         const int h = i / HEAD_DIM, d = i % HEAD_DIM;
         const float *op = opart + (size_t(t) * NHEAD + h) * nchunk * HEAD_DIM + d;
+        const float *f = fsh + h * nchunk;
         float o = 0.0f;
-        for (int c = 0; c < nchunk; c++) o += op[size_t(c) * HEAD_DIM];
+        for (int c = 0; c < nc; c++) o = __fadd_rn(o, __fmul_rn(f[c], op[size_t(c) * HEAD_DIM]));
         o = __fmul_rn(o, inv[h]);
         const float g = z[size_t(t) * WO_DIM + i];
         y[i] = __fmul_rn(o, 1.0f / (1.0f + expf(-g)));
@@ -420,6 +484,7 @@ __global__ void __launch_bounds__(256) attn_salience_kernel(const float *__restr
                                                             const StepParams *spp, float *sal,
                                                             float *pin_sal) {
     const int jj = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
     if (sp.n_live <= 0) return;
@@ -469,26 +534,37 @@ __global__ void arena_copy_kernel(const int2 *pairs, int n, uint8_t *const *kv, 
 int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const float *kn,
                           const float *rope, const StepParams *sp, int T, float *qr, float *z,
                           uint8_t *kv, float *qf, float *sal, cudaStream_t st) {
-    qk_prep_append_kernel<<<T, 256, 0, st>>>(proj, proj_ld, qn, kn, rope, sp, qr, z, kv, qf, sal);
+    QMA_CHECK_CUDA(launch_ex(qk_prep_append_kernel, dim3(T, 5), dim3(128), 0, st, 1, pdl_enabled(), proj, proj_ld, qn, kn,
+                             rope, sp, qr, z, kv, qf, sal));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
-    const int nchunk_sc = (a.nk_max + SC_POS - 1) / SC_POS;
-    attn_scores_kernel<<<dim3(nchunk_sc, NHEAD_KV, a.T), 256, 0, st>>>(
-        a.qr, a.kv, a.arena, a.live, a.sp, a.scores, a.nk_max, a.cmax, nchunk_sc);
-    QMA_CHECK_LAUNCH();
     const int nchunk = (a.nk_max + a.pv_chunk - 1) / a.pv_chunk;
-    attn_pv_kernel<<<dim3(nchunk, NHEAD_KV, a.T), 256, 0, st>>>(
-        a.scores, a.nk_max, a.cmax, nchunk_sc, a.kv, a.arena, a.live, a.sp, a.pv_chunk, a.opart,
-        a.lpart, nchunk);
+    QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), 0, st, 1, pdl_enabled(), a.qr,
+                             a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk, a.scores, a.cmax,
+                             a.lpart, a.opart));
     QMA_CHECK_LAUNCH();
-    attn_combine_kernel<<<a.T, 1024, 0, st>>>(a.opart, a.lpart, a.cmax, nchunk_sc, nchunk, a.z,
-                                              a.ml, a.xq, a.xd, a.xs);
+    const size_t fsh = sizeof(float) * NHEAD * size_t(nchunk);
+    if (fsh > 48 * 1024) {
+        static bool raised = false;
+        if (!raised) {
+            QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_combine_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                160 * 1024));
+            raised = true;
+        }
+        if (fsh > 160 * 1024) {
+            set_error("attention: %d position chunks exceed the combine kernel's shared memory", nchunk);
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
+    }
+    QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(a.T), dim3(1024), fsh, st, 1, pdl_enabled(), a.opart, a.cmax,
+                             a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs));
     QMA_CHECK_LAUNCH();
-    attn_salience_kernel<<<(a.nk_max + 255) / 256, 256, 0, st>>>(a.scores, a.nk_max, a.ml, a.live,
-                                                                 a.sp, a.sal, a.pin_sal);
+    QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, pdl_enabled(),
+                             a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }

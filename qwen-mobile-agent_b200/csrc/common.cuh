@@ -150,6 +150,100 @@ __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Asynchronous L2 prefetch of a byte range (16-byte aligned address, size a
+// multiple of 16): weights are requested before the data they combine with
+// is ready.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// Any byte range: shrunk to the 16-byte-aligned range inside it, so it never
+// reaches outside [p, p + bytes) (the allocation holding it starts 256-byte
+// aligned, so rounding the start down stays inside it as well).
+__device__ __forceinline__ void prefetch_l2_range(const void *p, size_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+    for (uintptr_t q = a; q < e; q += (uintptr_t(1) << 30)) {
+        const uintptr_t n = e - q < (uintptr_t(1) << 30) ? e - q : (uintptr_t(1) << 30);
+        prefetch_l2(reinterpret_cast<const void *>(q), uint32_t(n));
+    }
+}
+
+// Thread-block cluster helpers (split arrive / wait of the cluster barrier,
+// and a load from another CTA's shared memory).
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    cluster_arrive();
+    cluster_wait();
+}
+// address of `p` (this CTA's shared memory) in the shared memory of CTA `rank`
+template <class T> __device__ __forceinline__ T *cluster_map(T *p, unsigned rank) {
+    uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p)), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return reinterpret_cast<T *>(static_cast<uintptr_t>(r));
+}
+__device__ __forceinline__ float ld_cluster_f32(const float *remote) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                 : "=f"(v)
+                 : "r"(static_cast<uint32_t>(reinterpret_cast<uintptr_t>(remote)))
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_cluster_f64(double *remote, double v) {
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(static_cast<uint32_t>(reinterpret_cast<uintptr_t>(remote))),
+                 "d"(v)
+                 : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(float *remote, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(static_cast<uint32_t>(reinterpret_cast<uintptr_t>(remote))),
+                 "f"(v)
+                 : "memory");
+}
+
+// Kernel launch with optional thread-block cluster and programmatic
+// dependent launch (the kernel may start while the previous kernel on the
+// stream finishes; it must call pdl_wait() before touching that kernel's
+// outputs or writing anything it reads).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, int cluster, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    unsigned n = 0;
+    if (cluster > 1) {
+        at[n].id = cudaLaunchAttributeClusterDimension;
+        at[n].val.clusterDim.x = unsigned(cluster);
+        at[n].val.clusterDim.y = 1;
+        at[n].val.clusterDim.z = 1;
+        n++;
+    }
+    if (pdl) {
+        at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+// Programmatic dependent launch of the engine's kernels (on by default).
+bool pdl_enabled();
+
 // 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,
 // quants.c:18-26 / q8k.c:22-30).
 __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *s, int &d, int &m) {

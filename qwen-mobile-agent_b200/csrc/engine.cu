@@ -49,6 +49,8 @@ struct qma_cuda_model {
     size_t weight_bytes = 0;
 };
 
+constexpr int ARG_CTAS = 64;      // CTAs of the greedy argmax
+
 struct qma_cuda_state {
     qma_cuda_model *m = nullptr;
     int n_ctx = 0, n_pos = 0;
@@ -78,6 +80,9 @@ struct qma_cuda_state {
     float *logits = nullptr;    // [MAX_CHUNK][n_vocab] (logits_all) or [1][n_vocab]
     int logits_rows = 0;
     int *argmax_dev = nullptr;
+    float *argmax_pv = nullptr;         // per-CTA partial maxima
+    int *argmax_pi = nullptr;
+    unsigned *argmax_cnt = nullptr;     // ticket, zero between steps
     // attention scratch, grown on demand
     float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr, *ml = nullptr;
     size_t scores_cap = 0, cmax_cap = 0, opart_cap = 0, lpart_cap = 0;
@@ -399,6 +404,9 @@ static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     TRY(salloc(s, &s->moe_scratch, s->moe_scratch_bytes, st));
     TRY(salloc_t(s, &s->ml, size_t(TM) * NHEAD * 2, st));
     TRY(salloc_t(s, &s->argmax_dev, 4, st));
+    TRY(salloc_t(s, &s->argmax_pv, ARG_CTAS, st));
+    TRY(salloc_t(s, &s->argmax_pi, ARG_CTAS, st));
+    TRY(salloc_t(s, &s->argmax_cnt, 1, st));
     s->logits_rows = 1;
     TRY(salloc_t(s, &s->logits, size_t(m->n_vocab), st));
 #undef TRY
@@ -583,36 +591,61 @@ static int ensure_attn_scratch(qma_cuda_state *s, int T, int nk, int pv_chunk) {
     return QMA_CUDA_OK;
 }
 
-__global__ void argmax_kernel(const float *__restrict__ logits, int n, StepParams *sp, int *out) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
+// Greedy token of the last logits row: ARG_CTAS CTAs each reduce a slice to
+// (max, first index); the last CTA to finish (atomic ticket, reset for the
+// next step) reduces the slices.  Ties keep the lowest index.
+
+__device__ __forceinline__ void argmax_merge(float &v, int &idx, float ov, int oi) {
+    if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+}
+
+__global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ logits, int n,
+                                                     StepParams *sp, int *out, float *pv, int *pi,
+                                                     unsigned *cnt) {
+    __shared__ float bv[16];
+    __shared__ int bi[16];
+    __shared__ int last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
+    pdl_wait();
+    const int per = (n + gridDim.x - 1) / gridDim.x;
+    const int i0 = blockIdx.x * per, i1 = min(n, i0 + per);
     float v = -INFINITY;
     int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = i0 + tid; i < i1; i += blockDim.x) {
         const float x = logits[i];
         if (x > v) { v = x; idx = i; }     // ascending i: keeps the first maximum
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
-    }
-    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = v; bi[threadIdx.x >> 5] = idx; }
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) { bv[warp] = v; bi[warp] = idx; }
     __syncthreads();
-    if (threadIdx.x < 32) {
-        v = threadIdx.x < blockDim.x / 32 ? bv[threadIdx.x] : -INFINITY;
-        idx = threadIdx.x < blockDim.x / 32 ? bi[threadIdx.x] : 0x7fffffff;
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    if (warp == 0) {
+        v = lane < 16 ? bv[lane] : -INFINITY;
+        idx = lane < 16 ? bi[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1)
+            argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+        if (lane == 0) {
+            pv[blockIdx.x] = v;
+            pi[blockIdx.x] = idx;
+            __threadfence();
+            last = atomicAdd(cnt, 1u) == gridDim.x - 1;
         }
-        if (threadIdx.x == 0) {
-            *out = idx;
-            if (sp) {            // next decode step: this token at the next position
-                sp->token = idx;
-                sp->n_pos += 1;
-            }
+    }
+    __syncthreads();
+    if (!last || warp != 0) return;
+    __threadfence();
+    v = -INFINITY;
+    idx = 0x7fffffff;
+    for (int c = lane; c < int(gridDim.x); c += 32) argmax_merge(v, idx, __ldcg(pv + c), __ldcg(pi + c));
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) {
+        *out = idx;
+        *cnt = 0;
+        if (sp) {            // next decode step: this token at the next position
+            sp->token = idx;
+            sp->n_pos += 1;
         }
     }
 }
@@ -661,7 +694,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             break;
         }
         // x = x2 + moe(rms_norm(x2) * post_norm)
-        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st));
+        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false));
     }
     if (logits_mode) {
         const int rows = logits_mode == 2 ? T : 1;
@@ -763,8 +796,10 @@ static int capture_decode(qma_cuda_state *s) {
     fill_params(s, hs, s->n_pos, 1, 0);
     rc = forward(s, hs, nullptr, nk, 1);
     if (!rc) {
-        argmax_kernel<<<1, 1024, 0, st>>>(s->logits, s->m->n_vocab, s->sp_dev, s->argmax_dev);
-        if (cudaGetLastError() != cudaSuccess) rc = QMA_CUDA_ERR_CUDA;
+        if (launch_ex(argmax_kernel, dim3(ARG_CTAS), dim3(512), 0, st, 1, pdl_enabled(), s->logits,
+                      s->m->n_vocab, s->sp_dev, s->argmax_dev, s->argmax_pv, s->argmax_pi,
+                      s->argmax_cnt) != cudaSuccess)
+            rc = QMA_CUDA_ERR_CUDA;
     }
     const cudaError_t e = cudaStreamEndCapture(st, &g);
     if (rc) return rc;

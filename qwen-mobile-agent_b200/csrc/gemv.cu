@@ -32,6 +32,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, 
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        // this CTA's rows (8 consecutive warp row groups per sweep): into L2
+        // while the upstream kernel finishes
+        constexpr int RG = (32 / LPR) * RU;
+        for (int r0 = blockIdx.x * 8 * RG; r0 < n_out; r0 += nwarps * RG)
+            F::prefetch_rows(W, r0, min(8 * RG, n_out - r0), n_in);
+    }
+    pdl_wait();
     gemv_warp_rows<F, T, LPR, UPL, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, warp, nwarps,
                                        lane, resid);
 }
@@ -64,9 +73,8 @@ static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8
     long blocks = (warps_needed + 7) / 8;
     const long wave = long(num_sms()) * per_sm;
     if (blocks > wave) blocks = wave;
-    gemv_kernel<F, T, LPR, UPL, RU><<<int(blocks), 256, 0, st>>>(W, n_in, n_out, xq, xd, xsum,
-                                                                 out, out_ld, resid);
-    QMA_CHECK_LAUNCH();
+    QMA_CHECK_CUDA(launch_ex(gemv_kernel<F, T, LPR, UPL, RU>, dim3(unsigned(blocks)), dim3(256), 0, st, 1,
+                             pdl_enabled(), W, n_in, n_out, xq, xd, xsum, out, out_ld, resid));
     return QMA_CUDA_OK;
 }
 

@@ -43,6 +43,9 @@ struct FmtQ4K {
         a.xs01 = int(s[0]) + int(s[1]);
         a.xs23 = int(s[2]) + int(s[3]);
     }
+    __device__ static void prefetch_rows(Ptr W, int r0, int nrows, int n_in) {
+        prefetch_l2_range(W + size_t(r0) * (n_in / 256) * 144, size_t(nrows) * (n_in / 256) * 144);
+    }
     __device__ static void load_w(Wt &w, Ptr W, int row, int n_in, int u) {
         const uint8_t *b = W + size_t(row) * (n_in / 256) * 144 + (u >> 2) * 144;
         w.h = ld_stream16(b);
@@ -105,6 +108,12 @@ struct FmtQ6K {
         }
         a.xd = xd[u >> 1];
     }
+    __device__ static void prefetch_rows(const Ptr &P, int r0, int nrows, int n_in) {
+        prefetch_l2_range(P.ql + size_t(r0) * (n_in / 2), size_t(nrows) * (n_in / 2));
+        prefetch_l2_range(P.qh + size_t(r0) * (n_in / 4), size_t(nrows) * (n_in / 4));
+        prefetch_l2_range(P.sc + size_t(r0) * (n_in / 16), size_t(nrows) * (n_in / 16));
+        prefetch_l2_range(P.d + size_t(r0) * (n_in / 256), size_t(nrows) * (n_in / 256) * 2);
+    }
     __device__ static void load_w(Wt &w, const Ptr &P, int row, int n_in, int u) {
         const int sb = u >> 1, j = u & 1;
         const uint8_t *ql = P.ql + size_t(row) * (n_in / 2) + sb * 128 + j * 64;
@@ -166,6 +175,10 @@ struct FmtQ80 {
             a.x[4 * k] = v.x; a.x[4 * k + 1] = v.y; a.x[4 * k + 2] = v.z; a.x[4 * k + 3] = v.w;
         }
         a.xd = xd[u >> 2];
+    }
+    __device__ static void prefetch_rows(const Ptr &P, int r0, int nrows, int n_in) {
+        prefetch_l2_range(P.q + size_t(r0) * n_in, size_t(nrows) * n_in);
+        prefetch_l2_range(P.d + size_t(r0) * (n_in / 32), size_t(nrows) * (n_in / 32) * 2);
     }
     __device__ static void load_w(Wt &w, const Ptr &P, int row, int n_in, int u) {
         const int8_t *q = P.q + size_t(row) * n_in + u * 64;

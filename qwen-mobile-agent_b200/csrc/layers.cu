@@ -17,6 +17,7 @@ __global__ void __launch_bounds__(256) embed_q8_kernel(const int8_t *q, const __
                                                        const int *tokens, const StepParams *sp,
                                                        float *x) {
     const int t = blockIdx.x;
+    pdl_trigger();
     pdl_wait();
     const int tok = tokens ? tokens[t] : sp->token;
     const int i0 = threadIdx.x * 8;
@@ -32,6 +33,7 @@ __global__ void __launch_bounds__(256) embed_q8_kernel(const int8_t *q, const __
 __global__ void __launch_bounds__(256) embed_q4k_kernel(const uint8_t *W, const int *tokens,
                                                         const StepParams *sp, float *x) {
     const int t = blockIdx.x;
+    pdl_trigger();
     pdl_wait();
     const int tok = tokens ? tokens[t] : sp->token;
     const int i0 = threadIdx.x * 8;
@@ -54,6 +56,7 @@ __global__ void __launch_bounds__(256) embed_q4k_kernel(const uint8_t *W, const 
 __global__ void __launch_bounds__(256) embed_q6k_kernel(Q6Planes P, const int *tokens,
                                                         const StepParams *sp, float *x) {
     const int t = blockIdx.x;
+    pdl_trigger();
     pdl_wait();
     const int tok = tokens ? tokens[t] : sp->token;
     const int i0 = threadIdx.x * 8;
@@ -78,11 +81,11 @@ int launch_embed(const void *embd, int type, int n_vocab, const int *tokens,
                  const StepParams *sp, int T, float *x, cudaStream_t st) {
     if (type == QMA_TYPE_Q8_0) {
         const Q8Planes P = q8_planes(embd, n_vocab, EMBD);
-        embed_q8_kernel<<<T, 256, 0, st>>>(P.q, P.d, tokens, sp, x);
+        QMA_CHECK_CUDA(launch_ex(embed_q8_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), P.q, P.d, tokens, sp, x));
     } else if (type == QMA_TYPE_Q6_K) {
-        embed_q6k_kernel<<<T, 256, 0, st>>>(q6_planes(embd, n_vocab, EMBD), tokens, sp, x);
+        QMA_CHECK_CUDA(launch_ex(embed_q6k_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), q6_planes(embd, n_vocab, EMBD), tokens, sp, x));
     } else if (type == QMA_TYPE_Q4_K) {
-        embed_q4k_kernel<<<T, 256, 0, st>>>(static_cast<const uint8_t *>(embd), tokens, sp, x);
+        QMA_CHECK_CUDA(launch_ex(embed_q4k_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), static_cast<const uint8_t *>(embd), tokens, sp, x));
     } else {
         set_error("embed: unsupported token_embd type %d", type);
         return QMA_CUDA_ERR_UNSUPPORTED;
@@ -100,6 +103,7 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
                                                             int8_t *xq, float *xd, int16_t *xs) {
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ double red[8];
+    pdl_trigger();
     pdl_wait();
     const float4 *p = reinterpret_cast<const float4 *>(x + size_t(t) * EMBD + tid * 8);
     const float4 a = p[0], b = p[1];
@@ -128,7 +132,7 @@ int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *x
         set_error("rmsnorm_quant: n %d != %d", n, EMBD);
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
-    rmsnorm_quant_kernel<<<T, 256, 0, st>>>(x, w, xq, xd, xs);
+    QMA_CHECK_CUDA(launch_ex(rmsnorm_quant_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), x, w, xq, xd, xs));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -141,6 +145,7 @@ __global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ q
                                                      const float *__restrict__ w, float *state,
                                                      int T, float *out) {
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
     pdl_wait();
     if (ch >= CONV_DIM) return;
     const float4 wc = *reinterpret_cast<const float4 *>(w + size_t(ch) * 4);
@@ -163,7 +168,7 @@ __global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ q
 
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
                   cudaStream_t st) {
-    conv1d_kernel<<<CONV_DIM / 256, 256, 0, st>>>(qkv, ld, w, state, T, out);
+    QMA_CHECK_CUDA(launch_ex(conv1d_kernel, dim3(CONV_DIM / 256), dim3(256), 0, st, 1, pdl_enabled(), qkv, ld, w, state, T, out));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -191,6 +196,7 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     __shared__ double red[2][8];
     __shared__ float kqred[2][4];
     float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
+    pdl_trigger();
     pdl_wait();
     float M[16];
 #pragma unroll
@@ -258,8 +264,8 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
 
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
                const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st) {
-    gdn_kernel<<<dim3(4, VHEADS), 256, 0, st>>>(conv_out, proj, proj_ld, beta_off, alpha_off, dt, a,
-                                               ssm, T, o);
+    QMA_CHECK_CUDA(launch_ex(gdn_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj, proj_ld,
+                             beta_off, alpha_off, dt, a, ssm, T, o));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -274,6 +280,7 @@ __global__ void __launch_bounds__(1024) gated_norm_quant_kernel(const float *__r
                                                                 int8_t *xq, float *xd, int16_t *xs) {
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     __shared__ __align__(16) float y[VAL_DIM];
+    pdl_trigger();
     pdl_wait();
     const float4 v4 = *reinterpret_cast<const float4 *>(o + size_t(t) * VAL_DIM + h * SSTATE + lane * 4);
     float v[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(1024) gated_norm_quant_kernel(const float *__r
 
 int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
                             int8_t *xq, float *xd, int16_t *xs, cudaStream_t st) {
-    gated_norm_quant_kernel<<<T, 1024, 0, st>>>(o, z, z_ld, w, xq, xd, xs);
+    QMA_CHECK_CUDA(launch_ex(gated_norm_quant_kernel, dim3(T), dim3(1024), 0, st, 1, pdl_enabled(), o, z, z_ld, w, xq, xd, xs));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }

@@ -4,22 +4,21 @@
 // Reference: moe_ffn (nn.c:509-649), moe_expert_one_q8k (nn.c:412-439),
 // moe_shared_q8k (nn.c:446-473), the residual in qma_eval (nn.c:2246-2252).
 //
-// Three kernels per call (T tokens, grid.y = token):
-//   1. router   : 64 CTAs x 4 warps, one warp per expert.  Every CTA forms
-//                 xn = rms_norm(x2) * post_norm in shared memory, each warp
-//                 computes one router logit exactly in fp64 together with a
-//                 proven bound on the reference's sequential fp32 sum; the
-//                 last CTA to finish selects the top 8 (falling back to the
-//                 reference's own summation order for any rank the bound
-//                 cannot settle), renormalises the weights, quantizes xn to
-//                 Q8_K and computes the shared-expert gate.
-//   2. gate/up  : 9 slots (8 routed + shared) x 16 chunks of 32 rows; one
-//                 warp streams a gate row and an up row (Q4_K), SwiGLU.
-//   3. down     : 9 slots x 16 chunks of 128 output rows; each CTA
-//                 quantizes its slot's hidden vector to Q8_K in shared memory
-//                 and runs the Q6_K (or Q4_K) GEMV; the last of the 9 CTAs of
-//                 a chunk combines the slots in the reference's order and
-//                 adds the residual.
+// Two kernels per call (T tokens, grid.y = token), both thread-block
+// clusters of 16 CTAs exchanging data through distributed shared memory:
+//   1. router : per token, 16 CTAs x 16 experts.  Every CTA forms
+//               xn = rms_norm(x2) * post_norm, each warp computes two router
+//               logits exactly in fp64 with a proven bound on the
+//               reference's sequential fp32 sum and stores them in the
+//               leader CTA; the leader selects the top 8 (falling back to
+//               the reference's own summation order for any rank the bound
+//               cannot settle) and renormalises the weights.  CTAs 0..7 also
+//               quantize xn to Q8_K and form the shared-expert gate.
+//   2. experts: per (slot, token), 9 slots (8 routed + shared) x 16 CTAs:
+//               gate/up + SwiGLU rows, the hidden vector gathered across the
+//               cluster, Q8_K, down rows; the last of the 9 slot CTAs of a
+//               128-row chunk combines the slots in the reference's order
+//               and adds the residual.
 #include <math.h>
 
 #include "common.cuh"
@@ -166,135 +165,225 @@ __device__ bool select_top8(const double *sS, const double *sB, const int *cls, 
     return ok;
 }
 
-__global__ void __launch_bounds__(128) moe_router_kernel(const float *__restrict__ x2,
+// Exact logit S (fp64 sum of the fp32 products) and a bound B on the
+// reference's sequential fp32 sum, for the router row a warp holds (lane:
+// weights 64 l .. 64 l + 63).  The reference sums s += g_i * x_i in fp32
+// (nn.c:519-521).  With a_i = fl(g_i * x_i) (the same products) and S_i the
+// exact prefix sums, recursive summation satisfies |s_fp32 - S_n| <= u'
+// sum_i |S_i| with u' = 2^-24 (1 + n u) for n = 2048.  S_n is summed in fp64
+// (error ~1e-13 relative); sum_i |S_i| in fp32 prefix sums, whose own error
+// (< 1e-3 relative) the 1.01 factor covers.
+__device__ __forceinline__ void router_logit(const float4 (&wv)[16], const float *xn, int lane,
+                                             double &S, double &B) {
+    const float4 *xr = reinterpret_cast<const float4 *>(xn + lane * 68);
+    float a[64];
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+        const float4 xw = xr[k];
+        a[4 * k + 0] = __fmul_rn(wv[k].x, xw.x);
+        a[4 * k + 1] = __fmul_rn(wv[k].y, xw.y);
+        a[4 * k + 2] = __fmul_rn(wv[k].z, xw.z);
+        a[4 * k + 3] = __fmul_rn(wv[k].w, xw.w);
+    }
+    double t4[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+    for (int j = 0; j < 64; j++) t4[j & 3] += double(a[j]);
+    const double tl = (t4[0] + t4[1]) + (t4[2] + t4[3]);
+    double incl = tl;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    float p = float(incl - tl), el = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 64; j++) {
+        p += a[j];
+        el += fabsf(p);
+    }
+    const float E = warp_sum(el);
+    S = __shfl_sync(0xffffffffu, incl, 31);
+    B = double(E) * 0x1.0p-24 * 1.01 + 1e-30;
+}
+
+// Leader-side ranking of the 256 logits (256 threads, thread = expert):
+// top9[r] = the expert of rank r < 9 under (S descending, id ascending),
+// ranked on S rounded to fp32 (fast compares).  Two logits that fp32
+// rounding could tie or misorder are within one fp32 ulp of each other, far
+// inside the margin top_settled() demands between ranks, so such a ranking
+// is never accepted.  dred[0] receives the largest S + B among the
+// unselected (rank >= 8).
+__device__ __forceinline__ void rank_top(const double *sS, const double *sB, float *sf, int tid,
+                                         int lane, int warp, double *dred, int *top9) {
+    const double Se = sS[tid];
+    const float fe = float(Se);
+    sf[tid] = fe;
+    __syncthreads();
+    int r = 0;
+    const float4 *f4 = reinterpret_cast<const float4 *>(sf);
+#pragma unroll 4
+    for (int j4 = 0; j4 < MOE_NEXP / 4; j4++) {
+        const float4 v = f4[j4];
+        const int j = 4 * j4;
+        r += (v.x > fe) || (v.x == fe && j + 0 < tid);
+        r += (v.y > fe) || (v.y == fe && j + 1 < tid);
+        r += (v.z > fe) || (v.z == fe && j + 2 < tid);
+        r += (v.w > fe) || (v.w == fe && j + 3 < tid);
+    }
+    if (r <= MOE_TOPK) top9[r] = tid;
+    double u = r >= MOE_TOPK ? Se + sB[tid] : -INFINITY;
+    u = warp_max_d(u);
+    if (lane == 0) dred[warp] = u;      // dred's rms sums were consumed before the cluster barrier
+    __syncthreads();
+    if (tid == 0) {
+        double m = dred[0];
+        for (int w = 1; w < 8; w++) m = fmax(m, dred[w]);
+        dred[0] = m;
+    }
+    __syncthreads();
+}
+
+// Whether the ranking settles the reference's selection: the 8th expert's
+// probability is a normal float (then no lower class can compete) and the
+// intervals S +- B of consecutive selected experts, and of the 8th against
+// every unselected one, are separated with a margin that keeps the
+// probabilities' order strict after expf and division rounding.
+__device__ __forceinline__ bool top_settled(const double *sS, const double *sB, const int *top9,
+                                            const double *dred) {
+    if (p_class(sS[top9[MOE_TOPK - 1]], sS[top9[0]]) != 2) return false;
+    for (int k = 0; k < MOE_TOPK; k++) {
+        const int a = top9[k];
+        const double hi = k + 1 < MOE_TOPK ? sS[top9[k + 1]] + sB[top9[k + 1]] : dred[0];
+        if (!(sS[a] - sB[a] - hi > 1e-6 * (1.0 + fabs(sS[a])))) return false;
+    }
+    return true;
+}
+
+// Router: one cluster of RCL CTAs per token (grid (RCL, T)), 8 warps per
+// CTA, 2 experts per warp.  Every CTA forms xn = rms_norm(x2) * post_norm
+// (rms_norm_m, nn.c:348-357) in shared memory; each warp computes its two
+// exact logits and bounds and stores them into the leader CTA's shared
+// memory; CTAs 0..7 also quantize 256-block `rank` of xn to Q8_K (shared by
+// every expert) and send the leader their part of the shared-expert gate
+// input sum_i g_i * xq_i * xd (nn.c:453).  After the cluster barrier the
+// leader selects the top 8 (falling back to the reference's own summation
+// order for any rank the bounds cannot settle) and writes the renormalised
+// weights (nn.c:524-547) and the shared-expert gate sigmoid.
+constexpr int RCL = 16;                       // CTAs per router cluster
+constexpr int XCL = 16;                       // CTAs per expert cluster
+constexpr int XGU = MOE_FF / XCL;             // gate/up rows per expert CTA
+constexpr int XDN = MOE_EMBD / XCL;           // down rows per expert CTA
+static_assert(XDN == MOE_DOWN_CHUNK && XCL == MOE_DOWN_CHUNKS, "combine chunks = expert CTAs");
+
+__global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ x2,
                                                          const float *__restrict__ post_norm,
                                                          const float *__restrict__ Wr,
                                                          const float *__restrict__ gis,
                                                          MoeScratch s, int *sel_out,
                                                          float *w_out) {
+    const unsigned rank = cluster_rank();
     const int t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int e_mine = blockIdx.x * 4 + warp;
     __shared__ __align__(16) float xn[MOE_EMBD / 64 * 68];
-    __shared__ double dred[4];
-    __shared__ float fred[4];
-    __shared__ int is_last, need_exact, ncand;
+    __shared__ double dred[8];
     __shared__ double sS[MOE_NEXP], sB[MOE_NEXP];
+    __shared__ float gpart[MOE_EMBD / 256];
+    __shared__ int need_exact, ncand;
     __shared__ int cls[MOE_NEXP];
-    __shared__ int top[MOE_TOPK];
-    __shared__ float topL[MOE_TOPK];
+    __shared__ int top9[MOE_TOPK + 1];
     __shared__ int cand[MOE_NEXP];
+    __shared__ __align__(16) float sf[MOE_NEXP];
 
-    // router row of this warp's expert: independent of the upstream kernel,
-    // so it is requested before waiting on it
-    float4 wv[16];
+    // the two router rows of this warp: independent of the upstream kernel
+    const int e0 = int(rank) * (MOE_NEXP / RCL) + warp * 2;
+    float4 w0[16], w1[16];
     {
-        const float4 *wr = reinterpret_cast<const float4 *>(Wr + size_t(e_mine) * MOE_EMBD + lane * 64);
+        const float4 *r0 = reinterpret_cast<const float4 *>(Wr + size_t(e0) * MOE_EMBD + lane * 64);
+        const float4 *r1 = r0 + MOE_EMBD / 4;
 #pragma unroll
-        for (int k = 0; k < 16; k++) wv[k] = __ldg(wr + k);
+        for (int k = 0; k < 16; k++) {
+            w0[k] = __ldg(r0 + k);
+            w1[k] = __ldg(r1 + k);
+        }
     }
+    pdl_trigger();
     pdl_wait();
-    // ---- xn = rms_norm(x2) * post_norm (rms_norm_m, nn.c:348-357) -------
+    // ---- xn = rms_norm(x2) * post_norm ------------------------------------
     const float *x = x2 + size_t(t) * MOE_EMBD;
-    float xv[16];
+    float xv[8];
     double ss = 0.0;
 #pragma unroll
-    for (int k = 0; k < 16; k++) {
-        xv[k] = x[tid + 128 * k];
+    for (int k = 0; k < 8; k++) {
+        xv[k] = x[tid + 256 * k];
         ss += double(xv[k]) * double(xv[k]);
     }
     ss = warp_sum_d(ss);
     if (lane == 0) dred[warp] = ss;
     __syncthreads();
-    const double tot = (dred[0] + dred[1]) + (dred[2] + dred[3]);
+    const double tot = ((dred[0] + dred[1]) + (dred[2] + dred[3])) + ((dred[4] + dred[5]) + (dred[6] + dred[7]));
     const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
 #pragma unroll
-    for (int k = 0; k < 16; k++) {
-        const int i = tid + 128 * k;
+    for (int k = 0; k < 8; k++) {
+        const int i = tid + 256 * k;
         xn[xn_idx(i)] = __fmul_rn(__fmul_rn(xv[k], r), post_norm[i]);
     }
     __syncthreads();
-
-    // ---- one router logit per warp: exact value + bound -----------------
-    // The reference sums s += g_i * x_i sequentially in fp32 (nn.c:519-521).
-    // With a_i = fl(g_i * x_i) (the same products) and S_i the exact prefix
-    // sums, recursive summation satisfies |s_fp32 - S_n| <= u' sum_i |S_i|
-    // with u' = 2^-24 (1 + n u) for n = 2048.  S_n is summed in fp64
-    // (error ~1e-13 relative); sum_i |S_i| in fp32 prefix sums, whose own
-    // error (< 1e-3 relative) the 1.01 factor covers.
+    // ---- two exact logits per warp, sent to the leader ---------------------
     {
-        const float4 *xr = reinterpret_cast<const float4 *>(xn + lane * 68);
-        float a[64];
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            const float4 xw = xr[k];
-            a[4 * k + 0] = __fmul_rn(wv[k].x, xw.x);
-            a[4 * k + 1] = __fmul_rn(wv[k].y, xw.y);
-            a[4 * k + 2] = __fmul_rn(wv[k].z, xw.z);
-            a[4 * k + 3] = __fmul_rn(wv[k].w, xw.w);
-        }
-        double t4[4] = {0.0, 0.0, 0.0, 0.0};
-#pragma unroll
-        for (int j = 0; j < 64; j++) t4[j & 3] += double(a[j]);
-        const double tl = (t4[0] + t4[1]) + (t4[2] + t4[3]);
-        double incl = tl;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        float p = float(incl - tl), el = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 64; j++) {
-            p += a[j];
-            el += fabsf(p);
-        }
-        const float E = warp_sum(el);
-        const double S = __shfl_sync(0xffffffffu, incl, 31);
+        double S0, B0, S1, B1;
+        router_logit(w0, xn, lane, S0, B0);
+        router_logit(w1, xn, lane, S1, B1);
         if (lane == 0) {
-            s.S[size_t(t) * MOE_NEXP + e_mine] = S;
-            s.B[size_t(t) * MOE_NEXP + e_mine] = double(E) * 0x1.0p-24 * 1.01 + 1e-30;
+            st_cluster_f64(cluster_map(&sS[e0], 0), S0);
+            st_cluster_f64(cluster_map(&sB[e0], 0), B0);
+            st_cluster_f64(cluster_map(&sS[e0 + 1], 0), S1);
+            st_cluster_f64(cluster_map(&sB[e0 + 1], 0), B1);
         }
     }
+    // ---- Q8_K block `rank` of xn and its part of the shared-expert gate ----
+    if (rank < MOE_EMBD / 256 && warp == 0) {
+        const int blk = int(rank), i0 = blk * 256 + lane * 8;
+        const float4 a0 = *reinterpret_cast<const float4 *>(xn + xn_idx(i0));
+        const float4 a1 = *reinterpret_cast<const float4 *>(xn + xn_idx(i0 + 4));
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        int q[8];
+        float sc;
+        q8k_block_warp_q(v, lane, s.xq + size_t(t) * MOE_EMBD + blk * 256,
+                         s.xd + size_t(t) * (MOE_EMBD / 256) + blk,
+                         s.xs + size_t(t) * (MOE_EMBD / 16) + blk * 16, q, sc);
+        float gp = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; c++) gp += __fmul_rn(__fmul_rn(gis[i0 + c], float(q[c])), sc);
+        gp = warp_sum(gp);
+        if (lane == 0) st_cluster_f32(cluster_map(&gpart[blk], 0), gp);
+    }
+    cluster_sync();
+    if (rank != 0) return;
 
-    // ---- the last CTA of this token selects ------------------------------
-    __syncthreads();
+    // ---- leader: top 8 ------------------------------------------------------
+    // Thread e ranks expert e by (S descending, id ascending), counting the
+    // experts above it.  That is the reference's order (probability, then
+    // lowest id) whenever the 8th expert's probability is a normal float
+    // (class 2: the classes below only ever hold lower logits) and every
+    // decision is settled by the bounds; otherwise the exact path below runs.
+    rank_top(sS, sB, sf, tid, lane, warp, dred, top9);
     if (tid == 0) {
-        __threadfence();
-        const unsigned ticket = atomicAdd(&s.rcount[t], 1u);
-        is_last = ticket == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    for (int i = tid; i < MOE_NEXP; i += 128) {
-        sS[i] = __ldcg(&s.S[size_t(t) * MOE_NEXP + i]);
-        sB[i] = __ldcg(&s.B[size_t(t) * MOE_NEXP + i]);
-    }
-    __syncthreads();
-    if (warp == 0) {
-        double mx = -INFINITY;
-        for (int j = 0; j < 8; j++) mx = fmax(mx, sS[lane + 32 * j]);
-        mx = warp_max_d(mx);
-        for (int j = 0; j < 8; j++) cls[lane + 32 * j] = p_class(sS[lane + 32 * j], mx);
-        __syncwarp();
-        const bool ok = select_top8(sS, sB, cls, lane, top);
-        if (lane == 0) {
-            need_exact = !ok;
-            ncand = 0;
-        }
+        need_exact = !top_settled(sS, sB, top9, dred);
+        ncand = 0;
     }
     __syncthreads();
     if (need_exact) {
         // Every expert whose rank the bounds leave open gets its logit
         // recomputed in the reference's exact order, s = fl(s + fl(g_i x_i)),
         // i = 0..2047; their intervals then collapse to the exact value.
-        const int e8 = top[MOE_TOPK - 1];
+        const double mx = sS[top9[0]];
+        cls[tid] = p_class(sS[tid], mx);
+        const int e8 = top9[MOE_TOPK - 1];
         const double thresh = sS[e8] - sB[e8];
-        for (int e = tid; e < MOE_NEXP; e += 128)
-            if (cls[e] > 0 && sS[e] + sB[e] >= thresh - 1e-6 * (1.0 + fabs(sS[e8]))) cand[atomicAdd(&ncand, 1)] = e;
         __syncthreads();
-        for (int c = tid; c < ncand; c += 128) {
+        if (cls[tid] > 0 && sS[tid] + sB[tid] >= thresh - 1e-6 * (1.0 + fabs(sS[e8]))) cand[atomicAdd(&ncand, 1)] = tid;
+        __syncthreads();
+        for (int c = tid; c < ncand; c += 256) {
             const int e = cand[c];
             const float *wr = Wr + size_t(e) * MOE_EMBD;
             float acc = 0.0f;
@@ -304,97 +393,39 @@ __global__ void __launch_bounds__(128) moe_router_kernel(const float *__restrict
         }
         __syncthreads();
         if (warp == 0) {
-            double mx = -INFINITY;
-            for (int j = 0; j < 8; j++) mx = fmax(mx, sS[lane + 32 * j]);
-            mx = warp_max_d(mx);
-            for (int j = 0; j < 8; j++) cls[lane + 32 * j] = p_class(sS[lane + 32 * j], mx);
+            double m2 = -INFINITY;
+            for (int j = 0; j < 8; j++) m2 = fmax(m2, sS[lane + 32 * j]);
+            m2 = warp_max_d(m2);
+            for (int j = 0; j < 8; j++) cls[lane + 32 * j] = p_class(sS[lane + 32 * j], m2);
             __syncwarp();
-            select_top8(sS, sB, cls, lane, top);   // now settled by exact values
+            select_top8(sS, sB, cls, lane, top9);   // settled by exact values
         }
+        __syncthreads();
     }
-    __syncthreads();
-    if (tid < MOE_TOPK) topL[tid] = float(sS[top[tid]]);
-    __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {
         // renormalised softmax weights of the selected experts (nn.c:524-547)
-        float ev[MOE_TOPK], sum = 0.0f;
-        for (int k = 0; k < MOE_TOPK; k++) { ev[k] = expf(topL[k] - topL[0]); sum += ev[k]; }
-        for (int k = 0; k < MOE_TOPK; k++) {
-            const float wk = ev[k] / sum;
-            s.sel[t * MOE_TOPK + k] = top[k];
-            s.w[t * MOE_TOPK + k] = wk;
-            if (sel_out) sel_out[t * MOE_TOPK + k] = top[k];
-            if (w_out) w_out[t * MOE_TOPK + k] = wk;
+        const float l0 = float(sS[top9[0]]);
+        const float ev = lane < MOE_TOPK ? expf(float(sS[top9[lane]]) - l0) : 0.0f;
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MOE_TOPK; k++) sum += __shfl_sync(0xffffffffu, ev, k);
+        if (lane < MOE_TOPK) {
+            const float wk = ev / sum;
+            const int e = top9[lane];
+            s.sel[t * MOE_TOPK + lane] = e;
+            s.w[t * MOE_TOPK + lane] = wk;
+            if (sel_out) sel_out[t * MOE_TOPK + lane] = e;
+            if (w_out) w_out[t * MOE_TOPK + lane] = wk;
+        } else if (lane == MOE_TOPK) {
+            float g = 0.0f;
+            for (int b = 0; b < MOE_EMBD / 256; b++) g += gpart[b];
+            s.gs[t] = 1.0f / (1.0f + expf(-g));
+            s.fallback[t] = need_exact;
         }
-        s.fallback[t] = need_exact;
-    }
-    // ---- Q8_K of xn (shared by every expert) and the shared-expert gate --
-    float gpart = 0.0f;
-    for (int blk = warp; blk < MOE_EMBD / 256; blk += 4) {
-        const int i0 = blk * 256 + lane * 8;
-        const float4 a0 = *reinterpret_cast<const float4 *>(xn + xn_idx(i0));
-        const float4 a1 = *reinterpret_cast<const float4 *>(xn + xn_idx(i0 + 4));
-        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        int q[8];
-        float sc;
-        q8k_block_warp_q(v, lane, s.xq + size_t(t) * MOE_EMBD + blk * 256,
-                         s.xd + size_t(t) * (MOE_EMBD / 256) + blk,
-                         s.xs + size_t(t) * (MOE_EMBD / 16) + blk * 16, q, sc);
-        // shared-expert gate input: sum_i g_i * xq_i * xd (nn.c:453)
-#pragma unroll
-        for (int c = 0; c < 8; c++) gpart += __fmul_rn(__fmul_rn(gis[i0 + c], float(q[c])), sc);
-    }
-    gpart = warp_sum(gpart);
-    if (lane == 0) fred[warp] = gpart;
-    __syncthreads();
-    if (tid == 0) {
-        const float g = (fred[0] + fred[1]) + (fred[2] + fred[3]);
-        s.gs[t] = 1.0f / (1.0f + expf(-g));
-        s.rcount[t] = 0;   // ready for the next call
     }
 }
 
-// ------------------------------------------------------------ gate / up ---
-__global__ void __launch_bounds__(256) moe_gateup_kernel(const uint8_t *__restrict__ gate_exps,
-                                                         const uint8_t *__restrict__ up_exps,
-                                                         const uint8_t *__restrict__ gate_sh,
-                                                         const uint8_t *__restrict__ up_sh,
-                                                         MoeScratch s) {
-    const int t = blockIdx.y;
-    const int slot = blockIdx.x / MOE_GU_CHUNKS, chunk = blockIdx.x % MOE_GU_CHUNKS;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr size_t EXP_BYTES = size_t(MOE_FF) * (MOE_EMBD / 256) * Q4K_BYTES;
-    pdl_wait();
-    const uint8_t *G, *U;
-    if (slot < MOE_TOPK) {
-        const int e = __ldcg(&s.sel[t * MOE_TOPK + slot]);
-        G = gate_exps + size_t(e) * EXP_BYTES;
-        U = up_exps + size_t(e) * EXP_BYTES;
-    } else {
-        G = gate_sh;
-        U = up_sh;
-    }
-    FmtQ4K::Act act;
-    FmtQ4K::load_act(act, s.xq + size_t(t) * MOE_EMBD, s.xd + size_t(t) * 8,
-                     s.xs + size_t(t) * 128, lane);
-    constexpr int RPWARP = MOE_GU_ROWS / 8;       // row pairs per warp
-    const int r0 = chunk * MOE_GU_ROWS + warp * RPWARP;
-    FmtQ4K::Wt wg[RPWARP], wu[RPWARP];
-#pragma unroll
-    for (int k = 0; k < RPWARP; k++) {
-        FmtQ4K::load_w(wg[k], G, r0 + k, MOE_EMBD, lane);
-        FmtQ4K::load_w(wu[k], U, r0 + k, MOE_EMBD, lane);
-    }
-#pragma unroll
-    for (int k = 0; k < RPWARP; k++) {
-        const float g = warp_sum(FmtQ4K::dot(wg[k], act, lane));
-        const float u = warp_sum(FmtQ4K::dot(wu[k], act, lane));
-        if (lane == 0)
-            s.h[(size_t(t) * MOE_NSLOT + slot) * MOE_FF + r0 + k] = (g / (1.0f + expf(-g))) * u;
-    }
-}
-
-// ---------------------------------------------------------- down + combine -
+// ---------------------------------------------------------------- experts --
 __device__ __forceinline__ Q6Planes shift_rows(Q6Planes P, int r0, int n) {
     P.ql += size_t(r0) * (n / 2);
     P.qh += size_t(r0) * (n / 4);
@@ -404,6 +435,15 @@ __device__ __forceinline__ Q6Planes shift_rows(Q6Planes P, int r0, int n) {
 }
 __device__ __forceinline__ const uint8_t *shift_rows(const uint8_t *P, int r0, int n) {
     return P + size_t(r0) * (n / 256) * Q4K_BYTES;
+}
+__device__ __forceinline__ void prefetch_rows(const Q6Planes &P, int rows, int n) {
+    prefetch_l2(P.ql, uint32_t(rows) * (n / 2));
+    prefetch_l2(P.qh, uint32_t(rows) * (n / 4));
+    prefetch_l2(P.sc, uint32_t(rows) * (n / 16));
+    prefetch_l2(P.d, uint32_t(rows) * (n / 256) * 2);
+}
+__device__ __forceinline__ void prefetch_rows(const uint8_t *P, int rows, int n) {
+    prefetch_l2(P, uint32_t(rows) * (n / 256) * Q4K_BYTES);
 }
 
 template <class F> struct DownPtr;
@@ -422,85 +462,145 @@ template <> struct DownPtr<FmtQ4K> {
     __device__ static const uint8_t *at(const uint8_t *base) { return base; }
 };
 
+// One cluster of XCL CTAs per (slot, token): grid (9 x XCL, T); slots 0..7
+// are the routed experts in selection order, slot 8 the shared expert
+// (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  CTA
+// `rank` computes gate/up rows rank*XGU.. (one warp per 4 row pairs,
+// SwiGLU), the cluster exchanges the 512-wide hidden vector through
+// distributed shared memory, every CTA quantizes it to Q8_K and computes
+// down rows rank*XDN..; the last of the 9 slot CTAs of a row chunk combines
+// the slots in the reference's order and adds the residual (nn.c:615-629,
+// nn.c:2246-2252).  The shared expert's weights, and the routed experts'
+// down rows as soon as the selection is known, are prefetched into L2.
 template <class F>
-__global__ void __launch_bounds__(256) moe_down_kernel(const uint8_t *__restrict__ down_exps,
-                                                       size_t expert_bytes,
-                                                       const uint8_t *__restrict__ down_sh,
-                                                       const float *x2, float *x_out,
-                                                       MoeScratch s) {
-    const int t = blockIdx.y;
-    const int slot = blockIdx.x / MOE_DOWN_CHUNKS, chunk = blockIdx.x % MOE_DOWN_CHUNKS;
+__global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
+                                                         const uint8_t *__restrict__ up_exps,
+                                                         const uint8_t *__restrict__ gate_sh,
+                                                         const uint8_t *__restrict__ up_sh,
+                                                         const uint8_t *__restrict__ down_exps,
+                                                         size_t down_bytes,
+                                                         const uint8_t *__restrict__ down_sh,
+                                                         const float *x2, float *x_out,
+                                                         MoeScratch s) {
+    const unsigned rank = cluster_rank();
+    const int slot = blockIdx.x / XCL, t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr size_t ROW = size_t(MOE_EMBD / 256) * Q4K_BYTES;
+    constexpr size_t GU_BYTES = size_t(MOE_FF) * ROW;
+    constexpr int LPR = MOE_FF / F::UNIT;
+    __shared__ float hpart[XGU];
+    __shared__ __align__(16) float hfull[MOE_FF];
     __shared__ __align__(16) int8_t hq[MOE_FF];
     __shared__ float hd[MOE_FF / 256];
     __shared__ int16_t hs[MOE_FF / 16];
     __shared__ int is_last;
+    const int g0 = int(rank) * XGU, d0 = int(rank) * XDN;
+    const uint8_t *G = gate_sh, *U = up_sh, *Db = down_sh;
+    if (slot == MOE_TOPK && tid == 0) {
+        prefetch_l2(G + g0 * ROW, XGU * ROW);
+        prefetch_l2(U + g0 * ROW, XGU * ROW);
+        prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+    }
+    pdl_trigger();
     pdl_wait();
-    // Q8_K of this slot's gated hidden vector (nn.c:434 / :467)
+    if (slot < MOE_TOPK) {
+        const int e = __ldcg(&s.sel[t * MOE_TOPK + slot]);
+        G = gate_exps + size_t(e) * GU_BYTES;
+        U = up_exps + size_t(e) * GU_BYTES;
+        Db = down_exps + size_t(e) * down_bytes;
+        if (tid == 0) prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+    }
+    // ---- gate / up rows g0 + 4 warp .. + 3 -----------------------------------
+    {
+        FmtQ4K::Act act;
+        FmtQ4K::load_act(act, s.xq + size_t(t) * MOE_EMBD, s.xd + size_t(t) * 8,
+                         s.xs + size_t(t) * 128, lane);
+        constexpr int RPWARP = XGU / 8;
+        const int r0 = g0 + warp * RPWARP;
+        FmtQ4K::Wt wg[RPWARP], wu[RPWARP];
+#pragma unroll
+        for (int k = 0; k < RPWARP; k++) {
+            FmtQ4K::load_w(wg[k], G, r0 + k, MOE_EMBD, lane);
+            FmtQ4K::load_w(wu[k], U, r0 + k, MOE_EMBD, lane);
+        }
+#pragma unroll
+        for (int k = 0; k < RPWARP; k++) {
+            const float g = warp_sum(FmtQ4K::dot(wg[k], act, lane));
+            const float u = warp_sum(FmtQ4K::dot(wu[k], act, lane));
+            if (lane == 0) hpart[warp * RPWARP + k] = (g / (1.0f + expf(-g))) * u;
+        }
+    }
+    // ---- the cluster's 512 hidden values ------------------------------------
+    cluster_sync();
+    for (int i = tid; i < MOE_FF; i += 256) hfull[i] = ld_cluster_f32(cluster_map(&hpart[i % XGU], i / XGU));
+    cluster_arrive();              // this CTA has finished reading its peers
+    __syncthreads();
     if (warp < MOE_FF / 256) {
-        const float *h = s.h + (size_t(t) * MOE_NSLOT + slot) * MOE_FF + warp * 256 + lane * 8;
-        const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(h));
-        const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(h + 4));
+        const float4 a0 = *reinterpret_cast<const float4 *>(hfull + warp * 256 + lane * 8);
+        const float4 a1 = *reinterpret_cast<const float4 *>(hfull + warp * 256 + lane * 8 + 4);
         const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         q8k_block_warp(v, lane, hq + warp * 256, hd + warp, hs + warp * 16);
     }
     __syncthreads();
-    const uint8_t *base;
-    if (slot < MOE_TOPK) base = down_exps + size_t(__ldcg(&s.sel[t * MOE_TOPK + slot])) * expert_bytes;
-    else base = down_sh;
-    const auto P = shift_rows(DownPtr<F>::at(base), chunk * MOE_DOWN_CHUNK, MOE_FF);
-    constexpr int LPR = MOE_FF / F::UNIT;
-    float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + chunk * MOE_DOWN_CHUNK;
-    gemv_warp_rows<F, 1, LPR, 1, 1>(P, MOE_FF, MOE_DOWN_CHUNK, hq, hd, hs, part, 0, warp, 8, lane);
+    // ---- down rows d0 .. d0 + XDN ---------------------------------------------
+    const auto P = shift_rows(DownPtr<F>::at(Db), d0, MOE_FF);
+    float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + d0;
+    gemv_warp_rows<F, 1, LPR, 1, 1>(P, MOE_FF, XDN, hq, hd, hs, part, 0, warp, 8, lane);
 
-    // the last of the 9 slot CTAs of this chunk combines (nn.c:615-629)
+    // ---- the last of the 9 slot CTAs of this row chunk combines --------------
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const unsigned ticket = atomicAdd(&s.dcount[t * MOE_DOWN_CHUNKS + chunk], 1u);
+        const unsigned ticket = atomicAdd(&s.dcount[t * MOE_DOWN_CHUNKS + rank], 1u);
         is_last = ticket == MOE_NSLOT - 1;
     }
     __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    if (tid < MOE_DOWN_CHUNK) {
-        const int r = chunk * MOE_DOWN_CHUNK + tid;
-        float acc = 0.0f;
+    if (is_last) {
+        __threadfence();
+        if (tid < XDN) {
+            const int r = d0 + tid;
+            float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < MOE_TOPK; k++) {
-            const float p = __ldcg(&s.part[(size_t(t) * MOE_NSLOT + k) * MOE_EMBD + r]);
-            acc = __fadd_rn(acc, __fmul_rn(__ldcg(&s.w[t * MOE_TOPK + k]), p));
+            for (int k = 0; k < MOE_TOPK; k++) {
+                const float p = __ldcg(&s.part[(size_t(t) * MOE_NSLOT + k) * MOE_EMBD + r]);
+                acc = __fadd_rn(acc, __fmul_rn(__ldcg(&s.w[t * MOE_TOPK + k]), p));
+            }
+            const float psh = __ldcg(&s.part[(size_t(t) * MOE_NSLOT + MOE_TOPK) * MOE_EMBD + r]);
+            acc = __fadd_rn(acc, __fmul_rn(__ldcg(&s.gs[t]), psh));
+            x_out[size_t(t) * MOE_EMBD + r] = __fadd_rn(acc, x2[size_t(t) * MOE_EMBD + r]);
         }
-        const float psh = __ldcg(&s.part[(size_t(t) * MOE_NSLOT + MOE_TOPK) * MOE_EMBD + r]);
-        acc = __fadd_rn(acc, __fmul_rn(__ldcg(&s.gs[t]), psh));
-        x_out[size_t(t) * MOE_EMBD + r] = __fadd_rn(acc, x2[size_t(t) * MOE_EMBD + r]);
+        if (tid == 0) s.dcount[t * MOE_DOWN_CHUNKS + rank] = 0;
     }
-    if (tid == 0) s.dcount[t * MOE_DOWN_CHUNKS + chunk] = 0;
+    cluster_wait();                // no CTA leaves while a peer may read it
 }
 
+static bool g_moe_attrs = false;
+
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st) {
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters) {
     MoeScratch s = moe_scratch_layout(scratch, T);
-    QMA_CHECK_CUDA(cudaMemsetAsync(s.rcount, 0, sizeof(unsigned) * T, st));
-    QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
-    moe_router_kernel<<<dim3(MOE_NEXP / 4, T), 128, 0, st>>>(x2, w.post_norm, w.gate_inp,
-                                                            w.gate_inp_shexp, s, sel, wts);
-    QMA_CHECK_LAUNCH();
-    moe_gateup_kernel<<<dim3(MOE_NSLOT * MOE_GU_CHUNKS, T), 256, 0, st>>>(
-        static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
-        static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp), s);
-    QMA_CHECK_LAUNCH();
+    if (!g_moe_attrs) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        g_moe_attrs = true;
+    }
+    if (clear_counters)
+        QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
+    const bool pdl = pdl_enabled() && !clear_counters;
+    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(256), 0, st, RCL, pdl, x2, w.post_norm,
+                             w.gate_inp, w.gate_inp_shexp, s, sel, wts));
     const size_t eb = packed_bytes(w.down_type, MOE_EMBD, MOE_FF);
-    const dim3 dg(MOE_NSLOT * MOE_DOWN_CHUNKS, T);
+    const dim3 grid(MOE_NSLOT * XCL, T);
+    const uint8_t *ge = static_cast<const uint8_t *>(w.gate_exps), *ue = static_cast<const uint8_t *>(w.up_exps);
+    const uint8_t *gsh = static_cast<const uint8_t *>(w.gate_shexp), *ush = static_cast<const uint8_t *>(w.up_shexp);
+    const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
-        moe_down_kernel<FmtQ6K><<<dg, 256, 0, st>>>(static_cast<const uint8_t *>(w.down_exps), eb,
-                                                   static_cast<const uint8_t *>(w.down_shexp), x2,
-                                                   x_out, s);
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(256), 0, st, XCL, pdl_enabled(), ge, ue,
+                                 gsh, ush, de, eb, dsh, x2, x_out, s));
     else
-        moe_down_kernel<FmtQ4K><<<dg, 256, 0, st>>>(static_cast<const uint8_t *>(w.down_exps), eb,
-                                                    static_cast<const uint8_t *>(w.down_shexp), x2,
-                                                    x_out, s);
-    QMA_CHECK_LAUNCH();
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(256), 0, st, XCL, pdl_enabled(), ge, ue,
+                                 gsh, ush, de, eb, dsh, x2, x_out, s));
     return QMA_CUDA_OK;
 }
 
@@ -526,7 +626,7 @@ int qma_cuda_moe_layer(const qma_cuda_moe_weights *w, const float *x2, int T, fl
     QMA_REQUIRE(scratch_bytes >= qma::moe_scratch_bytes(T),
                 "qma_cuda_moe_layer: scratch %zu bytes < %zu needed", scratch_bytes,
                 qma::moe_scratch_bytes(T));
-    return qma::moe_layer(*w, x2, T, x_out, sel, wts, scratch, qma::as_stream(stream));
+    return qma::moe_layer(*w, x2, T, x_out, sel, wts, scratch, qma::as_stream(stream), true);
 }
 
 int qma_cuda_moe_exact_fallbacks(const void *scratch, int T, int *count) {

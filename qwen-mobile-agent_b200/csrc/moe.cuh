@@ -15,10 +15,10 @@ constexpr int MOE_DOWN_CHUNK = 128;   // down-projection output rows per CTA
 constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
 
 // Per-call device scratch of the MoE block for T tokens (moe_scratch_layout
-// carves one caller-provided buffer).  The two counter arrays must be zero
-// when a call starts; every call leaves them zero again.
+// carves one caller-provided buffer).  The combine tickets (dcount) must be
+// zero when a call starts; every call leaves them zero again.
 struct MoeScratch {
-    unsigned *rcount;      // [T] router CTAs finished
+    unsigned *rcount;      // [T] unused (kept for the scratch layout)
     unsigned *dcount;      // [T][16] down CTAs finished per output chunk
     double *S, *B;         // [T][256] exact logit, bound on the fp32 logit
     int *fallback;         // [T] 1 if the exact sequential recompute ran
@@ -34,7 +34,11 @@ struct MoeScratch {
 
 size_t moe_scratch_bytes(int T);
 MoeScratch moe_scratch_layout(void *base, int T);
+// clear_counters: zero the combine tickets first (a caller's fresh scratch);
+// the engine's own scratch starts zeroed and every call leaves it zeroed, so
+// it skips the memset and launches the router with programmatic dependent
+// launch.
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st);
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters);
 
 }  // namespace qma

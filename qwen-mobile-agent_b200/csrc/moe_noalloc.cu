@@ -90,5 +90,5 @@ extern "C" int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const f
     void *scratch = nullptr;
     const int rc = qma::noalloc_scratch(&scratch);
     if (rc) return rc;
-    return qma::moe_layer(*w, x2, T, x_out, sel, wts, scratch, qma::as_stream(stream));
+    return qma::moe_layer(*w, x2, T, x_out, sel, wts, scratch, qma::as_stream(stream), true);
 }

@@ -1,12 +1,23 @@
-"""Full-model parity: the engine's qma_eval replacement against the oracle's
-restatement of qma_eval and the golden fixture from the reference itself, on
-the 40-layer synthetic qwen35moe (configs[3] shapes; Q6_K embeddings and LM
-head, the types the reference supports).
+"""Full-model parity of the engine's qma_eval replacement on the 40-layer
+synthetic qwen35moe (configs[3] shapes; Q6_K embeddings and LM head, the
+types the reference supports), against the oracle's restatement of qma_eval
+(pinned bit-exact to the reference by tests/test_oracle_pin.py and the
+golden fixture).
 
-Bars: greedy tokens identical; last-token logits within 1e-3 scaled relative
-error.  The weights are generated on the device
-(byte-identical to the oracle's generator, tests/test_synth_gpu.py) and
-copied to the host for the oracle."""
+Why layer by layer: this random-init model is chaotic.  A 1-ulp difference
+anywhere (fp32 summation order, a libm expf) flips an int8 of a later Q8_K
+activation once in a while, and the top-8-of-256 routing of near-tied
+random logits turns such flips into O(1) differences within a few layers:
+the reference built with its own production flags (-O3 -ffast-math,
+oracle/Makefile ref-fast) differs from its strict build by 0.68 norm-rel at
+the first logits of the golden prompt.  So the gate is teacher forcing:
+each oracle layer gets the engine's own input for that layer, and each
+layer's output must agree within the fp32 tolerance.  What is integer or
+byte work is compared exactly: embedding rows, quantized KV records, the
+greedy decode graph against eager evaluation.
+
+The weights are generated on the device (byte-identical to the oracle's
+generator, tests/test_synth_gpu.py) and copied to the host for the oracle."""
 import ctypes as C
 import os
 
@@ -15,14 +26,17 @@ import pytest
 
 import oracle as O
 import qma_cuda as Q
-from helpers import assert_close
 
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "full_model.npz")
 SEED = 7
 N_CTX = 4096
-RTOL = 1e-3
+# per-layer bars of the teacher-forced comparison: norm-relative error of
+# the layer output over all tokens, and of the worst single token (a rare
+# Q8_K int8 flip moves one token's output by ~1e-3)
+RTOL_LAYER = 1e-3
+RTOL_TOKEN = 5e-3
 
 
 def device_blob(arr, n, size, seed):
@@ -48,70 +62,143 @@ def full(cuda):
     model = Q.Model(tp, n, host_blob=blob)
     om = O.lib().qo_model_new(arr, n, O._ptr(blob), O.N_VOCAB)
     assert om
+    O.lib().qo_set_threads(32)
     yield {"arr": arr, "n": n, "tp": tp, "blob": blob, "model": model, "om": om}
     O.lib().qo_model_free(om)
     model.close()
 
 
-def oracle_run(om, prompt, decode_tokens):
+def gpu_hidden(model, prompt, n_layers, decode_token=None):
+    """Residual stream after n_layers layers for the prompt (or, with
+    decode_token, for that token evaluated after the whole prompt)."""
+    st = Q.State(model, N_CTX)
+    try:
+        if decode_token is None:
+            return st.eval_hidden(prompt, n_layers)
+        st.eval(prompt)
+        return st.eval_hidden(np.array([decode_token], np.int32), n_layers)
+    finally:
+        st.close()
+
+
+def norm_rel(got, want, axis=None):
+    return np.linalg.norm(got - want, axis=axis) / np.linalg.norm(want, axis=axis)
+
+
+def test_oracle_full_forward_matches_reference_golden(full):
+    """The teacher itself: the oracle's qma_eval on the golden prompt and
+    greedy continuation reproduces the reference's own run (oracle/_ref,
+    tests/golden/make_golden.py) bit for bit at its top-64 logits."""
+    g = np.load(GOLDEN)
     L = O.lib()
     s = L.qo_state_new(N_CTX)
-    out = []
     try:
         lo = np.zeros(O.N_VOCAB, np.float32)
-        p = np.ascontiguousarray(prompt, np.int32)
-        L.qo_eval(om, s, O._ptr(p), len(p), O._ptr(lo), 0)
-        out.append(lo.copy())
-        for tok in decode_tokens:
-            one = np.array([tok], np.int32)
-            L.qo_eval(om, s, O._ptr(one), 1, O._ptr(lo), 0)
-            out.append(lo.copy())
+        p = np.ascontiguousarray(g["prompt"], np.int32)
+        L.qo_eval(full["om"], s, O._ptr(p), len(p), O._ptr(lo), 0)
+        toks = []
+        for k in range(len(g["greedy"]) + 1):
+            ids = g["top_ids"][k]
+            assert np.array_equal(lo[ids].view(np.uint32), g["top_vals"][k].astype(np.float32).view(np.uint32))
+            if k == len(g["greedy"]):
+                break
+            toks.append(int(np.argmax(lo)))
+            L.qo_eval(full["om"], s, O._ptr(np.array([toks[-1]], np.int32)), 1, O._ptr(lo), 0)
+        assert toks == list(g["greedy"])
     finally:
         L.qo_state_free(s)
-    return out
 
 
-@pytest.mark.parametrize("n_layers", [1, 3, 4, 8, 40])
-def test_hidden_state_after_n_layers(full, n_layers):
-    """Residual stream after the first n layers (GDN layers 0-2, attention
-    layer 3, ...) for a 5-token prompt then one decode token."""
-    prompt = np.array([11, 22, 33, 44, 55], np.int32)
-    st = Q.State(full["model"], N_CTX)
+def test_embedding_rows_bit_exact(full):
+    prompt = np.array([0, 1, 7, 151935, 62913], np.int32)
+    got = gpu_hidden(full["model"], prompt, 0)
+    want = np.zeros_like(got)
+    s = O.lib().qo_state_new(N_CTX)
+    O.lib().qo_eval_hidden(full["om"], s, O._ptr(prompt), len(prompt), 0, O._ptr(want))
+    O.lib().qo_state_free(s)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_layers_teacher_forced_prefill_and_decode(full):
+    """Every layer (30 gated-delta-net, 10 attention, each with its MoE
+    block) on a 24-token prompt at positions 0..23 and then on one decode
+    token at position 24, the oracle's layer fed the engine's input."""
     L = O.lib()
+    prompt = np.random.default_rng(SEED).integers(0, O.N_VOCAB, 24).astype(np.int32)
+    tok = 62913
+    xs = [gpu_hidden(full["model"], prompt, nl) for nl in range(41)]
+    xd = [gpu_hidden(full["model"], prompt, nl, tok) for nl in range(41)]
+    os_ = L.qo_state_new(N_CTX)
+    report = []
+    try:
+        for il in range(40):
+            out = np.zeros_like(xs[il])
+            L.qo_layer_forward(full["om"], os_, il, O._ptr(np.ascontiguousarray(xs[il])), len(prompt), 0,
+                               O._ptr(out))
+            report.append(("prefill", il, norm_rel(xs[il + 1], out), norm_rel(xs[il + 1], out, axis=1).max()))
+        for il in range(40):
+            out = np.zeros_like(xd[il])
+            L.qo_layer_forward(full["om"], os_, il, O._ptr(np.ascontiguousarray(xd[il])), 1, len(prompt),
+                               O._ptr(out))
+            e = norm_rel(xd[il + 1], out)
+            report.append(("decode", il, e, e))
+    finally:
+        L.qo_state_free(os_)
+    bad = [r for r in report if r[2] > RTOL_LAYER and r[0] == "prefill" or r[3] > RTOL_TOKEN]
+    assert not bad, "layers over tolerance (phase, layer, all-token, worst-token): %r" % bad
+    # a single decode token has no averaging: its layers must still be at
+    # the fp32 level typically, with rare int8 flips
+    dec = sorted(r[2] for r in report if r[0] == "decode")
+    assert dec[len(dec) // 2] <= RTOL_LAYER
+
+
+def test_kv_records_bit_exact(full):
+    """The quantized K/V records (q4 + q2, 240 bytes per slot and head) the
+    first attention layer appends for a single token, engine vs oracle."""
+    L = O.lib()
+    L.qo_state_kv_slot.restype = C.POINTER(C.c_uint8)
+    toks = np.array([11], np.int32)
+    st = Q.State(full["model"], N_CTX)
     os_ = L.qo_state_new(N_CTX)
     try:
-        for toks in (prompt, np.array([66], np.int32)):
-            got = st.eval_hidden(toks, n_layers)
-            want = np.zeros_like(got)
-            L.qo_eval_hidden(full["om"], os_, O._ptr(toks), len(toks), n_layers, O._ptr(want))
-            assert_close(got, want, RTOL, f"hidden after {n_layers} layers, T={len(toks)}")
+        st.eval_hidden(toks, -4)          # through the mixer of layer 3
+        want_h = np.zeros((1, 2048), np.float32)
+        L.qo_eval_hidden(full["om"], os_, O._ptr(toks), 1, -4, O._ptr(want_h))
+        for head in range(4):
+            got = np.zeros(240, np.uint8)
+            Q.call("qma_cuda_state_kv_slot", st.h, 0, head, 0, Q.ptr(got))
+            want = np.ctypeslib.as_array(L.qo_state_kv_slot(os_, 0, head, 0), (240,))
+            assert np.array_equal(got, want), f"KV head {head}: bytes {np.nonzero(got != want)[0][:16]}"
     finally:
         st.close()
         L.qo_state_free(os_)
 
 
-def test_prompt_and_greedy_decode_match_reference_and_oracle(full):
-    g = np.load(GOLDEN) if os.path.exists(GOLDEN) else None
-    rng = np.random.default_rng(SEED)
-    prompt = g["prompt"] if g is not None else rng.integers(0, O.N_VOCAB, 24).astype(np.int32)
-    st = Q.State(full["model"], N_CTX)
+def test_greedy_graph_matches_eager_eval_across_rebuild(full):
+    """decode_greedy (one CUDA graph per step, argmax on the device, the
+    graph re-captured when the HCM live index is rebuilt at position 128)
+    reproduces token by token what eager qma_cuda_eval calls compute."""
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, O.N_VOCAB, 122).astype(np.int32)
+    a = Q.State(full["model"], N_CTX)
+    b = Q.State(full["model"], N_CTX)
     try:
-        got0 = st.eval(prompt)
-        tok0 = int(np.argmax(got0))
-        toks, last = st.decode_greedy(tok0, 4)
+        la = a.eval(prompt)
+        lb = b.eval(prompt)
+        assert np.array_equal(la, lb)
+        tok = int(np.argmax(la))
+        toks, last = a.decode_greedy(tok, 12)     # toks[i]: step i's input token
+        fed = []
+        for _ in range(12):
+            fed.append(tok)
+            lb = b.eval(np.array([tok], np.int32))
+            tok = int(np.argmax(lb))
+        assert list(toks) == fed
+        assert np.array_equal(last, lb)
+        assert a.n_pos == b.n_pos == 122 + 12
     finally:
-        st.close()
-    want = oracle_run(full["om"], prompt, list(toks))
-    assert_close(got0, want[0], RTOL, "prompt logits")
-    assert tok0 == int(np.argmax(want[0]))
-    assert_close(last, want[-1], RTOL, "decode logits")
-    oracle_toks = [int(np.argmax(w)) for w in want[:-1]]
-    assert list(toks) == oracle_toks
-    if g is not None:
-        # the reference's own run (oracle/_ref) on the same weights
-        assert list(toks) == list(g["greedy"])
-        ids, vals = g["top_ids"][0], g["top_vals"][0]
-        assert_close(got0[ids], vals, RTOL, "prompt logits vs reference top-64")
+        a.close()
+        b.close()
 
 
 def test_model_synth_matches_model_load(full):
@@ -128,24 +215,6 @@ def test_model_synth_matches_model_load(full):
         assert np.array_equal(la, lb)
     finally:
         m2.close()
-
-
-def test_decode_after_live_index_rebuild(full):
-    # a 130-token prompt, then decoding: the first decode step (position 130
-    # >= 128) rebuilds the HCM live index, so decoding attends live index +
-    # tail rather than the dense range
-    rng = np.random.default_rng(21)
-    prompt = rng.integers(0, O.N_VOCAB, 130).astype(np.int32)
-    st = Q.State(full["model"], N_CTX)
-    try:
-        got = st.eval(prompt)
-        toks, last = st.decode_greedy(int(np.argmax(got)), 2)
-    finally:
-        st.close()
-    want = oracle_run(full["om"], prompt, list(toks))
-    assert_close(got, want[0], RTOL, "130-token prompt")
-    assert list(toks) == [int(np.argmax(w)) for w in want[:-1]]
-    assert_close(last, want[-1], RTOL, "decode after rebuild")
 
 
 def test_ecache_get_addresses_expert_records(full):
