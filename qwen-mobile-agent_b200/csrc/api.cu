@@ -20,6 +20,11 @@ void clear_error() { g_err[0] = 0; }
 
 bool pdl_enabled() { return true; }
 
+#ifdef QMA_TRACE
+__device__ unsigned long long g_trace[TRACE_CAP][2];
+__device__ unsigned g_trace_n;
+#endif
+
 size_t packed_bytes(int wtype, int rows, int n) {
     switch (wtype) {
     case QMA_TYPE_Q4_K: return size_t(rows) * (n / QK) * Q4K_BYTES;
@@ -131,3 +136,18 @@ int qma_cuda_repack(int wtype, const void *src, int rows, int n, void *dst, void
 }
 
 }  // extern "C"
+
+#ifdef QMA_TRACE
+// Trace build only: copy up to `cap` records (2 x u64 each) to `out`, return
+// how many were written since the last reset, and reset the ring.
+extern "C" int qma_trace_read(unsigned long long *out, int cap) {
+    unsigned n = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    cudaMemcpyFromSymbol(&n, qma::g_trace_n, sizeof(n));
+    const unsigned k = n < unsigned(cap) ? n : unsigned(cap);
+    if (k) cudaMemcpyFromSymbol(out, qma::g_trace, size_t(k) * 16);
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(qma::g_trace_n, &zero, sizeof(zero));
+    return int(n);
+}
+#endif

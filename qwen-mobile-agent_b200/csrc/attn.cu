@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
     const float *__restrict__ proj, int proj_ld, const float *__restrict__ qn,
     const float *__restrict__ kn, const float *__restrict__ rope, const StepParams *spp,
     float *qr, float *z, uint8_t *kv, float *qf, float *sal) {
+    QMA_TRACE_SCOPE(TK_QK_PREP);
     const int t = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float qfv[4];
     pdl_trigger();
@@ -303,6 +304,7 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
                                                          const StepParams *spp, int nk_max,
                                                          int span, int nchunk, float *scores,
                                                          float *mpart, float *lpart, float *opart) {
+    QMA_TRACE_SCOPE(TK_ATTN_CHUNK);
     const int chunk = blockIdx.x, kh = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ __align__(16) float qs[8 * QS_LD];
@@ -425,6 +427,7 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float *__restr
                                                             int nchunk, const float *__restrict__ z,
                                                             float *ml, int8_t *xq, float *xd,
                                                             int16_t *xs) {
+    QMA_TRACE_SCOPE(TK_ATTN_COMBINE);
     extern __shared__ float fsh[];              // [16][nchunk] chunk factors
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float inv[NHEAD];
@@ -483,6 +486,7 @@ __global__ void __launch_bounds__(256) attn_salience_kernel(const float *__restr
                                                             const int *__restrict__ live,
                                                             const StepParams *spp, float *sal,
                                                             float *pin_sal) {
+    QMA_TRACE_SCOPE(TK_SALIENCE);
     const int jj = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -563,9 +567,12 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(a.T), dim3(1024), fsh, st, 1, pdl_enabled(), a.opart, a.cmax,
                              a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs));
     QMA_CHECK_LAUNCH();
-    QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, pdl_enabled(),
+    return QMA_CUDA_OK;
+}
+
+int launch_salience(const AttnArgs &a, cudaStream_t st) {
+    QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, false,
                              a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
-    QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
 

@@ -30,7 +30,14 @@ struct AttnArgs {
 int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const float *kn,
                           const float *rope, const StepParams *sp, int T, float *qr, float *z,
                           uint8_t *kv, float *qf, float *sal, cudaStream_t st);
+// chunked attention + combine (the token's output, Q8_K for attn_output)
 int launch_attention(const AttnArgs &a, cudaStream_t st);
+// the salience EMA of the attended positions (needs the combine's max/sum)
+int launch_salience(const AttnArgs &a, cudaStream_t st);
+// positions per chunk CTA for T queries over at most nk positions
+__host__ __device__ inline int attn_span(int T, int nk) {
+    return T > 1 ? 256 : (nk <= 1024 ? 16 : (nk <= 4096 ? 32 : 64));
+}
 int launch_arena_copy(const int2 *pairs, int n, uint8_t *const *kv, uint8_t *const *arena,
                       const float *sal, float *pin_sal, int n_ctx, cudaStream_t st);
 

@@ -168,6 +168,50 @@ __device__ __forceinline__ void prefetch_l2_range(const void *p, size_t bytes) {
     }
 }
 
+// ------------------------------------------- bulk copies into shared memory --
+// Global -> this CTA's shared memory through the TMA engine (non-tensor
+// cp.async.bulk, no multicast), completion counted in bytes on an mbarrier.
+// Addresses 16-byte aligned, sizes multiples of 16.
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier: false after `limit` polls
+// (each poll may suspend the thread for a hardware-defined time).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = 1u << 22) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Thread-block cluster helpers (split arrive / wait of the cluster barrier,
 // and a load from another CTA's shared memory).
 __device__ __forceinline__ unsigned cluster_rank() {
@@ -243,6 +287,42 @@ static inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, 
 
 // Programmatic dependent launch of the engine's kernels (on by default).
 bool pdl_enabled();
+
+// ---------------------------------------------------------------- tracing --
+// Built with -DQMA_TRACE, every CTA of the forward kernels appends
+// {kernel id, CTA, entry ns, exit ns} (the GPU's global timer) to a device
+// ring, read back with qma_trace_read(); otherwise QMA_TRACE_SCOPE is empty.
+enum TraceKernel : uint32_t {
+    TK_EMBED = 1, TK_RMSNORM, TK_GEMV, TK_CONV, TK_GDN, TK_GATED_NORM, TK_QK_PREP, TK_ATTN_CHUNK,
+    TK_ATTN_COMBINE, TK_SALIENCE, TK_ROUTER, TK_EXPERT, TK_ARGMAX
+};
+#ifdef QMA_TRACE
+constexpr uint32_t TRACE_CAP = 1u << 22;
+extern __device__ unsigned long long g_trace[TRACE_CAP][2];
+extern __device__ unsigned g_trace_n;
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long v;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
+    return v;
+}
+struct TraceScope {
+    uint32_t id;
+    unsigned long long t0;
+    __device__ explicit TraceScope(uint32_t k) : id(k), t0(threadIdx.x == 0 ? gtimer() : 0) {}
+    __device__ ~TraceScope() {
+        if (threadIdx.x == 0) {
+            const unsigned i = atomicAdd(&g_trace_n, 1u) % TRACE_CAP;
+            const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+            g_trace[i][0] = (static_cast<unsigned long long>(id) << 56) |
+                            (static_cast<unsigned long long>(cta & 0xffffff) << 32) | (t0 & 0xffffffffull);
+            g_trace[i][1] = gtimer();
+        }
+    }
+};
+#define QMA_TRACE_SCOPE(k) ::qma::TraceScope qma_trace_scope_(k)
+#else
+#define QMA_TRACE_SCOPE(k) do {} while (0)
+#endif
 
 // 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,
 // quants.c:18-26 / q8k.c:22-30).

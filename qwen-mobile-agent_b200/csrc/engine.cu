@@ -99,6 +99,10 @@ struct qma_cuda_state {
     int graph_kernels = 0;
     size_t state_bytes = 0;
     bool stop_before_moe = false;   // qma_cuda_eval_hidden with n_layers < 0
+    // the salience update of an attention layer runs on a side stream,
+    // joined before the next attention layer (or the end of the step)
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     static constexpr int HCM_REBUILD_INIT = 128;
 };
 
@@ -348,6 +352,9 @@ static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     s->m = m;
     s->n_ctx = n_ctx;
     QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    QMA_CHECK_CUDA(cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming));
+    QMA_CHECK_CUDA(cudaEventCreateWithFlags(&s->ev_join, cudaEventDisableTiming));
     cudaStream_t st = s->st;
     int rc = 0;
 #define TRY(x) do { if ((rc = (x))) return rc; } while (0)
@@ -573,7 +580,8 @@ static int nk_upper(const qma_cuda_state *s, int pos_now, int T, bool graph) {
 }
 
 static int ensure_attn_scratch(qma_cuda_state *s, int T, int nk, int pv_chunk) {
-    const size_t nsc = size_t((nk + 63) / 64), npv = size_t((nk + pv_chunk - 1) / pv_chunk);
+    // cmax holds the per-chunk maxima of the chunked attention
+    const size_t npv = size_t((nk + pv_chunk - 1) / pv_chunk), nsc = npv;
     const bool moves = size_t(T) * NHEAD * nk > s->scores_cap || size_t(T) * NHEAD * nsc > s->cmax_cap ||
                        size_t(T) * NHEAD * npv * HEAD_DIM > s->opart_cap ||
                        size_t(T) * NHEAD * npv > s->lpart_cap;
@@ -602,6 +610,7 @@ __device__ __forceinline__ void argmax_merge(float &v, int &idx, float ov, int o
 __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ logits, int n,
                                                      StepParams *sp, int *out, float *pv, int *pi,
                                                      unsigned *cnt) {
+    QMA_TRACE_SCOPE(TK_ARGMAX);
     __shared__ float bv[16];
     __shared__ int bi[16];
     __shared__ int last;
@@ -660,13 +669,33 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
     int rc;
 #define TRY(x) do { if ((rc = (x))) return rc; } while (0)
     TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, tokens_dev, s->sp_dev, T, s->x, st));
-    const int pv_chunk = T == 1 ? 64 : 256;
+    const int pv_chunk = attn_span(T, nk_cap);
+    bool side_pending = false;     // a salience update is running on s->side
     for (int il = 0; il < n_layers; il++) {
         const LayerW &L = m->L[il];
-        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st));
+        // this layer's output projection, router and shared expert into L2
+        // while the input projection and the mixer run
+        Prefetch pf;
+        pf.p[0] = L.out_proj;
+        pf.bytes[0] = packed_bytes(L.out_type, EMBD, is_attn(il) ? WO_DIM : VAL_DIM);
+        pf.p[1] = L.moe.gate_inp;
+        pf.bytes[1] = sizeof(float) * size_t(EMBD) * 256;
+        pf.p[2] = L.moe.gate_shexp;
+        pf.bytes[2] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
+        pf.p[3] = L.moe.up_shexp;
+        pf.bytes[3] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
+        pf.p[4] = L.moe.down_shexp;
+        pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
+        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, pf));
         TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st));
         if (is_attn(il)) {
             const int lay = il / 4;
+            if (side_pending) {
+                // the previous layer's salience reads `scores` and writes
+                // the slot this append resets
+                QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
+                side_pending = false;
+            }
             TRY(launch_qk_prep_append(s->proj, L.in_rows, L.q_norm, L.k_norm, s->rope, s->sp_dev, T,
                                       s->qr, s->z, s->kv[lay], s->qf, s->sal, st));
             AttnArgs a;
@@ -677,6 +706,11 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             a.sal = s->sal + size_t(lay) * s->n_ctx;
             a.pin_sal = s->pin_sal + size_t(lay) * HCM_H_PIN;
             TRY(launch_attention(a, st));
+            QMA_CHECK_CUDA(cudaEventRecord(s->ev_fork, st));
+            QMA_CHECK_CUDA(cudaStreamWaitEvent(s->side, s->ev_fork, 0));
+            TRY(launch_salience(a, s->side));
+            QMA_CHECK_CUDA(cudaEventRecord(s->ev_join, s->side));
+            side_pending = true;
             TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
         } else {
             const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
@@ -696,6 +730,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         // x = x2 + moe(rms_norm(x2) * post_norm)
         TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false));
     }
+    if (side_pending) QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
     if (logits_mode) {
         const int rows = logits_mode == 2 ? T : 1;
         const float *xin = logits_mode == 2 ? s->x : s->x + size_t(T - 1) * EMBD;
@@ -704,6 +739,15 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
     }
 #undef TRY
     return QMA_CUDA_OK;
+}
+
+// A bounded wait inside a kernel that gave up (a copy that never landed)
+// fails the call instead of returning silently wrong results.
+static int check_wait_timeouts() {
+    const int n = moe_wait_timeouts();
+    if (n == 0) return QMA_CUDA_OK;
+    set_error("%d bounded waits for weight copies ran out (or the counter could not be read)", n);
+    return QMA_CUDA_ERR_TIMEOUT;
 }
 
 static void fill_params(qma_cuda_state *s, StepParams &p, int pos_now, int T, int token) {
@@ -760,7 +804,7 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
         QMA_CHECK_CUDA(cudaMemcpyAsync(s->sp_dev, s->sp_host, sizeof(StepParams),
                                        cudaMemcpyHostToDevice, st));
         const int nk = nk_upper(s, pos_now, T, false);
-        if ((rc = ensure_attn_scratch(s, T, nk, T == 1 ? 64 : 256))) return rc;
+        if ((rc = ensure_attn_scratch(s, T, nk, attn_span(T, nk)))) return rc;
         const bool last = done + T == n_tokens;
         const int mode = n_layers < NLAYER ? 0 : (logits_all ? 2 : (last && logits ? 1 : 0));
         if ((rc = forward(s, *s->sp_host, s->tokens_dev, nk, mode, n_layers))) return rc;
@@ -779,7 +823,7 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
         done += T;
     }
     s->n_pos += n_tokens;
-    return QMA_CUDA_OK;
+    return check_wait_timeouts();
 }
 
 // Capture one decode step (T = 1, token and position read from sp_dev,
@@ -787,7 +831,7 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
 static int capture_decode(qma_cuda_state *s) {
     cudaStream_t st = s->st;
     const int nk = nk_upper(s, s->n_pos, 1, true);
-    int rc = ensure_attn_scratch(s, 1, nk, 64);
+    int rc = ensure_attn_scratch(s, 1, nk, attn_span(1, nk));
     if (rc) return rc;
     QMA_CHECK_CUDA(cudaStreamSynchronize(st));
     cudaGraph_t g;
@@ -868,7 +912,7 @@ static int decode_greedy(qma_cuda_state *s, int token, int n_steps, int *tokens_
         QMA_CHECK_CUDA(cudaMemcpyAsync(logits, s->logits, sizeof(float) * m->n_vocab,
                                        cudaMemcpyDeviceToHost, st));
     QMA_CHECK_CUDA(cudaStreamSynchronize(st));
-    return QMA_CUDA_OK;
+    return check_wait_timeouts();
 }
 
 }  // namespace qma
@@ -927,6 +971,10 @@ int qma_cuda_state_free(qma_cuda_state *s) {
     for (void *p : s->allocs) cudaFree(p);
     for (float *p : {s->scores, s->cmax, s->opart, s->lpart}) if (p) cudaFree(p);
     if (s->sp_host) cudaFreeHost(s->sp_host);
+    cudaStreamSynchronize(s->side);
+    cudaEventDestroy(s->ev_fork);
+    cudaEventDestroy(s->ev_join);
+    cudaStreamDestroy(s->side);
     cudaStreamDestroy(s->st);
     delete s;
     return QMA_CUDA_OK;

@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, 
                                                    const int8_t *xq, const float *xd,
                                                    const int16_t *xsum, float *out, int out_ld,
                                                    const float *resid) {
+    QMA_TRACE_SCOPE(TK_GEMV);
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;

@@ -52,6 +52,13 @@ struct FmtQ4K {
         w.q0 = ld_stream16(b + 16 + (u & 3) * 32);
         w.q1 = ld_stream16(b + 32 + (u & 3) * 32);
     }
+    // the same unit from a copy of the rows in shared memory
+    __device__ static void load_w_smem(Wt &w, Ptr W, int row, int n_in, int u) {
+        const uint8_t *b = W + size_t(row) * (n_in / 256) * 144 + (u >> 2) * 144;
+        w.h = *reinterpret_cast<const uint4 *>(b);
+        w.q0 = *reinterpret_cast<const uint4 *>(b + 16 + (u & 3) * 32);
+        w.q1 = *reinterpret_cast<const uint4 *>(b + 32 + (u & 3) * 32);
+    }
     // exact integer sub-block sums (low nibbles -> sub-block 2g, high -> 2g+1)
     __device__ static void isums(const Wt &w, const Act &a, int &lo, int &hi) {
         const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
@@ -126,6 +133,15 @@ struct FmtQ6K {
         w.h1 = ld_stream16(qh + 16);
         w.sc = ld_stream8(P.sc + size_t(row) * (n_in / 16) + sb * 16 + j * 8);
         w.d = ld_stream2(P.d + size_t(row) * (n_in / 256) + sb);
+    }
+    __device__ static void load_w_smem(Wt &w, const Ptr &P, int row, int n_in, int u) {
+        const int sb = u >> 1, j = u & 1;
+        const uint4 *ql = reinterpret_cast<const uint4 *>(P.ql + size_t(row) * (n_in / 2) + sb * 128 + j * 64);
+        const uint4 *qh = reinterpret_cast<const uint4 *>(P.qh + size_t(row) * (n_in / 4) + sb * 64 + j * 32);
+        w.l0 = ql[0]; w.l1 = ql[1]; w.l2 = ql[2]; w.l3 = ql[3];
+        w.h0 = qh[0]; w.h1 = qh[1];
+        w.sc = *reinterpret_cast<const uint2 *>(P.sc + size_t(row) * (n_in / 16) + sb * 16 + j * 8);
+        w.d = *reinterpret_cast<const uint16_t *>(P.d + size_t(row) * (n_in / 256) + sb);
     }
     // exact sum over the 8 sixteen-lane groups of scale_g * sum((q-32)*xq)
     __device__ static int isum(const Wt &w, const Act &a) {
@@ -205,6 +221,13 @@ struct FmtQ80 {
         isums(w, a, i0, i1);
         const float d0 = h2f(uint16_t(w.d2 & 0xffff)), d1 = h2f(uint16_t(w.d2 >> 16));
         return (float(i0) * d0 + float(i1) * d1) * a.xd;
+    }
+};
+
+// A format whose weights are read from a copy in shared memory.
+template <class F> struct SmemRows : F {
+    __device__ static void load_w(typename F::Wt &w, const typename F::Ptr &W, int row, int n_in, int u) {
+        F::load_w_smem(w, W, row, n_in, u);
     }
 };
 

@@ -16,6 +16,7 @@ namespace qma {
 __global__ void __launch_bounds__(256) embed_q8_kernel(const int8_t *q, const __half *d,
                                                        const int *tokens, const StepParams *sp,
                                                        float *x) {
+    QMA_TRACE_SCOPE(TK_EMBED);
     const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -32,6 +33,7 @@ __global__ void __launch_bounds__(256) embed_q8_kernel(const int8_t *q, const __
 
 __global__ void __launch_bounds__(256) embed_q4k_kernel(const uint8_t *W, const int *tokens,
                                                         const StepParams *sp, float *x) {
+    QMA_TRACE_SCOPE(TK_EMBED);
     const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -55,6 +57,7 @@ __global__ void __launch_bounds__(256) embed_q4k_kernel(const uint8_t *W, const 
 // Q6_K planes (dequantize_row_q6_K, quants.c:50-75: y = d * sc * q)
 __global__ void __launch_bounds__(256) embed_q6k_kernel(Q6Planes P, const int *tokens,
                                                         const StepParams *sp, float *x) {
+    QMA_TRACE_SCOPE(TK_EMBED);
     const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -100,10 +103,13 @@ int launch_embed(const void *embd, int type, int n_vocab, const int *tokens,
 // eps) with a double accumulator.  One CTA per token, one warp per block.
 __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restrict__ x,
                                                             const float *__restrict__ w,
-                                                            int8_t *xq, float *xd, int16_t *xs) {
+                                                            int8_t *xq, float *xd, int16_t *xs,
+                                                            Prefetch pf) {
+    QMA_TRACE_SCOPE(TK_RMSNORM);
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ double red[8];
     pdl_trigger();
+    if (t == 0 && tid < Prefetch::N && pf.p[tid]) prefetch_l2_range(pf.p[tid], pf.bytes[tid]);
     pdl_wait();
     const float4 *p = reinterpret_cast<const float4 *>(x + size_t(t) * EMBD + tid * 8);
     const float4 a = p[0], b = p[1];
@@ -127,12 +133,12 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
 }
 
 int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *xq, float *xd,
-                         int16_t *xs, cudaStream_t st) {
+                         int16_t *xs, cudaStream_t st, const Prefetch &pf) {
     if (n != EMBD) {
         set_error("rmsnorm_quant: n %d != %d", n, EMBD);
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
-    QMA_CHECK_CUDA(launch_ex(rmsnorm_quant_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), x, w, xq, xd, xs));
+    QMA_CHECK_CUDA(launch_ex(rmsnorm_quant_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), x, w, xq, xd, xs, pf));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -144,6 +150,7 @@ int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *x
 __global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ qkv, int ld,
                                                      const float *__restrict__ w, float *state,
                                                      int T, float *out) {
+    QMA_TRACE_SCOPE(TK_CONV);
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -187,6 +194,7 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
                                                   const float *__restrict__ dt,
                                                   const float *__restrict__ av, float *ssm, int T,
                                                   float *o) {
+    QMA_TRACE_SCOPE(TK_GDN);
     const int rb = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qh = h % KHEADS;
@@ -278,6 +286,7 @@ __global__ void __launch_bounds__(1024) gated_norm_quant_kernel(const float *__r
                                                                 int z_ld,
                                                                 const float *__restrict__ w,
                                                                 int8_t *xq, float *xd, int16_t *xs) {
+    QMA_TRACE_SCOPE(TK_GATED_NORM);
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     __shared__ __align__(16) float y[VAL_DIM];
     pdl_trigger();

@@ -208,30 +208,43 @@ __device__ __forceinline__ void router_logit(const float4 (&wv)[16], const float
 
 // Leader-side ranking of the 256 logits (256 threads, thread = expert):
 // top9[r] = the expert of rank r < 9 under (S descending, id ascending),
-// ranked on S rounded to fp32 (fast compares).  Two logits that fp32
-// rounding could tie or misorder are within one fp32 ulp of each other, far
-// inside the margin top_settled() demands between ranks, so such a ranking
-// is never accepted.  dred[0] receives the largest S + B among the
-// unselected (rank >= 8).
-__device__ __forceinline__ void rank_top(const double *sS, const double *sB, float *sf, int tid,
-                                         int lane, int warp, double *dred, int *top9) {
-    const double Se = sS[tid];
-    const float fe = float(Se);
-    sf[tid] = fe;
+// ranked on S rounded to fp32.  Two logits that fp32 rounding could tie or
+// misorder are within one fp32 ulp of each other, far inside the margin
+// top_settled() demands between ranks, so such a ranking is never accepted.
+// Each warp sorts its 32 keys (sortable fp32 bits, then inverted id) with a
+// bitonic network in registers; the 8 warps' top 9 are ranked by counting.
+// dred[0] receives the largest S + B among the unselected (rank >= 8).
+__device__ __forceinline__ unsigned long long rank_key(double S, int e) {
+    uint32_t u = __float_as_uint(float(S));
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - uint32_t(e));
+}
+__device__ __forceinline__ void rank_top(const double *sS, const double *sB, unsigned long long *cand,
+                                         int tid, int lane, int warp, double *dred, int *top9) {
+    unsigned long long key = rank_key(sS[tid], tid);
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, j);
+            const bool desc = (lane & k) == 0 || k == 32;
+            const bool low = (lane & j) == 0;
+            key = (low == desc) ? (key > o ? key : o) : (key < o ? key : o);
+        }
+    if (lane <= MOE_TOPK) cand[warp * (MOE_TOPK + 1) + lane] = key;
     __syncthreads();
-    int r = 0;
-    const float4 *f4 = reinterpret_cast<const float4 *>(sf);
-#pragma unroll 4
-    for (int j4 = 0; j4 < MOE_NEXP / 4; j4++) {
-        const float4 v = f4[j4];
-        const int j = 4 * j4;
-        r += (v.x > fe) || (v.x == fe && j + 0 < tid);
-        r += (v.y > fe) || (v.y == fe && j + 1 < tid);
-        r += (v.z > fe) || (v.z == fe && j + 2 < tid);
-        r += (v.w > fe) || (v.w == fe && j + 3 < tid);
+    if (tid < 8 * (MOE_TOPK + 1)) {
+        const unsigned long long me = cand[tid];
+        int r = 0;
+        for (int j = 0; j < 8 * (MOE_TOPK + 1); j++) r += cand[j] > me;
+        if (r <= MOE_TOPK) top9[r] = int(0xffffffffu - uint32_t(me & 0xffffffffu));
     }
-    if (r <= MOE_TOPK) top9[r] = tid;
-    double u = r >= MOE_TOPK ? Se + sB[tid] : -INFINITY;
+    __syncthreads();
+    // best S + B among the unselected: everything but top9[0..7]
+    bool sel = false;
+#pragma unroll
+    for (int k = 0; k < MOE_TOPK; k++) sel |= top9[k] == tid;
+    double u = sel ? -INFINITY : sS[tid] + sB[tid];
     u = warp_max_d(u);
     if (lane == 0) dred[warp] = u;      // dred's rms sums were consumed before the cluster barrier
     __syncthreads();
@@ -281,6 +294,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
                                                          const float *__restrict__ gis,
                                                          MoeScratch s, int *sel_out,
                                                          float *w_out) {
+    QMA_TRACE_SCOPE(TK_ROUTER);
     const unsigned rank = cluster_rank();
     const int t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -292,7 +306,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
     __shared__ int cls[MOE_NEXP];
     __shared__ int top9[MOE_TOPK + 1];
     __shared__ int cand[MOE_NEXP];
-    __shared__ __align__(16) float sf[MOE_NEXP];
+    __shared__ unsigned long long rcand[8 * (MOE_TOPK + 1)];
 
     // the two router rows of this warp: independent of the upstream kernel
     const int e0 = int(rank) * (MOE_NEXP / RCL) + warp * 2;
@@ -366,7 +380,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
     // lowest id) whenever the 8th expert's probability is a normal float
     // (class 2: the classes below only ever hold lower logits) and every
     // decision is settled by the bounds; otherwise the exact path below runs.
-    rank_top(sS, sB, sf, tid, lane, warp, dred, top9);
+    rank_top(sS, sB, rcand, tid, lane, warp, dred, top9);
     if (tid == 0) {
         need_exact = !top_settled(sS, sB, top9, dred);
         ncand = 0;
@@ -465,13 +479,57 @@ template <> struct DownPtr<FmtQ4K> {
 // One cluster of XCL CTAs per (slot, token): grid (9 x XCL, T); slots 0..7
 // are the routed experts in selection order, slot 8 the shared expert
 // (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  CTA
-// `rank` computes gate/up rows rank*XGU.. (one warp per 4 row pairs,
-// SwiGLU), the cluster exchanges the 512-wide hidden vector through
-// distributed shared memory, every CTA quantizes it to Q8_K and computes
-// down rows rank*XDN..; the last of the 9 slot CTAs of a row chunk combines
-// the slots in the reference's order and adds the residual (nn.c:615-629,
-// nn.c:2246-2252).  The shared expert's weights, and the routed experts'
-// down rows as soon as the selection is known, are prefetched into L2.
+// `rank` owns gate/up rows rank*XGU.. and down rows rank*XDN..:
+//   1. its 32 gate and 32 up rows (74 KB) are copied into shared memory by
+//      the TMA engine as soon as the expert is known (the shared expert's
+//      before the router has finished), its down rows prefetched into L2;
+//   2. one warp per 4 row pairs computes silu(gate) * up;
+//   3. the cluster gathers the 512-wide hidden vector through distributed
+//      shared memory while the down rows are copied into the freed buffer;
+//   4. every CTA quantizes the hidden vector to Q8_K and computes its down
+//      rows; the last of the 9 slot CTAs of a row chunk combines the slots
+//      in the reference's order and adds the residual (nn.c:615-629,
+//      nn.c:2246-2252).
+// Every wait on a copy is bounded; a copy that never lands is counted in
+// g_moe_timeouts (the host fails the call) and the CTA still takes part in
+// the cluster barriers so that no peer waits forever.
+__device__ unsigned g_moe_timeouts;
+
+template <class F> struct DownBytes;
+template <> struct DownBytes<FmtQ6K> {
+    static constexpr uint32_t QL = XDN * (MOE_FF / 2), QH = XDN * (MOE_FF / 4), SC = XDN * (MOE_FF / 16),
+                              D = XDN * (MOE_FF / 256) * 2, ALL = QL + QH + SC + D;
+    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar) {
+        const Q6Planes P = shift_rows(DownPtr<FmtQ6K>::at(expert), d0, MOE_FF);
+        mbar_expect_tx(bar, ALL);
+        bulk_g2s(dst, P.ql, QL, bar);
+        bulk_g2s(dst + QL, P.qh, QH, bar);
+        bulk_g2s(dst + QL + QH, P.sc, SC, bar);
+        bulk_g2s(dst + QL + QH + SC, P.d, D, bar);
+    }
+    __device__ static Q6Planes at(const uint8_t *dst) {
+        Q6Planes P;
+        P.ql = dst;
+        P.qh = dst + QL;
+        P.sc = reinterpret_cast<const int8_t *>(dst + QL + QH);
+        P.d = reinterpret_cast<const __half *>(dst + QL + QH + SC);
+        return P;
+    }
+};
+template <> struct DownBytes<FmtQ4K> {
+    static constexpr uint32_t ALL = XDN * (MOE_FF / 256) * Q4K_BYTES;
+    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar) {
+        mbar_expect_tx(bar, ALL);
+        bulk_g2s(dst, shift_rows(expert, d0, MOE_FF), ALL, bar);
+    }
+    __device__ static const uint8_t *at(const uint8_t *dst) { return dst; }
+};
+constexpr uint32_t XROW = uint32_t(MOE_EMBD / 256) * Q4K_BYTES;     // one gate/up row
+constexpr uint32_t XGU_BYTES = XGU * XROW;                          // 32 rows
+constexpr size_t EXPERT_SMEM = 2 * size_t(XGU_BYTES);
+static_assert(DownBytes<FmtQ6K>::ALL <= EXPERT_SMEM && DownBytes<FmtQ4K>::ALL <= EXPERT_SMEM,
+              "down rows reuse the gate/up buffer");
+
 template <class F>
 __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
                                                          const uint8_t *__restrict__ up_exps,
@@ -482,12 +540,14 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
                                                          const uint8_t *__restrict__ down_sh,
                                                          const float *x2, float *x_out,
                                                          MoeScratch s) {
+    QMA_TRACE_SCOPE(TK_EXPERT);
+    extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
     const int slot = blockIdx.x / XCL, t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr size_t ROW = size_t(MOE_EMBD / 256) * Q4K_BYTES;
-    constexpr size_t GU_BYTES = size_t(MOE_FF) * ROW;
+    constexpr size_t GU_BYTES = size_t(MOE_FF) * XROW;
     constexpr int LPR = MOE_FF / F::UNIT;
+    __shared__ __align__(8) uint64_t bar[2];
     __shared__ float hpart[XGU];
     __shared__ __align__(16) float hfull[MOE_FF];
     __shared__ __align__(16) int8_t hq[MOE_FF];
@@ -495,40 +555,54 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
     __shared__ int16_t hs[MOE_FF / 16];
     __shared__ int is_last;
     const int g0 = int(rank) * XGU, d0 = int(rank) * XDN;
-    const uint8_t *G = gate_sh, *U = up_sh, *Db = down_sh;
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const uint8_t *Db = down_sh;
     if (slot == MOE_TOPK && tid == 0) {
-        prefetch_l2(G + g0 * ROW, XGU * ROW);
-        prefetch_l2(U + g0 * ROW, XGU * ROW);
+        mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
+        bulk_g2s(xbuf, gate_sh + g0 * XROW, XGU_BYTES, &bar[0]);
+        bulk_g2s(xbuf + XGU_BYTES, up_sh + g0 * XROW, XGU_BYTES, &bar[0]);
         prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
     }
     pdl_trigger();
     pdl_wait();
     if (slot < MOE_TOPK) {
         const int e = __ldcg(&s.sel[t * MOE_TOPK + slot]);
-        G = gate_exps + size_t(e) * GU_BYTES;
-        U = up_exps + size_t(e) * GU_BYTES;
         Db = down_exps + size_t(e) * down_bytes;
-        if (tid == 0) prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+        if (tid == 0) {
+            mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
+            bulk_g2s(xbuf, gate_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0]);
+            bulk_g2s(xbuf + XGU_BYTES, up_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0]);
+            prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+        }
     }
-    // ---- gate / up rows g0 + 4 warp .. + 3 -----------------------------------
+    // ---- gate / up rows g0 + 4 warp .. + 3 from shared memory ---------------
+    const bool gu_ok = mbar_wait(&bar[0], 0);
     {
         FmtQ4K::Act act;
         FmtQ4K::load_act(act, s.xq + size_t(t) * MOE_EMBD, s.xd + size_t(t) * 8,
                          s.xs + size_t(t) * 128, lane);
         constexpr int RPWARP = XGU / 8;
-        const int r0 = g0 + warp * RPWARP;
-        FmtQ4K::Wt wg[RPWARP], wu[RPWARP];
 #pragma unroll
         for (int k = 0; k < RPWARP; k++) {
-            FmtQ4K::load_w(wg[k], G, r0 + k, MOE_EMBD, lane);
-            FmtQ4K::load_w(wu[k], U, r0 + k, MOE_EMBD, lane);
+            const int r = warp * RPWARP + k;
+            FmtQ4K::Wt wg, wu;
+            FmtQ4K::load_w_smem(wg, xbuf, r, MOE_EMBD, lane);
+            FmtQ4K::load_w_smem(wu, xbuf + XGU_BYTES, r, MOE_EMBD, lane);
+            const float g = warp_sum(FmtQ4K::dot(wg, act, lane));
+            const float u = warp_sum(FmtQ4K::dot(wu, act, lane));
+            if (lane == 0) hpart[r] = gu_ok ? (g / (1.0f + expf(-g))) * u : 0.0f;
         }
-#pragma unroll
-        for (int k = 0; k < RPWARP; k++) {
-            const float g = warp_sum(FmtQ4K::dot(wg[k], act, lane));
-            const float u = warp_sum(FmtQ4K::dot(wu[k], act, lane));
-            if (lane == 0) hpart[warp * RPWARP + k] = (g / (1.0f + expf(-g))) * u;
-        }
+    }
+    __syncthreads();                    // gate/up rows consumed: reuse the buffer
+    if (tid == 0) {
+        if (!gu_ok) atomicAdd(&g_moe_timeouts, 1u);
+        fence_proxy_async_smem();
+        DownBytes<F>::issue(xbuf, Db, d0, &bar[1]);
     }
     // ---- the cluster's 512 hidden values ------------------------------------
     cluster_sync();
@@ -542,10 +616,17 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
         q8k_block_warp(v, lane, hq + warp * 256, hd + warp, hs + warp * 16);
     }
     __syncthreads();
-    // ---- down rows d0 .. d0 + XDN ---------------------------------------------
-    const auto P = shift_rows(DownPtr<F>::at(Db), d0, MOE_FF);
+    // ---- down rows d0 .. d0 + XDN from shared memory --------------------------
+    const bool dn_ok = mbar_wait(&bar[1], 0);
     float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + d0;
-    gemv_warp_rows<F, 1, LPR, 1, 1>(P, MOE_FF, XDN, hq, hd, hs, part, 0, warp, 8, lane);
+    if (dn_ok) {
+        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 1>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
+                                                  warp, 8, lane);
+    } else {
+        if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
+        if (tid < XDN) part[tid] = 0.0f;
+        mbar_wait(&bar[1], 0);          // let a late copy land before the CTA exits
+    }
 
     // ---- the last of the 9 slot CTAs of this row chunk combines --------------
     __syncthreads();
@@ -574,6 +655,16 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
     cluster_wait();                // no CTA leaves while a peer may read it
 }
 
+int moe_wait_timeouts() {
+    unsigned n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_moe_timeouts, sizeof(n)) != cudaSuccess) return -1;
+    if (n) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(g_moe_timeouts, &zero, sizeof(zero));
+    }
+    return int(n);
+}
+
 static bool g_moe_attrs = false;
 
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
@@ -583,6 +674,8 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
         g_moe_attrs = true;
     }
     if (clear_counters)
@@ -596,10 +689,10 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *gsh = static_cast<const uint8_t *>(w.gate_shexp), *ush = static_cast<const uint8_t *>(w.up_shexp);
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
-        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(256), 0, st, XCL, pdl_enabled(), ge, ue,
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(256), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
                                  gsh, ush, de, eb, dsh, x2, x_out, s));
     else
-        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(256), 0, st, XCL, pdl_enabled(), ge, ue,
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(256), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
                                  gsh, ush, de, eb, dsh, x2, x_out, s));
     return QMA_CUDA_OK;
 }

@@ -40,5 +40,8 @@ MoeScratch moe_scratch_layout(void *base, int T);
 // launch.
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
               float *wts, void *scratch, cudaStream_t st, bool clear_counters);
+// Bounded waits of the expert kernel that ran out since the last call (reset
+// by reading); -1 if the counter cannot be read.
+int moe_wait_timeouts();
 
 }  // namespace qma
