@@ -133,6 +133,32 @@ __device__ __forceinline__ int warp_sum_i(int v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+// Eight warp-wide sums at once (9 shuffles): afterwards lane l holds the sum
+// over the warp of v[warp_sum8_index(l)].
+__device__ __forceinline__ int warp_sum8_index(int lane) {
+    return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+}
+__device__ __forceinline__ float warp_sum8(const float (&v)[8], int lane) {
+    float a[4];
+    const bool h16 = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float mine = h16 ? v[4 + i] : v[i], other = h16 ? v[i] : v[4 + i];
+        a[i] = mine + __shfl_xor_sync(0xffffffffu, other, 16);
+    }
+    float b[2];
+    const bool h8 = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float mine = h8 ? a[2 + i] : a[i], other = h8 ? a[i] : a[2 + i];
+        b[i] = mine + __shfl_xor_sync(0xffffffffu, other, 8);
+    }
+    const bool h4 = lane & 4;
+    float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
+}
 // Sum over aligned groups of `width` lanes (width a power of two <= 32).
 __device__ __forceinline__ float group_sum(float v, int width) {
     for (int o = width >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -191,6 +217,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
+}
+// A large range as many 4 KB bulk copies issued by the 32 lanes of a warp
+// (the mbarrier's byte count must already be armed): the TMA engine keeps
+// several copies in flight, a single large one streams slowly.
+constexpr uint32_t BULK_PIECE = 4096;
+__device__ __forceinline__ void bulk_g2s_warp(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                              int lane) {
+    uint8_t *d = static_cast<uint8_t *>(dst);
+    const uint8_t *s = static_cast<const uint8_t *>(src);
+    for (uint32_t off = uint32_t(lane) * BULK_PIECE; off < bytes; off += 32 * BULK_PIECE)
+        bulk_g2s(d + off, s + off, bytes - off < BULK_PIECE ? bytes - off : BULK_PIECE, bar);
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
@@ -320,8 +357,20 @@ struct TraceScope {
     }
 };
 #define QMA_TRACE_SCOPE(k) ::qma::TraceScope qma_trace_scope_(k)
+// a point event `phase` of kernel k, recorded by thread 0 of the first CTA
+__device__ __forceinline__ void trace_mark(uint32_t k, uint32_t phase) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
+        const unsigned i = atomicAdd(&g_trace_n, 1u) % TRACE_CAP;
+        const unsigned long long t = gtimer();
+        g_trace[i][0] = (static_cast<unsigned long long>(k | 0x80u) << 56) |
+                        (static_cast<unsigned long long>(phase) << 32) | (t & 0xffffffffull);
+        g_trace[i][1] = t;
+    }
+}
+#define QMA_TRACE_MARK(k, phase) ::qma::trace_mark(k, phase)
 #else
 #define QMA_TRACE_SCOPE(k) do {} while (0)
+#define QMA_TRACE_MARK(k, phase) do {} while (0)
 #endif
 
 // 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,

@@ -1,5 +1,7 @@
 // gemv.cu -- standalone Q8_K quantization and quantized GEMV entry points
 // (qma_cuda_q8k_quant, qma_cuda_matvec, qma_cuda_dot_partials).
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemv.cuh"
 #include "quant.cuh"
@@ -24,8 +26,13 @@ __global__ void __launch_bounds__(256) q8k_quant_kernel(const float *__restrict_
 }
 
 // ---------------------------------------------------------------- GEMV ----
+// Single-token Q4_K projections: 3 CTAs per SM, so that one sweep of the
+// one-wave grid (4 rows per warp) covers the decode in-projections.
+template <class F, int T, int UPL>
+constexpr int gemv_min_blocks() { return std::is_same<F, FmtQ4K>::value && T == 1 && UPL == 1 ? 3 : 1; }
+
 template <class F, int T, int LPR, int UPL, int RU>
-__global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, int n_out,
+__global__ void __launch_bounds__(256, gemv_min_blocks<F, T, UPL>()) gemv_kernel(typename F::Ptr W, int n_in, int n_out,
                                                    const int8_t *xq, const float *xd,
                                                    const int16_t *xsum, float *out, int out_ld,
                                                    const float *resid) {
@@ -35,15 +42,125 @@ __global__ void __launch_bounds__(256) gemv_kernel(typename F::Ptr W, int n_in, 
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     pdl_trigger();
     if (threadIdx.x == 0) {
-        // this CTA's rows (8 consecutive warp row groups per sweep): into L2
-        // while the upstream kernel finishes
+        // this CTA's rows after the first sweep (8 consecutive warp row
+        // groups per sweep; the first sweep is loaded into registers before
+        // the wait): into L2 while the upstream kernel finishes
         constexpr int RG = (32 / LPR) * RU;
-        for (int r0 = blockIdx.x * 8 * RG; r0 < n_out; r0 += nwarps * RG)
+        for (int r0 = blockIdx.x * 8 * RG + nwarps * RG; r0 < n_out; r0 += nwarps * RG)
             F::prefetch_rows(W, r0, min(8 * RG, n_out - r0), n_in);
     }
+    gemv_warp_rows<F, T, LPR, UPL, RU, true>(W, n_in, n_out, xq, xd, xsum, out, out_ld, warp, nwarps,
+                                             lane, resid);
+}
+
+// Single-token GEMV over a row block per CTA staged whole in shared memory:
+// the bulk copy is issued at launch, before waiting on the upstream kernel
+// (whose output is the activation), so the weight transfer overlaps it;
+// after the wait only the activation load and the dot products remain.
+__device__ unsigned g_gemv_timeouts;
+
+// Rows of a 32-lanes-per-row matrix (n_in >= 2048): each warp takes an
+// equal share of the CTA's rows, in batches of up to 8 independent dot
+// products followed by one 8-way warp reduction.
+template <class F, int UPL>
+__device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in, int nr, const int8_t *xq,
+                                              const float *xd, const int16_t *xsum, float *out,
+                                              const float *resid, int warp, int nwarps, int lane) {
+    typename F::Act act[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; k++) F::load_act(act[k], xq, xd, xsum, lane + 32 * k);
+    const int idx = warp_sum8_index(lane);
+    // the CTA's rows spread evenly over its warps, in batches of up to 8
+    const int rpw = (nr + nwarps - 1) / nwarps;
+    const int r_end = min(nr, (warp + 1) * rpw);
+    for (int rb = warp * rpw; rb < r_end; rb += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            v[j] = 0.0f;
+            if (rb + j < r_end) {
+#pragma unroll
+                for (int k = 0; k < UPL; k++) {
+                    typename F::Wt w;
+                    F::load_w_smem(w, P, rb + j, n_in, lane + 32 * k);
+                    v[j] += F::dot(w, act[k], lane + 32 * k);
+                }
+            }
+        }
+        const float tot = warp_sum8(v, lane);
+        const int r = rb + idx;
+        if ((lane & 3) == 0 && r < r_end) out[r] = resid ? __fadd_rn(tot, resid[r]) : tot;
+    }
+}
+
+template <class F, int LPR, int UPL, int RU>
+__global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int n_in, int n_out,
+                                                          int rows_cta, const int8_t *xq,
+                                                          const float *xd, const int16_t *xsum,
+                                                          float *out, const float *resid) {
+    QMA_TRACE_SCOPE(TK_GEMV);
+    extern __shared__ __align__(128) uint8_t wbuf[];
+    __shared__ __align__(8) uint64_t bar;
+    const int r0 = blockIdx.x * rows_cta;
+    const int nr = min(rows_cta, n_out - r0);
+    if (threadIdx.x < 32 && nr > 0) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            mbar_fence_init();
+        }
+        __syncwarp();
+        Stage<F>::issue(W, r0, nr, n_in, wbuf, &bar, threadIdx.x);
+    }
+    __syncthreads();
+    pdl_trigger();
     pdl_wait();
-    gemv_warp_rows<F, T, LPR, UPL, RU>(W, n_in, n_out, xq, xd, xsum, out, out_ld, warp, nwarps,
-                                       lane, resid);
+    if (nr <= 0) return;
+    if (!mbar_wait(&bar, 0)) {
+        if (threadIdx.x == 0) atomicAdd(&g_gemv_timeouts, 1u);
+        mbar_wait(&bar, 0);     // let a late copy land before the CTA exits
+        return;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const auto P = Stage<F>::view(wbuf, nr, n_in);
+    if constexpr (LPR == 32)
+        staged_rows32<F, UPL>(P, n_in, nr, xq, xd, xsum, out + r0, resid ? resid + r0 : nullptr, warp, nwarps,
+                              lane);
+    else
+        gemv_warp_rows<SmemRows<F>, 1, LPR, UPL, RU>(P, n_in, nr, xq, xd, xsum, out + r0, 0, warp, nwarps,
+                                                     lane, resid ? resid + r0 : nullptr);
+}
+
+int gemv_wait_timeouts() {
+    unsigned n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_gemv_timeouts, sizeof(n)) != cudaSuccess) return -1;
+    if (n) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(g_gemv_timeouts, &zero, sizeof(zero));
+    }
+    return int(n);
+}
+
+constexpr uint32_t STAGED_MAX = 160 * 1024;    // shared memory per CTA for a staged GEMV
+
+template <class F, int LPR, int UPL, int RU>
+static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
+                         const float *xd, const int16_t *xsum, float *out, const float *resid,
+                         int rows_cta, uint32_t smem, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_staged_kernel<F, LPR, UPL, RU>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(STAGED_MAX)));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_staged_kernel<F, LPR, UPL, RU>,
+                                            cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        attr = true;
+    }
+    const int grid = (n_out + rows_cta - 1) / rows_cta;
+    // small row blocks (the output projections) take 8 warps, leaving room on
+    // the SM for the next kernel's CTAs (the router) to start early
+    const unsigned threads = rows_cta <= 64 ? 256 : 512;
+    QMA_CHECK_CUDA(launch_ex(gemv_staged_kernel<F, LPR, UPL, RU>, dim3(unsigned(grid)), dim3(threads), smem, st, 1,
+                             pdl_enabled(), W, n_in, n_out, rows_cta, xq, xd, xsum, out, resid));
+    return QMA_CUDA_OK;
 }
 
 static int g_num_sms = 0;
@@ -80,8 +197,9 @@ static int launch_gemv(const typename F::Ptr &W, int n_in, int n_out, const int8
 }
 
 // Shape dispatch: units per row U = n_in / F::UNIT.  Single-token passes
-// keep two row groups of loads in flight per warp.
-template <class F, int T, int RU = (T == 1 ? 2 : 1)>
+// keep four row groups of loads in flight per warp (so that one sweep of a
+// one-wave grid covers the decode projections).
+template <class F, int T, int RU = (T == 1 ? 4 : 1)>
 static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
                           const float *xd, const int16_t *xsum, float *out, int out_ld,
                           const float *resid, cudaStream_t st) {
@@ -99,10 +217,33 @@ static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const i
     }
 }
 
+// Single-token launch with each CTA's rows staged in shared memory when the
+// matrix spread over one CTA per SM fits (the decode projections); false
+// when it does not (the LM head streams through the register GEMV).
+template <class F>
+static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq, const float *xd,
+                       const int16_t *xsum, float *out, const float *resid, cudaStream_t st, int &rc) {
+    int rows_cta = (n_out + num_sms() - 1) / num_sms();
+    rows_cta = (rows_cta + 7) & ~7;
+    const uint32_t smem = Stage<F>::bytes(rows_cta, n_in);
+    if (smem > STAGED_MAX) return false;
+    const int U = n_in / F::UNIT;
+    switch (U) {
+    case 4: rc = launch_staged<F, 4, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    case 8: rc = launch_staged<F, 8, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    case 16: rc = launch_staged<F, 16, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    case 32: rc = launch_staged<F, 32, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    case 64: rc = launch_staged<F, 32, 2, 1>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    default: return false;
+    }
+}
+
 template <class F, int TMAX>
 static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, const int8_t *xq,
                        const float *xd, const int16_t *xsum, float *out, const float *resid,
                        cudaStream_t st) {
+    int rc;
+    if (T == 1 && pdl_enabled() && try_staged<F>(W, n_in, n_out, xq, xd, xsum, out, resid, st, rc)) return rc;
     int t0 = 0;
     while (t0 < T) {
         const int rem = T - t0;

@@ -204,6 +204,11 @@ struct FmtQ80 {
         w.q3 = ld_stream16(q + 48);
         w.d2 = ld_stream4(P.d + size_t(row) * (n_in / 32) + u * 2);
     }
+    __device__ static void load_w_smem(Wt &w, const Ptr &P, int row, int n_in, int u) {
+        const uint4 *q = reinterpret_cast<const uint4 *>(P.q + size_t(row) * n_in + u * 64);
+        w.q0 = q[0]; w.q1 = q[1]; w.q2 = q[2]; w.q3 = q[3];
+        w.d2 = *reinterpret_cast<const uint32_t *>(P.d + size_t(row) * (n_in / 32) + u * 2);
+    }
     __device__ static void isums(const Wt &w, const Act &a, int &i0, int &i1) {
         const uint32_t q[16] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w,
                                 w.q2.x, w.q2.y, w.q2.z, w.q2.w, w.q3.x, w.q3.y, w.q3.z, w.q3.w};
@@ -224,6 +229,67 @@ struct FmtQ80 {
     }
 };
 
+// Staging of rows [r0, r0 + nr) of a matrix into shared memory by the TMA
+// engine (one bulk copy per plane), and the view of that copy as a matrix
+// of nr rows.  Plane copies start 16-byte aligned (r0 a multiple of 8) and
+// are rounded up to 16 bytes, which stays inside the packed matrix (every
+// plane is padded to 16 bytes).
+__host__ __device__ constexpr uint32_t up16(uint32_t x) { return (x + 15u) & ~15u; }
+template <class F> struct Stage;
+template <> struct Stage<FmtQ4K> {
+    __host__ __device__ static uint32_t bytes(int nr, int n) { return up16(uint32_t(nr) * (n / 256) * 144); }
+    __device__ static void issue(const uint8_t *W, int r0, int nr, int n, uint8_t *dst, uint64_t *bar, int lane) {
+        const uint32_t b = bytes(nr, n);
+        if (lane == 0) mbar_expect_tx(bar, b);
+        __syncwarp();
+        bulk_g2s_warp(dst, W + size_t(r0) * (n / 256) * 144, b, bar, lane);
+    }
+    __device__ static const uint8_t *view(const uint8_t *dst, int, int) { return dst; }
+};
+template <> struct Stage<FmtQ6K> {
+    __host__ __device__ static uint32_t ql(int nr, int n) { return up16(uint32_t(nr) * (n / 2)); }
+    __host__ __device__ static uint32_t qh(int nr, int n) { return up16(uint32_t(nr) * (n / 4)); }
+    __host__ __device__ static uint32_t sc(int nr, int n) { return up16(uint32_t(nr) * (n / 16)); }
+    __host__ __device__ static uint32_t d(int nr, int n) { return up16(uint32_t(nr) * (n / 256) * 2); }
+    __host__ __device__ static uint32_t bytes(int nr, int n) { return ql(nr, n) + qh(nr, n) + sc(nr, n) + d(nr, n); }
+    __device__ static void issue(const Q6Planes &P, int r0, int nr, int n, uint8_t *dst, uint64_t *bar, int lane) {
+        if (lane == 0) mbar_expect_tx(bar, bytes(nr, n));
+        __syncwarp();
+        bulk_g2s_warp(dst, P.ql + size_t(r0) * (n / 2), ql(nr, n), bar, lane);
+        dst += ql(nr, n);
+        bulk_g2s_warp(dst, P.qh + size_t(r0) * (n / 4), qh(nr, n), bar, lane);
+        dst += qh(nr, n);
+        bulk_g2s_warp(dst, P.sc + size_t(r0) * (n / 16), sc(nr, n), bar, lane);
+        dst += sc(nr, n);
+        bulk_g2s_warp(dst, P.d + size_t(r0) * (n / 256), d(nr, n), bar, lane);
+    }
+    __device__ static Q6Planes view(const uint8_t *dst, int nr, int n) {
+        Q6Planes P;
+        P.ql = dst;
+        P.qh = dst + ql(nr, n);
+        P.sc = reinterpret_cast<const int8_t *>(P.qh + qh(nr, n));
+        P.d = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(P.sc) + sc(nr, n));
+        return P;
+    }
+};
+template <> struct Stage<FmtQ80> {
+    __host__ __device__ static uint32_t q(int nr, int n) { return up16(uint32_t(nr) * n); }
+    __host__ __device__ static uint32_t d(int nr, int n) { return up16(uint32_t(nr) * (n / 32) * 2); }
+    __host__ __device__ static uint32_t bytes(int nr, int n) { return q(nr, n) + d(nr, n); }
+    __device__ static void issue(const Q8Planes &P, int r0, int nr, int n, uint8_t *dst, uint64_t *bar, int lane) {
+        if (lane == 0) mbar_expect_tx(bar, bytes(nr, n));
+        __syncwarp();
+        bulk_g2s_warp(dst, P.q + size_t(r0) * n, q(nr, n), bar, lane);
+        bulk_g2s_warp(dst + q(nr, n), P.d + size_t(r0) * (n / 32), d(nr, n), bar, lane);
+    }
+    __device__ static Q8Planes view(const uint8_t *dst, int nr, int n) {
+        Q8Planes P;
+        P.q = reinterpret_cast<const int8_t *>(dst);
+        P.d = reinterpret_cast<const __half *>(dst + q(nr, n));
+        return P;
+    }
+};
+
 // A format whose weights are read from a copy in shared memory.
 template <class F> struct SmemRows : F {
     __device__ static void load_w(typename F::Wt &w, const typename F::Ptr &W, int row, int n_in, int u) {
@@ -236,8 +302,11 @@ template <class F> struct SmemRows : F {
 // than 32 units, else 32); each lane owns UPL units of the row; T tokens
 // are processed per pass with their activation slices in registers.  A warp
 // issues the loads of RU row groups before computing any of them, so every
-// lane keeps RU*UPL units of weights in flight.
-template <class F, int T, int LPR, int UPL, int RU>
+// lane keeps RU*UPL units of weights in flight.  With PRE, the first sweep's
+// weights are loaded before pdl_wait(): a launch sized so that one sweep
+// covers the matrix has all its weights in registers by the time the
+// upstream kernel's activations are ready.
+template <class F, int T, int LPR, int UPL, int RU, bool PRE = false>
 __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_in, int n_out,
                                                const int8_t *xq, const float *xd,
                                                const int16_t *xsum, float *out, int out_ld,
@@ -245,15 +314,8 @@ __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_i
                                                const float *resid = nullptr) {
     constexpr int RPW = 32 / LPR;
     const int lir = lane % LPR, slot = lane / LPR;
-    typename F::Act act[UPL][T];
-#pragma unroll
-    for (int k = 0; k < UPL; k++)
-#pragma unroll
-        for (int t = 0; t < T; t++)
-            F::load_act(act[k][t], xq + size_t(t) * n_in, xd + size_t(t) * (n_in / 256),
-                        xsum + size_t(t) * (n_in / 16), lir + k * LPR);
-    for (int rb = warp * RPW * RU; rb < n_out; rb += nwarps * RPW * RU) {
-        typename F::Wt w[RU][UPL];
+    typename F::Wt w[RU][UPL];
+    auto load_rows = [&](int rb) {
 #pragma unroll
         for (int ru = 0; ru < RU; ru++) {
             const int r = rb + ru * RPW + slot;
@@ -262,6 +324,21 @@ __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_i
                 for (int k = 0; k < UPL; k++) F::load_w(w[ru][k], W, r, n_in, lir + k * LPR);
             }
         }
+    };
+    const int rb0 = warp * RPW * RU;
+    if (PRE) {
+        load_rows(rb0);
+        pdl_wait();
+    }
+    typename F::Act act[UPL][T];
+#pragma unroll
+    for (int k = 0; k < UPL; k++)
+#pragma unroll
+        for (int t = 0; t < T; t++)
+            F::load_act(act[k][t], xq + size_t(t) * n_in, xd + size_t(t) * (n_in / 256),
+                        xsum + size_t(t) * (n_in / 16), lir + k * LPR);
+    for (int rb = rb0; rb < n_out; rb += nwarps * RPW * RU) {
+        if (!PRE || rb != rb0) load_rows(rb);
 #pragma unroll
         for (int ru = 0; ru < RU; ru++) {
             const int r = rb + ru * RPW + slot;
@@ -293,5 +370,7 @@ int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *x
            const float *xd, const int16_t *xsum, float *out, cudaStream_t st,
            const float *resid = nullptr);
 int num_sms();
+// Bounded waits of the staged GEMV that ran out since the last call.
+int gemv_wait_timeouts();
 
 }  // namespace qma

@@ -68,6 +68,9 @@ MoeScratch moe_scratch_layout(void *base, int T) {
     return s;
 }
 
+// Bounded waits of the MoE kernels that ran out (read and reset by the host).
+__device__ unsigned g_moe_timeouts;
+
 // --------------------------------------------------------------- helpers --
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -80,10 +83,9 @@ __device__ __forceinline__ double warp_max_d(double v) {
     return v;
 }
 
-// xn lives in shared memory in chunks of 64 floats padded to 68, so a lane
-// reading its own contiguous 64 elements with 16-byte loads is bank-conflict
-// free.
-__device__ __forceinline__ int xn_idx(int i) { return (i >> 6) * 68 + (i & 63); }
+// xn lives in shared memory in natural order (lanes read 16-byte words at
+// consecutive addresses).
+__device__ __forceinline__ int xn_idx(int i) { return i; }
 
 // The reference ranks experts by probability p = expf(l - max) / sum and
 // breaks ties to the lower expert id (repeated argmax with '>', nn.c:528-533).
@@ -166,43 +168,67 @@ __device__ bool select_top8(const double *sS, const double *sB, const int *cls, 
 }
 
 // Exact logit S (fp64 sum of the fp32 products) and a bound B on the
-// reference's sequential fp32 sum, for the router row a warp holds (lane:
-// weights 64 l .. 64 l + 63).  The reference sums s += g_i * x_i in fp32
+// reference's sequential fp32 sum, for one router row in shared memory (a
+// warp per row; lane l takes elements 128 k + 4 l .. +3 of chunk k, so the
+// 16-byte reads are consecutive).  The reference sums s += g_i * x_i in fp32
 // (nn.c:519-521).  With a_i = fl(g_i * x_i) (the same products) and S_i the
 // exact prefix sums, recursive summation satisfies |s_fp32 - S_n| <= u'
 // sum_i |S_i| with u' = 2^-24 (1 + n u) for n = 2048.  S_n is summed in fp64
-// (error ~1e-13 relative); sum_i |S_i| in fp32 prefix sums, whose own error
-// (< 1e-3 relative) the 1.01 factor covers.
-__device__ __forceinline__ void router_logit(const float4 (&wv)[16], const float *xn, int lane,
-                                             double &S, double &B) {
-    const float4 *xr = reinterpret_cast<const float4 *>(xn + lane * 68);
-    float a[64];
-#pragma unroll
-    for (int k = 0; k < 16; k++) {
-        const float4 xw = xr[k];
-        a[4 * k + 0] = __fmul_rn(wv[k].x, xw.x);
-        a[4 * k + 1] = __fmul_rn(wv[k].y, xw.y);
-        a[4 * k + 2] = __fmul_rn(wv[k].z, xw.z);
-        a[4 * k + 3] = __fmul_rn(wv[k].w, xw.w);
-    }
+// (error ~1e-13 relative); sum_i |S_i| from fp32 prefix sums in the natural
+// order (a warp scan per 128-element chunk), whose own error (< 1e-3
+// relative) the 1.01 factor covers.
+__device__ __forceinline__ void router_logit(const float *row, const float *xn, int lane, double &S,
+                                             double &B) {
     double t4[4] = {0.0, 0.0, 0.0, 0.0};
+    float P = 0.0f, el = 0.0f;        // P: prefix of the previous chunks
 #pragma unroll
-    for (int j = 0; j < 64; j++) t4[j & 3] += double(a[j]);
-    const double tl = (t4[0] + t4[1]) + (t4[2] + t4[3]);
-    double incl = tl;
+    for (int h = 0; h < 2; h++) {     // chunks 8 h .. 8 h + 7
+        // pass 1: the fp64 sum and the chunks' lane sums
+        float c[8];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const double v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
+        for (int k = 0; k < 8; k++) {
+            const int o = 128 * (8 * h + k) + 4 * lane;
+            const float4 g = *reinterpret_cast<const float4 *>(row + o);
+            const float4 x = *reinterpret_cast<const float4 *>(xn + o);
+            const float a0 = __fmul_rn(g.x, x.x), a1 = __fmul_rn(g.y, x.y);
+            const float a2 = __fmul_rn(g.z, x.z), a3 = __fmul_rn(g.w, x.w);
+            t4[0] += double(a0);
+            t4[1] += double(a1);
+            t4[2] += double(a2);
+            t4[3] += double(a3);
+            c[k] = (a0 + a1) + (a2 + a3);
+        }
+        // inclusive scan of the lane sums within each chunk (8 independent scans)
+        float incl[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) incl[k] = c[k];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float v = __shfl_up_sync(0xffffffffu, incl[k], o);
+                if (lane >= o) incl[k] += v;
+            }
+        // pass 2: the prefix sums in natural order (products recomputed)
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int o = 128 * (8 * h + k) + 4 * lane;
+            const float4 g = *reinterpret_cast<const float4 *>(row + o);
+            const float4 x = *reinterpret_cast<const float4 *>(xn + o);
+            float p = P + (incl[k] - c[k]);
+            p += __fmul_rn(g.x, x.x);
+            el += fabsf(p);
+            p += __fmul_rn(g.y, x.y);
+            el += fabsf(p);
+            p += __fmul_rn(g.z, x.z);
+            el += fabsf(p);
+            p += __fmul_rn(g.w, x.w);
+            el += fabsf(p);
+            P += __shfl_sync(0xffffffffu, incl[k], 31);
+        }
     }
-    float p = float(incl - tl), el = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 64; j++) {
-        p += a[j];
-        el += fabsf(p);
-    }
+    S = warp_sum_d((t4[0] + t4[1]) + (t4[2] + t4[3]));
     const float E = warp_sum(el);
-    S = __shfl_sync(0xffffffffu, incl, 31);
     B = double(E) * 0x1.0p-24 * 1.01 + 1e-30;
 }
 
@@ -283,22 +309,26 @@ __device__ __forceinline__ bool top_settled(const double *sS, const double *sB, 
 // order for any rank the bounds cannot settle) and writes the renormalised
 // weights (nn.c:524-547) and the shared-expert gate sigmoid.
 constexpr int RCL = 16;                       // CTAs per router cluster
-constexpr int XCL = 16;                       // CTAs per expert cluster
+constexpr uint32_t ROUTER_SMEM = uint32_t(MOE_NEXP / RCL) * MOE_EMBD * 4;   // 16 fp32 rows
+constexpr int XCL = 8;                        // CTAs per expert cluster (two fit in a GPC)
+constexpr int XTHREADS = 512;                 // threads per expert CTA
 constexpr int XGU = MOE_FF / XCL;             // gate/up rows per expert CTA
 constexpr int XDN = MOE_EMBD / XCL;           // down rows per expert CTA
 static_assert(XDN == MOE_DOWN_CHUNK && XCL == MOE_DOWN_CHUNKS, "combine chunks = expert CTAs");
 
-__global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ x2,
+__global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restrict__ x2,
                                                          const float *__restrict__ post_norm,
                                                          const float *__restrict__ Wr,
                                                          const float *__restrict__ gis,
                                                          MoeScratch s, int *sel_out,
                                                          float *w_out) {
     QMA_TRACE_SCOPE(TK_ROUTER);
+    extern __shared__ __align__(128) float rrows[];        // this CTA's 16 router rows
     const unsigned rank = cluster_rank();
     const int t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ __align__(16) float xn[MOE_EMBD / 64 * 68];
+    __shared__ __align__(8) uint64_t rbar;
+    __shared__ __align__(16) float xn[MOE_EMBD];
     __shared__ double dred[8];
     __shared__ double sS[MOE_NEXP], sB[MOE_NEXP];
     __shared__ float gpart[MOE_EMBD / 256];
@@ -308,20 +338,30 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
     __shared__ int cand[MOE_NEXP];
     __shared__ unsigned long long rcand[8 * (MOE_TOPK + 1)];
 
-    // the two router rows of this warp: independent of the upstream kernel
+    // this CTA's router rows: independent of the upstream kernel, copied
+    // into shared memory by the TMA engine before waiting on it
     const int e0 = int(rank) * (MOE_NEXP / RCL) + warp * 2;
-    float4 w0[16], w1[16];
-    {
-        const float4 *r0 = reinterpret_cast<const float4 *>(Wr + size_t(e0) * MOE_EMBD + lane * 64);
-        const float4 *r1 = r0 + MOE_EMBD / 4;
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            w0[k] = __ldg(r0 + k);
-            w1[k] = __ldg(r1 + k);
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_init(&rbar, 1);
+            mbar_fence_init();
+            mbar_expect_tx(&rbar, ROUTER_SMEM);
         }
+        __syncwarp();
+        bulk_g2s_warp(rrows, Wr + size_t(rank) * (MOE_NEXP / RCL) * MOE_EMBD, ROUTER_SMEM, &rbar, lane);
     }
+    // this CTA's slice of the shared-expert gate row (CTAs 0..7, warp 0)
+    float gisv[8] = {};
+    if (rank < MOE_EMBD / 256 && warp == 0) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gis + rank * 256 + lane * 8));
+        const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gis + rank * 256 + lane * 8 + 4));
+        gisv[0] = g0.x; gisv[1] = g0.y; gisv[2] = g0.z; gisv[3] = g0.w;
+        gisv[4] = g1.x; gisv[5] = g1.y; gisv[6] = g1.z; gisv[7] = g1.w;
+    }
+    QMA_TRACE_MARK(TK_ROUTER, 1);
     pdl_trigger();
     pdl_wait();
+    QMA_TRACE_MARK(TK_ROUTER, 2);
     // ---- xn = rms_norm(x2) * post_norm ------------------------------------
     const float *x = x2 + size_t(t) * MOE_EMBD;
     float xv[8];
@@ -342,11 +382,16 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
         xn[xn_idx(i)] = __fmul_rn(__fmul_rn(xv[k], r), post_norm[i]);
     }
     __syncthreads();
+    QMA_TRACE_MARK(TK_ROUTER, 3);
     // ---- two exact logits per warp, sent to the leader ---------------------
     {
+        if (!mbar_wait(&rbar, 0)) {
+            if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
+            mbar_wait(&rbar, 0);
+        }
         double S0, B0, S1, B1;
-        router_logit(w0, xn, lane, S0, B0);
-        router_logit(w1, xn, lane, S1, B1);
+        router_logit(rrows + size_t(warp * 2) * MOE_EMBD, xn, lane, S0, B0);
+        router_logit(rrows + size_t(warp * 2 + 1) * MOE_EMBD, xn, lane, S1, B1);
         if (lane == 0) {
             st_cluster_f64(cluster_map(&sS[e0], 0), S0);
             st_cluster_f64(cluster_map(&sB[e0], 0), B0);
@@ -367,11 +412,13 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
                          s.xs + size_t(t) * (MOE_EMBD / 16) + blk * 16, q, sc);
         float gp = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 8; c++) gp += __fmul_rn(__fmul_rn(gis[i0 + c], float(q[c])), sc);
+        for (int c = 0; c < 8; c++) gp += __fmul_rn(__fmul_rn(gisv[c], float(q[c])), sc);
         gp = warp_sum(gp);
         if (lane == 0) st_cluster_f32(cluster_map(&gpart[blk], 0), gp);
     }
+    QMA_TRACE_MARK(TK_ROUTER, 4);
     cluster_sync();
+    QMA_TRACE_MARK(TK_ROUTER, 5);
     if (rank != 0) return;
 
     // ---- leader: top 8 ------------------------------------------------------
@@ -416,6 +463,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
         }
         __syncthreads();
     }
+    QMA_TRACE_MARK(TK_ROUTER, 6);
     if (warp == 0) {
         // renormalised softmax weights of the selected experts (nn.c:524-547)
         const float l0 = float(sS[top9[0]]);
@@ -478,14 +526,17 @@ template <> struct DownPtr<FmtQ4K> {
 
 // One cluster of XCL CTAs per (slot, token): grid (9 x XCL, T); slots 0..7
 // are the routed experts in selection order, slot 8 the shared expert
-// (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  CTA
-// `rank` owns gate/up rows rank*XGU.. and down rows rank*XDN..:
-//   1. its 32 gate and 32 up rows (74 KB) are copied into shared memory by
+// (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  Clusters
+// of 8 (one CTA per SM): two fit in a GPC, so all 9 are co-resident beside
+// the router's cluster.  CTA `rank` owns gate/up rows rank*XGU.. and down
+// rows rank*XDN..:
+//   1. its 64 gate and 64 up rows (147 KB) are copied into shared memory by
 //      the TMA engine as soon as the expert is known (the shared expert's
 //      before the router has finished), its down rows prefetched into L2;
 //   2. one warp per 4 row pairs computes silu(gate) * up;
-//   3. the cluster gathers the 512-wide hidden vector through distributed
-//      shared memory while the down rows are copied into the freed buffer;
+//   3. every CTA pushes its 64 hidden values into all 8 CTAs' shared
+//      memory (one cluster barrier) while the down rows are copied into the
+//      freed buffer;
 //   4. every CTA quantizes the hidden vector to Q8_K and computes its down
 //      rows; the last of the 9 slot CTAs of a row chunk combines the slots
 //      in the reference's order and adds the residual (nn.c:615-629,
@@ -493,19 +544,18 @@ template <> struct DownPtr<FmtQ4K> {
 // Every wait on a copy is bounded; a copy that never lands is counted in
 // g_moe_timeouts (the host fails the call) and the CTA still takes part in
 // the cluster barriers so that no peer waits forever.
-__device__ unsigned g_moe_timeouts;
-
 template <class F> struct DownBytes;
 template <> struct DownBytes<FmtQ6K> {
     static constexpr uint32_t QL = XDN * (MOE_FF / 2), QH = XDN * (MOE_FF / 4), SC = XDN * (MOE_FF / 16),
                               D = XDN * (MOE_FF / 256) * 2, ALL = QL + QH + SC + D;
-    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar) {
+    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar, int lane) {
         const Q6Planes P = shift_rows(DownPtr<FmtQ6K>::at(expert), d0, MOE_FF);
-        mbar_expect_tx(bar, ALL);
-        bulk_g2s(dst, P.ql, QL, bar);
-        bulk_g2s(dst + QL, P.qh, QH, bar);
-        bulk_g2s(dst + QL + QH, P.sc, SC, bar);
-        bulk_g2s(dst + QL + QH + SC, P.d, D, bar);
+        if (lane == 0) mbar_expect_tx(bar, ALL);
+        __syncwarp();
+        bulk_g2s_warp(dst, P.ql, QL, bar, lane);
+        bulk_g2s_warp(dst + QL, P.qh, QH, bar, lane);
+        bulk_g2s_warp(dst + QL + QH, P.sc, SC, bar, lane);
+        bulk_g2s_warp(dst + QL + QH + SC, P.d, D, bar, lane);
     }
     __device__ static Q6Planes at(const uint8_t *dst) {
         Q6Planes P;
@@ -518,20 +568,21 @@ template <> struct DownBytes<FmtQ6K> {
 };
 template <> struct DownBytes<FmtQ4K> {
     static constexpr uint32_t ALL = XDN * (MOE_FF / 256) * Q4K_BYTES;
-    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar) {
-        mbar_expect_tx(bar, ALL);
-        bulk_g2s(dst, shift_rows(expert, d0, MOE_FF), ALL, bar);
+    __device__ static void issue(uint8_t *dst, const uint8_t *expert, int d0, uint64_t *bar, int lane) {
+        if (lane == 0) mbar_expect_tx(bar, ALL);
+        __syncwarp();
+        bulk_g2s_warp(dst, shift_rows(expert, d0, MOE_FF), ALL, bar, lane);
     }
     __device__ static const uint8_t *at(const uint8_t *dst) { return dst; }
 };
 constexpr uint32_t XROW = uint32_t(MOE_EMBD / 256) * Q4K_BYTES;     // one gate/up row
-constexpr uint32_t XGU_BYTES = XGU * XROW;                          // 32 rows
+constexpr uint32_t XGU_BYTES = XGU * XROW;                          // 64 rows
 constexpr size_t EXPERT_SMEM = 2 * size_t(XGU_BYTES);
 static_assert(DownBytes<FmtQ6K>::ALL <= EXPERT_SMEM && DownBytes<FmtQ4K>::ALL <= EXPERT_SMEM,
               "down rows reuse the gate/up buffer");
 
 template <class F>
-__global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
+__global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
                                                          const uint8_t *__restrict__ up_exps,
                                                          const uint8_t *__restrict__ gate_sh,
                                                          const uint8_t *__restrict__ up_sh,
@@ -562,53 +613,63 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
     }
     __syncthreads();
     const uint8_t *Db = down_sh;
-    if (slot == MOE_TOPK && tid == 0) {
-        mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
-        bulk_g2s(xbuf, gate_sh + g0 * XROW, XGU_BYTES, &bar[0]);
-        bulk_g2s(xbuf + XGU_BYTES, up_sh + g0 * XROW, XGU_BYTES, &bar[0]);
-        prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+    if (slot == MOE_TOPK && warp == 0) {
+        if (lane == 0) mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
+        __syncwarp();
+        bulk_g2s_warp(xbuf, gate_sh + g0 * XROW, XGU_BYTES, &bar[0], lane);
+        bulk_g2s_warp(xbuf + XGU_BYTES, up_sh + g0 * XROW, XGU_BYTES, &bar[0], lane);
+        if (lane == 0) prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
     }
-    pdl_trigger();
     pdl_wait();
     if (slot < MOE_TOPK) {
         const int e = __ldcg(&s.sel[t * MOE_TOPK + slot]);
         Db = down_exps + size_t(e) * down_bytes;
-        if (tid == 0) {
-            mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
-            bulk_g2s(xbuf, gate_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0]);
-            bulk_g2s(xbuf + XGU_BYTES, up_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0]);
-            prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
+        if (warp == 0) {
+            if (lane == 0) mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
+            __syncwarp();
+            bulk_g2s_warp(xbuf, gate_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0], lane);
+            bulk_g2s_warp(xbuf + XGU_BYTES, up_exps + size_t(e) * GU_BYTES + g0 * XROW, XGU_BYTES, &bar[0], lane);
+            if (lane == 0) prefetch_rows(shift_rows(DownPtr<F>::at(Db), d0, MOE_FF), XDN, MOE_FF);
         }
     }
     // ---- gate / up rows g0 + 4 warp .. + 3 from shared memory ---------------
+    FmtQ4K::Act act;
+    FmtQ4K::load_act(act, s.xq + size_t(t) * MOE_EMBD, s.xd + size_t(t) * 8, s.xs + size_t(t) * 128,
+                     lane);
+    QMA_TRACE_MARK(TK_EXPERT, 1);
     const bool gu_ok = mbar_wait(&bar[0], 0);
+    QMA_TRACE_MARK(TK_EXPERT, 2);
     {
-        FmtQ4K::Act act;
-        FmtQ4K::load_act(act, s.xq + size_t(t) * MOE_EMBD, s.xd + size_t(t) * 8,
-                         s.xs + size_t(t) * 128, lane);
-        constexpr int RPWARP = XGU / 8;
+        constexpr int RPWARP = XGU / (XTHREADS / 32);
+        static_assert(RPWARP == 4, "8 dots (4 gate + 4 up rows) per warp");
+        float dv[8];
 #pragma unroll
         for (int k = 0; k < RPWARP; k++) {
-            const int r = warp * RPWARP + k;
             FmtQ4K::Wt wg, wu;
-            FmtQ4K::load_w_smem(wg, xbuf, r, MOE_EMBD, lane);
-            FmtQ4K::load_w_smem(wu, xbuf + XGU_BYTES, r, MOE_EMBD, lane);
-            const float g = warp_sum(FmtQ4K::dot(wg, act, lane));
-            const float u = warp_sum(FmtQ4K::dot(wu, act, lane));
-            if (lane == 0) hpart[r] = gu_ok ? (g / (1.0f + expf(-g))) * u : 0.0f;
+            FmtQ4K::load_w_smem(wg, xbuf, warp * RPWARP + k, MOE_EMBD, lane);
+            FmtQ4K::load_w_smem(wu, xbuf + XGU_BYTES, warp * RPWARP + k, MOE_EMBD, lane);
+            dv[k] = FmtQ4K::dot(wg, act, lane);
+            dv[4 + k] = FmtQ4K::dot(wu, act, lane);
+        }
+        const float tot = warp_sum8(dv, lane);          // lane: row (index & 3), gate/up (index & 4)
+        const float u = __shfl_xor_sync(0xffffffffu, tot, 16);
+        if ((lane & 19) == 0) {                          // gate lanes, one per row
+            const float g = tot;
+            hpart[warp * RPWARP + (warp_sum8_index(lane) & 3)] = gu_ok ? (g / (1.0f + expf(-g))) * u : 0.0f;
         }
     }
     __syncthreads();                    // gate/up rows consumed: reuse the buffer
-    if (tid == 0) {
-        if (!gu_ok) atomicAdd(&g_moe_timeouts, 1u);
+    if (warp == 0) {
+        if (lane == 0 && !gu_ok) atomicAdd(&g_moe_timeouts, 1u);
         fence_proxy_async_smem();
-        DownBytes<F>::issue(xbuf, Db, d0, &bar[1]);
+        DownBytes<F>::issue(xbuf, Db, d0, &bar[1], lane);
     }
-    // ---- the cluster's 512 hidden values ------------------------------------
-    cluster_sync();
-    for (int i = tid; i < MOE_FF; i += 256) hfull[i] = ld_cluster_f32(cluster_map(&hpart[i % XGU], i / XGU));
-    cluster_arrive();              // this CTA has finished reading its peers
-    __syncthreads();
+    // ---- the cluster's 512 hidden values: every CTA pushes its 32 ----------
+    for (int i = tid; i < XGU * XCL; i += XTHREADS)
+        st_cluster_f32(cluster_map(&hfull[g0 + i % XGU], unsigned(i / XGU)), hpart[i % XGU]);
+    QMA_TRACE_MARK(TK_EXPERT, 3);
+    cluster_sync();                     // all pushes landed; no remote access after this
+    QMA_TRACE_MARK(TK_EXPERT, 4);
     if (warp < MOE_FF / 256) {
         const float4 a0 = *reinterpret_cast<const float4 *>(hfull + warp * 256 + lane * 8);
         const float4 a1 = *reinterpret_cast<const float4 *>(hfull + warp * 256 + lane * 8 + 4);
@@ -617,17 +678,23 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
     }
     __syncthreads();
     // ---- down rows d0 .. d0 + XDN from shared memory --------------------------
+    QMA_TRACE_MARK(TK_EXPERT, 5);
     const bool dn_ok = mbar_wait(&bar[1], 0);
+    QMA_TRACE_MARK(TK_EXPERT, 6);
     float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + d0;
     if (dn_ok) {
-        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 1>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
-                                                  warp, 8, lane);
+        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 2>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
+                                                  warp, XTHREADS / 32, lane);
     } else {
         if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
         if (tid < XDN) part[tid] = 0.0f;
         mbar_wait(&bar[1], 0);          // let a late copy land before the CTA exits
     }
 
+    QMA_TRACE_MARK(TK_EXPERT, 7);
+    // the next layer's kernels may launch now: this kernel's weight traffic
+    // is done, only the combine remains
+    pdl_trigger();
     // ---- the last of the 9 slot CTAs of this row chunk combines --------------
     __syncthreads();
     if (tid == 0) {
@@ -652,7 +719,6 @@ __global__ void __launch_bounds__(256) moe_expert_kernel(const uint8_t *__restri
         }
         if (tid == 0) s.dcount[t * MOE_DOWN_CHUNKS + rank] = 0;
     }
-    cluster_wait();                // no CTA leaves while a peer may read it
 }
 
 int moe_wait_timeouts() {
@@ -672,16 +738,21 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     MoeScratch s = moe_scratch_layout(scratch, T);
     if (!g_moe_attrs) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ROUTER_SMEM)));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
+        // the 9 expert clusters must be co-resident beside other kernels' CTAs:
+        // prefer the largest shared-memory carveout (two CTAs per SM)
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
         g_moe_attrs = true;
     }
     if (clear_counters)
         QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
     const bool pdl = pdl_enabled() && !clear_counters;
-    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(256), 0, st, RCL, pdl, x2, w.post_norm,
+    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(256), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
                              w.gate_inp, w.gate_inp_shexp, s, sel, wts));
     const size_t eb = packed_bytes(w.down_type, MOE_EMBD, MOE_FF);
     const dim3 grid(MOE_NSLOT * XCL, T);
@@ -689,10 +760,10 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *gsh = static_cast<const uint8_t *>(w.gate_shexp), *ush = static_cast<const uint8_t *>(w.up_shexp);
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
-        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(256), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
                                  gsh, ush, de, eb, dsh, x2, x_out, s));
     else
-        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(256), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
+        QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
                                  gsh, ush, de, eb, dsh, x2, x_out, s));
     return QMA_CUDA_OK;
 }

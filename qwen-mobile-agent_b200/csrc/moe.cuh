@@ -11,7 +11,7 @@ constexpr int MOE_FF = 512;           // N_FF_EXP / N_FF_SHEXP (qma.h:59-60)
 constexpr int MOE_NSLOT = MOE_TOPK + 1;   // routed experts + the shared expert
 constexpr int MOE_GU_ROWS = 32;       // gate/up row pairs per CTA
 constexpr int MOE_GU_CHUNKS = MOE_FF / MOE_GU_ROWS;
-constexpr int MOE_DOWN_CHUNK = 128;   // down-projection output rows per CTA
+constexpr int MOE_DOWN_CHUNK = 256;   // down-projection output rows per CTA
 constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
 
 // Per-call device scratch of the MoE block for T tokens (moe_scratch_layout
