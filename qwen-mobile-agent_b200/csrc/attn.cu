@@ -220,82 +220,38 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
 // ---------------------------------------------------- chunked attention ----
 // Grid (ceil(nk_max / span), KV head, query t), 256 threads.  A CTA covers
 // `span` attended positions of one KV head for its 8 query heads (GQA: KV
-// head = query head / 8) in sub-chunks of 64: the sub-chunk's K and V
+// head = query head / 8), in sub-chunks of up to SUB positions whose K and V
 // records (q4: 160 B, q2: 80 B) are staged in shared memory with 16-byte
-// loads; thread (position i, head pair hp) computes two scores with the
-// record kernels' own order (kvq4_dot / kvq2_dot, kvq.c:183-213: four lane
-// partial sums per sub-block, pairwise reduced); warp h keeps the running max
-// and sum of p = expf(s - max) for head h; thread d accumulates
-// sum p * V[d] for the 8 heads (kvq4_vacc / kvq2_vacc, kvq.c:215-241),
-// rescaled when the running max grows.  Outputs: the raw scores (for the
-// salience update) and per-CTA (max, sum, partial output).
-constexpr int SUB = 64;
-constexpr int QS_LD = HEAD_DIM + 4;      // padded query rows: conflict-free float4 reads
+// loads.  The record arithmetic of kvq.c:183-241 is folded: a sub-block
+// with scale d and offset m contributes d * sum(q_i x_i) + m * sum(x_i) to a
+// score, and p * d * q + p * m to an output, so the quantized values enter
+// as small integers (converted through the float exponent field) in fused
+// multiply-adds.  This reassociates the reference's fp32 sums; the
+// attention output agrees within fp32 rounding, not bit for bit.
+//   scores : thread (position i, head quad hq) -> 4 heads;
+//   softmax: warp h keeps the running max and sum of p = expf(s - max);
+//   p . V  : thread = output dim, 8 heads; p * d per (position, head,
+//            sub-block) precomputed in shared memory, sum p * m per
+//            (head, sub-block) accumulated separately.
+// Outputs: the raw scores (for the salience update) and per-CTA (max, sum,
+// partial output).
+constexpr int SUB = 128;
 
-__device__ __forceinline__ float q4_val(uint32_t nw, int k, float d, float m) {
-    return __fadd_rn(m, __fmul_rn(float((nw >> (4 * k)) & 0xF), d));
+__device__ __forceinline__ float small2f(uint32_t v) {      // exact float of v < 2^23
+    return __int_as_float(0x4B000000u | v) - 8388608.0f;
 }
 
-// two scores (heads qa, qb) of a staged record
-__device__ __forceinline__ void rec_dot2(const uint32_t *w, bool q2, const float *qa,
-                                         const float *qb, float &sa, float &sb_) {
-    float acc_a = 0.0f, acc_b = 0.0f;
-    if (!q2) {
-#pragma unroll 1
-        for (int sb = 0; sb < 8; sb++) {
-            const uint32_t hdr = w[5 * sb];
-            const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
-            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f}, b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int wi = 0; wi < 4; wi++) {
-                const uint32_t nw = w[5 * sb + 1 + wi];       // values 8 wi .. 8 wi + 7
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    const int i0 = sb * 32 + wi * 8 + half * 4;
-                    const float4 xa = *reinterpret_cast<const float4 *>(qa + i0);
-                    const float4 xb = *reinterpret_cast<const float4 *>(qb + i0);
-                    const float e0 = q4_val(nw, 4 * half + 0, d, m), e1 = q4_val(nw, 4 * half + 1, d, m);
-                    const float e2 = q4_val(nw, 4 * half + 2, d, m), e3 = q4_val(nw, 4 * half + 3, d, m);
-                    a[0] = __fadd_rn(a[0], __fmul_rn(e0, xa.x)); b[0] = __fadd_rn(b[0], __fmul_rn(e0, xb.x));
-                    a[1] = __fadd_rn(a[1], __fmul_rn(e1, xa.y)); b[1] = __fadd_rn(b[1], __fmul_rn(e1, xb.y));
-                    a[2] = __fadd_rn(a[2], __fmul_rn(e2, xa.z)); b[2] = __fadd_rn(b[2], __fmul_rn(e2, xb.z));
-                    a[3] = __fadd_rn(a[3], __fmul_rn(e3, xa.w)); b[3] = __fadd_rn(b[3], __fmul_rn(e3, xb.w));
-                }
-            }
-            acc_a = __fadd_rn(acc_a, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
-            acc_b = __fadd_rn(acc_b, __fadd_rn(__fadd_rn(b[0], b[1]), __fadd_rn(b[2], b[3])));
-        }
-    } else {
-#pragma unroll 1
-        for (int sb = 0; sb < 4; sb++) {
-            const uint32_t hdr = w[5 * sb];
-            const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
-            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f}, b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int wi = 0; wi < 4; wi++) {
-                const uint32_t pw = w[5 * sb + 1 + wi];       // values 16 wi .. 16 wi + 15
-#pragma unroll
-                for (int qd = 0; qd < 4; qd++) {
-                    const int i0 = sb * 64 + wi * 16 + qd * 4;
-                    const float4 xa = *reinterpret_cast<const float4 *>(qa + i0);
-                    const float4 xb = *reinterpret_cast<const float4 *>(qb + i0);
-                    const uint32_t by = pw >> (8 * qd);
-                    float e[4];
-#pragma unroll
-                    for (int l = 0; l < 4; l++) e[l] = __fadd_rn(m, __fmul_rn(float((by >> (2 * l)) & 3), d));
-                    a[0] = __fadd_rn(a[0], __fmul_rn(e[0], xa.x)); b[0] = __fadd_rn(b[0], __fmul_rn(e[0], xb.x));
-                    a[1] = __fadd_rn(a[1], __fmul_rn(e[1], xa.y)); b[1] = __fadd_rn(b[1], __fmul_rn(e[1], xb.y));
-                    a[2] = __fadd_rn(a[2], __fmul_rn(e[2], xa.z)); b[2] = __fadd_rn(b[2], __fmul_rn(e[2], xb.z));
-                    a[3] = __fadd_rn(a[3], __fmul_rn(e[3], xa.w)); b[3] = __fadd_rn(b[3], __fmul_rn(e[3], xb.w));
-                }
-            }
-            acc_a = __fadd_rn(acc_a, __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])));
-            acc_b = __fadd_rn(acc_b, __fadd_rn(__fadd_rn(b[0], b[1]), __fadd_rn(b[2], b[3])));
-        }
-    }
-    sa = acc_a;
-    sb_ = acc_b;
-}
+struct ChunkSmem {
+    float qT[HEAD_DIM][8];          // query, element-major (8 heads contiguous)
+    float X4[8][8], X2[8][4];       // query sums over 32- / 64-element sub-blocks
+    uint4 kst[SUB][10], vst[SUB][10];
+    const uint8_t *kp[SUB], *vp[SUB];
+    int isq2[SUB];
+    float ps[8][SUB];               // scores, then p
+    float W[SUB][8][8];             // p * d of V record i, sub-block sb, head h: [i][sb][h]
+    float U4[8][8], U2[8][4];       // sum p * m per head and q4 / q2 sub-block
+    float scl[8];
+};
 
 __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict__ qr,
                                                          const uint8_t *__restrict__ kv,
@@ -305,15 +261,10 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
                                                          int span, int nchunk, float *scores,
                                                          float *mpart, float *lpart, float *opart) {
     QMA_TRACE_SCOPE(TK_ATTN_CHUNK);
+    extern __shared__ __align__(16) uint8_t chunk_raw[];
+    ChunkSmem &S = *reinterpret_cast<ChunkSmem *>(chunk_raw);
     const int chunk = blockIdx.x, kh = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ __align__(16) float qs[8 * QS_LD];
-    __shared__ __align__(16) uint4 kst[SUB][10];
-    __shared__ __align__(16) uint4 vst[SUB][10];
-    __shared__ const uint8_t *kp[SUB], *vp[SUB];
-    __shared__ int isq2[SUB];
-    __shared__ float ps[8][SUB];
-    __shared__ float scl[8];
     pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
@@ -321,8 +272,29 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
     const int j0 = chunk * span;
     if (j0 >= nk) return;
     const int j1 = min(nk, j0 + span);
-    for (int i = tid; i < 8 * HEAD_DIM; i += 256)
-        qs[(i / HEAD_DIM) * QS_LD + i % HEAD_DIM] = qr[(size_t(t) * NHEAD + kh * 8) * HEAD_DIM + i];
+    for (int i = tid; i < 8 * HEAD_DIM; i += 256) {
+        const int h = i / HEAD_DIM, e = i % HEAD_DIM;
+        S.qT[e][h] = qr[(size_t(t) * NHEAD + kh * 8) * HEAD_DIM + i];
+    }
+    {   // warp h: sub-block sums of query head h
+        const float *q = qr + (size_t(t) * NHEAD + kh * 8 + warp) * HEAD_DIM;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = q[lane + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float x4 = warp_sum(v[k]);          // elements 32 k .. 32 k + 31
+            if (lane == 0) S.X4[warp][k] = x4;
+        }
+        if (lane < 4) S.X2[warp][lane] = 0.0f;
+        __syncwarp();
+        if (lane == 0)
+            for (int k = 0; k < 4; k++) S.X2[warp][k] = S.X4[warp][2 * k] + S.X4[warp][2 * k + 1];
+        if (lane < 8) {
+            S.U4[warp][lane] = 0.0f;
+            if (lane < 4) S.U2[warp][lane] = 0.0f;
+        }
+    }
     const uint8_t *kring = kv + size_t(kh) * sp.n_ctx * KVQ_SLOT;
     const uint8_t *vring = kv + size_t(NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT;
     const uint8_t *kar = arena + size_t(kh) * HCM_H_PIN * KVQ_SLOT;
@@ -334,81 +306,167 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
     const int d = tid;
     for (int b0 = j0; b0 < j1; b0 += SUB) {
         const int bn = min(SUB, j1 - b0);
-        __syncthreads();     // previous sub-chunk fully consumed
+        __syncthreads();     // previous sub-chunk fully consumed; query sums ready
         if (tid < bn) {
             bool q2;
-            kp[tid] = rec_of(sp, live, kring, kar, b0 + tid, q2);
+            S.kp[tid] = rec_of(sp, live, kring, kar, b0 + tid, q2);
             bool q2v;
-            vp[tid] = rec_of(sp, live, vring, var, b0 + tid, q2v);
-            isq2[tid] = q2;
+            S.vp[tid] = rec_of(sp, live, vring, var, b0 + tid, q2v);
+            S.isq2[tid] = q2;
         }
         __syncthreads();
         for (int idx = tid; idx < bn * 10; idx += 256) {
             const int i = idx / 10, wq = idx % 10;
-            if (wq < (isq2[i] ? 5 : 10)) {
-                kst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(kp[i]) + wq);
-                vst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(vp[i]) + wq);
+            if (wq < (S.isq2[i] ? 5 : 10)) {
+                S.kst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(S.kp[i]) + wq);
+                S.vst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(S.vp[i]) + wq);
             }
         }
         __syncthreads();
-        {   // scores: thread (i, hp)
-            const int i = tid >> 2, hp = tid & 3;
-            float sa = -INFINITY, sb = -INFINITY;
+        {   // scores: thread (position i, heads 4 hq .. 4 hq + 3)
+            const int i = tid & (SUB - 1), hq = tid >> 7;
+            float sc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (i < bn) {
-                rec_dot2(reinterpret_cast<const uint32_t *>(kst[i]), isq2[i] != 0, qs + (2 * hp) * QS_LD,
-                         qs + (2 * hp + 1) * QS_LD, sa, sb);
-                sa = __fmul_rn(sa, 0.0625f);       // 1 / sqrtf(256)
-                sb = __fmul_rn(sb, 0.0625f);
-                float *srow = scores + (size_t(t) * NHEAD + kh * 8 + 2 * hp) * nk_max + b0 + i;
-                srow[0] = sa;
-                srow[nk_max] = sb;
+                const uint32_t *w = reinterpret_cast<const uint32_t *>(S.kst[i]);
+                float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (!S.isq2[i]) {
+#pragma unroll 2
+                    for (int sb = 0; sb < 8; sb++) {
+                        const uint32_t hdr = w[5 * sb];
+                        const float dd = h2f(uint16_t(hdr & 0xffff)), mm = h2f(uint16_t(hdr >> 16));
+                        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                        for (int wi = 0; wi < 4; wi++) {
+                            const uint32_t nw = w[5 * sb + 1 + wi];
+#pragma unroll
+                            for (int k = 0; k < 8; k++) {
+                                const float qf = small2f((nw >> (4 * k)) & 0xFu);
+                                const float4 x = *reinterpret_cast<const float4 *>(&S.qT[sb * 32 + wi * 8 + k][4 * hq]);
+                                a4[0] = fmaf(qf, x.x, a4[0]);
+                                a4[1] = fmaf(qf, x.y, a4[1]);
+                                a4[2] = fmaf(qf, x.z, a4[2]);
+                                a4[3] = fmaf(qf, x.w, a4[3]);
+                            }
+                        }
+#pragma unroll
+                        for (int h = 0; h < 4; h++) s4[h] = fmaf(mm, S.X4[4 * hq + h][sb], fmaf(dd, a4[h], s4[h]));
+                    }
+                } else {
+#pragma unroll 1
+                    for (int sb = 0; sb < 4; sb++) {
+                        const uint32_t hdr = w[5 * sb];
+                        const float dd = h2f(uint16_t(hdr & 0xffff)), mm = h2f(uint16_t(hdr >> 16));
+                        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                        for (int wi = 0; wi < 4; wi++) {
+                            const uint32_t pw = w[5 * sb + 1 + wi];
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+                                const float qf = small2f((pw >> (2 * k)) & 3u);
+                                const float4 x = *reinterpret_cast<const float4 *>(&S.qT[sb * 64 + wi * 16 + k][4 * hq]);
+                                a4[0] = fmaf(qf, x.x, a4[0]);
+                                a4[1] = fmaf(qf, x.y, a4[1]);
+                                a4[2] = fmaf(qf, x.z, a4[2]);
+                                a4[3] = fmaf(qf, x.w, a4[3]);
+                            }
+                        }
+#pragma unroll
+                        for (int h = 0; h < 4; h++) s4[h] = fmaf(mm, S.X2[4 * hq + h][sb], fmaf(dd, a4[h], s4[h]));
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    sc[h] = __fmul_rn(s4[h], 0.0625f);    // 1 / sqrtf(256)
+                    scores[(size_t(t) * NHEAD + kh * 8 + 4 * hq + h) * nk_max + b0 + i] = sc[h];
+                }
             }
-            ps[2 * hp][i] = sa;
-            ps[2 * hp + 1][i] = sb;
+#pragma unroll
+            for (int h = 0; h < 4; h++) S.ps[4 * hq + h][i] = sc[h];
         }
         __syncthreads();
         {   // warp h: running max / sum of head h, p of this sub-chunk
             const int h = warp;
-            const float s0 = ps[h][lane], s1 = ps[h][lane + 32];
-            const float mloc = warp_max(fmaxf(s0, s1));
+            float sv[SUB / 32];
+            float mloc = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < SUB / 32; k++) {
+                sv[k] = S.ps[h][lane + 32 * k];
+                mloc = fmaxf(mloc, sv[k]);
+            }
+            mloc = warp_max(mloc);
             const float m_new = fmaxf(m_run, mloc);
-            const float p0 = lane < bn ? expf(s0 - m_new) : 0.0f;
-            const float p1 = lane + 32 < bn ? expf(s1 - m_new) : 0.0f;
+            float lsum = 0.0f;
+#pragma unroll
+            for (int k = 0; k < SUB / 32; k++) {
+                const float p = lane + 32 * k < bn ? expf(sv[k] - m_new) : 0.0f;
+                S.ps[h][lane + 32 * k] = p;
+                lsum += p;
+            }
             const float c = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-            l_run = __fadd_rn(__fmul_rn(l_run, c), warp_sum(p0 + p1));
+            l_run = __fadd_rn(__fmul_rn(l_run, c), warp_sum(lsum));
             m_run = m_new;
-            __syncwarp();
-            ps[h][lane] = p0;
-            ps[h][lane + 32] = p1;
-            if (lane == 0) scl[h] = c;
+            if (lane == 0) S.scl[h] = c;
         }
         __syncthreads();
-        // p . V for output dim d
-#pragma unroll
-        for (int h = 0; h < 8; h++) acc[h] = __fmul_rn(acc[h], scl[h]);
-        for (int i = 0; i < bn; i++) {
-            const uint32_t *w = reinterpret_cast<const uint32_t *>(vst[i]);
-            float v;
-            if (!isq2[i]) {
-                const int sb = d >> 5, l = d & 31;
-                const uint32_t hdr = w[5 * sb];
-                const uint32_t nw = w[5 * sb + 1 + (l >> 3)];
-                v = __fadd_rn(h2f(uint16_t(hdr >> 16)),
-                              __fmul_rn(float((nw >> (4 * (l & 7))) & 0xF), h2f(uint16_t(hdr & 0xffff))));
-            } else {
-                const int sb = d >> 6, l = d & 63;
-                const uint32_t hdr = w[5 * sb];
-                const uint32_t pw = w[5 * sb + 1 + (l >> 4)];
-                v = __fadd_rn(h2f(uint16_t(hdr >> 16)),
-                              __fmul_rn(float((pw >> (2 * (l & 15))) & 3), h2f(uint16_t(hdr & 0xffff))));
+        // p * d per (position, sub-block, head); sum p * m per (head, sub-block)
+        for (int e = tid; e < bn * 64; e += 256) {
+            const int i = e >> 6, sb = (e >> 3) & 7, h = e & 7;
+            float wv = 0.0f;
+            if (!S.isq2[i] || sb < 4) {
+                const uint32_t hdr = reinterpret_cast<const uint32_t *>(S.vst[i])[5 * sb];
+                wv = __fmul_rn(S.ps[h][i], h2f(uint16_t(hdr & 0xffff)));
             }
+            S.W[i][sb][h] = wv;
+        }
+        {   // thread (h, sb, quarter): a quarter of the positions, then a 4-lane sum
+            const int h = tid >> 5, sb = (tid >> 2) & 7, qtr = tid & 3;
+            float u4 = 0.0f, u2 = 0.0f;
+            for (int i = qtr; i < bn; i += 4) {
+                const uint32_t *w = reinterpret_cast<const uint32_t *>(S.vst[i]);
+                if (!S.isq2[i]) u4 = fmaf(S.ps[h][i], h2f(uint16_t(w[5 * sb] >> 16)), u4);
+                else if (sb < 4) u2 = fmaf(S.ps[h][i], h2f(uint16_t(w[5 * sb] >> 16)), u2);
+            }
+            u4 += __shfl_xor_sync(0xffffffffu, u4, 1);
+            u4 += __shfl_xor_sync(0xffffffffu, u4, 2);
+            u2 += __shfl_xor_sync(0xffffffffu, u2, 1);
+            u2 += __shfl_xor_sync(0xffffffffu, u2, 2);
+            if (qtr == 0) {
+                S.U4[h][sb] = fmaf(S.U4[h][sb], S.scl[h], u4);
+                if (sb < 4) S.U2[h][sb] = fmaf(S.U2[h][sb], S.scl[h], u2);
+            }
+        }
+        __syncthreads();
+        // p . V for output dim d (the q * (p d) part)
 #pragma unroll
-            for (int h = 0; h < 8; h++) acc[h] = __fadd_rn(acc[h], __fmul_rn(ps[h][i], v));
+        for (int h = 0; h < 8; h++) acc[h] = __fmul_rn(acc[h], S.scl[h]);
+        for (int i = 0; i < bn; i++) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(S.vst[i]);
+            float qf;
+            int sb;
+            if (!S.isq2[i]) {
+                sb = d >> 5;
+                qf = small2f((w[5 * sb + 1 + ((d & 31) >> 3)] >> (4 * (d & 7))) & 0xFu);
+            } else {
+                sb = d >> 6;
+                qf = small2f((w[5 * sb + 1 + ((d & 63) >> 4)] >> (2 * (d & 15))) & 3u);
+            }
+            const float4 wa = *reinterpret_cast<const float4 *>(&S.W[i][sb][0]);
+            const float4 wb = *reinterpret_cast<const float4 *>(&S.W[i][sb][4]);
+            acc[0] = fmaf(wa.x, qf, acc[0]);
+            acc[1] = fmaf(wa.y, qf, acc[1]);
+            acc[2] = fmaf(wa.z, qf, acc[2]);
+            acc[3] = fmaf(wa.w, qf, acc[3]);
+            acc[4] = fmaf(wb.x, qf, acc[4]);
+            acc[5] = fmaf(wb.y, qf, acc[5]);
+            acc[6] = fmaf(wb.z, qf, acc[6]);
+            acc[7] = fmaf(wb.w, qf, acc[7]);
         }
     }
+    __syncthreads();
     const size_t base = (size_t(t) * NHEAD + kh * 8) * nchunk + chunk;
 #pragma unroll
-    for (int h = 0; h < 8; h++) opart[(base + size_t(h) * nchunk) * HEAD_DIM + d] = acc[h];
+    for (int h = 0; h < 8; h++)
+        opart[(base + size_t(h) * nchunk) * HEAD_DIM + d] = acc[h] + S.U4[h][d >> 5] + S.U2[h][d >> 6];
     if (lane == 0) {
         mpart[base + size_t(warp) * nchunk] = m_run;
         lpart[base + size_t(warp) * nchunk] = l_run;
@@ -416,62 +474,63 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
 }
 
 // -------------------------------------- combine + sigmoid gate + Q8_K ----
-// Per query t: for head h, M = max of the CTA maxima, f_c = expf(m_c - M),
-// L = sum f_c l_c, o = (sum_c f_c o_c) * (1 / L) (the softmax of attn_worker,
-// nn.c:1340-1412), aout = o * sigmoid(gate) (nn.c:2157-2159), quantized to
-// Q8_K for attn_output; (M, L) per head are kept for the salience update.
-__global__ void __launch_bounds__(1024) attn_combine_kernel(const float *__restrict__ opart,
-                                                            const float *__restrict__ mpart,
-                                                            const float *__restrict__ lpart,
-                                                            const StepParams *spp, int span,
-                                                            int nchunk, const float *__restrict__ z,
-                                                            float *ml, int8_t *xq, float *xd,
-                                                            int16_t *xs) {
+// One CTA per (query head h, query t), thread = output dim: M = max of the
+// chunk maxima, f_c = expf(m_c - M), L = sum f_c l_c, o = (sum_c f_c o_c) *
+// (1 / L) (the softmax of attn_worker, nn.c:1340-1412), aout = o *
+// sigmoid(gate) (nn.c:2157-2159) and its Q8_K block (the head's 256 dims
+// are one block); (M, L) are kept for the salience update.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float *__restrict__ opart,
+                                                           const float *__restrict__ mpart,
+                                                           const float *__restrict__ lpart,
+                                                           const StepParams *spp, int span,
+                                                           int nchunk, const float *__restrict__ z,
+                                                           float *ml, int8_t *xq, float *xd,
+                                                           int16_t *xs) {
     QMA_TRACE_SCOPE(TK_ATTN_COMBINE);
-    extern __shared__ float fsh[];              // [16][nchunk] chunk factors
-    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float inv[NHEAD];
-    __shared__ __align__(16) float y[WO_DIM];
+    extern __shared__ float fsh[];              // [nchunk] chunk factors of this head
+    const int h = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float wred[8], wsum[8];
+    __shared__ __align__(16) float y[HEAD_DIM];
     pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
     const int nc = (nk_of(sp, t) + span - 1) / span;
-    if (warp < NHEAD) {
-        const size_t base = (size_t(t) * NHEAD + warp) * nchunk;
-        float m = -INFINITY;
-        for (int c = lane; c < nc; c += 32) m = fmaxf(m, mpart[base + c]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int c = lane; c < nc; c += 32) {
-            const float f = expf(mpart[base + c] - m);
-            fsh[warp * nchunk + c] = f;
-            l = __fadd_rn(l, __fmul_rn(f, lpart[base + c]));
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            inv[warp] = 1.0f / l;
-            ml[(size_t(t) * NHEAD + warp) * 2] = m;
-            ml[(size_t(t) * NHEAD + warp) * 2 + 1] = l;
-        }
-    }
+    const size_t base = (size_t(t) * NHEAD + h) * nchunk;
+    float m = -INFINITY;
+    for (int c = tid; c < nc; c += 256) m = fmaxf(m, mpart[base + c]);
+    m = warp_max(m);
+    if (lane == 0) wred[warp] = m;
     __syncthreads();
-    for (int i = tid; i < WO_DIM; i += 1024) {
-        const int h = i / HEAD_DIM, d = i % HEAD_DIM;
-        const float *op = opart + (size_t(t) * NHEAD + h) * nchunk * HEAD_DIM + d;
-        const float *f = fsh + h * nchunk;
-        float o = 0.0f;
-        for (int c = 0; c < nc; c++) o = __fadd_rn(o, __fmul_rn(f[c], op[size_t(c) * HEAD_DIM]));
-        o = __fmul_rn(o, inv[h]);
-        const float g = z[size_t(t) * WO_DIM + i];
-        y[i] = __fmul_rn(o, 1.0f / (1.0f + expf(-g)));
+    m = wred[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) m = fmaxf(m, wred[w]);
+    float l = 0.0f;
+    for (int c = tid; c < nc; c += 256) {
+        const float f = expf(mpart[base + c] - m);
+        fsh[c] = f;
+        l = __fadd_rn(l, __fmul_rn(f, lpart[base + c]));
     }
+    l = warp_sum(l);
+    if (lane == 0) wsum[warp] = l;
     __syncthreads();
-    if (warp < WO_DIM / 256) {
-        const float4 a = *reinterpret_cast<const float4 *>(y + warp * 256 + lane * 8);
-        const float4 b = *reinterpret_cast<const float4 *>(y + warp * 256 + lane * 8 + 4);
+    l = ((wsum[0] + wsum[1]) + (wsum[2] + wsum[3])) + ((wsum[4] + wsum[5]) + (wsum[6] + wsum[7]));
+    if (tid == 0) {
+        ml[(size_t(t) * NHEAD + h) * 2] = m;
+        ml[(size_t(t) * NHEAD + h) * 2 + 1] = l;
+    }
+    const float *op = opart + base * HEAD_DIM + tid;
+    float o = 0.0f;
+    for (int c = 0; c < nc; c++) o = __fadd_rn(o, __fmul_rn(fsh[c], op[size_t(c) * HEAD_DIM]));
+    o = __fmul_rn(o, 1.0f / l);
+    const float g = z[size_t(t) * WO_DIM + h * HEAD_DIM + tid];
+    y[tid] = __fmul_rn(o, 1.0f / (1.0f + expf(-g)));
+    __syncthreads();
+    if (warp == 0) {
+        const float4 a = *reinterpret_cast<const float4 *>(y + lane * 8);
+        const float4 b = *reinterpret_cast<const float4 *>(y + lane * 8 + 4);
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        q8k_block_warp(v, lane, xq + size_t(t) * WO_DIM + warp * 256, xd + size_t(t) * 16 + warp,
-                       xs + size_t(t) * 256 + warp * 16);
+        q8k_block_warp(v, lane, xq + size_t(t) * WO_DIM + h * 256, xd + size_t(t) * 16 + h,
+                       xs + size_t(t) * 256 + h * 16);
     }
 }
 
@@ -546,27 +605,23 @@ int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
     const int nchunk = (a.nk_max + a.pv_chunk - 1) / a.pv_chunk;
-    QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), 0, st, 1, pdl_enabled(), a.qr,
+    static bool attr = false;
+    if (!attr) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(sizeof(ChunkSmem))));
+        attr = true;
+    }
+    QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), sizeof(ChunkSmem), st, 1, pdl_enabled(), a.qr,
                              a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk, a.scores, a.cmax,
                              a.lpart, a.opart));
     QMA_CHECK_LAUNCH();
-    const size_t fsh = sizeof(float) * NHEAD * size_t(nchunk);
+    const size_t fsh = sizeof(float) * size_t(nchunk);
     if (fsh > 48 * 1024) {
-        static bool raised = false;
-        if (!raised) {
-            QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_combine_kernel,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                160 * 1024));
-            raised = true;
-        }
-        if (fsh > 160 * 1024) {
-            set_error("attention: %d position chunks exceed the combine kernel's shared memory", nchunk);
-            return QMA_CUDA_ERR_UNSUPPORTED;
-        }
+        set_error("attention: %d position chunks exceed the combine kernel's shared memory", nchunk);
+        return QMA_CUDA_ERR_UNSUPPORTED;
     }
-    QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(a.T), dim3(1024), fsh, st, 1, pdl_enabled(), a.opart, a.cmax,
-                             a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs));
-    QMA_CHECK_LAUNCH();
+    QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(NHEAD, a.T), dim3(256), fsh, st, 1, pdl_enabled(), a.opart,
+                             a.cmax, a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs));
     return QMA_CUDA_OK;
 }
 

@@ -36,7 +36,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t st);
 int launch_salience(const AttnArgs &a, cudaStream_t st);
 // positions per chunk CTA for T queries over at most nk positions
 __host__ __device__ inline int attn_span(int T, int nk) {
-    return T > 1 ? 256 : (nk <= 1024 ? 16 : (nk <= 4096 ? 32 : 64));
+    return T > 1 ? 256 : (nk <= 1024 ? 16 : (nk <= 4096 ? 32 : (nk <= 16384 ? 64 : 128)));
 }
 int launch_arena_copy(const int2 *pairs, int n, uint8_t *const *kv, uint8_t *const *arena,
                       const float *sal, float *pin_sal, int n_ctx, cudaStream_t st);

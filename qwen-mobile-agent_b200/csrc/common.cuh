@@ -325,6 +325,14 @@ static inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, 
 // Programmatic dependent launch of the engine's kernels (on by default).
 bool pdl_enabled();
 
+// Byte ranges (weights) the first kernel of a layer asks L2 to fetch ahead
+// of the kernels that use them.
+struct Prefetch {
+    static constexpr int N = 6;
+    const void *p[N] = {};
+    size_t bytes[N] = {};
+};
+
 // ---------------------------------------------------------------- tracing --
 // Built with -DQMA_TRACE, every CTA of the forward kernels appends
 // {kernel id, CTA, entry ns, exit ns} (the GPU's global timer) to a device

@@ -659,6 +659,12 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
     }
 }
 
+// Whether the MoE block's last combining CTA also computes the next layer's
+// RMSNorm + Q8_K (saving a launch).  Measured slower in the decode pipeline:
+// it lengthens the MoE block's serial tail, which is on the critical path,
+// by more than the separate norm kernel costs.
+constexpr bool kFuseNextNorm = false;
+
 // The forward of T tokens at the positions in *sp_dev (host copy hs):
 // embedding -> 40 layers -> (optionally) final norm + LM head.
 static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
@@ -671,10 +677,10 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
     TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, tokens_dev, s->sp_dev, T, s->x, st));
     const int pv_chunk = attn_span(T, nk_cap);
     bool side_pending = false;     // a salience update is running on s->side
-    for (int il = 0; il < n_layers; il++) {
+    // a layer's output projection, router and shared expert go into L2
+    // while its input projection and mixer run
+    auto plan = [&](int il) {
         const LayerW &L = m->L[il];
-        // this layer's output projection, router and shared expert into L2
-        // while the input projection and the mixer run
         Prefetch pf;
         pf.p[0] = L.out_proj;
         pf.bytes[0] = packed_bytes(L.out_type, EMBD, is_attn(il) ? WO_DIM : VAL_DIM);
@@ -686,8 +692,24 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         pf.bytes[3] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
         pf.p[4] = L.moe.down_shexp;
         pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
-        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, pf));
-        TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st));
+        return pf;
+    };
+    bool normed = false;           // s->xq already holds this layer's normed input
+    for (int il = 0; il < n_layers; il++) {
+        const LayerW &L = m->L[il];
+        if (!normed) TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
+        normed = false;
+        // a single token's gated-delta-net conv runs in the input projection's epilogue
+        ConvEpi ce;
+        const bool conv_fused = !is_attn(il) && T == 1 && pdl_enabled();
+        if (conv_fused) {
+            ce.w = L.conv1d;
+            ce.state = s->conv[il];
+            ce.out = s->conv_out;
+            ce.n = CONV_DIM;
+        }
+        TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st, nullptr,
+                   conv_fused ? &ce : nullptr));
         if (is_attn(il)) {
             const int lay = il / 4;
             if (side_pending) {
@@ -714,7 +736,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
         } else {
             const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
-            TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
+            if (!conv_fused) TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
             TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
                            L.dt, L.a, s->ssm[il], T, s->gdo, st));
             TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
@@ -728,13 +750,25 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             break;
         }
         // x = x2 + moe(rms_norm(x2) * post_norm)
-        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false));
+        // the MoE block also produces the next layer's (or the LM head's) normed input
+        NextNorm nn;
+        if (kFuseNextNorm && pdl_enabled() && il + 1 < n_layers) {
+            nn.w = m->L[il + 1].attn_norm;
+            nn.pf = plan(il + 1);
+        } else if (kFuseNextNorm && pdl_enabled() && il == NLAYER - 1 && T == 1 && logits_mode) {
+            nn.w = m->out_norm;
+        }
+        nn.xq = s->xq;
+        nn.xd = s->xd;
+        nn.xs = s->xs;
+        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false, nn.w ? &nn : nullptr));
+        normed = nn.w != nullptr;
     }
     if (side_pending) QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
     if (logits_mode) {
         const int rows = logits_mode == 2 ? T : 1;
         const float *xin = logits_mode == 2 ? s->x : s->x + size_t(T - 1) * EMBD;
-        TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
+        if (!normed) TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
         TRY(matvec(m->out_type, m->out, EMBD, m->n_vocab, rows, s->xq, s->xd, s->xs, s->logits, st));
     }
 #undef TRY

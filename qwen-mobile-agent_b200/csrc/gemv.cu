@@ -65,7 +65,8 @@ __device__ unsigned g_gemv_timeouts;
 template <class F, int UPL>
 __device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in, int nr, const int8_t *xq,
                                               const float *xd, const int16_t *xsum, float *out,
-                                              const float *resid, int warp, int nwarps, int lane) {
+                                              const float *resid, int warp, int nwarps, int lane,
+                                              int row0, const ConvEpi &conv) {
     typename F::Act act[UPL];
 #pragma unroll
     for (int k = 0; k < UPL; k++) F::load_act(act[k], xq, xd, xsum, lane + 32 * k);
@@ -89,7 +90,23 @@ __device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in
         }
         const float tot = warp_sum8(v, lane);
         const int r = rb + idx;
-        if ((lane & 3) == 0 && r < r_end) out[r] = resid ? __fadd_rn(tot, resid[r]) : tot;
+        if ((lane & 3) == 0 && r < r_end) {
+            out[r] = resid ? __fadd_rn(tot, resid[r]) : tot;
+            if (r + row0 < conv.n) {
+                const int c = r + row0;
+                const float4 wc = *reinterpret_cast<const float4 *>(conv.w + size_t(c) * 4);
+                float *stc = conv.state + size_t(c) * 3;
+                const float s0 = stc[0], s1 = stc[1], s2 = stc[2];
+                float sum = __fmul_rn(s0, wc.x);
+                sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
+                sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
+                sum = __fadd_rn(sum, __fmul_rn(tot, wc.w));
+                conv.out[c] = sum / (1.0f + expf(-sum));
+                stc[0] = s1;
+                stc[1] = s2;
+                stc[2] = tot;
+            }
+        }
     }
 }
 
@@ -97,7 +114,7 @@ template <class F, int LPR, int UPL, int RU>
 __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int n_in, int n_out,
                                                           int rows_cta, const int8_t *xq,
                                                           const float *xd, const int16_t *xsum,
-                                                          float *out, const float *resid) {
+                                                          float *out, const float *resid, ConvEpi conv) {
     QMA_TRACE_SCOPE(TK_GEMV);
     extern __shared__ __align__(128) uint8_t wbuf[];
     __shared__ __align__(8) uint64_t bar;
@@ -124,7 +141,7 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
     const auto P = Stage<F>::view(wbuf, nr, n_in);
     if constexpr (LPR == 32)
         staged_rows32<F, UPL>(P, n_in, nr, xq, xd, xsum, out + r0, resid ? resid + r0 : nullptr, warp, nwarps,
-                              lane);
+                              lane, r0, conv);
     else
         gemv_warp_rows<SmemRows<F>, 1, LPR, UPL, RU>(P, n_in, nr, xq, xd, xsum, out + r0, 0, warp, nwarps,
                                                      lane, resid ? resid + r0 : nullptr);
@@ -145,7 +162,7 @@ constexpr uint32_t STAGED_MAX = 160 * 1024;    // shared memory per CTA for a st
 template <class F, int LPR, int UPL, int RU>
 static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
                          const float *xd, const int16_t *xsum, float *out, const float *resid,
-                         int rows_cta, uint32_t smem, cudaStream_t st) {
+                         int rows_cta, uint32_t smem, cudaStream_t st, const ConvEpi &conv) {
     static bool attr = false;
     if (!attr) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_staged_kernel<F, LPR, UPL, RU>,
@@ -159,7 +176,7 @@ static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const in
     // the SM for the next kernel's CTAs (the router) to start early
     const unsigned threads = rows_cta <= 64 ? 256 : 512;
     QMA_CHECK_CUDA(launch_ex(gemv_staged_kernel<F, LPR, UPL, RU>, dim3(unsigned(grid)), dim3(threads), smem, st, 1,
-                             pdl_enabled(), W, n_in, n_out, rows_cta, xq, xd, xsum, out, resid));
+                             pdl_enabled(), W, n_in, n_out, rows_cta, xq, xd, xsum, out, resid, conv));
     return QMA_CUDA_OK;
 }
 
@@ -222,18 +239,22 @@ static int dispatch_shape(const typename F::Ptr &W, int n_in, int n_out, const i
 // when it does not (the LM head streams through the register GEMV).
 template <class F>
 static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq, const float *xd,
-                       const int16_t *xsum, float *out, const float *resid, cudaStream_t st, int &rc) {
+                       const int16_t *xsum, float *out, const float *resid, cudaStream_t st, int &rc,
+                       const ConvEpi &conv) {
     int rows_cta = (n_out + num_sms() - 1) / num_sms();
     rows_cta = (rows_cta + 7) & ~7;
     const uint32_t smem = Stage<F>::bytes(rows_cta, n_in);
     if (smem > STAGED_MAX) return false;
     const int U = n_in / F::UNIT;
     switch (U) {
-    case 4: rc = launch_staged<F, 4, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
-    case 8: rc = launch_staged<F, 8, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
-    case 16: rc = launch_staged<F, 16, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
-    case 32: rc = launch_staged<F, 32, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
-    case 64: rc = launch_staged<F, 32, 2, 1>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st); return true;
+    case 4: if (conv.n) return false;
+        rc = launch_staged<F, 4, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st, conv); return true;
+    case 8: if (conv.n) return false;
+        rc = launch_staged<F, 8, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st, conv); return true;
+    case 16: if (conv.n) return false;
+        rc = launch_staged<F, 16, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st, conv); return true;
+    case 32: rc = launch_staged<F, 32, 1, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st, conv); return true;
+    case 64: rc = launch_staged<F, 32, 2, 1>(W, n_in, n_out, xq, xd, xsum, out, resid, rows_cta, smem, st, conv); return true;
     default: return false;
     }
 }
@@ -241,9 +262,13 @@ static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8
 template <class F, int TMAX>
 static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, const int8_t *xq,
                        const float *xd, const int16_t *xsum, float *out, const float *resid,
-                       cudaStream_t st) {
+                       cudaStream_t st, const ConvEpi &conv) {
     int rc;
-    if (T == 1 && pdl_enabled() && try_staged<F>(W, n_in, n_out, xq, xd, xsum, out, resid, st, rc)) return rc;
+    if (T == 1 && pdl_enabled() && try_staged<F>(W, n_in, n_out, xq, xd, xsum, out, resid, st, rc, conv)) return rc;
+    if (conv.n) {
+        set_error("matvec: the conv epilogue needs the single-token staged path");
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
     int t0 = 0;
     while (t0 < T) {
         const int rem = T - t0;
@@ -277,17 +302,18 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
 
 int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
            const float *xd, const int16_t *xsum, float *out, cudaStream_t st,
-           const float *resid) {
+           const float *resid, const ConvEpi *conv) {
+    const ConvEpi ce = conv ? *conv : ConvEpi();
     switch (wtype) {
     case QMA_TYPE_Q4_K:
         return gemv_tokens<FmtQ4K, 4>(static_cast<const uint8_t *>(W), n_in, n_out, T, xq, xd,
-                                      xsum, out, resid, st);
+                                      xsum, out, resid, st, ce);
     case QMA_TYPE_Q6_K:
         return gemv_tokens<FmtQ6K, 2>(q6_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
-                                      out, resid, st);
+                                      out, resid, st, ce);
     case QMA_TYPE_Q8_0:
         return gemv_tokens<FmtQ80, 4>(q8_planes(W, n_out, n_in), n_in, n_out, T, xq, xd, xsum,
-                                      out, resid, st);
+                                      out, resid, st, ce);
     default:
         set_error("matvec: unsupported weight type %d", wtype);
         return QMA_CUDA_ERR_UNSUPPORTED;

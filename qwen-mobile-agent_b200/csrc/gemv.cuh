@@ -364,11 +364,22 @@ __device__ __forceinline__ void gemv_warp_rows(const typename F::Ptr &W, int n_i
     }
 }
 
+// Optional epilogue of a single-token GEMV over the gated delta net's input
+// projection: rows r < n are also the causal conv's channels (conv1d_layer
+// + SiLU, nn.c:717-741 / nn.c:2196), applied in the row's own thread with
+// the same operation order as the conv kernel.
+struct ConvEpi {
+    const float *w = nullptr;     // [n][4] taps
+    float *state = nullptr;       // [n][3] last three inputs
+    float *out = nullptr;         // [n] silu(conv)
+    int n = 0;
+};
+
 // Host launcher (gemv.cu): out[t][r] = <W[r], x_t> (+ resid[t][r]).  W is
 // the packed matrix; T tokens are processed in passes of 4/2/1.
 int matvec(int wtype, const void *W, int n_in, int n_out, int T, const int8_t *xq,
            const float *xd, const int16_t *xsum, float *out, cudaStream_t st,
-           const float *resid = nullptr);
+           const float *resid = nullptr, const ConvEpi *conv = nullptr);
 int num_sms();
 // Bounded waits of the staged GEMV that ran out since the last call.
 int gemv_wait_timeouts();

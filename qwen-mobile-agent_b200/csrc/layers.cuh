@@ -52,13 +52,6 @@ struct StepParams {
 // tokens: device [T] ids, or null to read StepParams::token (T = 1)
 int launch_embed(const void *embd, int type, int n_vocab, const int *tokens,
                  const StepParams *sp, int T, float *x, cudaStream_t st);
-// Byte ranges (weights) the first kernel of a layer asks L2 to fetch ahead
-// of the kernels that use them.
-struct Prefetch {
-    static constexpr int N = 6;
-    const void *p[N] = {};
-    size_t bytes[N] = {};
-};
 int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *xq, float *xd,
                          int16_t *xs, cudaStream_t st, const Prefetch &pf = Prefetch());
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,

@@ -590,7 +590,7 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
                                                          size_t down_bytes,
                                                          const uint8_t *__restrict__ down_sh,
                                                          const float *x2, float *x_out,
-                                                         MoeScratch s) {
+                                                         MoeScratch s, NextNorm nn) {
     QMA_TRACE_SCOPE(TK_EXPERT);
     extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
@@ -604,7 +604,8 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
     __shared__ __align__(16) int8_t hq[MOE_FF];
     __shared__ float hd[MOE_FF / 256];
     __shared__ int16_t hs[MOE_FF / 16];
-    __shared__ int is_last;
+    __shared__ int is_last, is_last2;
+    __shared__ double nred[8];
     const int g0 = int(rank) * XGU, d0 = int(rank) * XDN;
     if (tid == 0) {
         mbar_init(&bar[0], 1);
@@ -718,6 +719,42 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
             x_out[size_t(t) * MOE_EMBD + r] = __fadd_rn(acc, x2[size_t(t) * MOE_EMBD + r]);
         }
         if (tid == 0) s.dcount[t * MOE_DOWN_CHUNKS + rank] = 0;
+        if (nn.w) {
+            // the last of the token's MOE_DOWN_CHUNKS combiners normalizes it
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) is_last2 = atomicAdd(&s.rcount[t], 1u) == MOE_DOWN_CHUNKS - 1;
+            __syncthreads();
+            if (is_last2) {
+                __threadfence();
+                float v[8];
+                if (tid < 256) {
+                    const float4 *p = reinterpret_cast<const float4 *>(x_out + size_t(t) * MOE_EMBD + tid * 8);
+                    const float4 a = __ldcg(p), b = __ldcg(p + 1);
+                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                    double ss = 0.0;
+#pragma unroll
+                    for (int k = 0; k < 8; k++) ss += double(v[k]) * double(v[k]);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                    if (lane == 0) nred[warp] = ss;
+                }
+                __syncthreads();
+                if (tid < 256) {
+                    const double tot = ((nred[0] + nred[1]) + (nred[2] + nred[3])) + ((nred[4] + nred[5]) + (nred[6] + nred[7]));
+                    const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
+                    const float4 wa = *reinterpret_cast<const float4 *>(nn.w + tid * 8);
+                    const float4 wb = *reinterpret_cast<const float4 *>(nn.w + tid * 8 + 4);
+                    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], r), wv[k]);
+                    q8k_block_warp(v, lane, nn.xq + size_t(t) * MOE_EMBD + warp * 256, nn.xd + size_t(t) * 8 + warp,
+                                   nn.xs + size_t(t) * 128 + warp * 16);
+                }
+                if (t == 0 && tid < Prefetch::N && nn.pf.p[tid]) prefetch_l2_range(nn.pf.p[tid], nn.pf.bytes[tid]);
+                if (tid == 0) s.rcount[t] = 0;
+            }
+        }
     }
 }
 
@@ -734,7 +771,8 @@ int moe_wait_timeouts() {
 static bool g_moe_attrs = false;
 
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters) {
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters, const NextNorm *nnp) {
+    const NextNorm nn = nnp ? *nnp : NextNorm();
     MoeScratch s = moe_scratch_layout(scratch, T);
     if (!g_moe_attrs) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -749,8 +787,10 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
         g_moe_attrs = true;
     }
-    if (clear_counters)
+    if (clear_counters) {
         QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
+        QMA_CHECK_CUDA(cudaMemsetAsync(s.rcount, 0, sizeof(unsigned) * T, st));
+    }
     const bool pdl = pdl_enabled() && !clear_counters;
     QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(256), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
                              w.gate_inp, w.gate_inp_shexp, s, sel, wts));
@@ -761,10 +801,10 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, nn));
     else
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, nn));
     return QMA_CUDA_OK;
 }
 

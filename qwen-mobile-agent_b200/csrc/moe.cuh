@@ -18,7 +18,7 @@ constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
 // carves one caller-provided buffer).  The combine tickets (dcount) must be
 // zero when a call starts; every call leaves them zero again.
 struct MoeScratch {
-    unsigned *rcount;      // [T] unused (kept for the scratch layout)
+    unsigned *rcount;      // [T] output chunks finished (fused next norm)
     unsigned *dcount;      // [T][16] down CTAs finished per output chunk
     double *S, *B;         // [T][256] exact logit, bound on the fp32 logit
     int *fallback;         // [T] 1 if the exact sequential recompute ran
@@ -38,8 +38,20 @@ MoeScratch moe_scratch_layout(void *base, int T);
 // the engine's own scratch starts zeroed and every call leaves it zeroed, so
 // it skips the memset and launches the router with programmatic dependent
 // launch.
+// Optional fusion of the next RMSNorm into the MoE block: when w is set, the
+// last CTA to finish a token's output also computes rms_norm(x_out) * w and
+// its Q8_K blocks (the next matmul's input, rms_norm_m nn.c:348-357 +
+// nn.c:318-324, same arithmetic as the standalone kernel) and issues pf.
+struct NextNorm {
+    const float *w = nullptr;
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int16_t *xs = nullptr;
+    Prefetch pf;
+};
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters);
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters,
+              const NextNorm *nn = nullptr);
 // Bounded waits of the expert kernel that ran out since the last call (reset
 // by reading); -1 if the counter cannot be read.
 int moe_wait_timeouts();
