@@ -336,9 +336,9 @@ def run_decode_reference(args, world, rank):
 GN_OUT, GN_IN = 151936, 2048
 
 
-def gemv_bytes():
-    w = GN_OUT * (GN_IN // 256) * 144
-    return w + GN_IN * 4 + GN_IN + (GN_IN // 256) * 4 + (GN_IN // 16) * 2 + GN_OUT * 4
+def gemv_bytes(rows=GN_OUT, cols=GN_IN):
+    w = rows * (cols // 256) * 144
+    return w + cols * 4 + cols + (cols // 256) * 4 + (cols // 16) * 2 + rows * 4
 
 
 def run_gemv_ours(args, world, rank, local):
@@ -346,6 +346,7 @@ def run_gemv_ours(args, world, rank, local):
     import oracle as O
     import qma_cuda as Q
     Q.init(local)
+    GN_OUT, GN_IN = args.rows, args.cols
     dev = torch.device("cuda", local)
     W = O.synth_matrix("bench.lm_head", Q4_K, GN_OUT, GN_IN, seed=0)
     x = np.random.default_rng(rank).standard_normal((1, GN_IN)).astype(np.float32)
@@ -395,7 +396,7 @@ def run_gemv_ours(args, world, rank, local):
         torch.cuda.synchronize()
         e2e_ms += e0.elapsed_time(e1)
     e2e_ms = dist_max(e2e_ms, world)
-    b = gemv_bytes()
+    b = gemv_bytes(GN_OUT, GN_IN)
     peak, peak_kind = load_peaks()
     achieved = b / (gemv_ms / args.steps / 1e3) / 1e9
     if rank != 0:
@@ -405,11 +406,13 @@ def run_gemv_ours(args, world, rank, local):
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8xq4", "data": "synthetic",
-        "config": {"workload": "configs[1] Q4_K GEMV 151936x2048, batch 1",
+        "config": {"workload": f"{'configs[1] ' if (GN_OUT, GN_IN) == (151936, 2048) else ''}Q4_K GEMV {GN_OUT}x{GN_IN}, batch 1",
                    "l2": "256 MB L2 flush between timed steps", "base_metric": BASE_METRIC},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "gemv_kernel<FmtQ4K,1,32,1,2>", "algorithmic_bytes_per_launch": b},
+                     "kernel": "gemv_kernel<FmtQ4K,1,32,1,4> (register path)" if GN_OUT * GN_IN // 256 * 144 > 148 * 160 * 1024
+                               else "gemv_staged_kernel<FmtQ4K,32,1,2> (rows staged in shared memory)",
+                     "algorithmic_bytes_per_launch": b},
         "e2e": {"value": round(world * b * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": GN_IN * 4, "d2h_bytes_per_step": GN_OUT * 4},
         "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
@@ -425,6 +428,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--rows", type=int, default=GN_OUT, help="gemv: output rows")
+    ap.add_argument("--cols", type=int, default=GN_IN, help="gemv: input columns (multiple of 256)")
     ap.add_argument("--prompt", type=int, default=PROMPT,
                     help="decode: prompt tokens prefilled before the timed steps")
     args = ap.parse_args()
