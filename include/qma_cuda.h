@@ -62,9 +62,12 @@ int qma_cuda_q8k_quant(const float *x, int rows, int n, int8_t *xq, float *xd,
  * 16-byte aligned).  Q6_K (210 B blocks) and Q8_0 (34 B blocks) are not
  * 16-byte aligned, so they are repacked once, at load time, into planes per
  * matrix: Q6_K -> [ql rows*n/2][qh rows*n/4][scales rows*n/16][d rows*n/256
- * fp16]; Q8_0 -> [q rows*n][d rows*n/32 fp16].  Byte-for-byte the same
- * values; only their order changes (the reference's own load-time repack is
- * qma_align_model, gguf.c:674).  qma_cuda_packed_bytes() gives the size of a
+ * fp16]; Q8_0 -> [q rows*n][d rows*n/32 fp16].  Within each (row,
+ * super-block) of the ql and qh planes the 16-byte chunks are permuted
+ * (chunk c of segment s = row*(n/256)+sb at c ^ (s & 3) in ql, c ^ ((s>>1) & 1)
+ * in qh) so that warps read them from shared memory without bank conflicts.
+ * Byte-for-byte the same values; only their order changes (the reference's
+ * own load-time repack is qma_align_model, gguf.c:674).  qma_cuda_packed_bytes() gives the size of a
  * packed matrix (equal to the GGUF size, rounded up to 16 per plane). */
 size_t qma_cuda_packed_bytes(int wtype, int rows, int n);
 /* src: device GGUF-layout matrix [rows][n]; dst: device packed buffer of

@@ -37,7 +37,8 @@ size_t packed_bytes(int wtype, int rows, int n) {
     }
 }
 
-// GGUF Q6_K block (ql[128] qh[64] scales[16] d) -> planes; one thread/block.
+// GGUF Q6_K block (ql[128] qh[64] scales[16] d) -> planes, ql/qh chunks
+// swizzled (q6_ql_chunk / q6_qh_chunk); one thread per block.
 __global__ void repack_q6k_kernel(const uint8_t *__restrict__ src, int rows, int n,
                                   uint8_t *ql, uint8_t *qh, int8_t *sc, __half *d) {
     const int nb = n / QK;
@@ -49,8 +50,9 @@ __global__ void repack_q6k_kernel(const uint8_t *__restrict__ src, int rows, int
         uint8_t *oql = ql + r * (n / 2) + b * 128;
         uint8_t *oqh = qh + r * (n / 4) + b * 64;
         int8_t *osc = sc + r * (n / 16) + b * 16;
-        for (int k = 0; k < 128; k++) oql[k] = s[k];
-        for (int k = 0; k < 64; k++) oqh[k] = s[128 + k];
+        const int seg = int(i & 0x7fffffff);   // only s mod 4 matters
+        for (int k = 0; k < 128; k++) oql[(q6_ql_chunk(k >> 4, seg) << 4) | (k & 15)] = s[k];
+        for (int k = 0; k < 64; k++) oqh[(q6_qh_chunk(k >> 4, seg) << 4) | (k & 15)] = s[128 + k];
         for (int k = 0; k < 16; k++) osc[k] = static_cast<int8_t>(s[192 + k]);
         d[r * nb + b] = __ushort_as_half(uint16_t(s[208] | (s[209] << 8)));
     }

@@ -68,6 +68,17 @@ __host__ __device__ inline size_t q6_plane_qh(int rows, int n) { return size_t(r
 __host__ __device__ inline size_t q6_plane_sc(int rows, int n) { return size_t(rows) * n / 16; }
 __host__ __device__ inline size_t q6_plane_d(int rows, int n) { return size_t(rows) * (n / 256) * 2; }
 
+// Q6_K plane swizzle.  A segment is one (row, super-block) of a plane:
+// 128 B of ql (8 chunks of 16 B), 64 B of qh (4 chunks); s = row * (n/256)
+// + sb numbers the segments.  Chunk c of a ql segment is stored at chunk
+// c ^ (s & 3), chunk c of a qh segment at c ^ ((s >> 1) & 1).  The 8 lanes of
+// a quarter warp that read the same chunk of their unit from 4 consecutive
+// segments then hit 8 different 16-byte bank groups of shared memory (a
+// plain layout puts them on 2).  The key depends on s mod 4 only, so a copy
+// of rows r0.. with r0 * (n/256) a multiple of 4 keeps it.
+__host__ __device__ inline int q6_ql_chunk(int c, int s) { return c ^ (s & 3); }
+__host__ __device__ inline int q6_qh_chunk(int c, int s) { return c ^ ((s >> 1) & 1); }
+
 inline Q6Planes q6_planes(const void *base, int rows, int n) {
     const uint8_t *p = static_cast<const uint8_t *>(base);
     Q6Planes P;
@@ -155,6 +166,24 @@ __device__ __forceinline__ float warp_sum8(const float (&v)[8], int lane) {
     }
     const bool h4 = lane & 4;
     float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
+}
+// Four warp-wide sums at once (6 shuffles): afterwards lane l holds the sum
+// over the warp of v[warp_sum4_index(l)].
+__device__ __forceinline__ int warp_sum4_index(int lane) { return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1); }
+__device__ __forceinline__ float warp_sum4(const float (&v)[4], int lane) {
+    float a[2];
+    const bool h16 = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float mine = h16 ? v[2 + i] : v[i], other = h16 ? v[i] : v[2 + i];
+        a[i] = mine + __shfl_xor_sync(0xffffffffu, other, 16);
+    }
+    const bool h8 = lane & 8;
+    float c = (h8 ? a[1] : a[0]) + __shfl_xor_sync(0xffffffffu, h8 ? a[0] : a[1], 8);
+    c += __shfl_xor_sync(0xffffffffu, c, 4);
     c += __shfl_xor_sync(0xffffffffu, c, 2);
     c += __shfl_xor_sync(0xffffffffu, c, 1);
     return c;

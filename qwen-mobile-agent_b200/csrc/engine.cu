@@ -659,12 +659,6 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
     }
 }
 
-// Whether the MoE block's last combining CTA also computes the next layer's
-// RMSNorm + Q8_K (saving a launch).  Measured slower in the decode pipeline:
-// it lengthens the MoE block's serial tail, which is on the critical path,
-// by more than the separate norm kernel costs.
-constexpr bool kFuseNextNorm = false;
-
 // The forward of T tokens at the positions in *sp_dev (host copy hs):
 // embedding -> 40 layers -> (optionally) final norm + LM head.
 static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
@@ -694,11 +688,9 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
         return pf;
     };
-    bool normed = false;           // s->xq already holds this layer's normed input
     for (int il = 0; il < n_layers; il++) {
         const LayerW &L = m->L[il];
-        if (!normed) TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
-        normed = false;
+        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
         // a single token's gated-delta-net conv runs in the input projection's epilogue
         ConvEpi ce;
         const bool conv_fused = !is_attn(il) && T == 1 && pdl_enabled();
@@ -750,25 +742,13 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
             break;
         }
         // x = x2 + moe(rms_norm(x2) * post_norm)
-        // the MoE block also produces the next layer's (or the LM head's) normed input
-        NextNorm nn;
-        if (kFuseNextNorm && pdl_enabled() && il + 1 < n_layers) {
-            nn.w = m->L[il + 1].attn_norm;
-            nn.pf = plan(il + 1);
-        } else if (kFuseNextNorm && pdl_enabled() && il == NLAYER - 1 && T == 1 && logits_mode) {
-            nn.w = m->out_norm;
-        }
-        nn.xq = s->xq;
-        nn.xd = s->xd;
-        nn.xs = s->xs;
-        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false, nn.w ? &nn : nullptr));
-        normed = nn.w != nullptr;
+        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false));
     }
     if (side_pending) QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
     if (logits_mode) {
         const int rows = logits_mode == 2 ? T : 1;
         const float *xin = logits_mode == 2 ? s->x : s->x + size_t(T - 1) * EMBD;
-        if (!normed) TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
+        TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
         TRY(matvec(m->out_type, m->out, EMBD, m->n_vocab, rows, s->xq, s->xd, s->xs, s->logits, st));
     }
 #undef TRY

@@ -121,25 +121,31 @@ struct FmtQ6K {
         prefetch_l2_range(P.sc + size_t(r0) * (n_in / 16), size_t(nrows) * (n_in / 16));
         prefetch_l2_range(P.d + size_t(r0) * (n_in / 256), size_t(nrows) * (n_in / 256) * 2);
     }
+    // unit u = (sb, half j) of a row: ql chunks 4j..4j+3 and qh chunks 2j, 2j+1
+    // of segment s = row * (n_in/256) + sb, at their swizzled places
     __device__ static void load_w(Wt &w, const Ptr &P, int row, int n_in, int u) {
-        const int sb = u >> 1, j = u & 1;
-        const uint8_t *ql = P.ql + size_t(row) * (n_in / 2) + sb * 128 + j * 64;
-        const uint8_t *qh = P.qh + size_t(row) * (n_in / 4) + sb * 64 + j * 32;
-        w.l0 = ld_stream16(ql);
-        w.l1 = ld_stream16(ql + 16);
-        w.l2 = ld_stream16(ql + 32);
-        w.l3 = ld_stream16(ql + 48);
-        w.h0 = ld_stream16(qh);
-        w.h1 = ld_stream16(qh + 16);
+        const int sb = u >> 1, j = u & 1, s = row * (n_in / 256) + sb;
+        const uint8_t *ql = P.ql + size_t(row) * (n_in / 2) + sb * 128;
+        const uint8_t *qh = P.qh + size_t(row) * (n_in / 4) + sb * 64;
+        w.l0 = ld_stream16(ql + 16 * q6_ql_chunk(4 * j, s));
+        w.l1 = ld_stream16(ql + 16 * q6_ql_chunk(4 * j + 1, s));
+        w.l2 = ld_stream16(ql + 16 * q6_ql_chunk(4 * j + 2, s));
+        w.l3 = ld_stream16(ql + 16 * q6_ql_chunk(4 * j + 3, s));
+        w.h0 = ld_stream16(qh + 16 * q6_qh_chunk(2 * j, s));
+        w.h1 = ld_stream16(qh + 16 * q6_qh_chunk(2 * j + 1, s));
         w.sc = ld_stream8(P.sc + size_t(row) * (n_in / 16) + sb * 16 + j * 8);
         w.d = ld_stream2(P.d + size_t(row) * (n_in / 256) + sb);
     }
     __device__ static void load_w_smem(Wt &w, const Ptr &P, int row, int n_in, int u) {
-        const int sb = u >> 1, j = u & 1;
-        const uint4 *ql = reinterpret_cast<const uint4 *>(P.ql + size_t(row) * (n_in / 2) + sb * 128 + j * 64);
-        const uint4 *qh = reinterpret_cast<const uint4 *>(P.qh + size_t(row) * (n_in / 4) + sb * 64 + j * 32);
-        w.l0 = ql[0]; w.l1 = ql[1]; w.l2 = ql[2]; w.l3 = ql[3];
-        w.h0 = qh[0]; w.h1 = qh[1];
+        const int sb = u >> 1, j = u & 1, s = row * (n_in / 256) + sb;
+        const uint8_t *ql = P.ql + size_t(row) * (n_in / 2) + sb * 128;
+        const uint8_t *qh = P.qh + size_t(row) * (n_in / 4) + sb * 64;
+        w.l0 = *reinterpret_cast<const uint4 *>(ql + 16 * q6_ql_chunk(4 * j, s));
+        w.l1 = *reinterpret_cast<const uint4 *>(ql + 16 * q6_ql_chunk(4 * j + 1, s));
+        w.l2 = *reinterpret_cast<const uint4 *>(ql + 16 * q6_ql_chunk(4 * j + 2, s));
+        w.l3 = *reinterpret_cast<const uint4 *>(ql + 16 * q6_ql_chunk(4 * j + 3, s));
+        w.h0 = *reinterpret_cast<const uint4 *>(qh + 16 * q6_qh_chunk(2 * j, s));
+        w.h1 = *reinterpret_cast<const uint4 *>(qh + 16 * q6_qh_chunk(2 * j + 1, s));
         w.sc = *reinterpret_cast<const uint2 *>(P.sc + size_t(row) * (n_in / 16) + sb * 16 + j * 8);
         w.d = *reinterpret_cast<const uint16_t *>(P.d + size_t(row) * (n_in / 256) + sb);
     }

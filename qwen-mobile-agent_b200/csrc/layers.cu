@@ -64,8 +64,9 @@ __global__ void __launch_bounds__(256) embed_q6k_kernel(Q6Planes P, const int *t
     const int tok = tokens ? tokens[t] : sp->token;
     const int i0 = threadIdx.x * 8;
     const int sb = i0 / 256, half = (i0 % 256) / 128;
-    const uint8_t *ql = P.ql + size_t(tok) * (EMBD / 2) + sb * 128 + half * 64;
-    const uint8_t *qh = P.qh + size_t(tok) * (EMBD / 4) + sb * 64 + half * 32;
+    const int seg = tok * (EMBD / 256) + sb;
+    const uint8_t *ql = P.ql + size_t(tok) * (EMBD / 2) + sb * 128;
+    const uint8_t *qh = P.qh + size_t(tok) * (EMBD / 4) + sb * 64;
     const int8_t *sc = P.sc + size_t(tok) * (EMBD / 16) + sb * 16 + half * 8;
     const float d = __half2float(P.d[size_t(tok) * (EMBD / 256) + sb]);
     float *o = x + size_t(t) * EMBD + i0;
@@ -73,8 +74,11 @@ __global__ void __launch_bounds__(256) embed_q6k_kernel(Q6Planes P, const int *t
     for (int k = 0; k < 8; k++) {
         const int w = (i0 % 128) + k;
         const int L = w & 63, hi = w >> 6;
-        const int lo4 = hi ? (ql[L] >> 4) : (ql[L] & 0xF);
-        const int h2 = (qh[L & 31] >> (2 * ((L >> 5) + 2 * hi))) & 3;
+        const int bl = half * 64 + L, bh = half * 32 + (L & 31);   // bytes of the segment
+        const uint8_t qlb = ql[(q6_ql_chunk(bl >> 4, seg) << 4) | (bl & 15)];
+        const uint8_t qhb = qh[(q6_qh_chunk(bh >> 4, seg) << 4) | (bh & 15)];
+        const int lo4 = hi ? (qlb >> 4) : (qlb & 0xF);
+        const int h2 = (qhb >> (2 * ((L >> 5) + 2 * hi))) & 3;
         const int q = (lo4 | (h2 << 4)) - 32;
         o[k] = __fmul_rn(__fmul_rn(d, float(sc[w / 16])), float(q));
     }
@@ -109,7 +113,12 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ double red[8];
     pdl_trigger();
-    if (t == 0 && tid < Prefetch::N && pf.p[tid]) prefetch_l2_range(pf.p[tid], pf.bytes[tid]);
+    if (t == 0) {
+        // constant indices keep the parameter array out of local memory
+#pragma unroll
+        for (int i = 0; i < Prefetch::N; i++)
+            if (tid == i && pf.p[i]) prefetch_l2_range(pf.p[i], pf.bytes[i]);
+    }
     pdl_wait();
     const float4 *p = reinterpret_cast<const float4 *>(x + size_t(t) * EMBD + tid * 8);
     const float4 a = p[0], b = p[1];

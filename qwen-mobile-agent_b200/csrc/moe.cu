@@ -33,7 +33,6 @@ static inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t moe_scratch_bytes(int T) {
     size_t b = 0;
-    b += al256(sizeof(unsigned) * T);                     // rcount
     b += al256(sizeof(unsigned) * T * MOE_DOWN_CHUNKS);   // dcount
     b += al256(sizeof(double) * T * MOE_NEXP) * 2;        // S, B
     b += al256(sizeof(int) * T);                          // fallback
@@ -43,7 +42,6 @@ size_t moe_scratch_bytes(int T) {
     b += al256(sizeof(float) * T * (MOE_EMBD / 256));     // xd
     b += al256(sizeof(int16_t) * T * (MOE_EMBD / 16));    // xs
     b += al256(sizeof(float) * T);                        // gs
-    b += al256(sizeof(float) * T * MOE_NSLOT * MOE_FF);   // h
     b += al256(sizeof(float) * T * MOE_NSLOT * MOE_EMBD); // part
     return b;
 }
@@ -52,7 +50,6 @@ MoeScratch moe_scratch_layout(void *base, int T) {
     uint8_t *p = static_cast<uint8_t *>(base);
     MoeScratch s;
     auto take = [&](size_t n) { uint8_t *q = p; p += al256(n); return q; };
-    s.rcount = reinterpret_cast<unsigned *>(take(sizeof(unsigned) * T));
     s.dcount = reinterpret_cast<unsigned *>(take(sizeof(unsigned) * T * MOE_DOWN_CHUNKS));
     s.S = reinterpret_cast<double *>(take(sizeof(double) * T * MOE_NEXP));
     s.B = reinterpret_cast<double *>(take(sizeof(double) * T * MOE_NEXP));
@@ -63,7 +60,6 @@ MoeScratch moe_scratch_layout(void *base, int T) {
     s.xd = reinterpret_cast<float *>(take(sizeof(float) * T * (MOE_EMBD / 256)));
     s.xs = reinterpret_cast<int16_t *>(take(sizeof(int16_t) * T * (MOE_EMBD / 16)));
     s.gs = reinterpret_cast<float *>(take(sizeof(float) * T));
-    s.h = reinterpret_cast<float *>(take(sizeof(float) * T * MOE_NSLOT * MOE_FF));
     s.part = reinterpret_cast<float *>(take(sizeof(float) * T * MOE_NSLOT * MOE_EMBD));
     return s;
 }
@@ -174,17 +170,19 @@ __device__ bool select_top8(const double *sS, const double *sB, const int *cls, 
 // (nn.c:519-521).  With a_i = fl(g_i * x_i) (the same products) and S_i the
 // exact prefix sums, recursive summation satisfies |s_fp32 - S_n| <= u'
 // sum_i |S_i| with u' = 2^-24 (1 + n u) for n = 2048.  S_n is summed in fp64
-// (error ~1e-13 relative); sum_i |S_i| from fp32 prefix sums in the natural
-// order (a warp scan per 128-element chunk), whose own error (< 1e-3
-// relative) the 1.01 factor covers.
+// (error ~1e-13 relative).  sum_i |S_i| is bounded group by group: a lane's
+// four elements start at prefix Q (a warp scan per 128-element chunk) and
+//   sum_{i<4} |Q + a_0 + .. + a_i| <= 4|Q| + 4|a_0| + 3|a_1| + 2|a_2| + |a_3|.
+// The fp32 prefixes come from sums at most ~30 additions deep (error
+// <= 2e-6 sum|a|, under 0.1% of the bound, which is >= 4 sum|a|); the 1.01
+// factor covers that and the (1 + n u) term.
 __device__ __forceinline__ void router_logit(const float *row, const float *xn, int lane, double &S,
                                              double &B) {
     double t4[4] = {0.0, 0.0, 0.0, 0.0};
     float P = 0.0f, el = 0.0f;        // P: prefix of the previous chunks
 #pragma unroll
     for (int h = 0; h < 2; h++) {     // chunks 8 h .. 8 h + 7
-        // pass 1: the fp64 sum and the chunks' lane sums
-        float c[8];
+        float c[8], wa[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
             const int o = 128 * (8 * h + k) + 4 * lane;
@@ -197,6 +195,7 @@ __device__ __forceinline__ void router_logit(const float *row, const float *xn, 
             t4[2] += double(a2);
             t4[3] += double(a3);
             c[k] = (a0 + a1) + (a2 + a3);
+            wa[k] = (4.0f * fabsf(a0) + 3.0f * fabsf(a1)) + (2.0f * fabsf(a2) + fabsf(a3));
         }
         // inclusive scan of the lane sums within each chunk (8 independent scans)
         float incl[8];
@@ -209,21 +208,10 @@ __device__ __forceinline__ void router_logit(const float *row, const float *xn, 
                 const float v = __shfl_up_sync(0xffffffffu, incl[k], o);
                 if (lane >= o) incl[k] += v;
             }
-        // pass 2: the prefix sums in natural order (products recomputed)
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const int o = 128 * (8 * h + k) + 4 * lane;
-            const float4 g = *reinterpret_cast<const float4 *>(row + o);
-            const float4 x = *reinterpret_cast<const float4 *>(xn + o);
-            float p = P + (incl[k] - c[k]);
-            p += __fmul_rn(g.x, x.x);
-            el += fabsf(p);
-            p += __fmul_rn(g.y, x.y);
-            el += fabsf(p);
-            p += __fmul_rn(g.z, x.z);
-            el += fabsf(p);
-            p += __fmul_rn(g.w, x.w);
-            el += fabsf(p);
+            const float q = P + (incl[k] - c[k]);       // prefix before this lane's group
+            el += 4.0f * fabsf(q) + wa[k];
             P += __shfl_sync(0xffffffffu, incl[k], 31);
         }
     }
@@ -232,13 +220,14 @@ __device__ __forceinline__ void router_logit(const float *row, const float *xn, 
     B = double(E) * 0x1.0p-24 * 1.01 + 1e-30;
 }
 
-// Leader-side ranking of the 256 logits (256 threads, thread = expert):
-// top9[r] = the expert of rank r < 9 under (S descending, id ascending),
-// ranked on S rounded to fp32.  Two logits that fp32 rounding could tie or
-// misorder are within one fp32 ulp of each other, far inside the margin
-// top_settled() demands between ranks, so such a ranking is never accepted.
-// Each warp sorts its 32 keys (sortable fp32 bits, then inverted id) with a
-// bitonic network in registers; the 8 warps' top 9 are ranked by counting.
+// Leader-side ranking of the 256 logits (threads 0..255 = experts; the
+// other threads of the CTA only take part in the barriers): top9[r] = the
+// expert of rank r < 9 under (S descending, id ascending), ranked on S
+// rounded to fp32.  Two logits that fp32 rounding could tie or misorder are
+// within one fp32 ulp of each other, far inside the margin top_settled()
+// demands between ranks, so such a ranking is never accepted.  Each warp
+// sorts its 32 keys (sortable fp32 bits, then inverted id) with a bitonic
+// network in registers; the 8 warps' top 9 are ranked by counting.
 // dred[0] receives the largest S + B among the unselected (rank >= 8).
 __device__ __forceinline__ unsigned long long rank_key(double S, int e) {
     uint32_t u = __float_as_uint(float(S));
@@ -247,17 +236,20 @@ __device__ __forceinline__ unsigned long long rank_key(double S, int e) {
 }
 __device__ __forceinline__ void rank_top(const double *sS, const double *sB, unsigned long long *cand,
                                          int tid, int lane, int warp, double *dred, int *top9) {
-    unsigned long long key = rank_key(sS[tid], tid);
+    const bool mine = tid < MOE_NEXP;              // warp-uniform
+    if (mine) {
+        unsigned long long key = rank_key(sS[tid], tid);
 #pragma unroll
-    for (int k = 2; k <= 32; k <<= 1)
+        for (int k = 2; k <= 32; k <<= 1)
 #pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, j);
-            const bool desc = (lane & k) == 0 || k == 32;
-            const bool low = (lane & j) == 0;
-            key = (low == desc) ? (key > o ? key : o) : (key < o ? key : o);
-        }
-    if (lane <= MOE_TOPK) cand[warp * (MOE_TOPK + 1) + lane] = key;
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, j);
+                const bool desc = (lane & k) == 0 || k == 32;
+                const bool low = (lane & j) == 0;
+                key = (low == desc) ? (key > o ? key : o) : (key < o ? key : o);
+            }
+        if (lane <= MOE_TOPK) cand[warp * (MOE_TOPK + 1) + lane] = key;
+    }
     __syncthreads();
     if (tid < 8 * (MOE_TOPK + 1)) {
         const unsigned long long me = cand[tid];
@@ -267,16 +259,18 @@ __device__ __forceinline__ void rank_top(const double *sS, const double *sB, uns
     }
     __syncthreads();
     // best S + B among the unselected: everything but top9[0..7]
-    bool sel = false;
+    if (mine) {
+        bool sel = false;
 #pragma unroll
-    for (int k = 0; k < MOE_TOPK; k++) sel |= top9[k] == tid;
-    double u = sel ? -INFINITY : sS[tid] + sB[tid];
-    u = warp_max_d(u);
-    if (lane == 0) dred[warp] = u;      // dred's rms sums were consumed before the cluster barrier
+        for (int k = 0; k < MOE_TOPK; k++) sel |= top9[k] == tid;
+        double u = sel ? -INFINITY : sS[tid] + sB[tid];
+        u = warp_max_d(u);
+        if (lane == 0) dred[warp] = u;  // dred's rms sums were consumed before the cluster barrier
+    }
     __syncthreads();
     if (tid == 0) {
         double m = dred[0];
-        for (int w = 1; w < 8; w++) m = fmax(m, dred[w]);
+        for (int w = 1; w < MOE_NEXP / 32; w++) m = fmax(m, dred[w]);
         dred[0] = m;
     }
     __syncthreads();
@@ -298,38 +292,59 @@ __device__ __forceinline__ bool top_settled(const double *sS, const double *sB, 
     return true;
 }
 
-// Router: one cluster of RCL CTAs per token (grid (RCL, T)), 8 warps per
-// CTA, 2 experts per warp.  Every CTA forms xn = rms_norm(x2) * post_norm
-// (rms_norm_m, nn.c:348-357) in shared memory; each warp computes its two
-// exact logits and bounds and stores them into the leader CTA's shared
-// memory; CTAs 0..7 also quantize 256-block `rank` of xn to Q8_K (shared by
-// every expert) and send the leader their part of the shared-expert gate
-// input sum_i g_i * xq_i * xd (nn.c:453).  After the cluster barrier the
-// leader selects the top 8 (falling back to the reference's own summation
-// order for any rank the bounds cannot settle) and writes the renormalised
-// weights (nn.c:524-547) and the shared-expert gate sigmoid.
+// Router: one cluster of RCL CTAs per token (grid (RCL, T)), 16 warps per
+// CTA, one expert per warp.  Every CTA forms xn = rms_norm(x2) * post_norm
+// (rms_norm_m, nn.c:348-357) in shared memory; each warp computes its exact
+// logit and bound and stores them into the leader CTA's shared memory; CTAs
+// 0..7 also quantize 256-block `rank` of xn to Q8_K (shared by every expert)
+// and send the leader their part of the shared-expert gate input
+// sum_i g_i * xq_i * xd (nn.c:453).  After the cluster barrier the leader
+// selects the top 8 (falling back to the reference's own summation order for
+// any rank the bounds cannot settle) and writes the renormalised weights
+// (nn.c:524-547) and the shared-expert gate sigmoid.
 constexpr int RCL = 16;                       // CTAs per router cluster
-constexpr uint32_t ROUTER_SMEM = uint32_t(MOE_NEXP / RCL) * MOE_EMBD * 4;   // 16 fp32 rows
-constexpr int XCL = 8;                        // CTAs per expert cluster (two fit in a GPC)
+constexpr int RTHREADS = 512;                 // one warp per expert row
+constexpr int RROWS = MOE_NEXP / RCL;         // router rows per CTA
+constexpr uint32_t ROW_BYTES = MOE_EMBD * 4;
+constexpr uint32_t ROUTER_SMEM = uint32_t(RROWS) * ROW_BYTES;   // 16 fp32 rows
+static_assert(RROWS == RTHREADS / 32, "one router row per warp");
+constexpr int XCL = 16;                       // CTAs per expert cluster (two CTAs per SM)
 constexpr int XTHREADS = 512;                 // threads per expert CTA
 constexpr int XGU = MOE_FF / XCL;             // gate/up rows per expert CTA
 constexpr int XDN = MOE_EMBD / XCL;           // down rows per expert CTA
 static_assert(XDN == MOE_DOWN_CHUNK && XCL == MOE_DOWN_CHUNKS, "combine chunks = expert CTAs");
 
-__global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restrict__ x2,
-                                                         const float *__restrict__ post_norm,
-                                                         const float *__restrict__ Wr,
-                                                         const float *__restrict__ gis,
-                                                         MoeScratch s, int *sel_out,
-                                                         float *w_out) {
+// The reference's own summation order for one logit, s = fl(s + fl(g_i x_i))
+// for i = 0..2047 (nn.c:519-521), from a row and xn in shared memory.
+__device__ __forceinline__ float router_logit_seq(const float *row, const float *xn) {
+    float acc = 0.0f;
+#pragma unroll 4
+    for (int i = 0; i < MOE_EMBD; i += 4) {
+        const float4 g = *reinterpret_cast<const float4 *>(row + i);
+        const float4 x = *reinterpret_cast<const float4 *>(xn + i);
+        acc = __fadd_rn(acc, __fmul_rn(g.x, x.x));
+        acc = __fadd_rn(acc, __fmul_rn(g.y, x.y));
+        acc = __fadd_rn(acc, __fmul_rn(g.z, x.z));
+        acc = __fadd_rn(acc, __fmul_rn(g.w, x.w));
+    }
+    return acc;
+}
+
+__global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__restrict__ x2,
+                                                               const float *__restrict__ post_norm,
+                                                               const float *__restrict__ Wr,
+                                                               const float *__restrict__ gis,
+                                                               MoeScratch s, int *sel_out,
+                                                               float *w_out) {
     QMA_TRACE_SCOPE(TK_ROUTER);
     extern __shared__ __align__(128) float rrows[];        // this CTA's 16 router rows
     const unsigned rank = cluster_rank();
     const int t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = RTHREADS / 32;
     __shared__ __align__(8) uint64_t rbar;
     __shared__ __align__(16) float xn[MOE_EMBD];
-    __shared__ double dred[8];
+    __shared__ double dred[NW];
     __shared__ double sS[MOE_NEXP], sB[MOE_NEXP];
     __shared__ float gpart[MOE_EMBD / 256];
     __shared__ int need_exact, ncand;
@@ -340,7 +355,7 @@ __global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restr
 
     // this CTA's router rows: independent of the upstream kernel, copied
     // into shared memory by the TMA engine before waiting on it
-    const int e0 = int(rank) * (MOE_NEXP / RCL) + warp * 2;
+    const int e0 = int(rank) * RROWS + warp;
     if (warp == 0) {
         if (lane == 0) {
             mbar_init(&rbar, 1);
@@ -348,7 +363,7 @@ __global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restr
             mbar_expect_tx(&rbar, ROUTER_SMEM);
         }
         __syncwarp();
-        bulk_g2s_warp(rrows, Wr + size_t(rank) * (MOE_NEXP / RCL) * MOE_EMBD, ROUTER_SMEM, &rbar, lane);
+        bulk_g2s_warp(rrows, Wr + size_t(rank) * RROWS * MOE_EMBD, ROUTER_SMEM, &rbar, lane);
     }
     // this CTA's slice of the shared-expert gate row (CTAs 0..7, warp 0)
     float gisv[8] = {};
@@ -364,39 +379,40 @@ __global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restr
     QMA_TRACE_MARK(TK_ROUTER, 2);
     // ---- xn = rms_norm(x2) * post_norm ------------------------------------
     const float *x = x2 + size_t(t) * MOE_EMBD;
-    float xv[8];
+    constexpr int XPT = MOE_EMBD / RTHREADS;
+    float xv[XPT];
     double ss = 0.0;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        xv[k] = x[tid + 256 * k];
+    for (int k = 0; k < XPT; k++) {
+        xv[k] = x[tid + RTHREADS * k];
         ss += double(xv[k]) * double(xv[k]);
     }
     ss = warp_sum_d(ss);
     if (lane == 0) dred[warp] = ss;
     __syncthreads();
-    const double tot = ((dred[0] + dred[1]) + (dred[2] + dred[3])) + ((dred[4] + dred[5]) + (dred[6] + dred[7]));
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < NW; w++) tot += dred[w];
     const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int i = tid + 256 * k;
+    for (int k = 0; k < XPT; k++) {
+        const int i = tid + RTHREADS * k;
         xn[xn_idx(i)] = __fmul_rn(__fmul_rn(xv[k], r), post_norm[i]);
     }
     __syncthreads();
     QMA_TRACE_MARK(TK_ROUTER, 3);
-    // ---- two exact logits per warp, sent to the leader ---------------------
+    // ---- one exact logit per warp, sent to the leader -----------------------
+    bool rows_ok = mbar_wait(&rbar, 0);
+    if (!rows_ok) {
+        if (lane == 0) atomicAdd(&g_moe_timeouts, 1u);
+        mbar_wait(&rbar, 0);
+    }
     {
-        if (!mbar_wait(&rbar, 0)) {
-            if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
-            mbar_wait(&rbar, 0);
-        }
-        double S0, B0, S1, B1;
-        router_logit(rrows + size_t(warp * 2) * MOE_EMBD, xn, lane, S0, B0);
-        router_logit(rrows + size_t(warp * 2 + 1) * MOE_EMBD, xn, lane, S1, B1);
+        double S0, B0;
+        router_logit(rrows + size_t(warp) * MOE_EMBD, xn, lane, S0, B0);
         if (lane == 0) {
             st_cluster_f64(cluster_map(&sS[e0], 0), S0);
             st_cluster_f64(cluster_map(&sB[e0], 0), B0);
-            st_cluster_f64(cluster_map(&sS[e0 + 1], 0), S1);
-            st_cluster_f64(cluster_map(&sB[e0 + 1], 0), B1);
         }
     }
     // ---- Q8_K block `rank` of xn and its part of the shared-expert gate ----
@@ -422,11 +438,11 @@ __global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restr
     if (rank != 0) return;
 
     // ---- leader: top 8 ------------------------------------------------------
-    // Thread e ranks expert e by (S descending, id ascending), counting the
-    // experts above it.  That is the reference's order (probability, then
-    // lowest id) whenever the 8th expert's probability is a normal float
-    // (class 2: the classes below only ever hold lower logits) and every
-    // decision is settled by the bounds; otherwise the exact path below runs.
+    // Expert e ranks by (S descending, id ascending), counting the experts
+    // above it.  That is the reference's order (probability, then lowest id)
+    // whenever the 8th expert's probability is a normal float (class 2: the
+    // classes below only ever hold lower logits) and every decision is
+    // settled by the bounds; otherwise the exact path below runs.
     rank_top(sS, sB, rcand, tid, lane, warp, dred, top9);
     if (tid == 0) {
         need_exact = !top_settled(sS, sB, top9, dred);
@@ -435,24 +451,39 @@ __global__ void __launch_bounds__(256, 2) moe_router_kernel(const float *__restr
     __syncthreads();
     if (need_exact) {
         // Every expert whose rank the bounds leave open gets its logit
-        // recomputed in the reference's exact order, s = fl(s + fl(g_i x_i)),
-        // i = 0..2047; their intervals then collapse to the exact value.
+        // recomputed in the reference's exact order; its interval then
+        // collapses to the exact value.  The candidates' rows are copied, 16
+        // at a time, into the row buffer (its own rows are consumed).
         const double mx = sS[top9[0]];
-        cls[tid] = p_class(sS[tid], mx);
         const int e8 = top9[MOE_TOPK - 1];
         const double thresh = sS[e8] - sB[e8];
-        __syncthreads();
-        if (cls[tid] > 0 && sS[tid] + sB[tid] >= thresh - 1e-6 * (1.0 + fabs(sS[e8]))) cand[atomicAdd(&ncand, 1)] = tid;
-        __syncthreads();
-        for (int c = tid; c < ncand; c += 256) {
-            const int e = cand[c];
-            const float *wr = Wr + size_t(e) * MOE_EMBD;
-            float acc = 0.0f;
-            for (int i = 0; i < MOE_EMBD; i++) acc = __fadd_rn(acc, __fmul_rn(__ldg(wr + i), xn[xn_idx(i)]));
-            sS[e] = double(acc);
-            sB[e] = 0.0;
+        if (tid < MOE_NEXP) {
+            cls[tid] = p_class(sS[tid], mx);
+            if (cls[tid] > 0 && sS[tid] + sB[tid] >= thresh - 1e-6 * (1.0 + fabs(sS[e8])))
+                cand[atomicAdd(&ncand, 1)] = tid;
         }
         __syncthreads();
+        for (int base = 0, phase = 1; base < ncand; base += RROWS, phase ^= 1) {
+            const int nb = min(RROWS, ncand - base);
+            if (warp == 0) {
+                fence_proxy_async_smem();              // generic reads of the buffer are done
+                if (lane == 0) mbar_expect_tx(&rbar, uint32_t(nb) * ROW_BYTES);
+                __syncwarp();
+                for (int c = 0; c < nb; c++)
+                    bulk_g2s_warp(rrows + size_t(c) * MOE_EMBD, Wr + size_t(cand[base + c]) * MOE_EMBD,
+                                  ROW_BYTES, &rbar, lane);
+            }
+            if (!mbar_wait(&rbar, uint32_t(phase))) {
+                if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
+                mbar_wait(&rbar, uint32_t(phase));
+            }
+            if (tid < nb) {
+                const int e = cand[base + tid];
+                sS[e] = double(router_logit_seq(rrows + size_t(tid) * MOE_EMBD, xn));
+                sB[e] = 0.0;
+            }
+            __syncthreads();
+        }
         if (warp == 0) {
             double m2 = -INFINITY;
             for (int j = 0; j < 8; j++) m2 = fmax(m2, sS[lane + 32 * j]);
@@ -526,20 +557,21 @@ template <> struct DownPtr<FmtQ4K> {
 
 // One cluster of XCL CTAs per (slot, token): grid (9 x XCL, T); slots 0..7
 // are the routed experts in selection order, slot 8 the shared expert
-// (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  Clusters
-// of 8 (one CTA per SM): two fit in a GPC, so all 9 are co-resident beside
-// the router's cluster.  CTA `rank` owns gate/up rows rank*XGU.. and down
-// rows rank*XDN..:
-//   1. its 64 gate and 64 up rows (147 KB) are copied into shared memory by
+// (moe_expert_one_q8k nn.c:412-439, moe_shared_q8k nn.c:446-473).  144 CTAs
+// of 512 threads, sized (registers <= 64, 74 KB of shared memory) so that
+// two fit on an SM: the 9 clusters of 16 are co-resident beside the router's
+// cluster and the next kernels' early CTAs.  CTA `rank` owns gate/up rows
+// rank*XGU.. and down rows rank*XDN..:
+//   1. its 32 gate and 32 up rows (74 KB) are copied into shared memory by
 //      the TMA engine as soon as the expert is known (the shared expert's
 //      before the router has finished), its down rows prefetched into L2;
-//   2. one warp per 4 row pairs computes silu(gate) * up;
-//   3. every CTA pushes its 64 hidden values into all 8 CTAs' shared
+//   2. one warp per 2 row pairs computes silu(gate) * up;
+//   3. every CTA pushes its 32 hidden values into all 16 CTAs' shared
 //      memory (one cluster barrier) while the down rows are copied into the
 //      freed buffer;
-//   4. every CTA quantizes the hidden vector to Q8_K and computes its down
-//      rows; the last of the 9 slot CTAs of a row chunk combines the slots
-//      in the reference's order and adds the residual (nn.c:615-629,
+//   4. every CTA quantizes the hidden vector to Q8_K and computes its 128
+//      down rows; the last of the 9 slot CTAs of a row chunk combines the
+//      slots in the reference's order and adds the residual (nn.c:615-629,
 //      nn.c:2246-2252).
 // Every wait on a copy is bounded; a copy that never lands is counted in
 // g_moe_timeouts (the host fails the call) and the CTA still takes part in
@@ -576,13 +608,13 @@ template <> struct DownBytes<FmtQ4K> {
     __device__ static const uint8_t *at(const uint8_t *dst) { return dst; }
 };
 constexpr uint32_t XROW = uint32_t(MOE_EMBD / 256) * Q4K_BYTES;     // one gate/up row
-constexpr uint32_t XGU_BYTES = XGU * XROW;                          // 64 rows
+constexpr uint32_t XGU_BYTES = XGU * XROW;                          // 32 rows
 constexpr size_t EXPERT_SMEM = 2 * size_t(XGU_BYTES);
 static_assert(DownBytes<FmtQ6K>::ALL <= EXPERT_SMEM && DownBytes<FmtQ4K>::ALL <= EXPERT_SMEM,
               "down rows reuse the gate/up buffer");
 
 template <class F>
-__global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
+__global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *__restrict__ gate_exps,
                                                          const uint8_t *__restrict__ up_exps,
                                                          const uint8_t *__restrict__ gate_sh,
                                                          const uint8_t *__restrict__ up_sh,
@@ -590,7 +622,7 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
                                                          size_t down_bytes,
                                                          const uint8_t *__restrict__ down_sh,
                                                          const float *x2, float *x_out,
-                                                         MoeScratch s, NextNorm nn) {
+                                                         MoeScratch s) {
     QMA_TRACE_SCOPE(TK_EXPERT);
     extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
@@ -604,8 +636,7 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
     __shared__ __align__(16) int8_t hq[MOE_FF];
     __shared__ float hd[MOE_FF / 256];
     __shared__ int16_t hs[MOE_FF / 16];
-    __shared__ int is_last, is_last2;
-    __shared__ double nred[8];
+    __shared__ int is_last;
     const int g0 = int(rank) * XGU, d0 = int(rank) * XDN;
     if (tid == 0) {
         mbar_init(&bar[0], 1);
@@ -642,21 +673,21 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
     QMA_TRACE_MARK(TK_EXPERT, 2);
     {
         constexpr int RPWARP = XGU / (XTHREADS / 32);
-        static_assert(RPWARP == 4, "8 dots (4 gate + 4 up rows) per warp");
-        float dv[8];
+        static_assert(RPWARP == 2, "4 dots (2 gate + 2 up rows) per warp");
+        float dv[4];
 #pragma unroll
         for (int k = 0; k < RPWARP; k++) {
             FmtQ4K::Wt wg, wu;
             FmtQ4K::load_w_smem(wg, xbuf, warp * RPWARP + k, MOE_EMBD, lane);
             FmtQ4K::load_w_smem(wu, xbuf + XGU_BYTES, warp * RPWARP + k, MOE_EMBD, lane);
             dv[k] = FmtQ4K::dot(wg, act, lane);
-            dv[4 + k] = FmtQ4K::dot(wu, act, lane);
+            dv[2 + k] = FmtQ4K::dot(wu, act, lane);
         }
-        const float tot = warp_sum8(dv, lane);          // lane: row (index & 3), gate/up (index & 4)
+        const float tot = warp_sum4(dv, lane);          // lane: row (index & 1), gate/up (index & 2)
         const float u = __shfl_xor_sync(0xffffffffu, tot, 16);
-        if ((lane & 19) == 0) {                          // gate lanes, one per row
+        if ((lane & 23) == 0) {                          // gate lanes 0 and 8, one per row
             const float g = tot;
-            hpart[warp * RPWARP + (warp_sum8_index(lane) & 3)] = gu_ok ? (g / (1.0f + expf(-g))) * u : 0.0f;
+            hpart[warp * RPWARP + (warp_sum4_index(lane) & 1)] = gu_ok ? (g / (1.0f + expf(-g))) * u : 0.0f;
         }
     }
     __syncthreads();                    // gate/up rows consumed: reuse the buffer
@@ -684,7 +715,7 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
     QMA_TRACE_MARK(TK_EXPERT, 6);
     float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + d0;
     if (dn_ok) {
-        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 2>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
+        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 1>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
                                                   warp, XTHREADS / 32, lane);
     } else {
         if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
@@ -719,42 +750,6 @@ __global__ void __launch_bounds__(XTHREADS) moe_expert_kernel(const uint8_t *__r
             x_out[size_t(t) * MOE_EMBD + r] = __fadd_rn(acc, x2[size_t(t) * MOE_EMBD + r]);
         }
         if (tid == 0) s.dcount[t * MOE_DOWN_CHUNKS + rank] = 0;
-        if (nn.w) {
-            // the last of the token's MOE_DOWN_CHUNKS combiners normalizes it
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) is_last2 = atomicAdd(&s.rcount[t], 1u) == MOE_DOWN_CHUNKS - 1;
-            __syncthreads();
-            if (is_last2) {
-                __threadfence();
-                float v[8];
-                if (tid < 256) {
-                    const float4 *p = reinterpret_cast<const float4 *>(x_out + size_t(t) * MOE_EMBD + tid * 8);
-                    const float4 a = __ldcg(p), b = __ldcg(p + 1);
-                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-                    double ss = 0.0;
-#pragma unroll
-                    for (int k = 0; k < 8; k++) ss += double(v[k]) * double(v[k]);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                    if (lane == 0) nred[warp] = ss;
-                }
-                __syncthreads();
-                if (tid < 256) {
-                    const double tot = ((nred[0] + nred[1]) + (nred[2] + nred[3])) + ((nred[4] + nred[5]) + (nred[6] + nred[7]));
-                    const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
-                    const float4 wa = *reinterpret_cast<const float4 *>(nn.w + tid * 8);
-                    const float4 wb = *reinterpret_cast<const float4 *>(nn.w + tid * 8 + 4);
-                    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-                    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], r), wv[k]);
-                    q8k_block_warp(v, lane, nn.xq + size_t(t) * MOE_EMBD + warp * 256, nn.xd + size_t(t) * 8 + warp,
-                                   nn.xs + size_t(t) * 128 + warp * 16);
-                }
-                if (t == 0 && tid < Prefetch::N && nn.pf.p[tid]) prefetch_l2_range(nn.pf.p[tid], nn.pf.bytes[tid]);
-                if (tid == 0) s.rcount[t] = 0;
-            }
-        }
     }
 }
 
@@ -771,8 +766,7 @@ int moe_wait_timeouts() {
 static bool g_moe_attrs = false;
 
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters, const NextNorm *nnp) {
-    const NextNorm nn = nnp ? *nnp : NextNorm();
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters) {
     MoeScratch s = moe_scratch_layout(scratch, T);
     if (!g_moe_attrs) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -789,10 +783,9 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     }
     if (clear_counters) {
         QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
-        QMA_CHECK_CUDA(cudaMemsetAsync(s.rcount, 0, sizeof(unsigned) * T, st));
     }
     const bool pdl = pdl_enabled() && !clear_counters;
-    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(256), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
+    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
                              w.gate_inp, w.gate_inp_shexp, s, sel, wts));
     const size_t eb = packed_bytes(w.down_type, MOE_EMBD, MOE_FF);
     const dim3 grid(MOE_NSLOT * XCL, T);
@@ -801,10 +794,10 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s, nn));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s));
     else
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s, nn));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s));
     return QMA_CUDA_OK;
 }
 

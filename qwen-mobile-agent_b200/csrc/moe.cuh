@@ -9,17 +9,14 @@ constexpr int MOE_NEXP = 256;         // N_EXPERT (qma.h:57)
 constexpr int MOE_TOPK = 8;           // N_EXPERT_USED (qma.h:58)
 constexpr int MOE_FF = 512;           // N_FF_EXP / N_FF_SHEXP (qma.h:59-60)
 constexpr int MOE_NSLOT = MOE_TOPK + 1;   // routed experts + the shared expert
-constexpr int MOE_GU_ROWS = 32;       // gate/up row pairs per CTA
-constexpr int MOE_GU_CHUNKS = MOE_FF / MOE_GU_ROWS;
-constexpr int MOE_DOWN_CHUNK = 256;   // down-projection output rows per CTA
+constexpr int MOE_DOWN_CHUNK = 128;   // down-projection output rows per CTA
 constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
 
 // Per-call device scratch of the MoE block for T tokens (moe_scratch_layout
 // carves one caller-provided buffer).  The combine tickets (dcount) must be
 // zero when a call starts; every call leaves them zero again.
 struct MoeScratch {
-    unsigned *rcount;      // [T] output chunks finished (fused next norm)
-    unsigned *dcount;      // [T][16] down CTAs finished per output chunk
+    unsigned *dcount;      // [T][16] slot CTAs finished per 128-row output chunk
     double *S, *B;         // [T][256] exact logit, bound on the fp32 logit
     int *fallback;         // [T] 1 if the exact sequential recompute ran
     int *sel;              // [T][8] selected experts, selection order
@@ -28,7 +25,6 @@ struct MoeScratch {
     float *xd;             // [T][8]
     int16_t *xs;           // [T][128]
     float *gs;             // [T] shared-expert gate sigmoid
-    float *h;              // [T][9][512] silu(gate) * up per slot
     float *part;           // [T][9][2048] down projections per slot
 };
 
@@ -38,20 +34,8 @@ MoeScratch moe_scratch_layout(void *base, int T);
 // the engine's own scratch starts zeroed and every call leaves it zeroed, so
 // it skips the memset and launches the router with programmatic dependent
 // launch.
-// Optional fusion of the next RMSNorm into the MoE block: when w is set, the
-// last CTA to finish a token's output also computes rms_norm(x_out) * w and
-// its Q8_K blocks (the next matmul's input, rms_norm_m nn.c:348-357 +
-// nn.c:318-324, same arithmetic as the standalone kernel) and issues pf.
-struct NextNorm {
-    const float *w = nullptr;
-    int8_t *xq = nullptr;
-    float *xd = nullptr;
-    int16_t *xs = nullptr;
-    Prefetch pf;
-};
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters,
-              const NextNorm *nn = nullptr);
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters);
 // Bounded waits of the expert kernel that ran out since the last call (reset
 // by reading); -1 if the counter cannot be read.
 int moe_wait_timeouts();
