@@ -368,7 +368,7 @@ struct Prefetch {
 // ring, read back with qma_trace_read(); otherwise QMA_TRACE_SCOPE is empty.
 enum TraceKernel : uint32_t {
     TK_EMBED = 1, TK_RMSNORM, TK_GEMV, TK_CONV, TK_GDN, TK_GATED_NORM, TK_QK_PREP, TK_ATTN_CHUNK,
-    TK_ATTN_COMBINE, TK_SALIENCE, TK_ROUTER, TK_EXPERT, TK_ARGMAX
+    TK_ATTN_COMBINE, TK_SALIENCE, TK_ROUTER, TK_EXPERT, TK_ARGMAX, TK_MOE_NORM
 };
 #ifdef QMA_TRACE
 constexpr uint32_t TRACE_CAP = 1u << 22;

@@ -688,9 +688,11 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
         return pf;
     };
+    bool normed = false;           // s->xq already holds the next norm's output
     for (int il = 0; il < n_layers; il++) {
         const LayerW &L = m->L[il];
-        TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
+        if (!normed) TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
+        normed = false;
         // a single token's gated-delta-net conv runs in the input projection's epilogue
         ConvEpi ce;
         const bool conv_fused = !is_attn(il) && T == 1 && pdl_enabled();
@@ -741,14 +743,28 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
                                            cudaMemcpyDeviceToDevice, st));
             break;
         }
-        // x = x2 + moe(rms_norm(x2) * post_norm)
-        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false));
+        // x = x2 + moe(rms_norm(x2) * post_norm); the block's last kernel also
+        // forms the next RMSNorm's Q8_K input (the next layer's, or the
+        // output norm's for the rows the LM head reads)
+        MoeNormTail tail;
+        tail.xq = s->xq;
+        tail.xd = s->xd;
+        tail.xs = s->xs;
+        if (il + 1 < n_layers) {
+            tail.w = m->L[il + 1].attn_norm;
+            tail.pf = plan(il + 1);
+        } else if (logits_mode) {
+            tail.w = m->out_norm;
+            tail.norm_from = logits_mode == 2 ? 0 : T - 1;
+        }
+        TRY(moe_layer(L.moe, s->x2, T, s->x, nullptr, nullptr, s->moe_scratch, st, false, &tail));
+        normed = tail.w != nullptr;
     }
     if (side_pending) QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
     if (logits_mode) {
         const int rows = logits_mode == 2 ? T : 1;
         const float *xin = logits_mode == 2 ? s->x : s->x + size_t(T - 1) * EMBD;
-        TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
+        if (!normed) TRY(launch_rmsnorm_quant(xin, m->out_norm, rows, EMBD, s->xq, s->xd, s->xs, st));
         TRY(matvec(m->out_type, m->out, EMBD, m->n_vocab, rows, s->xq, s->xd, s->xs, s->logits, st));
     }
 #undef TRY

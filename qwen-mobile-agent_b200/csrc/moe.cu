@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
                                                          size_t down_bytes,
                                                          const uint8_t *__restrict__ down_sh,
                                                          const float *x2, float *x_out,
-                                                         MoeScratch s) {
+                                                         MoeScratch s, int combine) {
     QMA_TRACE_SCOPE(TK_EXPERT);
     extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
@@ -727,6 +727,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
     // the next layer's kernels may launch now: this kernel's weight traffic
     // is done, only the combine remains
     pdl_trigger();
+    if (!combine) return;               // moe_combine_norm_kernel combines
     // ---- the last of the 9 slot CTAs of this row chunk combines --------------
     __syncthreads();
     if (tid == 0) {
@@ -753,6 +754,70 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
     }
 }
 
+// Combine + residual + next RMSNorm + Q8_K, one CTA of 256 threads per
+// token, 8 rows per thread: the slots are combined in the reference's order
+// exactly as the expert kernel's combine does (nn.c:615-629, residual
+// nn.c:2246-2252), then rms_norm_m (nn.c:348-357) and the Q8_K quantization
+// of the next matmul (nn.c:318-324) with the arithmetic of
+// rmsnorm_quant_kernel.
+__global__ void __launch_bounds__(256) moe_combine_norm_kernel(MoeScratch s, const float *x2, float *x_out,
+                                                               const float *__restrict__ w, int norm_from,
+                                                               int8_t *xq, float *xd, int16_t *xs,
+                                                               Prefetch pf) {
+    QMA_TRACE_SCOPE(TK_MOE_NORM);
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ double red[8];
+    pdl_trigger();
+    if (t == 0) {
+#pragma unroll
+        for (int i = 0; i < Prefetch::N; i++)
+            if (tid == i && pf.p[i]) prefetch_l2_range(pf.p[i], pf.bytes[i]);
+    }
+    const bool norm = w != nullptr && t >= norm_from;
+    float wv[8] = {};
+    if (norm) {
+        const float4 wa = __ldg(reinterpret_cast<const float4 *>(w + tid * 8));
+        const float4 wb = __ldg(reinterpret_cast<const float4 *>(w + tid * 8 + 4));
+        wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
+        wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
+    }
+    pdl_wait();
+    const size_t r0 = size_t(t) * MOE_EMBD + tid * 8;
+    float acc[8] = {};
+#pragma unroll
+    for (int k = 0; k <= MOE_TOPK; k++) {
+        const float4 *pp = reinterpret_cast<const float4 *>(s.part + (size_t(t) * MOE_NSLOT + k) * MOE_EMBD + tid * 8);
+        const float4 a = __ldcg(pp), b = __ldcg(pp + 1);
+        const float p[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const float wk = k < MOE_TOPK ? __ldcg(&s.w[t * MOE_TOPK + k]) : __ldcg(&s.gs[t]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(wk, p[j]));
+    }
+    const float4 xa = __ldcg(reinterpret_cast<const float4 *>(x2 + r0));
+    const float4 xb = __ldcg(reinterpret_cast<const float4 *>(x2 + r0 + 4));
+    const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fadd_rn(acc[j], xr[j]);
+    reinterpret_cast<float4 *>(x_out + r0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(x_out + r0)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (!norm) return;                  // block-uniform
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) ss += double(v[k]) * double(v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    const double tot = ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
+    const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], r), wv[k]);
+    const int row = t - norm_from;
+    q8k_block_warp(v, lane, xq + size_t(row) * MOE_EMBD + warp * 256, xd + size_t(row) * 8 + warp,
+                   xs + size_t(row) * 128 + warp * 16);
+}
+
 int moe_wait_timeouts() {
     unsigned n = 0;
     if (cudaMemcpyFromSymbol(&n, g_moe_timeouts, sizeof(n)) != cudaSuccess) return -1;
@@ -766,7 +831,7 @@ int moe_wait_timeouts() {
 static bool g_moe_attrs = false;
 
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters) {
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters, const MoeNormTail *tail) {
     MoeScratch s = moe_scratch_layout(scratch, T);
     if (!g_moe_attrs) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -794,10 +859,13 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
     if (w.down_type == QMA_TYPE_Q6_K)
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1));
     else
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1));
+    if (tail)
+        QMA_CHECK_CUDA(launch_ex(moe_combine_norm_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), s, x2, x_out,
+                                 tail->w, tail->norm_from, tail->xq, tail->xd, tail->xs, tail->pf));
     return QMA_CUDA_OK;
 }
 

@@ -34,8 +34,23 @@ MoeScratch moe_scratch_layout(void *base, int T);
 // the engine's own scratch starts zeroed and every call leaves it zeroed, so
 // it skips the memset and launches the router with programmatic dependent
 // launch.
+// Optional tail of the MoE block (the engine's decode path): instead of the
+// expert CTAs' ticketed combine, one kernel after the experts combines the
+// slots, adds the residual and, when w is set, applies the next RMSNorm
+// (the next layer's attn_norm or the output norm) and its Q8_K
+// quantization to tokens norm_from.. (row t - norm_from of xq), issuing the
+// next layer's L2 prefetch plan pf.
+struct MoeNormTail {
+    const float *w = nullptr;
+    int norm_from = 0;
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int16_t *xs = nullptr;
+    Prefetch pf;
+};
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
-              float *wts, void *scratch, cudaStream_t st, bool clear_counters);
+              float *wts, void *scratch, cudaStream_t st, bool clear_counters,
+              const MoeNormTail *tail = nullptr);
 // Bounded waits of the expert kernel that ran out since the last call (reset
 // by reading); -1 if the counter cannot be read.
 int moe_wait_timeouts();
