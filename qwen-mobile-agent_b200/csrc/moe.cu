@@ -220,76 +220,69 @@ __device__ __forceinline__ void router_logit(const float *row, const float *xn, 
     B = double(E) * 0x1.0p-24 * 1.01 + 1e-30;
 }
 
-// Leader-side ranking of the 256 logits (threads 0..255 = experts; the
-// other threads of the CTA only take part in the barriers): top9[r] = the
-// expert of rank r < 9 under (S descending, id ascending), ranked on S
-// rounded to fp32.  Two logits that fp32 rounding could tie or misorder are
-// within one fp32 ulp of each other, far inside the margin top_settled()
-// demands between ranks, so such a ranking is never accepted.  Each warp
-// sorts its 32 keys (sortable fp32 bits, then inverted id) with a bitonic
-// network in registers; the 8 warps' top 9 are ranked by counting.
-// dred[0] receives the largest S + B among the unselected (rank >= 8).
-__device__ __forceinline__ unsigned long long rank_key(double S, int e) {
-    uint32_t u = __float_as_uint(float(S));
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - uint32_t(e));
+// Leader-side fast selection by one warp (lane l holds experts l + 32 j):
+// top9[r] = the expert of rank r < 9 by S rounded to fp32 (nine rounds of a
+// warp max over sortable 32-bit keys; equal keys go to the lowest lane,
+// then the lowest j).  Returns whether that ranking settles the reference's
+// selection: the 8th expert's probability is a normal float (then no lower
+// class can compete) and the intervals S +- B of consecutive selected
+// experts, and of the 8th against every unselected one, are separated with
+// a margin that keeps the probabilities' order strict after expf and
+// division rounding.  Two logits that fp32 rounding could tie or misorder
+// are within one fp32 ulp of each other, far inside that margin, so a
+// ranking they could spoil is never accepted; the exact path runs instead.
+__device__ __forceinline__ uint32_t sort_key(double S) {
+    const uint32_t u = __float_as_uint(float(S));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);   // > 0 for every non-NaN
 }
-__device__ __forceinline__ void rank_top(const double *sS, const double *sB, unsigned long long *cand,
-                                         int tid, int lane, int warp, double *dred, int *top9) {
-    const bool mine = tid < MOE_NEXP;              // warp-uniform
-    if (mine) {
-        unsigned long long key = rank_key(sS[tid], tid);
+__device__ bool select_fast(const double *sS, const double *sB, int lane, int *top9) {
+    uint32_t key[8];
 #pragma unroll
-        for (int k = 2; k <= 32; k <<= 1)
+    for (int j = 0; j < 8; j++) key[j] = sort_key(sS[lane + 32 * j]);
+    unsigned taken = 0;                                  // bit j: taken in rounds 0..7
+    int mine = -1;                                       // lane k's expert of rank k
+    int e8 = 0;
+#pragma unroll 1
+    for (int r = 0; r <= MOE_TOPK; r++) {
+        uint32_t m = 0;
 #pragma unroll
-            for (int j = k >> 1; j > 0; j >>= 1) {
-                const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, j);
-                const bool desc = (lane & k) == 0 || k == 32;
-                const bool low = (lane & j) == 0;
-                key = (low == desc) ? (key > o ? key : o) : (key < o ? key : o);
-            }
-        if (lane <= MOE_TOPK) cand[warp * (MOE_TOPK + 1) + lane] = key;
-    }
-    __syncthreads();
-    if (tid < 8 * (MOE_TOPK + 1)) {
-        const unsigned long long me = cand[tid];
-        int r = 0;
-        for (int j = 0; j < 8 * (MOE_TOPK + 1); j++) r += cand[j] > me;
-        if (r <= MOE_TOPK) top9[r] = int(0xffffffffu - uint32_t(me & 0xffffffffu));
-    }
-    __syncthreads();
-    // best S + B among the unselected: everything but top9[0..7]
-    if (mine) {
-        bool sel = false;
+        for (int j = 0; j < 8; j++) m = max(m, key[j]);
+        const uint32_t M = __reduce_max_sync(0xffffffffu, m);
+        const int owner = __ffs(__ballot_sync(0xffffffffu, m == M)) - 1;
+        int e = 0;
+        if (lane == owner) {
+            int jj = 0;
 #pragma unroll
-        for (int k = 0; k < MOE_TOPK; k++) sel |= top9[k] == tid;
-        double u = sel ? -INFINITY : sS[tid] + sB[tid];
-        u = warp_max_d(u);
-        if (lane == 0) dred[warp] = u;  // dred's rms sums were consumed before the cluster barrier
+            for (int j = 7; j >= 0; j--) if (key[j] == M) jj = j;
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (j == jj) {
+                    key[j] = 0;
+                    if (r < MOE_TOPK) taken |= 1u << j;
+                }
+            e = lane + 32 * jj;
+        }
+        e = __shfl_sync(0xffffffffu, e, owner);
+        if (lane == r) mine = e;
+        if (r == MOE_TOPK) e8 = e;
     }
-    __syncthreads();
-    if (tid == 0) {
-        double m = dred[0];
-        for (int w = 1; w < MOE_NEXP / 32; w++) m = fmax(m, dred[w]);
-        dred[0] = m;
+    if (lane <= MOE_TOPK) top9[lane] = lane == MOE_TOPK ? e8 : mine;
+    // largest S + B among the unselected (everything but ranks 0..7)
+    double ub = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        if (!((taken >> j) & 1u)) ub = fmax(ub, sS[lane + 32 * j] + sB[lane + 32 * j]);
+    ub = warp_max_d(ub);
+    // lane k < 8 checks the gap below rank k
+    const int nxt = __shfl_down_sync(0xffffffffu, mine, 1);
+    const int top0 = __shfl_sync(0xffffffffu, mine, 0);
+    bool ok = true;
+    if (lane < MOE_TOPK) {
+        const double hi = lane + 1 < MOE_TOPK ? sS[nxt] + sB[nxt] : ub;
+        ok = sS[mine] - sB[mine] - hi > 1e-6 * (1.0 + fabs(sS[mine]));
+        if (lane == MOE_TOPK - 1) ok = ok && p_class(sS[mine], sS[top0]) == 2;
     }
-    __syncthreads();
-}
-
-// Whether the ranking settles the reference's selection: the 8th expert's
-// probability is a normal float (then no lower class can compete) and the
-// intervals S +- B of consecutive selected experts, and of the 8th against
-// every unselected one, are separated with a margin that keeps the
-// probabilities' order strict after expf and division rounding.
-__device__ __forceinline__ bool top_settled(const double *sS, const double *sB, const int *top9,
-                                            const double *dred) {
-    if (p_class(sS[top9[MOE_TOPK - 1]], sS[top9[0]]) != 2) return false;
-    for (int k = 0; k < MOE_TOPK; k++) {
-        const int a = top9[k];
-        const double hi = k + 1 < MOE_TOPK ? sS[top9[k + 1]] + sB[top9[k + 1]] : dred[0];
-        if (!(sS[a] - sB[a] - hi > 1e-6 * (1.0 + fabs(sS[a])))) return false;
-    }
-    return true;
+    return __all_sync(0xffffffffu, ok);
 }
 
 // Router: one cluster of RCL CTAs per token (grid (RCL, T)), 16 warps per
@@ -351,7 +344,6 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     __shared__ int cls[MOE_NEXP];
     __shared__ int top9[MOE_TOPK + 1];
     __shared__ int cand[MOE_NEXP];
-    __shared__ unsigned long long rcand[8 * (MOE_TOPK + 1)];
 
     // this CTA's router rows: independent of the upstream kernel, copied
     // into shared memory by the TMA engine before waiting on it
@@ -443,10 +435,12 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     // whenever the 8th expert's probability is a normal float (class 2: the
     // classes below only ever hold lower logits) and every decision is
     // settled by the bounds; otherwise the exact path below runs.
-    rank_top(sS, sB, rcand, tid, lane, warp, dred, top9);
-    if (tid == 0) {
-        need_exact = !top_settled(sS, sB, top9, dred);
-        ncand = 0;
+    if (warp == 0) {
+        const bool ok = select_fast(sS, sB, lane, top9);
+        if (lane == 0) {
+            need_exact = !ok;
+            ncand = 0;
+        }
     }
     __syncthreads();
     if (need_exact) {
@@ -455,8 +449,12 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
         // collapses to the exact value.  The candidates' rows are copied, 16
         // at a time, into the row buffer (its own rows are consumed).
         const double mx = sS[top9[0]];
+        // an expert whose upper bound is below every selected expert's lower
+        // bound (with margin) is out of the top 8 whatever the exact values
         const int e8 = top9[MOE_TOPK - 1];
-        const double thresh = sS[e8] - sB[e8];
+        double thresh = INFINITY;
+#pragma unroll
+        for (int k = 0; k < MOE_TOPK; k++) thresh = fmin(thresh, sS[top9[k]] - sB[top9[k]]);
         if (tid < MOE_NEXP) {
             cls[tid] = p_class(sS[tid], mx);
             if (cls[tid] > 0 && sS[tid] + sB[tid] >= thresh - 1e-6 * (1.0 + fabs(sS[e8])))
