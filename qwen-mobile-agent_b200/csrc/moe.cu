@@ -68,11 +68,6 @@ MoeScratch moe_scratch_layout(void *base, int T) {
 __device__ unsigned g_moe_timeouts;
 
 // --------------------------------------------------------------- helpers --
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 __device__ __forceinline__ double warp_max_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -332,6 +327,9 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     QMA_TRACE_SCOPE(TK_ROUTER);
     extern __shared__ __align__(128) float rrows[];        // this CTA's 16 router rows
     const unsigned rank = cluster_rank();
+    // every CTA of the cluster must have started before its shared memory is
+    // written remotely: arrive now, wait just before the first remote store
+    cluster_arrive();
     const int t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = RTHREADS / 32;
@@ -399,6 +397,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
         if (lane == 0) atomicAdd(&g_moe_timeouts, 1u);
         mbar_wait(&rbar, 0);
     }
+    cluster_wait();
     {
         double S0, B0;
         router_logit(rrows + size_t(warp) * MOE_EMBD, xn, lane, S0, B0);
@@ -624,6 +623,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
     QMA_TRACE_SCOPE(TK_EXPERT);
     extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
+    cluster_arrive();                   // paired with the wait before the first remote store
     const int slot = blockIdx.x / XCL, t = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr size_t GU_BYTES = size_t(MOE_FF) * XROW;
@@ -695,6 +695,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
         DownBytes<F>::issue(xbuf, Db, d0, &bar[1], lane);
     }
     // ---- the cluster's 512 hidden values: every CTA pushes its 32 ----------
+    cluster_wait();                     // every CTA of the cluster has started
     for (int i = tid; i < XGU * XCL; i += XTHREADS)
         st_cluster_f32(cluster_map(&hfull[g0 + i % XGU], unsigned(i / XGU)), hpart[i % XGU]);
     QMA_TRACE_MARK(TK_EXPERT, 3);
