@@ -15,6 +15,9 @@ qma_cuda_eval with the token from and the logits to host memory.
 
 gemv: Q4_K 151936x2048 GEMV at batch 1 (quantize + GEMV).
 
+moe: one MoE FFN layer (router, top-8 + shared expert, SwiGLU,
+combine, residual) for one decode token through qma_cuda_moe_layer.
+
 N > 1 runs one independent replica per GPU (weak scaling, no collective).
 --impl reference times the reference's own CPU code (oracle/_ref, built
 from its sources) on the host cores for the same workload.
@@ -52,55 +55,67 @@ def load_peaks():
 
 # ------------------------------------------------------------------ clocks --
 class ClockSampler:
-    """nvidia-smi sampling of SM clock and throttle reasons while running."""
+    """SM clock and throttle reasons sampled every 10 ms through NVML while
+    the timed region runs (reading only; nvidia-smi at 100 ms if NVML is
+    missing)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
-        self.gpu, self.proc, self.lines = gpu_index, None, []
+        self.gpu, self.samples, self.mx, self.stop = gpu_index, [], None, threading.Event()
+        self.thread = None
+
+    def _nvml(self):
+        import pynvml as N
+        N.nvmlInit()
+        h = N.nvmlDeviceGetHandleByIndex(self.gpu)
+        self.mx = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+        get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            self.samples.append((float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)), int(get_reasons(h))))
+            time.sleep(0.01)
+        N.nvmlShutdown()
+
+    def _smi(self):
+        fields = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+        proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                                 "-i", str(self.gpu), "-lms", "100"],
+                                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        threading.Thread(target=lambda: (self.stop.wait(), proc.terminate()), daemon=True).start()
+        for line in proc.stdout:
+            f = [x.strip() for x in line.split(",")]
+            try:
+                self.samples.append((float(f[0]), int(f[2], 16)))
+                self.mx = float(f[1])
+            except (ValueError, IndexError):
+                pass
+
+    def _run(self):
+        try:
+            self._nvml()
+        except Exception:
+            try:
+                self._smi()
+            except OSError:
+                pass
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            threading.Thread(target=self._read, daemon=True).start()
-        except OSError:
-            self.proc = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({nm for _, r in self.samples for nm, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.mx,
+                "reasons": reasons, "samples": len(sm)}
 
 
 # ------------------------------------------------------------- distributed --
@@ -162,6 +177,58 @@ def decode_bytes_per_token(arr, n, live_positions):
     return int(total)
 
 
+MOE_TENSORS = ("post_attention_norm.weight", "ffn_gate_inp.weight", "ffn_gate_exps.weight",
+               "ffn_up_exps.weight", "ffn_down_exps.weight", "ffn_gate_inp_shexp.weight",
+               "ffn_gate_shexp.weight", "ffn_up_shexp.weight", "ffn_down_shexp.weight")
+# DRAM bytes (read + write) one MoE block call moves, from the ncu capture of
+# the moe workload summarised in profiles/moe_block_configs0.txt
+MOE_TRAFFIC_PER_BLOCK = 20591360
+
+
+def moe_block_bytes(arr, n, il=0):
+    """Algorithmic bytes of one MoE block for one token: the router rows and
+    norms, 8 routed experts' gate/up/down and the shared expert, the input
+    read and the output written."""
+    total = 2 * 2048 * 4
+    for i in range(n):
+        t = arr[i]
+        name = t.name.decode()
+        if not name.startswith(f"blk.{il}.") or name.split(".", 2)[2] not in MOE_TENSORS:
+            continue
+        total += t.nbytes // int(t.ne[2]) * 8 if "_exps." in name else t.nbytes
+    return int(total)
+
+
+def time_moe_blocks(weights, rounds, local):
+    """Mean device time of one qma_cuda_moe_layer call (one token), cycling
+    through the given layers' weights (CUDA events on the launching stream)."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    dev = torch.device("cuda", local)
+    x2 = torch.randn((1, 2048), dtype=torch.float32, device=dev)
+    out = torch.empty_like(x2)
+    scratch = torch.empty(Q.lib().qma_cuda_moe_scratch_bytes(1), dtype=torch.uint8, device=dev)
+    ms = torch.cuda.Stream(device=dev)
+    sp = ms.cuda_stream
+
+    def one(w):
+        Q.call("qma_cuda_moe_layer", C.byref(w), Q.ptr(x2), 1, Q.ptr(out), None, None, Q.ptr(scratch),
+               scratch.numel(), sp)
+
+    torch.cuda.synchronize()
+    for w in weights:
+        one(w)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ms)
+    for _ in range(rounds):
+        for w in weights:
+            one(w)
+    e1.record(ms)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (rounds * len(weights))
+
+
 def run_decode_ours(args, world, rank, local):
     import ctypes as C
     import torch
@@ -213,6 +280,16 @@ def run_decode_ours(args, world, rank, local):
         tok = int(np.argmax(logits))
     e2e_ms = dist_max(e2e_ms, world)
 
+    # the dominant kernel pair (router + experts, the largest share of the
+    # step): one MoE block per call through the C ABI, every layer in turn
+    wts = []
+    for il in range(40):
+        w = Q.MoeWeights()
+        Q.call("qma_cuda_model_moe_weights", model.h, il, C.byref(w))
+        wts.append(w)
+    moe_us = dist_max(time_moe_blocks(wts, 8, local), world)
+    moe_b = moe_block_bytes(arr, n)
+
     value = world * args.steps / (ms / 1e3)
     e2e_value = world * e2e_steps / (e2e_ms / 1e3)
     live = min(nk_pos, 4 + 4096 + 2048) + 64
@@ -240,10 +317,15 @@ def run_decode_ours(args, world, rank, local):
                    "l2": "each step streams ~2 GB of weights (> 126 MB L2)",
                    "prefill_s": round(t_prefill, 2), "model_synth_s": round(t_model, 2),
                    "base_metric": BASE_METRIC},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "whole decode step (one CUDA graph)",
-                     "algorithmic_bytes_per_launch": bpt},
+        "roofline": {"bound": "hbm", "achieved": round(moe_b / (moe_us * 1e3), 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(moe_b / (moe_us * 1e3) / peak, 4), "traffic": MOE_TRAFFIC_PER_BLOCK,
+                     "peak_kind": peak_kind,
+                     "kernel": "MoE block: moe_router_kernel + moe_expert_kernel<FmtQ6K> via qma_cuda_moe_layer, "
+                               "one token, the 40 layers' weights in turn",
+                     "us_per_launch": round(moe_us, 2), "algorithmic_bytes_per_launch": moe_b},
+        "step_roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(achieved / peak, 4), "kernel": "whole decode step (one CUDA graph)",
+                          "algorithmic_bytes_per_step": bpt},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": N_VOCAB * 4},
         "gpu_launches": int(kernels.value) * args.steps,
@@ -410,7 +492,8 @@ def run_gemv_ours(args, world, rank, local):
                    "l2": "256 MB L2 flush between timed steps", "base_metric": BASE_METRIC},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "gemv_kernel<FmtQ4K,1,32,1,4> (register path)" if GN_OUT * GN_IN // 256 * 144 > 148 * 160 * 1024
+                     "kernel": "gemv_stream_kernel<FmtQ4K,1> (per-SM row stream through 4 shared-memory stages)"
+                               if GN_OUT * GN_IN // 256 * 144 > 148 * 160 * 1024
                                else "gemv_staged_kernel<FmtQ4K,32,1,2> (rows staged in shared memory)",
                      "algorithmic_bytes_per_launch": b},
         "e2e": {"value": round(world * b * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
@@ -419,14 +502,107 @@ def run_gemv_ours(args, world, rank, local):
     }), flush=True)
 
 
+
+# ------------------------------------------------------------------- moe ---
+MOE_METRIC = "MoE FFN layer GB/s (one decode token)"
+
+
+def run_moe_ours(args, world, rank, local):
+    """one MoE FFN layer for one token, weights generated on the
+    GPU by the engine's synthetic generator (seed 0), activation ~N(0, 1);
+    a 256 MB L2 flush between timed calls."""
+    import ctypes as C
+    import torch
+    import oracle as O
+    import qma_cuda as Q
+    Q.init(local)
+    dev = torch.device("cuda", local)
+    arr, n, size = model_layout(Q8_0)
+    idx = O.tensor_index(arr, n)
+    d = {}
+    for name in MOE_TENSORS:
+        t = arr[idx[f"blk.0.{name}"]]
+        raw = torch.empty(int(t.nbytes), dtype=torch.uint8, device=dev)
+        nel = int(t.ne[0]) * int(t.ne[1]) * int(t.ne[2])
+        Q.call("qma_cuda_synth_tensor", t.name, int(t.type), nel, SEED, Q.ptr(raw), None)
+        if "down" in name and int(t.type) != Q4_K:
+            rows, n_in, nexp = int(t.ne[1]), int(t.ne[0]), int(t.ne[2])
+            pb, gb = Q.packed_bytes(int(t.type), rows, n_in), O.row_bytes(int(t.type), n_in) * rows
+            packed = torch.empty(pb * nexp, dtype=torch.uint8, device=dev)
+            for e in range(nexp):
+                Q.call("qma_cuda_repack", int(t.type), raw.data_ptr() + e * gb, rows, n_in,
+                       packed.data_ptr() + e * pb, None)
+            raw = packed
+        d[name] = raw
+    w = Q.MoeWeights(*[d[k].data_ptr() for k in MOE_TENSORS], Q6_K, Q6_K)
+    x = np.random.default_rng(SEED + rank).standard_normal((1, 2048)).astype(np.float32)
+    dx = torch.from_numpy(x).to(dev)
+    out = torch.empty_like(dx)
+    scratch = torch.empty(Q.lib().qma_cuda_moe_scratch_bytes(1), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def moe():
+        Q.call("qma_cuda_moe_layer", C.byref(w), Q.ptr(dx), 1, Q.ptr(out), None, None, Q.ptr(scratch),
+               scratch.numel(), sp)
+
+    for _ in range(max(args.warmup, 3)):
+        moe(); flush.zero_()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            ev[i][0].record(stream); moe(); ev[i][1].record(stream)
+            flush.zero_()
+        torch.cuda.synchronize()
+        dist_barrier(world)
+    t_ms = dist_max(sum(e[0].elapsed_time(e[1]) for e in ev), world)
+    hx = torch.from_numpy(x).pin_memory()
+    hout = torch.empty((1, 2048), dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_ms = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        e0.record(stream)
+        dx.copy_(hx, non_blocking=True); moe(); hout.copy_(out, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms += e0.elapsed_time(e1)
+    e2e_ms = dist_max(e2e_ms, world)
+    b = moe_block_bytes(arr, n)
+    peak, peak_kind = load_peaks()
+    achieved = b / (t_ms / args.steps / 1e3) / 1e9
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": MOE_METRIC, "value": round(world * achieved, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4",
+        "data": "synthetic",
+        "config": {"workload": "configs[0] one qwen35moe MoE FFN layer (router 2048x256 fp32, top-8 + shared "
+                               "expert, Q4_K gate/up, Q6_K down), one decode token",
+                   "l2": "256 MB L2 flush between timed steps", "base_metric": BASE_METRIC},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": MOE_TRAFFIC_PER_BLOCK, "peak_kind": peak_kind,
+                     "kernel": "MoE block: moe_router_kernel + moe_expert_kernel<FmtQ6K>",
+                     "algorithmic_bytes_per_launch": b},
+        "e2e": {"value": round(world * b * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": 2048 * 4, "d2h_bytes_per_step": 2048 * 4},
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
+    }), flush=True)
+
+
 # ------------------------------------------------------------------ main ---
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--rows", type=int, default=GN_OUT, help="gemv: output rows")
     ap.add_argument("--cols", type=int, default=GN_IN, help="gemv: input columns (multiple of 256)")
@@ -439,9 +615,11 @@ def main():
             if args.workload == "decode":
                 run_decode_reference(args, world, rank)
             else:
-                print(json.dumps({"impl": "reference", "unavailable": "gemv reference arm: use --workload decode"}))
+                print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} reference arm: use --workload decode"}))
         elif args.workload == "decode":
             run_decode_ours(args, world, rank, local)
+        elif args.workload == "moe":
+            run_moe_ours(args, world, rank, local)
         else:
             run_gemv_ours(args, world, rank, local)
     finally:

@@ -221,6 +221,12 @@ typedef struct {
     int down_shexp_type;
 } qma_cuda_moe_weights;
 
+/* The MoE block weights of model layer `layer` (0..39) as device pointers
+ * into the model, in the form qma_cuda_moe_layer takes them: the resolved
+ * per-layer ffn_* pointers and weight types of qma_t's layers[]
+ * (qma.h:202-212) that moe_ffn reads (nn.c:509-649). */
+int qma_cuda_model_moe_weights(const qma_cuda_model *m, int layer, qma_cuda_moe_weights *out);
+
 /* Device scratch bytes qma_cuda_moe_layer needs for T tokens. */
 size_t qma_cuda_moe_scratch_bytes(int T);
 

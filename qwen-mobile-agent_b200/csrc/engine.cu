@@ -988,6 +988,13 @@ int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const vo
     return QMA_CUDA_OK;
 }
 
+int qma_cuda_model_moe_weights(const qma_cuda_model *m, int layer, qma_cuda_moe_weights *out) {
+    qma::clear_error();
+    QMA_REQUIRE(m && out && layer >= 0 && layer < qma::NLAYER, "qma_cuda_model_moe_weights: bad layer %d", layer);
+    *out = m->L[layer].moe;
+    return QMA_CUDA_OK;
+}
+
 int qma_cuda_state_create(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     qma::clear_error();
     return qma::create_state(m, n_ctx, out);

@@ -147,6 +147,97 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
                                                      lane, resid ? resid + r0 : nullptr);
 }
 
+// Single-token GEMV over a matrix too large for one staged block per SM (the
+// LM head): one persistent CTA per SM streams its contiguous row range
+// through a ring of STREAM_NST shared-memory stages, each a bulk copy of
+// `rows_blk` rows.  The copies of the next stages are in flight while the
+// current one is computed, so every SM keeps ~STREAM_NST stages of weights
+// outstanding; the first stages are issued before waiting on the upstream
+// kernel.  Warp w computes rows w, w + 16, ... of a stage.
+constexpr int STREAM_NST = 4;
+constexpr uint32_t STREAM_STAGE = 36 * 1024;    // target bytes per stage
+
+template <class F, int UPL>
+__global__ void __launch_bounds__(512, 1) gemv_stream_kernel(typename F::Ptr W, int n_in, int n_out,
+                                                           int rows_cta, int rows_blk, uint32_t stage_bytes,
+                                                           const int8_t *xq, const float *xd,
+                                                           const int16_t *xsum, float *out,
+                                                           const float *resid) {
+    QMA_TRACE_SCOPE(TK_GEMV);
+    extern __shared__ __align__(128) uint8_t sbuf[];
+    __shared__ __align__(8) uint64_t bar[STREAM_NST];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int c0 = blockIdx.x * rows_cta;
+    const int c1 = min(n_out, c0 + rows_cta);
+    const int nblk = c1 > c0 ? (c1 - c0 + rows_blk - 1) / rows_blk : 0;
+    if (tid == 0) {
+        for (int i = 0; i < STREAM_NST; i++) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    auto issue = [&](int b) {
+        const int r0 = c0 + b * rows_blk, nr = min(rows_blk, c1 - r0);
+        Stage<F>::issue(W, r0, nr, n_in, sbuf + size_t(b % STREAM_NST) * stage_bytes, &bar[b % STREAM_NST], lane);
+    };
+    if (warp == 0)
+        for (int b = 0; b < min(STREAM_NST, nblk); b++) issue(b);
+    pdl_trigger();
+    pdl_wait();
+    typename F::Act act[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; k++) F::load_act(act[k], xq, xd, xsum, lane + 32 * k);
+    bool ok = true;
+    for (int b = 0; b < nblk; b++) {
+        const int st = b % STREAM_NST;
+        const uint32_t par = uint32_t(b / STREAM_NST) & 1u;
+        if (!mbar_wait(&bar[st], par)) {
+            ok = false;
+            mbar_wait(&bar[st], par);            // let a late copy land before reuse or exit
+        }
+        const int r0 = c0 + b * rows_blk, nr = min(rows_blk, c1 - r0);
+        const auto P = Stage<F>::view(sbuf + size_t(st) * stage_bytes, nr, n_in);
+        for (int r = warp; r < nr; r += nwarps) {
+            float v = 0.0f;
+#pragma unroll
+            for (int k = 0; k < UPL; k++) {
+                typename F::Wt w;
+                F::load_w_smem(w, P, r, n_in, lane + 32 * k);
+                v += F::dot(w, act[k], lane + 32 * k);
+            }
+            v = warp_sum(v);
+            if (lane == 0) out[r0 + r] = resid ? __fadd_rn(v, resid[r0 + r]) : v;
+        }
+        __syncthreads();                          // stage st consumed
+        if (warp == 0 && b + STREAM_NST < nblk) {
+            fence_proxy_async_smem();
+            issue(b + STREAM_NST);
+        }
+    }
+    if (!ok && lane == 0) atomicAdd(&g_gemv_timeouts, 1u);
+}
+
+template <class F, int UPL>
+static int launch_stream(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq, const float *xd,
+                         const int16_t *xsum, float *out, const float *resid, cudaStream_t st) {
+    const int row_bytes = int(Stage<F>::bytes(8, n_in) / 8);
+    int rows_blk = (int(STREAM_STAGE) / row_bytes) & ~7;
+    if (rows_blk < 8) rows_blk = 8;
+    const uint32_t stage_bytes = Stage<F>::bytes(rows_blk, n_in);
+    const size_t smem = size_t(stage_bytes) * STREAM_NST;
+    static bool attr = false;
+    if (!attr) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_stream_kernel<F, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(STREAM_NST * (STREAM_STAGE + 8 * 1024))));
+        attr = true;
+    }
+    const int grid = num_sms();
+    int rows_cta = (n_out + grid - 1) / grid;
+    rows_cta = (rows_cta + 7) & ~7;
+    QMA_CHECK_CUDA(launch_ex(gemv_stream_kernel<F, UPL>, dim3(unsigned(grid)), dim3(512), smem, st, 1, pdl_enabled(),
+                             W, n_in, n_out, rows_cta, rows_blk, stage_bytes, xq, xd, xsum, out, resid));
+    return QMA_CUDA_OK;
+}
+
 int gemv_wait_timeouts() {
     unsigned n = 0;
     if (cudaMemcpyFromSymbol(&n, g_gemv_timeouts, sizeof(n)) != cudaSuccess) return -1;
@@ -265,6 +356,11 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
                        cudaStream_t st, const ConvEpi &conv) {
     int rc;
     if (T == 1 && pdl_enabled() && try_staged<F>(W, n_in, n_out, xq, xd, xsum, out, resid, st, rc, conv)) return rc;
+    // a single token over a larger matrix (the LM head): streamed per SM
+    if (T == 1 && !conv.n && n_in == 32 * F::UNIT)
+        return launch_stream<F, 1>(W, n_in, n_out, xq, xd, xsum, out, resid, st);
+    if (T == 1 && !conv.n && n_in == 64 * F::UNIT)
+        return launch_stream<F, 2>(W, n_in, n_out, xq, xd, xsum, out, resid, st);
     if (conv.n) {
         set_error("matvec: the conv epilogue needs the single-token staged path");
         return QMA_CUDA_ERR_UNSUPPORTED;

@@ -134,6 +134,9 @@ class MoeWeights(C.Structure):
                 ("down_shexp_type", _i32)]
 
 
+_SIGS["qma_cuda_model_moe_weights"] = (_i32, [_vp, _i32, C.POINTER(MoeWeights)])
+
+
 class QmaError(RuntimeError):
     """A qma_cuda_* call returned a non-zero status."""
 

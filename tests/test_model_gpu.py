@@ -225,3 +225,30 @@ def test_ecache_get_addresses_expert_records(full):
     assert g.value - g0.value == 17 * 512 * 8 * 144
     assert d.value - d0.value == 17 * Q.packed_bytes(Q.Q6_K, 2048, 512)
     assert Q.lib().qma_cuda_ecache_get(full["model"].h, 40, 0, None, None, None) == Q.ERR_INVALID
+
+
+def test_model_moe_weights_run_the_layer_moe_block(full):
+    """qma_cuda_model_moe_weights hands out layer il's MoE weights in the
+    engine's layout: qma_cuda_moe_layer on them equals the oracle's FFN half
+    of that layer (routing bit-exact, output within 1e-3)."""
+    import torch
+    il, T = 7, 3
+    w = Q.MoeWeights()
+    Q.call("qma_cuda_model_moe_weights", full["model"].h, il, C.byref(w))
+    g0 = C.c_void_p()
+    Q.call("qma_cuda_ecache_get", full["model"].h, il, 0, C.byref(g0), None, None)
+    assert w.gate_exps == g0.value and w.down_type == Q.Q6_K
+    x2 = np.random.default_rng(il).standard_normal((T, 2048)).astype(np.float32)
+    dx = torch.from_numpy(x2).cuda()
+    out = torch.empty_like(dx)
+    sel = torch.empty((T, 8), dtype=torch.int32, device="cuda")
+    scratch = torch.empty(Q.lib().qma_cuda_moe_scratch_bytes(T), dtype=torch.uint8, device="cuda")
+    Q.call("qma_cuda_moe_layer", C.byref(w), Q.ptr(dx), T, Q.ptr(out), Q.ptr(sel), None, Q.ptr(scratch),
+           scratch.numel(), None)
+    torch.cuda.synchronize()
+    want = np.zeros_like(x2)
+    wsel = np.zeros((T, 8), np.int32)
+    O.lib().qo_moe_block(full["om"], il, O._ptr(x2), T, O._ptr(want), O._ptr(wsel), None)
+    assert np.array_equal(sel.cpu().numpy(), wsel)
+    assert norm_rel(out.cpu().numpy(), want) < 1e-3
+    assert Q.lib().qma_cuda_model_moe_weights(full["model"].h, 40, C.byref(w)) == Q.ERR_INVALID
