@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
 // `rows_blk` rows.  The copies of the next stages are in flight while the
 // current one is computed, so every SM keeps ~STREAM_NST stages of weights
 // outstanding; the first stages are issued before waiting on the upstream
-// kernel.  Warp w computes rows w, w + 16, ... of a stage.
+// kernel.  Warp w computes rows w, w + 16, ... of a stage; the last warp to
+// finish a stage issues its next copy (no CTA-wide barrier per stage).
 constexpr int STREAM_NST = 4;
 constexpr uint32_t STREAM_STAGE = 36 * 1024;    // target bytes per stage
 
@@ -166,12 +167,16 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(typename F::Ptr W, 
     QMA_TRACE_SCOPE(TK_GEMV);
     extern __shared__ __align__(128) uint8_t sbuf[];
     __shared__ __align__(8) uint64_t bar[STREAM_NST];
+    __shared__ unsigned done[STREAM_NST];          // warps finished with the stage's current block
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const int c0 = blockIdx.x * rows_cta;
     const int c1 = min(n_out, c0 + rows_cta);
     const int nblk = c1 > c0 ? (c1 - c0 + rows_blk - 1) / rows_blk : 0;
     if (tid == 0) {
-        for (int i = 0; i < STREAM_NST; i++) mbar_init(&bar[i], 1);
+        for (int i = 0; i < STREAM_NST; i++) {
+            mbar_init(&bar[i], 1);
+            done[i] = 0;
+        }
         mbar_fence_init();
     }
     __syncthreads();
@@ -207,10 +212,20 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(typename F::Ptr W, 
             v = warp_sum(v);
             if (lane == 0) out[r0 + r] = resid ? __fadd_rn(v, resid[r0 + r]) : v;
         }
-        __syncthreads();                          // stage st consumed
-        if (warp == 0 && b + STREAM_NST < nblk) {
-            fence_proxy_async_smem();
-            issue(b + STREAM_NST);
+        // the last warp done with this block refills the stage; the others
+        // go on to the next block without waiting
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&done[st], 1u) == unsigned(nwarps - 1);
+        }
+        if (__shfl_sync(0xffffffffu, last, 0)) {
+            if (lane == 0) done[st] = 0;
+            if (b + STREAM_NST < nblk) {
+                fence_proxy_async_smem();
+                issue(b + STREAM_NST);
+            }
         }
     }
     if (!ok && lane == 0) atomicAdd(&g_gemv_timeouts, 1u);

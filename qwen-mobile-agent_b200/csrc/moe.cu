@@ -21,6 +21,8 @@
 //               and adds the residual.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
@@ -573,6 +575,24 @@ template <> struct DownPtr<FmtQ4K> {
 // Every wait on a copy is bounded; a copy that never lands is counted in
 // g_moe_timeouts (the host fails the call) and the CTA still takes part in
 // the cluster barriers so that no peer waits forever.
+// The down rows' format, read from shared memory.  For Q6_K the hidden
+// vector's Q8_K bytes are read from a unit-interleaved copy (16-byte chunk k
+// of 128-byte unit u at chunk 4k + u): the four lanes of a row, which take
+// units 0..3, then hit four different bank groups instead of one.
+template <class F> struct DownRows : SmemRows<F> {};
+template <> struct DownRows<FmtQ6K> : SmemRows<FmtQ6K> {
+    __device__ static void load_act(Act &a, const int8_t *xq, const float *xd, const int16_t *, int u) {
+        const int4 *p = reinterpret_cast<const int4 *>(xq);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int4 v = p[4 * k + u];
+            a.x[4 * k] = v.x; a.x[4 * k + 1] = v.y; a.x[4 * k + 2] = v.z; a.x[4 * k + 3] = v.w;
+        }
+        a.xd = xd[u >> 1];
+    }
+};
+static_assert(MOE_FF / FmtQ6K::UNIT == 4, "interleave stride = units per down row");
+
 template <class F> struct DownBytes;
 template <> struct DownBytes<FmtQ6K> {
     static constexpr uint32_t QL = XDN * (MOE_FF / 2), QH = XDN * (MOE_FF / 4), SC = XDN * (MOE_FF / 16),
@@ -632,6 +652,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
     __shared__ float hpart[XGU];
     __shared__ __align__(16) float hfull[MOE_FF];
     __shared__ __align__(16) int8_t hq[MOE_FF];
+    __shared__ __align__(16) int8_t hqi[MOE_FF];           // unit-interleaved copy (Q6_K down rows)
     __shared__ float hd[MOE_FF / 256];
     __shared__ int16_t hs[MOE_FF / 16];
     __shared__ int is_last;
@@ -708,13 +729,21 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
         q8k_block_warp(v, lane, hq + warp * 256, hd + warp, hs + warp * 16);
     }
     __syncthreads();
+    if constexpr (std::is_same<F, FmtQ6K>::value) {
+        if (tid < MOE_FF / 16) {
+            const int u = tid >> 3, k = tid & 7;          // chunk k of 128-byte unit u
+            reinterpret_cast<int4 *>(hqi)[4 * k + u] = reinterpret_cast<const int4 *>(hq)[tid];
+        }
+        __syncthreads();
+    }
     // ---- down rows d0 .. d0 + XDN from shared memory --------------------------
     QMA_TRACE_MARK(TK_EXPERT, 5);
     const bool dn_ok = mbar_wait(&bar[1], 0);
     QMA_TRACE_MARK(TK_EXPERT, 6);
     float *part = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + d0;
     if (dn_ok) {
-        gemv_warp_rows<SmemRows<F>, 1, LPR, 1, 1>(DownBytes<F>::at(xbuf), MOE_FF, XDN, hq, hd, hs, part, 0,
+        gemv_warp_rows<DownRows<F>, 1, LPR, 1, 1>(DownBytes<F>::at(xbuf), MOE_FF, XDN,
+                                                  std::is_same<F, FmtQ6K>::value ? hqi : hq, hd, hs, part, 0,
                                                   warp, XTHREADS / 32, lane);
     } else {
         if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
