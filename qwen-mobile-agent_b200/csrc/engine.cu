@@ -83,6 +83,7 @@ struct qma_cuda_state {
     float *argmax_pv = nullptr;         // per-CTA partial maxima
     int *argmax_pi = nullptr;
     unsigned *argmax_cnt = nullptr;     // ticket, zero between steps
+    unsigned *gdn_cnt = nullptr;        // [16] gated-norm tickets, zero between layers
     // attention scratch, grown on demand
     float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr, *ml = nullptr;
     size_t scores_cap = 0, cmax_cap = 0, opart_cap = 0, lpart_cap = 0;
@@ -414,6 +415,7 @@ static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     TRY(salloc_t(s, &s->argmax_pv, ARG_CTAS, st));
     TRY(salloc_t(s, &s->argmax_pi, ARG_CTAS, st));
     TRY(salloc_t(s, &s->argmax_cnt, 1, st));
+    TRY(salloc_t(s, &s->gdn_cnt, VHEADS / 2, st));
     s->logits_rows = 1;
     TRY(salloc_t(s, &s->logits, size_t(m->n_vocab), st));
 #undef TRY
@@ -731,10 +733,17 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         } else {
             const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
             if (!conv_fused) TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
-            TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
-                           L.dt, L.a, s->ssm[il], T, s->gdo, st));
-            TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
-                                        s->xs, st));
+            if (T == 1) {
+                // one token: the gated norm + Q8_K run in the recurrence kernel's tail
+                const GdnNormArgs gna = {s->proj + CONV_DIM, L.ssm_norm, s->xq, s->xd, s->xs, s->gdn_cnt};
+                TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
+                               L.dt, L.a, s->ssm[il], T, s->gdo, st, &gna));
+            } else {
+                TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
+                               L.dt, L.a, s->ssm[il], T, s->gdo, st));
+                TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
+                                            s->xs, st));
+            }
             TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
         }
         if (il == n_layers - 1 && s->stop_before_moe) {

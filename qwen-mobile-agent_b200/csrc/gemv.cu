@@ -63,13 +63,10 @@ __device__ unsigned g_gemv_timeouts;
 // equal share of the CTA's rows, in batches of up to 8 independent dot
 // products followed by one 8-way warp reduction.
 template <class F, int UPL>
-__device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in, int nr, const int8_t *xq,
-                                              const float *xd, const int16_t *xsum, float *out,
+__device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in, int nr,
+                                              const typename F::Act (&act)[UPL], float *out,
                                               const float *resid, int warp, int nwarps, int lane,
                                               int row0, const ConvEpi &conv) {
-    typename F::Act act[UPL];
-#pragma unroll
-    for (int k = 0; k < UPL; k++) F::load_act(act[k], xq, xd, xsum, lane + 32 * k);
     const int idx = warp_sum8_index(lane);
     // the CTA's rows spread evenly over its warps, in batches of up to 8
     const int rpw = (nr + nwarps - 1) / nwarps;
@@ -131,20 +128,29 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
     __syncthreads();
     pdl_trigger();
     pdl_wait();
+    QMA_TRACE_MARK(TK_GEMV, 1);
     if (nr <= 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    // the activation slices load while the last weight bytes land
+    typename F::Act act[LPR == 32 ? UPL : 1];
+    if constexpr (LPR == 32) {
+#pragma unroll
+        for (int k = 0; k < UPL; k++) F::load_act(act[k], xq, xd, xsum, lane + 32 * k);
+    }
     if (!mbar_wait(&bar, 0)) {
         if (threadIdx.x == 0) atomicAdd(&g_gemv_timeouts, 1u);
         mbar_wait(&bar, 0);     // let a late copy land before the CTA exits
         return;
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    QMA_TRACE_MARK(TK_GEMV, 2);
     const auto P = Stage<F>::view(wbuf, nr, n_in);
     if constexpr (LPR == 32)
-        staged_rows32<F, UPL>(P, n_in, nr, xq, xd, xsum, out + r0, resid ? resid + r0 : nullptr, warp, nwarps,
-                              lane, r0, conv);
+        staged_rows32<F, UPL>(P, n_in, nr, act, out + r0, resid ? resid + r0 : nullptr, warp, nwarps, lane, r0,
+                              conv);
     else
         gemv_warp_rows<SmemRows<F>, 1, LPR, UPL, RU>(P, n_in, nr, xq, xd, xsum, out + r0, 0, warp, nwarps,
                                                      lane, resid ? resid + r0 : nullptr);
+    QMA_TRACE_MARK(TK_GEMV, 3);
 }
 
 // Single-token GEMV over a matrix too large for one staged block per SM (the
@@ -278,9 +284,7 @@ static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const in
         attr = true;
     }
     const int grid = (n_out + rows_cta - 1) / rows_cta;
-    // small row blocks (the output projections) take 8 warps, leaving room on
-    // the SM for the next kernel's CTAs (the router) to start early
-    const unsigned threads = rows_cta <= 64 ? 256 : 512;
+    const unsigned threads = 512;
     QMA_CHECK_CUDA(launch_ex(gemv_staged_kernel<F, LPR, UPL, RU>, dim3(unsigned(grid)), dim3(threads), smem, st, 1,
                              pdl_enabled(), W, n_in, n_out, rows_cta, xq, xd, xsum, out, resid, conv));
     return QMA_CUDA_OK;

@@ -190,6 +190,15 @@ int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T,
 }
 
 // ---------------------------------------------------- gated delta net -----
+struct GdnNorm {
+    const float *z = nullptr;     // gate row (the in-projection's z rows), token 0
+    const float *w = nullptr;     // ssm_norm [128]
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int16_t *xs = nullptr;
+    unsigned *cnt = nullptr;      // [16] tickets, zero between calls
+};
+
 // gdn_worker (nn.c:784-833) with the per-head L2 norms of q/k (l2norm_skv,
 // nn.c:744-761), the 16 -> 32 head expansion h % 16 (nn.c:2204), beta =
 // sigmoid(.) (nn.c:2170) and g = softplus(alpha + dt) * a (nn.c:2172-2180).
@@ -197,12 +206,17 @@ int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T,
 // updates independently given q, k, v_j, g, beta, so a head is split over 4
 // CTAs of 32 rows; 8 threads own a row (16 elements each), the rows stay in
 // registers across the T tokens.
+//
+// With gn.cnt set (one token), the gated RMSNorm and the Q8_K quantization
+// for ssm_out (the work of gated_norm_quant_kernel) follow in the same
+// kernel: the last of the 8 CTAs of a head pair (a ticket per pair) forms
+// that pair's 256-lane Q8_K block from the pair's outputs.
 __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv_out,
                                                   const float *__restrict__ proj, int proj_ld,
                                                   int beta_off, int alpha_off,
                                                   const float *__restrict__ dt,
                                                   const float *__restrict__ av, float *ssm, int T,
-                                                  float *o) {
+                                                  float *o, GdnNorm gn) {
     QMA_TRACE_SCOPE(TK_GDN);
     const int rb = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -277,12 +291,66 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
 #pragma unroll
     for (int k = 0; k < 4; k++)
         reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
+    if (!gn.cnt) return;
+    // ---- gated RMSNorm + Q8_K of head pair h >> 1 (T == 1) -----------------
+    // rms_norm_head(ssm_norm) (nn.c:360-372) then * silu(z) (nn.c:2238-2242),
+    // quantized like quantize_row_q8k (q8k.c:34-85)
+    __shared__ int is_last;
+    __shared__ double hss[8];
+    __shared__ float hmax[8];
+    const int pair = h >> 1;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        is_last = atomicAdd(&gn.cnt[pair], 1u) == 7u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int hh = pair * 2 + (tid >> 7), i = tid & (SSTATE - 1);   // thread = lane of the block
+    const float v = __ldcg(o + hh * SSTATE + i);
+    const double sq = warp_sum_d(double(v) * double(v));
+    if (lane == 0) hss[warp] = sq;
+    __syncthreads();
+    const int w0 = (tid >> 7) * 4;
+    const double tot = (hss[w0] + hss[w0 + 1]) + (hss[w0 + 2] + hss[w0 + 3]);
+    const float r = 1.0f / sqrtf(float(tot / SSTATE) + 1e-6f);
+    const float zz = gn.z[hh * SSTATE + i];
+    const float normed = __fmul_rn(v, __fmul_rn(r, gn.w[i]));
+    const float y = __fmul_rn(normed, zz / (1.0f + expf(-zz)));
+    const float am = warp_max(fabsf(y));
+    if (lane == 0) hmax[warp] = am;
+    __syncthreads();
+    float amax = hmax[0];
+#pragma unroll
+    for (int k = 1; k < 8; k++) amax = fmaxf(amax, hmax[k]);
+    const float sc = amax > 0.0f ? amax / 127.0f : 1.0f;
+    const float inv = 1.0f / sc;
+    int iv = static_cast<int>(roundf(__fmul_rn(y, inv)));
+    iv = iv > 127 ? 127 : (iv < -127 ? -127 : iv);
+    gn.xq[pair * 256 + tid] = static_cast<int8_t>(iv);
+    const int sum = group_sum_i(iv, 16);
+    if ((lane & 15) == 0) gn.xs[pair * 16 + (tid >> 4)] = static_cast<int16_t>(sum);
+    if (tid == 0) {
+        gn.xd[pair] = sc;
+        gn.cnt[pair] = 0;
+    }
 }
 
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
-               const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st) {
+               const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
+               const GdnNormArgs *norm) {
+    GdnNorm gn;
+    if (norm && T == 1) {
+        gn.z = norm->z;
+        gn.w = norm->w;
+        gn.xq = norm->xq;
+        gn.xd = norm->xd;
+        gn.xs = norm->xs;
+        gn.cnt = norm->cnt;
+    }
     QMA_CHECK_CUDA(launch_ex(gdn_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj, proj_ld,
-                             beta_off, alpha_off, dt, a, ssm, T, o));
+                             beta_off, alpha_off, dt, a, ssm, T, o, gn));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }

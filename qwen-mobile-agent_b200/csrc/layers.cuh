@@ -56,8 +56,19 @@ int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *x
                          int16_t *xs, cudaStream_t st, const Prefetch &pf = Prefetch());
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
                   cudaStream_t st);
+// Optional tail of a single-token gated delta net: the gated RMSNorm and the
+// Q8_K for ssm_out written to xq / xd / xs (cnt: 16 zeroed tickets).
+struct GdnNormArgs {
+    const float *z;
+    const float *w;
+    int8_t *xq;
+    float *xd;
+    int16_t *xs;
+    unsigned *cnt;
+};
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
-               const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st);
+               const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
+               const GdnNormArgs *norm = nullptr);
 int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
                             int8_t *xq, float *xd, int16_t *xs, cudaStream_t st);
 
