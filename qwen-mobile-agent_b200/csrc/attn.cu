@@ -473,6 +473,249 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
     }
 }
 
+// ------------------------------------------ single-token chunk attention --
+// The decode form of attn_chunk_kernel (one query token, span <= 64), same
+// outputs and the same folded record arithmetic, arranged for latency:
+//   * the records of every position but the newest (the one this step's
+//     qk_prep appends) are copied into shared memory before waiting on the
+//     upstream kernel: the live index and the older records were written
+//     before this step's first kernel started;
+//   * scores: thread (position i = tid / 4, dim quarter tid % 4) takes 64
+//     dims of all 8 query heads, then a 4-lane butterfly; the query rows are
+//     stored at row e ^ ((e >> 6) & 3) so the four quarters read different
+//     banks.
+constexpr int DSPAN = 64;
+
+struct DecSmem {
+    float qT[HEAD_DIM][8];
+    float X4[8][8], X2[8][4];
+    uint4 kst[DSPAN][10], vst[DSPAN][10];
+    int isq2[DSPAN];
+    float ps[8][DSPAN];
+    float W[DSPAN][8][8];
+    float U4[8][8], U2[8][4];
+};
+
+__device__ __forceinline__ int qrow(int e) { return e ^ ((e >> 6) & 3); }
+
+__global__ void __launch_bounds__(256) attn_decode_kernel(const float *__restrict__ qr,
+                                                          const uint8_t *__restrict__ kv,
+                                                          const uint8_t *__restrict__ arena,
+                                                          const int *__restrict__ live,
+                                                          const StepParams *spp, int nk_max,
+                                                          int span, int nchunk, float *scores,
+                                                          float *mpart, float *lpart, float *opart) {
+    QMA_TRACE_SCOPE(TK_ATTN_CHUNK);
+    extern __shared__ __align__(16) uint8_t dec_raw[];
+    DecSmem &S = *reinterpret_cast<DecSmem *>(dec_raw);
+    const int chunk = blockIdx.x, kh = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const StepParams sp = *spp;                  // written before this step began
+    const int nk = nk_of(sp, 0);
+    const int j0 = chunk * span;
+    if (j0 >= nk) {
+        pdl_trigger();
+        return;
+    }
+    const int bn = min(nk, j0 + span) - j0;
+    const uint8_t *kring = kv + size_t(kh) * sp.n_ctx * KVQ_SLOT;
+    const uint8_t *vring = kv + size_t(NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT;
+    const uint8_t *kar = arena + size_t(kh) * HCM_H_PIN * KVQ_SLOT;
+    const uint8_t *var = arena + size_t(NHEAD_KV + kh) * HCM_H_PIN * KVQ_SLOT;
+    // the ring slot qk_prep rewrites in this step: a record in it is read
+    // after the wait (the newest position, or an older one it overwrites)
+    const uint8_t *knew = kring + size_t(hcm_slot(sp.n_pos, sp.n_ctx)) * KVQ_SLOT;
+    // record words: thread (position i, word wq)
+    for (int idx = tid; idx < bn * 10; idx += 256) {
+        const int i = idx / 10, wq = idx % 10;
+        bool q2, q2v;
+        const uint8_t *kp = rec_of(sp, live, kring, kar, j0 + i, q2);
+        const uint8_t *vp = rec_of(sp, live, vring, var, j0 + i, q2v);
+        const bool late = kp == knew || kp == knew + KVQ2_OFF;
+        if (wq == 0) S.isq2[i] = int(q2) | (late ? 2 : 0);
+        if (!late && wq < (q2 ? 5 : 10)) {
+            S.kst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(kp) + wq);
+            S.vst[i][wq] = __ldg(reinterpret_cast<const uint4 *>(vp) + wq);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();
+    for (int idx = tid; idx < bn * 10; idx += 256) {
+        const int i = idx / 10, wq = idx % 10;
+        if (!(S.isq2[i] & 2)) continue;
+        bool q2, q2v;
+        const uint8_t *kp = rec_of(sp, live, kring, kar, j0 + i, q2);
+        const uint8_t *vp = rec_of(sp, live, vring, var, j0 + i, q2v);
+        if (wq < (q2 ? 5 : 10)) {
+            S.kst[i][wq] = __ldcg(reinterpret_cast<const uint4 *>(kp) + wq);
+            S.vst[i][wq] = __ldcg(reinterpret_cast<const uint4 *>(vp) + wq);
+        }
+    }
+    __syncthreads();
+    if (tid < bn) S.isq2[tid] &= 1;
+    for (int i = tid; i < 8 * HEAD_DIM; i += 256) {
+        const int h = i / HEAD_DIM, e = i % HEAD_DIM;
+        S.qT[qrow(e)][h] = qr[(size_t(kh) * 8) * HEAD_DIM + i];
+    }
+    {   // warp h: sub-block sums of query head h
+        const float *q = qr + (size_t(kh) * 8 + warp) * HEAD_DIM;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = q[lane + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float x4 = warp_sum(v[k]);
+            if (lane == 0) S.X4[warp][k] = x4;
+        }
+        __syncwarp();
+        if (lane < 4) S.X2[warp][lane] = S.X4[warp][2 * lane] + S.X4[warp][2 * lane + 1];
+    }
+    __syncthreads();
+    {   // scores: thread (position i, quarter qd) over dims 64 qd .. 64 qd + 63
+        const int i = tid >> 2, qd = tid & 3;
+        float s8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        const bool live_i = i < bn;
+        if (live_i) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(S.kst[i]);
+            if (!S.isq2[i]) {
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    const int sb = 2 * qd + half;
+                    const uint32_t hdr = w[5 * sb];
+                    const float dd = h2f(uint16_t(hdr & 0xffff)), mm = h2f(uint16_t(hdr >> 16));
+                    float a8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int wi = 0; wi < 4; wi++) {
+                        const uint32_t nw = w[5 * sb + 1 + wi];
+#pragma unroll
+                        for (int k = 0; k < 8; k++) {
+                            const float qf = small2f((nw >> (4 * k)) & 0xFu);
+                            const float *x = S.qT[qrow(sb * 32 + wi * 8 + k)];
+                            const float4 xa = *reinterpret_cast<const float4 *>(x);
+                            const float4 xb = *reinterpret_cast<const float4 *>(x + 4);
+                            a8[0] = fmaf(qf, xa.x, a8[0]); a8[1] = fmaf(qf, xa.y, a8[1]);
+                            a8[2] = fmaf(qf, xa.z, a8[2]); a8[3] = fmaf(qf, xa.w, a8[3]);
+                            a8[4] = fmaf(qf, xb.x, a8[4]); a8[5] = fmaf(qf, xb.y, a8[5]);
+                            a8[6] = fmaf(qf, xb.z, a8[6]); a8[7] = fmaf(qf, xb.w, a8[7]);
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 8; h++) s8[h] = fmaf(mm, S.X4[h][sb], fmaf(dd, a8[h], s8[h]));
+                }
+            } else {
+                const int sb = qd;
+                const uint32_t hdr = w[5 * sb];
+                const float dd = h2f(uint16_t(hdr & 0xffff)), mm = h2f(uint16_t(hdr >> 16));
+                float a8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int wi = 0; wi < 4; wi++) {
+                    const uint32_t pw = w[5 * sb + 1 + wi];
+#pragma unroll
+                    for (int k = 0; k < 16; k++) {
+                        const float qf = small2f((pw >> (2 * k)) & 3u);
+                        const float *x = S.qT[qrow(sb * 64 + wi * 16 + k)];
+                        const float4 xa = *reinterpret_cast<const float4 *>(x);
+                        const float4 xb = *reinterpret_cast<const float4 *>(x + 4);
+                        a8[0] = fmaf(qf, xa.x, a8[0]); a8[1] = fmaf(qf, xa.y, a8[1]);
+                        a8[2] = fmaf(qf, xa.z, a8[2]); a8[3] = fmaf(qf, xa.w, a8[3]);
+                        a8[4] = fmaf(qf, xb.x, a8[4]); a8[5] = fmaf(qf, xb.y, a8[5]);
+                        a8[6] = fmaf(qf, xb.z, a8[6]); a8[7] = fmaf(qf, xb.w, a8[7]);
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 8; h++) s8[h] = fmaf(mm, S.X2[h][sb], fmaf(dd, a8[h], s8[h]));
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 8; h++) {
+            s8[h] += __shfl_xor_sync(0xffffffffu, s8[h], 1);
+            s8[h] += __shfl_xor_sync(0xffffffffu, s8[h], 2);
+        }
+#pragma unroll
+        for (int h = 0; h < 8; h++) {
+            if ((h >> 1) != qd) continue;               // lane qd keeps heads 2 qd, 2 qd + 1
+            const float sc = live_i ? __fmul_rn(s8[h], 0.0625f) : -INFINITY;    // 1 / sqrtf(256)
+            if (live_i) scores[(size_t(kh) * 8 + h) * nk_max + j0 + i] = sc;
+            S.ps[h][i] = sc;
+        }
+    }
+    __syncthreads();
+    float m_h = -INFINITY, l_h = 0.0f;
+    {   // warp h: max and sum of p = expf(s - max) of head h over the chunk
+        const int h = warp;
+        const float s0 = S.ps[h][lane], s1 = S.ps[h][lane + 32];
+        m_h = warp_max(fmaxf(s0, s1));
+        const float p0 = lane < bn ? expf(s0 - m_h) : 0.0f;
+        const float p1 = lane + 32 < bn ? expf(s1 - m_h) : 0.0f;
+        S.ps[h][lane] = p0;
+        S.ps[h][lane + 32] = p1;
+        l_h = warp_sum(p0 + p1);
+    }
+    __syncthreads();
+    // p * d per (position, sub-block, head); sum p * m per (head, sub-block)
+    for (int e = tid; e < bn * 64; e += 256) {
+        const int i = e >> 6, sb = (e >> 3) & 7, h = e & 7;
+        float wv = 0.0f;
+        if (!S.isq2[i] || sb < 4) {
+            const uint32_t hdr = reinterpret_cast<const uint32_t *>(S.vst[i])[5 * sb];
+            wv = __fmul_rn(S.ps[h][i], h2f(uint16_t(hdr & 0xffff)));
+        }
+        S.W[i][sb][h] = wv;
+    }
+    {   // thread (h, sb, quarter): a quarter of the positions, then a 4-lane sum
+        const int h = tid >> 5, sb = (tid >> 2) & 7, qtr = tid & 3;
+        float u4 = 0.0f, u2 = 0.0f;
+        for (int i = qtr; i < bn; i += 4) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(S.vst[i]);
+            if (!S.isq2[i]) u4 = fmaf(S.ps[h][i], h2f(uint16_t(w[5 * sb] >> 16)), u4);
+            else if (sb < 4) u2 = fmaf(S.ps[h][i], h2f(uint16_t(w[5 * sb] >> 16)), u2);
+        }
+        u4 += __shfl_xor_sync(0xffffffffu, u4, 1);
+        u4 += __shfl_xor_sync(0xffffffffu, u4, 2);
+        u2 += __shfl_xor_sync(0xffffffffu, u2, 1);
+        u2 += __shfl_xor_sync(0xffffffffu, u2, 2);
+        if (qtr == 0) {
+            S.U4[h][sb] = u4;
+            if (sb < 4) S.U2[h][sb] = u2;
+        }
+    }
+    __syncthreads();
+    // p . V for output dim d (the q * (p d) part)
+    const int d = tid;
+    float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    for (int i = 0; i < bn; i++) {
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(S.vst[i]);
+        float qf;
+        int sb;
+        if (!S.isq2[i]) {
+            sb = d >> 5;
+            qf = small2f((w[5 * sb + 1 + ((d & 31) >> 3)] >> (4 * (d & 7))) & 0xFu);
+        } else {
+            sb = d >> 6;
+            qf = small2f((w[5 * sb + 1 + ((d & 63) >> 4)] >> (2 * (d & 15))) & 3u);
+        }
+        const float4 wa = *reinterpret_cast<const float4 *>(&S.W[i][sb][0]);
+        const float4 wb = *reinterpret_cast<const float4 *>(&S.W[i][sb][4]);
+        acc[0] = fmaf(wa.x, qf, acc[0]);
+        acc[1] = fmaf(wa.y, qf, acc[1]);
+        acc[2] = fmaf(wa.z, qf, acc[2]);
+        acc[3] = fmaf(wa.w, qf, acc[3]);
+        acc[4] = fmaf(wb.x, qf, acc[4]);
+        acc[5] = fmaf(wb.y, qf, acc[5]);
+        acc[6] = fmaf(wb.z, qf, acc[6]);
+        acc[7] = fmaf(wb.w, qf, acc[7]);
+    }
+    const size_t base = (size_t(kh) * 8) * nchunk + chunk;
+#pragma unroll
+    for (int h = 0; h < 8; h++)
+        opart[(base + size_t(h) * nchunk) * HEAD_DIM + d] = acc[h] + S.U4[h][d >> 5] + S.U2[h][d >> 6];
+    if (lane == 0) {
+        mpart[base + size_t(warp) * nchunk] = m_h;
+        lpart[base + size_t(warp) * nchunk] = l_h;
+    }
+}
+
 // -------------------------------------- combine + sigmoid gate + Q8_K ----
 // One CTA per (query head h, query t), thread = output dim: M = max of the
 // chunk maxima, f_c = expf(m_c - M), L = sum f_c l_c, o = (sum_c f_c o_c) *
@@ -611,9 +854,20 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
                                             int(sizeof(ChunkSmem))));
         attr = true;
     }
-    QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), sizeof(ChunkSmem), st, 1, pdl_enabled(), a.qr,
-                             a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk, a.scores, a.cmax,
-                             a.lpart, a.opart));
+    static bool attr_dec = false;
+    if (!attr_dec) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(sizeof(DecSmem))));
+        attr_dec = true;
+    }
+    if (a.T == 1 && a.pv_chunk <= DSPAN)
+        QMA_CHECK_CUDA(launch_ex(attn_decode_kernel, dim3(nchunk, NHEAD_KV), dim3(256), sizeof(DecSmem), st, 1,
+                                 pdl_enabled(), a.qr, a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk,
+                                 a.scores, a.cmax, a.lpart, a.opart));
+    else
+        QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), sizeof(ChunkSmem), st, 1,
+                                 pdl_enabled(), a.qr, a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk,
+                                 a.scores, a.cmax, a.lpart, a.opart));
     QMA_CHECK_LAUNCH();
     const size_t fsh = sizeof(float) * size_t(nchunk);
     if (fsh > 48 * 1024) {
