@@ -58,32 +58,28 @@ __device__ __forceinline__ const uint8_t *rec_of(const StepParams &sp, const int
 // old q4 record against the new vector (kvq4_qf, kvq.c:84-100), then writes
 // the q4 and q2 records (kvq4_quant / kvq2_quant, kvq.c:25-70), and the
 // slot's salience in every layer is reset to 0.
-__device__ __forceinline__ void head_norm(float (&x)[8], const float *w, int lane) {
+__device__ __forceinline__ void head_norm(float (&x)[8], const float (&wv)[8]) {
     double ss = 0.0;
 #pragma unroll
     for (int k = 0; k < 8; k++) ss += double(x[k]) * double(x[k]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float r = 1.0f / sqrtf(float(ss / HEAD_DIM) + 1e-6f);
-    const float4 w0 = *reinterpret_cast<const float4 *>(w + lane * 8);
-    const float4 w1 = *reinterpret_cast<const float4 *>(w + lane * 8 + 4);
-    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int k = 0; k < 8; k++) x[k] = __fmul_rn(x[k], __fmul_rn(r, wv[k]));
 }
 
-// rotate pairs (j, j+32), j < 32: lanes 0..3 hold j, lanes 4..7 hold j+32
-__device__ __forceinline__ void head_rope(float (&x)[8], const float *cs, int lane) {
+// rotate pairs (j, j+32), j < 32: lanes 0..3 hold j, lanes 4..7 hold j+32;
+// c / sn: the cos / sin of the lane's 8 pairs (lanes < 8)
+__device__ __forceinline__ void head_rope(float (&x)[8], const float (&c)[8], const float (&sn)[8], int lane) {
     float y[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) y[k] = __shfl_xor_sync(0xffffffffu, x[k], 4);
     if (lane < 8) {
-        const int j0 = (lane & 3) * 8;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const float c = cs[j0 + k], sn = cs[NROT / 2 + j0 + k];
-            if (lane < 4) x[k] = __fsub_rn(__fmul_rn(x[k], c), __fmul_rn(y[k], sn));
-            else x[k] = __fadd_rn(__fmul_rn(y[k], sn), __fmul_rn(x[k], c));
+            if (lane < 4) x[k] = __fsub_rn(__fmul_rn(x[k], c[k]), __fmul_rn(y[k], sn[k]));
+            else x[k] = __fadd_rn(__fmul_rn(y[k], sn[k]), __fmul_rn(x[k], c[k]));
         }
     }
 }
@@ -104,19 +100,38 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
     QMA_TRACE_SCOPE(TK_QK_PREP);
     const int t = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float qfv[4];
-    pdl_trigger();
-    pdl_wait();
+    // Everything but the projection row was written before this step began
+    // (step parameters, rope table, norm weights, the slot's old record):
+    // read it before waiting on the input projection.
     const StepParams sp = *spp;
     const int pos = sp.n_pos + t;
     const int slot = hcm_slot(pos, sp.n_ctx);
-    const float *row = proj + size_t(t) * proj_ld;
     const float *cs = rope + size_t(pos) * NROT;     // [32 cos][32 sin]
+    float wv[8], c[8], sn[8];
+    if (part < 4 || warp < 2) {
+        ld8(wv, (part < 4 ? qn : kn) + lane * 8);
+        if (lane < 8) {
+            ld8(c, cs + (lane & 3) * 8);
+            ld8(sn, cs + NROT / 2 + (lane & 3) * 8);
+        }
+    }
+    const int kh = warp & 1;
+    uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
+    uint32_t old_hdr = 0, old_nw = 0;
+    if (part == 4) {
+        const uint32_t *sbw = reinterpret_cast<const uint32_t *>(rec + (lane >> 2) * 20);
+        old_hdr = sbw[0];
+        old_nw = sbw[1 + (lane & 3)];
+    }
+    pdl_trigger();
+    pdl_wait();
+    const float *row = proj + size_t(t) * proj_ld;
     float x[8];
     if (part < 4) {
         const int h = part * 4 + warp;
         ld8(x, row + h * (2 * HEAD_DIM) + lane * 8);
-        head_norm(x, qn, lane);
-        head_rope(x, cs, lane);
+        head_norm(x, wv);
+        head_rope(x, c, sn, lane);
         st8(qr + (size_t(t) * NHEAD + h) * HEAD_DIM + lane * 8, x);
         float g[8];
         ld8(g, row + h * (2 * HEAD_DIM) + HEAD_DIM + lane * 8);
@@ -124,20 +139,16 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
         return;
     }
     // warp w: record w = K0, K1, V0, V1
-    const int kh = warp & 1;
     if (warp < 2) {
         ld8(x, row + WQ_DIM + kh * HEAD_DIM + lane * 8);
-        head_norm(x, kn, lane);
-        head_rope(x, cs, lane);
+        head_norm(x, wv);
+        head_rope(x, c, sn, lane);
     } else {
         ld8(x, row + WQ_DIM + WKV_DIM + kh * HEAD_DIM + lane * 8);
     }
-    uint8_t *rec = kv + (size_t(warp >> 1) * NHEAD_KV + kh) * sp.n_ctx * KVQ_SLOT + size_t(slot) * KVQ_SLOT;
     {   // Q-Hitter score of the slot's current q4 record against x (lane:
         // elements 8l .. 8l+7, sub-block l / 4)
-        const uint32_t *sbw = reinterpret_cast<const uint32_t *>(rec + (lane >> 2) * 20);
-        const uint32_t hdr = sbw[0];
-        const uint32_t nw = sbw[1 + (lane & 3)];
+        const uint32_t hdr = old_hdr, nw = old_nw;
         const float d = h2f(uint16_t(hdr & 0xffff)), m = h2f(uint16_t(hdr >> 16));
         double se = 0.0, sx = 0.0;
 #pragma unroll
@@ -181,8 +192,8 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
         blk[1 + (lane & 3)] = w;
         if ((lane & 3) == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
     }
-    // q2: 4 sub-blocks of 64; value i at bits 2 (i & 3) of payload byte i / 4,
-    // OR-ed into the existing payload.  Lane l: sub-block l / 8, values
+    // q2: 4 sub-blocks of 64; value i at bits 2 (i & 3) of payload byte i / 4;
+    // each payload word is assembled from a lane pair and stored whole.  Lane l: sub-block l / 8, values
     // 8 (l % 8) .. +7 = payload bytes 2 (l % 8), 2 (l % 8) + 1 = the half
     // (l % 2) of payload word (l % 8) / 2.
     {
@@ -206,7 +217,7 @@ __global__ void __launch_bounds__(128) qk_prep_append_kernel(
         w <<= 16 * (lane & 1);
         w |= __shfl_xor_sync(0xffffffffu, w, 1);
         uint32_t *blk = reinterpret_cast<uint32_t *>(rec + KVQ2_OFF + (lane >> 3) * 20);
-        if ((lane & 1) == 0) blk[1 + ((lane & 7) >> 1)] |= w;
+        if ((lane & 1) == 0) blk[1 + ((lane & 7) >> 1)] = w;   // both halves: the whole word
         if ((lane & 7) == 0) blk[0] = uint32_t(f2h(d)) | (uint32_t(f2h(mn)) << 16);
     }
     __syncthreads();

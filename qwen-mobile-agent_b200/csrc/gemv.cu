@@ -66,7 +66,8 @@ template <class F, int UPL>
 __device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in, int nr,
                                               const typename F::Act (&act)[UPL], float *out,
                                               const float *resid, int warp, int nwarps, int lane,
-                                              int row0, const ConvEpi &conv) {
+                                              int row0, const ConvEpi &conv, const float4 *cw,
+                                              const float *cs) {
     const int idx = warp_sum8_index(lane);
     // the CTA's rows spread evenly over its warps, in batches of up to 8
     const int rpw = (nr + nwarps - 1) / nwarps;
@@ -90,10 +91,12 @@ __device__ __forceinline__ void staged_rows32(const typename F::Ptr &P, int n_in
         if ((lane & 3) == 0 && r < r_end) {
             out[r] = resid ? __fadd_rn(tot, resid[r]) : tot;
             if (r + row0 < conv.n) {
+                // taps and state of the row were read into shared memory
+                // before the upstream wait
                 const int c = r + row0;
-                const float4 wc = *reinterpret_cast<const float4 *>(conv.w + size_t(c) * 4);
+                const float4 wc = cw[r];
                 float *stc = conv.state + size_t(c) * 3;
-                const float s0 = stc[0], s1 = stc[1], s2 = stc[2];
+                const float s0 = cs[3 * r], s1 = cs[3 * r + 1], s2 = cs[3 * r + 2];
                 float sum = __fmul_rn(s0, wc.x);
                 sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
                 sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
@@ -125,6 +128,22 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
         __syncwarp();
         Stage<F>::issue(W, r0, nr, n_in, wbuf, &bar, threadIdx.x);
     }
+    // the conv epilogue's taps and state for this CTA's rows: written by
+    // earlier steps only, so read before the upstream wait
+    constexpr int CONV_ROWS = 160;
+    __shared__ float4 cw[CONV_ROWS];
+    __shared__ float cs[3 * CONV_ROWS];
+    if (conv.n && nr <= CONV_ROWS) {
+        for (int r = threadIdx.x; r < nr; r += blockDim.x) {
+            const int c = r0 + r;
+            if (c < conv.n) {
+                cw[r] = *reinterpret_cast<const float4 *>(conv.w + size_t(c) * 4);
+                cs[3 * r] = conv.state[size_t(c) * 3];
+                cs[3 * r + 1] = conv.state[size_t(c) * 3 + 1];
+                cs[3 * r + 2] = conv.state[size_t(c) * 3 + 2];
+            }
+        }
+    }
     __syncthreads();
     pdl_trigger();
     pdl_wait();
@@ -146,7 +165,7 @@ __global__ void __launch_bounds__(512) gemv_staged_kernel(typename F::Ptr W, int
     const auto P = Stage<F>::view(wbuf, nr, n_in);
     if constexpr (LPR == 32)
         staged_rows32<F, UPL>(P, n_in, nr, act, out + r0, resid ? resid + r0 : nullptr, warp, nwarps, lane, r0,
-                              conv);
+                              conv, cw, cs);
     else
         gemv_warp_rows<SmemRows<F>, 1, LPR, UPL, RU>(P, n_in, nr, xq, xd, xsum, out + r0, 0, warp, nwarps,
                                                      lane, resid ? resid + r0 : nullptr);
@@ -354,7 +373,7 @@ static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8
     int rows_cta = (n_out + num_sms() - 1) / num_sms();
     rows_cta = (rows_cta + 7) & ~7;
     const uint32_t smem = Stage<F>::bytes(rows_cta, n_in);
-    if (smem > STAGED_MAX) return false;
+    if (smem > STAGED_MAX || (conv.n && rows_cta > 160)) return false;
     const int U = n_in / F::UNIT;
     switch (U) {
     case 4: if (conv.n) return false;
