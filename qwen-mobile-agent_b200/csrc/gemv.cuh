@@ -16,10 +16,6 @@
 
 namespace qma {
 
-__device__ __forceinline__ int hdr_byte(const uint4 &h, int k) {
-    const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
-    return (w >> ((k & 3) * 8)) & 0xff;
-}
 
 // ------------------------------------------------------------------ Q4_K --
 struct FmtQ4K {
@@ -74,21 +70,19 @@ struct FmtQ4K {
     __device__ static float dot(const Wt &w, const Act &a, int u) {
         int lo, hi;
         isums(w, a, lo, hi);
+        // get_scale_min_k4 (quants.c:18-26) for sub-blocks 2g and 2g+1, both
+        // at once on byte pairs and without branching on the lane's g:
+        //   j < 4 : sc = s[j] & 63, m = s[j+4] & 63
+        //   j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,
+        //           m  = (s[j+4] >> 4) | (s[j] >> 6) << 4
         const int g = u & 3;
-        int sc0, m0, sc1, m1;
-        {
-            const int j0 = 2 * g, j1 = 2 * g + 1;
-            // get_scale_min_k4 (quants.c:18-26) on the 12 header bytes
-            if (j0 < 4) {
-                sc0 = hdr_byte(w.h, j0) & 63; m0 = hdr_byte(w.h, j0 + 4) & 63;
-                sc1 = hdr_byte(w.h, j1) & 63; m1 = hdr_byte(w.h, j1 + 4) & 63;
-            } else {
-                sc0 = (hdr_byte(w.h, j0 + 4) & 0xF) | ((hdr_byte(w.h, j0 - 4) >> 6) << 4);
-                m0 = (hdr_byte(w.h, j0 + 4) >> 4) | ((hdr_byte(w.h, j0) >> 6) << 4);
-                sc1 = (hdr_byte(w.h, j1 + 4) & 0xF) | ((hdr_byte(w.h, j1 - 4) >> 6) << 4);
-                m1 = (hdr_byte(w.h, j1 + 4) >> 4) | ((hdr_byte(w.h, j1) >> 6) << 4);
-            }
-        }
+        const uint32_t sh = 16u * uint32_t(g & 1);
+        const uint32_t A = (w.h.y >> sh) & 0xffffu;        // s[2g'], s[2g'+1]
+        const uint32_t B = (w.h.z >> sh) & 0xffffu;        // s[4+2g'], s[5+2g']
+        const uint32_t Cc = (w.h.w >> sh) & 0xffffu;       // s[8+2g'], s[9+2g']
+        const uint32_t scp = g < 2 ? (A & 0x3f3fu) : ((Cc & 0x0f0fu) | ((A & 0xc0c0u) >> 2));
+        const uint32_t mp = g < 2 ? (B & 0x3f3fu) : (((Cc >> 4) & 0x0f0fu) | ((B & 0xc0c0u) >> 2));
+        const int sc0 = int(scp & 0xffu), sc1 = int(scp >> 8), m0 = int(mp & 0xffu), m1 = int(mp >> 8);
         const int I1 = sc0 * lo + sc1 * hi;
         const int I2 = m0 * a.xs01 + m1 * a.xs23;
         const float d = h2f(uint16_t(w.h.x & 0xffff));
