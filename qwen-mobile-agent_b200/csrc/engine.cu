@@ -815,6 +815,37 @@ static int maybe_rebuild(qma_cuda_state *s, int pos_now) {
     return QMA_CUDA_OK;
 }
 
+static int capture_decode(qma_cuda_state *s);
+
+// One token with its logits to the host: a replay of the captured decode
+// step (the same kernels eager launches would run, without ~300 host-side
+// launches per token).  The step's argmax also runs; eval ignores it.
+static int eval_one_graph(qma_cuda_state *s, int token, float *logits) {
+    cudaStream_t st = s->st;
+    int rc;
+    const int pos = s->n_pos;
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if ((rc = maybe_rebuild(s, pos))) return rc;
+    fill_params(s, *s->sp_host, pos, 1, token);
+    QMA_CHECK_CUDA(cudaMemcpyAsync(s->sp_dev, s->sp_host, sizeof(StepParams), cudaMemcpyHostToDevice, st));
+    if (!s->graph && (rc = capture_decode(s))) return rc;
+    s->tier[hcm_slot(pos, s->n_ctx)] = 2;
+    QMA_CHECK_CUDA(cudaGraphLaunch(s->graph, st));
+    if (logits)
+        QMA_CHECK_CUDA(cudaMemcpyAsync(logits, s->logits, sizeof(float) * s->m->n_vocab, cudaMemcpyDeviceToHost,
+                                       st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    s->n_pos += 1;
+    return check_wait_timeouts();
+}
+
+// QMA_CUDA_EAGER=1 in the environment: qma_cuda_eval launches every kernel
+// itself, also for single tokens (no graph replay), for debugging.
+static bool eager_only() {
+    const char *v = getenv("QMA_CUDA_EAGER");
+    return v && atoi(v) != 0;
+}
+
 static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logits, int logits_all,
                 int n_layers = NLAYER, float *hidden = nullptr) {
     qma_cuda_model *m = s->m;
@@ -825,6 +856,8 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
                   n_tokens, s->n_ctx);
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
+    if (n_tokens == 1 && !logits_all && n_layers == NLAYER && !hidden && pdl_enabled() && !eager_only())
+        return eval_one_graph(s, tokens[0], logits);
     if (logits_all && MAX_CHUNK > s->logits_rows) {
         void *p;
         QMA_CHECK_CUDA(cudaMalloc(&p, sizeof(float) * size_t(MAX_CHUNK) * m->n_vocab));

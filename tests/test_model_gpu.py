@@ -177,7 +177,9 @@ def test_kv_records_bit_exact(full):
 def test_greedy_graph_matches_eager_eval_across_rebuild(full):
     """decode_greedy (one CUDA graph per step, argmax on the device, the
     graph re-captured when the HCM live index is rebuilt at position 128)
-    reproduces token by token what eager qma_cuda_eval calls compute."""
+    reproduces token by token what eager qma_cuda_eval calls compute
+    (QMA_CUDA_EAGER=1: single-token eval launches every kernel itself
+    instead of replaying the decode graph)."""
     rng = np.random.default_rng(21)
     prompt = rng.integers(0, O.N_VOCAB, 122).astype(np.int32)
     a = Q.State(full["model"], N_CTX)
@@ -189,13 +191,41 @@ def test_greedy_graph_matches_eager_eval_across_rebuild(full):
         tok = int(np.argmax(la))
         toks, last = a.decode_greedy(tok, 12)     # toks[i]: step i's input token
         fed = []
-        for _ in range(12):
-            fed.append(tok)
-            lb = b.eval(np.array([tok], np.int32))
-            tok = int(np.argmax(lb))
+        os.environ["QMA_CUDA_EAGER"] = "1"
+        try:
+            for _ in range(12):
+                fed.append(tok)
+                lb = b.eval(np.array([tok], np.int32))
+                tok = int(np.argmax(lb))
+        finally:
+            del os.environ["QMA_CUDA_EAGER"]
         assert list(toks) == fed
         assert np.array_equal(last, lb)
         assert a.n_pos == b.n_pos == 122 + 12
+    finally:
+        a.close()
+        b.close()
+
+
+def test_single_token_eval_replays_the_decode_graph(full):
+    """qma_cuda_eval of one token (a replay of the captured decode step)
+    returns the logits eager launches compute, across the HCM rebuild."""
+    rng = np.random.default_rng(22)
+    prompt = rng.integers(0, O.N_VOCAB, 124).astype(np.int32)
+    a = Q.State(full["model"], N_CTX)
+    b = Q.State(full["model"], N_CTX)
+    try:
+        la, lb = a.eval(prompt), b.eval(prompt)
+        for i in range(8):
+            tok = np.array([int(np.argmax(la))], np.int32)
+            la = a.eval(tok)
+            os.environ["QMA_CUDA_EAGER"] = "1"
+            try:
+                lb = b.eval(tok)
+            finally:
+                del os.environ["QMA_CUDA_EAGER"]
+            assert np.array_equal(la, lb), f"step {i}"
+        assert a.n_pos == b.n_pos == 124 + 8
     finally:
         a.close()
         b.close()
