@@ -1,5 +1,6 @@
 // gemv.cu -- standalone Q8_K quantization and quantized GEMV entry points
 // (qma_cuda_q8k_quant, qma_cuda_matvec, qma_cuda_dot_partials).
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -388,6 +389,155 @@ static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8
     }
 }
 
+// ------------------------------------------------ Q4_K GEMM on tensor cores --
+// Several tokens against Q4_K rows (prefill chunks): int8 tensor-core MMAs
+// (mma.sync m16n8k32 s8 x s8 -> s32) compute each 32-element sub-block's
+// exact integer partial sum(q * xq) for 16 rows x 8 tokens at once; the
+// partials are folded with the sub-block scales in integer registers
+// (I1 = sum_j sc_j * P_j, exact), the mins through the Q8_K block sums
+// (I2 = sum_j m_j * bsum_j), and each super-block contributes
+// xd * (d * I1 - dmin * I2) in fp32 -- the GEMV's arithmetic per super-block
+// (dot_q4_K_q8k, q8k.c:89-131) with the integer part on the tensor cores.
+// A Q4_K sub-block pair (2g, 2g+1) is the low and high nibbles of the same
+// 32 bytes, so one 32-bit weight load per fragment register serves both.
+// Warp: 16 rows x (8 * GNT) tokens; CTA: 4 warps = 64 rows.
+constexpr int GNT = 4;
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// get_scale_min_k4 (quants.c:18-26) of all 8 sub-blocks of a super-block
+__device__ __forceinline__ void q4k_scales8(const uint8_t *hdr, int (&sc)[8], int (&mn)[8]) {
+    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(hdr + 4);
+    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(hdr + 8);
+    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(hdr + 12);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t a = (w0 >> (8 * j)) & 0xffu, b = (w1 >> (8 * j)) & 0xffu, c = (w2 >> (8 * j)) & 0xffu;
+        sc[j] = int(a & 63u);
+        mn[j] = int(b & 63u);
+        sc[j + 4] = int((c & 15u) | ((a >> 6) << 4));
+        mn[j + 4] = int((c >> 4) | ((b >> 6) << 4));
+    }
+}
+
+__global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__restrict__ W, int n_in, int n_out,
+                                                           int T, const int8_t *__restrict__ xq,
+                                                           const float *__restrict__ xd,
+                                                           const int16_t *__restrict__ xsum, float *out,
+                                                           const float *resid) {
+    QMA_TRACE_SCOPE(TK_GEMV);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int row0 = (blockIdx.x * 4 + warp) * 16;
+    const int tok0 = blockIdx.y * (8 * GNT);
+    pdl_trigger();
+    pdl_wait();
+    if (row0 >= n_out) return;
+    const int nsb = n_in / 256;
+    const size_t rb = size_t(nsb) * 144;
+    const uint8_t *wr0 = W + size_t(row0 + gid) * rb, *wr1 = wr0 + 8 * rb;
+    float acc[GNT][4];
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    // the two token columns this lane's accumulators hold, per token tile
+    int tc[GNT][2];
+    bool tv[GNT][2];
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            tc[n][c] = tok0 + 8 * n + 2 * tig + c;
+            tv[n][c] = tc[n][c] < T;
+        }
+    for (int sb = 0; sb < nsb; sb++) {
+        const uint8_t *h0 = wr0 + size_t(sb) * 144, *h1 = wr1 + size_t(sb) * 144;
+        int sc0[8], mn0[8], sc1[8], mn1[8];
+        q4k_scales8(h0, sc0, mn0);
+        q4k_scales8(h1, sc1, mn1);
+        const float d0 = h2f(*reinterpret_cast<const uint16_t *>(h0)), dm0 = h2f(*reinterpret_cast<const uint16_t *>(h0 + 2));
+        const float d1 = h2f(*reinterpret_cast<const uint16_t *>(h1)), dm1 = h2f(*reinterpret_cast<const uint16_t *>(h1 + 2));
+        int I1[GNT][4];
+#pragma unroll
+        for (int n = 0; n < GNT; n++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) I1[n][i] = 0;
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            // rows gid / gid + 8, bytes 32 g + 4 tig (k 0..15) and + 16 (k 16..31)
+            const uint32_t r0a = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 4 * tig);
+            const uint32_t r0b = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 16 + 4 * tig);
+            const uint32_t r1a = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 4 * tig);
+            const uint32_t r1b = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 16 + 4 * tig);
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int j = 2 * g + half;
+                const int sh = 4 * half;
+                const uint32_t a[4] = {(r0a >> sh) & 0x0f0f0f0fu, (r1a >> sh) & 0x0f0f0f0fu,
+                                       (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
+#pragma unroll
+                for (int n = 0; n < GNT; n++) {
+                    const int tk = tok0 + 8 * n + gid;           // B column = token
+                    uint32_t b0 = 0, b1 = 0;
+                    if (tk < T) {
+                        const int8_t *xp = xq + size_t(tk) * n_in + sb * 256 + 32 * j + 4 * tig;
+                        b0 = *reinterpret_cast<const uint32_t *>(xp);
+                        b1 = *reinterpret_cast<const uint32_t *>(xp + 16);
+                    }
+                    int p[4] = {0, 0, 0, 0};
+                    mma_s8(p, a, b0, b1);
+                    I1[n][0] += sc0[j] * p[0];
+                    I1[n][1] += sc0[j] * p[1];
+                    I1[n][2] += sc1[j] * p[2];
+                    I1[n][3] += sc1[j] * p[3];
+                }
+            }
+        }
+        // mins through the block sums of each token column, then the fp32 fold
+#pragma unroll
+        for (int n = 0; n < GNT; n++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                if (!tv[n][c]) continue;
+                const int16_t *bs = xsum + size_t(tc[n][c]) * (n_in / 16) + sb * 16;
+                int I2a = 0, I2b = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int pair = int(bs[2 * j]) + int(bs[2 * j + 1]);
+                    I2a += mn0[j] * pair;
+                    I2b += mn1[j] * pair;
+                }
+                const float x = xd[size_t(tc[n][c]) * nsb + sb];
+                acc[n][c] += x * (d0 * float(I1[n][c]) - dm0 * float(I2a));
+                acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
+            }
+    }
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (!tv[n][c]) continue;
+            const size_t o0 = size_t(tc[n][c]) * n_out + row0 + gid, o1 = o0 + 8;
+            out[o0] = resid ? __fadd_rn(acc[n][c], resid[o0]) : acc[n][c];
+            out[o1] = resid ? __fadd_rn(acc[n][2 + c], resid[o1]) : acc[n][2 + c];
+        }
+}
+
+static int launch_gemm_q4k(const uint8_t *W, int n_in, int n_out, int T, const int8_t *xq, const float *xd,
+                           const int16_t *xsum, float *out, const float *resid, cudaStream_t st) {
+    const dim3 grid(unsigned((n_out + 63) / 64), unsigned((T + 8 * GNT - 1) / (8 * GNT)));
+    QMA_CHECK_CUDA(launch_ex(gemm_q4k_mma_kernel, grid, dim3(128), 0, st, 1, pdl_enabled(), W, n_in, n_out, T, xq,
+                             xd, xsum, out, resid));
+    return QMA_CUDA_OK;
+}
+
 template <class F, int TMAX>
 static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, const int8_t *xq,
                        const float *xd, const int16_t *xsum, float *out, const float *resid,
@@ -402,6 +552,11 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
     if (conv.n) {
         set_error("matvec: the conv epilogue needs the single-token staged path");
         return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    // several tokens over Q4_K rows: the tensor-core GEMM
+    if constexpr (std::is_same<F, FmtQ4K>::value) {
+        if (T >= 8 && n_out % 16 == 0)
+            return launch_gemm_q4k(W, n_in, n_out, T, xq, xd, xsum, out, resid, st);
     }
     int t0 = 0;
     while (t0 < T) {
