@@ -134,11 +134,13 @@ def dist_setup():
 
 
 def dist_max(v, world):
+    """Max of v over the ranks (timings: the slowest rank decides)."""
     if world == 1:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

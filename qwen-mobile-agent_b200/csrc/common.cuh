@@ -62,7 +62,7 @@ struct Q8Planes {
     const int8_t *q;
     const __half *d;
 };
-static inline size_t pad16(size_t x) { return (x + 15) & ~size_t(15); }
+__host__ __device__ inline size_t pad16(size_t x) { return (x + 15) & ~size_t(15); }
 __host__ __device__ inline size_t q6_plane_ql(int rows, int n) { return size_t(rows) * n / 2; }
 __host__ __device__ inline size_t q6_plane_qh(int rows, int n) { return size_t(rows) * n / 4; }
 __host__ __device__ inline size_t q6_plane_sc(int rows, int n) { return size_t(rows) * n / 16; }
@@ -79,7 +79,7 @@ __host__ __device__ inline size_t q6_plane_d(int rows, int n) { return size_t(ro
 __host__ __device__ inline int q6_ql_chunk(int c, int s) { return c ^ (s & 3); }
 __host__ __device__ inline int q6_qh_chunk(int c, int s) { return c ^ ((s >> 1) & 1); }
 
-inline Q6Planes q6_planes(const void *base, int rows, int n) {
+__host__ __device__ inline Q6Planes q6_planes(const void *base, int rows, int n) {
     const uint8_t *p = static_cast<const uint8_t *>(base);
     Q6Planes P;
     P.ql = p;

@@ -403,29 +403,6 @@ static bool try_staged(const typename F::Ptr &W, int n_in, int n_out, const int8
 // Warp: 16 rows x (8 * GNT) tokens; CTA: 4 warps = 64 rows.
 constexpr int GNT = 4;
 
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// get_scale_min_k4 (quants.c:18-26) of all 8 sub-blocks of a super-block
-__device__ __forceinline__ void q4k_scales8(const uint8_t *hdr, int (&sc)[8], int (&mn)[8]) {
-    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(hdr + 4);
-    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(hdr + 8);
-    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(hdr + 12);
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const uint32_t a = (w0 >> (8 * j)) & 0xffu, b = (w1 >> (8 * j)) & 0xffu, c = (w2 >> (8 * j)) & 0xffu;
-        sc[j] = int(a & 63u);
-        mn[j] = int(b & 63u);
-        sc[j + 4] = int((c & 15u) | ((a >> 6) << 4));
-        mn[j + 4] = int((c >> 4) | ((b >> 6) << 4));
-    }
-}
-
 __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__restrict__ W, int n_in, int n_out,
                                                            int T, const int8_t *__restrict__ xq,
                                                            const float *__restrict__ xd,

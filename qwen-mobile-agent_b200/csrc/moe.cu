@@ -45,6 +45,15 @@ size_t moe_scratch_bytes(int T) {
     b += al256(sizeof(int16_t) * T * (MOE_EMBD / 16));    // xs
     b += al256(sizeof(float) * T);                        // gs
     b += al256(sizeof(float) * T * MOE_NSLOT * MOE_EMBD); // part
+    if (T >= MOE_GROUPED_MIN_T && T <= MOE_GROUPED_MAX_T) {
+        const size_t q = size_t(T) * MOE_NSLOT;
+        b += al256(sizeof(int) * (MOE_NEXP + 1));         // goff
+        b += al256(sizeof(int) * T * MOE_TOPK);           // plist
+        b += al256(sizeof(float) * q * 2 * MOE_FF);       // hg
+        b += al256(q * MOE_FF);                           // hq
+        b += al256(sizeof(float) * q * (MOE_FF / 256));   // hd
+        b += al256(sizeof(int16_t) * q * (MOE_FF / 16));  // hs
+    }
     return b;
 }
 
@@ -63,6 +72,16 @@ MoeScratch moe_scratch_layout(void *base, int T) {
     s.xs = reinterpret_cast<int16_t *>(take(sizeof(int16_t) * T * (MOE_EMBD / 16)));
     s.gs = reinterpret_cast<float *>(take(sizeof(float) * T));
     s.part = reinterpret_cast<float *>(take(sizeof(float) * T * MOE_NSLOT * MOE_EMBD));
+    s.goff = nullptr; s.plist = nullptr; s.hg = nullptr; s.hq = nullptr; s.hd = nullptr; s.hs = nullptr;
+    if (T >= MOE_GROUPED_MIN_T && T <= MOE_GROUPED_MAX_T) {
+        const size_t q = size_t(T) * MOE_NSLOT;
+        s.goff = reinterpret_cast<int *>(take(sizeof(int) * (MOE_NEXP + 1)));
+        s.plist = reinterpret_cast<int *>(take(sizeof(int) * T * MOE_TOPK));
+        s.hg = reinterpret_cast<float *>(take(sizeof(float) * q * 2 * MOE_FF));
+        s.hq = reinterpret_cast<int8_t *>(take(q * MOE_FF));
+        s.hd = reinterpret_cast<float *>(take(sizeof(float) * q * (MOE_FF / 256)));
+        s.hs = reinterpret_cast<int16_t *>(take(sizeof(int16_t) * q * (MOE_FF / 16)));
+    }
     return s;
 }
 
@@ -880,6 +899,17 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const bool pdl = pdl_enabled() && !clear_counters;
     QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
                              w.gate_inp, w.gate_inp_shexp, s, sel, wts));
+    if (s.goff && w.down_type == QMA_TYPE_Q6_K) {
+        // a chunk of tokens: experts grouped, tensor-core MMAs, then the combine
+        // (and the next norm when asked) in one kernel
+        int rc = moe_grouped(w, T, s, st);
+        if (rc) return rc;
+        const MoeNormTail none;
+        const MoeNormTail &tl = tail ? *tail : none;
+        QMA_CHECK_CUDA(launch_ex(moe_combine_norm_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), s, x2, x_out,
+                                 tl.w, tl.norm_from, tl.xq, tl.xd, tl.xs, tl.pf));
+        return QMA_CUDA_OK;
+    }
     const size_t eb = packed_bytes(w.down_type, MOE_EMBD, MOE_FF);
     const dim3 grid(MOE_NSLOT * XCL, T);
     const uint8_t *ge = static_cast<const uint8_t *>(w.gate_exps), *ue = static_cast<const uint8_t *>(w.up_exps);

@@ -10,6 +10,10 @@ constexpr int MOE_TOPK = 8;           // N_EXPERT_USED (qma.h:58)
 constexpr int MOE_FF = 512;           // N_FF_EXP / N_FF_SHEXP (qma.h:59-60)
 constexpr int MOE_NSLOT = MOE_TOPK + 1;   // routed experts + the shared expert
 constexpr int MOE_DOWN_CHUNK = 128;   // down-projection output rows per CTA
+// Chunks of MOE_GROUPED_MIN_T .. MOE_GROUPED_MAX_T tokens take the grouped
+// path (moe_grouped.cu): pairs grouped by expert, tensor-core MMAs.
+constexpr int MOE_GROUPED_MIN_T = 16;
+constexpr int MOE_GROUPED_MAX_T = 512;
 constexpr int MOE_DOWN_CHUNKS = MOE_EMBD / MOE_DOWN_CHUNK;
 
 // Per-call device scratch of the MoE block for T tokens (moe_scratch_layout
@@ -26,7 +30,15 @@ struct MoeScratch {
     int16_t *xs;           // [T][128]
     float *gs;             // [T] shared-expert gate sigmoid
     float *part;           // [T][9][2048] down projections per slot
+    // grouped path only (null below MOE_GROUPED_MIN_T tokens):
+    int *goff;             // [257] first pair of each expert in plist
+    int *plist;            // [T * 8] pair ids t * 8 + k grouped by expert
+    float *hg;             // [T * 9][1024] gate | up per pair slot
+    int8_t *hq;            // [T * 9][512] Q8_K of silu(gate) * up
+    float *hd;             // [T * 9][2]
+    int16_t *hs;           // [T * 9][32]
 };
+int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st);
 
 size_t moe_scratch_bytes(int T);
 MoeScratch moe_scratch_layout(void *base, int T);

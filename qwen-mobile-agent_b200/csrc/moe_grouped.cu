@@ -1,0 +1,309 @@
+// moe_grouped.cu -- the MoE FFN block for a chunk of tokens (prefill), with
+// the (token, expert) pairs grouped by expert so that each expert's weights
+// are read once per chunk and its tokens share int8 tensor-core MMAs.
+//
+// Same arithmetic as the per-token expert kernel (moe_expert_one_q8k
+// nn.c:412-439, moe_shared_q8k nn.c:446-473): the integer sub-block partials
+// sum(q * xq) are exact (mma.sync s8 x s8 -> s32), folded with the
+// sub-block scales in integer registers; each super-block adds
+// xd * (d * I1 - dmin * I2) (Q4_K) or d * xd * I (Q6_K) in fp32.  After the
+// router (moe_router_kernel), per chunk:
+//   1. moe_lists_kernel   : pair ids t * 8 + k grouped by expert, in token order;
+//   2. moe_gateup_kernel  : gate and up rows of every expert for its tokens
+//                           (the shared expert takes every token);
+//   3. moe_swiglu_kernel  : silu(gate) * up and its Q8_K per pair;
+//   4. moe_down_kernel    : down rows per expert, into the per-slot partials;
+//   5. moe_combine_norm_kernel (moe.cu) combines the slots.
+#include "common.cuh"
+#include "gemv.cuh"
+#include "moe.cuh"
+#include "quant.cuh"
+
+namespace qma {
+
+constexpr int GT = 32;          // tokens (pairs) per CTA tile: 4 MMA column tiles of 8
+constexpr int GR = 64;          // rows per CTA: 4 warps x 16
+constexpr int NSHARED = MOE_NEXP;   // group index of the shared expert
+
+// 1. ---------------------------------------------------------------- lists --
+// One CTA: thread e counts expert e's pairs, an exclusive scan gives the
+// offsets, then thread e lists its pairs in token order.
+__global__ void __launch_bounds__(256) moe_lists_kernel(const int *__restrict__ sel, int T, int *goff,
+                                                        int *plist) {
+    __shared__ int ssel[MOE_GROUPED_MAX_T * MOE_TOPK];
+    __shared__ int wsum[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
+    pdl_wait();
+    const int np = T * MOE_TOPK;
+    for (int p = tid; p < np; p += 256) ssel[p] = sel[p];
+    __syncthreads();
+    int cnt = 0;
+    for (int p = 0; p < np; p++) cnt += ssel[p] == tid;
+    // exclusive scan of the 256 counts
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; w++) base += wsum[w];
+    const int off = base + incl - cnt;
+    goff[tid] = off;
+    if (tid == 255) goff[256] = off + cnt;
+    int i = off;
+    for (int p = 0; p < np; p++)
+        if (ssel[p] == tid) plist[i++] = p;
+}
+
+// The pair slot of tile column tk of group e: routed pairs t * 8 + k, the
+// shared expert's T * 8 + t.
+__device__ __forceinline__ int pair_of(int e, int tk, int T, const int *goff, const int *plist) {
+    return e < NSHARED ? plist[goff[e] + tk] : T * MOE_TOPK + tk;
+}
+__device__ __forceinline__ int group_size(int e, int T, const int *goff) {
+    return e < NSHARED ? goff[e + 1] - goff[e] : T;
+}
+
+// 2. ---------------------------------------------------------- gate / up --
+// Grid (1024 / GR rows of [gate | up], 257 groups, ceil(T / GT) tiles); warp
+// w: 16 rows, 4 column tiles of 8 pairs.  Output hg[pair][1024].
+__global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restrict__ gate_exps,
+                                                         const uint8_t *__restrict__ up_exps,
+                                                         const uint8_t *__restrict__ gate_sh,
+                                                         const uint8_t *__restrict__ up_sh, int T,
+                                                         MoeScratch s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
+    const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    pdl_trigger();
+    pdl_wait();
+    const int ne = group_size(e, T, s.goff);
+    if (tok0 >= ne) return;
+    const int r = blockIdx.x * GR + warp * 16;          // row of [gate | up]
+    constexpr size_t RB = size_t(MOE_EMBD / 256) * Q4K_BYTES;
+    const uint8_t *W = r < MOE_FF ? (e < NSHARED ? gate_exps + size_t(e) * MOE_FF * RB : gate_sh)
+                                  : (e < NSHARED ? up_exps + size_t(e) * MOE_FF * RB : up_sh);
+    const int wr = r < MOE_FF ? r : r - MOE_FF;
+    const uint8_t *w0 = W + size_t(wr + gid) * RB, *w1 = w0 + 8 * RB;
+    // token (activation row) of B column gid of each tile; pair of accumulator
+    // columns 2 tig, 2 tig + 1
+    int tb[4], pc[4][2];
+#pragma unroll
+    for (int n = 0; n < 4; n++) {
+        const int tk = tok0 + 8 * n + gid;
+        tb[n] = tk < ne ? (e < NSHARED ? pair_of(e, tk, T, s.goff, s.plist) / MOE_TOPK : tk) : -1;
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const int tc = tok0 + 8 * n + 2 * tig + c;
+            pc[n][c] = tc < ne ? pair_of(e, tc, T, s.goff, s.plist) : -1;
+        }
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    for (int sb = 0; sb < MOE_EMBD / 256; sb++) {
+        const uint8_t *h0 = w0 + size_t(sb) * Q4K_BYTES, *h1 = w1 + size_t(sb) * Q4K_BYTES;
+        int sc0[8], mn0[8], sc1[8], mn1[8];
+        q4k_scales8(h0, sc0, mn0);
+        q4k_scales8(h1, sc1, mn1);
+        const float d0 = h2f(*reinterpret_cast<const uint16_t *>(h0)), dm0 = h2f(*reinterpret_cast<const uint16_t *>(h0 + 2));
+        const float d1 = h2f(*reinterpret_cast<const uint16_t *>(h1)), dm1 = h2f(*reinterpret_cast<const uint16_t *>(h1 + 2));
+        int I1[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; n++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) I1[n][i] = 0;
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const uint32_t r0a = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 4 * tig);
+            const uint32_t r0b = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 16 + 4 * tig);
+            const uint32_t r1a = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 4 * tig);
+            const uint32_t r1b = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 16 + 4 * tig);
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int j = 2 * g + half, sh = 4 * half;
+                const uint32_t a[4] = {(r0a >> sh) & 0x0f0f0f0fu, (r1a >> sh) & 0x0f0f0f0fu,
+                                       (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
+#pragma unroll
+                for (int n = 0; n < 4; n++) {
+                    uint32_t b0 = 0, b1 = 0;
+                    if (tb[n] >= 0) {
+                        const int8_t *xp = s.xq + size_t(tb[n]) * MOE_EMBD + sb * 256 + 32 * j + 4 * tig;
+                        b0 = *reinterpret_cast<const uint32_t *>(xp);
+                        b1 = *reinterpret_cast<const uint32_t *>(xp + 16);
+                    }
+                    int p[4] = {0, 0, 0, 0};
+                    mma_s8(p, a, b0, b1);
+                    I1[n][0] += sc0[j] * p[0];
+                    I1[n][1] += sc0[j] * p[1];
+                    I1[n][2] += sc1[j] * p[2];
+                    I1[n][3] += sc1[j] * p[3];
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < 4; n++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                if (pc[n][c] < 0) continue;
+                const int t = pc[n][c] < T * MOE_TOPK ? pc[n][c] / MOE_TOPK : pc[n][c] - T * MOE_TOPK;
+                const int16_t *bs = s.xs + size_t(t) * (MOE_EMBD / 16) + sb * 16;
+                int I2a = 0, I2b = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int pr = int(bs[2 * j]) + int(bs[2 * j + 1]);
+                    I2a += mn0[j] * pr;
+                    I2b += mn1[j] * pr;
+                }
+                const float x = s.xd[size_t(t) * (MOE_EMBD / 256) + sb];
+                acc[n][c] += x * (d0 * float(I1[n][c]) - dm0 * float(I2a));
+                acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
+            }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (pc[n][c] < 0) continue;
+            float *o = s.hg + size_t(pc[n][c]) * (2 * MOE_FF) + r + gid;
+            o[0] = acc[n][c];
+            o[8] = acc[n][2 + c];
+        }
+}
+
+// 3. -------------------------------------------------------- SwiGLU + Q8_K --
+// One CTA per pair slot, warp b: hidden block b of silu(gate) * up.
+__global__ void __launch_bounds__(64) moe_swiglu_kernel(MoeScratch s) {
+    const int q = blockIdx.x, lane = threadIdx.x & 31, b = threadIdx.x >> 5;
+    pdl_trigger();
+    pdl_wait();
+    const float *h = s.hg + size_t(q) * (2 * MOE_FF);
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = b * 256 + lane * 8 + k;
+        const float g = h[i], u = h[MOE_FF + i];
+        v[k] = (g / (1.0f + expf(-g))) * u;
+    }
+    q8k_block_warp(v, lane, s.hq + size_t(q) * MOE_FF + b * 256, s.hd + size_t(q) * 2 + b,
+                   s.hs + size_t(q) * (MOE_FF / 16) + b * 16);
+}
+
+// 4. ---------------------------------------------------------------- down --
+// Q6_K down rows (2048 x 512, planes with swizzled ql / qh chunks) of every
+// group for its pairs: m16n8k16 MMAs, one per 16-element sub-block with its
+// int8 scale.  Grid (2048 / GR, 257, tiles); output part[t][slot][row].
+__global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict__ down_exps, size_t down_bytes,
+                                                       const uint8_t *__restrict__ down_sh, int T,
+                                                       MoeScratch s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
+    const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    pdl_trigger();
+    pdl_wait();
+    const int ne = group_size(e, T, s.goff);
+    if (tok0 >= ne) return;
+    constexpr int N = MOE_FF, NSB = N / 256;
+    const int r0 = blockIdx.x * GR + warp * 16 + gid;   // rows r0 and r0 + 8
+    const Q6Planes P = q6_planes(e < NSHARED ? down_exps + size_t(e) * down_bytes : down_sh, MOE_EMBD, N);
+    int qb[4], pc[4][2];
+#pragma unroll
+    for (int n = 0; n < 4; n++) {
+        const int tk = tok0 + 8 * n + gid;
+        qb[n] = tk < ne ? pair_of(e, tk, T, s.goff, s.plist) : -1;
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const int tc = tok0 + 8 * n + 2 * tig + c;
+            pc[n][c] = tc < ne ? pair_of(e, tc, T, s.goff, s.plist) : -1;
+        }
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    for (int sb = 0; sb < NSB; sb++) {
+        int I[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; n++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) I[n][i] = 0;
+#pragma unroll 4
+        for (int g = 0; g < 16; g++) {
+            // elements 16 g + 4 tig .. + 3 of super-block sb: quad i of unit j
+            const int j = g >> 3, i = 4 * (g & 7) + tig;
+            const int hi = i >> 4, shift = 2 * (((i >> 3) & 1) + 2 * hi);
+            const int qi = i & 15, hq = i & 7;
+            uint32_t a[2];
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const int row = r0 + 8 * rr;
+                const int seg = row * NSB + sb;
+                const int cl = 4 * j + (qi >> 2), ch = 2 * j + (hq >> 2);
+                const uint32_t lw = *reinterpret_cast<const uint32_t *>(
+                    P.ql + size_t(row) * (N / 2) + sb * 128 + (q6_ql_chunk(cl, seg) << 4) + 4 * (qi & 3));
+                const uint32_t hw = *reinterpret_cast<const uint32_t *>(
+                    P.qh + size_t(row) * (N / 4) + sb * 64 + (q6_qh_chunk(ch, seg) << 4) + 4 * (hq & 3));
+                const uint32_t v = ((lw >> (4 * hi)) & 0x0f0f0f0fu) | (((hw >> shift) & 0x03030303u) << 4);
+                a[rr] = __vsub4(v, 0x20202020u);
+            }
+            const int sc0 = P.sc[size_t(r0) * (N / 16) + sb * 16 + g];
+            const int sc1 = P.sc[size_t(r0 + 8) * (N / 16) + sb * 16 + g];
+#pragma unroll
+            for (int n = 0; n < 4; n++) {
+                const uint32_t b0 = qb[n] >= 0
+                    ? *reinterpret_cast<const uint32_t *>(s.hq + size_t(qb[n]) * N + sb * 256 + 16 * g + 4 * tig)
+                    : 0u;
+                int p[4] = {0, 0, 0, 0};
+                mma_s8_k16(p, a[0], a[1], b0);
+                I[n][0] += sc0 * p[0];
+                I[n][1] += sc0 * p[1];
+                I[n][2] += sc1 * p[2];
+                I[n][3] += sc1 * p[3];
+            }
+        }
+        const float d0 = __half2float(P.d[size_t(r0) * NSB + sb]), d1 = __half2float(P.d[size_t(r0 + 8) * NSB + sb]);
+#pragma unroll
+        for (int n = 0; n < 4; n++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                if (pc[n][c] < 0) continue;
+                const float x = s.hd[size_t(pc[n][c]) * NSB + sb];
+                acc[n][c] += d0 * x * float(I[n][c]);
+                acc[n][2 + c] += d1 * x * float(I[n][2 + c]);
+            }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const int q = pc[n][c];
+            if (q < 0) continue;
+            const int t = q < T * MOE_TOPK ? q / MOE_TOPK : q - T * MOE_TOPK;
+            const int slot = q < T * MOE_TOPK ? q % MOE_TOPK : MOE_TOPK;
+            float *o = s.part + (size_t(t) * MOE_NSLOT + slot) * MOE_EMBD + r0;
+            o[0] = acc[n][c];
+            o[8] = acc[n][2 + c];
+        }
+}
+
+int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st) {
+    const bool pdl = pdl_enabled();
+    const int tiles = (T + GT - 1) / GT;
+    QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
+    QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, NSHARED + 1, tiles), dim3(128), 0, st, 1, pdl,
+                             static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
+                             static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp), T,
+                             s));
+    QMA_CHECK_CUDA(launch_ex(moe_swiglu_kernel, dim3(T * MOE_NSLOT), dim3(64), 0, st, 1, pdl, s));
+    QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, NSHARED + 1, tiles), dim3(128), 0, st, 1, pdl,
+                             static_cast<const uint8_t *>(w.down_exps), packed_bytes(w.down_type, MOE_EMBD, MOE_FF),
+                             static_cast<const uint8_t *>(w.down_shexp), T, s));
+    return QMA_CUDA_OK;
+}
+
+}  // namespace qma

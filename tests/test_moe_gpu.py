@@ -20,7 +20,7 @@ def layer(cuda):
     L.close()
 
 
-@pytest.mark.parametrize("T", [1, 4, 16])
+@pytest.mark.parametrize("T", [1, 4, 16, 37, 300])
 def test_moe_block_matches_oracle(layer, T):
     rng = np.random.default_rng(100 + T)
     x2 = rng.standard_normal((T, 2048)).astype(np.float32)
