@@ -246,9 +246,11 @@ def run_decode_ours(args, world, rank, local):
     stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(st.h), device=local)
     rng = np.random.default_rng(SEED + rank)
     prompt = rng.integers(0, N_VOCAB, args.prompt).astype(np.int32)
+    torch.cuda.nvtx.range_push("prefill")
     t0 = time.time()
     logits = st.eval(prompt)
     t_prefill = time.time() - t0
+    torch.cuda.nvtx.range_pop()
     tok = int(np.argmax(logits))
     toks, logits = st.decode_greedy(tok, max(args.warmup, 3))
     tok = int(np.argmax(logits))
