@@ -159,6 +159,10 @@ int qma_cuda_state_n_pos(const qma_cuda_state *s);
  * be NULL. */
 int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n_tokens,
                   float *logits, int logits_all);
+/* A single token with last-token logits replays the state's captured decode
+ * step (a CUDA graph, the kernels qma_cuda_decode_greedy runs); with
+ * QMA_CUDA_EAGER=1 in the environment every kernel is launched one by one
+ * instead (same results; for debugging). */
 
 /* Greedy decode kept on the device: feeds `token`, then each step's argmax
  * (lowest id on ties), for n_steps steps; step i's input token goes to
