@@ -84,6 +84,7 @@ struct qma_cuda_state {
     int *argmax_pi = nullptr;
     unsigned *argmax_cnt = nullptr;     // ticket, zero between steps
     unsigned *gdn_cnt = nullptr;        // [16] gated-norm tickets, zero between layers
+    float *gdn_kq = nullptr;            // [MAX_CHUNK][16] k . q of a prefill chunk
     // attention scratch, grown on demand
     float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr, *ml = nullptr;
     size_t scores_cap = 0, cmax_cap = 0, opart_cap = 0, lpart_cap = 0;
@@ -416,6 +417,7 @@ static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     TRY(salloc_t(s, &s->argmax_pi, ARG_CTAS, st));
     TRY(salloc_t(s, &s->argmax_cnt, 1, st));
     TRY(salloc_t(s, &s->gdn_cnt, VHEADS / 2, st));
+    TRY(salloc_t(s, &s->gdn_kq, size_t(MAX_CHUNK) * KHEADS, st));
     s->logits_rows = 1;
     TRY(salloc_t(s, &s->logits, size_t(m->n_vocab), st));
 #undef TRY
@@ -740,7 +742,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
                                L.dt, L.a, s->ssm[il], T, s->gdo, st, &gna));
             } else {
                 TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
-                               L.dt, L.a, s->ssm[il], T, s->gdo, st));
+                               L.dt, L.a, s->ssm[il], T, s->gdo, st, nullptr, s->gdn_kq));
                 TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
                                             s->xs, st));
             }

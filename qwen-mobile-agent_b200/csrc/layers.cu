@@ -337,9 +337,126 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     }
 }
 
+// ------------------------------------------- gated delta net, T tokens ----
+// A chunk of tokens in two kernels.  gdn_prep_kernel: per (token, K head)
+// the q / k L2 norms (l2norm_skv, nn.c:744-761), written in place over the
+// conv output, and k . q.  gdn_seq_kernel: the recurrence of gdn_kernel with
+// the same per-token arithmetic, the inputs of 32 tokens (normed q and k,
+// the CTA's 32 v values, beta, exp(g), k . q) staged in shared memory at a
+// time, so the token loop needs no barrier and no global load.
+__global__ void __launch_bounds__(256) gdn_prep_kernel(float *conv_out, float *kq) {
+    const int t = blockIdx.x, qh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float qs[SSTATE], ks[SSTATE];
+    __shared__ double red[8];
+    __shared__ float kqred[4];
+    pdl_trigger();
+    pdl_wait();
+    float *co = conv_out + size_t(t) * CONV_DIM;
+    const int idx = tid < SSTATE ? qh * SSTATE + tid : KEY_DIM + qh * SSTATE + tid - SSTATE;
+    const float val = co[idx];
+    double sq = double(val) * double(val);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    const int base = tid < SSTATE ? 0 : 4;
+    const double tot = (red[base] + red[base + 1]) + (red[base + 2] + red[base + 3]);
+    const float r = 1.0f / fmaxf(sqrtf(float(tot)), 1e-6f);
+    const float nv = __fmul_rn(val, r);
+    co[idx] = nv;
+    if (tid < SSTATE) qs[tid] = nv;
+    else ks[tid - SSTATE] = nv;
+    __syncthreads();
+    if (warp < 4) {
+        float p = __fmul_rn(ks[tid], qs[tid]);
+        p = warp_sum(p);
+        if (lane == 0) kqred[warp] = p;
+    }
+    __syncthreads();
+    if (tid == 0) kq[size_t(t) * KHEADS + qh] = (kqred[0] + kqred[1]) + (kqred[2] + kqred[3]);
+}
+
+constexpr int GDN_TB = 32;     // tokens staged per pass
+
+__global__ void __launch_bounds__(256) gdn_seq_kernel(const float *__restrict__ conv_out,
+                                                      const float *__restrict__ proj, int proj_ld,
+                                                      int beta_off, int alpha_off,
+                                                      const float *__restrict__ dt,
+                                                      const float *__restrict__ av,
+                                                      const float *__restrict__ kq, float *ssm, int T,
+                                                      float *o) {
+    QMA_TRACE_SCOPE(TK_GDN);
+    const int rb = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int qh = h % KHEADS;
+    const int j = rb * 32 + (tid >> 3);
+    const int part = tid & 7;
+    __shared__ __align__(16) float qs[GDN_TB][SSTATE], ks[GDN_TB][SSTATE];
+    __shared__ float vs[GDN_TB][32];
+    __shared__ float bs[GDN_TB], egs[GDN_TB], kqs[GDN_TB];
+    float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
+    pdl_trigger();
+    pdl_wait();
+    float M[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float4 v = reinterpret_cast<const float4 *>(Mrow)[k];
+        M[4 * k] = v.x; M[4 * k + 1] = v.y; M[4 * k + 2] = v.z; M[4 * k + 3] = v.w;
+    }
+    const float scale = 1.0f / sqrtf(float(SSTATE));
+    const float dth = dt[h], ah = av[h];
+    for (int t0 = 0; t0 < T; t0 += GDN_TB) {
+        const int nb = min(GDN_TB, T - t0);
+        __syncthreads();                  // the previous pass is consumed
+        for (int i = tid; i < nb * SSTATE; i += 256) {
+            const int tt = i / SSTATE, e = i % SSTATE;
+            const float *co = conv_out + size_t(t0 + tt) * CONV_DIM;
+            qs[tt][e] = co[qh * SSTATE + e];
+            ks[tt][e] = co[KEY_DIM + qh * SSTATE + e];
+        }
+        for (int i = tid; i < nb * 32; i += 256) {
+            const int tt = i / 32, rr = i % 32;
+            vs[tt][rr] = conv_out[size_t(t0 + tt) * CONV_DIM + 2 * KEY_DIM + h * SSTATE + rb * 32 + rr];
+        }
+        if (tid < nb) {
+            const int t = t0 + tid;
+            const float braw = proj[size_t(t) * proj_ld + beta_off + h];
+            bs[tid] = 1.0f / (1.0f + expf(-braw));
+            const float a = proj[size_t(t) * proj_ld + alpha_off + h] + dth;
+            const float sp = a > 20.0f ? a : log1pf(expf(a));
+            egs[tid] = expf(__fmul_rn(sp, ah));
+            kqs[tid] = kq[size_t(t) * KHEADS + qh];
+        }
+        __syncthreads();
+        for (int tt = 0; tt < nb; tt++) {
+            float dq = 0.0f, dk = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                dq = __fadd_rn(dq, __fmul_rn(M[i], qs[tt][part * 16 + i]));
+                dk = __fadd_rn(dk, __fmul_rn(M[i], ks[tt][part * 16 + i]));
+            }
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                dq += __shfl_xor_sync(0xffffffffu, dq, off);
+                dk += __shfl_xor_sync(0xffffffffu, dk, off);
+            }
+            const float expg = egs[tt];
+            const float delta = __fmul_rn(__fsub_rn(vs[tt][tid >> 3], __fmul_rn(expg, dk)), bs[tt]);
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                M[i] = __fadd_rn(__fmul_rn(expg, M[i]), __fmul_rn(ks[tt][part * 16 + i], delta));
+            if (part == 0)
+                o[size_t(t0 + tt) * VAL_DIM + h * SSTATE + j] =
+                    __fmul_rn(__fadd_rn(__fmul_rn(expg, dq), __fmul_rn(delta, kqs[tt])), scale);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
+}
+
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
                const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
-               const GdnNormArgs *norm) {
+               const GdnNormArgs *norm, float *kq_scratch) {
     GdnNorm gn;
     if (norm && T == 1) {
         gn.z = norm->z;
@@ -348,6 +465,15 @@ int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_o
         gn.xd = norm->xd;
         gn.xs = norm->xs;
         gn.cnt = norm->cnt;
+    }
+    if (T > 1 && kq_scratch) {
+        // the conv output is normed in place: only this path reads it after
+        QMA_CHECK_CUDA(launch_ex(gdn_prep_kernel, dim3(T, KHEADS), dim3(256), 0, st, 1, pdl_enabled(),
+                                 const_cast<float *>(conv_out), kq_scratch));
+        QMA_CHECK_CUDA(launch_ex(gdn_seq_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj,
+                                 proj_ld, beta_off, alpha_off, dt, a, kq_scratch, ssm, T, o));
+        QMA_CHECK_LAUNCH();
+        return QMA_CUDA_OK;
     }
     QMA_CHECK_CUDA(launch_ex(gdn_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj, proj_ld,
                              beta_off, alpha_off, dt, a, ssm, T, o, gn));

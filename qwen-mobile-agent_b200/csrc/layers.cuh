@@ -68,7 +68,9 @@ struct GdnNormArgs {
 };
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
                const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
-               const GdnNormArgs *norm = nullptr);
+               const GdnNormArgs *norm = nullptr, float *kq_scratch = nullptr);
+// (T > 1 with kq_scratch [T][16]: the two-kernel chunk form, which norms q
+// and k in place in conv_out.)
 int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
                             int8_t *xq, float *xd, int16_t *xs, cudaStream_t st);
 
