@@ -155,36 +155,55 @@ int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *x
 // --------------------------------------------------------------- conv1d ---
 // conv1d_layer (nn.c:717-741) + SiLU (nn.c:2196): width-4 causal conv per
 // channel over [3 state samples | T new samples], state <- last 3 samples.
-// One thread per channel (so each state row has exactly one writer).
+// Thread (channel, token): every output is independent given the inputs
+// (the same four products summed in the same order); the threads of the
+// last three tokens then write the channel's new state.
 __global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ qkv, int ld,
                                                      const float *__restrict__ w, float *state,
                                                      int T, float *out) {
     QMA_TRACE_SCOPE(TK_CONV);
-    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
     pdl_trigger();
     pdl_wait();
     if (ch >= CONV_DIM) return;
     const float4 wc = *reinterpret_cast<const float4 *>(w + size_t(ch) * 4);
-    float s0 = state[ch * 3 + 0], s1 = state[ch * 3 + 1], s2 = state[ch * 3 + 2];
-    for (int t = 0; t < T; t++) {
-        const float xin = qkv[size_t(t) * ld + ch];
-        float sum = __fmul_rn(s0, wc.x);
-        sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
-        sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
-        sum = __fadd_rn(sum, __fmul_rn(xin, wc.w));
-        out[size_t(t) * CONV_DIM + ch] = sum / (1.0f + expf(-sum));
-        s0 = s1;
-        s1 = s2;
-        s2 = xin;
+    // input k steps back from token t: a new sample, or the saved state
+    auto in = [&](int k) {
+        const int tt = t - k;
+        return tt >= 0 ? qkv[size_t(tt) * ld + ch] : state[ch * 3 + 3 + tt];
+    };
+    const float s0 = in(3), s1 = in(2), s2 = in(1), xin = in(0);
+    float sum = __fmul_rn(s0, wc.x);
+    sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
+    sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
+    sum = __fadd_rn(sum, __fmul_rn(xin, wc.w));
+    out[size_t(t) * CONV_DIM + ch] = sum / (1.0f + expf(-sum));
+}
+
+// The channel state after the chunk: the last three inputs (launched after
+// conv1d_kernel, which still reads the old state).
+__global__ void __launch_bounds__(256) conv1d_state_kernel(const float *__restrict__ qkv, int ld, float *state,
+                                                           int T) {
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    if (ch >= CONV_DIM) return;
+    float v[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int tt = T - 3 + k;       // sample k of the new state
+        v[k] = tt >= 0 ? qkv[size_t(tt) * ld + ch] : state[ch * 3 + 3 + tt];
     }
-    state[ch * 3 + 0] = s0;
-    state[ch * 3 + 1] = s1;
-    state[ch * 3 + 2] = s2;
+#pragma unroll
+    for (int k = 0; k < 3; k++) state[ch * 3 + k] = v[k];
 }
 
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
                   cudaStream_t st) {
-    QMA_CHECK_CUDA(launch_ex(conv1d_kernel, dim3(CONV_DIM / 256), dim3(256), 0, st, 1, pdl_enabled(), qkv, ld, w, state, T, out));
+    QMA_CHECK_CUDA(launch_ex(conv1d_kernel, dim3(CONV_DIM / 256, T), dim3(256), 0, st, 1, pdl_enabled(), qkv, ld, w,
+                             state, T, out));
+    QMA_CHECK_CUDA(launch_ex(conv1d_state_kernel, dim3(CONV_DIM / 256), dim3(256), 0, st, 1, pdl_enabled(), qkv, ld,
+                             state, T));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
