@@ -409,16 +409,20 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                                                            const int16_t *__restrict__ xsum, float *out,
                                                            const float *resid) {
     QMA_TRACE_SCOPE(TK_GEMV);
+    static_assert(8 * GNT == BT_COLS, "one staged activation tile per CTA");
+    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ int brow[BT_COLS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int row0 = (blockIdx.x * 4 + warp) * 16;
     const int tok0 = blockIdx.y * (8 * GNT);
+    const bool active = row0 < n_out;            // warp-uniform; every warp stages and syncs
+    if (threadIdx.x < BT_COLS) brow[threadIdx.x] = tok0 + int(threadIdx.x) < T ? tok0 + int(threadIdx.x) : -1;
     pdl_trigger();
     pdl_wait();
-    if (row0 >= n_out) return;
     const int nsb = n_in / 256;
     const size_t rb = size_t(nsb) * 144;
-    const uint8_t *wr0 = W + size_t(row0 + gid) * rb, *wr1 = wr0 + 8 * rb;
+    const uint8_t *wr0 = W + size_t(active ? row0 + gid : 0) * rb, *wr1 = wr0 + 8 * rb;
     float acc[GNT][4];
 #pragma unroll
     for (int n = 0; n < GNT; n++)
@@ -435,6 +439,10 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
             tv[n][c] = tc[n][c] < T;
         }
     for (int sb = 0; sb < nsb; sb++) {
+        __syncthreads();                          // the previous tile is consumed
+        stage_btile(bt, brow, xq, size_t(n_in), sb * 256);
+        __syncthreads();
+        if (!active) continue;
         const uint8_t *h0 = wr0 + size_t(sb) * 144, *h1 = wr1 + size_t(sb) * 144;
         int sc0[8], mn0[8], sc1[8], mn1[8];
         q4k_scales8(h0, sc0, mn0);
@@ -461,13 +469,9 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                                        (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
 #pragma unroll
                 for (int n = 0; n < GNT; n++) {
-                    const int tk = tok0 + 8 * n + gid;           // B column = token
-                    uint32_t b0 = 0, b1 = 0;
-                    if (tk < T) {
-                        const int8_t *xp = xq + size_t(tk) * n_in + sb * 256 + 32 * j + 4 * tig;
-                        b0 = *reinterpret_cast<const uint32_t *>(xp);
-                        b1 = *reinterpret_cast<const uint32_t *>(xp + 16);
-                    }
+                    const int8_t *bp = &bt[8 * n + gid][32 * j + 4 * tig];
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bp);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bp + 16);
                     int p[4] = {0, 0, 0, 0};
                     mma_s8(p, a, b0, b1);
                     I1[n][0] += sc0[j] * p[0];
@@ -496,6 +500,7 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                 acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
             }
     }
+    if (!active) return;
 #pragma unroll
     for (int n = 0; n < GNT; n++)
 #pragma unroll

@@ -396,6 +396,21 @@ __device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(b0));
 }
 
+// A 32-column tile of int8 activations for one 256-element super-block,
+// staged in shared memory for the MMA kernels' B fragments.  Column c is
+// activation row rows[c] (-1: zeros).  Rows are padded to 272 bytes so the
+// fragment reads (8 columns x 4 words) fall in 32 different banks.
+constexpr int BT_COLS = 32, BT_STRIDE = 272;
+__device__ __forceinline__ void stage_btile(int8_t (*bs)[BT_STRIDE], const int *rows, const int8_t *x, size_t ld,
+                                            int k0) {
+    for (int i = threadIdx.x; i < BT_COLS * 16; i += blockDim.x) {
+        const int c = i >> 4, q = i & 15;
+        int4 v = make_int4(0, 0, 0, 0);
+        if (rows[c] >= 0) v = *reinterpret_cast<const int4 *>(x + size_t(rows[c]) * ld + k0 + 16 * q);
+        *reinterpret_cast<int4 *>(&bs[c][16 * q]) = v;
+    }
+}
+
 // Optional epilogue of a single-token GEMV over the gated delta net's input
 // projection: rows r < n are also the causal conv's channels (conv1d_layer
 // + SiLU, nn.c:717-741 / nn.c:2196), applied in the row's own thread with

@@ -21,7 +21,7 @@
 
 namespace qma {
 
-constexpr int GT = 32;          // tokens (pairs) per CTA tile: 4 MMA column tiles of 8
+constexpr int GT = BT_COLS;     // tokens (pairs) per CTA tile: 4 MMA column tiles of 8
 constexpr int GR = 64;          // rows per CTA: 4 warps x 16
 constexpr int NSHARED = MOE_NEXP;   // group index of the shared expert
 
@@ -78,23 +78,26 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                                                          MoeScratch s) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
     const int ne = group_size(e, T, s.goff);
-    if (tok0 >= ne) return;
+    if (tok0 >= ne) return;                              // CTA-uniform
+    if (threadIdx.x < BT_COLS) {
+        const int tk = tok0 + int(threadIdx.x);
+        brow[threadIdx.x] = tk < ne ? (e < NSHARED ? pair_of(e, tk, T, s.goff, s.plist) / MOE_TOPK : tk) : -1;
+    }
     const int r = blockIdx.x * GR + warp * 16;          // row of [gate | up]
     constexpr size_t RB = size_t(MOE_EMBD / 256) * Q4K_BYTES;
     const uint8_t *W = r < MOE_FF ? (e < NSHARED ? gate_exps + size_t(e) * MOE_FF * RB : gate_sh)
                                   : (e < NSHARED ? up_exps + size_t(e) * MOE_FF * RB : up_sh);
     const int wr = r < MOE_FF ? r : r - MOE_FF;
     const uint8_t *w0 = W + size_t(wr + gid) * RB, *w1 = w0 + 8 * RB;
-    // token (activation row) of B column gid of each tile; pair of accumulator
-    // columns 2 tig, 2 tig + 1
-    int tb[4], pc[4][2];
+    // pair of accumulator columns 2 tig, 2 tig + 1 of each tile
+    int pc[4][2];
 #pragma unroll
     for (int n = 0; n < 4; n++) {
-        const int tk = tok0 + 8 * n + gid;
-        tb[n] = tk < ne ? (e < NSHARED ? pair_of(e, tk, T, s.goff, s.plist) / MOE_TOPK : tk) : -1;
 #pragma unroll
         for (int c = 0; c < 2; c++) {
             const int tc = tok0 + 8 * n + 2 * tig + c;
@@ -107,6 +110,9 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
     for (int sb = 0; sb < MOE_EMBD / 256; sb++) {
+        __syncthreads();                                 // the previous tile is consumed
+        stage_btile(bt, brow, s.xq, MOE_EMBD, sb * 256);
+        __syncthreads();
         const uint8_t *h0 = w0 + size_t(sb) * Q4K_BYTES, *h1 = w1 + size_t(sb) * Q4K_BYTES;
         int sc0[8], mn0[8], sc1[8], mn1[8];
         q4k_scales8(h0, sc0, mn0);
@@ -131,12 +137,9 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                                        (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
 #pragma unroll
                 for (int n = 0; n < 4; n++) {
-                    uint32_t b0 = 0, b1 = 0;
-                    if (tb[n] >= 0) {
-                        const int8_t *xp = s.xq + size_t(tb[n]) * MOE_EMBD + sb * 256 + 32 * j + 4 * tig;
-                        b0 = *reinterpret_cast<const uint32_t *>(xp);
-                        b1 = *reinterpret_cast<const uint32_t *>(xp + 16);
-                    }
+                    const int8_t *bp = &bt[8 * n + gid][32 * j + 4 * tig];
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bp);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bp + 16);
                     int p[4] = {0, 0, 0, 0};
                     mma_s8(p, a, b0, b1);
                     I1[n][0] += sc0[j] * p[0];
@@ -203,18 +206,22 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
                                                        MoeScratch s) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
     const int ne = group_size(e, T, s.goff);
-    if (tok0 >= ne) return;
+    if (tok0 >= ne) return;                              // CTA-uniform
+    if (threadIdx.x < BT_COLS) {
+        const int tk = tok0 + int(threadIdx.x);
+        brow[threadIdx.x] = tk < ne ? pair_of(e, tk, T, s.goff, s.plist) : -1;
+    }
     constexpr int N = MOE_FF, NSB = N / 256;
     const int r0 = blockIdx.x * GR + warp * 16 + gid;   // rows r0 and r0 + 8
     const Q6Planes P = q6_planes(e < NSHARED ? down_exps + size_t(e) * down_bytes : down_sh, MOE_EMBD, N);
-    int qb[4], pc[4][2];
+    int pc[4][2];
 #pragma unroll
     for (int n = 0; n < 4; n++) {
-        const int tk = tok0 + 8 * n + gid;
-        qb[n] = tk < ne ? pair_of(e, tk, T, s.goff, s.plist) : -1;
 #pragma unroll
         for (int c = 0; c < 2; c++) {
             const int tc = tok0 + 8 * n + 2 * tig + c;
@@ -227,6 +234,9 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
     for (int sb = 0; sb < NSB; sb++) {
+        __syncthreads();                                 // the previous tile is consumed
+        stage_btile(bt, brow, s.hq, N, sb * 256);
+        __syncthreads();
         int I[4][4];
 #pragma unroll
         for (int n = 0; n < 4; n++)
@@ -255,9 +265,7 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
             const int sc1 = P.sc[size_t(r0 + 8) * (N / 16) + sb * 16 + g];
 #pragma unroll
             for (int n = 0; n < 4; n++) {
-                const uint32_t b0 = qb[n] >= 0
-                    ? *reinterpret_cast<const uint32_t *>(s.hq + size_t(qb[n]) * N + sb * 256 + 16 * g + 4 * tig)
-                    : 0u;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&bt[8 * n + gid][16 * g + 4 * tig]);
                 int p[4] = {0, 0, 0, 0};
                 mma_s8_k16(p, a[0], a[1], b0);
                 I[n][0] += sc0 * p[0];
