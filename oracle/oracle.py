@@ -93,6 +93,7 @@ def lib() -> C.CDLL:
         L.qo_eval_hidden.argtypes = [vp, vp, vp, i32, i32, vp]
         L.qo_eval_hidden.restype = i32
         L.qo_layer_forward.argtypes = [vp, vp, i32, vp, i32, i32, vp]
+        L.qo_mixer_forward.argtypes = [vp, vp, i32, vp, i32, vp]
         L.qo_state_kv_slot.argtypes = [vp, i32, i32, i32]
         L.qo_state_kv_slot.restype = C.POINTER(C.c_uint8)
         L.qo_gdn_layer.argtypes = [vp, vp, i32, vp, i32, vp]

@@ -197,6 +197,11 @@ int qo_eval_hidden(const qo_model *m, qo_state *s, const int *tokens, int n_toke
  * from x_in [T][2048] to x_out, tokens at positions n_pos.. (parity aid). */
 void qo_layer_forward(const qo_model *m, qo_state *s, int il, const float *x_in, int T,
                       int n_pos, float *x_out);
+/* Layer il's mixer + residual over n_tokens caller-given inputs, chunked
+ * and HCM-rebuilt as qma_eval does (nn.c:2081-2245); advances the state's
+ * position (parity aid for long contexts). */
+void qo_mixer_forward(const qo_model *m, qo_state *s, int il, const float *x_in, int n_tokens,
+                      float *x_out);
 
 /* ---- per-layer pieces, for layer-level parity ------------------------------ */
 /* GDN (recurrent) layer core from the post-norm input xn [T][2048] to the

@@ -892,85 +892,120 @@ static void score_live(void *arg, int j0, int j1)
     }
 }
 
-/* attn_worker (nn.c:1215-1446) for all 16 heads, heads in order 0..15 */
+/* One head's queries t0..t1-1: scores, softmax and P.V over the live
+ * entries plus the dense tail since the last rebuild.  Leaves each query's
+ * exp-scores in scores + t * nmax and its denominator in sums[t] for the
+ * salience update, which runs afterwards in the reference's order. */
+typedef struct {
+    const qo_state *s;
+    const uint8_t *Ks, *Vs, *ApK, *ApV;
+    const float *Q;
+    float *out, *scores, *sums;
+    int h, n_pos, nmax;
+    float scale;
+} head_ctx;
+
+static void head_queries(void *arg, int t0, int t1)
+{
+    const head_ctx *c = arg;
+    const qo_state *s = c->s;
+    const int cap = s->n_ctx;
+    const int use_live = s->live_n > 0;
+    const int nl_all = s->live_n, n4 = s->n4, n_rq = s->n_ring_q4, batch_lo = s->rebuilt_at;
+    for (int t = t0; t < t1; t++) {
+        const int abs = c->n_pos + t;
+        const float *q = c->Q + (size_t)t * QO_WQ_DIM + (size_t)c->h * (QO_HEAD_DIM * 2);
+        float *scores = c->scores + (size_t)t * c->nmax;
+        const int nl = use_live ? nl_all : abs + 1;
+        float maxs = -1e30f;
+        int nk;
+        if (use_live) {
+            score_ctx sc = { s->live, n_rq, n4, c->Ks, c->ApK, q, c->scale, scores };
+            score_live(&sc, 0, nl);
+            for (int p = batch_lo; p <= abs; p++)
+                scores[nl + (p - batch_lo)] =
+                    qo_kvq4_dot(c->Ks + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, q) * c->scale;
+            nk = nl + (abs - batch_lo + 1);
+        } else {
+            for (int p = 0; p <= abs; p++)
+                scores[p] = qo_kvq4_dot(c->Ks + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, q) * c->scale;
+            nk = abs + 1;
+        }
+        for (int j = 0; j < nk; j++) if (scores[j] > maxs) maxs = scores[j];
+        float sum = 0.0f;
+        for (int j = 0; j < nk; j++) { scores[j] = expf(scores[j] - maxs); sum += scores[j]; }
+        float oacc[QO_HEAD_DIM];
+        memset(oacc, 0, sizeof(oacc));
+        if (use_live) {
+            for (int j = 0; j < nl; j++) {
+                const int e = s->live[j];
+                if (j < n_rq) qo_kvq4_vacc(c->Vs + (size_t)e * QO_KVQ_SLOT, scores[j], oacc);
+                else if (j < n4) qo_kvq4_vacc(c->ApV + (size_t)(e - QO_HCM_ARENA_BASE) * QO_KVQ_SLOT, scores[j], oacc);
+                else qo_kvq2_vacc(c->Vs + (size_t)e * QO_KVQ_SLOT + QO_KVQ2_OFF, scores[j], oacc);
+            }
+            for (int p = batch_lo; p <= abs; p++)
+                qo_kvq4_vacc(c->Vs + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, scores[nl + (p - batch_lo)], oacc);
+        } else {
+            for (int p = 0; p <= abs; p++)
+                qo_kvq4_vacc(c->Vs + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, scores[p], oacc);
+        }
+        const float inv = 1.0f / sum;
+        float *o = c->out + (size_t)t * QO_WO_DIM + (size_t)c->h * QO_HEAD_DIM;
+        for (int d = 0; d < QO_HEAD_DIM; d++) o[d] = oacc[d] * inv;
+        c->sums[t] = sum;
+    }
+}
+
+/* attn_worker (nn.c:1215-1446) for all 16 heads, heads in order 0..15.
+ * A head's queries are independent of one another (split over threads);
+ * the salience EMA then folds them in head-major, query-minor order. */
 static void attn_heads(qo_state *s, int lay, const float *Q, float *out, int T, int n_pos)
 {
     const int cap = s->n_ctx;
-    const float scale = 1.0f / sqrtf((float)QO_HEAD_DIM);
     const uint8_t *cb = s->kv[lay];
     const int use_live = s->live_n > 0;
     const int nmax = (use_live ? s->live_n + (n_pos + T - s->rebuilt_at) : n_pos + T) + 1;
-    float *scores = malloc(sizeof(float) * (size_t)nmax);
+    float *scores = malloc(sizeof(float) * (size_t)nmax * T);
+    float *sums = malloc(sizeof(float) * (size_t)T);
     const int nl_all = s->live_n, n4 = s->n4, n_rq = s->n_ring_q4, batch_lo = s->rebuilt_at;
     for (int h = 0; h < QO_HEAD; h++) {
         const int kh = h / (QO_HEAD / QO_HEAD_KV);
-        const uint8_t *Ks = cb + (size_t)kh * cap * QO_KVQ_SLOT;
-        const uint8_t *Vs = cb + (size_t)(QO_HEAD_KV + kh) * cap * QO_KVQ_SLOT;
-        const uint8_t *ApK = s->pin_kv[lay] + (size_t)kh * QO_HCM_H_PIN * QO_KVQ_SLOT;
-        const uint8_t *ApV = s->pin_kv[lay] + (size_t)(QO_HEAD_KV + kh) * QO_HCM_H_PIN * QO_KVQ_SLOT;
+        head_ctx hc = {
+            s, cb + (size_t)kh * cap * QO_KVQ_SLOT, cb + (size_t)(QO_HEAD_KV + kh) * cap * QO_KVQ_SLOT,
+            s->pin_kv[lay] + (size_t)kh * QO_HCM_H_PIN * QO_KVQ_SLOT,
+            s->pin_kv[lay] + (size_t)(QO_HEAD_KV + kh) * QO_HCM_H_PIN * QO_KVQ_SLOT,
+            Q, out, scores, sums, h, n_pos, nmax, 1.0f / sqrtf((float)QO_HEAD_DIM)
+        };
+        qo_pfor(T, head_queries, &hc);
+        if (!use_live) continue;
         float *sal = s->sal[lay];
         for (int t = 0; t < T; t++) {
             const int abs = n_pos + t;
-            const float *q = Q + (size_t)t * QO_WQ_DIM + (size_t)h * (QO_HEAD_DIM * 2);
-            const int nl = use_live ? nl_all : abs + 1;
-            float maxs = -1e30f;
-            int nk;
-            if (use_live) {
-                score_ctx sc = { s->live, n_rq, n4, Ks, ApK, q, scale, scores };
-                qo_pfor(nl, score_live, &sc);
-                for (int p = batch_lo; p <= abs; p++)
-                    scores[nl + (p - batch_lo)] =
-                        qo_kvq4_dot(Ks + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, q) * scale;
-                nk = nl + (abs - batch_lo + 1);
-            } else {
-                for (int p = 0; p <= abs; p++)
-                    scores[p] = qo_kvq4_dot(Ks + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, q) * scale;
-                nk = abs + 1;
+            const int nl = nl_all;
+            const float *sc = scores + (size_t)t * nmax;
+            const float sum = sums[t];
+            for (int j = 0; j < n_rq && j < nl; j++) {
+                const int sl = s->live[j];
+                sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] + QO_HCM_ALPHA * (sc[j] / sum);
             }
-            for (int j = 0; j < nk; j++) if (scores[j] > maxs) maxs = scores[j];
-            float sum = 0.0f;
-            for (int j = 0; j < nk; j++) { scores[j] = expf(scores[j] - maxs); sum += scores[j]; }
-            float oacc[QO_HEAD_DIM];
-            memset(oacc, 0, sizeof(oacc));
-            if (use_live) {
-                for (int j = 0; j < nl; j++) {
-                    const int e = s->live[j];
-                    if (j < n_rq) qo_kvq4_vacc(Vs + (size_t)e * QO_KVQ_SLOT, scores[j], oacc);
-                    else if (j < n4) qo_kvq4_vacc(ApV + (size_t)(e - QO_HCM_ARENA_BASE) * QO_KVQ_SLOT, scores[j], oacc);
-                    else qo_kvq2_vacc(Vs + (size_t)e * QO_KVQ_SLOT + QO_KVQ2_OFF, scores[j], oacc);
-                }
-                for (int p = batch_lo; p <= abs; p++)
-                    qo_kvq4_vacc(Vs + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, scores[nl + (p - batch_lo)], oacc);
-            } else {
-                for (int p = 0; p <= abs; p++)
-                    qo_kvq4_vacc(Vs + (size_t)hcm_slot(p, cap) * QO_KVQ_SLOT, scores[p], oacc);
+            for (int j = n_rq; j < n4 && j < nl; j++) {
+                const int a = s->live[j] - QO_HCM_ARENA_BASE;
+                float *psal = s->pin_sal[lay];
+                psal[a] = (1 - QO_HCM_ALPHA) * psal[a] + QO_HCM_ALPHA * (sc[j] / sum);
             }
-            const float inv = 1.0f / sum;
-            float *o = out + (size_t)t * QO_WO_DIM + (size_t)h * QO_HEAD_DIM;
-            for (int d = 0; d < QO_HEAD_DIM; d++) o[d] = oacc[d] * inv;
-            if (use_live) {
-                for (int j = 0; j < n_rq && j < nl; j++) {
-                    const int sl = s->live[j];
-                    sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] + QO_HCM_ALPHA * (scores[j] / sum);
-                }
-                for (int j = n_rq; j < n4 && j < nl; j++) {
-                    const int a = s->live[j] - QO_HCM_ARENA_BASE;
-                    float *psal = s->pin_sal[lay];
-                    psal[a] = (1 - QO_HCM_ALPHA) * psal[a] + QO_HCM_ALPHA * (scores[j] / sum);
-                }
-                for (int j = n4; j < nl; j++) {
-                    const int sl = s->live[j];
-                    sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] + QO_HCM_ALPHA * (scores[j] / sum);
-                }
-                for (int p = batch_lo; p <= abs; p++) {
-                    const int sl = hcm_slot(p, cap);
-                    sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] +
-                              QO_HCM_ALPHA * (scores[nl + (p - batch_lo)] / sum);
-                }
+            for (int j = n4; j < nl; j++) {
+                const int sl = s->live[j];
+                sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] + QO_HCM_ALPHA * (sc[j] / sum);
+            }
+            for (int p = batch_lo; p <= abs; p++) {
+                const int sl = hcm_slot(p, cap);
+                sal[sl] = (1 - QO_HCM_ALPHA) * sal[sl] +
+                          QO_HCM_ALPHA * (sc[nl + (p - batch_lo)] / sum);
             }
         }
     }
     free(scores);
+    free(sums);
 }
 
 static void attn_layer(const qo_model *m, qo_state *s, int il, const float *xn, int T,
@@ -1044,6 +1079,40 @@ int qo_eval_hidden(const qo_model *m, qo_state *s, const int *tokens, int n_toke
                    int n_layers, float *hidden)
 {
     return eval_impl(m, s, tokens, n_tokens, NULL, 0, n_layers, hidden);
+}
+
+/* Layer il's mixer and its residual (nn.c:2105-2245) over n_tokens inputs
+ * x_in [n_tokens][2048] taken from the caller instead of the layers below,
+ * in qma_eval's chunks of 512 with the HCM rebuild at each chunk start
+ * (nn.c:2081-2087), writing x_out = x_in + mixer(rms_norm(x_in)).  The
+ * state's position advances by n_tokens.  Parity aid for long contexts: the
+ * attention layer's heavy-hitter arena and salience are driven by the
+ * caller's inputs alone. */
+void qo_mixer_forward(const qo_model *m, qo_state *s, int il, const float *x_in, int n_tokens,
+                      float *x_out)
+{
+    const qo_layer *L = &m->L[il];
+    float *xn = malloc(sizeof(float) * (size_t)QO_MAX_CHUNK * QO_EMBD);
+    float *ra = malloc(sizeof(float) * (size_t)QO_MAX_CHUNK * QO_EMBD);
+    for (int done = 0; done < n_tokens;) {
+        const int T = (n_tokens - done < QO_MAX_CHUNK) ? n_tokens - done : QO_MAX_CHUNK;
+        const int pos_now = s->n_pos + done;
+        if (pos_now >= s->next_rebuild) {
+            hcm_rebuild(s, pos_now);
+            s->rebuilt_at = pos_now;
+            s->next_rebuild = pos_now + QO_HCM_REBUILD;
+        }
+        const float *x = x_in + (size_t)done * QO_EMBD;
+        rms_norm_m(xn, x, L->attn_norm, QO_EMBD, T);
+        if (QO_IS_ATTN(il)) attn_layer(m, s, il, xn, T, pos_now, ra);
+        else qo_gdn_layer(m, s, il, xn, T, ra);
+        for (size_t i = 0; i < (size_t)QO_EMBD * T; i++)
+            x_out[(size_t)done * QO_EMBD + i] = ra[i] + x[i];
+        done += T;
+    }
+    s->n_pos += n_tokens;
+    free(xn);
+    free(ra);
 }
 
 static int eval_impl(const qo_model *m, qo_state *s, const int *tokens, int n_tokens,

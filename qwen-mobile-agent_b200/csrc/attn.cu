@@ -871,7 +871,11 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
                                             int(sizeof(DecSmem))));
         attr_dec = true;
     }
-    if (a.T == 1 && a.pv_chunk <= DSPAN)
+    // QMA_CUDA_ATTN_GENERAL=1: single tokens through the multi-query kernel
+    // (a cross-check of the decode kernel; same results up to fp32 rounding)
+    static_assert(DSPAN <= 256, "decode spans fit the multi-query kernel's chunk");
+    const char *gen = getenv("QMA_CUDA_ATTN_GENERAL");
+    if (a.T == 1 && a.pv_chunk <= DSPAN && !(gen && atoi(gen) != 0))
         QMA_CHECK_CUDA(launch_ex(attn_decode_kernel, dim3(nchunk, NHEAD_KV), dim3(256), sizeof(DecSmem), st, 1,
                                  pdl_enabled(), a.qr, a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk,
                                  a.scores, a.cmax, a.lpart, a.opart));

@@ -152,6 +152,63 @@ def test_layers_teacher_forced_prefill_and_decode(full):
     assert dec[len(dec) // 2] <= RTOL_LAYER
 
 
+def test_long_context_attention_arena_teacher_forced(full):
+    """The first attention layer (layer 3) past the 4096-position hot
+    window.  A 4700-token prompt: the rebuild at position 4608 pins the
+    508 positions older than the hot window into the heavy-hitter arena,
+    which the last prompt chunk (92 queries, the multi-query kernel) and
+    then 40 single-token steps (the decode kernel) read; the rebuild at
+    4736 re-ranks the pinned entries by their salience.  The oracle's layer
+    gets the engine's own layer-3 inputs (qo_mixer_forward: qma_eval's
+    chunks and rebuilds, this layer only), and the attention's
+    contribution to the residual must agree within the fp32 tolerance."""
+    L = O.lib()
+    rng = np.random.default_rng(31)
+    prompt = rng.integers(0, O.N_VOCAB, 4700).astype(np.int32)
+    dec = rng.integers(0, O.N_VOCAB, 40).astype(np.int32)
+    n_ctx = 8192
+    a, b, c = (Q.State(full["model"], n_ctx) for _ in range(3))
+    try:
+        xin = [a.eval_hidden(prompt, 3)] + [a.eval_hidden(dec[i:i + 1], 3) for i in range(len(dec))]
+        got = [b.eval_hidden(prompt, -4)] + [b.eval_hidden(dec[i:i + 1], -4) for i in range(len(dec))]
+        # the same steps with single tokens through the multi-query kernel
+        c.eval_hidden(prompt, -4)
+        os.environ["QMA_CUDA_ATTN_GENERAL"] = "1"
+        try:
+            gen = [c.eval_hidden(dec[i:i + 1], -4) for i in range(len(dec))]
+        finally:
+            del os.environ["QMA_CUDA_ATTN_GENERAL"]
+    finally:
+        a.close()
+        b.close()
+        c.close()
+    os_ = L.qo_state_new(n_ctx)
+    want = []
+    try:
+        for x in xin:
+            out = np.zeros_like(x)
+            L.qo_mixer_forward(full["om"], os_, 3, O._ptr(np.ascontiguousarray(x)), len(x), O._ptr(out))
+            want.append(out)
+    finally:
+        L.qo_state_free(os_)
+    x_all, g_all, w_all = (np.concatenate(v) for v in (xin, got, want))
+    dg, dw = g_all - x_all, w_all - x_all           # the attention output projection
+    e_tok = norm_rel(dg, dw, axis=1)
+    arena_q = np.arange(4608, 4740)                 # queries that read the arena
+    print("attention delta norm-rel: all %.2e, worst %.2e, arena queries median %.2e"
+          % (norm_rel(dg, dw), e_tok.max(), np.median(e_tok[arena_q])))
+    assert norm_rel(dg, dw) <= RTOL_LAYER
+    assert np.median(e_tok[arena_q]) <= RTOL_LAYER
+    assert e_tok.max() <= 10 * RTOL_TOKEN
+    # decode kernel vs multi-query kernel on the same state: fp32 rounding,
+    # which now and then flips an int8 of the output projection's Q8_K input
+    d1 = np.concatenate(got[1:]) - np.concatenate(xin[1:])
+    d2 = np.concatenate(gen) - np.concatenate(xin[1:])
+    e_k = norm_rel(d1, d2, axis=1)
+    print("decode vs multi-query kernel: median %.2e, worst %.2e" % (np.median(e_k), e_k.max()))
+    assert np.median(e_k) <= 1e-4 and e_k.max() <= RTOL_TOKEN
+
+
 def test_kv_records_bit_exact(full):
     """The quantized K/V records (q4 + q2, 240 bytes per slot and head) the
     first attention layer appends for a single token, engine vs oracle."""
