@@ -2,7 +2,7 @@
 """Benchmark of the qma B200 engine; rank 0 prints one JSON line.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode|gemv]
+                  [--workload decode|gemv|moe|ep]
 
 decode (default; configs[3]): the full 40-layer random-init qwen35moe
 (hidden 2048, 3 GDN + 1 gated attention x 10, 256 experts top-8 + shared,
@@ -18,7 +18,12 @@ gemv: Q4_K 151936x2048 GEMV at batch 1 (quantize + GEMV).
 moe: one MoE FFN layer (router, top-8 + shared expert, SwiGLU,
 combine, residual) for one decode token through qma_cuda_moe_layer.
 
-N > 1 runs one independent replica per GPU (weak scaling, no collective).
+ep: the 40 MoE blocks with the 256 experts of every layer
+sharded 256/N over the N GPUs, 64 tokens per GPU per step, rows and down
+projections exchanged over NCCL (qma_cuda_ep_moe_layer); weak scaling.
+
+For decode, gemv and moe, N > 1 runs one independent replica per GPU (weak
+scaling, no collective): a batch-1 decode step does not shard.
 --impl reference times the reference's own CPU code (oracle/_ref, built
 from its sources) on the host cores for the same workload.
 """
@@ -599,6 +604,167 @@ def run_moe_ours(args, world, rank, local):
     }), flush=True)
 
 
+# -------------------------------------------------------- expert parallel --
+EP_METRIC = "EP tok/s (qwen35moe MoE blocks, experts sharded 256/N)"
+EP_T = 64                     # tokens per GPU per step: one decode step of 64 sequences
+EP_LAYERS = 40
+EP_LAUNCHES_PER_LAYER = 14    # router, plan, pack, lists, 2 x (gate/up, SwiGLU, down), recv plan, gather, unpack, combine
+Q4K_EXPERT = 512 * (2048 // 256) * 144      # gate or up rows of one expert
+Q6K_EXPERT_GGUF = 2048 * (512 // 256) * 210  # down rows of one expert, GGUF layout
+
+
+def ep_share_uid(world):
+    """The communicator id from rank 0 to every rank through the process
+    group (qma_cuda.ExpertParallel's share_uid)."""
+    def share(uid):
+        obj = [uid]
+        if world > 1:
+            import torch.distributed as dist
+            dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+    return share
+
+
+def ep_layer_weights(il, e0, n_local, dev):
+    """Layer il's MoE weights on the device with only experts e0 ..
+    e0 + n_local - 1 of the routed tables (the synthetic generator's bytes
+    of the whole tensor, sliced; down projections repacked)."""
+    import torch
+    import qma_cuda as Q
+    spec = [("post_attention_norm.weight", F32, 2048), ("ffn_gate_inp.weight", F32, 2048 * 256),
+            ("ffn_gate_exps.weight", Q4_K, 2048 * 512 * 256), ("ffn_up_exps.weight", Q4_K, 2048 * 512 * 256),
+            ("ffn_down_exps.weight", Q6_K, 512 * 2048 * 256), ("ffn_gate_inp_shexp.weight", F32, 2048),
+            ("ffn_gate_shexp.weight", Q4_K, 2048 * 512), ("ffn_up_shexp.weight", Q4_K, 2048 * 512),
+            ("ffn_down_shexp.weight", Q6_K, 512 * 2048)]
+    nbytes = {F32: lambda n: 4 * n, Q4_K: lambda n: n // 256 * 144, Q6_K: lambda n: n // 256 * 210}
+    pb = Q.packed_bytes(Q6_K, 2048, 512)
+    d = {}
+    for name, typ, nel in spec:
+        raw = torch.empty(nbytes[typ](nel), dtype=torch.uint8, device=dev)
+        Q.call("qma_cuda_synth_tensor", f"blk.{il}.{name}".encode(), typ, nel, SEED, Q.ptr(raw), None)
+        if name in ("ffn_gate_exps.weight", "ffn_up_exps.weight"):
+            raw = raw[e0 * Q4K_EXPERT:(e0 + n_local) * Q4K_EXPERT].clone()
+        elif typ == Q6_K:
+            ne = n_local if "_exps." in name else 1
+            first = e0 if "_exps." in name else 0
+            packed = torch.empty(pb * ne, dtype=torch.uint8, device=dev)
+            for e in range(ne):
+                Q.call("qma_cuda_repack", Q6_K, raw.data_ptr() + (first + e) * Q6K_EXPERT_GGUF, 2048, 512,
+                       packed.data_ptr() + e * pb, None)
+            raw = packed
+        d[name] = raw
+    w = Q.MoeWeights(*[d[k].data_ptr() for k in MOE_TENSORS], Q6_K, Q6_K)
+    return w, d
+
+
+def run_ep_ours(args, world, rank, local):
+    """configs[4]'s expert-parallel MoE: the 40 MoE blocks of the random-init
+    model, the 256 experts of every layer sharded 256/N over the N GPUs,
+    EP_T tokens per GPU per step (one decode step of EP_T sequences; weak
+    scaling), every layer's rows and down projections exchanged over NCCL.
+    A step runs the 40 blocks in sequence on the same tokens, from the same
+    input each step.  The weights of the 40 layers (21 GB / N per GPU) cycle
+    through L2 between reuses."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    Q.init(local)
+    dev = torch.device("cuda", local)
+    e0, n_local = Q.ep_shard(rank, world)
+    layers = [ep_layer_weights(il, e0, n_local, dev) for il in range(EP_LAYERS)]
+    torch.cuda.synchronize()
+
+    ep = Q.ExpertParallel(local, rank, world, EP_T, ep_share_uid(world))
+    x = np.random.default_rng(SEED + rank).standard_normal((EP_T, 2048)).astype(np.float32)
+    x0 = torch.from_numpy(x).to(dev)
+    buf = [torch.empty_like(x0), torch.empty_like(x0)]
+    sel = torch.empty((EP_LAYERS, EP_T, 8), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step(src=None, keep_sel=False):
+        buf[0].copy_(x0 if src is None else src, non_blocking=True)
+        for il, (w, _) in enumerate(layers):
+            ep.moe_layer(w, buf[il & 1], EP_T, buf[(il + 1) & 1], sel[il] if keep_sel else None, None, sp)
+        return buf[EP_LAYERS & 1]
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # bytes: the shard's experts that some rank's token selected, per layer
+    step(keep_sel=True)
+    torch.cuda.synchronize()
+    net = [0, 0]
+    for il in range(EP_LAYERS):
+        ep.moe_layer(layers[il][0], buf[0], EP_T, buf[1], None, None, sp)
+        s_, r_, _ = ep.stats()
+        net[0] += s_
+        net[1] += r_
+    all_sel = [sel]
+    if world > 1:
+        import torch.distributed as dist
+        all_sel = [torch.empty_like(sel) for _ in range(world)]
+        dist.all_gather(all_sel, sel)
+    all_sel = torch.stack(all_sel).cpu().numpy()
+    touched = sum(int(np.count_nonzero(np.bincount(all_sel[:, il].ravel(), minlength=256)[e0:e0 + n_local]))
+                  for il in range(EP_LAYERS))
+    expert_bytes = 2 * Q4K_EXPERT + Q6K_EXPERT_GGUF
+    step_bytes = touched * expert_bytes + EP_LAYERS * (expert_bytes + 2048 * 256 * 4 + 2 * 2048 * 4) \
+        + EP_LAYERS * 2 * EP_T * 2048 * 4
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        dist_barrier(world)
+    t_ms = dist_max(sum(e[0].elapsed_time(e[1]) for e in ev), world)
+    # end to end: the step's tokens from pinned host memory, its output back
+    hx = torch.from_numpy(x).pin_memory()
+    hout = torch.empty((EP_T, 2048), dtype=torch.float32).pin_memory()
+    e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, args.steps // 4)
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    e0_.record(stream)
+    for _ in range(e2e_steps):
+        dx = hx.to(dev, non_blocking=True)
+        hout.copy_(step(dx), non_blocking=True)
+    e1_.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dist_max(e0_.elapsed_time(e1_), world)
+    ep.close()
+    peak, peak_kind = load_peaks()
+    achieved = step_bytes / (t_ms / args.steps / 1e3) / 1e9
+    if rank != 0:
+        return
+    tok = world * EP_T
+    print(json.dumps({
+        "metric": EP_METRIC, "value": round(tok * args.steps / (t_ms / 1e3), 1), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4",
+        "data": "synthetic",
+        "config": {"workload": f"configs[4] expert-parallel MoE: the 40 MoE blocks of the random-init qwen35moe, "
+                               f"256 experts sharded 256/{world} per GPU, {EP_T} tokens per GPU per step, "
+                               f"NCCL point-to-point dispatch and return; router without the Zipf prior",
+                   "parallelism": f"ep{world}", "tokens_per_gpu": EP_T,
+                   "l2": "inputs larger than L2 (the 40 layers' weights cycle between reuses)",
+                   "base_metric": BASE_METRIC},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "whole EP step on rank 0 (40 layers: touched shard experts, router, shared expert)",
+                     "algorithmic_bytes_per_step": step_bytes},
+        "nvlink": {"sent_bytes_per_step": net[0], "recv_bytes_per_step": net[1]},
+        "e2e": {"value": round(tok * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": EP_T * 2048 * 4, "d2h_bytes_per_step": EP_T * 2048 * 4},
+        "gpu_launches": EP_LAUNCHES_PER_LAYER * EP_LAYERS * args.steps, "clocks": clk.summary(),
+        "cpu_baseline": None,
+    }), flush=True)
+
+
 # ------------------------------------------------------------------ main ---
 def main():
     ap = argparse.ArgumentParser()
@@ -606,7 +772,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--rows", type=int, default=GN_OUT, help="gemv: output rows")
     ap.add_argument("--cols", type=int, default=GN_IN, help="gemv: input columns (multiple of 256)")
@@ -624,6 +790,8 @@ def main():
             run_decode_ours(args, world, rank, local)
         elif args.workload == "moe":
             run_moe_ours(args, world, rank, local)
+        elif args.workload == "ep":
+            run_ep_ours(args, world, rank, local)
         else:
             run_gemv_ours(args, world, rank, local)
     finally:

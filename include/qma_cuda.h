@@ -265,6 +265,46 @@ int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const float *x2, i
  * is synchronised). */
 int qma_cuda_moe_exact_fallbacks(const void *scratch, int T, int *count);
 
+/* ---- expert parallelism --------------------------------------------------
+ * The MoE block with the 256 experts of each layer sharded over N ranks (one
+ * process per GPU; rank r owns experts r*256/N .. (r+1)*256/N - 1); the
+ * router, the shared expert and the combine run where the token lives.  New
+ * in this engine: the reference runs every expert of moe_ffn on one host
+ * (its (token, expert) task loop, moe_xpar_worker nn.c:652-707, and the
+ * ordered combine, nn.c:604-629, are what the exchange distributes).  Per
+ * layer the ranks exchange, over NCCL point-to-point transfers, one Q8_K
+ * row (2336 bytes) per (token, owning rank) and one fp32 [2048] down
+ * projection per (token, expert) pair; the result is bit-identical to
+ * qma_cuda_moe_layer on the same tokens (16 or more per call, its grouped
+ * path).  Each call blocks the host once, until the counts of the exchange
+ * are known. */
+#define QMA_CUDA_EP_UID_BYTES 128
+typedef struct qma_cuda_ep qma_cuda_ep;
+
+/* Rank 0 makes the communicator id (host bytes [QMA_CUDA_EP_UID_BYTES]) and
+ * hands it to every rank out of band. */
+int qma_cuda_ep_unique_id(uint8_t *uid);
+
+/* Collective over the N ranks: selects `device`, joins the communicator and
+ * allocates the exchange buffers for up to t_max tokens per rank and call
+ * (1..256, t_max * n_ranks <= 512). */
+int qma_cuda_ep_init(int device, const uint8_t *uid, int rank, int n_ranks, int t_max,
+                     qma_cuda_ep **out);
+int qma_cuda_ep_free(qma_cuda_ep *ep);
+
+/* Collective: every rank calls it for the same layer, each with its own
+ * tokens (0..t_max of them; a rank with none still serves its experts).
+ * Arguments as qma_cuda_moe_layer, except that w->gate_exps, up_exps and
+ * down_exps point at this rank's shard of the expert tables (its first
+ * expert at offset 0) and the down projections must be Q6_K. */
+int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const float *x2,
+                          int T, float *x_out, int32_t *sel, float *wts, void *stream);
+
+/* Bytes this rank sent and received in its last qma_cuda_ep_moe_layer call
+ * (itself included) and the rows its experts served. */
+int qma_cuda_ep_stats(const qma_cuda_ep *ep, uint64_t *sent_bytes, uint64_t *recv_bytes,
+                      int *rows_in);
+
 #ifdef __cplusplus
 }
 #endif

@@ -877,22 +877,43 @@ int moe_wait_timeouts() {
 
 static bool g_moe_attrs = false;
 
+static int moe_attrs() {
+    if (g_moe_attrs) return QMA_CUDA_OK;
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ROUTER_SMEM)));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
+    // the 9 expert clusters must be co-resident beside other kernels' CTAs:
+    // prefer the largest shared-memory carveout (two CTAs per SM)
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    g_moe_attrs = true;
+    return QMA_CUDA_OK;
+}
+
+int moe_route(const qma_cuda_moe_weights &w, const float *x2, int T, const MoeScratch &s, int *sel, float *wts,
+              cudaStream_t st) {
+    int rc = moe_attrs();
+    if (rc) return rc;
+    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, false, x2,
+                             w.post_norm, w.gate_inp, w.gate_inp_shexp, s, sel, wts));
+    return QMA_CUDA_OK;
+}
+
+int moe_combine(const MoeScratch &s, const float *x2, float *x_out, int T, cudaStream_t st) {
+    const MoeNormTail none;
+    QMA_CHECK_CUDA(launch_ex(moe_combine_norm_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), s, x2, x_out,
+                             none.w, none.norm_from, none.xq, none.xd, none.xs, none.pf));
+    return QMA_CUDA_OK;
+}
+
 int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_out, int *sel,
               float *wts, void *scratch, cudaStream_t st, bool clear_counters, const MoeNormTail *tail) {
     MoeScratch s = moe_scratch_layout(scratch, T);
-    if (!g_moe_attrs) {
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ROUTER_SMEM)));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
-        // the 9 expert clusters must be co-resident beside other kernels' CTAs:
-        // prefer the largest shared-memory carveout (two CTAs per SM)
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        g_moe_attrs = true;
-    }
+    int rc0 = moe_attrs();
+    if (rc0) return rc0;
     if (clear_counters) {
         QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
     }

@@ -39,6 +39,18 @@ struct MoeScratch {
     int16_t *hs;           // [T * 9][32]
 };
 int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st);
+// The grouped pipeline on part of the work: groups g0 .. g0 + ng - 1 of the
+// 257 (256 = the shared expert; routed group e reads expert e of the tables
+// w points at), the pair lists built first when `lists`, the SwiGLU on pair
+// slots q0 .. q0 + nq - 1.  The expert-parallel layer runs the routed groups
+// of its shard over received rows and the shared group over its own tokens.
+int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st, int g0, int ng,
+                      bool lists, int q0, int nq);
+// The router alone (RMSNorm, Q8_K of the normed input, exact top-8, the
+// shared-expert gate) into s, and the slot combine + residual alone.
+int moe_route(const qma_cuda_moe_weights &w, const float *x2, int T, const MoeScratch &s, int *sel, float *wts,
+              cudaStream_t st);
+int moe_combine(const MoeScratch &s, const float *x2, float *x_out, int T, cudaStream_t st);
 
 size_t moe_scratch_bytes(int T);
 MoeScratch moe_scratch_layout(void *base, int T);

@@ -75,9 +75,9 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                                                          const uint8_t *__restrict__ up_exps,
                                                          const uint8_t *__restrict__ gate_sh,
                                                          const uint8_t *__restrict__ up_sh, int T,
-                                                         MoeScratch s) {
+                                                         MoeScratch s, int e0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
-    const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    const int e = e0 + int(blockIdx.y), tok0 = blockIdx.z * GT;
     __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
@@ -181,8 +181,8 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
 
 // 3. -------------------------------------------------------- SwiGLU + Q8_K --
 // One CTA per pair slot, warp b: hidden block b of silu(gate) * up.
-__global__ void __launch_bounds__(64) moe_swiglu_kernel(MoeScratch s) {
-    const int q = blockIdx.x, lane = threadIdx.x & 31, b = threadIdx.x >> 5;
+__global__ void __launch_bounds__(64) moe_swiglu_kernel(MoeScratch s, int q0) {
+    const int q = q0 + int(blockIdx.x), lane = threadIdx.x & 31, b = threadIdx.x >> 5;
     pdl_trigger();
     pdl_wait();
     const float *h = s.hg + size_t(q) * (2 * MOE_FF);
@@ -203,9 +203,9 @@ __global__ void __launch_bounds__(64) moe_swiglu_kernel(MoeScratch s) {
 // int8 scale.  Grid (2048 / GR, 257, tiles); output part[t][slot][row].
 __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict__ down_exps, size_t down_bytes,
                                                        const uint8_t *__restrict__ down_sh, int T,
-                                                       MoeScratch s) {
+                                                       MoeScratch s, int e0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
-    const int e = blockIdx.y, tok0 = blockIdx.z * GT;
+    const int e = e0 + int(blockIdx.y), tok0 = blockIdx.z * GT;
     __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
@@ -299,19 +299,25 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
         }
 }
 
-int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st) {
+int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st, int g0, int ng,
+                      bool lists, int q0, int nq) {
     const bool pdl = pdl_enabled();
     const int tiles = (T + GT - 1) / GT;
-    QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
-    QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, NSHARED + 1, tiles), dim3(128), 0, st, 1, pdl,
+    if (lists)
+        QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
+    QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
                              static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
                              static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp), T,
-                             s));
-    QMA_CHECK_CUDA(launch_ex(moe_swiglu_kernel, dim3(T * MOE_NSLOT), dim3(64), 0, st, 1, pdl, s));
-    QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, NSHARED + 1, tiles), dim3(128), 0, st, 1, pdl,
+                             s, g0));
+    QMA_CHECK_CUDA(launch_ex(moe_swiglu_kernel, dim3(nq), dim3(64), 0, st, 1, pdl, s, q0));
+    QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
                              static_cast<const uint8_t *>(w.down_exps), packed_bytes(w.down_type, MOE_EMBD, MOE_FF),
-                             static_cast<const uint8_t *>(w.down_shexp), T, s));
+                             static_cast<const uint8_t *>(w.down_shexp), T, s, g0));
     return QMA_CUDA_OK;
+}
+
+int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st) {
+    return moe_grouped_range(w, T, s, st, 0, NSHARED + 1, true, 0, T * MOE_NSLOT);
 }
 
 }  // namespace qma

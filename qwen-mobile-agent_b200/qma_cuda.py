@@ -135,6 +135,59 @@ class MoeWeights(C.Structure):
 
 
 _SIGS["qma_cuda_model_moe_weights"] = (_i32, [_vp, _i32, C.POINTER(MoeWeights)])
+_SIGS.update({
+    "qma_cuda_ep_unique_id": (_i32, [_vp]),
+    "qma_cuda_ep_init": (_i32, [_i32, _vp, _i32, _i32, _i32, C.POINTER(_vp)]),
+    "qma_cuda_ep_free": (_i32, [_vp]),
+    "qma_cuda_ep_moe_layer": (_i32, [_vp, C.POINTER(MoeWeights), _vp, _i32, _vp, _vp, _vp, _vp]),
+    "qma_cuda_ep_stats": (_i32, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_i32)]),
+})
+
+EP_UID_BYTES = 128
+N_EXPERT = 256
+
+
+def ep_shard(rank: int, n_ranks: int) -> tuple[int, int]:
+    """(first expert, expert count) of a rank's shard: rank r owns experts
+    r * 256/N .. (r + 1) * 256/N - 1."""
+    if n_ranks < 1 or n_ranks > 8 or N_EXPERT % n_ranks or not 0 <= rank < n_ranks:
+        raise ValueError(f"rank {rank} of {n_ranks}: 1..8 ranks dividing 256")
+    n_local = N_EXPERT // n_ranks
+    return rank * n_local, n_local
+
+
+class ExpertParallel:
+    """One rank's handle on the expert-parallel MoE block (qma_cuda_ep_*).
+
+    share_uid(uid_or_None) -> bytes carries the communicator id from rank 0
+    to the others (rank 0 passes its id and gets it back; the others pass
+    None): a torch.distributed broadcast, a store, a file."""
+
+    def __init__(self, device: int, rank: int, n_ranks: int, t_max: int, share_uid):
+        ep_shard(rank, n_ranks)
+        uid = (C.c_uint8 * EP_UID_BYTES)()
+        if rank == 0:
+            call("qma_cuda_ep_unique_id", uid)
+        raw = share_uid(bytes(uid) if rank == 0 else None)
+        if len(raw) != EP_UID_BYTES:
+            raise ValueError(f"communicator id of {len(raw)} bytes")
+        uid = (C.c_uint8 * EP_UID_BYTES).from_buffer_copy(raw)
+        h = _vp()
+        call("qma_cuda_ep_init", device, uid, rank, n_ranks, t_max, C.byref(h))
+        self.h, self.rank, self.n_ranks, self.t_max = h, rank, n_ranks, t_max
+
+    def moe_layer(self, w: MoeWeights, x2, T: int, x_out, sel=None, wts=None, stream=None) -> None:
+        call("qma_cuda_ep_moe_layer", self.h, C.byref(w), ptr(x2), T, ptr(x_out), ptr(sel), ptr(wts), stream)
+
+    def stats(self) -> tuple[int, int, int]:
+        s, r, n = C.c_uint64(), C.c_uint64(), C.c_int()
+        call("qma_cuda_ep_stats", self.h, C.byref(s), C.byref(r), C.byref(n))
+        return s.value, r.value, n.value
+
+    def close(self) -> None:
+        if self.h:
+            call("qma_cuda_ep_free", self.h)
+            self.h = None
 
 
 class QmaError(RuntimeError):

@@ -33,3 +33,21 @@ def test_packed_sizes():
     assert Q.packed_bytes(Q.Q4_K, 512, 2048) == 512 * 8 * 144
     assert Q.packed_bytes(Q.Q6_K, 2048, 512) == 2048 * 2 * 210
     assert Q.packed_bytes(Q.Q8_0, 151936, 2048) == 151936 * 64 * 34
+
+
+def test_expert_parallel_arguments_and_shards():
+    import pytest
+    lib = Q.lib()
+    uid = (C.c_uint8 * Q.EP_UID_BYTES)()
+    h = C.c_void_p()
+    # rank counts that do not divide 256, ranks out of range, oversized chunks
+    for args in [(0, uid, 0, 3, 8), (0, uid, 2, 2, 8), (0, uid, 0, 2, 300), (0, uid, 0, 8, 128),
+                 (0, None, 0, 2, 8)]:
+        assert lib.qma_cuda_ep_init(*args, C.byref(h)) == Q.ERR_INVALID, args
+        assert "qma_cuda_ep_init" in Q.last_error()
+    assert lib.qma_cuda_ep_moe_layer(None, None, None, 1, None, None, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ep_free(None) == Q.OK
+    assert [Q.ep_shard(r, 4) for r in range(4)] == [(0, 64), (64, 64), (128, 64), (192, 64)]
+    assert Q.ep_shard(0, 1) == (0, 256)
+    with pytest.raises(ValueError):
+        Q.ep_shard(0, 3)

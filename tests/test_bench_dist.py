@@ -1,7 +1,8 @@
 """The multi-rank plumbing of bench.py on CPU (gloo, world size 2): every
-rank reports the slowest rank's time, and the barrier returns on all ranks.
-bench.py runs one independent replica per GPU; these helpers are its only
-cross-rank steps."""
+rank reports the slowest rank's time, the barrier returns on all ranks, and
+the expert-parallel workload's communicator id reaches every rank with the
+shard each rank then owns.  The replica workloads have no other cross-rank
+step; the expert-parallel exchange itself runs on GPUs (tests/test_ep_gpu.py)."""
 import os
 import socket
 import sys
@@ -29,6 +30,12 @@ def _rank(rank, world, port, out):
         bench.dist_barrier(world)
         out[rank] = bench.dist_max(1.5 + rank, world)
         bench.dist_barrier(world)
+        sys.path.insert(0, os.path.join(ROOT, "qwen-mobile-agent_b200"))
+        import qma_cuda as Q
+        uid = bytes(range(128)) if rank == 0 else None
+        got = bench.ep_share_uid(world)(uid)
+        out[("uid", rank)] = got == bytes(range(128))
+        out[("shard", rank)] = Q.ep_shard(rank, world)
     finally:
         dist.destroy_process_group()
 
@@ -44,4 +51,5 @@ def test_dist_max_and_barrier_gloo_two_ranks():
         for p in procs:
             p.join(120)
         assert all(p.exitcode == 0 for p in procs)
-        assert dict(out) == {0: 2.5, 1: 2.5}
+        assert dict(out) == {0: 2.5, 1: 2.5, ("uid", 0): True, ("uid", 1): True,
+                             ("shard", 0): (0, 128), ("shard", 1): (128, 128)}
