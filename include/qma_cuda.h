@@ -130,6 +130,20 @@ typedef struct qma_cuda_state qma_cuda_state;   /* one sequence's state    */
  * n_vocab comes from token_embd.weight. */
 int qma_cuda_model_load(int device, const qma_cuda_tensor *tensors, uint32_t n,
                         const void *host_data, uint64_t data_size, qma_cuda_model **out);
+/* The parsing half of qma_load (gguf.c:104-316) on a GGUF v2/v3 file: the
+ * tensor infos (host array of `cap` entries; *n_tensors receives the count,
+ * so cap 0 sizes the array), the file offset of the aligned data section
+ * and the tokenizer's token count (0 if the file has none).  Checks what
+ * qma_load checks: magic, metadata, qwen35moe hyper-parameters (40 layers,
+ * embedding 2048, heads 16/2, 64 rotary dims in sections 11/11/10, after
+ * dropping the "qwen35moe." / "qwen35." key prefix), supported types, whole
+ * blocks per row, every tensor inside the file.  Unlike qma_load it also
+ * accepts Q8_0 tensors.  Host only: touches no device. */
+int qma_cuda_gguf_scan(const char *path, qma_cuda_tensor *tensors, uint32_t cap,
+                       uint32_t *n_tensors, uint64_t *data_offset, uint64_t *n_tokens);
+/* qma_cuda_gguf_scan + qma_cuda_model_load on the file's data section
+ * (mapped read-only, unmapped before returning). */
+int qma_cuda_model_load_gguf(int device, const char *path, qma_cuda_model **out);
 /* Same model with random-init weights generated on the device
  * (qma_cuda_synth_tensor per tensor): no host copy of the weights. */
 int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n,

@@ -145,6 +145,9 @@ def ref() -> C.CDLL:
         R.qr_half_to_float.restype = f32
         R.qr_float_to_half.argtypes = [f32]
         R.qr_float_to_half.restype = C.c_uint16
+        R.qr_gguf_load.argtypes = [C.c_char_p, C.POINTER(Tensor), i32, C.POINTER(C.c_int),
+                                   C.POINTER(C.c_uint64), C.POINTER(C.c_int), C.c_char_p, i32]
+        R.qr_gguf_load.restype = i32
         R.qma_q8k_quant.argtypes = [vp, i32, vp, vp, vp]
         R.qma_q8k_dot.argtypes = [vp, i32, vp, vp, vp, i32]
         R.qma_q8k_dot.restype = f32

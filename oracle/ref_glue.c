@@ -203,3 +203,30 @@ int qr_state_n_pos(runstate_t *rs) { return rs->n_pos; }
 /* the reference's fp16 helpers (qma.h:101-152) as built here */
 float qr_half_to_float(uint16_t h) { return half_to_float(h); }
 uint16_t qr_float_to_half(float f) { return float_to_half(f); }
+
+/* qma_load (gguf.c:104-513) on a GGUF file: its tensor table (up to cap
+ * entries), the count, the data section's offset in the file and the
+ * vocabulary size; or -1 with qma_load's message in err. */
+int qr_gguf_load(const char *path, qr_tensor *out, int cap, int *n, uint64_t *data_off, int *n_vocab,
+                 char *err, int errlen)
+{
+    qma_t *m = calloc(1, sizeof(qma_t));
+    if (!m) return -1;
+    err[0] = 0;
+    int rc = qma_load(m, path, err, (size_t)errlen);
+    if (rc == 0) {
+        *n = (int)m->n_tensors;
+        for (int i = 0; i < cap && i < (int)m->n_tensors; i++) {
+            memcpy(out[i].name, m->tensors[i].name, sizeof out[i].name);
+            out[i].type = m->tensors[i].type;
+            for (int d = 0; d < 3; d++) out[i].ne[d] = m->tensors[i].ne[d];
+            out[i].off = m->tensors[i].off;
+            out[i].nbytes = m->tensors[i].nbytes;
+        }
+        *data_off = (uint64_t)(m->data - m->map);
+        *n_vocab = m->n_vocab;
+    }
+    if (m->fd >= 0 || m->tensors) qma_free(m);
+    free(m);
+    return rc;
+}

@@ -52,6 +52,9 @@ _TP = C.POINTER(Tensor)
 _SIGS.update({
     "qma_cuda_model_load": (_i32, [_i32, _TP, C.c_uint32, _vp, _u64, C.POINTER(_vp)]),
     "qma_cuda_model_synth": (_i32, [_i32, _TP, C.c_uint32, _u64, C.POINTER(_vp)]),
+    "qma_cuda_gguf_scan": (_i32, [C.c_char_p, _TP, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(_u64),
+                                  C.POINTER(_u64)]),
+    "qma_cuda_model_load_gguf": (_i32, [_i32, C.c_char_p, C.POINTER(_vp)]),
     "qma_cuda_model_free": (_i32, [_vp]),
     "qma_cuda_model_n_vocab": (_i32, [_vp]),
     "qma_cuda_ecache_get": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
@@ -67,12 +70,26 @@ _SIGS.update({
 })
 
 
-class Model:
-    """Device-resident qwen35moe weights (qma_cuda_model)."""
+def gguf_scan(path: str):
+    """qma_cuda_gguf_scan: (tensor table, count, data section offset in the
+    file, tokenizer token count)."""
+    n, off, ntok = C.c_uint32(), C.c_uint64(), C.c_uint64()
+    call("qma_cuda_gguf_scan", path.encode(), None, 0, C.byref(n), C.byref(off), C.byref(ntok))
+    arr = (Tensor * max(n.value, 1))()
+    call("qma_cuda_gguf_scan", path.encode(), arr, n.value, C.byref(n), C.byref(off), C.byref(ntok))
+    return arr, n.value, off.value, ntok.value
 
-    def __init__(self, tensors, n, host_blob=None, seed=None, device=0):
+
+class Model:
+    """Device-resident qwen35moe weights (qma_cuda_model): from a tensor
+    table plus a host data section, from random-init weights generated on
+    the device (seed), or from a GGUF file (gguf=path)."""
+
+    def __init__(self, tensors=None, n=0, host_blob=None, seed=None, device=0, gguf=None):
         h = _vp()
-        if host_blob is not None:
+        if gguf is not None:
+            call("qma_cuda_model_load_gguf", device, gguf.encode(), C.byref(h))
+        elif host_blob is not None:
             call("qma_cuda_model_load", device, tensors, n, ptr(host_blob), host_blob.nbytes, C.byref(h))
         else:
             call("qma_cuda_model_synth", device, tensors, n, seed, C.byref(h))

@@ -288,6 +288,39 @@ def test_single_token_eval_replays_the_decode_graph(full):
         b.close()
 
 
+def test_model_load_gguf_reads_the_file(full, tmp_path):
+    """qma_cuda_model_load_gguf on a GGUF file of the full layout (a sparse
+    file: token_embd's bytes written, every other tensor zero) yields the
+    embedding rows qma_cuda_model_load gives from the same bytes."""
+    import gguf_file as G
+    arr, n = full["arr"], full["n"]
+    tensors = []
+    for i in range(n):
+        ne = [int(d) for d in arr[i].ne]
+        tensors.append((arr[i].name.decode(), int(arr[i].type), tuple(ne if ne[2] > 1 else ne[:2]),
+                        int(arr[i].off)))
+    idx = O.tensor_index(arr, n)
+    emb = arr[idx["token_embd.weight"]]
+    p = tmp_path / "full.gguf"
+    start = G.write(p, G.qwen35moe_kv(), tensors, data_size=full["blob"].nbytes)
+    with open(p, "r+b") as f:
+        f.seek(start + emb.off)
+        f.write(full["blob"][emb.off:emb.off + emb.nbytes].tobytes())
+    m = Q.Model(gguf=str(p))
+    try:
+        assert m.n_vocab == full["model"].n_vocab
+        prompt = np.array([0, 5, 77, 151935], np.int32)
+        st = Q.State(m, 256)
+        try:
+            got = st.eval_hidden(prompt, 0)
+        finally:
+            st.close()
+        want = gpu_hidden(full["model"], prompt, 0)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        m.close()
+
+
 def test_model_synth_matches_model_load(full):
     m2 = Q.Model(full["tp"], full["n"], seed=SEED)
     try:
