@@ -208,6 +208,12 @@ void *qma_cuda_state_stream(const qma_cuda_state *s);
 /* Kernel launches in one captured decode step (0 before the first capture),
  * and the bytes of device memory the state holds. */
 int qma_cuda_state_stats(const qma_cuda_state *s, int *graph_kernels, uint64_t *state_bytes);
+/* Device pointer of the state's logits [n_vocab]: the last position's
+ * logits after a single-token qma_cuda_eval (also with logits NULL, which
+ * skips their copy to the host), after qma_cuda_decode_greedy, or after an
+ * eval of several tokens that returned the last token's logits
+ * (logits_all 0). */
+const float *qma_cuda_state_logits(const qma_cuda_state *s);
 
 /* ---- MoE FFN block ------------------------------------------------------
  * Replaces moe_ffn (nn.c:509-649) with its q8k expert kernels
@@ -278,6 +284,25 @@ int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const float *x2, i
  * needed the exact sequential recompute (host int, read after the stream
  * is synchronised). */
 int qma_cuda_moe_exact_fallbacks(const void *scratch, int T, int *count);
+
+/* ---- sampling -------------------------------------------------------------
+ * The first phase of qma's sampler on the GPU: repeat penalty, temperature
+ * and the top-k candidates, replacing sampler_candidates (sampler.c:36-95)
+ * so that k candidates instead of the logits cross to the host, where the
+ * grammar mask and sampler_pick (sampler.c:100-134) run unchanged.
+ * logits: device float [n_vocab] (e.g. qma_cuda_state_logits after a
+ * single-token qma_cuda_eval with logits NULL); last_tokens: host, the
+ * sampler's last n_last (0..64) tokens, oldest first; k = top_k clamped to
+ * 1..min(n_vocab, max_k), max_k 1..QMA_CUDA_SAMPLE_MAX_K.  Outputs (host):
+ * ids / lgs [k], the candidates' token ids and scaled logits, largest
+ * first, and *n_out = k.  The scaled logits are bit-identical to the
+ * reference's; candidates of equal value are ordered by token id (the
+ * reference's qsort leaves that order unspecified).  Blocks until done.
+ * Calls share a fixed device result array: they must not overlap. */
+#define QMA_CUDA_SAMPLE_MAX_K 64
+int qma_cuda_sample_candidates(const float *logits, int n_vocab, const int32_t *last_tokens,
+                               int n_last, float repeat_penalty, float temp, int top_k, int max_k,
+                               int32_t *ids, float *lgs, int *n_out, void *stream);
 
 /* ---- expert parallelism --------------------------------------------------
  * The MoE block with the 256 experts of each layer sharded over N ranks (one

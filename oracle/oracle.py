@@ -148,6 +148,8 @@ def ref() -> C.CDLL:
         R.qr_gguf_load.argtypes = [C.c_char_p, C.POINTER(Tensor), i32, C.POINTER(C.c_int),
                                    C.POINTER(C.c_uint64), C.POINTER(C.c_int), C.c_char_p, i32]
         R.qr_gguf_load.restype = i32
+        R.qr_sampler_candidates.argtypes = [i32, vp, vp, i32, f32, f32, i32, vp, vp, i32]
+        R.qr_sampler_candidates.restype = i32
         R.qma_q8k_quant.argtypes = [vp, i32, vp, vp, vp]
         R.qma_q8k_dot.argtypes = [vp, i32, vp, vp, vp, i32]
         R.qma_q8k_dot.restype = f32

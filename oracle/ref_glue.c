@@ -230,3 +230,15 @@ int qr_gguf_load(const char *path, qr_tensor *out, int cap, int *n, uint64_t *da
     free(m);
     return rc;
 }
+
+/* sampler_candidates (sampler.c:36-95) with a sampler set up by
+ * sampler_init and holding the given last tokens (oldest first). */
+int qr_sampler_candidates(int n_vocab, const float *logits, const int *last, int n_last, float penalty,
+                          float temp, int top_k, int *ids, float *lgs, int max_k)
+{
+    sampler_t s;
+    sampler_init(&s, 1, temp, top_k, 0.95f, penalty);
+    for (int i = 0; i < n_last && i < 64; i++) s.last_tokens[i] = last[i];
+    s.n_last = n_last < 64 ? n_last : 64;
+    return sampler_candidates(n_vocab, logits, &s, ids, lgs, max_k);
+}

@@ -1018,6 +1018,8 @@ int qma_cuda_model_free(qma_cuda_model *m) {
 
 int qma_cuda_model_n_vocab(const qma_cuda_model *m) { return m ? m->n_vocab : 0; }
 
+const float *qma_cuda_state_logits(const qma_cuda_state *s) { return s ? s->logits : nullptr; }
+
 int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const void **gate,
                         const void **up, const void **down) {
     qma::clear_error();

@@ -67,6 +67,9 @@ _SIGS.update({
     "qma_cuda_state_stream": (_vp, [_vp]),
     "qma_cuda_state_kv_slot": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "qma_cuda_state_stats": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_u64)]),
+    "qma_cuda_state_logits": (_vp, [_vp]),
+    "qma_cuda_sample_candidates": (_i32, [_vp, _i32, _vp, _i32, _f32, _f32, _i32, _i32, _vp, _vp,
+                                          C.POINTER(_i32), _vp]),
 })
 
 

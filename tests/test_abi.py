@@ -51,3 +51,15 @@ def test_expert_parallel_arguments_and_shards():
     assert Q.ep_shard(0, 1) == (0, 256)
     with pytest.raises(ValueError):
         Q.ep_shard(0, 3)
+
+
+def test_sampler_arguments():
+    lib = Q.lib()
+    ids = (C.c_int32 * 64)()
+    lgs = (C.c_float * 64)()
+    n = C.c_int()
+    last = (C.c_int32 * 65)()
+    for args in [(None, 10, None, 0, 1.0, 1.0, 5, 5), (1, 10, None, 0, 1.0, 1.0, 5, 65),
+                 (1, 10, last, 65, 1.0, 1.0, 5, 5), (1, 10, None, 3, 1.0, 1.0, 5, 5), (1, 0, None, 0, 1.0, 1.0, 5, 5)]:
+        assert lib.qma_cuda_sample_candidates(*args, ids, lgs, C.byref(n), None) == Q.ERR_INVALID, args
+    assert lib.qma_cuda_state_logits(None) is None

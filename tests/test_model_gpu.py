@@ -321,6 +321,50 @@ def test_model_load_gguf_reads_the_file(full, tmp_path):
         m.close()
 
 
+def _device_floats(dptr, n):
+    """n floats at a raw device address, copied to the host (cudaMemcpy of
+    the CUDA runtime the engine library already loaded)."""
+    rt = C.CDLL("libcudart.so.12")
+    host = np.zeros(n, np.float32)
+    assert rt.cudaMemcpy(C.c_void_p(host.ctypes.data), C.c_void_p(dptr), C.c_size_t(4 * n), 2) == 0
+    return host
+
+
+def test_state_logits_feed_the_gpu_sampler(full, ref_lib):
+    """A single-token eval without host logits leaves them on the device
+    (qma_cuda_state_logits): the same values the host copy returns, and the
+    GPU sampler's candidates on them equal the reference's
+    sampler_candidates on the host copy."""
+    rng = np.random.default_rng(23)
+    prompt = rng.integers(0, O.N_VOCAB, 16).astype(np.int32)
+    a, b = Q.State(full["model"], N_CTX), Q.State(full["model"], N_CTX)
+    try:
+        la = a.eval(prompt)
+        b.eval(prompt)
+        tok = np.array([int(np.argmax(la))], np.int32)
+        want_logits = a.eval(tok)
+        Q.call("qma_cuda_eval", full["model"].h, b.h, Q.ptr(tok), 1, None, 0)
+        dptr = Q.lib().qma_cuda_state_logits(b.h)
+        n = full["model"].n_vocab
+        host = _device_floats(dptr, n)
+        assert np.array_equal(host.view(np.uint32), want_logits.view(np.uint32))
+        last = np.array(list(prompt[-10:]) + [int(tok[0])], np.int32)
+        ids = np.zeros(64, np.int32)
+        lgs = np.zeros(64, np.float32)
+        cnt = C.c_int()
+        Q.call("qma_cuda_sample_candidates", dptr, n, Q.ptr(last), len(last), 1.1, 0.7, 40, 40, Q.ptr(ids),
+               Q.ptr(lgs), C.byref(cnt), None)
+        rids, rlgs = np.zeros(64, np.int32), np.zeros(64, np.float32)
+        rn = ref_lib.qr_sampler_candidates(n, want_logits.ctypes.data, last.ctypes.data, len(last), 1.1, 0.7, 40,
+                                           rids.ctypes.data, rlgs.ctypes.data, 40)
+        assert cnt.value == rn == 40
+        assert np.array_equal(ids[:40], rids[:40])
+        assert np.array_equal(lgs[:40].view(np.uint32), rlgs[:40].view(np.uint32))
+    finally:
+        a.close()
+        b.close()
+
+
 def test_model_synth_matches_model_load(full):
     m2 = Q.Model(full["tp"], full["n"], seed=SEED)
     try:
