@@ -208,6 +208,22 @@ void *qma_cuda_state_stream(const qma_cuda_state *s);
 /* Kernel launches in one captured decode step (0 before the first capture),
  * and the bytes of device memory the state holds. */
 int qma_cuda_state_stats(const qma_cuda_state *s, int *graph_kernels, uint64_t *state_bytes);
+/* Session files in the reference's byte formats (agent.c:409-416 writes
+ * them, agent.c:765-816 resumes from them): state_path as runstate_save
+ * (nn.c:2011-2025: int32 n_pos, then per gated-delta-net layer the conv
+ * state [8192][3] and recurrent state [32][128][128] floats), kv_path as
+ * the KV slab file (nn.c:1878-1935: per attention layer [4 heads][n_ctx]
+ * 240-byte records), salience_path as hcm_save (nn.c:1156-1171).  Any path
+ * may be NULL to skip that file.  Load checks sizes and n_ctx, and leaves
+ * the heavy-hitter bookkeeping as a fresh qma process has it after
+ * hcm_load (nn.c:947-970, 1173-1209): tiers, live index and quantisation
+ * scores cleared, the next rebuild at the first eval from position 128 on;
+ * a salience file whose arena sections are missing or cut short loads with
+ * no pinned entries, as hcm_load does. */
+int qma_cuda_state_save(const qma_cuda_state *s, const char *state_path, const char *kv_path,
+                        const char *salience_path);
+int qma_cuda_state_load(qma_cuda_state *s, const char *state_path, const char *kv_path,
+                        const char *salience_path);
 /* Device pointer of the state's logits [n_vocab]: the last position's
  * logits after a single-token qma_cuda_eval (also with logits NULL, which
  * skips their copy to the host), after qma_cuda_decode_greedy, or after an

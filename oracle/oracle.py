@@ -150,6 +150,10 @@ def ref() -> C.CDLL:
         R.qr_gguf_load.restype = i32
         R.qr_sampler_candidates.argtypes = [i32, vp, vp, i32, f32, f32, i32, vp, vp, i32]
         R.qr_sampler_candidates.restype = i32
+        R.qr_runstate_load.argtypes = [vp, C.c_char_p]
+        R.qr_runstate_load.restype = i32
+        R.qr_state_n_pos.argtypes = [vp]
+        R.qr_state_n_pos.restype = i32
         R.qma_q8k_quant.argtypes = [vp, i32, vp, vp, vp]
         R.qma_q8k_dot.argtypes = [vp, i32, vp, vp, vp, i32]
         R.qma_q8k_dot.restype = f32

@@ -242,3 +242,6 @@ int qr_sampler_candidates(int n_vocab, const float *logits, const int *last, int
     s.n_last = n_last < 64 ? n_last : 64;
     return sampler_candidates(n_vocab, logits, &s, ids, lgs, max_k);
 }
+
+/* runstate_load (nn.c:2027-2042) into a state made by qr_state_new. */
+int qr_runstate_load(runstate_t *rs, const char *path) { return runstate_load(rs, path); }

@@ -4,8 +4,10 @@
 //
 // Reference: qma_eval (nn.c:2056-2308), runstate_init_kv (nn.c:1878-1979),
 // hcm_rebuild (nn.c:981-1150), embed_row (nn.c:2044-2054), qma_load's tensor
-// resolution (gguf.c:302-345).
+// resolution (gguf.c:302-345), session files (runstate_save/load
+// nn.c:2011-2042, hcm_save/load nn.c:1156-1209).
 #include <math.h>
+#include <stdio.h>
 #include <string.h>
 
 #include <string>
@@ -1115,6 +1117,282 @@ int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int 
     QMA_REQUIRE(m && s && s->m == m && n_steps > 0 && token >= 0 && token < m->n_vocab,
                 "qma_cuda_decode_greedy: bad arguments");
     return qma::decode_greedy(s, token, n_steps, tokens_out, logits);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- session --
+// A sequence's state saved to and restored from the files
+// qma's session keeps (agent.c:409-416, 765-816), byte for byte in the
+// reference's formats:
+//   state    runstate_save / runstate_load (nn.c:2011-2042): int32 n_pos, then
+//            per gated-delta-net layer the conv state float [8192][3] and the
+//            recurrent state float [32][128][128] (row j of head h holds
+//            S[i][j] at j * 128 + i);
+//   kv       the KV slab file of runstate_init_kv (nn.c:1878-1935): per
+//            attention layer [K head 0, K head 1, V head 0, V head 1][n_ctx]
+//            240-byte records;
+//   salience hcm_save / hcm_load (nn.c:1156-1209): uint32 n_ctx, salience
+//            float [10][n_ctx], arena positions int32 [2048], arena salience
+//            float [10][2048], arena records [10][4][2048][240].
+// The engine's device buffers already use these layouts, so a save is one
+// device-to-host copy per section.  A load also resets the heavy-hitter
+// bookkeeping the way a fresh qma process starts (hcm_init, nn.c:947-970):
+// tiers, live index and quantisation scores cleared, the next rebuild due at
+// position 128, so the first eval after it rebuilds the live index from the
+// restored salience and arena.
+namespace qma {
+namespace {
+
+struct File {
+    FILE *f = nullptr;
+    explicit File(const char *path, const char *mode) { f = fopen(path, mode); }
+    ~File() {
+        if (f) fclose(f);
+    }
+};
+
+// device -> file, through a bounded host buffer
+int write_dev(FILE *f, const void *dev, size_t bytes, cudaStream_t st) {
+    static constexpr size_t CH = size_t(64) << 20;
+    std::vector<uint8_t> h(bytes < CH ? bytes : CH);
+    for (size_t o = 0; o < bytes; o += CH) {
+        const size_t n = bytes - o < CH ? bytes - o : CH;
+        QMA_CHECK_CUDA(cudaMemcpyAsync(h.data(), static_cast<const uint8_t *>(dev) + o, n, cudaMemcpyDeviceToHost,
+                                       st));
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+        if (fwrite(h.data(), 1, n, f) != n) {
+            set_error("session: write failed");
+            return QMA_CUDA_ERR_INVALID;
+        }
+    }
+    return QMA_CUDA_OK;
+}
+
+// file -> device; returns 1 (and copies nothing more) if the file ends early
+int read_dev(FILE *f, void *dev, size_t bytes, cudaStream_t st, bool *short_read) {
+    static constexpr size_t CH = size_t(64) << 20;
+    std::vector<uint8_t> h(bytes < CH ? bytes : CH);
+    for (size_t o = 0; o < bytes; o += CH) {
+        const size_t n = bytes - o < CH ? bytes - o : CH;
+        if (fread(h.data(), 1, n, f) != n) {
+            *short_read = true;
+            return QMA_CUDA_OK;
+        }
+        QMA_CHECK_CUDA(cudaMemcpyAsync(static_cast<uint8_t *>(dev) + o, h.data(), n, cudaMemcpyHostToDevice, st));
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    }
+    return QMA_CUDA_OK;
+}
+
+size_t conv_bytes() { return sizeof(float) * size_t(CONV_DIM) * 3; }
+size_t ssm_bytes() { return sizeof(float) * size_t(VHEADS) * SSTATE * SSTATE; }
+size_t kv_layer_bytes(int n_ctx) { return size_t(2) * NHEAD_KV * n_ctx * KVQ_SLOT; }
+size_t arena_layer_bytes() { return size_t(2) * NHEAD_KV * HCM_H_PIN * KVQ_SLOT; }
+
+int save_state(const qma_cuda_state *s, const char *path) {
+    File f(path, "wb");
+    if (!f.f) {
+        set_error("session: cannot write %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    const int32_t np = s->n_pos;
+    if (fwrite(&np, 4, 1, f.f) != 1) {
+        set_error("session: write failed");
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    for (int il = 0; il < NLAYER; il++) {
+        if (is_attn(il)) continue;
+        if ((rc = write_dev(f.f, s->conv[il], conv_bytes(), s->st))) return rc;
+        if ((rc = write_dev(f.f, s->ssm[il], ssm_bytes(), s->st))) return rc;
+    }
+    return QMA_CUDA_OK;
+}
+
+int save_kv(const qma_cuda_state *s, const char *path) {
+    File f(path, "wb");
+    if (!f.f) {
+        set_error("session: cannot write %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    for (int a = 0; a < NATTN; a++)
+        if ((rc = write_dev(f.f, s->kv[a], kv_layer_bytes(s->n_ctx), s->st))) return rc;
+    return QMA_CUDA_OK;
+}
+
+int save_salience(const qma_cuda_state *s, const char *path) {
+    File f(path, "wb");
+    if (!f.f) {
+        set_error("session: cannot write %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    const uint32_t nc = uint32_t(s->n_ctx);
+    if (fwrite(&nc, 4, 1, f.f) != 1) {
+        set_error("session: write failed");
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    if ((rc = write_dev(f.f, s->sal, sizeof(float) * size_t(NATTN) * s->n_ctx, s->st))) return rc;
+    if (fwrite(s->pin_pos.data(), sizeof(int32_t), HCM_H_PIN, f.f) != size_t(HCM_H_PIN)) {
+        set_error("session: write failed");
+        return QMA_CUDA_ERR_INVALID;
+    }
+    if ((rc = write_dev(f.f, s->pin_sal, sizeof(float) * size_t(NATTN) * HCM_H_PIN, s->st))) return rc;
+    for (int a = 0; a < NATTN; a++)
+        if ((rc = write_dev(f.f, s->arena[a], arena_layer_bytes(), s->st))) return rc;
+    return QMA_CUDA_OK;
+}
+
+int load_state(qma_cuda_state *s, const char *path) {
+    File f(path, "rb");
+    if (!f.f) {
+        set_error("session: cannot read %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int32_t np = 0;
+    if (fread(&np, 4, 1, f.f) != 1 || np < 0) {
+        set_error("session: %s: no position count", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    bool short_read = false;
+    for (int il = 0; il < NLAYER && !short_read; il++) {
+        if (is_attn(il)) continue;
+        if ((rc = read_dev(f.f, s->conv[il], conv_bytes(), s->st, &short_read))) return rc;
+        if (!short_read && (rc = read_dev(f.f, s->ssm[il], ssm_bytes(), s->st, &short_read))) return rc;
+    }
+    if (short_read) {
+        set_error("session: %s is shorter than the recurrent state", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    s->n_pos = np;
+    return QMA_CUDA_OK;
+}
+
+int load_kv(qma_cuda_state *s, const char *path) {
+    File f(path, "rb");
+    if (!f.f) {
+        set_error("session: cannot read %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    fseek(f.f, 0, SEEK_END);
+    const long size = ftell(f.f);
+    fseek(f.f, 0, SEEK_SET);
+    if (size < 0 || size_t(size) != NATTN * kv_layer_bytes(s->n_ctx)) {
+        set_error("session: %s holds %ld bytes, a KV slab of n_ctx %d holds %zu", path, size, s->n_ctx,
+                  NATTN * kv_layer_bytes(s->n_ctx));
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    bool short_read = false;
+    for (int a = 0; a < NATTN && !short_read; a++)
+        if ((rc = read_dev(f.f, s->kv[a], kv_layer_bytes(s->n_ctx), s->st, &short_read))) return rc;
+    if (short_read) {
+        set_error("session: %s: read failed", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    return QMA_CUDA_OK;
+}
+
+// hcm_load (nn.c:1173-1209): salience required; the arena sections are
+// optional (older files end after the salience: no pinned entries)
+int load_salience(qma_cuda_state *s, const char *path) {
+    File f(path, "rb");
+    if (!f.f) {
+        set_error("session: cannot read %s", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    uint32_t nc = 0;
+    if (fread(&nc, 4, 1, f.f) != 1 || int(nc) != s->n_ctx) {
+        set_error("session: %s was saved for another n_ctx", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    int rc;
+    bool short_read = false;
+    if ((rc = read_dev(f.f, s->sal, sizeof(float) * size_t(NATTN) * s->n_ctx, s->st, &short_read))) return rc;
+    if (short_read) {
+        set_error("session: %s: salience cut short", path);
+        return QMA_CUDA_ERR_INVALID;
+    }
+    std::vector<int32_t> pos(HCM_H_PIN);
+    const bool have_pos = fread(pos.data(), sizeof(int32_t), HCM_H_PIN, f.f) == size_t(HCM_H_PIN);
+    if (have_pos) {
+        std::vector<float> psal(size_t(NATTN) * HCM_H_PIN);
+        std::vector<uint8_t> rec(arena_layer_bytes());
+        bool ok = fread(psal.data(), sizeof(float), psal.size(), f.f) == psal.size();
+        if (ok) {
+            QMA_CHECK_CUDA(cudaMemcpyAsync(s->pin_sal, psal.data(), psal.size() * sizeof(float),
+                                           cudaMemcpyHostToDevice, s->st));
+            for (int a = 0; a < NATTN && ok; a++) {
+                ok = fread(rec.data(), 1, rec.size(), f.f) == rec.size();
+                if (ok) {
+                    QMA_CHECK_CUDA(cudaMemcpyAsync(s->arena[a], rec.data(), rec.size(), cudaMemcpyHostToDevice,
+                                                   s->st));
+                    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+                }
+            }
+        }
+        // a cut-short arena section leaves no pinned entries (nn.c:1193-1203)
+        s->pin_pos = ok ? pos : std::vector<int32_t>(HCM_H_PIN, -1);
+    } else {
+        s->pin_pos.assign(HCM_H_PIN, -1);
+    }
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+    return QMA_CUDA_OK;
+}
+
+// the heavy-hitter bookkeeping of a fresh process (hcm_init, nn.c:947-970)
+int reset_hcm(qma_cuda_state *s) {
+    s->live.assign(s->n_ctx, 0);
+    s->tier.assign(s->n_ctx, 0);
+    s->live_n = s->n4 = s->n_ring_q4 = 0;
+    s->rebuilt_at = 0;
+    s->next_rebuild = qma_cuda_state::HCM_REBUILD_INIT;
+    QMA_CHECK_CUDA(cudaMemsetAsync(s->qf, 0, sizeof(float) * size_t(s->n_ctx), s->st));
+    if (s->graph) {
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+    return QMA_CUDA_OK;
+}
+
+}  // namespace
+}  // namespace qma
+
+extern "C" {
+
+int qma_cuda_state_save(const qma_cuda_state *s, const char *state_path, const char *kv_path,
+                        const char *salience_path) {
+    using namespace qma;
+    clear_error();
+    QMA_REQUIRE(s, "qma_cuda_state_save: null state");
+    QMA_CHECK_CUDA(cudaSetDevice(s->m->device));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->side));
+    int rc;
+    if (state_path && (rc = save_state(s, state_path))) return rc;
+    if (kv_path && (rc = save_kv(s, kv_path))) return rc;
+    if (salience_path && (rc = save_salience(s, salience_path))) return rc;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_state_load(qma_cuda_state *s, const char *state_path, const char *kv_path,
+                        const char *salience_path) {
+    using namespace qma;
+    clear_error();
+    QMA_REQUIRE(s, "qma_cuda_state_load: null state");
+    QMA_CHECK_CUDA(cudaSetDevice(s->m->device));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(s->side));
+    int rc;
+    if (state_path && (rc = load_state(s, state_path))) return rc;
+    if (kv_path && (rc = load_kv(s, kv_path))) return rc;
+    if ((rc = reset_hcm(s))) return rc;
+    if (salience_path && (rc = load_salience(s, salience_path))) return rc;
+    return QMA_CUDA_OK;
 }
 
 }  // extern "C"

@@ -68,6 +68,8 @@ _SIGS.update({
     "qma_cuda_state_kv_slot": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "qma_cuda_state_stats": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_u64)]),
     "qma_cuda_state_logits": (_vp, [_vp]),
+    "qma_cuda_state_save": (_i32, [_vp, C.c_char_p, C.c_char_p, C.c_char_p]),
+    "qma_cuda_state_load": (_i32, [_vp, C.c_char_p, C.c_char_p, C.c_char_p]),
     "qma_cuda_sample_candidates": (_i32, [_vp, _i32, _vp, _i32, _f32, _f32, _i32, _i32, _vp, _vp,
                                           C.POINTER(_i32), _vp]),
 })
@@ -131,6 +133,14 @@ class State:
         out = np.zeros((len(toks), 2048), np.float32)
         call("qma_cuda_eval_hidden", self.model.h, self.h, ptr(toks), len(toks), n_layers, ptr(out))
         return out
+
+    def save(self, state_path=None, kv_path=None, salience_path=None):
+        enc = lambda p: None if p is None else str(p).encode()
+        call("qma_cuda_state_save", self.h, enc(state_path), enc(kv_path), enc(salience_path))
+
+    def load(self, state_path=None, kv_path=None, salience_path=None):
+        enc = lambda p: None if p is None else str(p).encode()
+        call("qma_cuda_state_load", self.h, enc(state_path), enc(kv_path), enc(salience_path))
 
     def decode_greedy(self, token: int, n_steps: int):
         import numpy as np

@@ -365,6 +365,67 @@ def test_state_logits_feed_the_gpu_sampler(full, ref_lib):
         b.close()
 
 
+def test_session_files_round_trip_and_resume(full, ref_lib, tmp_path):
+    """qma_cuda_state_save writes the reference's session files (state as
+    runstate_save, the KV slab file, salience as hcm_save): the reference's
+    own runstate_load reads the state file back (position and recurrent
+    state bytes), the KV file holds the engine's records at the reference's
+    offsets, a state loaded from the files saves them again byte for byte,
+    and the resumed state continues the sequence: its first token's logits
+    match the original state's within the fp32 tolerance (a resumed process
+    rebuilds the live index at once, so its attention sums the same
+    positions in another order) and two resumed states agree exactly."""
+    n_ctx = 512
+    rng = np.random.default_rng(29)
+    prompt = rng.integers(0, O.N_VOCAB, 300).astype(np.int32)
+    a = Q.State(full["model"], n_ctx)
+    b, c = Q.State(full["model"], n_ctx), Q.State(full["model"], n_ctx)
+    f1 = [tmp_path / n for n in ("state.bin", "kv.bin", "salience.bin")]
+    f2 = [tmp_path / n for n in ("state2.bin", "kv2.bin", "salience2.bin")]
+    try:
+        la = a.eval(prompt)
+        tok = int(np.argmax(la))
+        for _ in range(3):
+            tok = int(np.argmax(a.eval(np.array([tok], np.int32))))
+        a.save(*f1)
+        gdn = 30
+        assert f1[0].stat().st_size == 4 + gdn * 4 * (8192 * 3 + 32 * 128 * 128)
+        assert f1[1].stat().st_size == 10 * 4 * n_ctx * 240
+        assert f1[2].stat().st_size == 4 + 4 * (10 * n_ctx + 2048 + 10 * 2048) + 10 * 4 * 2048 * 240
+        rs = ref_lib.qr_state_new(n_ctx)
+        try:
+            assert ref_lib.qr_runstate_load(rs, str(f1[0]).encode()) == 0
+            assert ref_lib.qr_state_n_pos(rs) == a.n_pos == 303
+            raw = np.fromfile(f1[0], np.uint8)
+            conv0 = np.ctypeslib.as_array(ref_lib.qr_state_conv(rs, 0), (8192 * 3,))
+            ssm0 = np.ctypeslib.as_array(ref_lib.qr_state_ssm(rs, 0), (32 * 128 * 128,))
+            assert np.array_equal(conv0.view(np.uint8), raw[4:4 + 8192 * 3 * 4])
+            assert np.array_equal(ssm0.view(np.uint8), raw[4 + 8192 * 3 * 4:4 + 4 * (8192 * 3 + 32 * 128 * 128)])
+        finally:
+            ref_lib.qr_state_free(rs)
+        kvf = np.fromfile(f1[1], np.uint8).reshape(10, 4, n_ctx, 240)
+        for lay, head, slot in [(0, 0, 0), (3, 2, 17), (9, 3, 302)]:
+            rec = np.zeros(240, np.uint8)
+            Q.call("qma_cuda_state_kv_slot", a.h, lay, head, slot, Q.ptr(rec))
+            assert np.array_equal(kvf[lay, head, slot], rec)
+        sal = np.fromfile(f1[2], np.uint8)
+        assert int(sal[:4].view(np.uint32)[0]) == n_ctx
+        b.load(*f1)
+        c.load(*f1)
+        assert b.n_pos == 303
+        b.save(*f2)
+        for x, y in zip(f1, f2):
+            assert x.read_bytes() == y.read_bytes(), x.name
+        t = np.array([tok], np.int32)
+        la, lb, lc = a.eval(t), b.eval(t), c.eval(t)
+        assert np.array_equal(lb, lc)
+        assert norm_rel(lb, la) < RTOL_LAYER and int(np.argmax(lb)) == int(np.argmax(la))
+    finally:
+        a.close()
+        b.close()
+        c.close()
+
+
 def test_model_synth_matches_model_load(full):
     m2 = Q.Model(full["tp"], full["n"], seed=SEED)
     try:
