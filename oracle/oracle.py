@@ -94,6 +94,9 @@ def lib() -> C.CDLL:
         L.qo_eval_hidden.restype = i32
         L.qo_layer_forward.argtypes = [vp, vp, i32, vp, i32, i32, vp]
         L.qo_mixer_forward.argtypes = [vp, vp, i32, vp, i32, vp]
+        L.qo_state_resume.argtypes = [vp, C.c_char_p, C.c_char_p, i32]
+        L.qo_state_resume.restype = i32
+        L.qo_state_live_segments.argtypes = [vp, vp, vp, vp]
         L.qo_state_kv_slot.argtypes = [vp, i32, i32, i32]
         L.qo_state_kv_slot.restype = C.POINTER(C.c_uint8)
         L.qo_gdn_layer.argtypes = [vp, vp, i32, vp, i32, vp]

@@ -181,6 +181,11 @@ typedef struct qo_state qo_state;
 qo_state *qo_state_new(int n_ctx);
 void      qo_state_free(qo_state *s);
 int       qo_state_n_pos(const qo_state *s);
+/* a qma session resumed in a fresh process from the KV slab and salience
+ * files (hcm_load semantics, nn.c:1173-1209); 0 or -1 */
+int       qo_state_resume(qo_state *s, const char *kv_path, const char *sal_path, int n_pos);
+/* live index segments after the last rebuild: ring q4, + arena q4, + ring q2 */
+void      qo_state_live_segments(const qo_state *s, int *n_ring_q4, int *n4, int *live_n);
 /* 240-byte KV slot of attention layer lay, head (0,1 K; 2,3 V), ring slot */
 const uint8_t *qo_state_kv_slot(const qo_state *s, int lay, int head, int slot);
 /* qma_eval (nn.c:2056-2308), single-threaded, q8k path, quantized KV + HCM.

@@ -387,6 +387,56 @@ void qo_state_free(qo_state *s)
 }
 
 int qo_state_n_pos(const qo_state *s) { return s->n_pos; }
+
+/* A qma session resumed in a fresh process (agent.c:765-816): the KV slab
+ * file (runstate_init_kv's layout, nn.c:1878-1935) and the salience file
+ * read as hcm_load reads it (nn.c:1173-1209) into hcm_init's fresh
+ * bookkeeping (nn.c:947-970: tiers, live index and quantisation scores
+ * cleared, next rebuild at 128), the position count as runstate_load sets
+ * it.  The recurrent state is not read (callers drive single layers).
+ * Returns 0, or -1 when a file is missing, short or for another n_ctx. */
+int qo_state_resume(qo_state *s, const char *kv_path, const char *sal_path, int n_pos)
+{
+    const size_t per = (size_t)2 * QO_HEAD_KV * s->n_ctx * QO_KVQ_SLOT;
+    FILE *f = fopen(kv_path, "rb");
+    if (!f) return -1;
+    for (int l = 0; l < QO_ATTN_LAYERS; l++)
+        if (fread(s->kv[l], 1, per, f) != per) { fclose(f); return -1; }
+    fclose(f);
+    memset(s->tier, 0, (size_t)s->n_ctx);
+    memset(s->qf, 0, sizeof(float) * (size_t)s->n_ctx);
+    memset(s->live, 0, sizeof(int) * (size_t)s->n_ctx);
+    s->live_n = s->n4 = s->n_ring_q4 = s->rebuilt_at = 0;
+    s->next_rebuild = QO_HCM_REBUILD;
+    memset(s->pin_pos, -1, sizeof(s->pin_pos));
+    memset(s->pin_sal, 0, sizeof(s->pin_sal));
+    s->pin_n = 0;
+    f = fopen(sal_path, "rb");
+    if (!f) return -1;
+    uint32_t nc = 0;
+    if (fread(&nc, 4, 1, f) != 1 || (int)nc != s->n_ctx) { fclose(f); return -1; }
+    for (int l = 0; l < QO_ATTN_LAYERS; l++)
+        if (fread(s->sal[l], sizeof(float), (size_t)s->n_ctx, f) != (size_t)s->n_ctx) { fclose(f); return -1; }
+    s->n_pos = n_pos;
+    int ok = fread(s->pin_pos, sizeof(int32_t), QO_HCM_H_PIN, f) == (size_t)QO_HCM_H_PIN;
+    for (int l = 0; l < QO_ATTN_LAYERS && ok; l++)
+        ok = fread(s->pin_sal[l], sizeof(float), QO_HCM_H_PIN, f) == (size_t)QO_HCM_H_PIN;
+    for (int l = 0; l < QO_ATTN_LAYERS && ok; l++)
+        ok = fread(s->pin_kv[l], (size_t)2 * QO_HEAD_KV * QO_HCM_H_PIN, QO_KVQ_SLOT, f) == (size_t)QO_KVQ_SLOT;
+    fclose(f);
+    if (!ok) { memset(s->pin_pos, -1, sizeof(s->pin_pos)); return 0; }   /* optional arena */
+    for (int a = 0; a < QO_HCM_H_PIN; a++) s->pin_n += s->pin_pos[a] >= 0;
+    return 0;
+}
+
+/* The live index's segments after the last rebuild: [0, n_ring_q4) ring q4,
+ * [n_ring_q4, n4) arena q4, [n4, live_n) ring q2 (parity aid). */
+void qo_state_live_segments(const qo_state *s, int *n_ring_q4, int *n4, int *live_n)
+{
+    *n_ring_q4 = s->n_ring_q4;
+    *n4 = s->n4;
+    *live_n = s->live_n;
+}
 const uint8_t *qo_state_kv_slot(const qo_state *s, int lay, int head, int slot)
 {
     return s->kv[lay] + ((size_t)head * s->n_ctx + slot) * QO_KVQ_SLOT;

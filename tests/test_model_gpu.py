@@ -426,6 +426,60 @@ def test_session_files_round_trip_and_resume(full, ref_lib, tmp_path):
         c.close()
 
 
+def test_resumed_session_reads_the_q2_gist_teacher_forced(full, tmp_path):
+    """A session resumed past the hot window: the engine saves the state of
+    a 4700-token prompt (layers 0-2 and layer 3's mixer), two fresh states
+    load the files, and the first resumed token rebuilds the live index
+    with the tiers cleared, as a fresh qma process does -- the positions
+    older than the hot window are pinned into the arena and also listed in
+    the q2 gist segment, so the decode kernel reads q2 records.  The
+    oracle resumes from the same files (qo_state_resume: hcm_load into
+    hcm_init's fresh bookkeeping) and runs layer 3's mixer on the engine's
+    layer-3 inputs; the attention's residual contribution must agree
+    within the fp32 tolerance."""
+    L = O.lib()
+    n_ctx = 8192
+    rng = np.random.default_rng(37)
+    prompt = rng.integers(0, O.N_VOCAB, 4700).astype(np.int32)
+    dec = rng.integers(0, O.N_VOCAB, 6).astype(np.int32)
+    files = [tmp_path / n for n in ("state.bin", "kv.bin", "salience.bin")]
+    a = Q.State(full["model"], n_ctx)
+    try:
+        a.eval_hidden(prompt, -4)
+        a.save(*files)
+    finally:
+        a.close()
+    b, c = Q.State(full["model"], n_ctx), Q.State(full["model"], n_ctx)
+    try:
+        b.load(*files)
+        c.load(*files)
+        xin = [b.eval_hidden(dec[i:i + 1], 3) for i in range(len(dec))]
+        got = [c.eval_hidden(dec[i:i + 1], -4) for i in range(len(dec))]
+    finally:
+        b.close()
+        c.close()
+    os_ = L.qo_state_new(n_ctx)
+    want = []
+    try:
+        assert L.qo_state_resume(os_, str(files[1]).encode(), str(files[2]).encode(), len(prompt)) == 0
+        for x in xin:
+            out = np.zeros_like(x)
+            L.qo_mixer_forward(full["om"], os_, 3, O._ptr(np.ascontiguousarray(x)), 1, O._ptr(out))
+            want.append(out)
+        seg = [C.c_int(), C.c_int(), C.c_int()]
+        L.qo_state_live_segments(os_, *[C.byref(v) for v in seg])
+        n_ring_q4, n4, live_n = (v.value for v in seg)
+    finally:
+        L.qo_state_free(os_)
+    assert n4 > n_ring_q4 and live_n > n4, (n_ring_q4, n4, live_n)    # arena and q2 gist in use
+    x_all, g_all, w_all = (np.concatenate(v) for v in (xin, got, want))
+    dg, dw = g_all - x_all, w_all - x_all
+    e_tok = norm_rel(dg, dw, axis=1)
+    print("resumed attention delta norm-rel: all %.2e, worst %.2e; live segments %d / %d / %d"
+          % (norm_rel(dg, dw), e_tok.max(), n_ring_q4, n4, live_n))
+    assert norm_rel(dg, dw) <= RTOL_LAYER and e_tok.max() <= 10 * RTOL_TOKEN
+
+
 def test_model_synth_matches_model_load(full):
     m2 = Q.Model(full["tp"], full["n"], seed=SEED)
     try:
