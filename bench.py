@@ -158,8 +158,8 @@ def dist_barrier(world):
 
 # --------------------------------------------------------------- decode ----
 def model_layout(lm_type):
-    import oracle as O
-    return O.synth_layout(embd_type=lm_type, out_type=lm_type, down_type=Q6_K, proj_type=Q4_K)
+    import qma_cuda as Q
+    return Q.synth_layout(embd_type=lm_type, out_type=lm_type, down_type=Q6_K, proj_type=Q4_K)
 
 
 def decode_bytes_per_token(arr, n, live_positions):
@@ -167,13 +167,13 @@ def decode_bytes_per_token(arr, n, live_positions):
     (projections, norms, router, LM head), one token_embd row, 8 routed + 1
     shared expert per layer, GDN/conv state read+write, and the KV records the
     attention reads (q4 records of K and V for both KV heads)."""
-    import oracle as O
+    import qma_cuda as Q
     total = 0
     for i in range(n):
         t = arr[i]
         name = t.name.decode()
         if name == "token_embd.weight":
-            total += O.row_bytes(int(t.type), int(t.ne[0]))
+            total += Q.row_bytes(int(t.type), int(t.ne[0]))
         elif "_exps." in name:
             total += t.nbytes // int(t.ne[2]) * 8
         else:
@@ -347,8 +347,10 @@ def run_decode_ours(args, world, rank, local):
 def host_blob_for_reference(threads):
     """The same random-init model for the reference, with Q6_K embeddings and
     LM head (the reference has no Q8_0 weight kernels, gguf.c:272-287)."""
+    import ctypes as C
     import oracle as O
-    arr, n, size = model_layout(Q6_K)
+    qarr, n, size = model_layout(Q6_K)
+    arr = C.cast(qarr, C.POINTER(O.Tensor))         # the same struct, the oracle's ctypes class
     blob = O.synth_blob(arr, n, size, seed=SEED, threads=threads)
     return arr, n, size, blob
 
@@ -434,14 +436,15 @@ def gemv_bytes(rows=GN_OUT, cols=GN_IN):
 
 def run_gemv_ours(args, world, rank, local):
     import torch
-    import oracle as O
     import qma_cuda as Q
     Q.init(local)
     GN_OUT, GN_IN = args.rows, args.cols
     dev = torch.device("cuda", local)
-    W = O.synth_matrix("bench.lm_head", Q4_K, GN_OUT, GN_IN, seed=0)
+    # the weights from the engine's synthetic generator, on the device
+    dW = torch.empty(GN_OUT * Q.row_bytes(Q4_K, GN_IN), dtype=torch.uint8, device=dev)
+    Q.call("qma_cuda_synth_tensor", b"bench.lm_head", Q4_K, GN_OUT * GN_IN, 0, Q.ptr(dW), None)
     x = np.random.default_rng(rank).standard_normal((1, GN_IN)).astype(np.float32)
-    dW, dx = torch.from_numpy(W).to(dev), torch.from_numpy(x).to(dev)
+    dx = torch.from_numpy(x).to(dev)
     dq = torch.empty((1, GN_IN), dtype=torch.int8, device=dev)
     dd = torch.empty((1, GN_IN // 256), dtype=torch.float32, device=dev)
     ds = torch.empty((1, GN_IN // 16), dtype=torch.int16, device=dev)
@@ -522,12 +525,11 @@ def run_moe_ours(args, world, rank, local):
     a 256 MB L2 flush between timed calls."""
     import ctypes as C
     import torch
-    import oracle as O
     import qma_cuda as Q
     Q.init(local)
     dev = torch.device("cuda", local)
     arr, n, size = model_layout(Q8_0)
-    idx = O.tensor_index(arr, n)
+    idx = Q.tensor_index(arr, n)
     d = {}
     for name in MOE_TENSORS:
         t = arr[idx[f"blk.0.{name}"]]
@@ -536,7 +538,7 @@ def run_moe_ours(args, world, rank, local):
         Q.call("qma_cuda_synth_tensor", t.name, int(t.type), nel, SEED, Q.ptr(raw), None)
         if "down" in name and int(t.type) != Q4_K:
             rows, n_in, nexp = int(t.ne[1]), int(t.ne[0]), int(t.ne[2])
-            pb, gb = Q.packed_bytes(int(t.type), rows, n_in), O.row_bytes(int(t.type), n_in) * rows
+            pb, gb = Q.packed_bytes(int(t.type), rows, n_in), Q.row_bytes(int(t.type), n_in) * rows
             packed = torch.empty(pb * nexp, dtype=torch.uint8, device=dev)
             for e in range(nexp):
                 Q.call("qma_cuda_repack", int(t.type), raw.data_ptr() + e * gb, rows, n_in,

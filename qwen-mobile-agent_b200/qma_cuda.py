@@ -75,6 +75,77 @@ _SIGS.update({
 })
 
 
+# ----------------------------------------------------- synthetic model table --
+# The qwen35moe tensor table (the reference's tensor names, gguf.c:302-345,
+# with the shapes of the hyper-parameters in qma.h:28-64) over one data
+# section, each tensor 256-byte aligned: what a random-init model is
+# generated into (qma_cuda_model_synth) or loaded from.
+_BLOCK = {F32: (4, 1), Q8_0: (34, 32), Q4_K: (144, 256), Q6_K: (210, 256)}
+
+
+def row_bytes(wtype: int, n: int) -> int:
+    """GGUF bytes of one row of n elements of type wtype."""
+    bs, blk = _BLOCK[wtype]
+    return n // blk * bs
+
+
+def synth_layout(n_vocab=151936, embd_type=Q8_0, out_type=Q8_0, down_type=Q6_K, proj_type=Q4_K):
+    """(Tensor array, count, data-section bytes) of the 40-layer qwen35moe."""
+    E, FF, NE = 2048, 512, 256
+    t = []
+
+    def add(name, typ, ne0, ne1=1, ne2=1):
+        t.append((name, typ, (ne0, ne1, ne2)))
+
+    add("token_embd.weight", embd_type, E, n_vocab)
+    add("output_norm.weight", F32, E)
+    add("output.weight", out_type, E, n_vocab)
+    for il in range(40):
+        b = f"blk.{il}."
+        add(b + "attn_norm.weight", F32, E)
+        add(b + "post_attention_norm.weight", F32, E)
+        if (il + 1) % 4 == 0:                       # gated full attention
+            add(b + "attn_q.weight", proj_type, E, 8192)
+            add(b + "attn_k.weight", proj_type, E, 512)
+            add(b + "attn_v.weight", proj_type, E, 512)
+            add(b + "attn_output.weight", proj_type, 4096, E)
+            add(b + "attn_q_norm.weight", F32, 256)
+            add(b + "attn_k_norm.weight", F32, 256)
+        else:                                       # gated delta net
+            add(b + "attn_qkv.weight", proj_type, E, 8192)
+            add(b + "attn_gate.weight", proj_type, E, 4096)
+            add(b + "ssm_conv1d.weight", F32, 4, 8192)
+            add(b + "ssm_dt.bias", F32, 32)
+            add(b + "ssm_a", F32, 32)
+            add(b + "ssm_beta.weight", proj_type, E, 32)
+            add(b + "ssm_alpha.weight", proj_type, E, 32)
+            add(b + "ssm_norm.weight", F32, 128)
+            add(b + "ssm_out.weight", proj_type, 4096, E)
+        add(b + "ffn_gate_inp.weight", F32, E, NE)
+        add(b + "ffn_gate_exps.weight", Q4_K, E, FF, NE)
+        add(b + "ffn_up_exps.weight", Q4_K, E, FF, NE)
+        add(b + "ffn_down_exps.weight", down_type, FF, E, NE)
+        add(b + "ffn_gate_inp_shexp.weight", F32, E)
+        add(b + "ffn_gate_shexp.weight", Q4_K, E, FF)
+        add(b + "ffn_up_shexp.weight", Q4_K, E, FF)
+        add(b + "ffn_down_shexp.weight", down_type, FF, E)
+    arr = (Tensor * len(t))()
+    off = 0
+    for i, (name, typ, ne) in enumerate(t):
+        arr[i].name = name.encode()
+        arr[i].type = typ
+        for d in range(3):
+            arr[i].ne[d] = ne[d]
+        arr[i].off = off
+        arr[i].nbytes = row_bytes(typ, ne[0]) * ne[1] * ne[2]
+        off += (arr[i].nbytes + 255) // 256 * 256
+    return arr, len(t), off
+
+
+def tensor_index(arr, n) -> dict:
+    return {arr[i].name.decode(): i for i in range(n)}
+
+
 def gguf_scan(path: str):
     """qma_cuda_gguf_scan: (tensor table, count, data section offset in the
     file, tokenizer token count)."""

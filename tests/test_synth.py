@@ -28,3 +28,18 @@ def test_distributions():
     assert abs(n.mean() - 1.0) < 0.01
     a = O.synth_matrix("blk.0.ssm_a", O.F32, 1, 32).view(np.float32)
     assert (a < 0).all()
+
+
+def test_engine_tensor_table_matches_the_oracles():
+    """qma_cuda.synth_layout (the table bench.py and the engine's users
+    build the random-init model from) equals the oracle's qo_synth_layout:
+    names, types, shapes, offsets and sizes."""
+    import qma_cuda as Q
+    for cfg in [dict(embd_type=O.Q6_K, out_type=O.Q6_K), dict(), dict(down_type=O.Q4_K, proj_type=O.Q6_K),
+                dict(n_vocab=1000)]:
+        a, n, size = Q.synth_layout(**cfg)
+        b, m, size2 = O.synth_layout(**cfg)
+        assert (n, size) == (m, size2)
+        for i in range(n):
+            assert (a[i].name, a[i].type, tuple(a[i].ne), a[i].off, a[i].nbytes) == \
+                (b[i].name, b[i].type, tuple(b[i].ne), b[i].off, b[i].nbytes), i
