@@ -68,6 +68,40 @@ __device__ __forceinline__ int group_size(int e, int T, const int *goff) {
     return e < NSHARED ? goff[e + 1] - goff[e] : T;
 }
 
+// One lane's share of super-block sb of two Q4_K rows (rows gid and gid + 8
+// of a warp's 16): each row's 16-byte header and the quant words
+// 16 + 32 g + 4 tig and 32 + 32 g + 4 tig (g = 0..3), the A fragments of
+// the 8 sub-blocks.
+struct Q4Words {
+    uint4 h0, h1;
+    uint32_t q0[8], q1[8];
+    __device__ __forceinline__ void load(const uint8_t *w0, const uint8_t *w1, int sb, int tig) {
+        const uint8_t *b0 = w0 + size_t(sb) * Q4K_BYTES, *b1 = w1 + size_t(sb) * Q4K_BYTES;
+        h0 = __ldg(reinterpret_cast<const uint4 *>(b0));
+        h1 = __ldg(reinterpret_cast<const uint4 *>(b1));
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            q0[2 * g] = __ldg(reinterpret_cast<const uint32_t *>(b0 + 16 + 32 * g + 4 * tig));
+            q0[2 * g + 1] = __ldg(reinterpret_cast<const uint32_t *>(b0 + 32 + 32 * g + 4 * tig));
+            q1[2 * g] = __ldg(reinterpret_cast<const uint32_t *>(b1 + 16 + 32 * g + 4 * tig));
+            q1[2 * g + 1] = __ldg(reinterpret_cast<const uint32_t *>(b1 + 32 + 32 * g + 4 * tig));
+        }
+    }
+};
+
+// q4k_scales8 on the header's scale words (bytes 4..15 of the block)
+__device__ __forceinline__ void q4k_scales8_words(uint32_t w0, uint32_t w1, uint32_t w2, int (&sc)[8],
+                                                  int (&mn)[8]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t a = (w0 >> (8 * j)) & 0xffu, b = (w1 >> (8 * j)) & 0xffu, c = (w2 >> (8 * j)) & 0xffu;
+        sc[j] = int(a & 63u);
+        mn[j] = int(b & 63u);
+        sc[j + 4] = int((c & 15u) | ((a >> 6) << 4));
+        mn[j + 4] = int((c >> 4) | ((b >> 6) << 4));
+    }
+}
+
 // 2. ---------------------------------------------------------- gate / up --
 // Grid (1024 / GR rows of [gate | up], 257 groups, ceil(T / GT) tiles); warp
 // w: 16 rows, 4 column tiles of 8 pairs.  Output hg[pair][1024].
@@ -109,16 +143,22 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
     for (int n = 0; n < 4; n++)
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    // the two rows' words of super-block sb: the 16-byte header (d, dmin,
+    // 12 scale bytes) and this lane's 8 quant words; the next super-block's
+    // are loaded before this one's activation tile is staged, so their HBM
+    // latency overlaps the staging and the MMAs
+    Q4Words cur, nxt;
+    cur.load(w0, w1, 0, tig);
     for (int sb = 0; sb < MOE_EMBD / 256; sb++) {
+        if (sb + 1 < MOE_EMBD / 256) nxt.load(w0, w1, sb + 1, tig);
         __syncthreads();                                 // the previous tile is consumed
         stage_btile(bt, brow, s.xq, MOE_EMBD, sb * 256);
         __syncthreads();
-        const uint8_t *h0 = w0 + size_t(sb) * Q4K_BYTES, *h1 = w1 + size_t(sb) * Q4K_BYTES;
         int sc0[8], mn0[8], sc1[8], mn1[8];
-        q4k_scales8(h0, sc0, mn0);
-        q4k_scales8(h1, sc1, mn1);
-        const float d0 = h2f(*reinterpret_cast<const uint16_t *>(h0)), dm0 = h2f(*reinterpret_cast<const uint16_t *>(h0 + 2));
-        const float d1 = h2f(*reinterpret_cast<const uint16_t *>(h1)), dm1 = h2f(*reinterpret_cast<const uint16_t *>(h1 + 2));
+        q4k_scales8_words(cur.h0.y, cur.h0.z, cur.h0.w, sc0, mn0);
+        q4k_scales8_words(cur.h1.y, cur.h1.z, cur.h1.w, sc1, mn1);
+        const float d0 = h2f(uint16_t(cur.h0.x & 0xffffu)), dm0 = h2f(uint16_t(cur.h0.x >> 16));
+        const float d1 = h2f(uint16_t(cur.h1.x & 0xffffu)), dm1 = h2f(uint16_t(cur.h1.x >> 16));
         int I1[4][4];
 #pragma unroll
         for (int n = 0; n < 4; n++)
@@ -126,10 +166,8 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
             for (int i = 0; i < 4; i++) I1[n][i] = 0;
 #pragma unroll
         for (int g = 0; g < 4; g++) {
-            const uint32_t r0a = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 4 * tig);
-            const uint32_t r0b = *reinterpret_cast<const uint32_t *>(h0 + 16 + 32 * g + 16 + 4 * tig);
-            const uint32_t r1a = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 4 * tig);
-            const uint32_t r1b = *reinterpret_cast<const uint32_t *>(h1 + 16 + 32 * g + 16 + 4 * tig);
+            const uint32_t r0a = cur.q0[2 * g], r0b = cur.q0[2 * g + 1];
+            const uint32_t r1a = cur.q1[2 * g], r1b = cur.q1[2 * g + 1];
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 const int j = 2 * g + half, sh = 4 * half;
@@ -167,6 +205,7 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                 acc[n][c] += x * (d0 * float(I1[n][c]) - dm0 * float(I2a));
                 acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
             }
+        cur = nxt;
     }
 #pragma unroll
     for (int n = 0; n < 4; n++)
