@@ -148,6 +148,14 @@ int qma_cuda_model_load_gguf(int device, const char *path, qma_cuda_model **out)
  * (qma_cuda_synth_tensor per tensor): no host copy of the weights. */
 int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n,
                          uint64_t seed, qma_cuda_model **out);
+/* The table check qma_cuda_model_load and qma_cuda_model_synth run before
+ * allocating anything, on its own (host only, touches no device): every
+ * tensor the forward uses is present with the shape the kernels are written
+ * for (qma.h:28-64: e.g. ffn_gate_exps [2048][512][256], norm vectors of
+ * 2048 / 256 / 128) and a supported type, and, with data_size > 0, lies in
+ * a data section of data_size bytes.  The reference's qma_load checks the
+ * hyper-parameters only (gguf.c:226-234) and trusts the shapes. */
+int qma_cuda_model_check(const qma_cuda_tensor *tensors, uint32_t n, uint64_t data_size);
 int qma_cuda_model_free(qma_cuda_model *m);
 int qma_cuda_model_n_vocab(const qma_cuda_model *m);
 /* Replaces qma_ecache_get (ecache.h:95, ecache.c:414-498): the expert
@@ -290,8 +298,10 @@ int qma_cuda_moe_layer(const qma_cuda_moe_weights *w, const float *x2, int T,
  * until the process exits).  At most QMA_CUDA_MOE_NOALLOC_MAX_T tokens per
  * call; larger T is rejected with QMA_CUDA_ERR_INVALID.  The first call on
  * each device looks up that device's copy of the array (make it before any
- * stream capture on the device).  All calls share the array: calls that
- * overlap on the GPU race and must not be issued. */
+ * stream capture on the device); the address is kept for the life of the
+ * process, so after a cudaDeviceReset() of a device this entry point must
+ * not be called on that device again.  All calls share the array: calls
+ * that overlap on the GPU race and must not be issued. */
 #define QMA_CUDA_MOE_NOALLOC_MAX_T 4
 int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const float *x2, int T,
                                float *x_out, int32_t *sel, float *wts, void *stream);
@@ -313,7 +323,12 @@ int qma_cuda_moe_exact_fallbacks(const void *scratch, int T, int *count);
  * ids / lgs [k], the candidates' token ids and scaled logits, largest
  * first, and *n_out = k.  The scaled logits are bit-identical to the
  * reference's; candidates of equal value are ordered by token id (the
- * reference's qsort leaves that order unspecified).  Blocks until done.
+ * reference's qsort leaves that order unspecified).  When several tokens tie
+ * exactly at the k-th value, the engine keeps the lowest ids among them; the
+ * reference's min-heap (strict '>', sampler.c:74-85) keeps whichever tied
+ * tokens its insertion order leaves, so the candidate SET can differ from
+ * the reference's in that case only.  -0.0 and +0.0 rank as equal.  Blocks
+ * until done.
  * Calls share a fixed device result array: they must not overlap. */
 #define QMA_CUDA_SAMPLE_MAX_K 64
 int qma_cuda_sample_candidates(const float *logits, int n_vocab, const int32_t *last_tokens,
@@ -345,6 +360,16 @@ int qma_cuda_ep_unique_id(uint8_t *uid);
  * (1..256, t_max * n_ranks <= 512). */
 int qma_cuda_ep_init(int device, const uint8_t *uid, int rank, int n_ranks, int t_max,
                      qma_cuda_ep **out);
+/* qma_cuda_ep_init with a wall-clock limit (milliseconds) on every host-side
+ * wait of the handle: joining the communicator (a rank that never joins),
+ * and each qma_cuda_ep_moe_layer's exchange.  Past the limit the
+ * communicator is aborted (its peers' pending transfers fail rather than
+ * wait) and the call returns QMA_CUDA_ERR_TIMEOUT; an aborted handle only
+ * accepts qma_cuda_ep_free.  qma_cuda_ep_init takes the limit from
+ * QMA_CUDA_EP_TIMEOUT_MS in the environment, default 300000.  The reference
+ * has no counterpart (it runs on one host). */
+int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ranks, int t_max,
+                             int timeout_ms, qma_cuda_ep **out);
 int qma_cuda_ep_free(qma_cuda_ep *ep);
 
 /* Collective: every rank calls it for the same layer, each with its own

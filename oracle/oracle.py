@@ -83,6 +83,8 @@ def lib() -> C.CDLL:
         L.qo_moe_ffn.argtypes = [vp, i32, vp, i32, vp, vp, vp]
         L.qo_moe_block.argtypes = [vp, i32, vp, i32, vp, vp, vp]
         L.qo_router_logits.argtypes = [vp, vp, vp]
+        L.qo_route.argtypes = [vp, vp, vp, i32, vp, vp]
+        L.qo_moe_route.argtypes = [vp, vp, vp, vp, i32, vp, vp]
         L.qo_state_new.argtypes = [i32]
         L.qo_state_new.restype = vp
         L.qo_state_free.argtypes = [vp]
@@ -213,6 +215,22 @@ def matmul(x: np.ndarray, W: np.ndarray, wtype: int, n_in: int, n_out: int) -> n
     out = np.zeros((x.shape[0], n_out), np.float32)
     lib().qo_matmul(_ptr(x), _ptr(W), n_in, n_out, x.shape[0], wtype, _ptr(out))
     return out
+
+
+def moe_route(post_norm: np.ndarray, gate_inp: np.ndarray, x2: np.ndarray, bias=None):
+    """Routing of the FFN half of a layer (rms_norm_m * post_norm, then the
+    router of moe_ffn, nn.c:513-551) for tokens x2 [T][2048]: (sel int32
+    [T][8], w float32 [T][8]) in selection order.  bias (256 floats,
+    optional) is added to each logit (the configs[4] router prior)."""
+    x2 = np.ascontiguousarray(x2, dtype=np.float32).reshape(-1, 2048)
+    pn = np.ascontiguousarray(post_norm, dtype=np.float32)
+    gi = np.ascontiguousarray(gate_inp, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    T = x2.shape[0]
+    sel = np.zeros((T, 8), np.int32)
+    w = np.zeros((T, 8), np.float32)
+    lib().qo_moe_route(_ptr(pn), _ptr(gi), None if b is None else _ptr(b), _ptr(x2), T, _ptr(sel), _ptr(w))
+    return sel, w
 
 
 def dot_partials(W: np.ndarray, wtype: int, n_in: int, xq, xd, xs):

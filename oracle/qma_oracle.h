@@ -175,6 +175,13 @@ void qo_moe_block(const qo_model *m, int il, const float *x2, int T, float *out,
 /* router only: logits (256) of one token in the reference's sequential
  * fp32 order (nn.c:513-523) */
 void qo_router_logits(const float *gate_inp, const float *x, float *logits);
+/* routing of T normed tokens (nn.c:513-551): sel/wt [T][8] in selection
+ * order; bias (256, optional) is added to each fp32 logit before the
+ * softmax (the configs[4] router prior; the reference has none) */
+void qo_route(const float *gate_inp, const float *bias, const float *x, int T, int *sel, float *wt);
+/* the same from the residual input x2: rms_norm_m * post_norm first */
+void qo_moe_route(const float *post_norm, const float *gate_inp, const float *bias, const float *x2, int T,
+                  int *sel, float *wt);
 
 /* ---- sequence state + full forward ---------------------------------------- */
 typedef struct qo_state qo_state;

@@ -222,16 +222,19 @@ static void moe_tasks(void *arg, int i0, int i1)
     }
 }
 
-void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
-                int *sel_out, float *w_out)
+/* Router of moe_ffn (nn.c:513-551) for T normed tokens: the sequential fp32
+ * logits, then (the engine's configs[4] extension, absent in the reference)
+ * one fp32 addition of bias[e] per logit when bias is given, softmax (expf
+ * of l - max, divided by the sum), eight rounds of argmax with '>' (ties to
+ * the lower id) and the renormalised weights. */
+void qo_route(const float *gate_inp, const float *bias, const float *x, int T, int *sel, float *wt)
 {
-    const qo_layer *L = &m->L[il];
-    int *sel = malloc(sizeof(int) * (size_t)T * QO_EXPERT_USED);
-    float *wt = malloc(sizeof(float) * (size_t)T * QO_EXPERT_USED);
     for (int t = 0; t < T; t++) {
         const float *xp = x + (size_t)t * QO_EMBD;
         float logits[QO_EXPERT];
-        qo_router_logits(L->gate_inp, xp, logits);
+        qo_router_logits(gate_inp, xp, logits);
+        if (bias)
+            for (int e = 0; e < QO_EXPERT; e++) logits[e] = logits[e] + bias[e];
         float mx = -1e30f;
         for (int e = 0; e < QO_EXPERT; e++) if (logits[e] > mx) mx = logits[e];
         float sum = 0;
@@ -249,6 +252,26 @@ void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
         for (int k = 0; k < QO_EXPERT_USED; k++) ws += wt[t * 8 + k];
         for (int k = 0; k < QO_EXPERT_USED; k++) wt[t * 8 + k] /= ws;
     }
+}
+
+/* rms_norm_m (nn.c:348-357) with post_attention_norm, then qo_route: the
+ * routing of the FFN half of a layer from its residual input x2. */
+void qo_moe_route(const float *post_norm, const float *gate_inp, const float *bias, const float *x2, int T,
+                  int *sel, float *wt)
+{
+    float *xn = malloc(sizeof(float) * (size_t)T * QO_EMBD);
+    rms_norm_m(xn, x2, post_norm, QO_EMBD, T);
+    qo_route(gate_inp, bias, xn, T, sel, wt);
+    free(xn);
+}
+
+void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
+                int *sel_out, float *w_out)
+{
+    const qo_layer *L = &m->L[il];
+    int *sel = malloc(sizeof(int) * (size_t)T * QO_EXPERT_USED);
+    float *wt = malloc(sizeof(float) * (size_t)T * QO_EXPERT_USED);
+    qo_route(L->gate_inp, NULL, x, T, sel, wt);
     int8_t *xq = malloc((size_t)T * QO_EMBD);
     float *xd = malloc(sizeof(float) * (size_t)T * (QO_EMBD / QO_QK_K));
     int16_t *xs = malloc(sizeof(int16_t) * (size_t)T * (QO_EMBD / 16));

@@ -859,17 +859,13 @@ int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
     const int nchunk = (a.nk_max + a.pv_chunk - 1) / a.pv_chunk;
-    static bool attr = false;
-    if (!attr) {
+    static PerDevice attr;
+    if (!attr.done()) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(sizeof(ChunkSmem))));
-        attr = true;
-    }
-    static bool attr_dec = false;
-    if (!attr_dec) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(sizeof(DecSmem))));
-        attr_dec = true;
+        attr.mark();
     }
     // QMA_CUDA_ATTN_GENERAL=1: single tokens through the multi-query kernel
     // (a cross-check of the decode kernel; same results up to fp32 rounding)

@@ -6,6 +6,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "qma_cuda.h"
 
 namespace qma {
@@ -358,6 +360,27 @@ static inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, 
 
 // Programmatic dependent launch of the engine's kernels (on by default).
 bool pdl_enabled();
+
+// One-time set-up that CUDA keeps per device (kernel attributes such as the
+// dynamic shared-memory limit or non-portable cluster sizes): one bit per
+// device that has it.  A process that drives several GPUs sets it on each
+// device at that device's first call.  Devices past 63 redo it every call.
+struct PerDevice {
+    std::atomic<unsigned long long> mask{0};
+    static int current() {
+        int d = 0;
+        if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+        return d;
+    }
+    bool done() const {
+        const int d = current();
+        return d < 64 && ((mask.load(std::memory_order_acquire) >> d) & 1ull);
+    }
+    void mark() {
+        const int d = current();
+        if (d < 64) mask.fetch_or(1ull << d, std::memory_order_acq_rel);
+    }
+};
 
 // Byte ranges (weights) the first kernel of a layer asks L2 to fetch ahead
 // of the kernels that use them.

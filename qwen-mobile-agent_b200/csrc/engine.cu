@@ -138,10 +138,17 @@ struct Loader {
     bool synth;
     uint64_t seed;
     cudaStream_t st;
+    // dry: check names, shapes, types and data ranges only (host, no device
+    // memory or stream touched; the pointers handed out are placeholders)
+    bool dry = false;
     uint8_t *tmp = nullptr;
     size_t tmp_cap = 0;
 
     int dalloc(void **p, size_t bytes) {
+        if (dry) {
+            *p = reinterpret_cast<void *>(uintptr_t(256));
+            return QMA_CUDA_OK;
+        }
         QMA_CHECK_CUDA(cudaMalloc(p, bytes ? bytes : 16));
         m->allocs.push_back(*p);
         m->weight_bytes += bytes;
@@ -152,24 +159,38 @@ struct Loader {
         const uint64_t nel = uint64_t(x->ne[0]) * uint64_t(x->ne[1] ? x->ne[1] : 1) *
                              uint64_t(x->ne[2] ? x->ne[2] : 1);
         const size_t bytes = gguf_row_bytes(x->type, x->ne[0]) * (nel / uint64_t(x->ne[0]));
-        if (synth) return synth_tensor_gguf(x->name, int(x->type), nel, seed, dst, st);
-        if (x->off + bytes > host_size) {
+        if (synth) return dry ? QMA_CUDA_OK : synth_tensor_gguf(x->name, int(x->type), nel, seed, dst, st);
+        if (x->off > host_size || bytes > host_size - x->off) {
             set_error("model_load: tensor %s out of the data section", x->name);
             return QMA_CUDA_ERR_INVALID;
         }
+        if (dry) return QMA_CUDA_OK;
         QMA_CHECK_CUDA(cudaMemcpyAsync(dst, host + x->off, bytes, cudaMemcpyHostToDevice, st));
         return QMA_CUDA_OK;
     }
-    const qma_cuda_tensor *need(const char *name, int *rc) {
+    // The tensor `name` with the shape the kernels are written for: every
+    // device buffer is sized from ne[], so a shape the kernels do not expect
+    // (another expert count, a short norm vector) is refused here instead of
+    // letting a kernel read past an allocation.  ne[1] / ne[2] of 0 read as 1.
+    const qma_cuda_tensor *need(const char *name, int *rc, int64_t e0, int64_t e1, int64_t e2 = 1) {
         const qma_cuda_tensor *x = find_tensor(t, n, name);
         if (!x) {
             set_error("model_load: missing tensor %s", name);
             *rc = QMA_CUDA_ERR_INVALID;
+            return nullptr;
+        }
+        const int64_t n1 = x->ne[1] ? x->ne[1] : 1, n2 = x->ne[2] ? x->ne[2] : 1;
+        if (x->ne[0] != e0 || n1 != e1 || n2 != e2) {
+            set_error("model_load: %s has shape [%lld, %lld, %lld], expected [%lld, %lld, %lld]", name,
+                      (long long)x->ne[0], (long long)n1, (long long)n2, (long long)e0, (long long)e1,
+                      (long long)e2);
+            *rc = QMA_CUDA_ERR_INVALID;
+            return nullptr;
         }
         return x;
     }
     int ensure_tmp(size_t bytes) {
-        if (bytes <= tmp_cap) return QMA_CUDA_OK;
+        if (dry || bytes <= tmp_cap) return QMA_CUDA_OK;
         if (tmp) {
             QMA_CHECK_CUDA(cudaStreamSynchronize(st));
             cudaFree(tmp);
@@ -179,9 +200,9 @@ struct Loader {
         return QMA_CUDA_OK;
     }
     // F32 vector / matrix, kept as is
-    int f32(const char *name, const float **out) {
+    int f32(const char *name, const float **out, int64_t e0, int64_t e1 = 1) {
         int rc = 0;
-        const qma_cuda_tensor *x = need(name, &rc);
+        const qma_cuda_tensor *x = need(name, &rc, e0, e1);
         if (rc) return rc;
         if (x->type != QMA_TYPE_F32) {
             set_error("model_load: %s must be F32", name);
@@ -195,13 +216,16 @@ struct Loader {
         return QMA_CUDA_OK;
     }
     // quantized matrices stacked along rows (all of one type), packed
-    int stacked(const std::vector<std::string> &names, void **out, int *type, int *rows_out) {
+    // names[i] must be [ncols, rows[i]]
+    int stacked(const std::vector<std::string> &names, const std::vector<int64_t> &nrows, int64_t width,
+                void **out, int *type, int *rows_out) {
         int rc = 0;
         std::vector<const qma_cuda_tensor *> xs;
         int64_t rows = 0, ncols = -1;
         int ty = -1;
-        for (auto &nm : names) {
-            const qma_cuda_tensor *x = need(nm.c_str(), &rc);
+        for (size_t i = 0; i < names.size(); i++) {
+            const std::string &nm = names[i];
+            const qma_cuda_tensor *x = need(nm.c_str(), &rc, width, nrows[i]);
             if (rc) return rc;
             if (ty < 0) { ty = int(x->type); ncols = x->ne[0]; }
             if (int(x->type) != ty || x->ne[0] != ncols) {
@@ -210,6 +234,10 @@ struct Loader {
             }
             rows += x->ne[1];
             xs.push_back(x);
+        }
+        if (ty != QMA_TYPE_Q4_K && ty != QMA_TYPE_Q6_K && ty != QMA_TYPE_Q8_0) {
+            set_error("model_load: %s must be Q4_K, Q6_K or Q8_0 (type %d)", names[0].c_str(), ty);
+            return QMA_CUDA_ERR_UNSUPPORTED;
         }
         const size_t rb = gguf_row_bytes(ty, ncols);
         if ((rc = ensure_tmp(rb * size_t(rows)))) return rc;
@@ -220,17 +248,21 @@ struct Loader {
         }
         void *d;
         if ((rc = dalloc(&d, packed_bytes(ty, int(rows), int(ncols))))) return rc;
-        if ((rc = repack(ty, tmp, int(rows), int(ncols), d, st))) return rc;
+        if (!dry && (rc = repack(ty, tmp, int(rows), int(ncols), d, st))) return rc;
         *out = d;
         *type = ty;
         if (rows_out) *rows_out = int(rows);
         return QMA_CUDA_OK;
     }
     // 3-D expert tensor [ne2 experts][ne1 rows][ne0]: one packed matrix each
-    int experts(const char *name, void **out, int *type) {
+    int experts(const char *name, void **out, int *type, int64_t e0, int64_t e1) {
         int rc = 0;
-        const qma_cuda_tensor *x = need(name, &rc);
+        const qma_cuda_tensor *x = need(name, &rc, e0, e1, MOE_NEXP);
         if (rc) return rc;
+        if (x->type != QMA_TYPE_Q4_K && x->type != QMA_TYPE_Q6_K) {
+            set_error("model_load: %s must be Q4_K or Q6_K (type %u)", name, x->type);
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
         const int rows = int(x->ne[1]), cols = int(x->ne[0]), ne = int(x->ne[2]);
         const size_t gb = gguf_row_bytes(int(x->type), cols) * rows;
         const size_t pb = packed_bytes(int(x->type), rows, cols);
@@ -238,7 +270,7 @@ struct Loader {
         if ((rc = fetch(x, tmp))) return rc;
         void *d;
         if ((rc = dalloc(&d, pb * ne))) return rc;
-        for (int e = 0; e < ne; e++)
+        for (int e = 0; e < ne && !dry; e++)
             if ((rc = repack(int(x->type), tmp + gb * e, rows, cols, static_cast<uint8_t *>(d) + pb * e, st)))
                 return rc;
         *out = d;
@@ -247,74 +279,102 @@ struct Loader {
     }
 };
 
+// dry: the host-only check of the table (names, shapes, types, data
+// ranges) that runs before anything is allocated; *out is left untouched.
 static int build_model(int device, const qma_cuda_tensor *t, uint32_t n, const void *host,
-                       uint64_t host_size, bool synth, uint64_t seed, qma_cuda_model **out) {
-    QMA_REQUIRE(t && n > 0 && out && (synth || host), "model: bad arguments");
-    QMA_CHECK_CUDA(cudaSetDevice(device));
+                       uint64_t host_size, bool synth, uint64_t seed, qma_cuda_model **out,
+                       bool dry = false) {
+    QMA_REQUIRE(t && n > 0 && (out || dry) && (synth || host || dry), "model: bad arguments");
+    if (!dry) {
+        int rc0 = build_model(device, t, n, host, host_size, synth || !host, seed, nullptr, true);
+        if (rc0) return rc0;
+        QMA_CHECK_CUDA(cudaSetDevice(device));
+    }
     qma_cuda_model *m = new qma_cuda_model();
     m->device = device;
-    cudaStream_t st;
-    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    cudaStream_t st = nullptr;
+    if (!dry) QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     Loader ld{m, t, n, static_cast<const uint8_t *>(host), host_size, synth, seed, st};
+    ld.dry = dry;
     int rc = 0;
     char nm[96];
     auto fail = [&](int code) {
-        cudaStreamSynchronize(st);
-        if (ld.tmp) cudaFree(ld.tmp);
-        cudaStreamDestroy(st);
-        for (void *p : m->allocs) cudaFree(p);
+        if (!dry) {
+            cudaStreamSynchronize(st);
+            if (ld.tmp) cudaFree(ld.tmp);
+            cudaStreamDestroy(st);
+            for (void *p : m->allocs) cudaFree(p);
+        }
         delete m;
         return code;
     };
     const qma_cuda_tensor *te = find_tensor(t, n, "token_embd.weight");
-    if (!te || te->ne[0] != EMBD) {
-        set_error("model: token_embd.weight missing or not %d wide", EMBD);
+    if (!te || te->ne[0] != EMBD || te->ne[1] < 1 || te->ne[1] > (int64_t(1) << 22) ||
+        (te->ne[2] != 0 && te->ne[2] != 1)) {
+        set_error("model: token_embd.weight missing or not [%d, 1..%d]", EMBD, 1 << 22);
         return fail(QMA_CUDA_ERR_INVALID);
     }
     m->n_vocab = int(te->ne[1]);
+    const int64_t V = m->n_vocab;
     int rows;
-    if ((rc = ld.stacked({"token_embd.weight"}, &m->embd, &m->embd_type, &rows))) return fail(rc);
-    if ((rc = ld.stacked({"output.weight"}, &m->out, &m->out_type, &rows))) return fail(rc);
-    if ((rc = ld.f32("output_norm.weight", &m->out_norm))) return fail(rc);
+    if ((rc = ld.stacked({"token_embd.weight"}, {V}, EMBD, &m->embd, &m->embd_type, &rows))) return fail(rc);
+    if ((rc = ld.stacked({"output.weight"}, {V}, EMBD, &m->out, &m->out_type, &rows))) return fail(rc);
+    if ((rc = ld.f32("output_norm.weight", &m->out_norm, EMBD))) return fail(rc);
     for (int il = 0; il < NLAYER; il++) {
         LayerW &L = m->L[il];
         auto N = [&](const char *s) { snprintf(nm, sizeof(nm), "blk.%d.%s", il, s); return std::string(nm); };
-        if ((rc = ld.f32(N("attn_norm.weight").c_str(), &L.attn_norm))) return fail(rc);
-        if ((rc = ld.f32(N("post_attention_norm.weight").c_str(), &L.post_norm))) return fail(rc);
+        if ((rc = ld.f32(N("attn_norm.weight").c_str(), &L.attn_norm, EMBD))) return fail(rc);
+        if ((rc = ld.f32(N("post_attention_norm.weight").c_str(), &L.post_norm, EMBD))) return fail(rc);
         if (is_attn(il)) {
             if ((rc = ld.stacked({N("attn_q.weight"), N("attn_k.weight"), N("attn_v.weight")},
-                                 &L.in_proj, &L.in_type, &L.in_rows))) return fail(rc);
-            if ((rc = ld.stacked({N("attn_output.weight")}, &L.out_proj, &L.out_type, &rows))) return fail(rc);
-            if ((rc = ld.f32(N("attn_q_norm.weight").c_str(), &L.q_norm))) return fail(rc);
-            if ((rc = ld.f32(N("attn_k_norm.weight").c_str(), &L.k_norm))) return fail(rc);
+                                 {WQ_DIM, WKV_DIM, WKV_DIM}, EMBD, &L.in_proj, &L.in_type, &L.in_rows)))
+                return fail(rc);
+            if ((rc = ld.stacked({N("attn_output.weight")}, {EMBD}, WO_DIM, &L.out_proj, &L.out_type, &rows)))
+                return fail(rc);
+            if ((rc = ld.f32(N("attn_q_norm.weight").c_str(), &L.q_norm, HEAD_DIM))) return fail(rc);
+            if ((rc = ld.f32(N("attn_k_norm.weight").c_str(), &L.k_norm, HEAD_DIM))) return fail(rc);
         } else {
             if ((rc = ld.stacked({N("attn_qkv.weight"), N("attn_gate.weight"), N("ssm_beta.weight"),
-                                  N("ssm_alpha.weight")}, &L.in_proj, &L.in_type, &L.in_rows))) return fail(rc);
-            if ((rc = ld.stacked({N("ssm_out.weight")}, &L.out_proj, &L.out_type, &rows))) return fail(rc);
-            if ((rc = ld.f32(N("ssm_conv1d.weight").c_str(), &L.conv1d))) return fail(rc);
-            if ((rc = ld.f32(N("ssm_dt.bias").c_str(), &L.dt))) return fail(rc);
-            if ((rc = ld.f32(N("ssm_a").c_str(), &L.a))) return fail(rc);
-            if ((rc = ld.f32(N("ssm_norm.weight").c_str(), &L.ssm_norm))) return fail(rc);
+                                  N("ssm_alpha.weight")}, {CONV_DIM, VAL_DIM, VHEADS, VHEADS}, EMBD, &L.in_proj,
+                                 &L.in_type, &L.in_rows))) return fail(rc);
+            if ((rc = ld.stacked({N("ssm_out.weight")}, {EMBD}, VAL_DIM, &L.out_proj, &L.out_type, &rows)))
+                return fail(rc);
+            if ((rc = ld.f32(N("ssm_conv1d.weight").c_str(), &L.conv1d, 4, CONV_DIM))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_dt.bias").c_str(), &L.dt, VHEADS))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_a").c_str(), &L.a, VHEADS))) return fail(rc);
+            if ((rc = ld.f32(N("ssm_norm.weight").c_str(), &L.ssm_norm, SSTATE))) return fail(rc);
         }
         qma_cuda_moe_weights &w = L.moe;
         w.post_norm = L.post_norm;
-        if ((rc = ld.f32(N("ffn_gate_inp.weight").c_str(), &w.gate_inp))) return fail(rc);
-        if ((rc = ld.f32(N("ffn_gate_inp_shexp.weight").c_str(), &w.gate_inp_shexp))) return fail(rc);
+        if ((rc = ld.f32(N("ffn_gate_inp.weight").c_str(), &w.gate_inp, EMBD, MOE_NEXP))) return fail(rc);
+        if ((rc = ld.f32(N("ffn_gate_inp_shexp.weight").c_str(), &w.gate_inp_shexp, EMBD))) return fail(rc);
         int ty;
         void *p;
-        if ((rc = ld.experts(N("ffn_gate_exps.weight").c_str(), &p, &ty))) return fail(rc);
+        if ((rc = ld.experts(N("ffn_gate_exps.weight").c_str(), &p, &ty, EMBD, MOE_FF))) return fail(rc);
         w.gate_exps = p;
-        if ((rc = ld.experts(N("ffn_up_exps.weight").c_str(), &p, &ty))) return fail(rc);
+        if (ty != QMA_TYPE_Q4_K) { set_error("model: expert gate/up must be Q4_K"); return fail(QMA_CUDA_ERR_UNSUPPORTED); }
+        if ((rc = ld.experts(N("ffn_up_exps.weight").c_str(), &p, &ty, EMBD, MOE_FF))) return fail(rc);
         w.up_exps = p;
         if (ty != QMA_TYPE_Q4_K) { set_error("model: expert gate/up must be Q4_K"); return fail(QMA_CUDA_ERR_UNSUPPORTED); }
-        if ((rc = ld.experts(N("ffn_down_exps.weight").c_str(), &p, &w.down_type))) return fail(rc);
+        if ((rc = ld.experts(N("ffn_down_exps.weight").c_str(), &p, &w.down_type, MOE_FF, EMBD))) return fail(rc);
         w.down_exps = p;
-        if ((rc = ld.stacked({N("ffn_gate_shexp.weight")}, &p, &ty, &rows))) return fail(rc);
+        if ((rc = ld.stacked({N("ffn_gate_shexp.weight")}, {MOE_FF}, EMBD, &p, &ty, &rows))) return fail(rc);
         w.gate_shexp = p;
-        if ((rc = ld.stacked({N("ffn_up_shexp.weight")}, &p, &ty, &rows))) return fail(rc);
+        if (ty != QMA_TYPE_Q4_K) { set_error("model: shared expert gate/up must be Q4_K"); return fail(QMA_CUDA_ERR_UNSUPPORTED); }
+        if ((rc = ld.stacked({N("ffn_up_shexp.weight")}, {MOE_FF}, EMBD, &p, &ty, &rows))) return fail(rc);
         w.up_shexp = p;
-        if ((rc = ld.stacked({N("ffn_down_shexp.weight")}, &p, &w.down_shexp_type, &rows))) return fail(rc);
+        if (ty != QMA_TYPE_Q4_K) { set_error("model: shared expert gate/up must be Q4_K"); return fail(QMA_CUDA_ERR_UNSUPPORTED); }
+        if ((rc = ld.stacked({N("ffn_down_shexp.weight")}, {EMBD}, MOE_FF, &p, &w.down_shexp_type, &rows)))
+            return fail(rc);
         w.down_shexp = p;
+        if ((w.down_type != QMA_TYPE_Q6_K && w.down_type != QMA_TYPE_Q4_K) || w.down_shexp_type != w.down_type) {
+            set_error("model: expert down projections must be Q6_K or Q4_K, routed and shared alike");
+            return fail(QMA_CUDA_ERR_UNSUPPORTED);
+        }
+    }
+    if (dry) {
+        delete m;
+        return QMA_CUDA_OK;
     }
     QMA_CHECK_CUDA(cudaStreamSynchronize(st));
     if (ld.tmp) cudaFree(ld.tmp);
@@ -1007,6 +1067,11 @@ int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n,
                          qma_cuda_model **out) {
     qma::clear_error();
     return qma::build_model(device, tensors, n, nullptr, 0, true, seed, out);
+}
+
+int qma_cuda_model_check(const qma_cuda_tensor *tensors, uint32_t n, uint64_t data_size) {
+    qma::clear_error();
+    return qma::build_model(0, tensors, n, nullptr, data_size, data_size == 0, 0, nullptr, true);
 }
 
 int qma_cuda_model_free(qma_cuda_model *m) {

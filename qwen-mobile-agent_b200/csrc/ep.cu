@@ -30,7 +30,11 @@
 // qma_cuda_moe_layer's grouped path bit for bit.
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
+#include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -194,20 +198,84 @@ struct qma_cuda_ep {
     int *h_allcnt = nullptr;          // pinned [N][N][2]
     uint64_t sent = 0, recvd = 0;     // bytes of the last call
     int rows_in = 0;
+    int timeout_ms = 0;               // wall-clock limit of every host-side wait
+    bool aborted = false;             // the communicator was aborted after a failure
 };
 
 namespace {
 
-int ep_nccl(ncclResult_t r, const char *what) {
+using Clock = std::chrono::steady_clock;
+
+int ms_since(Clock::time_point t0) {
+    return int(std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count());
+}
+
+// Ends the communicator after a failure or a timeout: its peers' pending
+// operations fail instead of waiting for this rank forever.
+void ep_abort(qma_cuda_ep *ep) {
+    if (ep->comm && !ep->aborted) ncclCommAbort(ep->comm);
+    ep->comm = nullptr;
+    ep->aborted = true;
+}
+
+// The communicator is non-blocking: a call may return ncclInProgress while
+// it connects to its peers (the first transfer to a peer sets up that
+// connection).  Poll its state until it settles, for at most the handle's
+// wall-clock limit; a peer that never answers aborts the communicator and
+// fails the call with QMA_CUDA_ERR_TIMEOUT.
+int ep_settle(qma_cuda_ep *ep, ncclResult_t r, const char *what) {
+    const Clock::time_point t0 = Clock::now();
+    while (r == ncclInProgress) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t q = ncclCommGetAsyncError(ep->comm, &st);
+        r = q != ncclSuccess ? q : st;
+        if (r != ncclInProgress) break;
+        if (ms_since(t0) > ep->timeout_ms) {
+            ep_abort(ep);
+            qma::set_error("%s: no answer from the other ranks within %d ms (communicator aborted)", what,
+                           ep->timeout_ms);
+            return QMA_CUDA_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
     if (r == ncclSuccess) return QMA_CUDA_OK;
     qma::set_error("%s: %s", what, ncclGetErrorString(r));
+    ep_abort(ep);
     return QMA_CUDA_ERR_CUDA;
 }
 #define EP_NCCL(call)                                        \
     do {                                                     \
-        int rc_ = ep_nccl((call), #call);                    \
+        int rc_ = ep_settle(ep, (call), #call);              \
         if (rc_) return rc_;                                 \
     } while (0)
+
+// The stream's work (including transfers that wait on other ranks) done,
+// for at most the wall-clock limit; an asynchronous communicator error or
+// the limit aborts the communicator.
+int ep_sync(qma_cuda_ep *ep, cudaStream_t st) {
+    const Clock::time_point t0 = Clock::now();
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(st);
+        if (e == cudaSuccess) return QMA_CUDA_OK;
+        if (e != cudaErrorNotReady) {
+            qma::set_error("qma_cuda_ep_moe_layer: %s", cudaGetErrorString(e));
+            return QMA_CUDA_ERR_CUDA;
+        }
+        ncclResult_t as = ncclSuccess;
+        if (ncclCommGetAsyncError(ep->comm, &as) != ncclSuccess || (as != ncclSuccess && as != ncclInProgress)) {
+            qma::set_error("qma_cuda_ep_moe_layer: communicator error: %s", ncclGetErrorString(as));
+            ep_abort(ep);
+            return QMA_CUDA_ERR_CUDA;
+        }
+        if (ms_since(t0) > ep->timeout_ms) {
+            ep_abort(ep);
+            qma::set_error("qma_cuda_ep_moe_layer: the exchange did not finish within %d ms (communicator aborted)",
+                           ep->timeout_ms);
+            return QMA_CUDA_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
 
 int ep_alloc(qma_cuda_ep *ep, size_t bytes, void **out) {
     void *p = nullptr;
@@ -222,7 +290,12 @@ int ep_alloc(qma_cuda_ep *ep, size_t bytes, void **out) {
 }
 
 void ep_release(qma_cuda_ep *ep) {
-    if (ep->comm) ncclCommDestroy(ep->comm);
+    if (ep->comm) {
+        // a communicator whose peers may be gone cannot be finalized
+        // collectively: abort it instead of waiting for them
+        if (ep->aborted) ncclCommAbort(ep->comm);
+        else ncclCommDestroy(ep->comm);
+    }
     for (void *p : ep->allocs) cudaFree(p);
     if (ep->h_allcnt) cudaFreeHost(ep->h_allcnt);
     delete ep;
@@ -236,14 +309,29 @@ int qma_cuda_ep_unique_id(uint8_t *uid) {
     qma::clear_error();
     QMA_REQUIRE(uid, "qma_cuda_ep_unique_id: null output");
     ncclUniqueId id;
-    EP_NCCL(ncclGetUniqueId(&id));
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        qma::set_error("qma_cuda_ep_unique_id: %s", ncclGetErrorString(r));
+        return QMA_CUDA_ERR_CUDA;
+    }
     static_assert(sizeof(id) == QMA_CUDA_EP_UID_BYTES, "NCCL unique id size");
     memcpy(uid, &id, sizeof(id));
     return QMA_CUDA_OK;
 }
 
+int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ranks, int t_max, int timeout_ms,
+                             qma_cuda_ep **out);
+
 int qma_cuda_ep_init(int device, const uint8_t *uid, int rank, int n_ranks, int t_max, qma_cuda_ep **out) {
+    const char *env = getenv("QMA_CUDA_EP_TIMEOUT_MS");
+    const int ms = env && atoi(env) > 0 ? atoi(env) : 300000;
+    return qma_cuda_ep_init_timeout(device, uid, rank, n_ranks, t_max, ms, out);
+}
+
+int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ranks, int t_max, int timeout_ms,
+                             qma_cuda_ep **out) {
     qma::clear_error();
+    QMA_REQUIRE(timeout_ms > 0, "qma_cuda_ep_init: timeout %d ms must be positive", timeout_ms);
     QMA_REQUIRE(uid && out, "qma_cuda_ep_init: null argument");
     QMA_REQUIRE(n_ranks >= 1 && n_ranks <= qma::EP_MAX_RANKS && qma::MOE_NEXP % n_ranks == 0,
                 "qma_cuda_ep_init: %d ranks (1..8, dividing 256)", n_ranks);
@@ -259,6 +347,7 @@ int qma_cuda_ep_init(int device, const uint8_t *uid, int rank, int n_ranks, int 
     ep->t_max = t_max;
     ep->n_local = qma::MOE_NEXP / n_ranks;
     ep->r_max = t_max * n_ranks;
+    ep->timeout_ms = timeout_ms;
     using namespace qma;
     // both scratch views carry the grouped buffers (16 rows at least)
     const int tl = t_max < MOE_GROUPED_MIN_T ? MOE_GROUPED_MIN_T : t_max;
@@ -296,12 +385,22 @@ int qma_cuda_ep_init(int device, const uint8_t *uid, int rank, int n_ranks, int 
     ep->prow = static_cast<int *>(p[11]);
     ncclUniqueId id;
     memcpy(&id, uid, sizeof(id));
-    ncclResult_t r = ncclCommInitRank(&ep->comm, n_ranks, id, rank);
-    if (r != ncclSuccess) {
+    // non-blocking initialisation, polled against the wall-clock limit: a
+    // rank that never joins fails the others' init instead of hanging it
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&ep->comm, n_ranks, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
         ep->comm = nullptr;
         ep_release(ep);
-        set_error("qma_cuda_ep_init: ncclCommInitRank: %s", ncclGetErrorString(r));
+        set_error("qma_cuda_ep_init: ncclCommInitRankConfig: %s", ncclGetErrorString(r));
         return QMA_CUDA_ERR_CUDA;
+    }
+    if ((rc = ep_settle(ep, r, "qma_cuda_ep_init"))) {
+        const std::string msg = qma_cuda_last_error();
+        ep_release(ep);
+        set_error("%s", msg.c_str());
+        return rc;
     }
     *out = ep;
     return QMA_CUDA_OK;
@@ -326,6 +425,7 @@ int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const 
                 "qma_cuda_ep_moe_layer: missing weight pointer");
     QMA_REQUIRE(w->down_type == QMA_TYPE_Q6_K && w->down_shexp_type == QMA_TYPE_Q6_K,
                 "qma_cuda_ep_moe_layer: down projections must be Q6_K");
+    QMA_REQUIRE(!ep->aborted && ep->comm, "qma_cuda_ep_moe_layer: the communicator was aborted after a failure");
     cudaStream_t st = as_stream(stream);
     const int n = ep->n, me = ep->rank;
     int rc;
@@ -342,7 +442,7 @@ int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const 
     // 4: counts, then the dispatch
     EP_NCCL(ncclAllGather(ep->cnt, ep->allcnt, 2 * n, ncclInt32, ep->comm, st));
     QMA_CHECK_CUDA(cudaMemcpyAsync(ep->h_allcnt, ep->allcnt, sizeof(int) * 2 * n * n, cudaMemcpyDeviceToHost, st));
-    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if ((rc = ep_sync(ep, st))) return rc;
     const int *ac = ep->h_allcnt;      // ac[(src * n + dst) * 2 + {0 rows, 1 pairs}]
     auto rows_to = [&](int s, int d) { return ac[(s * n + d) * 2]; };
     auto pairs_to = [&](int s, int d) { return ac[(s * n + d) * 2 + 1]; };

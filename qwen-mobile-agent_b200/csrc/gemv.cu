@@ -265,11 +265,11 @@ static int launch_stream(const typename F::Ptr &W, int n_in, int n_out, const in
     if (rows_blk < 8) rows_blk = 8;
     const uint32_t stage_bytes = Stage<F>::bytes(rows_blk, n_in);
     const size_t smem = size_t(stage_bytes) * STREAM_NST;
-    static bool attr = false;
-    if (!attr) {
+    static PerDevice attr;
+    if (!attr.done()) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_stream_kernel<F, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(STREAM_NST * (STREAM_STAGE + 8 * 1024))));
-        attr = true;
+        attr.mark();
     }
     const int grid = num_sms();
     int rows_cta = (n_out + grid - 1) / grid;
@@ -295,13 +295,13 @@ template <class F, int LPR, int UPL, int RU>
 static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const int8_t *xq,
                          const float *xd, const int16_t *xsum, float *out, const float *resid,
                          int rows_cta, uint32_t smem, cudaStream_t st, const ConvEpi &conv) {
-    static bool attr = false;
-    if (!attr) {
+    static PerDevice attr;
+    if (!attr.done()) {
         QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_staged_kernel<F, LPR, UPL, RU>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(STAGED_MAX)));
         QMA_CHECK_CUDA(cudaFuncSetAttribute(gemv_staged_kernel<F, LPR, UPL, RU>,
                                             cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        attr = true;
+        attr.mark();
     }
     const int grid = (n_out + rows_cta - 1) / rows_cta;
     const unsigned threads = 512;
@@ -310,15 +310,17 @@ static int launch_staged(const typename F::Ptr &W, int n_in, int n_out, const in
     return QMA_CUDA_OK;
 }
 
-static int g_num_sms = 0;
+// SM count of the current device (looked up once per device)
+static std::atomic<int> g_num_sms[64];
 int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
+    int dev = PerDevice::current();
+    if (dev < 0 || dev >= 64) dev = 0;
+    int n = g_num_sms[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_num_sms[dev].store(n, std::memory_order_relaxed);
     }
-    return g_num_sms;
+    return n;
 }
 
 // One full wave: as many 256-thread CTAs as fit on every SM at once (from

@@ -219,12 +219,20 @@ int parse(const uint8_t *base, size_t size, std::vector<qma_cuda_tensor> &tensor
                            (long long)t.ne[0]);
             return QMA_CUDA_ERR_UNSUPPORTED;
         }
-        if (t.ne[1] < 1 || t.ne[2] < 1) {
+        if (t.ne[0] < 1 || t.ne[1] < 1 || t.ne[2] < 1 || t.ne[0] > INT32_MAX || t.ne[1] > INT32_MAX ||
+            t.ne[2] > INT32_MAX) {
             qma::set_error("gguf: tensor %s: bad shape", t.name);
             return QMA_CUDA_ERR_INVALID;
         }
-        t.nbytes = rb * uint64_t(t.ne[1]) * uint64_t(t.ne[2]);
-        if (t.off > avail || t.nbytes > avail - t.off) {
+        // the product rb * ne1 * ne2 is formed only once each factor is known
+        // to fit in the file, so it cannot wrap around
+        const uint64_t ne1 = uint64_t(t.ne[1]), ne2 = uint64_t(t.ne[2]);
+        if (t.off > avail || ne1 > (avail - t.off) / rb || ne2 > (avail - t.off) / (rb * ne1)) {
+            qma::set_error("gguf: tensor %s lies outside the file", t.name);
+            return QMA_CUDA_ERR_INVALID;
+        }
+        t.nbytes = rb * ne1 * ne2;
+        if (t.nbytes > avail - t.off) {
             qma::set_error("gguf: tensor %s lies outside the file", t.name);
             return QMA_CUDA_ERR_INVALID;
         }

@@ -875,10 +875,10 @@ int moe_wait_timeouts() {
     return int(n);
 }
 
-static bool g_moe_attrs = false;
+static PerDevice g_moe_attrs;
 
 static int moe_attrs() {
-    if (g_moe_attrs) return QMA_CUDA_OK;
+    if (g_moe_attrs.done()) return QMA_CUDA_OK;
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ROUTER_SMEM)));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -889,7 +889,7 @@ static int moe_attrs() {
     // prefer the largest shared-memory carveout (two CTAs per SM)
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    g_moe_attrs = true;
+    g_moe_attrs.mark();
     return QMA_CUDA_OK;
 }
 

@@ -30,9 +30,11 @@ struct SmpArgs {
 __device__ int g_smp_ids[SMP_MAX_K];
 __device__ float g_smp_lgs[SMP_MAX_K];
 
-// float -> unsigned key with the same order (larger float, larger key)
+// float -> unsigned key with the same order (larger float, larger key);
+// -0.0f maps to the key of +0.0f, since the reference's float comparisons
+// treat the two as equal
 __device__ __forceinline__ unsigned order_key(float f) {
-    const unsigned b = __float_as_uint(f);
+    const unsigned b = __float_as_uint(f == 0.0f ? 0.0f : f);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 

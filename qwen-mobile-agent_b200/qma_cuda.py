@@ -52,6 +52,7 @@ _TP = C.POINTER(Tensor)
 _SIGS.update({
     "qma_cuda_model_load": (_i32, [_i32, _TP, C.c_uint32, _vp, _u64, C.POINTER(_vp)]),
     "qma_cuda_model_synth": (_i32, [_i32, _TP, C.c_uint32, _u64, C.POINTER(_vp)]),
+    "qma_cuda_model_check": (_i32, [_TP, C.c_uint32, _u64]),
     "qma_cuda_gguf_scan": (_i32, [C.c_char_p, _TP, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(_u64),
                                   C.POINTER(_u64)]),
     "qma_cuda_model_load_gguf": (_i32, [_i32, C.c_char_p, C.POINTER(_vp)]),
@@ -144,6 +145,12 @@ def synth_layout(n_vocab=151936, embd_type=Q8_0, out_type=Q8_0, down_type=Q6_K, 
 
 def tensor_index(arr, n) -> dict:
     return {arr[i].name.decode(): i for i in range(n)}
+
+
+def model_check(arr, n, data_size: int = 0) -> None:
+    """qma_cuda_model_check: raise QmaError unless the table has every
+    tensor with the shapes and types the kernels are written for."""
+    call("qma_cuda_model_check", arr, n, data_size)
 
 
 def gguf_scan(path: str):
@@ -239,6 +246,7 @@ _SIGS["qma_cuda_model_moe_weights"] = (_i32, [_vp, _i32, C.POINTER(MoeWeights)])
 _SIGS.update({
     "qma_cuda_ep_unique_id": (_i32, [_vp]),
     "qma_cuda_ep_init": (_i32, [_i32, _vp, _i32, _i32, _i32, C.POINTER(_vp)]),
+    "qma_cuda_ep_init_timeout": (_i32, [_i32, _vp, _i32, _i32, _i32, _i32, C.POINTER(_vp)]),
     "qma_cuda_ep_free": (_i32, [_vp]),
     "qma_cuda_ep_moe_layer": (_i32, [_vp, C.POINTER(MoeWeights), _vp, _i32, _vp, _vp, _vp, _vp]),
     "qma_cuda_ep_stats": (_i32, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_i32)]),
@@ -264,7 +272,7 @@ class ExpertParallel:
     to the others (rank 0 passes its id and gets it back; the others pass
     None): a torch.distributed broadcast, a store, a file."""
 
-    def __init__(self, device: int, rank: int, n_ranks: int, t_max: int, share_uid):
+    def __init__(self, device: int, rank: int, n_ranks: int, t_max: int, share_uid, timeout_ms=None):
         ep_shard(rank, n_ranks)
         uid = (C.c_uint8 * EP_UID_BYTES)()
         if rank == 0:
@@ -274,7 +282,10 @@ class ExpertParallel:
             raise ValueError(f"communicator id of {len(raw)} bytes")
         uid = (C.c_uint8 * EP_UID_BYTES).from_buffer_copy(raw)
         h = _vp()
-        call("qma_cuda_ep_init", device, uid, rank, n_ranks, t_max, C.byref(h))
+        if timeout_ms is None:
+            call("qma_cuda_ep_init", device, uid, rank, n_ranks, t_max, C.byref(h))
+        else:
+            call("qma_cuda_ep_init_timeout", device, uid, rank, n_ranks, t_max, int(timeout_ms), C.byref(h))
         self.h, self.rank, self.n_ranks, self.t_max = h, rank, n_ranks, t_max
 
     def moe_layer(self, w: MoeWeights, x2, T: int, x_out, sel=None, wts=None, stream=None) -> None:

@@ -63,3 +63,50 @@ def test_sampler_arguments():
                  (1, 10, last, 65, 1.0, 1.0, 5, 5), (1, 10, None, 3, 1.0, 1.0, 5, 5), (1, 0, None, 0, 1.0, 1.0, 5, 5)]:
         assert lib.qma_cuda_sample_candidates(*args, ids, lgs, C.byref(n), None) == Q.ERR_INVALID, args
     assert lib.qma_cuda_state_logits(None) is None
+
+
+def test_model_table_check_refuses_shapes_the_kernels_do_not_handle():
+    """The loader's up-front table check (host only): the qwen35moe table
+    passes; a table with another expert count, a short norm vector, a
+    missing tensor or a tensor past the data section is refused before
+    anything is allocated."""
+    import pytest
+    arr, n, size = Q.synth_layout()
+    Q.model_check(arr, n)
+    Q.model_check(arr, n, size)
+    idx = Q.tensor_index(arr, n)
+
+    def refused(mutate, what):
+        arr2, n2, _ = Q.synth_layout()
+        mutate(arr2)
+        with pytest.raises(Q.QmaError) as e:
+            Q.model_check(arr2, n2)
+        assert e.value.status == Q.ERR_INVALID, what
+        assert what in str(e.value), (what, str(e.value))
+
+    refused(lambda a: a[idx["blk.3.ffn_gate_exps.weight"]].ne.__setitem__(2, 128), "blk.3.ffn_gate_exps.weight")
+    refused(lambda a: a[idx["blk.7.ffn_down_exps.weight"]].ne.__setitem__(1, 1024), "blk.7.ffn_down_exps.weight")
+    refused(lambda a: a[idx["blk.0.ssm_norm.weight"]].ne.__setitem__(0, 64), "blk.0.ssm_norm.weight")
+    refused(lambda a: a[idx["blk.3.attn_k_norm.weight"]].ne.__setitem__(0, 128), "blk.3.attn_k_norm.weight")
+    refused(lambda a: a[idx["blk.12.ffn_gate_inp.weight"]].ne.__setitem__(1, 64), "blk.12.ffn_gate_inp.weight")
+    refused(lambda a: a[idx["output.weight"]].ne.__setitem__(1, 1000), "output.weight")
+    refused(lambda a: setattr(a[idx["blk.39.ffn_up_shexp.weight"]], "name", b"blk.39.renamed"),
+            "blk.39.ffn_up_shexp.weight")
+    # a data section too short for the last tensor
+    with pytest.raises(Q.QmaError) as e:
+        Q.model_check(arr, n, size - 4096)
+    assert e.value.status == Q.ERR_INVALID
+    # an unsupported expert type
+    arr3, n3, _ = Q.synth_layout()
+    arr3[idx["blk.5.ffn_up_exps.weight"]].type = Q.Q8_0
+    with pytest.raises(Q.QmaError) as e:
+        Q.model_check(arr3, n3)
+    assert e.value.status in (Q.ERR_UNSUPPORTED, Q.ERR_INVALID)
+
+
+def test_expert_parallel_init_timeout_argument():
+    lib = Q.lib()
+    uid = (C.c_uint8 * Q.EP_UID_BYTES)()
+    h = C.c_void_p()
+    assert lib.qma_cuda_ep_init_timeout(0, uid, 0, 2, 8, 0, C.byref(h)) == Q.ERR_INVALID
+    assert "timeout" in Q.last_error()

@@ -127,3 +127,45 @@ def test_expert_parallel_two_ranks_match_one_gpu():
                 assert rec["ref_rel"] < 1e-3, (case, r)
             assert rec["oracle_rel"] < 1e-3, (case, r)
         assert sum(r["sent"] for r in recs) == sum(r["recv"] for r in recs)
+
+
+def _lonely_rank(results):
+    """Rank 0 of a two-rank communicator whose rank 1 never joins."""
+    import ctypes as C
+    import qma_cuda as Q
+    try:
+        Q.init(0)
+        uid = (C.c_uint8 * Q.EP_UID_BYTES)()
+        Q.call("qma_cuda_ep_unique_id", uid)
+        h = C.c_void_p()
+        t0 = time.time()
+        rc = Q.lib().qma_cuda_ep_init_timeout(0, uid, 0, 2, 8, 2000, C.byref(h))
+        results.put((rc, time.time() - t0, Q.last_error(), h.value))
+    except Exception:
+        import traceback
+        results.put((None, 0.0, traceback.format_exc(), None))
+
+
+def test_expert_parallel_init_times_out_when_a_rank_never_joins():
+    """Failure detection on the host: the second rank of the communicator
+    never starts, so the first rank's non-blocking NCCL initialisation never
+    completes; after its 2-second limit the call aborts the communicator and
+    returns QMA_CUDA_ERR_TIMEOUT instead of waiting forever.  No kernel runs
+    (the wait is on the host); the scenario runs in a child process."""
+    import torch
+    import qma_cuda as Q
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank, args=(results,))
+    p.start()
+    try:
+        rc, took, msg, h = results.get(timeout=180)
+    finally:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rc == Q.ERR_TIMEOUT, (rc, msg)
+    assert "2000 ms" in msg and h is None, msg
+    assert 1.5 < took < 90, took
