@@ -559,7 +559,8 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
         "tokens_per_gpu": T, "sequences": EP_SEQS, "scaling": "strong (64 sequences in total)",
         "ep1_tok_per_s": round(ep1_value, 1) if ep1_value else (round(value, 1) if world == 1 else None),
         "e2e_tok_per_s": round(EP_SEQS * e2e_steps / (e2e_ms / 1e3), 1),
-        "nvlink": {"sent_bytes_per_step": net[0], "recv_bytes_per_step": net[1], "rank": rank},
+        "exchange": {"sent_bytes_per_step": net[0], "recv_bytes_per_step": net[1], "rank": rank,
+                     "note": "rank 0's NCCL transfers, its own share included (over NVLink at N > 1)"},
         "ep_parity": ok_all, "parity_detail": detail,
         "router_prior": "none (uniform router: the Zipf(1.1) prior of configs[4] is not applied)",
         "collectives": "per layer: NCCL all-gather of the counts, grouped send/recv dispatch and return",
@@ -979,6 +980,81 @@ def run_ep_ours(args, world, rank, local):
     }), flush=True)
 
 
+# -------------------------------------------------------------------- gdn --
+GDN_METRIC = "GDN layer decode us/step (configs[2])"
+# algorithmic bytes of one gated-delta-net layer step: the stacked Q4_K
+# in-projection (12352 x 2048), ssm_out (2048 x 4096), conv state r+w,
+# recurrent state r+w, norms, the input and output vectors
+GDN_STEP_BYTES = 12352 * 8 * 144 + 2048 * 16 * 144 + 2 * 8192 * 3 * 4 + 2 * 32 * 128 * 128 * 4 \
+    + (2048 + 128 + 4 * 8192 + 64) * 4 + 2 * 2048 * 4
+
+
+def run_gdn_ours(args, world, rank, local):
+    """gated-delta-net layer 0 of the random-init model (Q4_K
+    projections, zero state): 1024 single-token steps through
+    qma_cuda_gdn_step (device time of each call, CUDA events on the state's
+    stream), then a 4096-token prefill in 8 calls of 512 (the chunked
+    gated-delta form) on a fresh state."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    Q.init(local)
+    dev = torch.device("cuda", local)
+    arr, n, size = model_layout(Q8_0)
+    model = Q.Model(C.cast(arr, C.POINTER(Q.Tensor)), n, seed=SEED, device=local)
+    x = torch.from_numpy(np.random.default_rng(SEED + rank).standard_normal((4096, 2048)).astype(np.float32)).to(dev)
+    out = torch.empty_like(x)
+
+    def steps(st, n_steps, per):
+        stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(st.h), device=local)
+        evs = []
+        for i in range(n_steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            Q.call("qma_cuda_gdn_step", st.h, 0, Q.ptr(x) + i * per * 8192, per, Q.ptr(out) + i * per * 8192, 1)
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs)
+
+    st = Q.State(model, 8192)
+    steps(st, 16, 1)                                   # warm-up
+    st.close()
+    st = Q.State(model, 8192)
+    with ClockSampler(local) as clk:
+        dist_barrier(world)
+        dec_ms = dist_max(steps(st, 1024, 1), world)
+        dist_barrier(world)
+    st.close()
+    st = Q.State(model, 8192)
+    pre_ms = dist_max(steps(st, 8, 512), world)
+    st.close()
+    model.close()
+    if rank != 0:
+        return
+    peak, peak_kind = load_peaks()
+    us = dec_ms * 1e3 / 1024
+    achieved = GDN_STEP_BYTES / (us * 1e3)
+    print(json.dumps({
+        "metric": GDN_METRIC, "value": round(us, 3), "unit": "us/step", "n_gpus": world, "steps": 1024,
+        "warmup": 16, "ms_per_step": round(dec_ms / 1024, 5), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xq4 projections, fp32 recurrence", "data": "synthetic",
+        "config": {"workload": "configs[2] gated-delta-net layer 0: hidden 2048, 16 QK / 32 V heads of 128, "
+                               "fp32 state 32x128x128 from zero, conv 4, Q4_K projections; 1024 decode steps, "
+                               "then a 4096-token prefill in chunks of 512 (gated-delta chunks of 64)",
+                   "per_step": "each step is one qma_cuda_gdn_step call (norm, in-projection + conv, "
+                               "recurrence + gated norm, ssm_out + residual), device time",
+                   "base_metric": BASE_METRIC},
+        "prefill": {"tokens": 4096, "ms": round(pre_ms, 3), "tok_per_s": round(4096 / (pre_ms / 1e3), 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "one decode step of the layer (5 kernels)",
+                     "algorithmic_bytes_per_launch": GDN_STEP_BYTES},
+        "e2e": {"value": round(us, 3), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 5 * 1024, "clocks": clk.summary(), "cpu_baseline": None,
+    }), flush=True)
+
+
 # ------------------------------------------------------------------ main ---
 def main():
     ap = argparse.ArgumentParser()
@@ -986,7 +1062,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep", "gdn"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ep", action="store_true", help="decode: skip the expert-parallel leg")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the configs[1] GEMV leg")
@@ -1008,6 +1084,8 @@ def main():
             run_moe_ours(args, world, rank, local)
         elif args.workload == "ep":
             run_ep_ours(args, world, rank, local)
+        elif args.workload == "gdn":
+            run_gdn_ours(args, world, rank, local)
         else:
             run_gemv_ours(args, world, rank, local)
     finally:

@@ -158,13 +158,37 @@ int qma_cuda_model_synth(int device, const qma_cuda_tensor *tensors, uint32_t n,
 int qma_cuda_model_check(const qma_cuda_tensor *tensors, uint32_t n, uint64_t data_size);
 int qma_cuda_model_free(qma_cuda_model *m);
 int qma_cuda_model_n_vocab(const qma_cuda_model *m);
-/* Replaces qma_ecache_get (ecache.h:95, ecache.c:414-498): the expert
- * record of (layer, expert) is HBM-resident; returns device pointers to its
- * gate / up (Q4_K rows) and down (packed) matrices.  Never fails for valid
- * ids; there is nothing to hint or prefetch (qma_ecache_hint/prefetch have
- * no work to do when every expert is resident). */
+/* ---- expert cache (ecache.h:87-123) ---------------------------------------
+ * Every expert record of the model is HBM-resident, so the cache API keeps
+ * its contract with no slot pool behind it: lookups never miss, records
+ * never move, and the read-ahead calls become L2 residency hints (the
+ * record's bytes requested into the 126 MB L2 ahead of the kernels that
+ * read them). */
+/* Replaces qma_ecache_get (ecache.h:95, ecache.c:414-498): device pointers
+ * to the gate / up (Q4_K rows) and down (packed) matrices of expert
+ * `expert` of layer `layer`.  Never fails for valid ids. */
 int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const void **gate,
                         const void **up, const void **down);
+/* Replaces qma_ecache_hint (ecache.h:119, ecache.c:399-410): the records
+ * this layer is about to read, in order (host ids, n clamped to 64 as the
+ * reference does).  Asks L2 for their bytes on `stream` (no wait, no
+ * completion to observe); results never depend on it. */
+int qma_cuda_ecache_hint(const qma_cuda_model *m, int layer, const int *ids, int n, void *stream);
+/* Replaces qma_ecache_prefetch (ecache.h:123, ecache.c:378-397): a
+ * speculative fill for a layer that has not routed yet; the same L2
+ * request as a hint (nothing is pinned or counted here either). */
+int qma_cuda_ecache_prefetch(const qma_cuda_model *m, int layer, const int *ids, int n, void *stream);
+/* Replace qma_ecache_hold / qma_ecache_release (ecache.h:97-104,
+ * ecache.c:500-520): hold is get() with the record claimed until the next
+ * release; at most 64 holds between releases (QMA_CUDA_ERR_STATE past
+ * that, where the reference returns NULL), and one release ends them all.
+ * The pointers stay valid for the model's life either way (nothing is ever
+ * evicted); the count keeps callers written against the reference's
+ * contract honest.  qma_cuda_ecache_held returns the current count. */
+int qma_cuda_ecache_hold(qma_cuda_model *m, int layer, int expert, const void **gate, const void **up,
+                         const void **down);
+int qma_cuda_ecache_release(qma_cuda_model *m);
+int qma_cuda_ecache_held(const qma_cuda_model *m);
 
 /* Replaces runstate_init_kv (nn.c:1878-1979) plus the HCM statics
  * (nn.c:912-937): KV ring of n_ctx slots (4-bit + 2-bit records, 240 B per
@@ -204,6 +228,31 @@ int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int 
  * nn.c:2253-2266). */
 int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens,
                          int n_tokens, int n_layers, float *hidden);
+
+/* ---- layer-level parity points -------------------------------------------
+ * One layer's mixer (the half before the MoE block) on caller activations,
+ * against the state's per-layer memory.  x: device float [n_tokens][2048],
+ * the residual stream entering layer `layer` at the state's positions
+ * n_pos .. n_pos + n_tokens - 1 (1..512 tokens); x_out: device float
+ * [n_tokens][2048], the residual after the mixer (x + mixer(rms_norm(x) *
+ * attn_norm)).  With advance != 0 the call also does what qma_eval does at
+ * a chunk start and end for these positions: the heavy-hitter live index is
+ * rebuilt first when one is due (nn.c:2074-2088), and n_pos moves on by
+ * n_tokens afterwards; with advance 0 the state's position is left as is
+ * (several layers may then be run for the same positions).  Synchronous on
+ * the state's stream.
+ *
+ * qma_cuda_gdn_step replaces a gated-delta-net layer's mixer (nn.c:2164-2244:
+ * projections, conv1d_layer nn.c:717-741, l2norm_skv nn.c:744-761,
+ * gdn_worker nn.c:784-833, the gated norm and ssm_out); the layer's conv
+ * and recurrent state in `s` advance.  qma_cuda_attn_decode replaces an
+ * attention layer's (nn.c:2110-2163: projections, q/k norm, rope_imrope
+ * nn.c:841-861, kv_append nn.c:1455-1509, attn_worker nn.c:1215-1446 over
+ * the live index and the tail since the last rebuild, the gate and
+ * attn_output); the K/V records are appended to the layer's ring and the
+ * layer's salience is updated. */
+int qma_cuda_gdn_step(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance);
+int qma_cuda_attn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance);
 
 /* Copies the 240-byte KV slot (q4 record + q2 record, kvq.h:22-29) of
  * attention layer `lay` (0..9, model layer 4*lay+3), head `head` (0, 1 = K

@@ -10,6 +10,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -49,6 +50,10 @@ struct qma_cuda_model {
     const float *out_norm = nullptr;
     qma::LayerW L[qma::NLAYER];
     size_t weight_bytes = 0;
+    // expert-cache holds (qma_ecache_hold / _release, ecache.c:500-520):
+    // bookkeeping only, every record stays resident for the model's life
+    std::mutex ec_mu;
+    int ec_held = 0;
 };
 
 constexpr int ARG_CTAS = 64;      // CTAs of the greedy argmax
@@ -87,6 +92,7 @@ struct qma_cuda_state {
     unsigned *argmax_cnt = nullptr;     // ticket, zero between steps
     unsigned *gdn_cnt = nullptr;        // [16] gated-norm tickets, zero between layers
     float *gdn_kq = nullptr;            // [MAX_CHUNK][16] k . q of a prefill chunk
+    float *gdn_chunk = nullptr;         // chunked gated-delta scratch (W, U, P, G of a prefill chunk)
     // attention scratch, grown on demand
     float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr, *ml = nullptr;
     size_t scores_cap = 0, cmax_cap = 0, opart_cap = 0, lpart_cap = 0;
@@ -480,6 +486,7 @@ static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
     TRY(salloc_t(s, &s->argmax_cnt, 1, st));
     TRY(salloc_t(s, &s->gdn_cnt, VHEADS / 2, st));
     TRY(salloc_t(s, &s->gdn_kq, size_t(MAX_CHUNK) * KHEADS, st));
+    TRY(salloc_t(s, &s->gdn_chunk, gdn_chunk_scratch_bytes() / sizeof(float), st));
     s->logits_rows = 1;
     TRY(salloc_t(s, &s->logits, size_t(m->n_vocab), st));
 #undef TRY
@@ -725,6 +732,72 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
     }
 }
 
+// The mixer half of layer il (gated delta net or gated attention) on the
+// T tokens whose normed Q8_K input is in s->xq / xd / xs and residual in
+// s->x; writes the residual after it to s->x2 (nn.c:2107-2246).
+// side_pending: a salience update of an earlier attention layer is still
+// running on s->side (joined here before the next one starts).
+static int mixer(qma_cuda_state *s, int il, int T, int nk_cap, int pv_chunk, bool &side_pending) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    const LayerW &L = m->L[il];
+    int rc;
+#define TRY(x) do { if ((rc = (x))) return rc; } while (0)
+    // a single token's gated-delta-net conv runs in the input projection's epilogue
+    ConvEpi ce;
+    const bool conv_fused = !is_attn(il) && T == 1 && pdl_enabled();
+    if (conv_fused) {
+        ce.w = L.conv1d;
+        ce.state = s->conv[il];
+        ce.out = s->conv_out;
+        ce.n = CONV_DIM;
+    }
+    TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st, nullptr,
+               conv_fused ? &ce : nullptr));
+    if (is_attn(il)) {
+        const int lay = il / 4;
+        if (side_pending) {
+            // the previous layer's salience reads `scores` and writes
+            // the slot this append resets
+            QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
+            side_pending = false;
+        }
+        TRY(launch_qk_prep_append(s->proj, L.in_rows, L.q_norm, L.k_norm, s->rope, s->sp_dev, T,
+                                  s->qr, s->z, s->kv[lay], s->qf, s->sal, st));
+        AttnArgs a;
+        a.qr = s->qr; a.kv = s->kv[lay]; a.arena = s->arena[lay]; a.live = s->live_dev;
+        a.sp = s->sp_dev; a.T = T; a.nk_max = nk_cap; a.pv_chunk = pv_chunk;
+        a.scores = s->scores; a.cmax = s->cmax; a.opart = s->opart; a.lpart = s->lpart;
+        a.ml = s->ml; a.z = s->z; a.xq = s->xq; a.xd = s->xd; a.xs = s->xs;
+        a.sal = s->sal + size_t(lay) * s->n_ctx;
+        a.pin_sal = s->pin_sal + size_t(lay) * HCM_H_PIN;
+        TRY(launch_attention(a, st));
+        QMA_CHECK_CUDA(cudaEventRecord(s->ev_fork, st));
+        QMA_CHECK_CUDA(cudaStreamWaitEvent(s->side, s->ev_fork, 0));
+        TRY(launch_salience(a, s->side));
+        QMA_CHECK_CUDA(cudaEventRecord(s->ev_join, s->side));
+        side_pending = true;
+        TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
+    } else {
+        const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
+        if (!conv_fused) TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
+        if (T == 1) {
+            // one token: the gated norm + Q8_K run in the recurrence kernel's tail
+            const GdnNormArgs gna = {s->proj + CONV_DIM, L.ssm_norm, s->xq, s->xd, s->xs, s->gdn_cnt};
+            TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
+                           L.dt, L.a, s->ssm[il], T, s->gdo, st, &gna));
+        } else {
+            TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
+                           L.dt, L.a, s->ssm[il], T, s->gdo, st, nullptr, s->gdn_kq, s->gdn_chunk));
+            TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
+                                        s->xs, st));
+        }
+        TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
+    }
+#undef TRY
+    return QMA_CUDA_OK;
+}
+
 // The forward of T tokens at the positions in *sp_dev (host copy hs):
 // embedding -> 40 layers -> (optionally) final norm + LM head.
 static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
@@ -759,57 +832,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
         const LayerW &L = m->L[il];
         if (!normed) TRY(launch_rmsnorm_quant(s->x, L.attn_norm, T, EMBD, s->xq, s->xd, s->xs, st, plan(il)));
         normed = false;
-        // a single token's gated-delta-net conv runs in the input projection's epilogue
-        ConvEpi ce;
-        const bool conv_fused = !is_attn(il) && T == 1 && pdl_enabled();
-        if (conv_fused) {
-            ce.w = L.conv1d;
-            ce.state = s->conv[il];
-            ce.out = s->conv_out;
-            ce.n = CONV_DIM;
-        }
-        TRY(matvec(L.in_type, L.in_proj, EMBD, L.in_rows, T, s->xq, s->xd, s->xs, s->proj, st, nullptr,
-                   conv_fused ? &ce : nullptr));
-        if (is_attn(il)) {
-            const int lay = il / 4;
-            if (side_pending) {
-                // the previous layer's salience reads `scores` and writes
-                // the slot this append resets
-                QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
-                side_pending = false;
-            }
-            TRY(launch_qk_prep_append(s->proj, L.in_rows, L.q_norm, L.k_norm, s->rope, s->sp_dev, T,
-                                      s->qr, s->z, s->kv[lay], s->qf, s->sal, st));
-            AttnArgs a;
-            a.qr = s->qr; a.kv = s->kv[lay]; a.arena = s->arena[lay]; a.live = s->live_dev;
-            a.sp = s->sp_dev; a.T = T; a.nk_max = nk_cap; a.pv_chunk = pv_chunk;
-            a.scores = s->scores; a.cmax = s->cmax; a.opart = s->opart; a.lpart = s->lpart;
-            a.ml = s->ml; a.z = s->z; a.xq = s->xq; a.xd = s->xd; a.xs = s->xs;
-            a.sal = s->sal + size_t(lay) * s->n_ctx;
-            a.pin_sal = s->pin_sal + size_t(lay) * HCM_H_PIN;
-            TRY(launch_attention(a, st));
-            QMA_CHECK_CUDA(cudaEventRecord(s->ev_fork, st));
-            QMA_CHECK_CUDA(cudaStreamWaitEvent(s->side, s->ev_fork, 0));
-            TRY(launch_salience(a, s->side));
-            QMA_CHECK_CUDA(cudaEventRecord(s->ev_join, s->side));
-            side_pending = true;
-            TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
-        } else {
-            const int ld = L.in_rows;     // qkv 8192 | gate 4096 | beta 32 | alpha 32
-            if (!conv_fused) TRY(launch_conv1d(s->proj, ld, L.conv1d, s->conv[il], T, s->conv_out, st));
-            if (T == 1) {
-                // one token: the gated norm + Q8_K run in the recurrence kernel's tail
-                const GdnNormArgs gna = {s->proj + CONV_DIM, L.ssm_norm, s->xq, s->xd, s->xs, s->gdn_cnt};
-                TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
-                               L.dt, L.a, s->ssm[il], T, s->gdo, st, &gna));
-            } else {
-                TRY(launch_gdn(s->conv_out, s->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS,
-                               L.dt, L.a, s->ssm[il], T, s->gdo, st, nullptr, s->gdn_kq));
-                TRY(launch_gated_norm_quant(s->gdo, s->proj + CONV_DIM, ld, L.ssm_norm, T, s->xq, s->xd,
-                                            s->xs, st));
-            }
-            TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, s->xq, s->xd, s->xs, s->x2, st, s->x));
-        }
+        TRY(mixer(s, il, T, nk_cap, pv_chunk, side_pending));
         if (il == n_layers - 1 && s->stop_before_moe) {
             // parity aid: return the residual after the mixer of this layer
             QMA_CHECK_CUDA(cudaMemcpyAsync(s->x, s->x2, sizeof(float) * size_t(T) * EMBD,
@@ -963,6 +986,44 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
     return check_wait_timeouts();
 }
 
+// One layer's mixer on caller activations (the layer-level parity points):
+// x [T][2048] device residual input at the state's positions n_pos ..
+// n_pos + T - 1; out [T][2048] device residual after the mixer.  With
+// advance, the live index is rebuilt first when due (as qma_eval does at a
+// chunk start, nn.c:2074-2088) and n_pos moves on by T afterwards.
+static int mixer_call(qma_cuda_state *s, int il, const float *x, int T, float *out, bool advance) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    if (s->n_pos + T > s->n_ctx - HCM_SINK) {
+        set_error("mixer: %d + %d positions exceed this state's ring of %d (no wrap-around)", s->n_pos, T,
+                  s->n_ctx);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    int rc;
+    const int pos_now = s->n_pos;
+    if (advance && (rc = maybe_rebuild(s, pos_now))) return rc;
+    if (is_attn(il))
+        for (int t = 0; t < T; t++) s->tier[hcm_slot(pos_now + t, s->n_ctx)] = 2;   // kv_append
+    fill_params(s, *s->sp_host, pos_now, T, 0);
+    QMA_CHECK_CUDA(cudaMemcpyAsync(s->sp_dev, s->sp_host, sizeof(StepParams), cudaMemcpyHostToDevice, st));
+    const int nk = nk_upper(s, pos_now, T, false);
+    if ((rc = ensure_attn_scratch(s, T, nk, attn_span(T, nk)))) return rc;
+    QMA_CHECK_CUDA(cudaMemcpyAsync(s->x, x, sizeof(float) * size_t(T) * EMBD, cudaMemcpyDeviceToDevice, st));
+    if ((rc = launch_rmsnorm_quant(s->x, m->L[il].attn_norm, T, EMBD, s->xq, s->xd, s->xs, st))) return rc;
+    bool side_pending = false;
+    if ((rc = mixer(s, il, T, nk, attn_span(T, nk), side_pending))) return rc;
+    if (side_pending) QMA_CHECK_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
+    QMA_CHECK_CUDA(cudaMemcpyAsync(out, s->x2, sizeof(float) * size_t(T) * EMBD, cudaMemcpyDeviceToDevice, st));
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if (advance) s->n_pos += T;
+    if (s->graph) {          // the decode graph's step parameters are stale now
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    return check_wait_timeouts();
+}
+
 // Capture one decode step (T = 1, token and position read from sp_dev,
 // argmax writes the next token and advances the position) as a graph.
 static int capture_decode(qma_cuda_state *s) {
@@ -1101,6 +1162,89 @@ int qma_cuda_ecache_get(const qma_cuda_model *m, int layer, int expert, const vo
     return QMA_CUDA_OK;
 }
 
+namespace qma {
+
+constexpr int EC_PF_MAX = 64;      // ecache.h:52
+
+// One CTA: thread i asks L2 for record i / 3 of the list (its gate, up or
+// down matrix), as a speculative fill with no completion to wait for.
+struct EcRange {
+    const void *p[3 * EC_PF_MAX];
+    uint32_t bytes[3 * EC_PF_MAX];
+};
+__global__ void ecache_l2_fill_kernel(EcRange r, int n) {
+    const int i = threadIdx.x;
+    if (i < n) prefetch_l2_range(r.p[i], r.bytes[i]);
+}
+
+static int ecache_fill(const qma_cuda_model *m, int layer, const int *ids, int n, void *stream, const char *fn) {
+    QMA_REQUIRE(m && layer >= 0 && layer < NLAYER && n >= 0 && (ids || n == 0), "%s: bad arguments", fn);
+    if (n > EC_PF_MAX) n = EC_PF_MAX;        // as the reference clamps (ecache.c:406)
+    const qma_cuda_moe_weights &w = m->L[layer].moe;
+    const size_t gu = size_t(MOE_FF) * (MOE_EMBD / 256) * Q4K_BYTES;
+    const size_t dn = packed_bytes(w.down_type, MOE_EMBD, MOE_FF);
+    EcRange r{};
+    int k = 0;
+    for (int i = 0; i < n; i++) {
+        QMA_REQUIRE(ids[i] >= 0 && ids[i] < MOE_NEXP, "%s: expert id %d", fn, ids[i]);
+        r.p[k] = static_cast<const uint8_t *>(w.gate_exps) + gu * ids[i];
+        r.bytes[k++] = uint32_t(gu);
+        r.p[k] = static_cast<const uint8_t *>(w.up_exps) + gu * ids[i];
+        r.bytes[k++] = uint32_t(gu);
+        r.p[k] = static_cast<const uint8_t *>(w.down_exps) + dn * ids[i];
+        r.bytes[k++] = uint32_t(dn);
+    }
+    if (!k) return QMA_CUDA_OK;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    ecache_l2_fill_kernel<<<1, 3 * EC_PF_MAX, 0, as_stream(stream)>>>(r, k);
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+}  // namespace qma
+
+int qma_cuda_ecache_hint(const qma_cuda_model *m, int layer, const int *ids, int n, void *stream) {
+    qma::clear_error();
+    return qma::ecache_fill(m, layer, ids, n, stream, "qma_cuda_ecache_hint");
+}
+
+int qma_cuda_ecache_prefetch(const qma_cuda_model *m, int layer, const int *ids, int n, void *stream) {
+    qma::clear_error();
+    return qma::ecache_fill(m, layer, ids, n, stream, "qma_cuda_ecache_prefetch");
+}
+
+int qma_cuda_ecache_hold(qma_cuda_model *m, int layer, int expert, const void **gate, const void **up,
+                         const void **down) {
+    qma::clear_error();
+    QMA_REQUIRE(m, "qma_cuda_ecache_hold: null model");
+    {
+        std::lock_guard<std::mutex> lock(m->ec_mu);
+        if (m->ec_held >= qma::EC_PF_MAX) {
+            qma::set_error("qma_cuda_ecache_hold: %d records held already (at most %d until a release)",
+                           m->ec_held, qma::EC_PF_MAX);
+            return QMA_CUDA_ERR_STATE;
+        }
+        const int rc = qma_cuda_ecache_get(m, layer, expert, gate, up, down);
+        if (rc) return rc;
+        m->ec_held++;
+    }
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_ecache_release(qma_cuda_model *m) {
+    qma::clear_error();
+    QMA_REQUIRE(m, "qma_cuda_ecache_release: null model");
+    std::lock_guard<std::mutex> lock(m->ec_mu);
+    m->ec_held = 0;
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_ecache_held(const qma_cuda_model *m) {
+    if (!m) return -1;
+    std::lock_guard<std::mutex> lock(const_cast<qma_cuda_model *>(m)->ec_mu);
+    return m->ec_held;
+}
+
 int qma_cuda_model_moe_weights(const qma_cuda_model *m, int layer, qma_cuda_moe_weights *out) {
     qma::clear_error();
     QMA_REQUIRE(m && out && layer >= 0 && layer < qma::NLAYER, "qma_cuda_model_moe_weights: bad layer %d", layer);
@@ -1174,6 +1318,24 @@ int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens
     const int rc = qma::eval(s, tokens, n_tokens, nullptr, 0, n_layers < 0 ? -n_layers : n_layers, hidden);
     s->stop_before_moe = false;
     return rc;
+}
+
+int qma_cuda_gdn_step(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance) {
+    qma::clear_error();
+    QMA_REQUIRE(s && x && x_out && layer >= 0 && layer < qma::NLAYER && !qma::is_attn(layer) && n_tokens >= 1 &&
+                    n_tokens <= qma::MAX_CHUNK,
+                "qma_cuda_gdn_step: bad arguments (layer %d must be a gated-delta-net layer, 1..%d tokens)", layer,
+                qma::MAX_CHUNK);
+    return qma::mixer_call(s, layer, x, n_tokens, x_out, advance != 0);
+}
+
+int qma_cuda_attn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance) {
+    qma::clear_error();
+    QMA_REQUIRE(s && x && x_out && layer >= 0 && layer < qma::NLAYER && qma::is_attn(layer) && n_tokens >= 1 &&
+                    n_tokens <= qma::MAX_CHUNK,
+                "qma_cuda_attn_decode: bad arguments (layer %d must be an attention layer, 1..%d tokens)", layer,
+                qma::MAX_CHUNK);
+    return qma::mixer_call(s, layer, x, n_tokens, x_out, advance != 0);
 }
 
 int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,

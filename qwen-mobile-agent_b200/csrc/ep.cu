@@ -230,13 +230,17 @@ int ep_settle(qma_cuda_ep *ep, ncclResult_t r, const char *what) {
         const ncclResult_t q = ncclCommGetAsyncError(ep->comm, &st);
         r = q != ncclSuccess ? q : st;
         if (r != ncclInProgress) break;
-        if (ms_since(t0) > ep->timeout_ms) {
+        const int el = ms_since(t0);
+        if (el > ep->timeout_ms) {
             ep_abort(ep);
             qma::set_error("%s: no answer from the other ranks within %d ms (communicator aborted)", what,
                            ep->timeout_ms);
             return QMA_CUDA_ERR_TIMEOUT;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        // a transfer enqueue settles within microseconds: poll without
+        // sleeping at first, then back off (connection set-up, a slow peer)
+        if (el < 20) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(200));
     }
     if (r == ncclSuccess) return QMA_CUDA_OK;
     qma::set_error("%s: %s", what, ncclGetErrorString(r));
@@ -267,13 +271,15 @@ int ep_sync(qma_cuda_ep *ep, cudaStream_t st) {
             ep_abort(ep);
             return QMA_CUDA_ERR_CUDA;
         }
-        if (ms_since(t0) > ep->timeout_ms) {
+        const int el = ms_since(t0);
+        if (el > ep->timeout_ms) {
             ep_abort(ep);
             qma::set_error("qma_cuda_ep_moe_layer: the exchange did not finish within %d ms (communicator aborted)",
                            ep->timeout_ms);
             return QMA_CUDA_ERR_TIMEOUT;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (el < 20) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(100));
     }
 }
 

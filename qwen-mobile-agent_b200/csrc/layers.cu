@@ -473,9 +473,282 @@ __global__ void __launch_bounds__(256) gdn_seq_kernel(const float *__restrict__ 
         reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
 }
 
+// ------------------------------------- gated delta net, chunked form -------
+// The recurrence of gdn_kernel per V-head h over a chunk of C tokens, in the
+// chunked form of the gated delta rule (Yang, Kautz, Hatamizadeh, "Gated
+// Delta Networks", 2024: the WY / UT-transform representation).  With the
+// state S (k-dim i x v-dim j; the engine stores M[j][i] = S[i][j]), per
+// token  S_t = e_t (I - b_t k_t k_t^T) S_{t-1} + b_t k_t v_t^T  and
+// o_t = S_t^T q_t / sqrt(128)  (gdn_worker, nn.c:784-833).  Inside a chunk
+// that starts from S_0, with G_t = g_0 + .. + g_t (e_t = exp(g_t)):
+//   delta_t = b_t (v_t - e_t S_{t-1}^T k_t)      satisfies
+//   (I + A) Delta = diag(b) V - diag(b exp(G)) K S_0,
+//   A[t][s] = b_t exp(G_t - G_s) k_t . k_s  (s < t), so with
+//   W = (I + A)^-1 diag(b exp(G)) K,  U = (I + A)^-1 diag(b) V:
+//   Delta = U - W S_0
+//   o_t   = (exp(G_t) q_t^T S_0 + sum_{s<=t} exp(G_t - G_s) (q_t . k_s) delta_s) / sqrt(128)
+//   S_C   = exp(G_last) S_0 + sum_s exp(G_last - G_s) k_s delta_s^T.
+// Everything but the last three lines is independent of S_0, so
+// gdn_chunk_prep_kernel forms W, U and P[t][s] = exp(G_t - G_s) (q_t . k_s)
+// for all chunks at once, and gdn_chunk_scan_kernel walks the chunks in
+// order, each CTA owning 32 state columns j of one head (columns are
+// independent).  fp32 throughout; the decays appear only as exp of
+// non-positive differences (no under- or overflow from long products).
+constexpr int GC = 64;                 // tokens per chunk
+constexpr int GC_MAX_CHUNKS = MAX_CHUNK / GC;
+
+struct GdnChunkBufs {
+    float *W;      // [32 heads][chunks][GC][128]
+    float *U;      // [32][chunks][GC][128]
+    float *P;      // [32][chunks][GC][GC]
+    float *G;      // [32][chunks][GC]
+};
+
+__device__ __forceinline__ float gdn_beta(const float *proj, int proj_ld, int beta_off, int t, int h) {
+    const float braw = proj[size_t(t) * proj_ld + beta_off + h];
+    return 1.0f / (1.0f + expf(-braw));
+}
+__device__ __forceinline__ float gdn_g(const float *proj, int proj_ld, int alpha_off, int t, int h, float dth,
+                                       float ah) {
+    const float a = proj[size_t(t) * proj_ld + alpha_off + h] + dth;
+    const float sp = a > 20.0f ? a : log1pf(expf(a));
+    return __fmul_rn(sp, ah);
+}
+
+constexpr int GCP_LD = SSTATE + 1;     // padded row of the prep kernel's q / k tiles
+constexpr size_t GDN_PREP_SMEM = sizeof(float) * (2 * GC * GCP_LD + GC * (GC + 1) + 3 * GC);
+
+// Grid (chunks, 32 V-heads), 256 threads.  q / k are already L2-normed in
+// conv_out (gdn_prep_kernel).
+__global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const float *__restrict__ conv_out,
+                                                             const float *__restrict__ proj, int proj_ld,
+                                                             int beta_off, int alpha_off,
+                                                             const float *__restrict__ dt,
+                                                             const float *__restrict__ av, int T,
+                                                             GdnChunkBufs bufs) {
+    extern __shared__ __align__(16) float gsm[];
+    float *Ks = gsm;                              // [GC][GCP_LD]
+    float *Qs = Ks + GC * GCP_LD;                 // [GC][GCP_LD]
+    float *As = Qs + GC * GCP_LD;                 // [GC][GC + 1]
+    float *Gs = As + GC * (GC + 1);               // [GC]
+    float *Bs = Gs + GC;                          // [GC] beta
+    float *EGs = Bs + GC;                         // [GC] beta * exp(G)
+    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qh = h % KHEADS, nch = gridDim.x;
+    const int t0 = c * GC, n = min(GC, T - t0);
+    pdl_trigger();
+    pdl_wait();
+    for (int idx = tid; idx < GC * SSTATE; idx += 256) {
+        const int t = idx / SSTATE, i = idx % SSTATE;
+        const float *co = conv_out + size_t(t0 + t) * CONV_DIM;
+        Qs[t * GCP_LD + i] = t < n ? co[qh * SSTATE + i] : 0.0f;
+        Ks[t * GCP_LD + i] = t < n ? co[KEY_DIM + qh * SSTATE + i] : 0.0f;
+    }
+    if (warp == 0) {
+        // G: inclusive prefix sum of g over the chunk (two tokens per lane)
+        const float dth = dt[h], ah = av[h];
+        float g0 = 0.0f, g1 = 0.0f;
+        if (2 * lane < n) g0 = gdn_g(proj, proj_ld, alpha_off, t0 + 2 * lane, h, dth, ah);
+        if (2 * lane + 1 < n) g1 = gdn_g(proj, proj_ld, alpha_off, t0 + 2 * lane + 1, h, dth, ah);
+        float incl = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const float ex = incl - (g0 + g1);
+        Gs[2 * lane] = ex + g0;
+        Gs[2 * lane + 1] = ex + g0 + g1;
+    }
+    __syncthreads();
+    if (tid < GC) {
+        const float b = tid < n ? gdn_beta(proj, proj_ld, beta_off, t0 + tid, h) : 0.0f;
+        Bs[tid] = b;
+        EGs[tid] = b * expf(Gs[tid]);
+    }
+    // k_t . k_s and q_t . k_s: thread (r, l) owns t = r + 16 a, s = l + 16 b
+    {
+        const int r = tid >> 4, l = tid & 15;
+        float kk[4][4] = {}, qk[4][4] = {};
+        for (int i = 0; i < SSTATE; i++) {
+            float kt[4], qt[4], ks[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                kt[a] = Ks[(r + 16 * a) * GCP_LD + i];
+                qt[a] = Qs[(r + 16 * a) * GCP_LD + i];
+                ks[a] = Ks[(l + 16 * a) * GCP_LD + i];
+            }
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int b = 0; b < 4; b++) {
+                    kk[a][b] = fmaf(kt[a], ks[b], kk[a][b]);
+                    qk[a][b] = fmaf(qt[a], ks[b], qk[a][b]);
+                }
+        }
+        __syncthreads();                          // Gs, Bs visible
+        float *P = bufs.P + (size_t(h) * nch + c) * GC * GC;
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int t = r + 16 * a, s2 = l + 16 * b;
+                const float dec = s2 <= t && t < n ? expf(Gs[t] - Gs[s2]) : 0.0f;
+                As[t * (GC + 1) + s2] = s2 < t ? Bs[t] * dec * kk[a][b] : 0.0f;
+                P[t * GC + s2] = dec * qk[a][b];
+            }
+    }
+    __syncthreads();
+    // forward substitution X_t = R_t - sum_{s<t} A[t][s] X_s, one column per
+    // thread: columns 0..127 of W (R_t = b_t exp(G_t) k_t), of U (R_t = b_t v_t)
+    {
+        const int col = tid & (SSTATE - 1);
+        const bool isU = tid >= SSTATE;
+        float x[GC];
+#pragma unroll
+        for (int t = 0; t < GC; t++) {
+            float acc;
+            if (isU)
+                acc = t < n ? Bs[t] * conv_out[size_t(t0 + t) * CONV_DIM + 2 * KEY_DIM + h * SSTATE + col] : 0.0f;
+            else
+                acc = EGs[t] * Ks[t * GCP_LD + col];
+#pragma unroll
+            for (int s2 = 0; s2 < t; s2++) acc = fmaf(-As[t * (GC + 1) + s2], x[s2], acc);
+            x[t] = acc;
+        }
+        float *dst = (isU ? bufs.U : bufs.W) + (size_t(h) * nch + c) * GC * SSTATE + col;
+#pragma unroll
+        for (int t = 0; t < GC; t++) dst[t * SSTATE] = x[t];
+    }
+    if (tid < GC) bufs.G[(size_t(h) * nch + c) * GC + tid] = Gs[tid];
+}
+
+// Grid (4 column blocks, 32 V-heads), 256 threads: thread (jl = tid / 8,
+// part = tid % 8) holds M[j][part * 16 .. + 15] of state row j = 32 * block
+// + jl through all chunks, as gdn_seq_kernel does.
+constexpr size_t GDN_SCAN_SMEM =
+    sizeof(float) * (3 * GC * SSTATE + GC * 32 + GC * (GC + 1) + 2 * GC * 33 + 2 * GC);
+
+__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const float *__restrict__ conv_out, int T,
+                                                             GdnChunkBufs bufs, float *ssm, float *o) {
+    QMA_TRACE_SCOPE(TK_GDN);
+    extern __shared__ __align__(16) float gsm[];
+    float *Ws = gsm;                              // [GC][128]
+    float *Qs = Ws + GC * SSTATE;                 // [GC][128]
+    float *Ks = Qs + GC * SSTATE;                 // [GC][128]
+    float *Us = Ks + GC * SSTATE;                 // [GC][32]
+    float *Ps = Us + GC * 32;                     // [GC][GC + 1]
+    float *Ds = Ps + GC * (GC + 1);               // [GC][33] delta
+    float *QSs = Ds + GC * 33;                    // [GC][33] q^T S_0
+    float *Gs = QSs + GC * 33;                    // [GC]
+    float *DEC = Gs + GC;                         // [GC] exp(G_last - G_s)
+    const int rb = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int qh = h % KHEADS, jl = tid >> 3, part = tid & 7, j = rb * 32 + jl;
+    const int nch = (T + GC - 1) / GC;
+    const float scale = 1.0f / sqrtf(float(SSTATE));
+    pdl_trigger();
+    pdl_wait();
+    float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
+    float M[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float4 v = reinterpret_cast<const float4 *>(Mrow)[k];
+        M[4 * k] = v.x; M[4 * k + 1] = v.y; M[4 * k + 2] = v.z; M[4 * k + 3] = v.w;
+    }
+    for (int c = 0; c < nch; c++) {
+        const int t0 = c * GC, n = min(GC, T - t0);
+        const size_t cb = size_t(h) * nch + c;
+        __syncthreads();                          // the previous chunk is consumed
+        for (int idx = tid; idx < GC * SSTATE / 4; idx += 256) {
+            const int t = idx / (SSTATE / 4), i4 = idx % (SSTATE / 4);
+            reinterpret_cast<float4 *>(Ws)[idx] = reinterpret_cast<const float4 *>(bufs.W + cb * GC * SSTATE)[idx];
+            float4 qv = make_float4(0.f, 0.f, 0.f, 0.f), kv = qv;
+            if (t < n) {
+                const float *co = conv_out + size_t(t0 + t) * CONV_DIM;
+                qv = reinterpret_cast<const float4 *>(co + qh * SSTATE)[i4];
+                kv = reinterpret_cast<const float4 *>(co + KEY_DIM + qh * SSTATE)[i4];
+            }
+            reinterpret_cast<float4 *>(Qs)[idx] = qv;
+            reinterpret_cast<float4 *>(Ks)[idx] = kv;
+        }
+        for (int idx = tid; idx < GC * 32; idx += 256) {
+            const int t = idx / 32, jj = idx % 32;
+            Us[idx] = bufs.U[(cb * GC + t) * SSTATE + rb * 32 + jj];
+        }
+        for (int idx = tid; idx < GC * GC; idx += 256) {
+            const int t = idx / GC, s2 = idx % GC;
+            Ps[t * (GC + 1) + s2] = bufs.P[cb * GC * GC + idx];
+        }
+        if (tid < GC) Gs[tid] = bufs.G[cb * GC + tid];
+        __syncthreads();
+        if (tid < GC) DEC[tid] = tid < n ? expf(Gs[n - 1] - Gs[tid]) : 0.0f;
+        // delta_t = U_t - W_t^T S_0 and q_t^T S_0 for this thread's row j
+        for (int t = 0; t < n; t++) {
+            const float4 *wr = reinterpret_cast<const float4 *>(Ws + t * SSTATE + part * 16);
+            const float4 *qr = reinterpret_cast<const float4 *>(Qs + t * SSTATE + part * 16);
+            float dw = 0.0f, dq = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 w4 = wr[k], q4 = qr[k];
+                dw = fmaf(w4.x, M[4 * k], dw); dw = fmaf(w4.y, M[4 * k + 1], dw);
+                dw = fmaf(w4.z, M[4 * k + 2], dw); dw = fmaf(w4.w, M[4 * k + 3], dw);
+                dq = fmaf(q4.x, M[4 * k], dq); dq = fmaf(q4.y, M[4 * k + 1], dq);
+                dq = fmaf(q4.z, M[4 * k + 2], dq); dq = fmaf(q4.w, M[4 * k + 3], dq);
+            }
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                dw += __shfl_xor_sync(0xffffffffu, dw, off);
+                dq += __shfl_xor_sync(0xffffffffu, dq, off);
+            }
+            if (part == 0) {
+                Ds[t * 33 + jl] = Us[t * 32 + jl] - dw;
+                QSs[t * 33 + jl] = dq;
+            }
+        }
+        __syncthreads();
+        // o_t = (exp(G_t) q_t^T S_0 + sum_{s<=t} P[t][s] delta_s) * scale, the 8
+        // threads of a row taking t = part, part + 8, ..
+        for (int t = part; t < n; t += 8) {
+            float acc = expf(Gs[t]) * QSs[t * 33 + jl];
+            for (int s2 = 0; s2 <= t; s2++) acc = fmaf(Ps[t * (GC + 1) + s2], Ds[s2 * 33 + jl], acc);
+            o[size_t(t0 + t) * VAL_DIM + h * SSTATE + j] = acc * scale;
+        }
+        // S_C = exp(G_last) S_0 + sum_s exp(G_last - G_s) k_s delta_s^T
+        const float el = expf(Gs[n - 1]);
+#pragma unroll
+        for (int i = 0; i < 16; i++) M[i] *= el;
+        for (int s2 = 0; s2 < n; s2++) {
+            const float cf = DEC[s2] * Ds[s2 * 33 + jl];
+            const float4 *kr = reinterpret_cast<const float4 *>(Ks + s2 * SSTATE + part * 16);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 k4 = kr[k];
+                M[4 * k] = fmaf(cf, k4.x, M[4 * k]); M[4 * k + 1] = fmaf(cf, k4.y, M[4 * k + 1]);
+                M[4 * k + 2] = fmaf(cf, k4.z, M[4 * k + 2]); M[4 * k + 3] = fmaf(cf, k4.w, M[4 * k + 3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
+}
+
+// QMA_CUDA_GDN_SEQ=1 in the environment: chunks of tokens run the
+// token-sequential recurrence (gdn_seq_kernel) instead of the chunked form,
+// as a cross-check (same results up to fp32 rounding).
+static bool gdn_sequential() {
+    const char *v = getenv("QMA_CUDA_GDN_SEQ");
+    return v && atoi(v) != 0;
+}
+
+size_t gdn_chunk_scratch_bytes() {
+    const size_t per = size_t(VHEADS) * GC_MAX_CHUNKS;
+    return sizeof(float) * per * (2 * GC * SSTATE + GC * GC + GC);
+}
+
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
                const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
-               const GdnNormArgs *norm, float *kq_scratch) {
+               const GdnNormArgs *norm, float *kq_scratch, float *chunk_scratch) {
     GdnNorm gn;
     if (norm && T == 1) {
         gn.z = norm->z;
@@ -489,6 +762,29 @@ int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_o
         // the conv output is normed in place: only this path reads it after
         QMA_CHECK_CUDA(launch_ex(gdn_prep_kernel, dim3(T, KHEADS), dim3(256), 0, st, 1, pdl_enabled(),
                                  const_cast<float *>(conv_out), kq_scratch));
+        if (chunk_scratch && T <= MAX_CHUNK && !gdn_sequential()) {
+            static PerDevice attr;
+            if (!attr.done()) {
+                QMA_CHECK_CUDA(cudaFuncSetAttribute(gdn_chunk_prep_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(GDN_PREP_SMEM)));
+                QMA_CHECK_CUDA(cudaFuncSetAttribute(gdn_chunk_scan_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(GDN_SCAN_SMEM)));
+                attr.mark();
+            }
+            const int nch = (T + GC - 1) / GC;
+            GdnChunkBufs b;
+            const size_t per = size_t(VHEADS) * nch;
+            b.W = chunk_scratch;
+            b.U = b.W + per * GC * SSTATE;
+            b.P = b.U + per * GC * SSTATE;
+            b.G = b.P + per * GC * GC;
+            QMA_CHECK_CUDA(launch_ex(gdn_chunk_prep_kernel, dim3(nch, VHEADS), dim3(256), GDN_PREP_SMEM, st, 1,
+                                     pdl_enabled(), conv_out, proj, proj_ld, beta_off, alpha_off, dt, a, T, b));
+            QMA_CHECK_CUDA(launch_ex(gdn_chunk_scan_kernel, dim3(4, VHEADS), dim3(256), GDN_SCAN_SMEM, st, 1,
+                                     pdl_enabled(), conv_out, T, b, ssm, o));
+            QMA_CHECK_LAUNCH();
+            return QMA_CUDA_OK;
+        }
         QMA_CHECK_CUDA(launch_ex(gdn_seq_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj,
                                  proj_ld, beta_off, alpha_off, dt, a, kq_scratch, ssm, T, o));
         QMA_CHECK_LAUNCH();

@@ -68,9 +68,11 @@ struct GdnNormArgs {
 };
 int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
                const float *dt, const float *a, float *ssm, int T, float *o, cudaStream_t st,
-               const GdnNormArgs *norm = nullptr, float *kq_scratch = nullptr);
-// (T > 1 with kq_scratch [T][16]: the two-kernel chunk form, which norms q
-// and k in place in conv_out.)
+               const GdnNormArgs *norm = nullptr, float *kq_scratch = nullptr, float *chunk_scratch = nullptr);
+// (T > 1 with kq_scratch [T][16]: q and k are L2-normed in place in conv_out
+// first; then, with chunk_scratch (gdn_chunk_scratch_bytes(), T <= 512), the
+// chunked gated-delta form, else the token-sequential recurrence.)
+size_t gdn_chunk_scratch_bytes();
 int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
                             int8_t *xq, float *xd, int16_t *xs, cudaStream_t st);
 

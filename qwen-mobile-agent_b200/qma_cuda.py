@@ -59,12 +59,19 @@ _SIGS.update({
     "qma_cuda_model_free": (_i32, [_vp]),
     "qma_cuda_model_n_vocab": (_i32, [_vp]),
     "qma_cuda_ecache_get": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "qma_cuda_ecache_hint": (_i32, [_vp, _i32, _vp, _i32, _vp]),
+    "qma_cuda_ecache_prefetch": (_i32, [_vp, _i32, _vp, _i32, _vp]),
+    "qma_cuda_ecache_hold": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "qma_cuda_ecache_release": (_i32, [_vp]),
+    "qma_cuda_ecache_held": (_i32, [_vp]),
     "qma_cuda_state_create": (_i32, [_vp, _i32, C.POINTER(_vp)]),
     "qma_cuda_state_free": (_i32, [_vp]),
     "qma_cuda_state_n_pos": (_i32, [_vp]),
     "qma_cuda_eval": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32]),
     "qma_cuda_decode_greedy": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
     "qma_cuda_eval_hidden": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "qma_cuda_gdn_step": (_i32, [_vp, _i32, _vp, _i32, _vp, _i32]),
+    "qma_cuda_attn_decode": (_i32, [_vp, _i32, _vp, _i32, _vp, _i32]),
     "qma_cuda_state_stream": (_vp, [_vp]),
     "qma_cuda_state_kv_slot": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "qma_cuda_state_stats": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_u64)]),

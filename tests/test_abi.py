@@ -110,3 +110,15 @@ def test_expert_parallel_init_timeout_argument():
     h = C.c_void_p()
     assert lib.qma_cuda_ep_init_timeout(0, uid, 0, 2, 8, 0, C.byref(h)) == Q.ERR_INVALID
     assert "timeout" in Q.last_error()
+
+
+def test_layer_entry_points_and_ecache_reject_bad_arguments():
+    lib = Q.lib()
+    assert lib.qma_cuda_gdn_step(None, 0, 1, 1, 1, 1) == Q.ERR_INVALID
+    assert "qma_cuda_gdn_step" in Q.last_error()
+    assert lib.qma_cuda_attn_decode(None, 3, 1, 1, 1, 1) == Q.ERR_INVALID
+    assert lib.qma_cuda_ecache_hint(None, 0, None, 0, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ecache_prefetch(None, 0, None, 0, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ecache_hold(None, 0, 0, None, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ecache_release(None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ecache_held(None) == -1

@@ -531,3 +531,210 @@ def test_model_moe_weights_run_the_layer_moe_block(full):
     assert np.array_equal(sel.cpu().numpy(), wsel)
     assert norm_rel(out.cpu().numpy(), want) < 1e-3
     assert Q.lib().qma_cuda_model_moe_weights(full["model"].h, 40, C.byref(w)) == Q.ERR_INVALID
+
+
+def test_ecache_hint_prefetch_hold_release(full):
+    """The rest of the expert-cache contract (ecache.h:97-123): hint and
+    prefetch accept up to 64 ids (more are clamped, as the reference
+    does) and leave results unchanged; hold hands out get()'s pointers and
+    counts, the 65th hold before a release is refused, and one release
+    ends every hold."""
+    import torch
+    m = full["model"].h
+    ids = np.array([3, 200, 17, 255, 0, 9, 77, 128], np.int32)
+    Q.call("qma_cuda_ecache_hint", m, 5, Q.ptr(ids), len(ids), None)
+    many = np.arange(100, dtype=np.int32) % 256
+    Q.call("qma_cuda_ecache_prefetch", m, 6, Q.ptr(many), len(many), None)
+    torch.cuda.synchronize()
+    bad = np.array([256], np.int32)
+    assert Q.lib().qma_cuda_ecache_hint(m, 5, Q.ptr(bad), 1, None) == Q.ERR_INVALID
+    assert Q.lib().qma_cuda_ecache_prefetch(m, 40, Q.ptr(ids), 1, None) == Q.ERR_INVALID
+    g, u, d = C.c_void_p(), C.c_void_p(), C.c_void_p()
+    g1, u1, d1 = C.c_void_p(), C.c_void_p(), C.c_void_p()
+    Q.call("qma_cuda_ecache_release", m)
+    for k in range(64):
+        Q.call("qma_cuda_ecache_hold", m, 2, k, C.byref(g), C.byref(u), C.byref(d))
+        Q.call("qma_cuda_ecache_get", m, 2, k, C.byref(g1), C.byref(u1), C.byref(d1))
+        assert (g.value, u.value, d.value) == (g1.value, u1.value, d1.value)
+    assert Q.lib().qma_cuda_ecache_held(m) == 64
+    assert Q.lib().qma_cuda_ecache_hold(m, 2, 64, C.byref(g), None, None) == Q.ERR_STATE
+    Q.call("qma_cuda_ecache_release", m)
+    assert Q.lib().qma_cuda_ecache_held(m) == 0
+    Q.call("qma_cuda_ecache_hold", m, 2, 64, C.byref(g), None, None)
+    Q.call("qma_cuda_ecache_release", m)
+
+
+# ---- layer-level parity points (qma_cuda_gdn_step / qma_cuda_attn_decode) --
+GDN_STATE_FLOATS = 8192 * 3 + 32 * 128 * 128
+
+
+def gpu_mixer(st, fn, il, x, advance=1):
+    """One call of a layer-level entry point on device copies of x."""
+    import torch
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    out = torch.empty_like(dx)
+    Q.call(fn, st.h, il, Q.ptr(dx), len(x), Q.ptr(out), advance)
+    return out.cpu().numpy()
+
+
+def engine_gdn_state(st, il, path):
+    """conv [8192*3] and ssm [32*128*128] of gated-delta-net layer il, read
+    from the state's runstate_save-format file (nn.c:2011-2025)."""
+    st.save(state_path=path)
+    raw = np.fromfile(path, np.float32, offset=4)
+    k = sum(1 for l in range(il) if (l + 1) % 4)
+    s = raw[k * GDN_STATE_FLOATS:(k + 1) * GDN_STATE_FLOATS]
+    return s[:8192 * 3], s[8192 * 3:]
+
+
+def oracle_gdn_state(os_, il):
+    L = O.lib()
+    conv = np.ctypeslib.as_array(L.qo_state_conv(os_, il), (8192 * 3,)).copy()
+    ssm = np.ctypeslib.as_array(L.qo_state_ssm(os_, il), (32 * 128 * 128,)).copy()
+    return conv, ssm
+
+
+def oracle_mixer(full, il, chunks, n_ctx):
+    """qo_mixer_forward over the given input chunks on a fresh oracle state;
+    returns the outputs and the state (caller frees it)."""
+    L = O.lib()
+    os_ = L.qo_state_new(n_ctx)
+    outs = []
+    for x in chunks:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        L.qo_mixer_forward(full["om"], os_, il, O._ptr(x), len(x), O._ptr(out))
+        outs.append(out)
+    return outs, os_
+
+
+def test_gdn_step_configs2_decode_1024_steps(full, tmp_path):
+    """configs[2], decode: gated-delta-net layer 0 for 1024 single-token
+    steps from a zero state (inputs ~N(0,1), seeded) through
+    qma_cuda_gdn_step, against the oracle's sequential gdn_worker
+    restatement (qo_mixer_forward, nn.c:784-833 with its conv and
+    projections).  The layer's contribution to the residual must agree
+    within 1e-3 norm-relative over all steps (5e-3 for the worst step: a
+    rare Q8_K int8 flip), and after 1024 steps the recurrent and conv
+    state within 1e-3: no drift of the recurrence over a long decode."""
+    il, n = 0, 1024
+    x = np.random.default_rng(2024).standard_normal((n, 2048)).astype(np.float32)
+    st = Q.State(full["model"], 4096)
+    try:
+        got = np.concatenate([gpu_mixer(st, "qma_cuda_gdn_step", il, x[i:i + 1]) for i in range(n)])
+        assert st.n_pos == n
+        conv_g, ssm_g = engine_gdn_state(st, il, tmp_path / "state.bin")
+    finally:
+        st.close()
+    (want,), os_ = oracle_mixer(full, il, [x], 4096)
+    try:
+        conv_w, ssm_w = oracle_gdn_state(os_, il)
+    finally:
+        O.lib().qo_state_free(os_)
+    dg, dw = got - x, want - x
+    e_tok = norm_rel(dg, dw, axis=1)
+    print("gdn decode 1024: all %.2e worst %.2e last-64 %.2e ssm %.2e conv %.2e"
+          % (norm_rel(dg, dw), e_tok.max(), norm_rel(dg[-64:], dw[-64:]), norm_rel(ssm_g, ssm_w),
+             norm_rel(conv_g, conv_w)))
+    assert norm_rel(dg, dw) <= RTOL_LAYER
+    assert e_tok.max() <= RTOL_TOKEN
+    assert norm_rel(dg[-64:], dw[-64:]) <= RTOL_LAYER
+    assert norm_rel(ssm_g, ssm_w) <= RTOL_LAYER
+    assert norm_rel(conv_g, conv_w) <= RTOL_LAYER
+
+
+@pytest.mark.parametrize("form", ["chunked", "sequential"])
+def test_gdn_step_configs2_prefill_4096(full, tmp_path, form):
+    """configs[2], prefill: layer 0 over a 4096-token prompt (8 calls of
+    512 tokens through qma_cuda_gdn_step) against the oracle's
+    token-sequential recurrence over the same 4096 inputs; outputs and the
+    final recurrent and conv state within 1e-3 norm-relative.  Both forms
+    of the engine's multi-token recurrence: the chunked gated-delta form
+    (64-token chunks, the default) and the token-sequential kernel
+    (QMA_CUDA_GDN_SEQ=1)."""
+    il, n = 0, 4096
+    x = np.random.default_rng(4096).standard_normal((n, 2048)).astype(np.float32)
+    st = Q.State(full["model"], 8192)
+    if form == "sequential":
+        os.environ["QMA_CUDA_GDN_SEQ"] = "1"
+    try:
+        got = np.concatenate([gpu_mixer(st, "qma_cuda_gdn_step", il, x[i:i + 512]) for i in range(0, n, 512)])
+        conv_g, ssm_g = engine_gdn_state(st, il, tmp_path / "state.bin")
+    finally:
+        os.environ.pop("QMA_CUDA_GDN_SEQ", None)
+        st.close()
+    (want,), os_ = oracle_mixer(full, il, [x], 8192)
+    try:
+        conv_w, ssm_w = oracle_gdn_state(os_, il)
+    finally:
+        O.lib().qo_state_free(os_)
+    dg, dw = got - x, want - x
+    e_tok = norm_rel(dg, dw, axis=1)
+    print("gdn prefill 4096 (%s): all %.2e worst %.2e ssm %.2e conv %.2e"
+          % (form, norm_rel(dg, dw), e_tok.max(), norm_rel(ssm_g, ssm_w), norm_rel(conv_g, conv_w)))
+    assert norm_rel(dg, dw) <= RTOL_LAYER
+    assert e_tok.max() <= RTOL_TOKEN
+    assert norm_rel(ssm_g, ssm_w) <= RTOL_LAYER
+    assert norm_rel(conv_g, conv_w) <= RTOL_LAYER
+
+
+def test_attn_decode_matches_oracle_mixer(full):
+    """qma_cuda_attn_decode on attention layer 3 from an empty ring: a
+    300-token chunk (multi-query kernel), then 30 single tokens (decode
+    kernel) past the live-index rebuild at position 300, against the
+    oracle's layer (qo_mixer_forward: the same chunks and rebuilds).  Also:
+    advance 0 leaves the position alone, and the entry points refuse the
+    other kind of layer."""
+    il = 3
+    rng = np.random.default_rng(333)
+    x = rng.standard_normal((330, 2048)).astype(np.float32)
+    chunks = [x[:300]] + [x[i:i + 1] for i in range(300, 330)]
+    st = Q.State(full["model"], 4096)
+    try:
+        got = [gpu_mixer(st, "qma_cuda_attn_decode", il, c) for c in chunks]
+        assert st.n_pos == 330
+        again = gpu_mixer(st, "qma_cuda_attn_decode", il, x[329:330], advance=0)
+        assert st.n_pos == 330 and np.isfinite(again).all()
+        assert Q.lib().qma_cuda_attn_decode(st.h, 0, 1, 1, 1, 1) == Q.ERR_INVALID
+        assert Q.lib().qma_cuda_gdn_step(st.h, 3, 1, 1, 1, 1) == Q.ERR_INVALID
+    finally:
+        st.close()
+    want, os_ = oracle_mixer(full, il, chunks, 4096)
+    O.lib().qo_state_free(os_)
+    g_all, w_all = np.concatenate(got), np.concatenate(want)
+    dg, dw = g_all - x, w_all - x
+    e_tok = norm_rel(dg, dw, axis=1)
+    print("attn mixer: all %.2e worst %.2e decode steps %.2e"
+          % (norm_rel(dg, dw), e_tok.max(), norm_rel(dg[300:], dw[300:])))
+    assert norm_rel(dg, dw) <= RTOL_LAYER
+    assert norm_rel(dg[300:], dw[300:]) <= RTOL_LAYER
+    assert e_tok.max() <= RTOL_TOKEN
+
+
+def test_gdn_step_ragged_chunks_match_sequential(full):
+    """The chunked form on chunk lengths that are not multiples of 64 (2,
+    63, 65, 130, 511 tokens), continuing one state, against the
+    token-sequential kernel on the same calls: outputs within 1e-4
+    norm-relative (two fp32 orders of the same recurrence)."""
+    import torch
+    il = 4
+    sizes = [2, 63, 65, 130, 511]
+    x = np.random.default_rng(77).standard_normal((sum(sizes), 2048)).astype(np.float32)
+    outs = {}
+    for form in ("chunked", "sequential"):
+        st = Q.State(full["model"], 4096)
+        if form == "sequential":
+            os.environ["QMA_CUDA_GDN_SEQ"] = "1"
+        try:
+            o, k = [], 0
+            for n in sizes:
+                o.append(gpu_mixer(st, "qma_cuda_gdn_step", il, x[k:k + n]))
+                k += n
+            outs[form] = np.concatenate(o)
+        finally:
+            os.environ.pop("QMA_CUDA_GDN_SEQ", None)
+            st.close()
+    d1, d2 = outs["chunked"] - x, outs["sequential"] - x
+    e = norm_rel(d1, d2)
+    print("gdn ragged chunks: chunked vs sequential %.2e" % e)
+    assert e <= 1e-4
