@@ -252,6 +252,13 @@ int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens
  * attn_output); the K/V records are appended to the layer's ring and the
  * layer's salience is updated. */
 int qma_cuda_gdn_step(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance);
+/* n_tokens single-token steps of gated-delta-net layer `layer` in order,
+ * each through the decode kernels (as qma_eval's decode runs the layer,
+ * one token at a time), queued back to back with one synchronisation at
+ * the end; the same arguments as qma_cuda_gdn_step with advance 1 and any
+ * n_tokens.  (qma_cuda_gdn_step with n_tokens > 1 runs them as one prefill
+ * chunk instead.) */
+int qma_cuda_gdn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out);
 int qma_cuda_attn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance);
 
 /* Copies the 240-byte KV slot (q4 record + q2 record, kvq.h:22-29) of

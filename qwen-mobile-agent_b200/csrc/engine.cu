@@ -1024,6 +1024,37 @@ static int mixer_call(qma_cuda_state *s, int il, const float *x, int T, float *o
     return check_wait_timeouts();
 }
 
+// n_tokens single-token steps of gated-delta-net layer il back to back (the
+// decode kernels, one token at a time, no host synchronisation between
+// them): the recurrence of a GDN layer reads no step parameters, so the
+// tokens only need to run in order.
+static int gdn_decode_call(qma_cuda_state *s, int il, const float *x, int n_tokens, float *out) {
+    qma_cuda_model *m = s->m;
+    cudaStream_t st = s->st;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    if (s->n_pos + n_tokens > s->n_ctx - HCM_SINK) {
+        set_error("gdn_decode: %d + %d positions exceed this state's ring of %d", s->n_pos, n_tokens, s->n_ctx);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    int rc;
+    bool side_pending = false;
+    for (int t = 0; t < n_tokens; t++) {
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->x, x + size_t(t) * EMBD, sizeof(float) * EMBD, cudaMemcpyDeviceToDevice,
+                                       st));
+        if ((rc = launch_rmsnorm_quant(s->x, m->L[il].attn_norm, 1, EMBD, s->xq, s->xd, s->xs, st))) return rc;
+        if ((rc = mixer(s, il, 1, 1, attn_span(1, 1), side_pending))) return rc;
+        QMA_CHECK_CUDA(cudaMemcpyAsync(out + size_t(t) * EMBD, s->x2, sizeof(float) * EMBD,
+                                       cudaMemcpyDeviceToDevice, st));
+    }
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    s->n_pos += n_tokens;
+    if (s->graph) {
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    return check_wait_timeouts();
+}
+
 // Capture one decode step (T = 1, token and position read from sp_dev,
 // argmax writes the next token and advances the position) as a graph.
 static int capture_decode(qma_cuda_state *s) {
@@ -1327,6 +1358,13 @@ int qma_cuda_gdn_step(qma_cuda_state *s, int layer, const float *x, int n_tokens
                 "qma_cuda_gdn_step: bad arguments (layer %d must be a gated-delta-net layer, 1..%d tokens)", layer,
                 qma::MAX_CHUNK);
     return qma::mixer_call(s, layer, x, n_tokens, x_out, advance != 0);
+}
+
+int qma_cuda_gdn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out) {
+    qma::clear_error();
+    QMA_REQUIRE(s && x && x_out && layer >= 0 && layer < qma::NLAYER && !qma::is_attn(layer) && n_tokens >= 1,
+                "qma_cuda_gdn_decode: bad arguments (layer %d must be a gated-delta-net layer)", layer);
+    return qma::gdn_decode_call(s, layer, x, n_tokens, x_out);
 }
 
 int qma_cuda_attn_decode(qma_cuda_state *s, int layer, const float *x, int n_tokens, float *x_out, int advance) {

@@ -368,7 +368,15 @@ int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ran
         size_t(ep->r_max) * MOE_TOPK * MOE_EMBD * sizeof(float), size_t(t_max) * MOE_TOPK * MOE_EMBD * sizeof(float),
         size_t(t_max) * EP_MAX_RANKS * sizeof(int), size_t(t_max) * MOE_TOPK * sizeof(int),
         sizeof(int) * (2 * n_ranks + 2 * n_ranks * n_ranks), size_t(ep->r_max) * MOE_TOPK * sizeof(int)};
-    for (int i = 0; i < 12 && !rc; i++) rc = ep_alloc(ep, sizes[i], &p[i]);
+    for (int i = 0; i < 12 && !rc; i++) {
+        rc = ep_alloc(ep, sizes[i], &p[i]);
+        // zeroed: the MoE scratch's tickets must start at zero (every call
+        // leaves them zero again)
+        if (!rc && cudaMemset(p[i], 0, sizes[i]) != cudaSuccess) {
+            set_error("qma_cuda_ep_init: cudaMemset: %s", cudaGetErrorString(cudaGetLastError()));
+            rc = QMA_CUDA_ERR_CUDA;
+        }
+    }
     if (!rc && cudaMallocHost(&ep->h_allcnt, sizeof(int) * 2 * n_ranks * n_ranks) != cudaSuccess) {
         ep->h_allcnt = nullptr;
         set_error("qma_cuda_ep_init: pinned host buffer");

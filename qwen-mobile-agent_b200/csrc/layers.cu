@@ -247,7 +247,9 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     __shared__ float kqred[2][4];
     float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
     pdl_trigger();
-    pdl_wait();
+    // the recurrent state and the head's constants do not depend on the
+    // upstream kernel (the previous writer of the state finished before it
+    // started): read them while it runs
     float M[16];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
@@ -256,6 +258,7 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     }
     const float scale = 1.0f / sqrtf(float(SSTATE));
     const float dth = dt[h], ah = av[h];
+    pdl_wait();
     for (int t = 0; t < T; t++) {
         const int buf = t & 1;
         const float *co = conv_out + size_t(t) * CONV_DIM;

