@@ -202,8 +202,8 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                     I2b += mn1[j] * pr;
                 }
                 const float x = s.xd[size_t(t) * (MOE_EMBD / 256) + sb];
-                acc[n][c] += x * (d0 * float(I1[n][c]) - dm0 * float(I2a));
-                acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
+                acc[n][c] = q4k_fold(acc[n][c], x, d0, dm0, I1[n][c], I2a);
+                acc[n][2 + c] = q4k_fold(acc[n][2 + c], x, d1, dm1, I1[n][2 + c], I2b);
             }
         cur = nxt;
     }
@@ -320,8 +320,8 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
             for (int c = 0; c < 2; c++) {
                 if (pc[n][c] < 0) continue;
                 const float x = s.hd[size_t(pc[n][c]) * NSB + sb];
-                acc[n][c] += d0 * x * float(I[n][c]);
-                acc[n][2 + c] += d1 * x * float(I[n][2 + c]);
+                acc[n][c] = q6k_fold(acc[n][c], x, d0, I[n][c]);
+                acc[n][2 + c] = q6k_fold(acc[n][2 + c], x, d1, I[n][2 + c]);
             }
     }
 #pragma unroll
@@ -344,10 +344,15 @@ int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s,
     const int tiles = (T + GT - 1) / GT;
     if (lists)
         QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
-    QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
-                             static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
-                             static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp), T,
-                             s, g0));
+    if (tc_disabled()) {
+        QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
+                                 static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
+                                 static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp),
+                                 T, s, g0));
+    } else {
+        const int rc = launch_gateup_tc(w, T, s, st, g0, ng);
+        if (rc) return rc;
+    }
     QMA_CHECK_CUDA(launch_ex(moe_swiglu_kernel, dim3(nq), dim3(64), 0, st, 1, pdl, s, q0));
     QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
                              static_cast<const uint8_t *>(w.down_exps), packed_bytes(w.down_type, MOE_EMBD, MOE_FF),

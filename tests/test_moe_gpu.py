@@ -98,3 +98,28 @@ def test_moe_exact_fallback_on_ties(cuda, edit, scale):
         assert_close(got, want, 1e-3, "moe ties")
     finally:
         L.close()
+
+
+@pytest.mark.parametrize("T", [16, 37, 300])
+def test_grouped_gateup_tcgen05_bit_identical_to_mma_sync(layer, T):
+    """The grouped path's gate/up GEMM on the 5th-generation tensor cores
+    (tcgen05 int8 MMAs, accumulators in tensor memory, the Q4_K sub-block
+    scales folded into two int8 digits of the weights) against the
+    warp-level mma.sync kernel (QMA_CUDA_MMA_SYNC=1): the integer
+    super-block sums are exact in both and the fp32 fold is shared, so the
+    block's output is the same bits; both within the oracle's tolerance."""
+    import os
+    rng = np.random.default_rng(900 + T)
+    x2 = rng.standard_normal((T, 2048)).astype(np.float32)
+    got, gsel, _, _ = layer.gpu(x2)
+    os.environ["QMA_CUDA_MMA_SYNC"] = "1"
+    try:
+        ref, rsel, _, _ = layer.gpu(x2)
+    finally:
+        del os.environ["QMA_CUDA_MMA_SYNC"]
+    assert np.array_equal(gsel, rsel)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), \
+        f"max |diff| {np.abs(got - ref).max():.3e}"
+    want, wsel, _ = layer.oracle(x2)
+    assert np.array_equal(gsel, wsel)
+    assert_close(got, want, 1e-3, f"moe tc T={T}")
