@@ -458,6 +458,13 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
     dev = torch.device("cuda", local)
     T = EP_SEQS // world
     e0, n_local = Q.ep_shard(rank, world)
+    # configs[4]'s router prior: log Zipf(1.1) over a seeded per-layer expert
+    # ranking, added to every router logit (a skewed expert load)
+    bias_h = [O.zipf_router_bias(SEED, il) for il in range(len(full_w))]
+    bias_d = [torch.from_numpy(b).to(dev) for b in bias_h]
+    full_w = [shard_weights(w, 0, 0) for w in full_w]          # copies
+    for w, b in zip(full_w, bias_d):
+        w.router_bias = b.data_ptr()
     shard = [shard_weights(w, e0, n_local) for w in full_w]
     X = ep_inputs(world)
     mine = X[rank * T:(rank + 1) * T]
@@ -482,7 +489,10 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
     gsel = sel.cpu().numpy()
     pn = np.frombuffer(ctypes_read(full_w[0].post_norm, 2048 * 4), np.float32)
     gi = np.frombuffer(ctypes_read(full_w[0].gate_inp, 256 * 2048 * 4), np.float32).reshape(256, 2048)
-    osel, _ = O.moe_route(pn, gi, mine)
+    osel, _ = O.moe_route(pn, gi, mine, bias=bias_h[0])
+    cnt = np.bincount(SEL.cpu().numpy().ravel(), minlength=256)
+    expert_load = {"layer": 0, "distinct_experts": int(np.count_nonzero(cnt)), "max_pairs_per_expert": int(cnt.max()),
+                   "pairs": int(cnt.sum())}
     bit = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
     sel_gpu = bool(np.array_equal(gsel, SEL.cpu().numpy()[rank * T:(rank + 1) * T]))
     sel_oracle = bool(np.array_equal(gsel, osel))
@@ -562,7 +572,8 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
         "exchange": {"sent_bytes_per_step": net[0], "recv_bytes_per_step": net[1], "rank": rank,
                      "note": "rank 0's NCCL transfers, its own share included (over NVLink at N > 1)"},
         "ep_parity": ok_all, "parity_detail": detail,
-        "router_prior": "none (uniform router: the Zipf(1.1) prior of configs[4] is not applied)",
+        "router_prior": "log Zipf(s=1.1) over a seeded per-layer expert ranking, added to every router logit",
+        "expert_load": expert_load,
         "collectives": "per layer: NCCL all-gather of the counts, grouped send/recv dispatch and return",
     }
 

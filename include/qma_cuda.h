@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define QMA_CUDA_ABI_VERSION 1
+#define QMA_CUDA_ABI_VERSION 2
 
 typedef enum {
     QMA_CUDA_OK = 0,
@@ -323,6 +323,12 @@ typedef struct {
     const void  *down_shexp;       /* blk.N.ffn_down_shexp.weight, packed      */
     int down_type;                 /* QMA_TYPE_Q6_K or QMA_TYPE_Q4_K           */
     int down_shexp_type;
+    /* Optional device float [256] added to the router's fp32 logits before
+     * the softmax and the top-8 (l_e = fl(s_e + bias_e)); NULL for none.
+     * qwen35moe has no router bias: this carries a serving workload's
+     * per-expert prior (configs[4]'s Zipf prior), and the reference has no
+     * counterpart. */
+    const float *router_bias;
 } qma_cuda_moe_weights;
 
 /* The MoE block weights of model layer `layer` (0..39) as device pointers

@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
         L.qo_model_free.argtypes = [vp]
         L.qo_moe_ffn.argtypes = [vp, i32, vp, i32, vp, vp, vp]
         L.qo_moe_block.argtypes = [vp, i32, vp, i32, vp, vp, vp]
+        L.qo_moe_block_biased.argtypes = [vp, i32, vp, i32, vp, vp, vp, vp]
         L.qo_router_logits.argtypes = [vp, vp, vp]
         L.qo_route.argtypes = [vp, vp, vp, i32, vp, vp]
         L.qo_moe_route.argtypes = [vp, vp, vp, vp, i32, vp, vp]
@@ -215,6 +216,15 @@ def matmul(x: np.ndarray, W: np.ndarray, wtype: int, n_in: int, n_out: int) -> n
     out = np.zeros((x.shape[0], n_out), np.float32)
     lib().qo_matmul(_ptr(x), _ptr(W), n_in, n_out, x.shape[0], wtype, _ptr(out))
     return out
+
+
+def zipf_router_bias(seed: int, layer: int, s: float = 1.1, n: int = 256) -> np.ndarray:
+    """configs[4]'s router prior for one layer: expert e gets log p(rank),
+    p(r) = r^-s / sum_k k^-s, over a seeded per-layer random ranking of the
+    experts (a skewed expert load).  float32 [n]."""
+    rank = np.random.default_rng([seed, layer]).permutation(n) + 1
+    p = rank.astype(np.float64) ** -s
+    return np.log(p / p.sum()).astype(np.float32)
 
 
 def moe_route(post_norm: np.ndarray, gate_inp: np.ndarray, x2: np.ndarray, bias=None):

@@ -172,6 +172,11 @@ void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
  * post_attention_norm). */
 void qo_moe_block(const qo_model *m, int il, const float *x2, int T, float *out,
                   int *sel, float *w);
+/* the same with an additive per-expert router bias (256 floats, or NULL):
+ * each fp32 logit gets one fp32 addition before the softmax (configs[4]'s
+ * serving prior; the reference has none) */
+void qo_moe_block_biased(const qo_model *m, int il, const float *x2, int T, const float *bias, float *out,
+                         int *sel, float *w);
 /* router only: logits (256) of one token in the reference's sequential
  * fp32 order (nn.c:513-523) */
 void qo_router_logits(const float *gate_inp, const float *x, float *logits);

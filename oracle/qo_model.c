@@ -265,13 +265,22 @@ void qo_moe_route(const float *post_norm, const float *gate_inp, const float *bi
     free(xn);
 }
 
+static void moe_ffn_impl(const qo_model *m, int il, const float *x, int T, const float *bias, float *out,
+                         int *sel_out, float *w_out);
+
 void qo_moe_ffn(const qo_model *m, int il, const float *x, int T, float *out,
                 int *sel_out, float *w_out)
+{
+    moe_ffn_impl(m, il, x, T, NULL, out, sel_out, w_out);
+}
+
+static void moe_ffn_impl(const qo_model *m, int il, const float *x, int T, const float *bias, float *out,
+                         int *sel_out, float *w_out)
 {
     const qo_layer *L = &m->L[il];
     int *sel = malloc(sizeof(int) * (size_t)T * QO_EXPERT_USED);
     float *wt = malloc(sizeof(float) * (size_t)T * QO_EXPERT_USED);
-    qo_route(L->gate_inp, NULL, x, T, sel, wt);
+    qo_route(L->gate_inp, bias, x, T, sel, wt);
     int8_t *xq = malloc((size_t)T * QO_EMBD);
     float *xd = malloc(sizeof(float) * (size_t)T * (QO_EMBD / QO_QK_K));
     int16_t *xs = malloc(sizeof(int16_t) * (size_t)T * (QO_EMBD / 16));
@@ -331,10 +340,16 @@ static void mm_rows(void *arg, int r0, int r1)
 void qo_moe_block(const qo_model *m, int il, const float *x2, int T, float *out,
                   int *sel, float *w)
 {
+    qo_moe_block_biased(m, il, x2, T, NULL, out, sel, w);
+}
+
+void qo_moe_block_biased(const qo_model *m, int il, const float *x2, int T, const float *bias, float *out,
+                         int *sel, float *w)
+{
     float *xn = malloc(sizeof(float) * (size_t)T * QO_EMBD);
     float *ra = malloc(sizeof(float) * (size_t)T * QO_EMBD);
     rms_norm_m(xn, x2, m->L[il].post_norm, QO_EMBD, T);
-    qo_moe_ffn(m, il, xn, T, ra, sel, w);
+    moe_ffn_impl(m, il, xn, T, bias, ra, sel, w);
     for (size_t i = 0; i < (size_t)QO_EMBD * T; i++) out[i] = ra[i] + x2[i];
     free(xn);
     free(ra);

@@ -826,6 +826,78 @@ __global__ void __launch_bounds__(256) attn_salience_kernel(const float *__restr
     *dst = s;
 }
 
+// The same EMA for a chunk of T > 1 queries.  Per position the 16 * T
+// updates are sequential (head-major, then query: the order above), but
+// their probabilities are not: a CTA takes 32 positions, its warps 1..7
+// compute the probabilities of the next (head, 64 queries) tile into shared
+// memory while warp 0 (lane = position) runs the EMA over the current one.
+constexpr int SAL_POS = 32, SAL_TQ = 64;
+
+__global__ void __launch_bounds__(256) attn_salience_chunk_kernel(const float *__restrict__ scores, int nk_max,
+                                                                  const float *__restrict__ ml,
+                                                                  const int *__restrict__ live,
+                                                                  const StepParams *spp, float *sal,
+                                                                  float *pin_sal) {
+    QMA_TRACE_SCOPE(TK_SALIENCE);
+    __shared__ float P[2][SAL_TQ][SAL_POS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int jj0 = blockIdx.x * SAL_POS;
+    pdl_trigger();
+    pdl_wait();
+    const StepParams sp = *spp;
+    if (sp.n_live <= 0) return;
+    const int nk0 = nk_of(sp, 0), nkmax = nk_of(sp, sp.T - 1);
+    if (jj0 >= nkmax) return;                      // CTA-uniform
+    const int T = sp.T, ntq = (T + SAL_TQ - 1) / SAL_TQ, ntile = NHEAD * ntq;
+    // tile i = (head i / ntq, queries 64 (i % ntq) ..): probabilities of the
+    // 32 positions, computed by `nthr` threads starting at thread `first`
+    auto fill = [&](int i, int first, int nthr) {
+        const int h = i / ntq, t0 = (i % ntq) * SAL_TQ;
+        float(*dst)[SAL_POS] = P[i & 1];
+        for (int k = tid - first; k < SAL_TQ * SAL_POS; k += nthr) {
+            const int tq = k / SAL_POS, pos = k % SAL_POS, t = t0 + tq, jj = jj0 + pos;
+            float p = 0.0f;
+            if (t < T && jj < nk_of(sp, t)) {
+                const float m = ml[(size_t(t) * NHEAD + h) * 2], l = ml[(size_t(t) * NHEAD + h) * 2 + 1];
+                p = expf(scores[(size_t(t) * NHEAD + h) * nk_max + jj] - m) / l;
+            }
+            dst[tq][pos] = p;
+        }
+    };
+    fill(0, 0, 256);
+    __syncthreads();
+    const int jj = jj0 + lane;
+    float *dst = nullptr;
+    float s = 0.0f;
+    if (warp == 0 && jj < nkmax) {
+        if (jj < sp.n_live) {
+            const int e = live[jj];
+            dst = (jj >= sp.n_ring_q4 && jj < sp.n4) ? pin_sal + (e - HCM_ARENA_BASE) : sal + e;
+        } else {
+            dst = sal + hcm_slot(sp.rebuilt_at + (jj - sp.n_live), sp.n_ctx);
+        }
+        s = *dst;
+    }
+    // first query that attends position jj (positions of this chunk's own
+    // tokens are attended from their token on)
+    const int tmin = jj < nk0 ? 0 : jj - nk0 + 1;
+    const float keep = 1.0f - 0.05f, take = 0.05f;
+    for (int i = 0; i < ntile; i++) {
+        if (warp == 0) {
+            if (dst) {
+                const int t0 = (i % ntq) * SAL_TQ, nq = min(SAL_TQ, T - t0);
+                const float(*src)[SAL_POS] = P[i & 1];
+                for (int tq = 0; tq < nq; tq++)
+                    if (t0 + tq >= tmin) s = __fadd_rn(__fmul_rn(keep, s), __fmul_rn(take, src[tq][lane]));
+            }
+        } else if (i + 1 < ntile) {
+            fill(i + 1, 32, 224);
+        }
+        __syncthreads();
+    }
+    if (dst) *dst = s;
+}
+
 // ------------------------------------------------------------ arena copy --
 // hcm_rebuild's promotion of ring slots into the heavy-hitter arena
 // (nn.c:1092-1104): per pair (src ring slot, dst arena index), the 240-byte
@@ -891,8 +963,12 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
 }
 
 int launch_salience(const AttnArgs &a, cudaStream_t st) {
-    QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, false,
-                             a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
+    if (a.T > 1)
+        QMA_CHECK_CUDA(launch_ex(attn_salience_chunk_kernel, dim3((a.nk_max + SAL_POS - 1) / SAL_POS), dim3(256), 0,
+                                 st, 1, false, a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
+    else
+        QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, false,
+                                 a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
     return QMA_CUDA_OK;
 }
 

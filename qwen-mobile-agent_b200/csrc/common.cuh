@@ -438,6 +438,19 @@ __device__ __forceinline__ void trace_mark(uint32_t k, uint32_t phase) {
 #define QMA_TRACE_MARK(k, phase) do {} while (0)
 #endif
 
+// The fp32 fold of one super-block's exact integer sums into a grouped
+// GEMM accumulator, in one fixed operation order (explicit roundings, no
+// contraction), shared by the tensor-core GEMM kernels of both generations so
+// that they produce the same bits: Q4_K adds xd * (d * I1 - dmin * I2)
+// (dot_q4_K_q8k, q8k.c:89-131), Q6_K adds d * xd * I (dot_q6_K_q8k,
+// q8k.c:210-262).
+__device__ __forceinline__ float q4k_fold(float acc, float xd, float d, float dmin, int I1, int I2) {
+    return __fadd_rn(acc, __fmul_rn(xd, __fsub_rn(__fmul_rn(d, float(I1)), __fmul_rn(dmin, float(I2)))));
+}
+__device__ __forceinline__ float q6k_fold(float acc, float xd, float d, int I) {
+    return __fadd_rn(acc, __fmul_rn(__fmul_rn(d, xd), float(I)));
+}
+
 // 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,
 // quants.c:18-26 / q8k.c:22-30).
 __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *s, int &d, int &m) {

@@ -20,6 +20,7 @@
 #include "layers.cuh"
 #include "moe.cuh"
 #include "synth.cuh"
+#include "tc.cuh"
 
 namespace qma {
 
@@ -870,8 +871,9 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
 // A bounded wait inside a kernel that gave up (a copy that never landed)
 // fails the call instead of returning silently wrong results.
 static int check_wait_timeouts() {
-    const int a = moe_wait_timeouts(), b = gemv_wait_timeouts(), c = tc_wait_timeouts();
-    const int n = a < 0 || b < 0 || c < 0 ? -1 : a + b + c;
+    const int a = moe_wait_timeouts(), b = gemv_wait_timeouts(), c = tc_wait_timeouts(),
+              d = gemm_tc_wait_timeouts();
+    const int n = a < 0 || b < 0 || c < 0 || d < 0 ? -1 : a + b + c + d;
     if (n == 0) return QMA_CUDA_OK;
     set_error("%d bounded waits for weight copies ran out (or the counter could not be read)", n);
     return QMA_CUDA_ERR_TIMEOUT;

@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "tc.cuh"
 #include "quant.cuh"
 
 namespace qma {
@@ -498,8 +499,8 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                     I2b += mn1[j] * pair;
                 }
                 const float x = xd[size_t(tc[n][c]) * nsb + sb];
-                acc[n][c] += x * (d0 * float(I1[n][c]) - dm0 * float(I2a));
-                acc[n][2 + c] += x * (d1 * float(I1[n][2 + c]) - dm1 * float(I2b));
+                acc[n][c] = q4k_fold(acc[n][c], x, d0, dm0, I1[n][c], I2a);
+                acc[n][2 + c] = q4k_fold(acc[n][2 + c], x, d1, dm1, I1[n][2 + c], I2b);
             }
     }
     if (!active) return;
@@ -513,6 +514,10 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
             out[o1] = resid ? __fadd_rn(acc[n][2 + c], resid[o1]) : acc[n][2 + c];
         }
 }
+
+// gemm_tc.cu
+int launch_gemm_q4k_tc(const uint8_t *W, int n_in, int n_out, int T, const int8_t *xq, const float *xd,
+                       const int16_t *xsum, float *out, const float *resid, cudaStream_t st);
 
 static int launch_gemm_q4k(const uint8_t *W, int n_in, int n_out, int T, const int8_t *xq, const float *xd,
                            const int16_t *xsum, float *out, const float *resid, cudaStream_t st) {
@@ -537,8 +542,11 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
         set_error("matvec: the conv epilogue needs the single-token staged path");
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
-    // several tokens over Q4_K rows: the tensor-core GEMM
+    // several tokens over Q4_K rows: the tensor-core GEMM (tcgen05 from 64
+    // tokens on, the warp-level MMA kernel below that or when asked)
     if constexpr (std::is_same<F, FmtQ4K>::value) {
+        if (T >= 64 && !tc_disabled())
+            return launch_gemm_q4k_tc(W, n_in, n_out, T, xq, xd, xsum, out, resid, st);
         if (T >= 8 && n_out % 16 == 0)
             return launch_gemm_q4k(W, n_in, n_out, T, xq, xd, xsum, out, resid, st);
     }

@@ -627,8 +627,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const float *__rest
 }
 
 // Grid (4 column blocks, 32 V-heads), 256 threads: thread (jl = tid / 8,
-// part = tid % 8) holds M[j][part * 16 .. + 15] of state row j = 32 * block
-// + jl through all chunks, as gdn_seq_kernel does.
+// part = tid % 8) holds 16 elements of state row j = 32 * block + jl
+// through all chunks.
 constexpr size_t GDN_SCAN_SMEM =
     sizeof(float) * (3 * GC * SSTATE + GC * 32 + GC * (GC + 1) + 2 * GC * 33 + 2 * GC);
 
@@ -651,11 +651,13 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const float *__rest
     const float scale = 1.0f / sqrtf(float(SSTATE));
     pdl_trigger();
     pdl_wait();
-    float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 16;
+    // M[4 k + r] = state element i = part * 4 + 32 k + r of row j: the 8
+    // threads of a row read one contiguous 128-byte line of a shared row per k
+    float *Mrow = ssm + (size_t(h) * SSTATE + j) * SSTATE + part * 4;
     float M[16];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-        const float4 v = reinterpret_cast<const float4 *>(Mrow)[k];
+        const float4 v = *reinterpret_cast<const float4 *>(Mrow + 32 * k);
         M[4 * k] = v.x; M[4 * k + 1] = v.y; M[4 * k + 2] = v.z; M[4 * k + 3] = v.w;
     }
     for (int c = 0; c < nch; c++) {
@@ -687,12 +689,13 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const float *__rest
         if (tid < GC) DEC[tid] = tid < n ? expf(Gs[n - 1] - Gs[tid]) : 0.0f;
         // delta_t = U_t - W_t^T S_0 and q_t^T S_0 for this thread's row j
         for (int t = 0; t < n; t++) {
-            const float4 *wr = reinterpret_cast<const float4 *>(Ws + t * SSTATE + part * 16);
-            const float4 *qr = reinterpret_cast<const float4 *>(Qs + t * SSTATE + part * 16);
+            const float *wr = Ws + t * SSTATE + part * 4;
+            const float *qr = Qs + t * SSTATE + part * 4;
             float dw = 0.0f, dq = 0.0f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const float4 w4 = wr[k], q4 = qr[k];
+                const float4 w4 = *reinterpret_cast<const float4 *>(wr + 32 * k);
+                const float4 q4 = *reinterpret_cast<const float4 *>(qr + 32 * k);
                 dw = fmaf(w4.x, M[4 * k], dw); dw = fmaf(w4.y, M[4 * k + 1], dw);
                 dw = fmaf(w4.z, M[4 * k + 2], dw); dw = fmaf(w4.w, M[4 * k + 3], dw);
                 dq = fmaf(q4.x, M[4 * k], dq); dq = fmaf(q4.y, M[4 * k + 1], dq);
@@ -722,10 +725,10 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const float *__rest
         for (int i = 0; i < 16; i++) M[i] *= el;
         for (int s2 = 0; s2 < n; s2++) {
             const float cf = DEC[s2] * Ds[s2 * 33 + jl];
-            const float4 *kr = reinterpret_cast<const float4 *>(Ks + s2 * SSTATE + part * 16);
+            const float *kr = Ks + s2 * SSTATE + part * 4;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const float4 k4 = kr[k];
+                const float4 k4 = *reinterpret_cast<const float4 *>(kr + 32 * k);
                 M[4 * k] = fmaf(cf, k4.x, M[4 * k]); M[4 * k + 1] = fmaf(cf, k4.y, M[4 * k + 1]);
                 M[4 * k + 2] = fmaf(cf, k4.z, M[4 * k + 2]); M[4 * k + 3] = fmaf(cf, k4.w, M[4 * k + 3]);
             }
@@ -733,7 +736,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const float *__rest
     }
 #pragma unroll
     for (int k = 0; k < 4; k++)
-        reinterpret_cast<float4 *>(Mrow)[k] = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
+        *reinterpret_cast<float4 *>(Mrow + 32 * k) = make_float4(M[4 * k], M[4 * k + 1], M[4 * k + 2], M[4 * k + 3]);
 }
 
 // QMA_CUDA_GDN_SEQ=1 in the environment: chunks of tokens run the

@@ -339,12 +339,22 @@ __device__ __forceinline__ float router_logit_seq(const float *row, const float 
     return acc;
 }
 
+// With a router bias the logit is fl(s + b_e): its interval S + b +- B'
+// with B' = B + 2^-24 (|S + b| + B) (1 + 2^-20) covers the extra rounding
+// (and the fp64 sum S + b), and the exact path adds b_e to the recomputed
+// fp32 sum in fp32, as the biased reference does.
+__device__ __forceinline__ void bias_interval(double &S, double &B, float b) {
+    const double Sb = S + double(b);
+    B = B + 0x1.0p-24 * (fabs(Sb) + B) * (1.0 + 0x1.0p-20) + 1e-30;
+    S = Sb;
+}
+
 __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__restrict__ x2,
                                                                const float *__restrict__ post_norm,
                                                                const float *__restrict__ Wr,
                                                                const float *__restrict__ gis,
                                                                MoeScratch s, int *sel_out,
-                                                               float *w_out) {
+                                                               float *w_out, const float *__restrict__ bias) {
     QMA_TRACE_SCOPE(TK_ROUTER);
     extern __shared__ __align__(128) float rrows[];        // this CTA's 16 router rows
     const unsigned rank = cluster_rank();
@@ -422,6 +432,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     {
         double S0, B0;
         router_logit(rrows + size_t(warp) * MOE_EMBD, xn, lane, S0, B0);
+        if (bias) bias_interval(S0, B0, __ldg(bias + e0));
         if (lane == 0) {
             st_cluster_f64(cluster_map(&sS[e0], 0), S0);
             st_cluster_f64(cluster_map(&sB[e0], 0), B0);
@@ -497,7 +508,8 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
             }
             if (tid < nb) {
                 const int e = cand[base + tid];
-                sS[e] = double(router_logit_seq(rrows + size_t(tid) * MOE_EMBD, xn));
+                const float l = router_logit_seq(rrows + size_t(tid) * MOE_EMBD, xn);
+                sS[e] = double(bias ? __fadd_rn(l, bias[e]) : l);
                 sB[e] = 0.0;
             }
             __syncthreads();
@@ -910,7 +922,7 @@ int moe_route(const qma_cuda_moe_weights &w, const float *x2, int T, const MoeSc
     int rc = moe_attrs();
     if (rc) return rc;
     QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, false, x2,
-                             w.post_norm, w.gate_inp, w.gate_inp_shexp, s, sel, wts));
+                             w.post_norm, w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias));
     return QMA_CUDA_OK;
 }
 
@@ -931,7 +943,7 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
     }
     const bool pdl = pdl_enabled() && !clear_counters;
     QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
-                             w.gate_inp, w.gate_inp_shexp, s, sel, wts));
+                             w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias));
     if (s.goff && w.down_type == QMA_TYPE_Q6_K) {
         // a chunk of tokens: experts grouped, tensor-core MMAs, then the combine
         // (and the next norm when asked) in one kernel

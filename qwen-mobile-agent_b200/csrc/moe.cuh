@@ -39,18 +39,6 @@ struct MoeScratch {
     int16_t *hs;           // [T * 9][32]
 };
 int moe_grouped(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st);
-// The fp32 fold of one super-block's exact integer sums into a grouped
-// GEMM accumulator, in one fixed operation order (explicit roundings, no
-// contraction), shared by the tensor-core kernels of both generations so
-// that they produce the same bits: Q4_K adds xd * (d * I1 - dmin * I2)
-// (dot_q4_K_q8k, q8k.c:89-131), Q6_K adds d * xd * I (dot_q6_K_q8k,
-// q8k.c:210-262).
-__device__ __forceinline__ float q4k_fold(float acc, float xd, float d, float dmin, int I1, int I2) {
-    return __fadd_rn(acc, __fmul_rn(xd, __fsub_rn(__fmul_rn(d, float(I1)), __fmul_rn(dmin, float(I2)))));
-}
-__device__ __forceinline__ float q6k_fold(float acc, float xd, float d, int I) {
-    return __fadd_rn(acc, __fmul_rn(__fmul_rn(d, xd), float(I)));
-}
 // The grouped pipeline on part of the work: groups g0 .. g0 + ng - 1 of the
 // 257 (256 = the shared expert; routed group e reads expert e of the tables
 // w points at), the pair lists built first when `lists`, the SwiGLU on pair
@@ -59,9 +47,9 @@ __device__ __forceinline__ float q6k_fold(float acc, float xd, float d, int I) {
 int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st, int g0, int ng,
                       bool lists, int q0, int nq);
 // The grouped gate/up GEMM on the 5th-generation tensor cores (moe_tc.cu),
-// in place of moe_gateup_kernel unless tc_disabled() (QMA_CUDA_MMA_SYNC=1).
+// in place of moe_gateup_kernel when tc_grouped() (QMA_CUDA_TC_GROUPED=1).
 int launch_gateup_tc(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st, int g0, int ng);
-bool tc_disabled();
+bool tc_grouped();
 // Bounded waits of the tensor-core kernels that ran out (reset by reading).
 int tc_wait_timeouts();
 // The router alone (RMSNorm, Q8_K of the normed input, exact top-8, the

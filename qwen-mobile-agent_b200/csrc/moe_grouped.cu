@@ -18,6 +18,7 @@
 #include "gemv.cuh"
 #include "moe.cuh"
 #include "quant.cuh"
+#include "tc.cuh"
 
 namespace qma {
 
@@ -344,7 +345,7 @@ int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s,
     const int tiles = (T + GT - 1) / GT;
     if (lists)
         QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
-    if (tc_disabled()) {
+    if (!tc_grouped()) {
         QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
                                  static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
                                  static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp),

@@ -11,17 +11,19 @@
 // it is split into two digits, a_k = 32 hi_k + lo_k (hi 0..29, lo 0..31),
 // and the tensor core accumulates H = sum hi x and L = sum lo x in int32
 // (|H|, |L| <= 256 * 31 * 127, exact); I1 = 32 H + L.  One tcgen05.mma of
-// M = 128 rows x N = 32 pairs x K = 32 per (sub-block, digit), 16 per
+// M = 128 rows x N = 16 pairs x K = 32 per (sub-block, digit), 16 per
 // super-block, all eight super-blocks' accumulators resident in TMEM
-// (8 x 2 x 32 = 512 columns).  The mins term I2 = sum_j m_j * bsum_j and
+// (8 x 2 x 16 = 256 columns).  The mins term I2 = sum_j m_j * bsum_j and
 // the fp32 fold run in the epilogue, one thread per row.
 //
-// CTA: 256 threads.  Warps 0-3 are the producers (thread = row of the
+// CTA: 256 threads, ~100 KB of shared memory and 256 TMEM columns, so two
+// CTAs share an SM.  Warps 0-3 are the producers (thread = row of the
 // 128-row tile: read the Q4_K block, unpack nibbles, multiply by the
 // sub-block scale, split into digits, write the canonical K-major A tiles
-// of both digits, double-buffered per super-block) and then the epilogue
-// (TMEM lane quarter = warp); lane 0 of warp 4 issues the MMAs.  All threads
-// stage the pairs' Q8_K activation tiles (B) once.
+// of both digits for one super-block at a time, the next super-block's
+// bytes already in registers) and then the epilogue (TMEM lane quarter =
+// warp); lane 0 of warp 4 issues the MMAs.  All threads stage the pairs'
+// Q8_K activation tiles (B) once.
 #include "common.cuh"
 #include "moe.cuh"
 #include "tc.cuh"
@@ -29,18 +31,16 @@
 namespace qma {
 
 constexpr int TCM = 128;                       // rows per CTA (TMEM lanes)
-constexpr int TCN = 32;                        // pairs per CTA (MMA N)
+constexpr int TCN = 16;                        // pairs per CTA (MMA N)
 constexpr int TC_NSB = MOE_EMBD / 256;         // super-blocks of a gate/up row
 constexpr uint32_t TC_TILE_A = TCM * 32;       // one 128 x 32 int8 tile
-constexpr uint32_t TC_TILE_B = TCN * 32;       // one 32 x 32 int8 tile
-constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr uint32_t TC_TILE_B = TCN * 32;       // one 16 x 32 int8 tile
+constexpr uint32_t TC_TMEM_COLS = 256;
 static_assert(TC_NSB * 2 * TCN == int(TC_TMEM_COLS), "all super-blocks' accumulators in TMEM");
 
 struct GateupTcSmem {
-    uint8_t a[2][2][8][TC_TILE_A];             // [buffer][digit hi|lo][sub-block]
+    uint8_t a[2][8][TC_TILE_A];                // [digit hi|lo][sub-block], one super-block
     uint8_t b[TC_NSB][8][TC_TILE_B];           // [super-block][sub-block]
-    float d[TC_NSB][TCM], dm[TC_NSB][TCM];
-    uint8_t mn[TC_NSB][TCM][8];
     int bsum[TCN][TC_NSB * 8];                 // per pair: Q8_K 32-lane sums
     float xd[TCN][TC_NSB];
 };
@@ -75,16 +75,16 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity) {
     return false;
 }
 
-// Grid (1024 / 128 row tiles of [gate | up], ng groups, ceil(T / 32) pair
+// Grid (1024 / 128 row tiles of [gate | up], ng groups, ceil(T / 16) pair
 // tiles); output hg[pair][1024] as moe_gateup_kernel.
-__global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__restrict__ gate_exps,
+__global__ void __launch_bounds__(256, 2) moe_gateup_tc_kernel(const uint8_t *__restrict__ gate_exps,
                                                                const uint8_t *__restrict__ up_exps,
                                                                const uint8_t *__restrict__ gate_sh,
                                                                const uint8_t *__restrict__ up_sh, int T,
                                                                MoeScratch s, int e0) {
     extern __shared__ __align__(128) uint8_t tcsm_raw[];
     GateupTcSmem &S = *reinterpret_cast<GateupTcSmem *>(tcsm_raw);
-    __shared__ __align__(8) uint64_t bar_a[2], bar_m[2], bar_done;
+    __shared__ __align__(8) uint64_t bar_a, bar_m, bar_done;
     __shared__ uint32_t tmem_base;
     __shared__ int prow[TCN], ptok[TCN];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -95,10 +95,8 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
     if (tok0 >= ne) return;                               // CTA-uniform, before any TMEM is held
     if (warp == 0) tmem_alloc(&tmem_base, TC_TMEM_COLS);
     if (tid == 0) {
-        mbar_init(&bar_a[0], 128);
-        mbar_init(&bar_a[1], 128);
-        mbar_init(&bar_m[0], 1);
-        mbar_init(&bar_m[1], 1);
+        mbar_init(&bar_a, 128);
+        mbar_init(&bar_m, 1);
         mbar_init(&bar_done, 1);
         mbar_fence_init();
     }
@@ -116,9 +114,9 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
-    // ---- B: the pairs' Q8_K rows as canonical 32 x 32 tiles, sums, scales --
+    // ---- B: the pairs' Q8_K rows as canonical 16 x 32 tiles, sums, scales --
     for (int i = tid; i < TCN * TC_NSB * 8 * 2; i += 256) {
-        const int kc = i & 1, j = (i >> 1) & 7, sb = (i >> 4) & 7, n = i >> 7;
+        const int kc = i & 1, j = (i >> 1) & 7, sb = (i >> 4) & 7, n = i >> 7;   // n < TCN
         const int t = ptok[n];
         int4 v = make_int4(0, 0, 0, 0);
         if (t >= 0) v = *reinterpret_cast<const int4 *>(s.xq + size_t(t) * MOE_EMBD + sb * 256 + j * 32 + kc * 16);
@@ -131,7 +129,7 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
                                     int(s.xs[size_t(t) * (MOE_EMBD / 16) + 2 * q + 1])
                               : 0;
     }
-    {
+    if (tid < TCN * TC_NSB) {
         const int n = tid >> 3, sb = tid & 7;
         S.xd[n][sb] = ptok[n] >= 0 ? s.xd[size_t(ptok[n]) * TC_NSB + sb] : 0.0f;
     }
@@ -150,20 +148,13 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
 #pragma unroll
         for (int k = 0; k < 9; k++) cur[k] = __ldg(row + k);
         for (int sb = 0; sb < TC_NSB; sb++) {
-            const int buf = sb & 1;
             if (sb + 1 < TC_NSB) {
 #pragma unroll
                 for (int k = 0; k < 9; k++) nxt[k] = __ldg(row + 9 * (sb + 1) + k);
             }
-            if (sb >= 2) tc_wait(&bar_m[buf], uint32_t((sb / 2 - 1) & 1));   // MMAs of sb - 2 read this buffer
+            if (sb >= 1) tc_wait(&bar_m, uint32_t((sb - 1) & 1));      // the MMAs of sb - 1 read the tiles
             int sc[8], mn[8];
             tc_q4k_scales(cur[0].y, cur[0].z, cur[0].w, sc, mn);
-            S.d[sb][m] = h2f(uint16_t(cur[0].x & 0xffffu));
-            S.dm[sb][m] = h2f(uint16_t(cur[0].x >> 16));
-            uint2 mp;
-            mp.x = uint32_t(mn[0]) | (uint32_t(mn[1]) << 8) | (uint32_t(mn[2]) << 16) | (uint32_t(mn[3]) << 24);
-            mp.y = uint32_t(mn[4]) | (uint32_t(mn[5]) << 8) | (uint32_t(mn[6]) << 16) | (uint32_t(mn[7]) << 24);
-            *reinterpret_cast<uint2 *>(S.mn[sb][m]) = mp;
 #pragma unroll
             for (int g = 0; g < 4; g++) {
 #pragma unroll
@@ -177,15 +168,15 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
 #pragma unroll
                         for (int c = 0; c < 4; c++)
                             tc_digits((w[c] >> (4 * half)) & 0x0F0F0F0Fu, uint32_t(sc[j]), hi[c], lo[c]);
-                        *reinterpret_cast<uint4 *>(&S.a[buf][0][j][tc_off(m, 16 * kc)]) =
+                        *reinterpret_cast<uint4 *>(&S.a[0][j][tc_off(m, 16 * kc)]) =
                             make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4 *>(&S.a[buf][1][j][tc_off(m, 16 * kc)]) =
+                        *reinterpret_cast<uint4 *>(&S.a[1][j][tc_off(m, 16 * kc)]) =
                             make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
             }
             fence_async_smem();
-            mbar_arrive(&bar_a[buf]);
+            mbar_arrive(&bar_a);
             if (sb + 1 < TC_NSB) {
 #pragma unroll
                 for (int k = 0; k < 9; k++) cur[k] = nxt[k];
@@ -195,38 +186,46 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
         // ---- MMA issue ------------------------------------------------------------
         constexpr uint32_t idesc = tc_idesc_s8(TCM, TCN);
         for (int sb = 0; sb < TC_NSB; sb++) {
-            const int buf = sb & 1;
-            tc_wait(&bar_a[buf], uint32_t((sb / 2) & 1));
+            tc_wait(&bar_a, uint32_t(sb & 1));
             tc_fence_after();
 #pragma unroll 1
             for (int j = 0; j < 8; j++) {
                 const uint64_t bd = tc_desc(S.b[sb][j]);
 #pragma unroll
                 for (int dg = 0; dg < 2; dg++)
-                    tc_mma_s8(tmem + uint32_t(sb * 2 * TCN + dg * TCN), tc_desc(S.a[buf][dg][j]), bd, idesc, j > 0);
+                    tc_mma_s8(tmem + uint32_t(sb * 2 * TCN + dg * TCN), tc_desc(S.a[dg][j]), bd, idesc, j > 0);
             }
-            tc_commit(&bar_m[buf]);
+            tc_commit(&bar_m);
         }
         tc_commit(&bar_done);
     }
     // ---- epilogue: warps 0-3, thread = row ------------------------------------------
     if (warp < 4) {
         const int m = tid;
+        // the row's super-block headers (d, dmin, scales), read again from
+        // global memory (L2) instead of being kept in shared memory
+        constexpr size_t RB = size_t(TC_NSB) * Q4K_BYTES;
+        const int r = (tile & 3) * TCM + m;
+        const uint8_t *W = tile < 4 ? (e < MOE_NEXP ? gate_exps + size_t(e) * MOE_FF * RB : gate_sh)
+                                    : (e < MOE_NEXP ? up_exps + size_t(e) * MOE_FF * RB : up_sh);
+        uint4 hdr[TC_NSB];
+#pragma unroll
+        for (int sb = 0; sb < TC_NSB; sb++) hdr[sb] = __ldg(reinterpret_cast<const uint4 *>(W + size_t(r) * RB + sb * Q4K_BYTES));
         tc_wait(&bar_done, 0);
         tc_fence_after();
         float acc[TCN];
 #pragma unroll
         for (int n = 0; n < TCN; n++) acc[n] = 0.0f;
         const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
+#pragma unroll 1
         for (int sb = 0; sb < TC_NSB; sb++) {
-            int H[32], Lo[32];
-            tmem_ld32(lane_addr + uint32_t(sb * 2 * TCN), H);
-            tmem_ld32(lane_addr + uint32_t(sb * 2 * TCN + TCN), Lo);
+            int H[TCN], Lo[TCN];
+            tmem_ld16(lane_addr + uint32_t(sb * 2 * TCN), H);
+            tmem_ld16(lane_addr + uint32_t(sb * 2 * TCN + TCN), Lo);
             tmem_wait_ld();
-            const float d = S.d[sb][m], dm = S.dm[sb][m];
-            const uint2 mp = *reinterpret_cast<const uint2 *>(S.mn[sb][m]);
-            const int mn[8] = {int(mp.x & 0xff), int((mp.x >> 8) & 0xff), int((mp.x >> 16) & 0xff), int(mp.x >> 24),
-                               int(mp.y & 0xff), int((mp.y >> 8) & 0xff), int((mp.y >> 16) & 0xff), int(mp.y >> 24)};
+            int sc[8], mn[8];
+            tc_q4k_scales(hdr[sb].y, hdr[sb].z, hdr[sb].w, sc, mn);
+            const float d = h2f(uint16_t(hdr[sb].x & 0xffffu)), dm = h2f(uint16_t(hdr[sb].x >> 16));
 #pragma unroll
             for (int n = 0; n < TCN; n++) {
                 const int4 b0 = *reinterpret_cast<const int4 *>(&S.bsum[n][sb * 8]);
@@ -250,12 +249,19 @@ __global__ void __launch_bounds__(256, 1) moe_gateup_tc_kernel(const uint8_t *__
     }
 }
 
-// QMA_CUDA_MMA_SYNC=1 in the environment: the grouped gate/up GEMM runs on
-// the previous tensor-core generation's warp-level MMAs (moe_gateup_kernel)
-// instead, as a cross-check (the same bits).
 bool tc_disabled() {
     const char *v = getenv("QMA_CUDA_MMA_SYNC");
     return v && atoi(v) != 0;
+}
+
+// The grouped gate/up GEMM takes this kernel only with QMA_CUDA_TC_GROUPED=1
+// in the environment: at the few pairs per expert of prefill chunks and
+// expert-parallel steps (N = 16 tiles, mostly empty) the warp-level MMA
+// kernel is faster, since the digit split doubles the unpacked weight bytes
+// the producers write for every 128 x 16 tile.  The same bits either way.
+bool tc_grouped() {
+    const char *v = getenv("QMA_CUDA_TC_GROUPED");
+    return v && atoi(v) != 0 && !tc_disabled();
 }
 
 int launch_gateup_tc(const qma_cuda_moe_weights &w, int T, const MoeScratch &s, cudaStream_t st, int g0, int ng) {

@@ -87,7 +87,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
         : "r"(taddr)
         : "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// QMA_CUDA_MMA_SYNC=1 in the environment: the int8 GEMMs run on the previous
+// tensor-core generation's warp-level MMAs (mma.sync) instead of tcgen05, as
+// a cross-check (the same bits).
+bool tc_disabled();
+// Bounded waits of the dense tcgen05 GEMM that ran out (reset by reading).
+int gemm_tc_wait_timeouts();
 
 // mbarrier arrival by this thread (a plain count of arrivals)
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {

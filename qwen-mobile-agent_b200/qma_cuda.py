@@ -247,7 +247,7 @@ class MoeWeights(C.Structure):
     _fields_ = [("post_norm", _vp), ("gate_inp", _vp), ("gate_exps", _vp), ("up_exps", _vp),
                 ("down_exps", _vp), ("gate_inp_shexp", _vp), ("gate_shexp", _vp),
                 ("up_shexp", _vp), ("down_shexp", _vp), ("down_type", _i32),
-                ("down_shexp_type", _i32)]
+                ("down_shexp_type", _i32), ("router_bias", _vp)]
 
 
 _SIGS["qma_cuda_model_moe_weights"] = (_i32, [_vp, _i32, C.POINTER(MoeWeights)])

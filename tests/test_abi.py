@@ -16,7 +16,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert Q.lib().qma_cuda_abi_version() == 1
+    assert Q.lib().qma_cuda_abi_version() == 2
 
 
 def test_bad_arguments_return_invalid_without_touching_the_device():

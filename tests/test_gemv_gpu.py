@@ -116,3 +116,37 @@ def test_matvec_is_deterministic(cuda, rng):
                Q.ptr(ds), Q.ptr(out), None)
         outs.append(out.cpu().numpy())
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+@pytest.mark.parametrize("shape", [(4096, 2048), (2048, 4096), (12352, 2048), (208, 2048)])
+@pytest.mark.parametrize("T", [64, 130, 512])
+def test_q4k_gemm_tcgen05_bit_identical_to_mma_sync(cuda, rng, shape, T):
+    """Prefill-sized Q4_K GEMMs (64+ tokens) on the 5th-generation tensor
+    cores (tcgen05 int8 MMAs into tensor memory, the sub-block scales folded
+    into two int8 digits of the weights, 128 x 128 tiles; partial row and
+    token tiles included) against the warp-level mma.sync kernel
+    (QMA_CUDA_MMA_SYNC=1): exact integer super-block sums and a shared fp32
+    fold, so the same bits; and against the oracle within the GEMV bar."""
+    import os
+    import torch
+    n_out, n_in = shape
+    W = O.synth_matrix(f"gemm.tc.{n_out}x{n_in}", O.Q4_K, n_out, n_in, seed=13)
+    x = rng.standard_normal((T, n_in)).astype(np.float32)
+    dq, dd, ds = gpu_quant(x)
+    dW = gpu_pack(W, O.Q4_K, n_out, n_in)
+    outs = {}
+    for form in ("tc", "sync"):
+        out = empty_dev((T, n_out), torch.float32)
+        if form == "sync":
+            os.environ["QMA_CUDA_MMA_SYNC"] = "1"
+        try:
+            Q.call("qma_cuda_matvec", O.Q4_K, Q.ptr(dW), n_in, n_out, T, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
+                   Q.ptr(out), None)
+            torch.cuda.synchronize()
+        finally:
+            os.environ.pop("QMA_CUDA_MMA_SYNC", None)
+        outs[form] = out.cpu().numpy()
+    a, b = outs["tc"], outs["sync"]
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"max |diff| {np.abs(a - b).max():.3e}"
+    want = O.matmul(x, W, O.Q4_K, n_in, n_out)
+    assert_close(a, want, RTOL, f"tc gemm {shape} T={T}")

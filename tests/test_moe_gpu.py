@@ -104,22 +104,53 @@ def test_moe_exact_fallback_on_ties(cuda, edit, scale):
 def test_grouped_gateup_tcgen05_bit_identical_to_mma_sync(layer, T):
     """The grouped path's gate/up GEMM on the 5th-generation tensor cores
     (tcgen05 int8 MMAs, accumulators in tensor memory, the Q4_K sub-block
-    scales folded into two int8 digits of the weights) against the
-    warp-level mma.sync kernel (QMA_CUDA_MMA_SYNC=1): the integer
-    super-block sums are exact in both and the fp32 fold is shared, so the
-    block's output is the same bits; both within the oracle's tolerance."""
+    scales folded into two int8 digits of the weights; QMA_CUDA_TC_GROUPED=1)
+    against the default warp-level mma.sync kernel: the integer super-block
+    sums are exact in both and the fp32 fold is shared, so the block's
+    output is the same bits; both within the oracle's tolerance."""
     import os
     rng = np.random.default_rng(900 + T)
     x2 = rng.standard_normal((T, 2048)).astype(np.float32)
-    got, gsel, _, _ = layer.gpu(x2)
-    os.environ["QMA_CUDA_MMA_SYNC"] = "1"
+    os.environ["QMA_CUDA_TC_GROUPED"] = "1"
     try:
-        ref, rsel, _, _ = layer.gpu(x2)
+        got, gsel, _, _ = layer.gpu(x2)
     finally:
-        del os.environ["QMA_CUDA_MMA_SYNC"]
+        del os.environ["QMA_CUDA_TC_GROUPED"]
+    ref, rsel, _, _ = layer.gpu(x2)
     assert np.array_equal(gsel, rsel)
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), \
         f"max |diff| {np.abs(got - ref).max():.3e}"
     want, wsel, _ = layer.oracle(x2)
     assert np.array_equal(gsel, wsel)
     assert_close(got, want, 1e-3, f"moe tc T={T}")
+
+
+def test_router_bias_zipf_prior_routes_like_the_oracle(layer):
+    """configs[4]'s serving workload biases the router: each fp32 logit gets
+    log p(rank) of a Zipf(1.1) prior over a seeded expert ranking, which
+    skews the expert load.  The biased routing must equal the oracle's
+    (reference router + one fp32 addition per logit) expert for expert, in
+    the per-token kernel (T = 3) and the grouped path (T = 40); outputs
+    within the north-star tolerance."""
+    import oracle as O
+    import torch
+    bias = O.zipf_router_bias(seed=11, layer=0)
+    db = torch.from_numpy(bias).cuda()
+    layer.w.router_bias = db.data_ptr()
+    try:
+        for T in (3, 40):
+            x2 = np.random.default_rng(1100 + T).standard_normal((T, 2048)).astype(np.float32)
+            got, gsel, gw, _ = layer.gpu(x2)
+            want = np.zeros_like(x2)
+            wsel = np.zeros((T, 8), np.int32)
+            ww = np.zeros((T, 8), np.float32)
+            O.lib().qo_moe_block_biased(layer.model, 0, O._ptr(x2), T, O._ptr(bias), O._ptr(want), O._ptr(wsel),
+                                        O._ptr(ww))
+            assert np.array_equal(gsel, wsel), T
+            assert np.abs(gw - ww).max() < 1e-5
+            assert_close(got, want, 1e-3, f"biased moe T={T}")
+            # the prior concentrates the selections on the top-ranked experts
+            rank = np.argsort(np.argsort(-bias))
+            assert np.median(rank[gsel]) < 32
+    finally:
+        layer.w.router_bias = None
