@@ -232,7 +232,7 @@ __device__ __forceinline__ void prefetch_l2_range(const void *p, size_t bytes) {
 
 // ------------------------------------------- bulk copies into shared memory --
 // Global -> this CTA's shared memory through the TMA engine (non-tensor
-// cp.async.bulk, no multicast), completion counted in bytes on an mbarrier.
+// cp.async.bulk into this CTA alone), completion counted in bytes on an mbarrier.
 // Addresses 16-byte aligned, sizes multiples of 16.
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

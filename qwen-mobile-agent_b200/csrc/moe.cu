@@ -548,6 +548,207 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     }
 }
 
+// Router of several tokens (prefill chunks, expert-parallel steps): the
+// single-token kernel's arithmetic, with each cluster taking RTPC tokens so
+// that its 2 MB of router rows are staged into shared memory once per RTPC
+// tokens instead of once per token.  Every warp computes its row's logits
+// for the cluster's tokens in turn; the leader's warps 0..RTPC-1 select the
+// tokens' top 8 side by side, then any token the bounds leave open takes
+// the exact path in turn (the whole CTA, the candidate rows staged through
+// the consumed row buffer as above).
+constexpr int RTPC = 4;                       // tokens per router cluster
+struct RouterMultiSmem {
+    float rows[RROWS][MOE_EMBD];              // this CTA's router rows (128 KB)
+    float xn[RTPC][MOE_EMBD];
+    double S[RTPC][MOE_NEXP], B[RTPC][MOE_NEXP];
+};
+constexpr size_t ROUTER_MULTI_SMEM = sizeof(RouterMultiSmem);
+
+__global__ void __launch_bounds__(RTHREADS, 1) moe_router_multi_kernel(const float *__restrict__ x2, int T,
+                                                                     const float *__restrict__ post_norm,
+                                                                     const float *__restrict__ Wr,
+                                                                     const float *__restrict__ gis,
+                                                                     MoeScratch s, int *sel_out, float *w_out,
+                                                                     const float *__restrict__ bias) {
+    QMA_TRACE_SCOPE(TK_ROUTER);
+    extern __shared__ __align__(128) uint8_t rmsm_raw[];
+    RouterMultiSmem &R = *reinterpret_cast<RouterMultiSmem *>(rmsm_raw);
+    const unsigned rank = cluster_rank();
+    cluster_arrive();
+    const int t0 = blockIdx.y * RTPC, nt = min(RTPC, T - t0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = RTHREADS / 32;
+    __shared__ __align__(8) uint64_t rbar;
+    __shared__ double dred[RTPC][NW];
+    __shared__ float gpart[RTPC][MOE_EMBD / 256];
+    __shared__ int need_exact[RTPC], ncand;
+    __shared__ int cls[MOE_NEXP];
+    __shared__ int top9[RTPC][MOE_TOPK + 1];
+    __shared__ int cand[MOE_NEXP];
+    const int e0 = int(rank) * RROWS + warp;
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_init(&rbar, 1);
+            mbar_fence_init();
+            mbar_expect_tx(&rbar, ROUTER_SMEM);
+        }
+        __syncwarp();
+        bulk_g2s_warp(&R.rows[0][0], Wr + size_t(rank) * RROWS * MOE_EMBD, ROUTER_SMEM, &rbar, lane);
+    }
+    float gisv[8] = {};
+    if (rank < MOE_EMBD / 256 && warp == 0) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gis + rank * 256 + lane * 8));
+        const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gis + rank * 256 + lane * 8 + 4));
+        gisv[0] = g0.x; gisv[1] = g0.y; gisv[2] = g0.z; gisv[3] = g0.w;
+        gisv[4] = g1.x; gisv[5] = g1.y; gisv[6] = g1.z; gisv[7] = g1.w;
+    }
+    pdl_trigger();
+    pdl_wait();
+    // ---- xn of each token (rms_norm_m, nn.c:348-357) ---------------------------
+    constexpr int XPT = MOE_EMBD / RTHREADS;
+    float xv[RTPC][XPT];
+#pragma unroll
+    for (int u = 0; u < RTPC; u++) {
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < XPT; k++) {
+            xv[u][k] = u < nt ? x2[size_t(t0 + u) * MOE_EMBD + tid + RTHREADS * k] : 0.0f;
+            ss += double(xv[u][k]) * double(xv[u][k]);
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) dred[u][warp] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < RTPC; u++) {
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < NW; w++) tot += dred[u][w];
+        const float r = 1.0f / sqrtf(float(tot / MOE_EMBD) + 1e-6f);
+#pragma unroll
+        for (int k = 0; k < XPT; k++) {
+            const int i = tid + RTHREADS * k;
+            R.xn[u][i] = __fmul_rn(__fmul_rn(xv[u][k], r), post_norm[i]);
+        }
+    }
+    __syncthreads();
+    // ---- the tokens' exact logits of this warp's row ------------------------------
+    if (!mbar_wait(&rbar, 0)) {
+        if (lane == 0) atomicAdd(&g_moe_timeouts, 1u);
+        mbar_wait(&rbar, 0);
+    }
+    cluster_wait();
+    for (int u = 0; u < nt; u++) {
+        double S0, B0;
+        router_logit(&R.rows[warp][0], R.xn[u], lane, S0, B0);
+        if (bias) bias_interval(S0, B0, __ldg(bias + e0));
+        if (lane == 0) {
+            st_cluster_f64(cluster_map(&R.S[u][e0], 0), S0);
+            st_cluster_f64(cluster_map(&R.B[u][e0], 0), B0);
+        }
+    }
+    // ---- Q8_K block `rank` of each token's xn, its shared-expert gate part ---
+    if (rank < MOE_EMBD / 256 && warp == 0) {
+        const int blk = int(rank), i0 = blk * 256 + lane * 8;
+        for (int u = 0; u < nt; u++) {
+            const int t = t0 + u;
+            const float4 a0 = *reinterpret_cast<const float4 *>(&R.xn[u][i0]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&R.xn[u][i0 + 4]);
+            const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            int q[8];
+            float sc;
+            q8k_block_warp_q(v, lane, s.xq + size_t(t) * MOE_EMBD + blk * 256,
+                             s.xd + size_t(t) * (MOE_EMBD / 256) + blk,
+                             s.xs + size_t(t) * (MOE_EMBD / 16) + blk * 16, q, sc);
+            float gp = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) gp += __fmul_rn(__fmul_rn(gisv[c], float(q[c])), sc);
+            gp = warp_sum(gp);
+            if (lane == 0) st_cluster_f32(cluster_map(&gpart[u][blk], 0), gp);
+        }
+    }
+    cluster_sync();
+    if (rank != 0) return;
+
+    // ---- leader: each token's top 8 -----------------------------------------------
+    if (warp < nt) {
+        const bool ok = select_fast(R.S[warp], R.B[warp], lane, top9[warp]);
+        if (lane == 0) need_exact[warp] = !ok;
+    }
+    __syncthreads();
+    uint32_t phase = 1;
+    for (int u = 0; u < nt; u++) {
+        if (!need_exact[u]) continue;                  // CTA-uniform
+        double *sS = R.S[u], *sB = R.B[u];
+        const int *tp = top9[u];
+        if (tid == 0) ncand = 0;
+        __syncthreads();
+        const double mx = sS[tp[0]];
+        const int e8 = tp[MOE_TOPK - 1];
+        double thresh = INFINITY;
+#pragma unroll
+        for (int k = 0; k < MOE_TOPK; k++) thresh = fmin(thresh, sS[tp[k]] - sB[tp[k]]);
+        if (tid < MOE_NEXP) {
+            cls[tid] = p_class(sS[tid], mx);
+            if (cls[tid] > 0 && sS[tid] + sB[tid] >= thresh - 1e-6 * (1.0 + fabs(sS[e8])))
+                cand[atomicAdd(&ncand, 1)] = tid;
+        }
+        __syncthreads();
+        for (int base = 0; base < ncand; base += RROWS, phase ^= 1) {
+            const int nb = min(RROWS, ncand - base);
+            if (warp == 0) {
+                fence_proxy_async_smem();
+                if (lane == 0) mbar_expect_tx(&rbar, uint32_t(nb) * ROW_BYTES);
+                __syncwarp();
+                for (int c = 0; c < nb; c++)
+                    bulk_g2s_warp(&R.rows[c][0], Wr + size_t(cand[base + c]) * MOE_EMBD, ROW_BYTES, &rbar, lane);
+            }
+            if (!mbar_wait(&rbar, phase)) {
+                if (tid == 0) atomicAdd(&g_moe_timeouts, 1u);
+                mbar_wait(&rbar, phase);
+            }
+            if (tid < nb) {
+                const int e = cand[base + tid];
+                const float l = router_logit_seq(&R.rows[tid][0], R.xn[u]);
+                sS[e] = double(bias ? __fadd_rn(l, bias[e]) : l);
+                sB[e] = 0.0;
+            }
+            __syncthreads();
+        }
+        if (warp == 0) {
+            double m2 = -INFINITY;
+            for (int j = 0; j < 8; j++) m2 = fmax(m2, sS[lane + 32 * j]);
+            m2 = warp_max_d(m2);
+            for (int j = 0; j < 8; j++) cls[lane + 32 * j] = p_class(sS[lane + 32 * j], m2);
+            __syncwarp();
+            select_top8(sS, sB, cls, lane, top9[u]);
+        }
+        __syncthreads();
+    }
+    if (warp < nt) {
+        const int u = warp, t = t0 + u;
+        const double *sS = R.S[u];
+        const float l0 = float(sS[top9[u][0]]);
+        const float ev = lane < MOE_TOPK ? expf(float(sS[top9[u][lane]]) - l0) : 0.0f;
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MOE_TOPK; k++) sum += __shfl_sync(0xffffffffu, ev, k);
+        if (lane < MOE_TOPK) {
+            const float wk = ev / sum;
+            const int e = top9[u][lane];
+            s.sel[t * MOE_TOPK + lane] = e;
+            s.w[t * MOE_TOPK + lane] = wk;
+            if (sel_out) sel_out[t * MOE_TOPK + lane] = e;
+            if (w_out) w_out[t * MOE_TOPK + lane] = wk;
+        } else if (lane == MOE_TOPK) {
+            float g = 0.0f;
+            for (int b = 0; b < MOE_EMBD / 256; b++) g += gpart[u][b];
+            s.gs[t] = 1.0f / (1.0f + expf(-g));
+            s.fallback[t] = need_exact[u];
+        }
+    }
+}
+
 // ---------------------------------------------------------------- experts --
 __device__ __forceinline__ Q6Planes shift_rows(Q6Planes P, int r0, int n) {
     P.ql += size_t(r0) * (n / 2);
@@ -905,6 +1106,9 @@ static int moe_attrs() {
     if (g_moe_attrs.done()) return QMA_CUDA_OK;
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ROUTER_SMEM)));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_multi_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_router_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(ROUTER_MULTI_SMEM)));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ4K>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     QMA_CHECK_CUDA(cudaFuncSetAttribute(moe_expert_kernel<FmtQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(EXPERT_SMEM)));
@@ -917,12 +1121,22 @@ static int moe_attrs() {
     return QMA_CUDA_OK;
 }
 
+// The router for T tokens: the single-token kernel per token below 8 tokens
+// (decode), the multi-token kernel (RTPC tokens per cluster) from 8 on.
+static cudaError_t launch_router(const qma_cuda_moe_weights &w, const float *x2, int T, const MoeScratch &s, int *sel,
+                                 float *wts, cudaStream_t st, bool pdl) {
+    if (T >= 8)
+        return launch_ex(moe_router_multi_kernel, dim3(RCL, (T + RTPC - 1) / RTPC), dim3(RTHREADS), ROUTER_MULTI_SMEM,
+                         st, RCL, pdl, x2, T, w.post_norm, w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias);
+    return launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
+                     w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias);
+}
+
 int moe_route(const qma_cuda_moe_weights &w, const float *x2, int T, const MoeScratch &s, int *sel, float *wts,
               cudaStream_t st) {
     int rc = moe_attrs();
     if (rc) return rc;
-    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, false, x2,
-                             w.post_norm, w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias));
+    QMA_CHECK_CUDA(launch_router(w, x2, T, s, sel, wts, st, false));
     return QMA_CUDA_OK;
 }
 
@@ -942,8 +1156,7 @@ int moe_layer(const qma_cuda_moe_weights &w, const float *x2, int T, float *x_ou
         QMA_CHECK_CUDA(cudaMemsetAsync(s.dcount, 0, sizeof(unsigned) * T * MOE_DOWN_CHUNKS, st));
     }
     const bool pdl = pdl_enabled() && !clear_counters;
-    QMA_CHECK_CUDA(launch_ex(moe_router_kernel, dim3(RCL, T), dim3(RTHREADS), ROUTER_SMEM, st, RCL, pdl, x2, w.post_norm,
-                             w.gate_inp, w.gate_inp_shexp, s, sel, wts, w.router_bias));
+    QMA_CHECK_CUDA(launch_router(w, x2, T, s, sel, wts, st, pdl));
     if (s.goff && w.down_type == QMA_TYPE_Q6_K) {
         // a chunk of tokens: experts grouped, tensor-core MMAs, then the combine
         // (and the next norm when asked) in one kernel

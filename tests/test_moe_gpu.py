@@ -85,12 +85,15 @@ def _aligned_inputs(L, T, scale, seed):
     return (rng.standard_normal((T, 2048)) + scale * np.sign(W0)[None, :]).astype(np.float32)
 
 
+@pytest.mark.parametrize("T", [6, 13], ids=["per_token_router", "multi_token_router"])
 @pytest.mark.parametrize("edit,scale", [(_near_tie_router, 0.3), (_underflow_router, 3.0)],
                          ids=["near_ties", "underflow_ties"])
-def test_moe_exact_fallback_on_ties(cuda, edit, scale):
+def test_moe_exact_fallback_on_ties(cuda, edit, scale, T):
+    """T = 6 runs the one-token-per-cluster router, T = 13 the router of 4
+    tokens per cluster (a last cluster of one token)."""
     L = MoeLayer(il=0, seed=0, edit_router=edit)
     try:
-        x2 = _aligned_inputs(L, 6, scale, seed=11)
+        x2 = _aligned_inputs(L, T, scale, seed=11)
         want, wsel, _ = L.oracle(x2)
         got, gsel, _, fallbacks = L.gpu(x2)
         assert fallbacks > 0, "crafted ties should need the exact recompute"
