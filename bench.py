@@ -49,6 +49,7 @@ N_VOCAB = 151936
 PROMPT = 8192
 N_CTX = 65536
 SEED = 0
+BATCH_SEQS, BATCH_PROMPT, BATCH_DECODE = 64, 2048, 128     # configs[4]
 
 
 def load_peaks():
@@ -314,6 +315,7 @@ def run_decode_ours(args, world, rank, local):
     moe_us = dist_max(time_moe_blocks(wts, 8, local), world)
     moe_b = moe_block_bytes(arr, n)
     ep = None if args.no_ep else run_ep_on_model(model, wts, args, world, rank, local)
+    batch = None if args.no_batch else run_batch_on_model(model, wts, args, world, rank, local)
 
     value = world * args.steps / (ms / 1e3)
     e2e_value = world * e2e_steps / (e2e_ms / 1e3)
@@ -366,10 +368,13 @@ def run_decode_ours(args, world, rank, local):
         "cpu_baseline": cpu,
         "gemv": gemv,
         "ep": ep,
+        "batch": batch,
     }
     print(json.dumps(line), flush=True)
     if ep is not None and not ep.get("ep_parity"):
         sys.exit("expert-parallel parity check failed: " + json.dumps(ep.get("parity_detail")))
+    if batch is not None and not batch.get("parity"):
+        sys.exit("batched decode parity check failed: " + json.dumps(batch.get("parity_detail")))
 
 
 def host_blob_for_reference(threads):
@@ -575,6 +580,162 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
         "router_prior": "log Zipf(s=1.1) over a seeded per-layer expert ranking, added to every router logit",
         "expert_load": expert_load,
         "collectives": "per layer: NCCL all-gather of the counts, grouped send/recv dispatch and return",
+    }
+
+
+def dist_gather_i64(vals, world):
+    """vals (int64 [k], the same k on every rank) of every rank, in rank
+    order (an NCCL all-gather through the process group)."""
+    vals = np.ascontiguousarray(vals, np.int64)
+    if world == 1:
+        return [vals]
+    import torch
+    import torch.distributed as dist
+    t = torch.from_numpy(vals).cuda()
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.cpu().numpy() for o in out]
+
+
+def logits_digest(rows):
+    """One int64 per logits row: a hash of its exact bytes."""
+    import hashlib
+    return np.array([int.from_bytes(hashlib.blake2b(np.ascontiguousarray(r).tobytes(), digest_size=8).digest(),
+                                    "little", signed=True) for r in rows], np.int64)
+
+
+def run_batch_on_model(model, full_w, args, world, rank, local):
+    """configs[4] end to end: 64 concurrent sequences of the full model,
+    each prefilled with its own 2048-token prompt (seeded ids, untimed), then
+    decoded greedily in batched steps of one token per sequence
+    (qma_cuda_batch_eval: host token ids in, greedy ids out) to 128 tokens
+    each, the router biased by the log-Zipf(1.1) prior.  At N > 1 the 64
+    sequences are split 64/N per GPU (attention and gated-delta state are
+    per sequence) and every MoE block runs expert-parallel over the N GPUs
+    (experts sharded 256/N, NCCL exchange per layer).
+
+    Parity, before timing, on 64 sequences with 32-token prompts and three
+    decode steps: at N > 1 every sequence's logits must equal, bit for bit,
+    those of rank 0 decoding all 64 sequences alone on one GPU (local MoE
+    blocks); at N = 1 a 64-row step must equal the same sequences stepped
+    as four steps of 16 rows.  A mismatch makes the run exit non-zero."""
+    import ctypes as C
+    import torch
+    import oracle as O
+    import qma_cuda as Q
+    dev = torch.device("cuda", local)
+    n_here = BATCH_SEQS // world
+    first = rank * n_here
+    bias_d = [torch.from_numpy(O.zipf_router_bias(SEED, il)).to(dev) for il in range(len(full_w))]
+    for il, b in enumerate(bias_d):
+        Q.call("qma_cuda_model_set_router_bias", model.h, il, b.data_ptr())
+    ep, shard = None, None
+    if world > 1:
+        e0, n_local = Q.ep_shard(rank, world)
+        shard = []
+        for w, b in zip(full_w, bias_d):
+            s_ = shard_weights(w, e0, n_local)
+            s_.router_bias = b.data_ptr()
+            shard.append(s_)
+        ep = Q.ExpertParallel(local, rank, world, n_here, ep_share_uid(world), timeout_ms=300000)
+
+    def prompts(n_tok, seed):
+        return [np.random.default_rng([seed, g]).integers(0, N_VOCAB, n_tok).astype(np.int32)
+                for g in range(BATCH_SEQS)]
+
+    def prefill(batch, pr, ids):
+        sids = np.concatenate([np.full(len(pr[g]), i, np.int32) for i, g in enumerate(ids)])
+        lo, g = batch.eval(sids, np.concatenate([pr[g] for g in ids]), logits=False, greedy=True)
+        ends = np.cumsum([len(pr[g]) for g in ids]) - 1
+        return g[ends].astype(np.int32)
+
+    # ---- parity ----------------------------------------------------------------
+    P_TOK, P_STEPS = 32, 3
+    pr = prompts(P_TOK, SEED + 11)
+    mine = list(range(first, first + n_here))
+    b = Q.Batch(model, n_here, 4096)
+    tok = prefill(b, pr, mine)
+    if ep is not None:
+        b.set_ep(ep, shard)
+    sids = np.arange(n_here, dtype=np.int32)
+    digests = []
+    for _ in range(P_STEPS):
+        lo, g = b.eval(sids, tok)
+        digests.append(logits_digest(lo))
+        tok = g.astype(np.int32)
+    b.close()
+    got = np.concatenate([np.concatenate(dist_gather_i64(d, world)) for d in digests])
+    ok, detail = True, {}
+    if rank == 0:
+        ref = Q.Batch(model, BATCH_SEQS, 4096)
+        tok = prefill(ref, pr, list(range(BATCH_SEQS)))
+        allids = np.arange(BATCH_SEQS, dtype=np.int32)
+        want = []
+        for _ in range(P_STEPS):
+            if world > 1:
+                lo, g = ref.eval(allids, tok)
+            else:
+                lo = np.empty((BATCH_SEQS, N_VOCAB), np.float32)
+                g = np.empty(BATCH_SEQS, np.int32)
+                for q in range(0, BATCH_SEQS, 16):
+                    l_, g_ = ref.eval(allids[q:q + 16], tok[q:q + 16])
+                    lo[q:q + 16], g[q:q + 16] = l_, g_
+            want.append(logits_digest(lo))
+            tok = g.astype(np.int32)
+        ref.close()
+        want = np.concatenate(want)
+        ok = bool(np.array_equal(got, want))
+        detail = {"rows_compared": int(want.size), "rows_equal": int((got == want).sum()),
+                  "reference": "rank 0 alone, all 64 sequences, local MoE blocks" if world > 1
+                  else "the same sequences stepped 16 rows at a time"}
+    ok = dist_min(float(ok), world) > 0.5
+
+    # ---- timed: 2048-token prompts, 128 decode tokens per sequence ----------------
+    pr = prompts(BATCH_PROMPT, SEED + 12)
+    b = Q.Batch(model, n_here, BATCH_PROMPT + 256)
+    t0 = time.time()
+    tok = prefill(b, pr, mine)
+    t_prefill = dist_max(time.time() - t0, world)
+    if ep is not None:
+        b.set_ep(ep, shard)
+    stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(Q.lib().qma_cuda_batch_seq(b.h, 0)),
+                                       device=local)
+    warm = max(args.warmup, 3)
+    steps = max(1, BATCH_DECODE - warm)
+    for _ in range(warm):
+        _, g = b.eval(sids, tok, logits=False)
+        tok = g.astype(np.int32)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(steps):
+        _, g = b.eval(sids, tok, logits=False)
+        tok = g.astype(np.int32)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_ms = dist_max(ev0.elapsed_time(ev1), world)
+    n_pos = b.n_pos(0)
+    b.close()
+    if ep is not None:
+        ep.close()
+    for il in range(len(full_w)):
+        Q.call("qma_cuda_model_set_router_bias", model.h, il, None)
+    torch.cuda.synchronize()
+    del bias_d
+    value = BATCH_SEQS * steps / (t_ms / 1e3)
+    return {
+        "metric": "batched decode tok/s @N (configs[4]: 64 sequences, full model, EP over N GPUs)",
+        "tok_per_s": round(value, 1), "ms_per_step": round(t_ms / steps, 3), "n_ranks": world,
+        "sequences": BATCH_SEQS, "sequences_per_gpu": n_here, "prompt_tokens": BATCH_PROMPT,
+        "decode_tokens_per_sequence": warm + steps, "timed_steps": steps, "positions_at_end": n_pos,
+        "prefill_s": round(t_prefill, 2),
+        "moe": "expert-parallel, 256/N experts per GPU, NCCL exchange per layer" if world > 1
+               else "local (all 256 experts on the GPU)",
+        "api": "qma_cuda_batch_eval per step: token ids H2D, greedy ids D2H, host loop",
+        "h2d_bytes_per_step": n_here * 8, "d2h_bytes_per_step": n_here * 4,
+        "router_prior": "log Zipf(s=1.1) over a seeded per-layer expert ranking",
+        "parity": ok, "parity_detail": detail,
     }
 
 
@@ -1088,6 +1249,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ep", action="store_true", help="decode: skip the expert-parallel leg")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the configs[1] GEMV leg")
+    ap.add_argument("--no-batch", action="store_true", help="decode: skip the configs[4] batched-decode leg")
     ap.add_argument("--rows", type=int, default=GN_OUT, help="gemv: output rows")
     ap.add_argument("--cols", type=int, default=GN_IN, help="gemv: input columns (multiple of 256)")
     ap.add_argument("--prompt", type=int, default=PROMPT,

@@ -229,6 +229,46 @@ int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int 
 int qma_cuda_eval_hidden(qma_cuda_model *m, qma_cuda_state *s, const int *tokens,
                          int n_tokens, int n_layers, float *hidden);
 
+/* ---- multi-sequence state ------------------------------------------------
+ * n_seq sequences of n_ctx positions each, decoded together: the state of a
+ * serving loop with many concurrent sequences (each sequence is a full
+ * runstate_t, qma.h:254-276, with its own KV ring, recurrent state and HCM
+ * tiers; the reference runs one sequence per process).  All sequences of a
+ * batch run on one stream. */
+typedef struct qma_cuda_batch qma_cuda_batch;
+int qma_cuda_batch_create(qma_cuda_model *m, int n_seq, int n_ctx, qma_cuda_batch **out);
+int qma_cuda_batch_free(qma_cuda_batch *b);
+int qma_cuda_batch_n_seq(const qma_cuda_batch *b);
+/* Sequence seq's own state (owned by the batch; qma_cuda_state_n_pos,
+ * _save, _load and qma_cuda_eval work on it), or NULL. */
+qma_cuda_state *qma_cuda_batch_seq(qma_cuda_batch *b, int seq);
+
+/* qma_eval over several sequences (nn.c:2056-2308 per sequence):
+ * tokens[i] is appended to sequence seq_ids[i] (0..n_seq-1), each
+ * sequence's tokens in the order given.  The sequences given one token are
+ * evaluated together in batched steps of up to 512 (one token per
+ * sequence: the projections, router, experts and LM head run once over all
+ * rows; the conv, gated-delta recurrence and attention of each row use its
+ * own sequence's state); a sequence given several tokens (a prompt) is
+ * prefilled through its own state first.  For the last token of each
+ * sequence in the call, row i of logits (host [n_tokens][n_vocab],
+ * optional) receives its logits and greedy[i] (host int [n_tokens],
+ * optional) its argmax (lowest id on ties); other rows are left as they
+ * are.  Sequences are independent: a sequence's results do not depend on
+ * which others share its steps, as long as the steps have the same kind
+ * of rows (16 or more, the grouped expert path). */
+int qma_cuda_batch_eval(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n_tokens,
+                        float *logits, int *greedy);
+/* Parity entry point: one token per sequence, the first n_layers layers
+ * (0..40) of a batched step; hidden (host [n_tokens][2048]) receives the
+ * residual stream after them, row i for tokens[i].  The sequences advance
+ * as in qma_cuda_batch_eval. */
+int qma_cuda_batch_eval_hidden(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n_tokens,
+                               int n_layers, float *hidden);
+/* Device logits [rows][n_vocab] of the last batched step (row t for its
+ * t-th sequence in ascending id order). */
+const float *qma_cuda_batch_logits(const qma_cuda_batch *b);
+
 /* ---- layer-level parity points -------------------------------------------
  * One layer's mixer (the half before the MoE block) on caller activations,
  * against the state's per-layer memory.  x: device float [n_tokens][2048],
@@ -336,6 +376,12 @@ typedef struct {
  * per-layer ffn_* pointers and weight types of qma_t's layers[]
  * (qma.h:202-212) that moe_ffn reads (nn.c:509-649). */
 int qma_cuda_model_moe_weights(const qma_cuda_model *m, int layer, qma_cuda_moe_weights *out);
+/* Set (or, with NULL, clear) the router bias of layer `layer`'s MoE block
+ * for every later evaluation with this model (device float [256], owned by
+ * the caller, see qma_cuda_moe_weights.router_bias).  A state's captured
+ * decode step keeps the pointer it was captured with: set the bias before
+ * the first single-token evaluation of a state. */
+int qma_cuda_model_set_router_bias(qma_cuda_model *m, int layer, const float *bias);
 
 /* Device scratch bytes qma_cuda_moe_layer needs for T tokens. */
 size_t qma_cuda_moe_scratch_bytes(int T);
@@ -441,6 +487,14 @@ int qma_cuda_ep_free(qma_cuda_ep *ep);
  * expert at offset 0) and the down projections must be Q6_K. */
 int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const float *x2,
                           int T, float *x_out, int32_t *sel, float *wts, void *stream);
+
+/* Route the MoE blocks of a batch's steps through the expert-parallel
+ * exchange: shard points at 40 per-layer weight views (this rank's expert
+ * shard, as qma_cuda_ep_moe_layer takes them).  Every rank then calls
+ * qma_cuda_batch_eval in lockstep, one token for each of at most t_max
+ * sequences per call (a data-parallel share of the sequences per rank);
+ * ep NULL goes back to the local MoE block. */
+int qma_cuda_batch_set_ep(qma_cuda_batch *b, qma_cuda_ep *ep, const qma_cuda_moe_weights *shard);
 
 /* Bytes this rank sent and received in its last qma_cuda_ep_moe_layer call
  * (itself included) and the rows its experts served. */

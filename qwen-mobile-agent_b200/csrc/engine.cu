@@ -114,6 +114,7 @@ struct qma_cuda_state {
     // joined before the next attention layer (or the end of the step)
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool shared_stream = false;     // st / side belong to a batch
     static constexpr int HCM_REBUILD_INIT = 128;
 };
 
@@ -416,14 +417,21 @@ static int grow(float **p, size_t *cap, size_t need) {
     return QMA_CUDA_OK;
 }
 
-static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out) {
+// shared: a stream the state runs on (its salience updates included)
+// instead of streams of its own, for the sequences of a batch.
+static int create_state(qma_cuda_model *m, int n_ctx, qma_cuda_state **out, cudaStream_t shared = nullptr) {
     QMA_REQUIRE(m && out && n_ctx > HCM_SINK + 1, "state: bad arguments (n_ctx %d)", n_ctx);
     QMA_CHECK_CUDA(cudaSetDevice(m->device));
     qma_cuda_state *s = new qma_cuda_state();
     s->m = m;
     s->n_ctx = n_ctx;
-    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-    QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    if (shared) {
+        s->st = s->side = shared;
+        s->shared_stream = true;
+    } else {
+        QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+        QMA_CHECK_CUDA(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    }
     QMA_CHECK_CUDA(cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming));
     QMA_CHECK_CUDA(cudaEventCreateWithFlags(&s->ev_join, cudaEventDisableTiming));
     cudaStream_t st = s->st;
@@ -799,6 +807,24 @@ static int mixer(qma_cuda_state *s, int il, int T, int nk_cap, int pv_chunk, boo
     return QMA_CUDA_OK;
 }
 
+// A layer's output projection, router and shared expert go into L2 while
+// its input projection and mixer run.
+static Prefetch layer_plan(const qma_cuda_model *m, int il) {
+    const LayerW &L = m->L[il];
+    Prefetch pf;
+    pf.p[0] = L.out_proj;
+    pf.bytes[0] = packed_bytes(L.out_type, EMBD, is_attn(il) ? WO_DIM : VAL_DIM);
+    pf.p[1] = L.moe.gate_inp;
+    pf.bytes[1] = sizeof(float) * size_t(EMBD) * 256;
+    pf.p[2] = L.moe.gate_shexp;
+    pf.bytes[2] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
+    pf.p[3] = L.moe.up_shexp;
+    pf.bytes[3] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
+    pf.p[4] = L.moe.down_shexp;
+    pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
+    return pf;
+}
+
 // The forward of T tokens at the positions in *sp_dev (host copy hs):
 // embedding -> 40 layers -> (optionally) final norm + LM head.
 static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_dev, int nk_cap,
@@ -811,23 +837,7 @@ static int forward(qma_cuda_state *s, const StepParams &hs, const int *tokens_de
     TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, tokens_dev, s->sp_dev, T, s->x, st));
     const int pv_chunk = attn_span(T, nk_cap);
     bool side_pending = false;     // a salience update is running on s->side
-    // a layer's output projection, router and shared expert go into L2
-    // while its input projection and mixer run
-    auto plan = [&](int il) {
-        const LayerW &L = m->L[il];
-        Prefetch pf;
-        pf.p[0] = L.out_proj;
-        pf.bytes[0] = packed_bytes(L.out_type, EMBD, is_attn(il) ? WO_DIM : VAL_DIM);
-        pf.p[1] = L.moe.gate_inp;
-        pf.bytes[1] = sizeof(float) * size_t(EMBD) * 256;
-        pf.p[2] = L.moe.gate_shexp;
-        pf.bytes[2] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
-        pf.p[3] = L.moe.up_shexp;
-        pf.bytes[3] = packed_bytes(QMA_TYPE_Q4_K, 512, EMBD);
-        pf.p[4] = L.moe.down_shexp;
-        pf.bytes[4] = packed_bytes(L.moe.down_shexp_type, EMBD, 512);
-        return pf;
-    };
+    auto plan = [&](int il) { return layer_plan(m, il); };
     bool normed = false;           // s->xq already holds the next norm's output
     for (int il = 0; il < n_layers; il++) {
         const LayerW &L = m->L[il];
@@ -1278,6 +1288,13 @@ int qma_cuda_ecache_held(const qma_cuda_model *m) {
     return m->ec_held;
 }
 
+int qma_cuda_model_set_router_bias(qma_cuda_model *m, int layer, const float *bias) {
+    qma::clear_error();
+    QMA_REQUIRE(m && layer >= 0 && layer < qma::NLAYER, "qma_cuda_model_set_router_bias: bad arguments");
+    m->L[layer].moe.router_bias = bias;
+    return QMA_CUDA_OK;
+}
+
 int qma_cuda_model_moe_weights(const qma_cuda_model *m, int layer, qma_cuda_moe_weights *out) {
     qma::clear_error();
     QMA_REQUIRE(m && out && layer >= 0 && layer < qma::NLAYER, "qma_cuda_model_moe_weights: bad layer %d", layer);
@@ -1302,8 +1319,10 @@ int qma_cuda_state_free(qma_cuda_state *s) {
     cudaStreamSynchronize(s->side);
     cudaEventDestroy(s->ev_fork);
     cudaEventDestroy(s->ev_join);
-    cudaStreamDestroy(s->side);
-    cudaStreamDestroy(s->st);
+    if (!s->shared_stream) {
+        cudaStreamDestroy(s->side);
+        cudaStreamDestroy(s->st);
+    }
     delete s;
     return QMA_CUDA_OK;
 }
@@ -1661,5 +1680,349 @@ int qma_cuda_state_load(qma_cuda_state *s, const char *state_path, const char *k
     if (salience_path && (rc = load_salience(s, salience_path))) return rc;
     return QMA_CUDA_OK;
 }
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ batch --
+// n_seq sequences decoded together (the multi-sequence state of a serving
+// loop; the reference's runstate_t, qma.h:254-276, is one sequence, and
+// qma_eval, nn.c:2056-2308, runs one).  Each sequence is a full state of
+// its own (KV ring, recurrent state, HCM tiers) on the batch's stream.  A
+// step of one token from each of T sequences runs the token-parallel work
+// once over all T rows: the RMSNorms, the input and output projections
+// (the tensor-core GEMM from 8 rows on), the router and experts (the
+// grouped path from 16 rows on, or the expert-parallel exchange), the LM
+// head; the mixers run per sequence: the conv and gated-delta recurrence as
+// one launch that looks up each row's own state through a pointer table,
+// attention (its KV ring, live index and salience) once per sequence.
+// Sequences given several tokens in one call are prefilled through their
+// own state (the single-sequence chunked path).
+struct qma_cuda_batch {
+    qma_cuda_model *m = nullptr;
+    int n_seq = 0, n_ctx = 0, t_step = 0;        // t_step: rows per batched step
+    cudaStream_t st = nullptr;
+    std::vector<qma_cuda_state *> seqs;
+    qma_cuda_state *work = nullptr;              // activations of a batched step
+    std::vector<void *> allocs;
+    float **conv_tab = nullptr, **ssm_tab = nullptr;   // device [NLAYER][n_seq]
+    int *seq_dev = nullptr;                      // device [t_step] sequence of each row
+    qma::StepParams *sp_dev = nullptr;           // device [n_seq]: sequence i's kernels read entry i
+    qma::StepParams *sp_host = nullptr;          // pinned [n_seq]
+    int *h_tok = nullptr, *h_seq = nullptr;      // pinned [t_step]
+    float *logits = nullptr;                     // device [t_step][n_vocab]
+    int *greedy_dev = nullptr;                   // device [t_step]
+    float *h_row = nullptr;                      // pinned [n_vocab], a prefilled sequence's logits
+    qma_cuda_ep *ep = nullptr;                   // expert-parallel MoE blocks, when set
+    std::vector<qma_cuda_moe_weights> ep_w;      // this rank's shard views, per layer
+};
+
+namespace qma {
+
+// Greedy id of each logits row: one CTA per row, ties to the lowest id.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float *__restrict__ logits, int n, int *out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *x = logits + size_t(row) * n;
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = tid; i < n; i += blockDim.x) {
+        const float xv = x[i];
+        if (xv > v) { v = xv; idx = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) { bv[warp] = v; bi[warp] = idx; }
+    __syncthreads();
+    if (warp) return;
+    v = lane < int(blockDim.x >> 5) ? bv[lane] : -INFINITY;
+    idx = lane < int(blockDim.x >> 5) ? bi[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) out[row] = idx;
+}
+
+static int batch_free(qma_cuda_batch *b) {
+    if (!b) return QMA_CUDA_OK;
+    cudaSetDevice(b->m->device);
+    if (b->st) cudaStreamSynchronize(b->st);
+    for (qma_cuda_state *c : b->seqs) qma_cuda_state_free(c);
+    if (b->work) qma_cuda_state_free(b->work);
+    for (void *p : b->allocs) cudaFree(p);
+    for (void *p : {static_cast<void *>(b->sp_host), static_cast<void *>(b->h_tok), static_cast<void *>(b->h_seq),
+                    static_cast<void *>(b->h_row)})
+        if (p) cudaFreeHost(p);
+    if (b->st) cudaStreamDestroy(b->st);
+    delete b;
+    return QMA_CUDA_OK;
+}
+
+static int batch_create(qma_cuda_model *m, int n_seq, int n_ctx, qma_cuda_batch **out) {
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    qma_cuda_batch *b = new qma_cuda_batch();
+    b->m = m;
+    b->n_seq = n_seq;
+    b->n_ctx = n_ctx;
+    b->t_step = n_seq < MAX_CHUNK ? n_seq : MAX_CHUNK;
+    int rc = QMA_CUDA_OK;
+    auto dalloc = [&](void **p, size_t bytes) -> int {
+        QMA_CHECK_CUDA(cudaMalloc(p, bytes));
+        b->allocs.push_back(*p);
+        QMA_CHECK_CUDA(cudaMemset(*p, 0, bytes));
+        return QMA_CUDA_OK;
+    };
+    auto fail = [&](int e) {
+        batch_free(b);
+        return e;
+    };
+    if (cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess) {
+        set_error("batch: stream creation failed");
+        return fail(QMA_CUDA_ERR_CUDA);
+    }
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->sp_dev), sizeof(StepParams) * n_seq))) return fail(rc);
+    for (int i = 0; i < n_seq; i++) {
+        qma_cuda_state *c = nullptr;
+        if ((rc = create_state(m, n_ctx, &c, b->st))) return fail(rc);
+        b->seqs.push_back(c);
+        c->sp_dev = b->sp_dev + i;       // its own kernels read its entry of the batch's array
+    }
+    if ((rc = create_state(m, HCM_SINK + 2, &b->work, b->st))) return fail(rc);
+    std::vector<float *> tab(size_t(NLAYER) * n_seq, nullptr);
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->conv_tab), sizeof(float *) * tab.size()))) return fail(rc);
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->ssm_tab), sizeof(float *) * tab.size()))) return fail(rc);
+    for (int il = 0; il < NLAYER; il++)
+        for (int i = 0; i < n_seq; i++) tab[size_t(il) * n_seq + i] = b->seqs[i]->conv[il];
+    if (cudaMemcpy(b->conv_tab, tab.data(), sizeof(float *) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(QMA_CUDA_ERR_CUDA);
+    for (int il = 0; il < NLAYER; il++)
+        for (int i = 0; i < n_seq; i++) tab[size_t(il) * n_seq + i] = b->seqs[i]->ssm[il];
+    if (cudaMemcpy(b->ssm_tab, tab.data(), sizeof(float *) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(QMA_CUDA_ERR_CUDA);
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->seq_dev), sizeof(int) * b->t_step))) return fail(rc);
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->greedy_dev), sizeof(int) * b->t_step))) return fail(rc);
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->logits), sizeof(float) * size_t(b->t_step) * m->n_vocab)))
+        return fail(rc);
+    if (cudaMallocHost(&b->sp_host, sizeof(StepParams) * n_seq) != cudaSuccess ||
+        cudaMallocHost(&b->h_tok, sizeof(int) * b->t_step) != cudaSuccess ||
+        cudaMallocHost(&b->h_seq, sizeof(int) * b->t_step) != cudaSuccess ||
+        cudaMallocHost(&b->h_row, sizeof(float) * m->n_vocab) != cudaSuccess) {
+        set_error("batch: pinned host allocation failed");
+        return fail(QMA_CUDA_ERR_NOMEM);
+    }
+    memset(b->sp_host, 0, sizeof(StepParams) * n_seq);
+    if (cudaStreamSynchronize(b->st) != cudaSuccess) return fail(QMA_CUDA_ERR_CUDA);
+    *out = b;
+    return QMA_CUDA_OK;
+}
+
+// One token from each of T distinct sequences (rows t of the step; row t
+// is row rows[t] of the caller's logits / greedy / hidden).  n_layers <
+// NLAYER stops after that many layers and returns the residual stream in
+// hidden (host [n][2048]), the layer-level parity point.
+static int batch_step(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int T, float *logits_host,
+                      int64_t logits_ld, const int *rows, int *greedy, int n_layers, float *hidden) {
+    qma_cuda_model *m = b->m;
+    qma_cuda_state *w = b->work;
+    cudaStream_t st = b->st;
+    int rc;
+#define TRY(x) do { if ((rc = (x))) return rc; } while (0)
+    std::vector<int> nk(T);
+    for (int t = 0; t < T; t++) {
+        qma_cuda_state *c = b->seqs[seq_ids[t]];
+        const int pos = c->n_pos;
+        if (pos + 1 > c->n_ctx - HCM_SINK) {
+            set_error("batch: sequence %d is full (%d positions of a ring of %d)", seq_ids[t], pos, c->n_ctx);
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
+        TRY(maybe_rebuild(c, pos));
+        c->tier[hcm_slot(pos, c->n_ctx)] = 2;      // kv_append
+        nk[t] = nk_upper(c, pos, 1, false);
+        TRY(ensure_attn_scratch(c, 1, nk[t], attn_span(1, nk[t])));
+    }
+    // the previous step ended with a synchronize: the pinned buffers are free
+    for (int t = 0; t < T; t++) {
+        qma_cuda_state *c = b->seqs[seq_ids[t]];
+        fill_params(c, b->sp_host[seq_ids[t]], c->n_pos, 1, tokens[t]);
+        b->h_tok[t] = tokens[t];
+        b->h_seq[t] = seq_ids[t];
+    }
+    QMA_CHECK_CUDA(cudaMemcpyAsync(w->tokens_dev, b->h_tok, sizeof(int) * T, cudaMemcpyHostToDevice, st));
+    QMA_CHECK_CUDA(cudaMemcpyAsync(b->seq_dev, b->h_seq, sizeof(int) * T, cudaMemcpyHostToDevice, st));
+    QMA_CHECK_CUDA(cudaMemcpyAsync(b->sp_dev, b->sp_host, sizeof(StepParams) * b->n_seq, cudaMemcpyHostToDevice, st));
+    TRY(launch_embed(m->embd, m->embd_type, m->n_vocab, w->tokens_dev, b->sp_dev, T, w->x, st));
+    for (int il = 0; il < n_layers; il++) {
+        const LayerW &L = m->L[il];
+        const int ld = L.in_rows;
+        TRY(launch_rmsnorm_quant(w->x, L.attn_norm, T, EMBD, w->xq, w->xd, w->xs, st, layer_plan(m, il)));
+        TRY(matvec(L.in_type, L.in_proj, EMBD, ld, T, w->xq, w->xd, w->xs, w->proj, st));
+        if (is_attn(il)) {
+            const int lay = il / 4;
+            for (int t = 0; t < T; t++) {
+                qma_cuda_state *c = b->seqs[seq_ids[t]];
+                TRY(launch_qk_prep_append(w->proj + size_t(t) * ld, ld, L.q_norm, L.k_norm, c->rope, c->sp_dev, 1,
+                                          c->qr, c->z, c->kv[lay], c->qf, c->sal, st));
+                AttnArgs a;
+                a.qr = c->qr; a.kv = c->kv[lay]; a.arena = c->arena[lay]; a.live = c->live_dev;
+                a.sp = c->sp_dev; a.T = 1; a.nk_max = nk[t]; a.pv_chunk = attn_span(1, nk[t]);
+                a.scores = c->scores; a.cmax = c->cmax; a.opart = c->opart; a.lpart = c->lpart;
+                a.ml = c->ml; a.z = c->z;
+                a.xq = w->xq + size_t(t) * WO_DIM;
+                a.xd = w->xd + size_t(t) * (WO_DIM / 256);
+                a.xs = w->xs + size_t(t) * (WO_DIM / 16);
+                a.sal = c->sal + size_t(lay) * c->n_ctx;
+                a.pin_sal = c->pin_sal + size_t(lay) * HCM_H_PIN;
+                TRY(launch_attention(a, st));
+                TRY(launch_salience(a, st));
+            }
+            TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, w->xq, w->xd, w->xs, w->x2, st, w->x));
+        } else {
+            const SeqTable conv{b->conv_tab + size_t(il) * b->n_seq, b->seq_dev};
+            const SeqTable ssm{b->ssm_tab + size_t(il) * b->n_seq, b->seq_dev};
+            TRY(launch_conv1d_seqs(w->proj, ld, L.conv1d, conv, T, w->conv_out, st));
+            TRY(launch_gdn_seqs(w->conv_out, w->proj, ld, CONV_DIM + VAL_DIM, CONV_DIM + VAL_DIM + VHEADS, L.dt, L.a,
+                                ssm, T, w->gdo, st));
+            TRY(launch_gated_norm_quant(w->gdo, w->proj + CONV_DIM, ld, L.ssm_norm, T, w->xq, w->xd, w->xs, st));
+            TRY(matvec(L.out_type, L.out_proj, VAL_DIM, EMBD, T, w->xq, w->xd, w->xs, w->x2, st, w->x));
+        }
+        // x = x2 + moe(rms_norm(x2) * post_norm)
+        if (b->ep)
+            TRY(qma_cuda_ep_moe_layer(b->ep, &b->ep_w[il], w->x2, T, w->x, nullptr, nullptr, st));
+        else
+            TRY(moe_layer(L.moe, w->x2, T, w->x, nullptr, nullptr, w->moe_scratch, st, false, nullptr));
+    }
+    if (hidden)
+        for (int t = 0; t < T; t++)
+            QMA_CHECK_CUDA(cudaMemcpyAsync(hidden + size_t(rows[t]) * EMBD, w->x + size_t(t) * EMBD,
+                                           sizeof(float) * EMBD, cudaMemcpyDeviceToHost, st));
+    if (n_layers == NLAYER && (logits_host || greedy)) {
+        TRY(launch_rmsnorm_quant(w->x, m->out_norm, T, EMBD, w->xq, w->xd, w->xs, st));
+        TRY(matvec(m->out_type, m->out, EMBD, m->n_vocab, T, w->xq, w->xd, w->xs, b->logits, st));
+        if (greedy) {
+            argmax_rows_kernel<<<T, 1024, 0, st>>>(b->logits, m->n_vocab, b->greedy_dev);
+            QMA_CHECK_LAUNCH();
+            QMA_CHECK_CUDA(cudaMemcpyAsync(b->h_tok, b->greedy_dev, sizeof(int) * T, cudaMemcpyDeviceToHost, st));
+        }
+        if (logits_host)
+            for (int t = 0; t < T; t++)
+                QMA_CHECK_CUDA(cudaMemcpyAsync(logits_host + rows[t] * logits_ld, b->logits + size_t(t) * m->n_vocab,
+                                               sizeof(float) * m->n_vocab, cudaMemcpyDeviceToHost, st));
+    }
+    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if (greedy)
+        for (int t = 0; t < T; t++) greedy[rows[t]] = b->h_tok[t];
+    for (int t = 0; t < T; t++) b->seqs[seq_ids[t]]->n_pos += 1;
+#undef TRY
+    return check_wait_timeouts();
+}
+
+// tokens[i] extends sequence seq_ids[i]; see qma_cuda_batch_eval.
+static int batch_eval(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n, float *logits, int *greedy,
+                      int n_layers, float *hidden) {
+    qma_cuda_model *m = b->m;
+    QMA_CHECK_CUDA(cudaSetDevice(m->device));
+    std::vector<std::vector<int>> rows_of(b->n_seq);
+    for (int i = 0; i < n; i++) rows_of[seq_ids[i]].push_back(i);
+    std::vector<int> one_seq, one_tok, one_row;
+    int rc;
+    for (int q = 0; q < b->n_seq; q++) {
+        const std::vector<int> &r = rows_of[q];
+        if (r.empty()) continue;
+        if (r.size() == 1) {
+            one_seq.push_back(q);
+            one_tok.push_back(tokens[r[0]]);
+            one_row.push_back(r[0]);
+            continue;
+        }
+        if (hidden || b->ep) {
+            set_error("batch: %s takes one token per sequence (sequence %d has %d)",
+                      hidden ? "the hidden-state entry point" : "an expert-parallel batch", q, int(r.size()));
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
+        // a prompt: the sequence's own chunked prefill, logits of its last token
+        std::vector<int> toks(r.size());
+        for (size_t k = 0; k < r.size(); k++) toks[k] = tokens[r[k]];
+        const bool want = logits || greedy;
+        if ((rc = eval(b->seqs[q], toks.data(), int(toks.size()), want ? b->h_row : nullptr, 0))) return rc;
+        if (logits) memcpy(logits + int64_t(r.back()) * m->n_vocab, b->h_row, sizeof(float) * m->n_vocab);
+        if (greedy) {
+            int best = 0;
+            for (int v = 1; v < m->n_vocab; v++)
+                if (b->h_row[v] > b->h_row[best]) best = v;
+            greedy[r.back()] = best;
+        }
+    }
+    for (size_t i0 = 0; i0 < one_seq.size(); i0 += b->t_step) {
+        const int T = int(std::min(one_seq.size() - i0, size_t(b->t_step)));
+        if (b->ep && i0 > 0) {
+            set_error("batch: an expert-parallel step takes at most %d sequences", b->t_step);
+            return QMA_CUDA_ERR_UNSUPPORTED;
+        }
+        if ((rc = batch_step(b, one_seq.data() + i0, one_tok.data() + i0, T, logits, m->n_vocab, one_row.data() + i0,
+                             greedy, n_layers, hidden)))
+            return rc;
+    }
+    return QMA_CUDA_OK;
+}
+
+}  // namespace qma
+
+extern "C" {
+
+int qma_cuda_batch_create(qma_cuda_model *m, int n_seq, int n_ctx, qma_cuda_batch **out) {
+    qma::clear_error();
+    QMA_REQUIRE(m && out && n_seq >= 1 && n_seq <= 4096 && n_ctx > qma::HCM_SINK + 1,
+                "qma_cuda_batch_create: bad arguments (n_seq %d, n_ctx %d)", n_seq, n_ctx);
+    *out = nullptr;
+    return qma::batch_create(m, n_seq, n_ctx, out);
+}
+
+int qma_cuda_batch_free(qma_cuda_batch *b) {
+    qma::clear_error();
+    return qma::batch_free(b);
+}
+
+qma_cuda_state *qma_cuda_batch_seq(qma_cuda_batch *b, int seq) {
+    return b && seq >= 0 && seq < b->n_seq ? b->seqs[seq] : nullptr;
+}
+
+int qma_cuda_batch_n_seq(const qma_cuda_batch *b) { return b ? b->n_seq : 0; }
+
+int qma_cuda_batch_set_ep(qma_cuda_batch *b, qma_cuda_ep *ep, const qma_cuda_moe_weights *shard) {
+    qma::clear_error();
+    QMA_REQUIRE(b && (!ep || shard), "qma_cuda_batch_set_ep: bad arguments");
+    b->ep = ep;
+    b->ep_w.clear();
+    if (ep) b->ep_w.assign(shard, shard + qma::NLAYER);
+    return QMA_CUDA_OK;
+}
+
+static int batch_args(const qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n, const char *fn) {
+    QMA_REQUIRE(b && seq_ids && tokens && n > 0, "%s: bad arguments", fn);
+    for (int i = 0; i < n; i++) {
+        QMA_REQUIRE(seq_ids[i] >= 0 && seq_ids[i] < b->n_seq, "%s: sequence id %d out of range (0..%d)", fn,
+                    seq_ids[i], b->n_seq - 1);
+        QMA_REQUIRE(tokens[i] >= 0 && tokens[i] < b->m->n_vocab, "%s: token %d out of range", fn, tokens[i]);
+    }
+    return QMA_CUDA_OK;
+}
+
+int qma_cuda_batch_eval(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n_tokens, float *logits,
+                        int *greedy) {
+    qma::clear_error();
+    int rc;
+    if ((rc = batch_args(b, seq_ids, tokens, n_tokens, "qma_cuda_batch_eval"))) return rc;
+    return qma::batch_eval(b, seq_ids, tokens, n_tokens, logits, greedy, qma::NLAYER, nullptr);
+}
+
+int qma_cuda_batch_eval_hidden(qma_cuda_batch *b, const int *seq_ids, const int *tokens, int n_tokens, int n_layers,
+                               float *hidden) {
+    qma::clear_error();
+    int rc;
+    if ((rc = batch_args(b, seq_ids, tokens, n_tokens, "qma_cuda_batch_eval_hidden"))) return rc;
+    QMA_REQUIRE(hidden && n_layers >= 0 && n_layers <= qma::NLAYER, "qma_cuda_batch_eval_hidden: bad arguments");
+    return qma::batch_eval(b, seq_ids, tokens, n_tokens, nullptr, nullptr, n_layers, hidden);
+}
+
+const float *qma_cuda_batch_logits(const qma_cuda_batch *b) { return b ? b->logits : nullptr; }
 
 }  // extern "C"

@@ -180,6 +180,33 @@ __global__ void __launch_bounds__(256) conv1d_kernel(const float *__restrict__ q
     out[size_t(t) * CONV_DIM + ch] = sum / (1.0f + expf(-sum));
 }
 
+// One token of each of n sequences (grid (CONV_DIM / 256, n)): token t
+// convolves its own sequence's three saved samples (sequence seq[t]) and
+// moves that state on by one sample, the arithmetic of conv1d_kernel with
+// T = 1.  Every sequence appears at most once, so no two threads share a
+// state row.
+__global__ void __launch_bounds__(256) conv1d_seqs_kernel(const float *__restrict__ qkv, int ld,
+                                                          const float *__restrict__ w, SeqTable sq,
+                                                          float *out) {
+    QMA_TRACE_SCOPE(TK_CONV);
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    float *state = sq.state[sq.seq[t]];
+    pdl_trigger();
+    pdl_wait();
+    if (ch >= CONV_DIM) return;
+    const float4 wc = *reinterpret_cast<const float4 *>(w + size_t(ch) * 4);
+    const float s0 = state[ch * 3], s1 = state[ch * 3 + 1], s2 = state[ch * 3 + 2];
+    const float xin = qkv[size_t(t) * ld + ch];
+    float sum = __fmul_rn(s0, wc.x);
+    sum = __fadd_rn(sum, __fmul_rn(s1, wc.y));
+    sum = __fadd_rn(sum, __fmul_rn(s2, wc.z));
+    sum = __fadd_rn(sum, __fmul_rn(xin, wc.w));
+    out[size_t(t) * CONV_DIM + ch] = sum / (1.0f + expf(-sum));
+    state[ch * 3] = s1;
+    state[ch * 3 + 1] = s2;
+    state[ch * 3 + 2] = xin;
+}
+
 // The channel state after the chunk: the last three inputs (launched after
 // conv1d_kernel, which still reads the old state).
 __global__ void __launch_bounds__(256) conv1d_state_kernel(const float *__restrict__ qkv, int ld, float *state,
@@ -196,6 +223,14 @@ __global__ void __launch_bounds__(256) conv1d_state_kernel(const float *__restri
     }
 #pragma unroll
     for (int k = 0; k < 3; k++) state[ch * 3 + k] = v[k];
+}
+
+int launch_conv1d_seqs(const float *qkv, int ld, const float *w, const SeqTable &sq, int n, float *out,
+                       cudaStream_t st) {
+    QMA_CHECK_CUDA(launch_ex(conv1d_seqs_kernel, dim3(CONV_DIM / 256, n), dim3(256), 0, st, 1, pdl_enabled(), qkv,
+                             ld, w, sq, out));
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
 }
 
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
@@ -235,9 +270,17 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
                                                   int beta_off, int alpha_off,
                                                   const float *__restrict__ dt,
                                                   const float *__restrict__ av, float *ssm, int T,
-                                                  float *o, GdnNorm gn) {
+                                                  float *o, GdnNorm gn, SeqTable seqs) {
     QMA_TRACE_SCOPE(TK_GDN);
     const int rb = blockIdx.x, h = blockIdx.y;
+    if (seqs.state) {
+        // one token of each of gridDim.z sequences: token z, sequence seq[z]
+        const int z = blockIdx.z;
+        ssm = seqs.state[seqs.seq[z]];
+        conv_out += size_t(z) * CONV_DIM;
+        proj += size_t(z) * proj_ld;
+        o += size_t(z) * VAL_DIM;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qh = h % KHEADS;
     const int j = rb * 32 + (tid >> 3);          // state row
@@ -797,7 +840,16 @@ int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_o
         return QMA_CUDA_OK;
     }
     QMA_CHECK_CUDA(launch_ex(gdn_kernel, dim3(4, VHEADS), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj, proj_ld,
-                             beta_off, alpha_off, dt, a, ssm, T, o, gn));
+                             beta_off, alpha_off, dt, a, ssm, T, o, gn, SeqTable()));
+    QMA_CHECK_LAUNCH();
+    return QMA_CUDA_OK;
+}
+
+int launch_gdn_seqs(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
+                    const float *dt, const float *a, const SeqTable &sq, int n, float *o, cudaStream_t st) {
+    QMA_CHECK_CUDA(launch_ex(gdn_kernel, dim3(4, VHEADS, n), dim3(256), 0, st, 1, pdl_enabled(), conv_out, proj,
+                             proj_ld, beta_off, alpha_off, dt, a, static_cast<float *>(nullptr), 1, o, GdnNorm(),
+                             sq));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }

@@ -56,6 +56,16 @@ int launch_rmsnorm_quant(const float *x, const float *w, int T, int n, int8_t *x
                          int16_t *xs, cudaStream_t st, const Prefetch &pf = Prefetch());
 int launch_conv1d(const float *qkv, int ld, const float *w, float *state, int T, float *out,
                   cudaStream_t st);
+// Per-token recurrent state of a batch of sequences: token t of a step
+// belongs to sequence seq[t] (device [n], distinct), whose state for the
+// layer is state[seq[t]] (device table of pointers).
+struct SeqTable {
+    float *const *state = nullptr;
+    const int *seq = nullptr;
+};
+// conv1d + SiLU of one token per sequence (row t of qkv, its own state)
+int launch_conv1d_seqs(const float *qkv, int ld, const float *w, const SeqTable &sq, int n, float *out,
+                       cudaStream_t st);
 // Optional tail of a single-token gated delta net: the gated RMSNorm and the
 // Q8_K for ssm_out written to xq / xd / xs (cnt: 16 zeroed tickets).
 struct GdnNormArgs {
@@ -73,6 +83,10 @@ int launch_gdn(const float *conv_out, const float *proj, int proj_ld, int beta_o
 // first; then, with chunk_scratch (gdn_chunk_scratch_bytes(), T <= 512), the
 // chunked gated-delta form, else the token-sequential recurrence.)
 size_t gdn_chunk_scratch_bytes();
+// The single-token recurrence for one token of each of n sequences (row t
+// of conv_out / proj / o, state sq.state[sq.seq[t]]), without the norm tail.
+int launch_gdn_seqs(const float *conv_out, const float *proj, int proj_ld, int beta_off, int alpha_off,
+                    const float *dt, const float *a, const SeqTable &sq, int n, float *o, cudaStream_t st);
 int launch_gated_norm_quant(const float *o, const float *z, int z_ld, const float *w, int T,
                             int8_t *xq, float *xd, int16_t *xs, cudaStream_t st);
 

@@ -251,6 +251,7 @@ class MoeWeights(C.Structure):
 
 
 _SIGS["qma_cuda_model_moe_weights"] = (_i32, [_vp, _i32, C.POINTER(MoeWeights)])
+_SIGS["qma_cuda_model_set_router_bias"] = (_i32, [_vp, _i32, _vp])
 _SIGS.update({
     "qma_cuda_ep_unique_id": (_i32, [_vp]),
     "qma_cuda_ep_init": (_i32, [_i32, _vp, _i32, _i32, _i32, C.POINTER(_vp)]),
@@ -258,6 +259,14 @@ _SIGS.update({
     "qma_cuda_ep_free": (_i32, [_vp]),
     "qma_cuda_ep_moe_layer": (_i32, [_vp, C.POINTER(MoeWeights), _vp, _i32, _vp, _vp, _vp, _vp]),
     "qma_cuda_ep_stats": (_i32, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_i32)]),
+    "qma_cuda_batch_create": (_i32, [_vp, _i32, _i32, C.POINTER(_vp)]),
+    "qma_cuda_batch_free": (_i32, [_vp]),
+    "qma_cuda_batch_n_seq": (_i32, [_vp]),
+    "qma_cuda_batch_seq": (_vp, [_vp, _i32]),
+    "qma_cuda_batch_eval": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "qma_cuda_batch_eval_hidden": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "qma_cuda_batch_logits": (_vp, [_vp]),
+    "qma_cuda_batch_set_ep": (_i32, [_vp, _vp, C.POINTER(MoeWeights)]),
 })
 
 EP_UID_BYTES = 128
@@ -307,6 +316,56 @@ class ExpertParallel:
     def close(self) -> None:
         if self.h:
             call("qma_cuda_ep_free", self.h)
+            self.h = None
+
+
+class Batch:
+    """n_seq sequences decoded together (qma_cuda_batch)."""
+
+    def __init__(self, model: Model, n_seq: int, n_ctx: int):
+        h = _vp()
+        call("qma_cuda_batch_create", model.h, n_seq, n_ctx, C.byref(h))
+        self.h, self.model, self.n_seq = h, model, n_seq
+        self._ep_w = None
+
+    def n_pos(self, seq: int) -> int:
+        return lib().qma_cuda_state_n_pos(lib().qma_cuda_batch_seq(self.h, seq))
+
+    def eval(self, seq_ids, tokens, logits=True, greedy=True):
+        """(logits [n][n_vocab] or None, greedy [n] or None); rows of each
+        sequence's last token in the call are filled (-1 / 0 elsewhere)."""
+        import numpy as np
+        sids = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        if len(sids) != len(toks):
+            raise ValueError("seq_ids and tokens differ in length")
+        lo = np.zeros((len(toks), self.model.n_vocab), np.float32) if logits else None
+        g = np.full(len(toks), -1, np.int32) if greedy else None
+        call("qma_cuda_batch_eval", self.h, ptr(sids), ptr(toks), len(toks), ptr(lo), ptr(g))
+        return lo, g
+
+    def eval_hidden(self, seq_ids, tokens, n_layers: int):
+        import numpy as np
+        sids = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros((len(toks), 2048), np.float32)
+        call("qma_cuda_batch_eval_hidden", self.h, ptr(sids), ptr(toks), len(toks), n_layers, ptr(out))
+        return out
+
+    def set_ep(self, ep, shard_weights) -> None:
+        """Route the MoE blocks through ep (an ExpertParallel) with this
+        rank's 40 shard views; ep None restores the local block."""
+        if ep is None:
+            call("qma_cuda_batch_set_ep", self.h, None, None)
+            self._ep_w = None
+            return
+        arr = (MoeWeights * len(shard_weights))(*shard_weights)
+        call("qma_cuda_batch_set_ep", self.h, ep.h, arr)
+        self._ep_w = arr
+
+    def close(self):
+        if self.h:
+            call("qma_cuda_batch_free", self.h)
             self.h = None
 
 

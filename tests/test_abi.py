@@ -122,3 +122,20 @@ def test_layer_entry_points_and_ecache_reject_bad_arguments():
     assert lib.qma_cuda_ecache_hold(None, 0, 0, None, None, None) == Q.ERR_INVALID
     assert lib.qma_cuda_ecache_release(None) == Q.ERR_INVALID
     assert lib.qma_cuda_ecache_held(None) == -1
+
+
+def test_batch_entry_points_reject_bad_arguments():
+    lib = Q.lib()
+    h = C.c_void_p()
+    assert lib.qma_cuda_batch_create(None, 4, 4096, C.byref(h)) == Q.ERR_INVALID
+    assert lib.qma_cuda_batch_create(1, 0, 4096, C.byref(h)) == Q.ERR_INVALID
+    assert lib.qma_cuda_batch_create(1, 4, 4, C.byref(h)) == Q.ERR_INVALID      # n_ctx below the sink
+    ids = (C.c_int * 1)(0)
+    assert lib.qma_cuda_batch_eval(None, ids, ids, 1, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_batch_eval_hidden(None, ids, ids, 1, 40, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_batch_set_ep(None, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_batch_seq(None, 0) is None
+    assert lib.qma_cuda_batch_n_seq(None) == 0
+    assert lib.qma_cuda_batch_logits(None) is None
+    assert lib.qma_cuda_batch_free(None) == Q.OK
+    assert lib.qma_cuda_model_set_router_bias(None, 0, None) == Q.ERR_INVALID

@@ -751,3 +751,101 @@ def test_gdn_step_ragged_chunks_match_sequential(full):
     # two fp32 orders of one recurrence; a rare Q8_K int8 flip of the
     # ssm_out input moves single tokens by ~1e-3
     assert e <= 5e-4
+
+
+# ------------------------------------------------------ multi-sequence batch --
+def _batch_prefill(batch, prompts, **kw):
+    sids = np.concatenate([np.full(len(p), i, np.int32) for i, p in enumerate(prompts)])
+    return batch.eval(sids, np.concatenate(prompts), **kw)
+
+
+def test_batch_decode_layers_teacher_forced(full):
+    """Three sequences with prompts of different lengths decode one token
+    each in one batched step (per-row conv / gated-delta state through the
+    sequence table, attention per sequence, shared projections and MoE);
+    every layer of every row, fed to the oracle's layer with that sequence's
+    own prefix, agrees within the single-token tolerance."""
+    L = O.lib()
+    rng = np.random.default_rng(SEED + 1)
+    prompts = [rng.integers(0, O.N_VOCAB, n).astype(np.int32) for n in (24, 17, 30)]
+    toks = np.array([62913, 5, 151935], np.int32)
+    sids = np.arange(len(prompts), dtype=np.int32)
+
+    def batch_hidden(nl):
+        b = Q.Batch(full["model"], len(prompts), N_CTX)
+        try:
+            _batch_prefill(b, prompts, logits=False, greedy=False)
+            h = b.eval_hidden(sids, toks, nl)
+            assert [b.n_pos(i) for i in range(len(prompts))] == [len(p) + 1 for p in prompts]
+            return h
+        finally:
+            b.close()
+
+    xd = [batch_hidden(nl) for nl in range(41)]
+    report = []
+    for i, p in enumerate(prompts):
+        xs = [gpu_hidden(full["model"], p, nl) for nl in range(41)]
+        os_ = L.qo_state_new(N_CTX)
+        try:
+            for il in range(40):
+                out = np.zeros_like(xs[il])
+                L.qo_layer_forward(full["om"], os_, il, O._ptr(np.ascontiguousarray(xs[il])), len(p), 0,
+                                   O._ptr(out))
+            for il in range(40):
+                x = np.ascontiguousarray(xd[il][i:i + 1])
+                out = np.zeros_like(x)
+                L.qo_layer_forward(full["om"], os_, il, O._ptr(x), 1, len(p), O._ptr(out))
+                report.append((i, il, norm_rel(xd[il + 1][i:i + 1], out)))
+        finally:
+            L.qo_state_free(os_)
+    worst = max(report, key=lambda r: r[2])
+    print("batched decode, worst layer (seq, layer, norm-rel): %r" % (worst,))
+    bad = [r for r in report if r[2] > RTOL_TOKEN]
+    assert not bad, "rows over tolerance (seq, layer, norm-rel): %r" % bad
+
+
+def test_batch_steps_independent_of_the_other_sequences(full):
+    """32 sequences: their prompts prefilled in one call (each through its
+    own state: the logits equal a lone state's bit for bit), then three
+    decode steps taken once as one 32-row step and once as two 16-row steps
+    (the second half first, in reverse order).  Every sequence's logits and
+    greedy token agree bit for bit: a row's results do not depend on the
+    other rows of its step (same path: the GEMM projections, the grouped
+    experts)."""
+    B, P = 32, 8
+    rng = np.random.default_rng(SEED + 2)
+    prompts = rng.integers(0, O.N_VOCAB, (B, P)).astype(np.int32)
+    a = Q.Batch(full["model"], B, N_CTX)
+    b = Q.Batch(full["model"], B, N_CTX)
+    try:
+        la, ga = _batch_prefill(a, list(prompts))
+        lb, gb = _batch_prefill(b, list(prompts))
+        last = np.arange(B) * P + P - 1
+        assert np.array_equal(la[last].view(np.uint32), lb[last].view(np.uint32))
+        assert np.array_equal(ga[last], np.argmax(la[last], axis=1))
+        assert (np.delete(ga, last) == -1).all()
+        st = Q.State(full["model"], N_CTX)
+        try:
+            lone = st.eval(prompts[5])
+        finally:
+            st.close()
+        assert np.array_equal(lone.view(np.uint32), la[last[5]].view(np.uint32))
+        tok = ga[last].astype(np.int32)
+        sids = np.arange(B, dtype=np.int32)
+        for step in range(3):
+            la, ga = a.eval(sids, tok)
+            h2, h1 = sids[16:][::-1].copy(), sids[:16].copy()
+            l2, g2 = b.eval(h2, tok[h2])
+            l1, g1 = b.eval(h1, tok[h1])
+            lb = np.empty_like(la)
+            gb = np.empty_like(ga)
+            lb[h2], gb[h2] = l2, g2
+            lb[h1], gb[h1] = l1, g1
+            diff = np.nonzero((la.view(np.uint32) != lb.view(np.uint32)).any(axis=1))[0]
+            assert diff.size == 0, "step %d: rows differ for sequences %r" % (step, diff.tolist())
+            assert np.array_equal(ga, gb) and np.array_equal(ga, np.argmax(la, axis=1))
+            tok = ga.astype(np.int32)
+        assert [a.n_pos(i) for i in range(B)] == [P + 3] * B
+    finally:
+        a.close()
+        b.close()
