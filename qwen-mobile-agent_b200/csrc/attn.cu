@@ -96,9 +96,13 @@ __device__ __forceinline__ void st8(float *p, const float (&x)[8]) {
 __global__ void __launch_bounds__(128) qk_prep_append_kernel(
     const float *__restrict__ proj, int proj_ld, const float *__restrict__ qn,
     const float *__restrict__ kn, const float *__restrict__ rope, const StepParams *spp,
-    float *qr, float *z, uint8_t *kv, float *qf, float *sal) {
+    float *qr, float *z, uint8_t *kv, float *qf, float *sal, const AttnRow *rows) {
     QMA_TRACE_SCOPE(TK_QK_PREP);
     const int t = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (rows) {                 // one token of sequence row blockIdx.z
+        const AttnRow &r = rows[blockIdx.z];
+        proj = r.proj; rope = r.rope; spp = r.sp; qr = r.qr; z = r.z; kv = r.kv; qf = r.qf; sal = r.sal_all;
+    }
     __shared__ float qfv[4];
     // Everything but the projection row was written before this step began
     // (step parameters, rope table, norm weights, the slot's old record):
@@ -515,11 +519,17 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float *__restric
                                                           const int *__restrict__ live,
                                                           const StepParams *spp, int nk_max,
                                                           int span, int nchunk, float *scores,
-                                                          float *mpart, float *lpart, float *opart) {
+                                                          float *mpart, float *lpart, float *opart,
+                                                          const AttnRow *rows) {
     QMA_TRACE_SCOPE(TK_ATTN_CHUNK);
     extern __shared__ __align__(16) uint8_t dec_raw[];
     DecSmem &S = *reinterpret_cast<DecSmem *>(dec_raw);
     const int chunk = blockIdx.x, kh = blockIdx.y;
+    if (rows) {                 // sequence row blockIdx.z
+        const AttnRow &r = rows[blockIdx.z];
+        qr = r.qr; kv = r.kv; arena = r.arena; live = r.live; spp = r.sp; nk_max = r.nk_max; span = r.span;
+        nchunk = r.nchunk; scores = r.scores; mpart = r.cmax; lpart = r.lpart; opart = r.opart;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const StepParams sp = *spp;                  // written before this step began
     const int nk = nk_of(sp, 0);
@@ -739,10 +749,15 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float *__restri
                                                            const StepParams *spp, int span,
                                                            int nchunk, const float *__restrict__ z,
                                                            float *ml, int8_t *xq, float *xd,
-                                                           int16_t *xs) {
+                                                           int16_t *xs, const AttnRow *rows) {
     QMA_TRACE_SCOPE(TK_ATTN_COMBINE);
     extern __shared__ float fsh[];              // [nchunk] chunk factors of this head
     const int h = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (rows) {                 // sequence row blockIdx.z
+        const AttnRow &r = rows[blockIdx.z];
+        opart = r.opart; mpart = r.cmax; lpart = r.lpart; spp = r.sp; span = r.span; nchunk = r.nchunk; z = r.z;
+        ml = r.ml; xq = r.xq; xd = r.xd; xs = r.xs;
+    }
     __shared__ float wred[8], wsum[8];
     __shared__ __align__(16) float y[HEAD_DIM];
     pdl_trigger();
@@ -798,9 +813,14 @@ __global__ void __launch_bounds__(256) attn_salience_kernel(const float *__restr
                                                             int nk_max, const float *__restrict__ ml,
                                                             const int *__restrict__ live,
                                                             const StepParams *spp, float *sal,
-                                                            float *pin_sal) {
+                                                            float *pin_sal, const AttnRow *rows) {
     QMA_TRACE_SCOPE(TK_SALIENCE);
     const int jj = blockIdx.x * blockDim.x + threadIdx.x;
+    if (rows) {                 // sequence row blockIdx.z
+        const AttnRow &r = rows[blockIdx.z];
+        scores = r.scores; nk_max = r.nk_max; ml = r.ml; live = r.live; spp = r.sp; sal = r.sal;
+        pin_sal = r.pin_sal;
+    }
     pdl_trigger();
     pdl_wait();
     const StepParams sp = *spp;
@@ -924,7 +944,7 @@ int launch_qk_prep_append(const float *proj, int proj_ld, const float *qn, const
                           const float *rope, const StepParams *sp, int T, float *qr, float *z,
                           uint8_t *kv, float *qf, float *sal, cudaStream_t st) {
     QMA_CHECK_CUDA(launch_ex(qk_prep_append_kernel, dim3(T, 5), dim3(128), 0, st, 1, pdl_enabled(), proj, proj_ld, qn, kn,
-                             rope, sp, qr, z, kv, qf, sal));
+                             rope, sp, qr, z, kv, qf, sal, static_cast<const AttnRow *>(nullptr)));
     QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
@@ -946,7 +966,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     if (a.T == 1 && a.pv_chunk <= DSPAN && !(gen && atoi(gen) != 0))
         QMA_CHECK_CUDA(launch_ex(attn_decode_kernel, dim3(nchunk, NHEAD_KV), dim3(256), sizeof(DecSmem), st, 1,
                                  pdl_enabled(), a.qr, a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk,
-                                 a.scores, a.cmax, a.lpart, a.opart));
+                                 a.scores, a.cmax, a.lpart, a.opart, static_cast<const AttnRow *>(nullptr)));
     else
         QMA_CHECK_CUDA(launch_ex(attn_chunk_kernel, dim3(nchunk, NHEAD_KV, a.T), dim3(256), sizeof(ChunkSmem), st, 1,
                                  pdl_enabled(), a.qr, a.kv, a.arena, a.live, a.sp, a.nk_max, a.pv_chunk, nchunk,
@@ -958,7 +978,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
     QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(NHEAD, a.T), dim3(256), fsh, st, 1, pdl_enabled(), a.opart,
-                             a.cmax, a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs));
+                             a.cmax, a.lpart, a.sp, a.pv_chunk, nchunk, a.z, a.ml, a.xq, a.xd, a.xs,
+                             static_cast<const AttnRow *>(nullptr)));
     return QMA_CUDA_OK;
 }
 
@@ -968,7 +989,39 @@ int launch_salience(const AttnArgs &a, cudaStream_t st) {
                                  st, 1, false, a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
     else
         QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((a.nk_max + 255) / 256), dim3(256), 0, st, 1, false,
-                                 a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal));
+                                 a.scores, a.nk_max, a.ml, a.live, a.sp, a.sal, a.pin_sal,
+                                 static_cast<const AttnRow *>(nullptr)));
+    return QMA_CUDA_OK;
+}
+
+int launch_attention_rows(const AttnRow *rows, int n, int proj_ld, const float *qn, const float *kn, int max_nchunk,
+                          int max_nk, cudaStream_t st) {
+    static PerDevice attr;
+    if (!attr.done()) {
+        QMA_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(sizeof(DecSmem))));
+        attr.mark();
+    }
+    const size_t fsh = sizeof(float) * size_t(max_nchunk);
+    if (fsh > 48 * 1024) {
+        set_error("attention: %d position chunks exceed the combine kernel's shared memory", max_nchunk);
+        return QMA_CUDA_ERR_UNSUPPORTED;
+    }
+    const StepParams *nsp = nullptr;
+    const float *nf = nullptr;
+    float *nw = nullptr;
+    QMA_CHECK_CUDA(launch_ex(qk_prep_append_kernel, dim3(1, 5, n), dim3(128), 0, st, 1, pdl_enabled(), nf, proj_ld,
+                             qn, kn, nf, nsp, nw, nw, static_cast<uint8_t *>(nullptr), nw, nw, rows));
+    QMA_CHECK_CUDA(launch_ex(attn_decode_kernel, dim3(max_nchunk, NHEAD_KV, n), dim3(256), sizeof(DecSmem), st, 1,
+                             pdl_enabled(), nf, static_cast<const uint8_t *>(nullptr),
+                             static_cast<const uint8_t *>(nullptr), static_cast<const int *>(nullptr), nsp, 0, 1, 1,
+                             nw, nw, nw, nw, rows));
+    QMA_CHECK_CUDA(launch_ex(attn_combine_kernel, dim3(NHEAD, 1, n), dim3(256), fsh, st, 1, pdl_enabled(), nf, nf, nf,
+                             nsp, 1, 1, nf, nw, static_cast<int8_t *>(nullptr), nw, static_cast<int16_t *>(nullptr),
+                             rows));
+    QMA_CHECK_CUDA(launch_ex(attn_salience_kernel, dim3((max_nk + 255) / 256, 1, n), dim3(256), 0, st, 1, false, nf,
+                             0, nf, static_cast<const int *>(nullptr), nsp, nw, nw, rows));
+    QMA_CHECK_LAUNCH();
     return QMA_CUDA_OK;
 }
 

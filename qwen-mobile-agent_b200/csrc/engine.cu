@@ -1712,6 +1712,7 @@ struct qma_cuda_batch {
     float *logits = nullptr;                     // device [t_step][n_vocab]
     int *greedy_dev = nullptr;                   // device [t_step]
     float *h_row = nullptr;                      // pinned [n_vocab], a prefilled sequence's logits
+    qma::AttnRow *rows_dev = nullptr, *rows_host = nullptr;   // [NATTN][t_step] attention arguments of a step
     qma_cuda_ep *ep = nullptr;                   // expert-parallel MoE blocks, when set
     std::vector<qma_cuda_moe_weights> ep_w;      // this rank's shard views, per layer
 };
@@ -1750,7 +1751,7 @@ static int batch_free(qma_cuda_batch *b) {
     if (b->work) qma_cuda_state_free(b->work);
     for (void *p : b->allocs) cudaFree(p);
     for (void *p : {static_cast<void *>(b->sp_host), static_cast<void *>(b->h_tok), static_cast<void *>(b->h_seq),
-                    static_cast<void *>(b->h_row)})
+                    static_cast<void *>(b->h_row), static_cast<void *>(b->rows_host)})
         if (p) cudaFreeHost(p);
     if (b->st) cudaStreamDestroy(b->st);
     delete b;
@@ -1802,7 +1803,9 @@ static int batch_create(qma_cuda_model *m, int n_seq, int n_ctx, qma_cuda_batch 
     if ((rc = dalloc(reinterpret_cast<void **>(&b->greedy_dev), sizeof(int) * b->t_step))) return fail(rc);
     if ((rc = dalloc(reinterpret_cast<void **>(&b->logits), sizeof(float) * size_t(b->t_step) * m->n_vocab)))
         return fail(rc);
-    if (cudaMallocHost(&b->sp_host, sizeof(StepParams) * n_seq) != cudaSuccess ||
+    if ((rc = dalloc(reinterpret_cast<void **>(&b->rows_dev), sizeof(AttnRow) * NATTN * b->t_step))) return fail(rc);
+    if (cudaMallocHost(&b->rows_host, sizeof(AttnRow) * NATTN * b->t_step) != cudaSuccess ||
+        cudaMallocHost(&b->sp_host, sizeof(StepParams) * n_seq) != cudaSuccess ||
         cudaMallocHost(&b->h_tok, sizeof(int) * b->t_step) != cudaSuccess ||
         cudaMallocHost(&b->h_seq, sizeof(int) * b->t_step) != cudaSuccess ||
         cudaMallocHost(&b->h_row, sizeof(float) * m->n_vocab) != cudaSuccess) {
@@ -1846,6 +1849,45 @@ static int batch_step(qma_cuda_batch *b, const int *seq_ids, const int *tokens, 
         b->h_tok[t] = tokens[t];
         b->h_seq[t] = seq_ids[t];
     }
+    // the attention arguments of every (attention layer, row): one launch per
+    // kernel serves all rows while every span fits the decode kernel
+    // (QMA_CUDA_ATTN_PER_SEQ=1 in the environment: one sequence at a time,
+    // the same kernels and results, as a cross-check)
+    const char *per_seq = getenv("QMA_CUDA_ATTN_PER_SEQ");
+    bool rows_ok = !(per_seq && atoi(per_seq) != 0);
+    int max_nchunk = 1, max_nk = 1;
+    for (int t = 0; t < T; t++) {
+        const int span = attn_span(1, nk[t]);
+        rows_ok = rows_ok && span <= ATTN_ROWS_MAX_SPAN;
+        max_nchunk = std::max(max_nchunk, (nk[t] + span - 1) / span);
+        max_nk = std::max(max_nk, nk[t]);
+    }
+    if (rows_ok) {
+        for (int lay = 0; lay < NATTN; lay++)
+            for (int t = 0; t < T; t++) {
+                qma_cuda_state *c = b->seqs[seq_ids[t]];
+                AttnRow &r = b->rows_host[size_t(lay) * b->t_step + t];
+                r.sp = c->sp_dev;
+                r.proj = w->proj + size_t(t) * m->L[4 * lay + 3].in_rows;
+                r.rope = c->rope;
+                r.qr = c->qr; r.z = c->z;
+                r.kv = c->kv[lay]; r.arena = c->arena[lay]; r.live = c->live_dev;
+                r.qf = c->qf; r.sal_all = c->sal;
+                r.scores = c->scores; r.cmax = c->cmax; r.lpart = c->lpart; r.opart = c->opart; r.ml = c->ml;
+                r.xq = w->xq + size_t(t) * WO_DIM;
+                r.xd = w->xd + size_t(t) * (WO_DIM / 256);
+                r.xs = w->xs + size_t(t) * (WO_DIM / 16);
+                r.sal = c->sal + size_t(lay) * c->n_ctx;
+                r.pin_sal = c->pin_sal + size_t(lay) * HCM_H_PIN;
+                r.nk_max = nk[t];
+                r.span = attn_span(1, nk[t]);
+                r.nchunk = (nk[t] + r.span - 1) / r.span;
+            }
+        for (int lay = 0; lay < NATTN; lay++)
+            QMA_CHECK_CUDA(cudaMemcpyAsync(b->rows_dev + size_t(lay) * b->t_step,
+                                           b->rows_host + size_t(lay) * b->t_step, sizeof(AttnRow) * T,
+                                           cudaMemcpyHostToDevice, st));
+    }
     QMA_CHECK_CUDA(cudaMemcpyAsync(w->tokens_dev, b->h_tok, sizeof(int) * T, cudaMemcpyHostToDevice, st));
     QMA_CHECK_CUDA(cudaMemcpyAsync(b->seq_dev, b->h_seq, sizeof(int) * T, cudaMemcpyHostToDevice, st));
     QMA_CHECK_CUDA(cudaMemcpyAsync(b->sp_dev, b->sp_host, sizeof(StepParams) * b->n_seq, cudaMemcpyHostToDevice, st));
@@ -1855,7 +1897,12 @@ static int batch_step(qma_cuda_batch *b, const int *seq_ids, const int *tokens, 
         const int ld = L.in_rows;
         TRY(launch_rmsnorm_quant(w->x, L.attn_norm, T, EMBD, w->xq, w->xd, w->xs, st, layer_plan(m, il)));
         TRY(matvec(L.in_type, L.in_proj, EMBD, ld, T, w->xq, w->xd, w->xs, w->proj, st));
-        if (is_attn(il)) {
+        if (is_attn(il) && rows_ok) {
+            TRY(launch_attention_rows(b->rows_dev + size_t(il / 4) * b->t_step, T, ld, L.q_norm, L.k_norm, max_nchunk,
+                                      max_nk, st));
+            TRY(matvec(L.out_type, L.out_proj, WO_DIM, EMBD, T, w->xq, w->xd, w->xs, w->x2, st, w->x));
+        } else if (is_attn(il)) {
+            // a sequence past 16384 attended positions: the general kernels, one sequence at a time
             const int lay = il / 4;
             for (int t = 0; t < T; t++) {
                 qma_cuda_state *c = b->seqs[seq_ids[t]];

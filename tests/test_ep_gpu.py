@@ -169,3 +169,106 @@ def test_expert_parallel_init_times_out_when_a_rank_never_joins():
     assert rc == Q.ERR_TIMEOUT, (rc, msg)
     assert "2000 ms" in msg and h is None, msg
     assert 1.5 < took < 90, took
+
+
+# ------------------------------------------ full-model batch, expert-parallel --
+B_PER_RANK, B_PROMPT, B_STEPS = 16, 8, 2
+
+
+def _row_digests(lo):
+    import hashlib
+    return [hashlib.blake2b(r.tobytes(), digest_size=8).hexdigest() for r in lo]
+
+
+def _batch_worker(rank, uid_path, results):
+    """Rank r decodes sequences r*16 .. r*16+15 of the full synthetic model
+    with its MoE blocks expert-parallel over both GPUs; rank 0 then decodes
+    all 32 sequences alone with local MoE blocks (the one-GPU engine)."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    try:
+        torch.cuda.set_device(rank)
+        Q.init(rank)
+        arr, n, _ = Q.synth_layout()
+        model = Q.Model(C.cast(arr, C.POINTER(Q.Tensor)), n, seed=3, device=rank)
+        e0, _ = Q.ep_shard(rank, N_RANKS)
+        gb = 512 * (2048 // 256) * 144
+        db = Q.packed_bytes(14, 2048, 512)
+        shard = []
+        for il in range(40):
+            w = Q.MoeWeights()
+            Q.call("qma_cuda_model_moe_weights", model.h, il, C.byref(w))
+            w.gate_exps += e0 * gb
+            w.up_exps += e0 * gb
+            w.down_exps += e0 * db
+            shard.append(w)
+        ep = Q.ExpertParallel(rank, rank, N_RANKS, B_PER_RANK, _share_file(uid_path, rank))
+        prompts = [np.random.default_rng([5, g]).integers(0, 151936, B_PROMPT).astype(np.int32)
+                   for g in range(N_RANKS * B_PER_RANK)]
+
+        def run(batch, ids, use_ep):
+            sids = np.repeat(np.arange(len(ids), dtype=np.int32), B_PROMPT)
+            _, g = batch.eval(sids, np.concatenate([prompts[q] for q in ids]), logits=False)
+            tok = g[B_PROMPT - 1::B_PROMPT].astype(np.int32)
+            if use_ep:
+                batch.set_ep(ep, shard)
+            digests, toks = [], []
+            for _ in range(B_STEPS):
+                lo, g = batch.eval(np.arange(len(ids), dtype=np.int32), tok)
+                digests.append(_row_digests(lo))
+                toks.append(g.tolist())
+                tok = g.astype(np.int32)
+            return digests, toks
+
+        b = Q.Batch(model, B_PER_RANK, 256)
+        mine = run(b, list(range(rank * B_PER_RANK, (rank + 1) * B_PER_RANK)), True)
+        b.close()
+        ep.close()
+        ref = None
+        if rank == 0:
+            r = Q.Batch(model, N_RANKS * B_PER_RANK, 256)
+            ref = run(r, list(range(N_RANKS * B_PER_RANK)), False)
+            r.close()
+        model.close()
+        results.put((rank, (mine, ref), None))
+    except Exception:                   # reported by the parent
+        import traceback
+        results.put((rank, None, traceback.format_exc()))
+
+
+def test_expert_parallel_full_model_batch_matches_one_gpu():
+    """configs[4]'s serving shape on two GPUs: 32 sequences, 16 per GPU, the
+    attention and gated-delta state of each sequence on its own GPU and the
+    MoE blocks of every batched step expert-parallel (128 experts per GPU).
+    Every sequence's logits after each of two decode steps equal, bit for
+    bit, those of the same sequences decoded on one GPU with local MoE
+    blocks, and so do the greedy tokens."""
+    import torch
+    if not torch.cuda.is_available() or torch.cuda.device_count() < N_RANKS:
+        pytest.skip(f"needs {N_RANKS} GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    with tempfile.TemporaryDirectory() as tmp:
+        uid_path = os.path.join(tmp, "uid")
+        procs = [ctx.Process(target=_batch_worker, args=(r, uid_path, results)) for r in range(N_RANKS)]
+        for p in procs:
+            p.start()
+        got = {}
+        try:
+            for _ in range(N_RANKS):
+                rank, out, err = results.get(timeout=900)
+                assert err is None, f"rank {rank}:\n{err}"
+                got[rank] = out
+        finally:
+            for p in procs:
+                p.join(timeout=60)
+                if p.is_alive():
+                    p.kill()
+    ref_digests, ref_toks = got[0][1]
+    for step in range(B_STEPS):
+        ep_digests = sum((got[r][0][0][step] for r in range(N_RANKS)), [])
+        ep_toks = sum((got[r][0][1][step] for r in range(N_RANKS)), [])
+        bad = [q for q in range(len(ep_digests)) if ep_digests[q] != ref_digests[step][q]]
+        assert not bad, "step %d: sequences %r differ from the one-GPU engine" % (step, bad)
+        assert ep_toks == ref_toks[step]

@@ -846,6 +846,15 @@ def test_batch_steps_independent_of_the_other_sequences(full):
             assert np.array_equal(ga, gb) and np.array_equal(ga, np.argmax(la, axis=1))
             tok = ga.astype(np.int32)
         assert [a.n_pos(i) for i in range(B)] == [P + 3] * B
+        # the attention of all rows in one launch per kernel (row tables)
+        # equals one sequence at a time, bit for bit
+        os.environ["QMA_CUDA_ATTN_PER_SEQ"] = "1"
+        try:
+            lb, gb = b.eval(sids, tok)
+        finally:
+            os.environ.pop("QMA_CUDA_ATTN_PER_SEQ", None)
+        la, ga = a.eval(sids, tok)
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32)) and np.array_equal(ga, gb)
     finally:
         a.close()
         b.close()
