@@ -13,7 +13,18 @@ with CUDA events on the engine's stream.  A step streams ~2 GB of weights
 (> L2), so no L2 flush is needed.  `e2e` times the same steps through
 qma_cuda_eval with the token from and the logits to host memory.
 
+The default line also carries the configs[1] GEMV (`gemv`), the configs[4]
+expert-parallel MoE blocks (`ep`) and the configs[4] batched decode of 64
+sequences (`batch`, expert-parallel over the N GPUs at N > 1).
+
 gemv: Q4_K 151936x2048 GEMV at batch 1 (quantize + GEMV).
+
+batch: the `batch` leg alone (--prompt, --no-parity).
+
+prefill: 512-token chunks of the full model after a 1024-token prompt.
+
+gdn: one gated-delta-net layer, 1024 decode steps and a
+4096-token chunked prefill.
 
 moe: one MoE FFN layer (router, top-8 + shared expert, SwiGLU,
 combine, residual) for one decode token through qma_cuda_moe_layer.
@@ -190,7 +201,7 @@ MOE_TENSORS = ("post_attention_norm.weight", "ffn_gate_inp.weight", "ffn_gate_ex
                "ffn_gate_shexp.weight", "ffn_up_shexp.weight", "ffn_down_shexp.weight")
 # DRAM bytes (read + write) one MoE block call moves, from the ncu capture of
 # the moe workload summarised in profiles/moe_block_configs0.txt
-MOE_TRAFFIC_PER_BLOCK = 20591360
+MOE_TRAFFIC_PER_BLOCK = 20624128
 
 
 def moe_block_bytes(arr, n, il=0):
@@ -604,7 +615,7 @@ def logits_digest(rows):
                                     "little", signed=True) for r in rows], np.int64)
 
 
-def run_batch_on_model(model, full_w, args, world, rank, local):
+def run_batch_on_model(model, full_w, args, world, rank, local, prompt_len=None, check=True, max_steps=None):
     """configs[4] end to end: 64 concurrent sequences of the full model,
     each prefilled with its own 2048-token prompt (seeded ids, untimed), then
     decoded greedily in batched steps of one token per sequence
@@ -649,50 +660,53 @@ def run_batch_on_model(model, full_w, args, world, rank, local):
         ends = np.cumsum([len(pr[g]) for g in ids]) - 1
         return g[ends].astype(np.int32)
 
-    # ---- parity ----------------------------------------------------------------
-    P_TOK, P_STEPS = 32, 3
-    pr = prompts(P_TOK, SEED + 11)
+    prompt_len = prompt_len or BATCH_PROMPT
     mine = list(range(first, first + n_here))
-    b = Q.Batch(model, n_here, 4096)
-    tok = prefill(b, pr, mine)
-    if ep is not None:
-        b.set_ep(ep, shard)
     sids = np.arange(n_here, dtype=np.int32)
-    digests = []
-    for _ in range(P_STEPS):
-        lo, g = b.eval(sids, tok)
-        digests.append(logits_digest(lo))
-        tok = g.astype(np.int32)
-    b.close()
-    got = np.concatenate([np.concatenate(dist_gather_i64(d, world)) for d in digests])
-    ok, detail = True, {}
-    if rank == 0:
-        ref = Q.Batch(model, BATCH_SEQS, 4096)
-        tok = prefill(ref, pr, list(range(BATCH_SEQS)))
-        allids = np.arange(BATCH_SEQS, dtype=np.int32)
-        want = []
+    ok, detail = True, {"skipped": True}
+    if check:
+        # ---- parity ----------------------------------------------------------------
+        P_TOK, P_STEPS = 32, 3
+        pr = prompts(P_TOK, SEED + 11)
+        b = Q.Batch(model, n_here, 4096)
+        tok = prefill(b, pr, mine)
+        if ep is not None:
+            b.set_ep(ep, shard)
+        digests = []
         for _ in range(P_STEPS):
-            if world > 1:
-                lo, g = ref.eval(allids, tok)
-            else:
-                lo = np.empty((BATCH_SEQS, N_VOCAB), np.float32)
-                g = np.empty(BATCH_SEQS, np.int32)
-                for q in range(0, BATCH_SEQS, 16):
-                    l_, g_ = ref.eval(allids[q:q + 16], tok[q:q + 16])
-                    lo[q:q + 16], g[q:q + 16] = l_, g_
-            want.append(logits_digest(lo))
+            lo, g = b.eval(sids, tok)
+            digests.append(logits_digest(lo))
             tok = g.astype(np.int32)
-        ref.close()
-        want = np.concatenate(want)
-        ok = bool(np.array_equal(got, want))
-        detail = {"rows_compared": int(want.size), "rows_equal": int((got == want).sum()),
-                  "reference": "rank 0 alone, all 64 sequences, local MoE blocks" if world > 1
-                  else "the same sequences stepped 16 rows at a time"}
+        b.close()
+        got = np.concatenate([np.concatenate(dist_gather_i64(d, world)) for d in digests])
+        detail = {}
+        if rank == 0:
+            ref = Q.Batch(model, BATCH_SEQS, 4096)
+            tok = prefill(ref, pr, list(range(BATCH_SEQS)))
+            allids = np.arange(BATCH_SEQS, dtype=np.int32)
+            want = []
+            for _ in range(P_STEPS):
+                if world > 1:
+                    lo, g = ref.eval(allids, tok)
+                else:
+                    lo = np.empty((BATCH_SEQS, N_VOCAB), np.float32)
+                    g = np.empty(BATCH_SEQS, np.int32)
+                    for q in range(0, BATCH_SEQS, 16):
+                        l_, g_ = ref.eval(allids[q:q + 16], tok[q:q + 16])
+                        lo[q:q + 16], g[q:q + 16] = l_, g_
+                want.append(logits_digest(lo))
+                tok = g.astype(np.int32)
+            ref.close()
+            want = np.concatenate(want)
+            ok = bool(np.array_equal(got, want))
+            detail = {"rows_compared": int(want.size), "rows_equal": int((got == want).sum()),
+                      "reference": "rank 0 alone, all 64 sequences, local MoE blocks" if world > 1
+                      else "the same sequences stepped 16 rows at a time"}
     ok = dist_min(float(ok), world) > 0.5
 
-    # ---- timed: 2048-token prompts, 128 decode tokens per sequence ----------------
-    pr = prompts(BATCH_PROMPT, SEED + 12)
-    b = Q.Batch(model, n_here, BATCH_PROMPT + 256)
+    # ---- timed: prompt_len-token prompts (2048), 128 decode tokens per sequence ----
+    pr = prompts(prompt_len, SEED + 12)
+    b = Q.Batch(model, n_here, prompt_len + 256)
     t0 = time.time()
     tok = prefill(b, pr, mine)
     t_prefill = dist_max(time.time() - t0, world)
@@ -702,18 +716,22 @@ def run_batch_on_model(model, full_w, args, world, rank, local):
                                        device=local)
     warm = max(args.warmup, 3)
     steps = max(1, BATCH_DECODE - warm)
+    if max_steps:
+        steps = max(1, min(steps, max_steps))
     for _ in range(warm):
         _, g = b.eval(sids, tok, logits=False)
         tok = g.astype(np.int32)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist_barrier(world)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("capture")
     ev0.record(stream)
     for _ in range(steps):
         _, g = b.eval(sids, tok, logits=False)
         tok = g.astype(np.int32)
     ev1.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     t_ms = dist_max(ev0.elapsed_time(ev1), world)
     n_pos = b.n_pos(0)
     b.close()
@@ -727,7 +745,7 @@ def run_batch_on_model(model, full_w, args, world, rank, local):
     return {
         "metric": "batched decode tok/s @N (configs[4]: 64 sequences, full model, EP over N GPUs)",
         "tok_per_s": round(value, 1), "ms_per_step": round(t_ms / steps, 3), "n_ranks": world,
-        "sequences": BATCH_SEQS, "sequences_per_gpu": n_here, "prompt_tokens": BATCH_PROMPT,
+        "sequences": BATCH_SEQS, "sequences_per_gpu": n_here, "prompt_tokens": prompt_len,
         "decode_tokens_per_sequence": warm + steps, "timed_steps": steps, "positions_at_end": n_pos,
         "prefill_s": round(t_prefill, 2),
         "moe": "expert-parallel, 256/N experts per GPU, NCCL exchange per layer" if world > 1
@@ -1238,6 +1256,88 @@ def run_gdn_ours(args, world, rank, local):
     }), flush=True)
 
 
+def run_batch_ours(args, world, rank, local):
+    """configs[4] alone: the batched-decode leg of the default line on its
+    own model (--prompt sets the prompt length; --steps caps the timed
+    steps), printed as its own line."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    Q.init(local)
+    arr, n, size = model_layout(Q8_0)
+    model = Q.Model(C.cast(arr, C.POINTER(Q.Tensor)), n, seed=SEED, device=local)
+    wts = []
+    for il in range(40):
+        w = Q.MoeWeights()
+        Q.call("qma_cuda_model_moe_weights", model.h, il, C.byref(w))
+        wts.append(w)
+    prompt = args.prompt if args.prompt != PROMPT else BATCH_PROMPT
+    with ClockSampler(local) as clk:
+        r = run_batch_on_model(model, wts, args, world, rank, local, prompt_len=prompt, check=not args.no_parity,
+                               max_steps=args.steps)
+    model.close()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": r["metric"], "value": r["tok_per_s"], "unit": "tok/s", "n_gpus": world, "steps": r["timed_steps"],
+        "warmup": r["decode_tokens_per_sequence"] - r["timed_steps"], "ms_per_step": r["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xq4",
+        "data": "synthetic", "config": {"workload": "configs[4] batched decode", **{k: v for k, v in r.items()
+                                                                                   if k not in ("metric",)}},
+        "clocks": clk.summary(), "e2e": {"value": r["tok_per_s"], "unit": "tok/s",
+                                         "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                                         "d2h_bytes_per_step": r["d2h_bytes_per_step"]},
+    }), flush=True)
+    if not r["parity"]:
+        sys.exit("batched decode parity check failed")
+
+
+def run_prefill_ours(args, world, rank, local):
+    """Prefill throughput of the full model: a 1024-token prompt (untimed),
+    W warm-up chunks, then K chunks of 512 tokens through qma_cuda_eval
+    (last-token logits), timed with CUDA events on the state's stream inside
+    an NVTX range "capture"."""
+    import ctypes as C
+    import torch
+    import qma_cuda as Q
+    Q.init(local)
+    arr, n, size = model_layout(Q8_0)
+    model = Q.Model(C.cast(arr, C.POINTER(Q.Tensor)), n, seed=SEED, device=local)
+    K, W = max(1, args.steps), args.warmup
+    st = Q.State(model, 1024 + 512 * (K + W) + 64)
+    stream = torch.cuda.ExternalStream(Q.lib().qma_cuda_state_stream(st.h), device=local)
+    rng = np.random.default_rng(SEED + rank)
+    st.eval(rng.integers(0, N_VOCAB, 1024).astype(np.int32))
+    for _ in range(W):
+        st.eval(rng.integers(0, N_VOCAB, 512).astype(np.int32))
+    chunks = [rng.integers(0, N_VOCAB, 512).astype(np.int32) for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("capture")
+        e0.record(stream)
+        for c in chunks:
+            st.eval(c)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        dist_barrier(world)
+    ms = dist_max(e0.elapsed_time(e1), world)
+    st.close()
+    model.close()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "qwen35moe prefill tok/s (512-token chunks)", "value": round(world * 512 * K / (ms / 1e3), 1),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4", "data": "synthetic",
+        "config": {"workload": "full model prefill: 512-token chunks after a 1024-token prompt, one state",
+                   "replicas": world},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 # ------------------------------------------------------------------ main ---
 def main():
     ap = argparse.ArgumentParser()
@@ -1245,7 +1345,9 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep", "gdn"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep", "gdn", "batch",
+                                                             "prefill"])
+    ap.add_argument("--no-parity", action="store_true", help="batch: skip the in-run parity check")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ep", action="store_true", help="decode: skip the expert-parallel leg")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the configs[1] GEMV leg")
@@ -1270,6 +1372,10 @@ def main():
             run_ep_ours(args, world, rank, local)
         elif args.workload == "gdn":
             run_gdn_ours(args, world, rank, local)
+        elif args.workload == "batch":
+            run_batch_ours(args, world, rank, local)
+        elif args.workload == "prefill":
+            run_prefill_ours(args, world, rank, local)
         else:
             run_gemv_ours(args, world, rank, local)
     finally:
