@@ -602,7 +602,9 @@ def dist_gather_i64(vals, world):
         return [vals]
     import torch
     import torch.distributed as dist
-    t = torch.from_numpy(vals).cuda()
+    t = torch.from_numpy(vals)
+    if dist.get_backend() == "nccl":
+        t = t.cuda()
     out = [torch.empty_like(t) for _ in range(world)]
     dist.all_gather(out, t)
     return [o.cpu().numpy() for o in out]

@@ -454,8 +454,15 @@ int qma_cuda_sample_candidates(const float *logits, int n_vocab, const int32_t *
  * row (2336 bytes) per (token, owning rank) and one fp32 [2048] down
  * projection per (token, expert) pair; the result is bit-identical to
  * qma_cuda_moe_layer on the same tokens (16 or more per call, its grouped
- * path).  Each call blocks the host once, until the counts of the exchange
- * are known. */
+ * path).  The exchange has a fixed capacity: every rank sends every rank a
+ * block of t_max rows (padding rows carry no expert) and gets each block's
+ * slot partials back whole, so no count has to reach the host and a call
+ * only queues work on the stream (a step of layers runs back to back and
+ * can be captured in a CUDA graph); qma_cuda_ep_sync waits for it with the
+ * handle's wall-clock limit.  QMA_CUDA_EP_COUNTED=1 in the environment
+ * switches to exact-size transfers (the [N][2] counts all-gathered and read
+ * on the host: one host synchronisation per call, fewer bytes on NVLink,
+ * the same results). */
 #define QMA_CUDA_EP_UID_BYTES 128
 typedef struct qma_cuda_ep qma_cuda_ep;
 
@@ -496,8 +503,17 @@ int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const 
  * ep NULL goes back to the local MoE block. */
 int qma_cuda_batch_set_ep(qma_cuda_batch *b, qma_cuda_ep *ep, const qma_cuda_moe_weights *shard);
 
+/* The stream's work done, exchanges with the other ranks included, waiting
+ * at most the handle's wall-clock limit: past it, or on a communicator
+ * error, the communicator is aborted (the peers' pending transfers fail)
+ * and the call returns QMA_CUDA_ERR_TIMEOUT / QMA_CUDA_ERR_CUDA.  Use it
+ * instead of a plain stream synchronisation after expert-parallel calls, so
+ * that a rank that died does not hang the others. */
+int qma_cuda_ep_sync(qma_cuda_ep *ep, void *stream);
+
 /* Bytes this rank sent and received in its last qma_cuda_ep_moe_layer call
- * (itself included) and the rows its experts served. */
+ * (itself included) and the rows its experts served (-1 with the
+ * fixed-capacity exchange, whose count stays on the device). */
 int qma_cuda_ep_stats(const qma_cuda_ep *ep, uint64_t *sent_bytes, uint64_t *recv_bytes,
                       int *rows_in);
 

@@ -1954,7 +1954,10 @@ static int batch_step(qma_cuda_batch *b, const int *seq_ids, const int *tokens, 
                 QMA_CHECK_CUDA(cudaMemcpyAsync(logits_host + rows[t] * logits_ld, b->logits + size_t(t) * m->n_vocab,
                                                sizeof(float) * m->n_vocab, cudaMemcpyDeviceToHost, st));
     }
-    QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if (b->ep)
+        TRY(qma_cuda_ep_sync(b->ep, st));      // bounded: a dead peer fails the step instead of hanging it
+    else
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
     if (greedy)
         for (int t = 0; t < T; t++) greedy[rows[t]] = b->h_tok[t];
     for (int t = 0; t < T; t++) b->seqs[seq_ids[t]]->n_pos += 1;

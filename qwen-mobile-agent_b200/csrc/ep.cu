@@ -13,15 +13,18 @@
 //                           (token, destination), deduplicated over the k,
 //                           with the token's 8 shard-local expert ids
 //                           (-1 where another rank owns the expert);
-//   4. all-gather of the [N][2] counts, then the dispatch: grouped
-//      ncclSend / ncclRecv, rows landing in the receiver's scratch in source
-//      rank order;
+//   4. the dispatch: grouped ncclSend / ncclRecv of fixed blocks of t_max
+//      rows per destination (padding rows carry no expert), rows landing in
+//      the receiver's scratch in source rank order (or, with the counted
+//      exchange, an all-gather of the [N][2] counts read on the host and
+//      exact-size transfers);
 //   5. the grouped expert pipeline (moe_grouped.cu) on the received rows,
-//      groups = the shard's experts; ep_recv_plan_kernel / ep_gather_kernel
-//      pack each owned pair's down projection (fp32 [2048]) in (row, k)
-//      order, which is the source's pair order;
-//   6. the return transfer, ep_unpack_kernel into the source's slot
-//      partials, the shared expert on the source's own tokens, and the
+//      groups = the shard's experts (counted exchange: ep_recv_plan_kernel /
+//      ep_gather_kernel pack each owned pair's down projection in (row, k)
+//      order, the source's pair order);
+//   6. the return transfer (the blocks' slot partials whole, or the packed
+//      pairs), ep_unpack_fixed_kernel / ep_unpack_kernel into the source's
+//      slot partials, the shared expert on the source's own tokens, and the
 //      combine in the reference's order (moe_xpar_worker + combine,
 //      nn.c:604-629, 652-707; residual nn.c:2246-2252).
 //
@@ -185,6 +188,24 @@ __global__ void __launch_bounds__(256) ep_unpack_kernel(const float *__restrict_
     dst[threadIdx.x + 256] = src[threadIdx.x + 256];
 }
 
+// 6'. ----------------------------------------------- unpack, fixed blocks --
+// The fixed-capacity exchange returns, from each rank d, the slot partials
+// of the whole block of rows this rank sent it: row j of block d holds
+// token t's pairs at its slots k (those whose expert d owns).  Grid (T * 8),
+// 256 threads: slot k of token t from its owner's block.
+__global__ void __launch_bounds__(256) ep_unpack_fixed_kernel(const float *__restrict__ ret,
+                                                              const int *__restrict__ sel,
+                                                              const int *__restrict__ tokidx, int n_local, int t_max,
+                                                              float *part) {
+    const int q = blockIdx.x, t = q / MOE_TOPK, k = q % MOE_TOPK;
+    const int d = sel[q] / n_local, j = tokidx[t * EP_MAX_RANKS + d];
+    const float4 *src =
+        reinterpret_cast<const float4 *>(ret + ((size_t(d) * t_max + j) * MOE_NSLOT + k) * MOE_EMBD);
+    float4 *dst = reinterpret_cast<float4 *>(part + (size_t(t) * MOE_NSLOT + k) * MOE_EMBD);
+    dst[threadIdx.x] = src[threadIdx.x];
+    dst[threadIdx.x + 256] = src[threadIdx.x + 256];
+}
+
 }  // namespace qma
 
 struct qma_cuda_ep {
@@ -194,6 +215,7 @@ struct qma_cuda_ep {
     qma::MoeScratch sl{}, sr{};       // own tokens; received rows
     qma::EpSend snd{};
     float *ret_send = nullptr, *ret_recv = nullptr;
+    float *ret_fixed = nullptr;       // [N][t_max][9][2048]: the blocks' slot partials, returned
     int *tokidx = nullptr, *srcrow = nullptr, *cnt = nullptr, *allcnt = nullptr, *prow = nullptr;
     int *h_allcnt = nullptr;          // pinned [N][N][2]
     uint64_t sent = 0, recvd = 0;     // bytes of the last call
@@ -309,7 +331,80 @@ void ep_release(qma_cuda_ep *ep) {
 
 }  // namespace
 
+// QMA_CUDA_EP_COUNTED=1 in the environment: the counted exchange (the
+// [N][2] counts all-gathered and read on the host, exact-size transfers,
+// one host synchronisation per layer) instead of the fixed-capacity one;
+// the same results, fewer bytes on NVLink.
+static bool ep_counted() {
+    const char *v = getenv("QMA_CUDA_EP_COUNTED");
+    return v && atoi(v) != 0;
+}
+
+// The fixed-capacity exchange: every rank sends every rank (itself
+// included) its whole block of t_max rows, padding rows carrying no
+// shard-local expert (ids -1), so no count has to reach the host; the
+// receiver runs the grouped experts over all N * t_max rows (the expert
+// lists skip the padding) and returns each block's slot partials whole.
+// Nothing in a call waits on the host: a step of layers is queued back to
+// back (and can be captured in a CUDA graph); qma_cuda_ep_sync is the
+// bounded wait for its end.
+static int ep_moe_fixed(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const float *x2, int T, float *x_out, int32_t *sel,
+                 float *wts, cudaStream_t st) {
+    using namespace qma;
+    const int n = ep->n, tm = ep->t_max, R = n * tm;
+    int rc;
+    QMA_CHECK_CUDA(cudaMemsetAsync(ep->snd.meta, 0xff, sizeof(int) * size_t(R) * EP_ROW_META, st));
+    if (T > 0) {
+        if ((rc = moe_route(*w, x2, T, ep->sl, sel, wts, st))) return rc;
+        ep_plan_kernel<<<1, EP_MAX_T, 0, st>>>(ep->sl.sel, T, n, ep->n_local, ep->tokidx, ep->srcrow, ep->cnt);
+        QMA_CHECK_LAUNCH();
+        ep_pack_kernel<<<dim3(T, n), 128, 0, st>>>(ep->sl, ep->tokidx, tm, ep->n_local, ep->snd);
+        QMA_CHECK_LAUNCH();
+    }
+    const size_t row_bytes = MOE_EMBD + 4 * (MOE_EMBD / 256) + 2 * (MOE_EMBD / 16) + 4 * EP_ROW_META;
+    EP_NCCL(ncclGroupStart());
+    for (int d = 0; d < n; d++) {
+        const size_t row = size_t(d) * tm, c = size_t(tm);
+        EP_NCCL(ncclSend(ep->snd.xq + row * MOE_EMBD, c * MOE_EMBD, ncclInt8, d, ep->comm, st));
+        EP_NCCL(ncclSend(ep->snd.xd + row * (MOE_EMBD / 256), c * (MOE_EMBD / 256), ncclFloat32, d, ep->comm, st));
+        EP_NCCL(ncclSend(ep->snd.xs + row * (MOE_EMBD / 16), c * (MOE_EMBD / 16) * 2, ncclInt8, d, ep->comm, st));
+        EP_NCCL(ncclSend(ep->snd.meta + row * EP_ROW_META, c * EP_ROW_META, ncclInt32, d, ep->comm, st));
+    }
+    for (int s = 0; s < n; s++) {
+        const size_t row = size_t(s) * tm, c = size_t(tm);
+        EP_NCCL(ncclRecv(ep->sr.xq + row * MOE_EMBD, c * MOE_EMBD, ncclInt8, s, ep->comm, st));
+        EP_NCCL(ncclRecv(ep->sr.xd + row * (MOE_EMBD / 256), c * (MOE_EMBD / 256), ncclFloat32, s, ep->comm, st));
+        EP_NCCL(ncclRecv(ep->sr.xs + row * (MOE_EMBD / 16), c * (MOE_EMBD / 16) * 2, ncclInt8, s, ep->comm, st));
+        EP_NCCL(ncclRecv(ep->sr.sel + row * EP_ROW_META, c * EP_ROW_META, ncclInt32, s, ep->comm, st));
+    }
+    EP_NCCL(ncclGroupEnd());
+    if ((rc = moe_grouped_range(*w, R, ep->sr, st, 0, ep->n_local, true, 0, R * MOE_TOPK))) return rc;
+    // the shared expert of the own tokens needs no exchange
+    if (T > 0 && (rc = moe_grouped_range(*w, T, ep->sl, st, MOE_NEXP, 1, false, T * MOE_TOPK, T))) return rc;
+    const size_t blk = size_t(tm) * MOE_NSLOT * MOE_EMBD;
+    EP_NCCL(ncclGroupStart());
+    for (int s = 0; s < n; s++) EP_NCCL(ncclSend(ep->sr.part + s * blk, blk, ncclFloat32, s, ep->comm, st));
+    for (int d = 0; d < n; d++) EP_NCCL(ncclRecv(ep->ret_fixed + d * blk, blk, ncclFloat32, d, ep->comm, st));
+    EP_NCCL(ncclGroupEnd());
+    if (T > 0) {
+        ep_unpack_fixed_kernel<<<T * MOE_TOPK, 256, 0, st>>>(ep->ret_fixed, ep->sl.sel, ep->tokidx, ep->n_local, tm,
+                                                             ep->sl.part);
+        QMA_CHECK_LAUNCH();
+        if ((rc = moe_combine(ep->sl, x2, x_out, T, st))) return rc;
+    }
+    ep->sent = ep->recvd = uint64_t(n) * (tm * row_bytes + blk * 4);
+    ep->rows_in = -1;
+    return QMA_CUDA_OK;
+}
+
 extern "C" {
+
+int qma_cuda_ep_sync(qma_cuda_ep *ep, void *stream) {
+    qma::clear_error();
+    QMA_REQUIRE(ep, "qma_cuda_ep_sync: null handle");
+    QMA_REQUIRE(!ep->aborted && ep->comm, "qma_cuda_ep_sync: the communicator was aborted after a failure");
+    return ep_sync(ep, qma::as_stream(stream));
+}
 
 int qma_cuda_ep_unique_id(uint8_t *uid) {
     qma::clear_error();
@@ -359,16 +454,17 @@ int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ran
     const int tl = t_max < MOE_GROUPED_MIN_T ? MOE_GROUPED_MIN_T : t_max;
     const int tr = ep->r_max < MOE_GROUPED_MIN_T ? MOE_GROUPED_MIN_T : ep->r_max;
     const size_t rows = size_t(n_ranks) * t_max;
-    void *p[12];
+    void *p[13];
     int rc = 0;
-    const size_t sizes[12] = {
+    const size_t sizes[13] = {
         moe_scratch_bytes(tl), moe_scratch_bytes(tr),
         rows * MOE_EMBD, rows * sizeof(float) * (MOE_EMBD / 256), rows * sizeof(int16_t) * (MOE_EMBD / 16),
         rows * sizeof(int) * EP_ROW_META,
         size_t(ep->r_max) * MOE_TOPK * MOE_EMBD * sizeof(float), size_t(t_max) * MOE_TOPK * MOE_EMBD * sizeof(float),
         size_t(t_max) * EP_MAX_RANKS * sizeof(int), size_t(t_max) * MOE_TOPK * sizeof(int),
-        sizeof(int) * (2 * n_ranks + 2 * n_ranks * n_ranks), size_t(ep->r_max) * MOE_TOPK * sizeof(int)};
-    for (int i = 0; i < 12 && !rc; i++) {
+        sizeof(int) * (2 * n_ranks + 2 * n_ranks * n_ranks), size_t(ep->r_max) * MOE_TOPK * sizeof(int),
+        size_t(ep->r_max) * MOE_NSLOT * MOE_EMBD * sizeof(float)};
+    for (int i = 0; i < 13 && !rc; i++) {
         rc = ep_alloc(ep, sizes[i], &p[i]);
         // zeroed: the MoE scratch's tickets must start at zero (every call
         // leaves them zero again)
@@ -397,6 +493,7 @@ int qma_cuda_ep_init_timeout(int device, const uint8_t *uid, int rank, int n_ran
     ep->cnt = static_cast<int *>(p[10]);
     ep->allcnt = ep->cnt + 2 * n_ranks;
     ep->prow = static_cast<int *>(p[11]);
+    ep->ret_fixed = static_cast<float *>(p[12]);
     ncclUniqueId id;
     memcpy(&id, uid, sizeof(id));
     // non-blocking initialisation, polled against the wall-clock limit: a
@@ -441,6 +538,7 @@ int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const 
                 "qma_cuda_ep_moe_layer: down projections must be Q6_K");
     QMA_REQUIRE(!ep->aborted && ep->comm, "qma_cuda_ep_moe_layer: the communicator was aborted after a failure");
     cudaStream_t st = as_stream(stream);
+    if (!ep_counted()) return ep_moe_fixed(ep, w, x2, T, x_out, sel, wts, st);
     const int n = ep->n, me = ep->rank;
     int rc;
     // 1-3: route, plan, pack (T == 0: this rank only serves others)

@@ -12,18 +12,21 @@
 // (sub-block, digit), accumulating H = sum hi x and L = sum lo x over the
 // super-block in int32 (exact), I1 = 32 H + L.
 //
-// CTA (416 threads) = 128 rows x 128 tokens, the super-blocks in order as a
-// three-stage pipeline:
+// CTA (416 threads) = 128 rows x 128 tokens (N = 64 MMAs when the tile
+// holds at most 64), the super-blocks in order as a three-stage pipeline
+// over two buffers of every operand:
 //   warps 0-3 (producers, thread = row): the super-block's Q4_K block ->
 //     nibbles x scale -> two digit tiles (canonical K-major A), and the
 //     tokens' Q8_K slice (B), their 32-lane sums and scales;
 //   warp 4, one lane: the 16 MMAs of the super-block into one of two TMEM
 //     buffers (2 x 256 columns), then a commit;
 //   warps 5-12 (epilogue, thread = row of its TMEM lane quarter, half of
-//     the tokens): the super-block's H and L from TMEM, the mins and the
-//     fp32 fold into 64 register accumulators.
+//     the tile's tokens): the super-block's H and L from TMEM, the mins and
+//     the fp32 fold into up to 64 register accumulators.
 // The producer of super-block sb + 1 overlaps the MMAs of sb and the
-// epilogue of sb - 1.  Every wait is a bounded mbarrier wait.
+// epilogue of sb - 1; it reuses the buffers of sb - 1 once the MMAs and the
+// epilogue of sb - 1 are done with them.  Every wait is a bounded mbarrier
+// wait.
 #include "common.cuh"
 #include "gemv.cuh"
 #include "tc.cuh"
@@ -37,7 +40,7 @@ constexpr int GT_THREADS = 416;               // 4 producer warps, 1 MMA warp, 8
 constexpr int GT_EPI = 256;                   // epilogue threads
 
 struct GemmTcSmem {
-    uint8_t a[2][8][GT_TILE_A];                // [digit][sub-block] of one super-block (64 KB)
+    uint8_t a[2][2][8][GT_TILE_A];             // [buffer][digit][sub-block]           (128 KB)
     uint8_t b[2][8][GT_TILE_B];                // [buffer][sub-block]                  (64 KB)
     int bsum[2][GTN][8];                       // [buffer][token][sub-block]
     float xd[2][GTN];
@@ -81,7 +84,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     QMA_TRACE_SCOPE(TK_GEMV);
     extern __shared__ __align__(128) uint8_t gtsm_raw[];
     GemmTcSmem &S = *reinterpret_cast<GemmTcSmem *>(gtsm_raw);
-    __shared__ __align__(8) uint64_t bar_a, bar_mma[2], bar_epi[2];
+    __shared__ __align__(8) uint64_t bar_a[2], bar_mma[2], bar_epi[2];
     __shared__ uint32_t tmem_base;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r0 = blockIdx.x * GTM, t0 = blockIdx.y * GTN;
@@ -91,7 +94,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     pdl_wait();
     if (warp == 0) tmem_alloc(&tmem_base, GT_TMEM_COLS);
     if (tid == 0) {
-        mbar_init(&bar_a, 128);
+        mbar_init(&bar_a[0], 128);
+        mbar_init(&bar_a[1], 128);
         mbar_init(&bar_mma[0], 1);
         mbar_init(&bar_mma[1], 1);
         mbar_init(&bar_epi[0], GT_EPI);
@@ -117,11 +121,12 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
 #pragma unroll
                 for (int k = 0; k < 9; k++) nxt[k] = live ? __ldg(row + 9 * (sb + 1) + k) : make_uint4(0, 0, 0, 0);
             }
-            // the A tiles are free once the MMAs of sb - 1 completed (which also
-            // frees B buffer `buf`, last read by sb - 2); the sums and scales of
-            // buffer `buf` once the epilogue of sb - 2 is done with them
-            if (sb >= 1) gt_wait(&bar_mma[(sb - 1) & 1], uint32_t(((sb - 1) >> 1) & 1));
-            if (sb >= 2) gt_wait(&bar_epi[buf], uint32_t(((sb - 2) >> 1) & 1));
+            // buffer `buf` (A, B) is free once the MMAs of sb - 2 completed, its
+            // sums and scales once the epilogue of sb - 2 is done with them
+            if (sb >= 2) {
+                gt_wait(&bar_mma[buf], uint32_t(((sb - 2) >> 1) & 1));
+                gt_wait(&bar_epi[buf], uint32_t(((sb - 2) >> 1) & 1));
+            }
             int sc[8], mn[8];
             gt_scales(cur[0].y, cur[0].z, cur[0].w, sc, mn);
 #pragma unroll
@@ -137,8 +142,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
 #pragma unroll
                         for (int c = 0; c < 4; c++)
                             gt_digits((w[c] >> (4 * half)) & 0x0F0F0F0Fu, uint32_t(sc[j]), hi[c], lo[c]);
-                        *reinterpret_cast<uint4 *>(&S.a[0][j][tc_off(m, 16 * kc)]) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4 *>(&S.a[1][j][tc_off(m, 16 * kc)]) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4 *>(&S.a[buf][0][j][tc_off(m, 16 * kc)]) =
+                            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4 *>(&S.a[buf][1][j][tc_off(m, 16 * kc)]) =
+                            make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
             }
@@ -158,7 +165,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
                 S.xd[buf][m] = tv ? xd[size_t(t) * nsb + sb] : 0.0f;
             }
             fence_async_smem();
-            mbar_arrive(&bar_a);
+            mbar_arrive(&bar_a[buf]);
             if (sb + 1 < nsb) {
 #pragma unroll
                 for (int k = 0; k < 9; k++) cur[k] = nxt[k];
@@ -167,18 +174,19 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     } else if (warp == 4) {
         // ---- MMA issue --------------------------------------------------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc_s8(GTM, GTN);
+            // a tile of at most 64 tokens: N = 64 (the B rows past 64 are not read)
+            const uint32_t idesc = T - t0 <= GTN / 2 ? tc_idesc_s8(GTM, GTN / 2) : tc_idesc_s8(GTM, GTN);
             for (int sb = 0; sb < nsb; sb++) {
                 const int buf = sb & 1;
-                gt_wait(&bar_a, uint32_t(sb & 1));
+                gt_wait(&bar_a[buf], uint32_t((sb >> 1) & 1));
                 if (sb >= 2) gt_wait(&bar_epi[buf], uint32_t(((sb - 2) >> 1) & 1));   // TMEM buffer free
                 tc_fence_after();
                 const uint32_t d0 = tmem + uint32_t(buf * 2 * GTN);
 #pragma unroll 1
                 for (int j = 0; j < 8; j++) {
                     const uint64_t bd = tc_desc(S.b[buf][j]);
-                    tc_mma_s8(d0, tc_desc(S.a[0][j]), bd, idesc, j > 0);
-                    tc_mma_s8(d0 + GTN, tc_desc(S.a[1][j]), bd, idesc, j > 0);
+                    tc_mma_s8(d0, tc_desc(S.a[buf][0][j]), bd, idesc, j > 0);
+                    tc_mma_s8(d0 + GTN, tc_desc(S.a[buf][1][j]), bd, idesc, j > 0);
                 }
                 tc_commit(&bar_mma[buf]);
             }
@@ -187,8 +195,12 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     } else {
         // ---- epilogue: warps 5..12, row m = 32 (warp % 4) + lane, tokens of half
         // (warp - 5) / 4 of the tile ------------------------------------------------
+        // the tile's tokens split evenly over the two halves of the epilogue
+        // warps, in multiples of 16 (a tile of 64 tokens: 32 each)
         constexpr int NH = GTN / 2;
-        const int q4 = warp & 3, m = 32 * q4 + lane, r = r0 + m, n0 = ((warp - 5) >> 2) * NH;
+        const int ntile = min(T - t0, GTN), half = ((ntile + 31) / 32) * 16;
+        const int n0 = ((warp - 5) >> 2) * half, cnt = max(0, min(half, ntile - n0));
+        const int q4 = warp & 3, m = 32 * q4 + lane, r = r0 + m;
         const bool live = r < n_out;
         const uint8_t *hrow = W + size_t(live ? r : 0) * RB;
         const uint32_t lane_addr = tmem + (uint32_t(32 * q4) << 16);
@@ -205,6 +217,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
             tc_fence_after();
 #pragma unroll
             for (int c0 = 0; c0 < NH; c0 += 16) {
+                if (c0 >= cnt) break;                // warp-uniform: past this half's tokens
                 int H[16], L[16];
                 tmem_ld16(lane_addr + uint32_t(buf * 2 * GTN + n0 + c0), H);
                 tmem_ld16(lane_addr + uint32_t(buf * 2 * GTN + GTN + n0 + c0), L);
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
 #pragma unroll
             for (int n = 0; n < NH; n++) {
                 const int t = t0 + n0 + n;
-                if (t < T) {
+                if (n < cnt && t < T) {
                     const size_t o = size_t(t) * n_out + r;
                     out[o] = resid ? __fadd_rn(acc[n], resid[o]) : acc[n];
                 }

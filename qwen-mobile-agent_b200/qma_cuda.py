@@ -259,6 +259,7 @@ _SIGS.update({
     "qma_cuda_ep_free": (_i32, [_vp]),
     "qma_cuda_ep_moe_layer": (_i32, [_vp, C.POINTER(MoeWeights), _vp, _i32, _vp, _vp, _vp, _vp]),
     "qma_cuda_ep_stats": (_i32, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_i32)]),
+    "qma_cuda_ep_sync": (_i32, [_vp, _vp]),
     "qma_cuda_batch_create": (_i32, [_vp, _i32, _i32, C.POINTER(_vp)]),
     "qma_cuda_batch_free": (_i32, [_vp]),
     "qma_cuda_batch_n_seq": (_i32, [_vp]),
@@ -307,6 +308,10 @@ class ExpertParallel:
 
     def moe_layer(self, w: MoeWeights, x2, T: int, x_out, sel=None, wts=None, stream=None) -> None:
         call("qma_cuda_ep_moe_layer", self.h, C.byref(w), ptr(x2), T, ptr(x_out), ptr(sel), ptr(wts), stream)
+
+    def sync(self, stream=None) -> None:
+        """Bounded wait for the stream's work, exchanges included."""
+        call("qma_cuda_ep_sync", self.h, stream)
 
     def stats(self) -> tuple[int, int, int]:
         s, r, n = C.c_uint64(), C.c_uint64(), C.c_int()

@@ -41,10 +41,12 @@ def _share_file(path, rank):
     return share
 
 
-def _worker(rank, uid_path, results):
+def _worker(rank, uid_path, results, counted=False):
     import torch
     from helpers import MoeLayer, to_dev, empty_dev
     import qma_cuda as Q
+    if counted:
+        os.environ["QMA_CUDA_EP_COUNTED"] = "1"
     try:
         torch.cuda.set_device(rank)
         Q.init(rank)
@@ -90,7 +92,10 @@ def _worker(rank, uid_path, results):
         results.put((rank, None, traceback.format_exc()))
 
 
-def test_expert_parallel_two_ranks_match_one_gpu():
+@pytest.mark.parametrize("counted", [False, True], ids=["fixed_capacity", "counted"])
+def test_expert_parallel_two_ranks_match_one_gpu(counted):
+    """Both exchanges: fixed-capacity blocks (no count on the host) and
+    exact-size transfers after an all-gather of the counts."""
     import torch
     if not torch.cuda.is_available() or torch.cuda.device_count() < N_RANKS:
         pytest.skip(f"needs {N_RANKS} GPUs")
@@ -98,7 +103,7 @@ def test_expert_parallel_two_ranks_match_one_gpu():
     results = ctx.Queue()
     with tempfile.TemporaryDirectory() as tmp:
         uid_path = os.path.join(tmp, "uid")
-        procs = [ctx.Process(target=_worker, args=(r, uid_path, results)) for r in range(N_RANKS)]
+        procs = [ctx.Process(target=_worker, args=(r, uid_path, results, counted)) for r in range(N_RANKS)]
         for p in procs:
             p.start()
         got = {}
