@@ -9,8 +9,12 @@
  * calling thread.  Nothing here ever calls exit().
  *
  * Pointer conventions: arguments documented "device" are CUDA device
- * pointers; "host" are ordinary host pointers.  Weight type ids are GGML's
- * (qma.h:67-69): 12 = Q4_K, 14 = Q6_K, plus 8 = Q8_0.
+ * pointers; "host" are ordinary host pointers.  Device buffers are read
+ * with 16-byte vector loads: activation, weight and output buffers must be
+ * 16-byte aligned and scratch buffers 256-byte aligned (cudaMalloc's
+ * alignment satisfies both); a misaligned pointer is refused with
+ * QMA_CUDA_ERR_INVALID.  Weight type ids are GGML's (qma.h:67-69):
+ * 12 = Q4_K, 14 = Q6_K, plus 8 = Q8_0.
  *
  * Each entry point names the reference interface it replaces (qma sources,
  * file:line).

@@ -47,6 +47,8 @@ void clear_error();
     } while (0)
 
 static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+// Device buffers handed across the C ABI are read with 16-byte vector loads.
+static inline bool aligned_to(const void *p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
 
 // ------------------------------------------------------------ block formats
 constexpr int QK = 256;            // super-block lanes (QK_K, qma.h:74)
@@ -449,6 +451,27 @@ __device__ __forceinline__ float q4k_fold(float acc, float xd, float d, float dm
 }
 __device__ __forceinline__ float q6k_fold(float acc, float xd, float d, int I) {
     return __fadd_rn(acc, __fmul_rn(__fmul_rn(d, xd), float(I)));
+}
+
+// I2 = sum_j m_j (s_2j + s_2j+1) of one Q4_K super-block: the eight 6-bit
+// mins m_j against the Q8_K activation's sixteen 16-lane sums s (int16 at p,
+// 16-byte aligned), as eight 2-way 16 x 8-bit integer dot products over
+// byte-duplicated mins (md[i] = bytes m_2i, m_2i, m_2i+1, m_2i+1).  Exact:
+// the same integer as the plain sum.
+__device__ __forceinline__ void q4k_mins_dup(const int (&mn)[8], int (&md)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) md[i] = (mn[2 * i] * 0x0101) | ((mn[2 * i + 1] * 0x0101) << 16);
+}
+__device__ __forceinline__ int q4k_i2(const int16_t *p, const int (&md)[4]) {
+    const int4 u = __ldg(reinterpret_cast<const int4 *>(p)), v = __ldg(reinterpret_cast<const int4 *>(p) + 1);
+    int r = __dp2a_lo(u.x, md[0], 0);
+    r = __dp2a_hi(u.y, md[0], r);
+    r = __dp2a_lo(u.z, md[1], r);
+    r = __dp2a_hi(u.w, md[1], r);
+    r = __dp2a_lo(v.x, md[2], r);
+    r = __dp2a_hi(v.y, md[2], r);
+    r = __dp2a_lo(v.z, md[3], r);
+    return __dp2a_hi(v.w, md[3], r);
 }
 
 // 6-bit scale/min unpack of a Q4_K super-block (get_scale_min_k4,

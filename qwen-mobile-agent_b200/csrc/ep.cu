@@ -530,6 +530,7 @@ int qma_cuda_ep_moe_layer(qma_cuda_ep *ep, const qma_cuda_moe_weights *w, const 
     using namespace qma;
     clear_error();
     QMA_REQUIRE(ep && w && x2 && x_out, "qma_cuda_ep_moe_layer: null argument");
+    QMA_REQUIRE(aligned_to(x2, 16) && aligned_to(x_out, 16), "qma_cuda_ep_moe_layer: x2 / x_out must be 16-byte aligned");
     QMA_REQUIRE(T >= 0 && T <= ep->t_max, "qma_cuda_ep_moe_layer: T %d (0..%d)", T, ep->t_max);
     QMA_REQUIRE(w->post_norm && w->gate_inp && w->gate_exps && w->up_exps && w->down_exps && w->gate_inp_shexp &&
                     w->gate_shexp && w->up_shexp && w->down_shexp,

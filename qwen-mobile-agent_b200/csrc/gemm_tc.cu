@@ -42,7 +42,7 @@ constexpr int GT_EPI = 256;                   // epilogue threads
 struct GemmTcSmem {
     uint8_t a[2][2][8][GT_TILE_A];             // [buffer][digit][sub-block]           (128 KB)
     uint8_t b[2][8][GT_TILE_B];                // [buffer][sub-block]                  (64 KB)
-    int bsum[2][GTN][8];                       // [buffer][token][sub-block]
+    int16_t bsum[2][GTN][8];                   // [buffer][token][sub-block]: 32-lane sums (|s| <= 4064)
     float xd[2][GTN];
 };
 constexpr size_t GEMM_TC_SMEM = sizeof(GemmTcSmem);
@@ -159,9 +159,22 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
                     const int4 v = tv ? __ldg(src + c) : make_int4(0, 0, 0, 0);
                     *reinterpret_cast<int4 *>(&S.b[buf][c >> 1][tc_off(m, 16 * (c & 1))]) = v;
                 }
-                const int16_t *bs = xsum + size_t(tv ? t : 0) * (n_in / 16) + sb * 16;
+                // the token's sixteen 16-lane sums -> eight 32-lane sums, one store
+                int4 bv = make_int4(0, 0, 0, 0);
+                if (tv) {
+                    const int4 *bs = reinterpret_cast<const int4 *>(xsum + size_t(t) * (n_in / 16) + sb * 16);
+                    const int4 u = __ldg(bs), v = __ldg(bs + 1);
+                    const int w[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+                    uint32_t pk[4];
 #pragma unroll
-                for (int j = 0; j < 8; j++) S.bsum[buf][m][j] = tv ? int(bs[2 * j]) + int(bs[2 * j + 1]) : 0;
+                    for (int i = 0; i < 4; i++) {
+                        const int s0 = int(int16_t(w[2 * i] & 0xffff)) + (w[2 * i] >> 16);
+                        const int s1 = int(int16_t(w[2 * i + 1] & 0xffff)) + (w[2 * i + 1] >> 16);
+                        pk[i] = (uint32_t(s0) & 0xffffu) | (uint32_t(s1) << 16);
+                    }
+                    bv = make_int4(int(pk[0]), int(pk[1]), int(pk[2]), int(pk[3]));
+                }
+                *reinterpret_cast<int4 *>(&S.bsum[buf][m][0]) = bv;
                 S.xd[buf][m] = tv ? xd[size_t(t) * nsb + sb] : 0.0f;
             }
             fence_async_smem();
@@ -212,6 +225,9 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
             const uint4 h = __ldg(reinterpret_cast<const uint4 *>(hrow + size_t(sb) * Q4K_BYTES));
             int sc[8], mn[8];
             gt_scales(h.y, h.z, h.w, sc, mn);
+            // the eight 6-bit mins as packed bytes for the 16 x 8-bit dot products
+            const int mlo = mn[0] | (mn[1] << 8) | (mn[2] << 16) | (mn[3] << 24);
+            const int mhi = mn[4] | (mn[5] << 8) | (mn[6] << 16) | (mn[7] << 24);
             const float d = h2f(uint16_t(h.x & 0xffffu)), dm = h2f(uint16_t(h.x >> 16));
             gt_wait(&bar_mma[buf], uint32_t((sb >> 1) & 1));
             tc_fence_after();
@@ -224,10 +240,12 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
                 tmem_wait_ld();
 #pragma unroll
                 for (int n = 0; n < 16; n++) {
-                    const int4 b0 = *reinterpret_cast<const int4 *>(&S.bsum[buf][n0 + c0 + n][0]);
-                    const int4 b1 = *reinterpret_cast<const int4 *>(&S.bsum[buf][n0 + c0 + n][4]);
-                    const int I2 = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w + mn[4] * b1.x +
-                                   mn[5] * b1.y + mn[6] * b1.z + mn[7] * b1.w;
+                    // I2 = sum_j m_j bsum_j: four 2-way 16 x 8-bit integer dot products
+                    const int4 b = *reinterpret_cast<const int4 *>(&S.bsum[buf][n0 + c0 + n][0]);
+                    int I2 = __dp2a_lo(b.x, mlo, 0);
+                    I2 = __dp2a_hi(b.y, mlo, I2);
+                    I2 = __dp2a_lo(b.z, mhi, I2);
+                    I2 = __dp2a_hi(b.w, mhi, I2);
                     acc[c0 + n] = q4k_fold(acc[c0 + n], S.xd[buf][n0 + c0 + n], d, dm, 32 * H[n] + L[n], I2);
                 }
             }

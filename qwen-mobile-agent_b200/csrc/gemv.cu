@@ -485,19 +485,16 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
             }
         }
         // mins through the block sums of each token column, then the fp32 fold
+        int md0[4], md1[4];
+        q4k_mins_dup(mn0, md0);
+        q4k_mins_dup(mn1, md1);
 #pragma unroll
         for (int n = 0; n < GNT; n++)
 #pragma unroll
             for (int c = 0; c < 2; c++) {
                 if (!tv[n][c]) continue;
                 const int16_t *bs = xsum + size_t(tc[n][c]) * (n_in / 16) + sb * 16;
-                int I2a = 0, I2b = 0;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int pair = int(bs[2 * j]) + int(bs[2 * j + 1]);
-                    I2a += mn0[j] * pair;
-                    I2b += mn1[j] * pair;
-                }
+                const int I2a = q4k_i2(bs, md0), I2b = q4k_i2(bs, md1);
                 const float x = xd[size_t(tc[n][c]) * nsb + sb];
                 acc[n][c] = q4k_fold(acc[n][c], x, d0, dm0, I1[n][c], I2a);
                 acc[n][2 + c] = q4k_fold(acc[n][2 + c], x, d1, dm1, I1[n][2 + c], I2b);
@@ -647,6 +644,9 @@ int qma_cuda_matvec(int wtype, const void *W, int n_in, int n_out, int T, const 
     qma::clear_error();
     QMA_REQUIRE(W && xq && xd && xsum && out && n_in > 0 && n_in % 256 == 0 && n_out > 0 && T > 0,
                 "qma_cuda_matvec: bad arguments (n_in %d, n_out %d, T %d)", n_in, n_out, T);
+    QMA_REQUIRE(qma::aligned_to(W, 16) && qma::aligned_to(xq, 16) && qma::aligned_to(xd, 16) &&
+                    qma::aligned_to(xsum, 16) && qma::aligned_to(out, 16),
+                "qma_cuda_matvec: device buffers must be 16-byte aligned");
     return qma::matvec(wtype, W, n_in, n_out, T, xq, xd, xsum, out, qma::as_stream(stream));
 }
 

@@ -1200,6 +1200,8 @@ int qma_cuda_moe_layer(const qma_cuda_moe_weights *w, const float *x2, int T, fl
     qma::clear_error();
     QMA_REQUIRE(w && x2 && x_out && scratch && T > 0 && T <= 65535,
                 "qma_cuda_moe_layer: bad arguments (T %d)", T);
+    QMA_REQUIRE(qma::aligned_to(x2, 16) && qma::aligned_to(x_out, 16) && qma::aligned_to(scratch, 256),
+                "qma_cuda_moe_layer: x2 / x_out must be 16-byte and scratch 256-byte aligned");
     QMA_REQUIRE(w->post_norm && w->gate_inp && w->gate_exps && w->up_exps && w->down_exps &&
                     w->gate_inp_shexp && w->gate_shexp && w->up_shexp && w->down_shexp,
                 "qma_cuda_moe_layer: missing weight pointer");

@@ -188,6 +188,9 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                 }
             }
         }
+        int md0[4], md1[4];
+        q4k_mins_dup(mn0, md0);
+        q4k_mins_dup(mn1, md1);
 #pragma unroll
         for (int n = 0; n < 4; n++)
 #pragma unroll
@@ -195,13 +198,7 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                 if (pc[n][c] < 0) continue;
                 const int t = pc[n][c] < T * MOE_TOPK ? pc[n][c] / MOE_TOPK : pc[n][c] - T * MOE_TOPK;
                 const int16_t *bs = s.xs + size_t(t) * (MOE_EMBD / 16) + sb * 16;
-                int I2a = 0, I2b = 0;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int pr = int(bs[2 * j]) + int(bs[2 * j + 1]);
-                    I2a += mn0[j] * pr;
-                    I2b += mn1[j] * pr;
-                }
+                const int I2a = q4k_i2(bs, md0), I2b = q4k_i2(bs, md1);
                 const float x = s.xd[size_t(t) * (MOE_EMBD / 256) + sb];
                 acc[n][c] = q4k_fold(acc[n][c], x, d0, dm0, I1[n][c], I2a);
                 acc[n][2 + c] = q4k_fold(acc[n][2 + c], x, d1, dm1, I1[n][2 + c], I2b);

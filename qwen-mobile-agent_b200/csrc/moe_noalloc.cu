@@ -70,6 +70,8 @@ extern "C" int qma_cuda_moe_layer_noalloc(const qma_cuda_moe_weights *w, const f
                                           void *stream) {
     qma::clear_error();
     QMA_REQUIRE(w && x2 && x_out && T > 0, "qma_cuda_moe_layer_noalloc: bad arguments (T %d)", T);
+    QMA_REQUIRE(qma::aligned_to(x2, 16) && qma::aligned_to(x_out, 16),
+                "qma_cuda_moe_layer_noalloc: x2 / x_out must be 16-byte aligned");
     if (T > QMA_CUDA_MOE_NOALLOC_MAX_T) {
         qma::set_error("qma_cuda_moe_layer_noalloc: T = %d tokens exceeds the fixed scratch "
                        "capacity of %d tokens; use qma_cuda_moe_layer with caller scratch",

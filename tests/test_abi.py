@@ -28,6 +28,19 @@ def test_bad_arguments_return_invalid_without_touching_the_device():
     assert lib.qma_cuda_repack(Q.Q6_K, None, 4, 512, None, None) == Q.ERR_INVALID
 
 
+def test_misaligned_device_pointers_are_refused():
+    lib = Q.lib()
+    # 16-byte vector loads read the activation sums and rows: an unaligned
+    # buffer is refused before anything is launched
+    assert lib.qma_cuda_matvec(Q.Q4_K, 256, 2048, 16, 16, 256, 256, 258, 256, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_matvec(Q.Q4_K, 256, 2048, 16, 16, 264, 256, 256, 256, None) == Q.ERR_INVALID
+    assert "aligned" in Q.last_error()
+    w = Q.MoeWeights(*([256] * 9), Q.Q6_K, Q.Q6_K)
+    assert lib.qma_cuda_moe_layer(C.byref(w), 260, 1, 256, None, None, 512, 1 << 20, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_moe_layer(C.byref(w), 256, 1, 256, None, None, 512 + 16, 1 << 20, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_moe_layer_noalloc(C.byref(w), 256, 1, 260, None, None, None) == Q.ERR_INVALID
+
+
 def test_packed_sizes():
     # Q4_K stays in GGUF order; Q6_K / Q8_0 planes hold exactly the GGUF bytes
     assert Q.packed_bytes(Q.Q4_K, 512, 2048) == 512 * 8 * 144
