@@ -590,7 +590,10 @@ def run_ep_on_model(model, full_w, args, world, rank, local):
         "ep_parity": ok_all, "parity_detail": detail,
         "router_prior": "log Zipf(s=1.1) over a seeded per-layer expert ranking, added to every router logit",
         "expert_load": expert_load,
-        "collectives": "per layer: NCCL all-gather of the counts, grouped send/recv dispatch and return",
+        "collectives": "per layer: grouped NCCL send/recv of fixed blocks of 64/N rows per peer (dispatch) and of "
+                       "their slot partials (return); no host synchronisation"
+                       if not os.environ.get("QMA_CUDA_EP_COUNTED") else
+                       "per layer: NCCL all-gather of the counts (read on the host), exact-size send/recv",
     }
 
 
