@@ -10,6 +10,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -103,7 +104,7 @@ struct qma_cuda_state {
     std::vector<uint8_t> tier;
     std::vector<int> pin_pos;
     int live_n = 0, n4 = 0, n_ring_q4 = 0, rebuilt_at = 0, next_rebuild = HCM_REBUILD_INIT;
-    std::vector<float> h_sal, h_qf, h_pin_sal;
+    float *h_sal = nullptr, *h_qf = nullptr, *h_pin_sal = nullptr;   // pinned, the rebuild's reads
     // decode graph
     cudaGraphExec_t graph = nullptr;
     int graph_nk = -1;
@@ -551,12 +552,15 @@ static int hcm_rebuild(qma_cuda_state *s, int n_pos) {
         }
         s->live_n = s->n4 = s->n_ring_q4 = n_pos;
     } else {
-        s->h_sal.resize(size_t(NATTN) * cap);
-        s->h_qf.resize(cap);
-        s->h_pin_sal.resize(size_t(NATTN) * HCM_H_PIN);
-        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_sal.data(), s->sal, s->h_sal.size() * 4, cudaMemcpyDeviceToHost, st));
-        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_qf.data(), s->qf, s->h_qf.size() * 4, cudaMemcpyDeviceToHost, st));
-        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_pin_sal.data(), s->pin_sal, s->h_pin_sal.size() * 4,
+        if (!s->h_sal) {
+            QMA_CHECK_CUDA(cudaMallocHost(&s->h_sal, sizeof(float) * NATTN * size_t(cap)));
+            QMA_CHECK_CUDA(cudaMallocHost(&s->h_qf, sizeof(float) * size_t(cap)));
+            QMA_CHECK_CUDA(cudaMallocHost(&s->h_pin_sal, sizeof(float) * NATTN * size_t(HCM_H_PIN)));
+        }
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_sal, s->sal, sizeof(float) * NATTN * size_t(cap), cudaMemcpyDeviceToHost,
+                                       st));
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_qf, s->qf, sizeof(float) * size_t(cap), cudaMemcpyDeviceToHost, st));
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_pin_sal, s->pin_sal, sizeof(float) * NATTN * size_t(HCM_H_PIN),
                                        cudaMemcpyDeviceToHost, st));
         QMA_CHECK_CUDA(cudaStreamSynchronize(st));
         int n = 0;
@@ -588,30 +592,45 @@ static int hcm_rebuild(qma_cuda_state *s, int n_pos) {
             for (int l = 0; l < NATTN; l++) sc += s->h_pin_sal[size_t(l) * HCM_H_PIN + a];
             heap_push(heap, hn, sc, a, 1);
         }
+        // Each winner not yet in the arena takes the first free slot, else
+        // evicts the lowest-scoring occupied slot that no winner keeps
+        // (lowest index on equal scores), as the reference's scans do
+        // (nn.c:1092-1127).  Without rescanning every slot per winner: a
+        // slot's score changes only when a winner takes it, and then it is
+        // kept, so one list of the occupied, unkept slots sorted by (score,
+        // index) serves every eviction; free slots only fill, so the first
+        // free one is found by a forward pointer.
         std::vector<int> new_arena(HCM_H_PIN, -1);
-        for (int i = 0; i < hn; i++) new_arena[i] = heap[i].is_arena ? heap[i].pos : -1;
+        std::vector<uint8_t> kept(HCM_H_PIN, 0);
+        for (int i = 0; i < hn; i++) {
+            new_arena[i] = heap[i].is_arena ? heap[i].pos : -1;
+            if (new_arena[i] >= 0) kept[new_arena[i]] = 1;
+        }
+        std::vector<std::pair<float, int>> evict;
+        for (int a = 0; a < HCM_H_PIN; a++) {
+            if (s->pin_pos[a] < 0 || kept[a]) continue;
+            float sc = 0.0f;
+            for (int l = 0; l < NATTN; l++) sc += s->h_pin_sal[size_t(l) * HCM_H_PIN + a];
+            if (sc < 1e30f) evict.push_back(std::make_pair(sc, a));   // the scans' bound (never NaN)
+        }
+        std::sort(evict.begin(), evict.end());
+        size_t ev = 0;
+        int next_free = 0;
         std::vector<int2> pairs;
         for (int i = 0; i < hn; i++) {
             if (heap[i].is_arena) continue;
             const int src = hcm_slot(heap[i].pos, cap);
             int slot = -1;
-            for (int a = 0; a < HCM_H_PIN; a++) if (s->pin_pos[a] < 0) { slot = a; break; }
-            if (slot < 0) {
-                float worst = 1e30f;
-                int wi = -1;
-                for (int a = 0; a < HCM_H_PIN; a++) {
-                    if (s->pin_pos[a] < 0) continue;
-                    bool kept = false;
-                    for (int k = 0; k < hn; k++) if (new_arena[k] == a) { kept = true; break; }
-                    if (kept) continue;
-                    float sc = 0.0f;
-                    for (int l = 0; l < NATTN; l++) sc += s->h_pin_sal[size_t(l) * HCM_H_PIN + a];
-                    if (sc < worst) { worst = sc; wi = a; }
-                }
-                slot = wi;
+            while (next_free < HCM_H_PIN && s->pin_pos[next_free] >= 0) next_free++;
+            if (next_free < HCM_H_PIN) {
+                slot = next_free;
+            } else {
+                while (ev < evict.size() && kept[evict[ev].second]) ev++;
+                if (ev < evict.size()) slot = evict[ev].second;
             }
             if (slot < 0) continue;
             new_arena[i] = slot;
+            kept[slot] = 1;
             pairs.push_back(make_int2(src, slot));
             for (int l = 0; l < NATTN; l++)
                 s->h_pin_sal[size_t(l) * HCM_H_PIN + slot] = s->h_sal[size_t(l) * cap + src];
@@ -1316,6 +1335,7 @@ int qma_cuda_state_free(qma_cuda_state *s) {
     for (void *p : s->allocs) cudaFree(p);
     for (float *p : {s->scores, s->cmax, s->opart, s->lpart}) if (p) cudaFree(p);
     if (s->sp_host) cudaFreeHost(s->sp_host);
+    for (float *p : {s->h_sal, s->h_qf, s->h_pin_sal}) if (p) cudaFreeHost(p);
     cudaStreamSynchronize(s->side);
     cudaEventDestroy(s->ev_fork);
     cudaEventDestroy(s->ev_join);

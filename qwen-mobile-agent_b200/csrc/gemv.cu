@@ -512,6 +512,111 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
         }
 }
 
+// ------------------------------------------------ Q8_0 GEMM on tensor cores --
+// Several tokens against Q8_0 rows (the LM head of a batched step, the
+// logits of a prefill chunk): one mma.sync m16n8k32 (s8 x s8 -> s32) per
+// 32-element block gives its exact integer dot for 16 rows x 8 tokens; a
+// 64-element unit contributes (i0 d0 + i1 d1) xd in fp32 as in FmtQ80::dot,
+// the units summed in order.  Warp: 16 rows x 32 tokens; CTA: 4 warps = 64
+// rows.  Grid (token tiles, row blocks): the token tiles of one row block
+// run next to each other, so the weight rows are read from HBM once.
+__global__ void __launch_bounds__(128) gemm_q80_mma_kernel(Q8Planes P, int n_in, int n_out, int T,
+                                                           const int8_t *__restrict__ xq,
+                                                           const float *__restrict__ xd, float *out,
+                                                           const float *resid) {
+    QMA_TRACE_SCOPE(TK_GEMV);
+    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ int brow[BT_COLS];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int row0 = (blockIdx.y * 4 + warp) * 16;
+    const int tok0 = blockIdx.x * (8 * GNT);
+    const bool active = row0 < n_out;            // warp-uniform; every warp stages and syncs
+    if (threadIdx.x < BT_COLS) brow[threadIdx.x] = tok0 + int(threadIdx.x) < T ? tok0 + int(threadIdx.x) : -1;
+    pdl_trigger();
+    pdl_wait();
+    const int nsb = n_in / 256, nb = n_in / 32;
+    const int8_t *q0 = P.q + size_t(active ? row0 + gid : 0) * n_in, *q1 = q0 + size_t(8) * n_in;
+    const __half *dr0 = P.d + size_t(active ? row0 + gid : 0) * nb, *dr1 = dr0 + size_t(8) * nb;
+    float acc[GNT][4];
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    int tc[GNT][2];
+    bool tv[GNT][2];
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            tc[n][c] = tok0 + 8 * n + 2 * tig + c;
+            tv[n][c] = tc[n][c] < T;
+        }
+    for (int sb = 0; sb < nsb; sb++) {
+        __syncthreads();                          // the previous tile is consumed
+        stage_btile(bt, brow, xq, size_t(n_in), sb * 256);
+        __syncthreads();
+        if (!active) continue;
+        float x[GNT][2];
+#pragma unroll
+        for (int n = 0; n < GNT; n++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) x[n][c] = tv[n][c] ? xd[size_t(tc[n][c]) * nsb + sb] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {             // units of 64: blocks 2u, 2u + 1
+            int p[2][GNT][4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int k = sb * 256 + 32 * (2 * u + h) + 4 * tig;
+                const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(q0 + k),
+                                       *reinterpret_cast<const uint32_t *>(q1 + k),
+                                       *reinterpret_cast<const uint32_t *>(q0 + k + 16),
+                                       *reinterpret_cast<const uint32_t *>(q1 + k + 16)};
+#pragma unroll
+                for (int n = 0; n < GNT; n++) {
+                    const int8_t *bp = &bt[8 * n + gid][32 * (2 * u + h) + 4 * tig];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) p[h][n][i] = 0;
+                    mma_s8(p[h][n], a, *reinterpret_cast<const uint32_t *>(bp),
+                           *reinterpret_cast<const uint32_t *>(bp + 16));
+                }
+            }
+            const int b = sb * 8 + 2 * u;
+            const float d00 = __half2float(dr0[b]), d01 = __half2float(dr0[b + 1]);
+            const float d10 = __half2float(dr1[b]), d11 = __half2float(dr1[b + 1]);
+#pragma unroll
+            for (int n = 0; n < GNT; n++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const float t0 = __fmul_rn(__fadd_rn(__fmul_rn(float(p[0][n][c]), d00),
+                                                         __fmul_rn(float(p[1][n][c]), d01)), x[n][c]);
+                    const float t1 = __fmul_rn(__fadd_rn(__fmul_rn(float(p[0][n][2 + c]), d10),
+                                                         __fmul_rn(float(p[1][n][2 + c]), d11)), x[n][c]);
+                    acc[n][c] = __fadd_rn(acc[n][c], t0);
+                    acc[n][2 + c] = __fadd_rn(acc[n][2 + c], t1);
+                }
+        }
+    }
+    if (!active) return;
+#pragma unroll
+    for (int n = 0; n < GNT; n++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (!tv[n][c]) continue;
+            const size_t o0 = size_t(tc[n][c]) * n_out + row0 + gid, o1 = o0 + 8;
+            out[o0] = resid ? __fadd_rn(acc[n][c], resid[o0]) : acc[n][c];
+            out[o1] = resid ? __fadd_rn(acc[n][2 + c], resid[o1]) : acc[n][2 + c];
+        }
+}
+
+static int launch_gemm_q80(const Q8Planes &P, int n_in, int n_out, int T, const int8_t *xq, const float *xd,
+                           float *out, const float *resid, cudaStream_t st) {
+    const dim3 grid(unsigned((T + 8 * GNT - 1) / (8 * GNT)), unsigned((n_out + 63) / 64));
+    QMA_CHECK_CUDA(launch_ex(gemm_q80_mma_kernel, grid, dim3(128), 0, st, 1, pdl_enabled(), P, n_in, n_out, T, xq,
+                             xd, out, resid));
+    return QMA_CUDA_OK;
+}
+
 // gemm_tc.cu
 int launch_gemm_q4k_tc(const uint8_t *W, int n_in, int n_out, int T, const int8_t *xq, const float *xd,
                        const int16_t *xsum, float *out, const float *resid, cudaStream_t st);
@@ -546,6 +651,12 @@ static int gemv_tokens(const typename F::Ptr &W, int n_in, int n_out, int T, con
             return launch_gemm_q4k_tc(W, n_in, n_out, T, xq, xd, xsum, out, resid, st);
         if (T >= 8 && n_out % 16 == 0)
             return launch_gemm_q4k(W, n_in, n_out, T, xq, xd, xsum, out, resid, st);
+    }
+    // several tokens over Q8_0 rows (batched LM head, prefill logits): the
+    // MMA kernel reads the rows once for every 32 tokens instead of once per
+    // pass of 4
+    if constexpr (std::is_same<F, FmtQ80>::value) {
+        if (T >= 8 && n_out % 16 == 0) return launch_gemm_q80(W, n_in, n_out, T, xq, xd, out, resid, st);
     }
     int t0 = 0;
     while (t0 < T) {

@@ -85,22 +85,24 @@ def test_integer_partials_bit_exact(cuda, rng, wtype, shape):
     assert np.array_equal(got.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_K, O.Q6_K])
-def test_lm_head_shape(cuda, rng, wtype):
+@pytest.mark.parametrize("wtype,T", [(O.Q8_0, 1), (O.Q4_K, 1), (O.Q6_K, 1), (O.Q8_0, 37)])
+def test_lm_head_shape(cuda, rng, wtype, T):
+    """The 151936 x 2048 LM head; Q8_0 with 37 tokens takes the MMA GEMM of a
+    batched step (two token tiles, the second partial)."""
     import torch
     n_out, n_in = 151936, 2048
     W = O.synth_matrix(f"lmhead.{wtype}", wtype, n_out, n_in, seed=13)
-    x = rng.standard_normal((1, n_in)).astype(np.float32)
+    x = rng.standard_normal((T, n_in)).astype(np.float32)
     want = O.matmul(x, W, wtype, n_in, n_out)
     dq, dd, ds = gpu_quant(x)
     dP = gpu_pack(W, wtype, n_out, n_in)
-    out = empty_dev((1, n_out), torch.float32)
-    Q.call("qma_cuda_matvec", wtype, Q.ptr(dP), n_in, n_out, 1, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
+    out = empty_dev((T, n_out), torch.float32)
+    Q.call("qma_cuda_matvec", wtype, Q.ptr(dP), n_in, n_out, T, Q.ptr(dq), Q.ptr(dd), Q.ptr(ds),
            Q.ptr(out), None)
     torch.cuda.synchronize()
     got = out.cpu().numpy()
-    assert_close(got, want, RTOL, f"lm head type {wtype}")
-    assert int(got.argmax()) == int(want.argmax())
+    assert_close(got, want, RTOL, f"lm head type {wtype} T={T}")
+    assert np.array_equal(got.argmax(axis=1), want.argmax(axis=1))
 
 
 def test_matvec_is_deterministic(cuda, rng):
