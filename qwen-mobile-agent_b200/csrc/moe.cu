@@ -47,7 +47,7 @@ size_t moe_scratch_bytes(int T) {
     b += al256(sizeof(float) * T * MOE_NSLOT * MOE_EMBD); // part
     if (T >= MOE_GROUPED_MIN_T && T <= MOE_GROUPED_MAX_T) {
         const size_t q = size_t(T) * MOE_NSLOT;
-        b += al256(sizeof(int) * (MOE_NEXP + 1));         // goff
+        b += al256(sizeof(int) * 2 * (MOE_NEXP + 1));     // goff, active-expert list
         b += al256(sizeof(int) * T * MOE_TOPK);           // plist
         b += al256(sizeof(float) * q * 2 * MOE_FF);       // hg
         b += al256(q * MOE_FF);                           // hq
@@ -75,7 +75,7 @@ MoeScratch moe_scratch_layout(void *base, int T) {
     s.goff = nullptr; s.plist = nullptr; s.hg = nullptr; s.hq = nullptr; s.hd = nullptr; s.hs = nullptr;
     if (T >= MOE_GROUPED_MIN_T && T <= MOE_GROUPED_MAX_T) {
         const size_t q = size_t(T) * MOE_NSLOT;
-        s.goff = reinterpret_cast<int *>(take(sizeof(int) * (MOE_NEXP + 1)));
+        s.goff = reinterpret_cast<int *>(take(sizeof(int) * 2 * (MOE_NEXP + 1)));
         s.plist = reinterpret_cast<int *>(take(sizeof(int) * T * MOE_TOPK));
         s.hg = reinterpret_cast<float *>(take(sizeof(float) * q * 2 * MOE_FF));
         s.hq = reinterpret_cast<int8_t *>(take(q * MOE_FF));

@@ -31,7 +31,8 @@ struct MoeScratch {
     float *gs;             // [T] shared-expert gate sigmoid
     float *part;           // [T][9][2048] down projections per slot
     // grouped path only (null below MOE_GROUPED_MIN_T tokens):
-    int *goff;             // [257] first pair of each expert in plist
+    int *goff;             // [257] first pair of each expert in plist, then [1 + 256]: the
+                           // number of experts with pairs and their ids, ascending
     int *plist;            // [T * 8] pair ids t * 8 + k grouped by expert
     float *hg;             // [T * 9][1024] gate | up per pair slot
     int8_t *hq;            // [T * 9][512] Q8_K of silu(gate) * up

@@ -14,6 +14,8 @@
 //   3. moe_swiglu_kernel  : silu(gate) * up and its Q8_K per pair;
 //   4. moe_down_kernel    : down rows per expert, into the per-slot partials;
 //   5. moe_combine_norm_kernel (moe.cu) combines the slots.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
@@ -28,7 +30,10 @@ constexpr int NSHARED = MOE_NEXP;   // group index of the shared expert
 
 // 1. ---------------------------------------------------------------- lists --
 // One CTA: thread e counts expert e's pairs, an exclusive scan gives the
-// offsets, then thread e lists its pairs in token order.
+// offsets, then thread e lists its pairs in token order; the experts that
+// have pairs are also listed compactly (goff[257] = their number, then
+// their ids ascending) so that the expert kernels launch no CTA for the
+// others.
 __global__ void __launch_bounds__(256) moe_lists_kernel(const int *__restrict__ sel, int T, int *goff,
                                                         int *plist) {
     __shared__ int ssel[MOE_GROUPED_MAX_T * MOE_TOPK];
@@ -55,9 +60,28 @@ __global__ void __launch_bounds__(256) moe_lists_kernel(const int *__restrict__ 
     const int off = base + incl - cnt;
     goff[tid] = off;
     if (tid == 255) goff[256] = off + cnt;
+    // the active experts, ascending: the rank of e among them
+    __shared__ int wact[8];
+    const unsigned am = __ballot_sync(0xffffffffu, cnt > 0);
+    if (lane == 0) wact[warp] = __popc(am);
+    __syncthreads();
+    int abase = 0;
+    for (int w = 0; w < warp; w++) abase += wact[w];
+    int *act = goff + MOE_NEXP + 1;
+    if (cnt > 0) act[1 + abase + __popc(am & ((1u << lane) - 1u))] = tid;
+    if (tid == 255) act[0] = abase + __popc(am);
     int i = off;
     for (int p = 0; p < np; p++)
         if (ssel[p] == tid) plist[i++] = p;
+}
+
+// The group of grid row y of an expert kernel: rows below nyr take the
+// active routed experts in order (-1 past the last), the row after them the
+// shared expert.
+__device__ __forceinline__ int group_of_row(int y, int nyr, const int *goff) {
+    if (y >= nyr) return NSHARED;
+    const int *act = goff + MOE_NEXP + 1;
+    return y < act[0] ? act[1 + y] : -1;
 }
 
 // The pair slot of tile column tk of group e: routed pairs t * 8 + k, the
@@ -110,13 +134,15 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                                                          const uint8_t *__restrict__ up_exps,
                                                          const uint8_t *__restrict__ gate_sh,
                                                          const uint8_t *__restrict__ up_sh, int T,
-                                                         MoeScratch s, int e0) {
+                                                         MoeScratch s, int nyr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
-    const int e = e0 + int(blockIdx.y), tok0 = blockIdx.z * GT;
+    const int tok0 = blockIdx.z * GT;
     __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
+    const int e = group_of_row(int(blockIdx.y), nyr, s.goff);
+    if (e < 0) return;                                   // CTA-uniform: no more active experts
     const int ne = group_size(e, T, s.goff);
     if (tok0 >= ne) return;                              // CTA-uniform
     if (threadIdx.x < BT_COLS) {
@@ -240,13 +266,15 @@ __global__ void __launch_bounds__(64) moe_swiglu_kernel(MoeScratch s, int q0) {
 // int8 scale.  Grid (2048 / GR, 257, tiles); output part[t][slot][row].
 __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict__ down_exps, size_t down_bytes,
                                                        const uint8_t *__restrict__ down_sh, int T,
-                                                       MoeScratch s, int e0) {
+                                                       MoeScratch s, int nyr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
-    const int e = e0 + int(blockIdx.y), tok0 = blockIdx.z * GT;
+    const int tok0 = blockIdx.z * GT;
     __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
+    const int e = group_of_row(int(blockIdx.y), nyr, s.goff);
+    if (e < 0) return;                                   // CTA-uniform: no more active experts
     const int ne = group_size(e, T, s.goff);
     if (tok0 >= ne) return;                              // CTA-uniform
     if (threadIdx.x < BT_COLS) {
@@ -342,19 +370,28 @@ int moe_grouped_range(const qma_cuda_moe_weights &w, int T, const MoeScratch &s,
     const int tiles = (T + GT - 1) / GT;
     if (lists)
         QMA_CHECK_CUDA(launch_ex(moe_lists_kernel, dim3(1), dim3(256), 0, st, 1, pdl, s.sel, T, s.goff, s.plist));
+    // grid rows: the routed groups of [g0, g0 + ng) through the active-expert
+    // list (at most one per pair), then the shared expert if in range
+    const int nr = g0 < NSHARED ? std::min(g0 + ng, NSHARED) - g0 : 0;
+    const int nyr = std::min(nr, T * MOE_TOPK);
+    const int ny = nyr + (g0 + ng > NSHARED ? 1 : 0);
+    if (nr > 0 && g0 != 0) {
+        set_error("grouped experts: routed groups must start at expert 0 (got %d)", g0);
+        return QMA_CUDA_ERR_INVALID;
+    }
     if (!tc_grouped()) {
-        QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
+        QMA_CHECK_CUDA(launch_ex(moe_gateup_kernel, dim3(2 * MOE_FF / GR, ny, tiles), dim3(128), 0, st, 1, pdl,
                                  static_cast<const uint8_t *>(w.gate_exps), static_cast<const uint8_t *>(w.up_exps),
                                  static_cast<const uint8_t *>(w.gate_shexp), static_cast<const uint8_t *>(w.up_shexp),
-                                 T, s, g0));
+                                 T, s, nyr));
     } else {
         const int rc = launch_gateup_tc(w, T, s, st, g0, ng);
         if (rc) return rc;
     }
     QMA_CHECK_CUDA(launch_ex(moe_swiglu_kernel, dim3(nq), dim3(64), 0, st, 1, pdl, s, q0));
-    QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, ng, tiles), dim3(128), 0, st, 1, pdl,
+    QMA_CHECK_CUDA(launch_ex(moe_down_kernel, dim3(MOE_EMBD / GR, ny, tiles), dim3(128), 0, st, 1, pdl,
                              static_cast<const uint8_t *>(w.down_exps), packed_bytes(w.down_type, MOE_EMBD, MOE_FF),
-                             static_cast<const uint8_t *>(w.down_shexp), T, s, g0));
+                             static_cast<const uint8_t *>(w.down_shexp), T, s, nyr));
     return QMA_CUDA_OK;
 }
 
