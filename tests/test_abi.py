@@ -59,6 +59,7 @@ def test_expert_parallel_arguments_and_shards():
         assert lib.qma_cuda_ep_init(*args, C.byref(h)) == Q.ERR_INVALID, args
         assert "qma_cuda_ep_init" in Q.last_error()
     assert lib.qma_cuda_ep_moe_layer(None, None, None, 1, None, None, None, None) == Q.ERR_INVALID
+    assert lib.qma_cuda_ep_sync(None, None) == Q.ERR_INVALID
     assert lib.qma_cuda_ep_free(None) == Q.OK
     assert [Q.ep_shard(r, 4) for r in range(4)] == [(0, 64), (64, 64), (128, 64), (192, 64)]
     assert Q.ep_shard(0, 1) == (0, 256)
