@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                                                            const float *resid) {
     QMA_TRACE_SCOPE(TK_GEMV);
     static_assert(8 * GNT == BT_COLS, "one staged activation tile per CTA");
-    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ __align__(16) int8_t bt[2][BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
@@ -441,11 +441,20 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
             tc[n][c] = tok0 + 8 * n + 2 * tig + c;
             tv[n][c] = tc[n][c] < T;
         }
+    // activation tiles double-buffered: tile sb + 1 is copied while sb's MMAs run
+    __syncthreads();                              // brow
+    stage_btile_async(bt[0], brow, xq, size_t(n_in), 0);
     for (int sb = 0; sb < nsb; sb++) {
-        __syncthreads();                          // the previous tile is consumed
-        stage_btile(bt, brow, xq, size_t(n_in), sb * 256);
-        __syncthreads();
+        __syncthreads();                          // the tile of sb - 1 is consumed
+        if (sb + 1 < nsb) {
+            stage_btile_async(bt[(sb + 1) & 1], brow, xq, size_t(n_in), (sb + 1) * 256);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                          // tile sb is in shared memory
         if (!active) continue;
+        const int8_t(*bt_)[BT_STRIDE] = bt[sb & 1];
         const uint8_t *h0 = wr0 + size_t(sb) * 144, *h1 = wr1 + size_t(sb) * 144;
         int sc0[8], mn0[8], sc1[8], mn1[8];
         q4k_scales8(h0, sc0, mn0);
@@ -472,7 +481,7 @@ __global__ void __launch_bounds__(128) gemm_q4k_mma_kernel(const uint8_t *__rest
                                        (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
 #pragma unroll
                 for (int n = 0; n < GNT; n++) {
-                    const int8_t *bp = &bt[8 * n + gid][32 * j + 4 * tig];
+                    const int8_t *bp = &bt_[8 * n + gid][32 * j + 4 * tig];
                     const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bp);
                     const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bp + 16);
                     int p[4] = {0, 0, 0, 0};
@@ -525,7 +534,7 @@ __global__ void __launch_bounds__(128) gemm_q80_mma_kernel(Q8Planes P, int n_in,
                                                            const float *__restrict__ xd, float *out,
                                                            const float *resid) {
     QMA_TRACE_SCOPE(TK_GEMV);
-    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ __align__(16) int8_t bt[2][BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
@@ -552,11 +561,19 @@ __global__ void __launch_bounds__(128) gemm_q80_mma_kernel(Q8Planes P, int n_in,
             tc[n][c] = tok0 + 8 * n + 2 * tig + c;
             tv[n][c] = tc[n][c] < T;
         }
+    __syncthreads();                              // brow
+    stage_btile_async(bt[0], brow, xq, size_t(n_in), 0);
     for (int sb = 0; sb < nsb; sb++) {
-        __syncthreads();                          // the previous tile is consumed
-        stage_btile(bt, brow, xq, size_t(n_in), sb * 256);
-        __syncthreads();
+        __syncthreads();                          // the tile of sb - 1 is consumed
+        if (sb + 1 < nsb) {
+            stage_btile_async(bt[(sb + 1) & 1], brow, xq, size_t(n_in), (sb + 1) * 256);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                          // tile sb is in shared memory
         if (!active) continue;
+        const int8_t(*bt_)[BT_STRIDE] = bt[sb & 1];
         float x[GNT][2];
 #pragma unroll
         for (int n = 0; n < GNT; n++)
@@ -574,7 +591,7 @@ __global__ void __launch_bounds__(128) gemm_q80_mma_kernel(Q8Planes P, int n_in,
                                        *reinterpret_cast<const uint32_t *>(q1 + k + 16)};
 #pragma unroll
                 for (int n = 0; n < GNT; n++) {
-                    const int8_t *bp = &bt[8 * n + gid][32 * (2 * u + h) + 4 * tig];
+                    const int8_t *bp = &bt_[8 * n + gid][32 * (2 * u + h) + 4 * tig];
 #pragma unroll
                     for (int i = 0; i < 4; i++) p[h][n][i] = 0;
                     mma_s8(p[h][n], a, *reinterpret_cast<const uint32_t *>(bp),

@@ -411,6 +411,30 @@ __device__ __forceinline__ void stage_btile(int8_t (*bs)[BT_STRIDE], const int *
     }
 }
 
+// The same tile staged with cp.async (16-byte global -> shared copies that
+// bypass the registers; a column without a row is zero-filled: source size
+// 0), committed as one group: the caller waits with cp_async_wait<n>() and a
+// barrier, so the next super-block's tile can be in flight while this one's
+// MMAs run.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void stage_btile_async(int8_t (*bs)[BT_STRIDE], const int *rows, const int8_t *x,
+                                                  size_t ld, int k0) {
+    for (int i = threadIdx.x; i < BT_COLS * 16; i += blockDim.x) {
+        const int c = i >> 4, q = i & 15, r = rows[c];
+        cp_async16(&bs[c][16 * q], r >= 0 ? x + size_t(r) * ld + k0 + 16 * q : x, r >= 0);
+    }
+    cp_async_commit();
+}
+
 // Optional epilogue of a single-token GEMV over the gated delta net's input
 // projection: rows r < n are also the causal conv's channels (conv1d_layer
 // + SiLU, nn.c:717-741 / nn.c:2196), applied in the row's own thread with

@@ -130,14 +130,14 @@ __device__ __forceinline__ void q4k_scales8_words(uint32_t w0, uint32_t w1, uint
 // 2. ---------------------------------------------------------- gate / up --
 // Grid (1024 / GR rows of [gate | up], 257 groups, ceil(T / GT) tiles); warp
 // w: 16 rows, 4 column tiles of 8 pairs.  Output hg[pair][1024].
-__global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restrict__ gate_exps,
+__global__ void __launch_bounds__(128, 4) moe_gateup_kernel(const uint8_t *__restrict__ gate_exps,
                                                          const uint8_t *__restrict__ up_exps,
                                                          const uint8_t *__restrict__ gate_sh,
                                                          const uint8_t *__restrict__ up_sh, int T,
                                                          MoeScratch s, int nyr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     const int tok0 = blockIdx.z * GT;
-    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ __align__(16) int8_t bt[2][BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
@@ -176,11 +176,20 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
     // latency overlaps the staging and the MMAs
     Q4Words cur, nxt;
     cur.load(w0, w1, 0, tig);
+    // activation tiles double-buffered: tile sb + 1 is copied while sb's MMAs run
+    __syncthreads();                                     // brow
+    stage_btile_async(bt[0], brow, s.xq, MOE_EMBD, 0);
     for (int sb = 0; sb < MOE_EMBD / 256; sb++) {
         if (sb + 1 < MOE_EMBD / 256) nxt.load(w0, w1, sb + 1, tig);
-        __syncthreads();                                 // the previous tile is consumed
-        stage_btile(bt, brow, s.xq, MOE_EMBD, sb * 256);
-        __syncthreads();
+        __syncthreads();                                 // the tile of sb - 1 is consumed
+        if (sb + 1 < MOE_EMBD / 256) {
+            stage_btile_async(bt[(sb + 1) & 1], brow, s.xq, MOE_EMBD, (sb + 1) * 256);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                                 // tile sb is in shared memory
+        const int8_t(*bt_)[BT_STRIDE] = bt[sb & 1];
         int sc0[8], mn0[8], sc1[8], mn1[8];
         q4k_scales8_words(cur.h0.y, cur.h0.z, cur.h0.w, sc0, mn0);
         q4k_scales8_words(cur.h1.y, cur.h1.z, cur.h1.w, sc1, mn1);
@@ -202,7 +211,7 @@ __global__ void __launch_bounds__(128) moe_gateup_kernel(const uint8_t *__restri
                                        (r0b >> sh) & 0x0f0f0f0fu, (r1b >> sh) & 0x0f0f0f0fu};
 #pragma unroll
                 for (int n = 0; n < 4; n++) {
-                    const int8_t *bp = &bt[8 * n + gid][32 * j + 4 * tig];
+                    const int8_t *bp = &bt_[8 * n + gid][32 * j + 4 * tig];
                     const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bp);
                     const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bp + 16);
                     int p[4] = {0, 0, 0, 0};
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
                                                        MoeScratch s, int nyr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     const int tok0 = blockIdx.z * GT;
-    __shared__ __align__(16) int8_t bt[BT_COLS][BT_STRIDE];
+    __shared__ __align__(16) int8_t bt[2][BT_COLS][BT_STRIDE];
     __shared__ int brow[BT_COLS];
     pdl_trigger();
     pdl_wait();
@@ -298,10 +307,18 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
     for (int n = 0; n < 4; n++)
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    __syncthreads();                                     // brow
+    stage_btile_async(bt[0], brow, s.hq, N, 0);
     for (int sb = 0; sb < NSB; sb++) {
-        __syncthreads();                                 // the previous tile is consumed
-        stage_btile(bt, brow, s.hq, N, sb * 256);
-        __syncthreads();
+        __syncthreads();                                 // the tile of sb - 1 is consumed
+        if (sb + 1 < NSB) {
+            stage_btile_async(bt[(sb + 1) & 1], brow, s.hq, N, (sb + 1) * 256);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                                 // tile sb is in shared memory
+        const int8_t(*bt_)[BT_STRIDE] = bt[sb & 1];
         int I[4][4];
 #pragma unroll
         for (int n = 0; n < 4; n++)
@@ -330,7 +347,7 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const uint8_t *__restrict
             const int sc1 = P.sc[size_t(r0 + 8) * (N / 16) + sb * 16 + g];
 #pragma unroll
             for (int n = 0; n < 4; n++) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&bt[8 * n + gid][16 * g + 4 * tig]);
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&bt_[8 * n + gid][16 * g + 4 * tig]);
                 int p[4] = {0, 0, 0, 0};
                 mma_s8_k16(p, a[0], a[1], b0);
                 I[n][0] += sc0 * p[0];
