@@ -1079,6 +1079,7 @@ def run_ep_ours(args, world, rank, local):
     import torch
     import qma_cuda as Q
     Q.init(local)
+    EP_T = args.tokens
     dev = torch.device("cuda", local)
     e0, n_local = Q.ep_shard(rank, world)
     layers = [ep_layer_weights(il, e0, n_local, dev) for il in range(EP_LAYERS)]
@@ -1353,6 +1354,7 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "moe", "ep", "gdn", "batch",
                                                              "prefill"])
     ap.add_argument("--no-parity", action="store_true", help="batch: skip the in-run parity check")
+    ap.add_argument("--tokens", type=int, default=EP_T, help="ep: tokens per GPU per step (1..256)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ep", action="store_true", help="decode: skip the expert-parallel leg")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the configs[1] GEMV leg")
