@@ -15,7 +15,7 @@ def empty_dev(shape, dtype):
 def assert_close(got, want, rtol, what=""):
     """|got - want| <= rtol * (|want| + mean|want|) element-wise: relative
     error with a floor at the output's mean magnitude, so outputs that cancel
-    to ~0 are judged against the scale of their neighbours."""
+    to ~0 are measured against the scale of their neighbours."""
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
     assert got.shape == want.shape, (got.shape, want.shape)
