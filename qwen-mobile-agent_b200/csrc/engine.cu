@@ -409,12 +409,29 @@ static int salloc_t(qma_cuda_state *s, T **p, size_t count, cudaStream_t st) {
     return rc;
 }
 
-static int grow(float **p, size_t *cap, size_t need) {
+// Attention scratch that grows with the attended context: stream-ordered
+// allocations on the state's stream (no device synchronisation, no host
+// wait: a prefill grows these buffers at almost every chunk, and a
+// synchronous cudaFree / cudaMalloc pair there stalled chunks by up to a
+// second), at least 1.5x the old size so that growth is rare; the device's
+// default pool keeps freed blocks for reuse.
+static int grow(float **p, size_t *cap, cudaStream_t st, size_t need) {
     if (need <= *cap) return QMA_CUDA_OK;
-    if (*p) cudaFree(*p);
+    static PerDevice pool_set;
+    if (!pool_set.done()) {
+        int dev = 0;
+        cudaMemPool_t pool;
+        QMA_CHECK_CUDA(cudaGetDevice(&dev));
+        QMA_CHECK_CUDA(cudaDeviceGetDefaultMemPool(&pool, dev));
+        uint64_t keep = UINT64_MAX;
+        QMA_CHECK_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        pool_set.mark();
+    }
+    const size_t n = std::max(need, *cap + *cap / 2);
+    if (*p) QMA_CHECK_CUDA(cudaFreeAsync(*p, st));
     *p = nullptr;
-    QMA_CHECK_CUDA(cudaMalloc(p, need * sizeof(float)));
-    *cap = need;
+    QMA_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void **>(p), n * sizeof(float), st));
+    *cap = n;
     return QMA_CUDA_OK;
 }
 
@@ -693,10 +710,10 @@ static int ensure_attn_scratch(qma_cuda_state *s, int T, int nk, int pv_chunk) {
         s->graph = nullptr;
     }
     int rc;
-    if ((rc = grow(&s->scores, &s->scores_cap, size_t(T) * NHEAD * nk))) return rc;
-    if ((rc = grow(&s->cmax, &s->cmax_cap, size_t(T) * NHEAD * nsc))) return rc;
-    if ((rc = grow(&s->opart, &s->opart_cap, size_t(T) * NHEAD * npv * HEAD_DIM))) return rc;
-    if ((rc = grow(&s->lpart, &s->lpart_cap, size_t(T) * NHEAD * npv))) return rc;
+    if ((rc = grow(&s->scores, &s->scores_cap, s->st, size_t(T) * NHEAD * nk))) return rc;
+    if ((rc = grow(&s->cmax, &s->cmax_cap, s->st, size_t(T) * NHEAD * nsc))) return rc;
+    if ((rc = grow(&s->opart, &s->opart_cap, s->st, size_t(T) * NHEAD * npv * HEAD_DIM))) return rc;
+    if ((rc = grow(&s->lpart, &s->lpart_cap, s->st, size_t(T) * NHEAD * npv))) return rc;
     return QMA_CUDA_OK;
 }
 
@@ -1339,7 +1356,8 @@ int qma_cuda_state_free(qma_cuda_state *s) {
     cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     for (void *p : s->allocs) cudaFree(p);
-    for (float *p : {s->scores, s->cmax, s->opart, s->lpart}) if (p) cudaFree(p);
+    for (float *p : {s->scores, s->cmax, s->opart, s->lpart}) if (p) cudaFreeAsync(p, s->st);
+    cudaStreamSynchronize(s->st);
     if (s->sp_host) cudaFreeHost(s->sp_host);
     for (float *p : {s->h_sal, s->h_qf, s->h_pin_sal}) if (p) cudaFreeHost(p);
     cudaStreamSynchronize(s->side);
