@@ -999,6 +999,12 @@ static int eval(qma_cuda_state *s, const int *tokens, int n_tokens, float *logit
         s->allocs.push_back(p);
         s->logits = static_cast<float *>(p);
         s->logits_rows = MAX_CHUNK;
+        if (s->graph) {
+            // a captured decode step writes the old logits buffer
+            QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+            cudaGraphExecDestroy(s->graph);
+            s->graph = nullptr;
+        }
     }
     int done = 0, rc;
     while (done < n_tokens) {

@@ -288,6 +288,34 @@ def test_single_token_eval_replays_the_decode_graph(full):
         b.close()
 
 
+def test_single_token_eval_after_logits_all(full):
+    """A logits-for-every-token evaluation enlarges the state's logits
+    buffer; single-token evaluations after it (decode graph replays) must
+    return the new step's logits, as eager launches compute them."""
+    rng = np.random.default_rng(23)
+    prompt = rng.integers(0, O.N_VOCAB, 40).astype(np.int32)
+    a = Q.State(full["model"], N_CTX)
+    b = Q.State(full["model"], N_CTX)
+    try:
+        la, lb = a.eval(prompt[:30]), b.eval(prompt[:30])
+        la = a.eval(np.array([int(np.argmax(la))], np.int32))    # captures a decode graph
+        lb = b.eval(np.array([int(np.argmax(lb))], np.int32))
+        all_a = a.eval(prompt[30:], logits_all=True)
+        all_b = b.eval(prompt[30:], logits_all=True)
+        assert np.array_equal(all_a.view(np.uint32), all_b.view(np.uint32))
+        tok = np.array([int(np.argmax(all_a[-1]))], np.int32)
+        la = a.eval(tok)
+        os.environ["QMA_CUDA_EAGER"] = "1"
+        try:
+            lb = b.eval(tok)
+        finally:
+            del os.environ["QMA_CUDA_EAGER"]
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    finally:
+        a.close()
+        b.close()
+
+
 def test_model_load_gguf_reads_the_file(full, tmp_path):
     """qma_cuda_model_load_gguf on a GGUF file of the full layout (a sparse
     file: token_embd's bytes written, every other tensor zero) yields the
