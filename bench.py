@@ -1250,7 +1250,7 @@ def run_gdn_ours(args, world, rank, local):
                                "then a 4096-token prefill in chunks of 512 (gated-delta chunks of 64)",
                    "per_step": "1024 single-token steps queued back to back by qma_cuda_gdn_decode (per "
                                "step: norm, in-projection + conv, recurrence + gated norm, ssm_out + "
-                               "residual, on the caller's rows), device time / 1024",
+                               "residual, and two 8 KB device copies), device time / 1024",
                    "base_metric": BASE_METRIC},
         "prefill": {"tokens": 4096, "ms": round(pre_ms, 3), "tok_per_s": round(4096 / (pre_ms / 1e3), 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -1092,19 +1092,18 @@ static int gdn_decode_call(qma_cuda_state *s, int il, const float *x, int n_toke
     }
     int rc;
     bool side_pending = false;
-    // the mixer reads its residual input from s->x and writes s->x2: point
-    // them at the caller's rows of this step instead of copying (restored on
-    // every return), so the steps' kernels follow each other directly
-    struct Rows {
-        qma_cuda_state *s;
-        float *x, *x2;
-        ~Rows() { s->x = x; s->x2 = x2; }
-    } keep{s, s->x, s->x2};
     for (int t = 0; t < n_tokens; t++) {
-        s->x = const_cast<float *>(x) + size_t(t) * EMBD;
-        s->x2 = out + size_t(t) * EMBD;
+        // the copies also order the steps: the gated-delta kernel and the
+        // in-projection's conv epilogue read the layer's recurrent and conv
+        // state before their upstream wait, which is safe only once the
+        // previous step's writers have finished; a copy in the stream ends
+        // the chain of early-launched kernels between two steps
+        QMA_CHECK_CUDA(cudaMemcpyAsync(s->x, x + size_t(t) * EMBD, sizeof(float) * EMBD, cudaMemcpyDeviceToDevice,
+                                       st));
         if ((rc = launch_rmsnorm_quant(s->x, m->L[il].attn_norm, 1, EMBD, s->xq, s->xd, s->xs, st))) return rc;
         if ((rc = mixer(s, il, 1, 1, attn_span(1, 1), side_pending))) return rc;
+        QMA_CHECK_CUDA(cudaMemcpyAsync(out + size_t(t) * EMBD, s->x2, sizeof(float) * EMBD,
+                                       cudaMemcpyDeviceToDevice, st));
     }
     QMA_CHECK_CUDA(cudaStreamSynchronize(st));
     s->n_pos += n_tokens;
