@@ -117,3 +117,33 @@ def test_gdn_layer_and_state_bit_exact(layer0, ref_lib, rng):
     finally:
         L.qo_state_free(os_)
         ref_lib.qr_state_free(rs)
+
+
+def test_zero_router_bias_is_the_unbiased_block(layer0, rng):
+    """The biased oracle block (configs[4]'s router prior: one fp32 addition
+    per logit, then the reference's selection) with a zero bias is the
+    unbiased block bit for bit: the block whose moe_ffn is pinned to the
+    reference above."""
+    om, _, _ = layer0
+    T = 3
+    x = rng.standard_normal((T, 2048)).astype(np.float32)
+    o1, o2 = np.zeros((T, 2048), np.float32), np.zeros((T, 2048), np.float32)
+    s1, s2 = np.zeros((T, 8), np.int32), np.zeros((T, 8), np.int32)
+    zero = np.zeros(256, np.float32)
+    O.lib().qo_moe_block_biased(om, 0, p(x), T, p(zero), p(o1), p(s1), None)
+    O.lib().qo_moe_block(om, 0, p(x), T, p(o2), p(s2), None)
+    assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+    assert np.array_equal(s1, s2)
+
+
+def test_zipf_router_prior():
+    """log p(rank) of a Zipf(1.1) law over a seeded per-layer ranking: a
+    permutation of the same 256 log-probabilities in every layer, summing
+    (as probabilities) to one, reproducible from the seed."""
+    a, b = O.zipf_router_bias(7, 0), O.zipf_router_bias(7, 1)
+    assert a.dtype == np.float32 and a.shape == (256,)
+    assert np.array_equal(a, O.zipf_router_bias(7, 0))
+    assert not np.array_equal(a, b) and np.array_equal(np.sort(a), np.sort(b))
+    assert abs(np.exp(a.astype(np.float64)).sum() - 1.0) < 1e-5
+    r = np.arange(1, 257, dtype=np.float64) ** -1.1
+    assert np.allclose(np.sort(a)[::-1], np.log(r / r.sum()), atol=1e-6)
