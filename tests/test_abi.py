@@ -1,6 +1,9 @@
 """The C-ABI library loads on a CPU-only machine, exports every function the
 header declares, and rejects bad arguments with a status (no GPU needed)."""
 import ctypes as C
+import os
+
+import pytest
 
 import qma_cuda as Q
 
@@ -153,3 +156,60 @@ def test_batch_entry_points_reject_bad_arguments():
     assert lib.qma_cuda_batch_logits(None) is None
     assert lib.qma_cuda_batch_free(None) == Q.OK
     assert lib.qma_cuda_model_set_router_bias(None, 0, None) == Q.ERR_INVALID
+
+
+C_CALLER = r"""
+/* A C99 caller of the engine, as qma's nn.c would bind it: every entry
+ * point is called once with arguments the library refuses before touching
+ * a device (null handles, bad sizes), so the program runs without a GPU. */
+#include <stdio.h>
+#include <string.h>
+#include "qma_cuda.h"
+
+int main(void)
+{
+    int bad = 0;
+    qma_cuda_model *m = NULL;
+    qma_cuda_state *s = NULL;
+    qma_cuda_batch *b = NULL;
+    qma_cuda_ep *ep = NULL;
+    qma_cuda_moe_weights w;
+    int ids[1] = {0}, toks[1] = {0}, greedy[1];
+    memset(&w, 0, sizeof w);
+    if (qma_cuda_abi_version() != QMA_CUDA_ABI_VERSION) bad |= 1;
+    if (qma_cuda_state_create(NULL, 4096, &s) != QMA_CUDA_ERR_INVALID) bad |= 2;
+    if (qma_cuda_eval(NULL, NULL, toks, 1, NULL, 0) != QMA_CUDA_ERR_INVALID) bad |= 4;
+    if (qma_cuda_batch_create(NULL, 4, 4096, &b) != QMA_CUDA_ERR_INVALID) bad |= 8;
+    if (qma_cuda_batch_eval(NULL, ids, toks, 1, NULL, greedy) != QMA_CUDA_ERR_INVALID) bad |= 16;
+    if (strlen(qma_cuda_last_error()) == 0) bad |= 1024;     /* the refusal says why */
+    if (qma_cuda_moe_layer(&w, NULL, 1, NULL, NULL, NULL, NULL, 0, NULL) != QMA_CUDA_ERR_INVALID) bad |= 32;
+    if (qma_cuda_ep_moe_layer(ep, &w, NULL, 1, NULL, NULL, NULL, NULL) != QMA_CUDA_ERR_INVALID) bad |= 64;
+    if (qma_cuda_gdn_step(NULL, 0, NULL, 1, NULL, 1) != QMA_CUDA_ERR_INVALID) bad |= 128;
+    if (qma_cuda_ecache_get(m, 0, 0, NULL, NULL, NULL) == QMA_CUDA_OK) bad |= 256;
+    if (qma_cuda_model_free(NULL) != QMA_CUDA_OK) bad |= 512;
+    printf("%d\n", bad);
+    return bad != 0;
+}
+"""
+
+
+def test_header_is_c99_and_links(tmp_path):
+    """include/qma_cuda.h compiles as strict C99 (the reference's language)
+    and a C program calling the entry points links against libqma_cuda.so
+    and runs (argument checks only, no device needed)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(Q.LIB_PATH)
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", str(src),
+                        "-I", os.path.join(root, "include"), "-L", libdir, "-lqma_cuda",
+                        "-Wl,-rpath," + libdir, "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "0", (r.stdout, r.stderr)
