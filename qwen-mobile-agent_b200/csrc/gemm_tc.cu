@@ -12,12 +12,15 @@
 // (sub-block, digit), accumulating H = sum hi x and L = sum lo x over the
 // super-block in int32 (exact), I1 = 32 H + L.
 //
-// CTA (416 threads) = 128 rows x 128 tokens (N = 64 MMAs when the tile
-// holds at most 64), the super-blocks in order as a three-stage pipeline
-// over two buffers of every operand:
-//   warps 0-3 (producers, thread = row): the super-block's Q4_K block ->
-//     nibbles x scale -> two digit tiles (canonical K-major A), and the
-//     tokens' Q8_K slice (B), their 32-lane sums and scales;
+// CTA (416 threads) = 128 rows x tn tokens, tn = 128, 64 or 32 chosen per
+// launch (the narrowest that keeps the grid within one wave of CTAs, so a
+// projection with few row tiles still spreads over the SMs; N = 32 / 64
+// MMAs when the tile holds at most that many tokens), the super-blocks in
+// order as a three-stage pipeline over two buffers of every operand:
+//   warps 0-3 (producers, thread = row): the tokens' Q8_K slice (B, by
+//     16-byte asynchronous copies, in flight while the rest is formed),
+//     their 32-lane sums and scales, and the super-block's Q4_K block ->
+//     nibbles x scale -> two digit tiles (canonical K-major A);
 //   warp 4, one lane: the 16 MMAs of the super-block into one of two TMEM
 //     buffers (2 x 256 columns), then a commit;
 //   warps 5-12 (epilogue, thread = row of its TMEM lane quarter, half of
@@ -74,9 +77,11 @@ __device__ __forceinline__ void gt_scales(uint32_t w0, uint32_t w1, uint32_t w2,
     }
 }
 
-// Grid (ceil(n_out / 128), ceil(T / 128)).
+// Grid (ceil(n_out / 128), ceil(T / tn)), tn in {32, 64, 128}.  One CTA per
+// SM, 128 registers a thread (13 warps, allocated as 16, fill the register
+// file).
 __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_t *__restrict__ W, int n_in,
-                                                                   int n_out, int T,
+                                                                   int n_out, int T, int tn,
                                                                    const int8_t *__restrict__ xq,
                                                                    const float *__restrict__ xd,
                                                                    const int16_t *__restrict__ xsum, float *out,
@@ -87,7 +92,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     __shared__ __align__(8) uint64_t bar_a[2], bar_mma[2], bar_epi[2];
     __shared__ uint32_t tmem_base;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int r0 = blockIdx.x * GTM, t0 = blockIdx.y * GTN;
+    const int r0 = blockIdx.x * GTM, t0 = blockIdx.y * tn;
     const int nsb = n_in / 256;
     const size_t RB = size_t(nsb) * Q4K_BYTES;
     pdl_trigger();
@@ -127,6 +132,27 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
                 gt_wait(&bar_mma[buf], uint32_t(((sb - 2) >> 1) & 1));
                 gt_wait(&bar_epi[buf], uint32_t(((sb - 2) >> 1) & 1));
             }
+            // B: token m of the tile (the first tn producers take one token
+            // each): its 256 Q8_K values by asynchronous copies straight into
+            // the canonical layout (zeros past T), its sums and scale into
+            // registers, all in flight while the weight digits are formed
+            const int t = t0 + m;
+            const bool tb = m < tn, tv = tb && t < T;
+            int4 bu = make_int4(0, 0, 0, 0), bw = make_int4(0, 0, 0, 0);
+            float xs = 0.0f;
+            if (tb) {
+                const int8_t *src = xq + size_t(tv ? t : 0) * n_in + sb * 256;
+#pragma unroll
+                for (int c = 0; c < 16; c++)
+                    cp_async16(&S.b[buf][c >> 1][tc_off(m, 16 * (c & 1))], src + 16 * c, tv);
+                if (tv) {
+                    const int4 *bs = reinterpret_cast<const int4 *>(xsum + size_t(t) * (n_in / 16) + sb * 16);
+                    bu = __ldg(bs);
+                    bw = __ldg(bs + 1);
+                    xs = xd[size_t(t) * nsb + sb];
+                }
+            }
+            cp_async_commit();
             int sc[8], mn[8];
             gt_scales(cur[0].y, cur[0].z, cur[0].w, sc, mn);
 #pragma unroll
@@ -149,34 +175,21 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
                     }
                 }
             }
-            // B: token m of the tile (the 128 producers take one token each)
-            {
-                const int t = t0 + m;
-                const bool tv = t < T;
-                const int4 *src = reinterpret_cast<const int4 *>(xq + size_t(tv ? t : 0) * n_in + sb * 256);
-#pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    const int4 v = tv ? __ldg(src + c) : make_int4(0, 0, 0, 0);
-                    *reinterpret_cast<int4 *>(&S.b[buf][c >> 1][tc_off(m, 16 * (c & 1))]) = v;
-                }
+            if (tb) {
                 // the token's sixteen 16-lane sums -> eight 32-lane sums, one store
-                int4 bv = make_int4(0, 0, 0, 0);
-                if (tv) {
-                    const int4 *bs = reinterpret_cast<const int4 *>(xsum + size_t(t) * (n_in / 16) + sb * 16);
-                    const int4 u = __ldg(bs), v = __ldg(bs + 1);
-                    const int w[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
-                    uint32_t pk[4];
+                const int w[8] = {bu.x, bu.y, bu.z, bu.w, bw.x, bw.y, bw.z, bw.w};
+                uint32_t pk[4];
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int s0 = int(int16_t(w[2 * i] & 0xffff)) + (w[2 * i] >> 16);
-                        const int s1 = int(int16_t(w[2 * i + 1] & 0xffff)) + (w[2 * i + 1] >> 16);
-                        pk[i] = (uint32_t(s0) & 0xffffu) | (uint32_t(s1) << 16);
-                    }
-                    bv = make_int4(int(pk[0]), int(pk[1]), int(pk[2]), int(pk[3]));
+                for (int i = 0; i < 4; i++) {
+                    const int s0 = int(int16_t(w[2 * i] & 0xffff)) + (w[2 * i] >> 16);
+                    const int s1 = int(int16_t(w[2 * i + 1] & 0xffff)) + (w[2 * i + 1] >> 16);
+                    pk[i] = (uint32_t(s0) & 0xffffu) | (uint32_t(s1) << 16);
                 }
-                *reinterpret_cast<int4 *>(&S.bsum[buf][m][0]) = bv;
-                S.xd[buf][m] = tv ? xd[size_t(t) * nsb + sb] : 0.0f;
+                *reinterpret_cast<int4 *>(&S.bsum[buf][m][0]) =
+                    make_int4(int(pk[0]), int(pk[1]), int(pk[2]), int(pk[3]));
+                S.xd[buf][m] = xs;
             }
+            cp_async_wait<0>();
             fence_async_smem();
             mbar_arrive(&bar_a[buf]);
             if (sb + 1 < nsb) {
@@ -187,8 +200,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
     } else if (warp == 4) {
         // ---- MMA issue --------------------------------------------------------------
         if (lane == 0) {
-            // a tile of at most 64 tokens: N = 64 (the B rows past 64 are not read)
-            const uint32_t idesc = T - t0 <= GTN / 2 ? tc_idesc_s8(GTM, GTN / 2) : tc_idesc_s8(GTM, GTN);
+            // N = the narrowest of 32 / 64 / 128 that covers the tile's tokens
+            // (B rows past N are not read)
+            const int nt = min(T - t0, tn);
+            const uint32_t idesc = tc_idesc_s8(GTM, nt <= 32 ? 32 : nt <= 64 ? 64 : GTN);
             for (int sb = 0; sb < nsb; sb++) {
                 const int buf = sb & 1;
                 gt_wait(&bar_a[buf], uint32_t((sb >> 1) & 1));
@@ -211,7 +226,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemm_q4k_tc_kernel(const uint8_
         // the tile's tokens split evenly over the two halves of the epilogue
         // warps, in multiples of 16 (a tile of 64 tokens: 32 each)
         constexpr int NH = GTN / 2;
-        const int ntile = min(T - t0, GTN), half = ((ntile + 31) / 32) * 16;
+        const int ntile = min(T - t0, tn), half = ((ntile + 31) / 32) * 16;
         const int n0 = ((warp - 5) >> 2) * half, cnt = max(0, min(half, ntile - n0));
         const int q4 = warp & 3, m = 32 * q4 + lane, r = r0 + m;
         const bool live = r < n_out;
@@ -279,9 +294,18 @@ int launch_gemm_q4k_tc(const uint8_t *W, int n_in, int n_out, int T, const int8_
                                             int(GEMM_TC_SMEM)));
         attr.mark();
     }
-    const dim3 grid(unsigned((n_out + GTM - 1) / GTM), unsigned((T + GTN - 1) / GTN));
+    // token tile: the narrowest of 32 / 64 whose grid still fits one wave
+    // (one CTA per SM), else 128
+    const int rt = (n_out + GTM - 1) / GTM;
+    int tn = GTN;
+    for (const int c : {32, 64})
+        if (rt * ((T + c - 1) / c) <= num_sms()) {
+            tn = c;
+            break;
+        }
+    const dim3 grid(unsigned(rt), unsigned((T + tn - 1) / tn));
     QMA_CHECK_CUDA(launch_ex(gemm_q4k_tc_kernel, grid, dim3(GT_THREADS), GEMM_TC_SMEM, st, 1, pdl_enabled(), W, n_in,
-                             n_out, T, xq, xd, xsum, out, resid));
+                             n_out, T, tn, xq, xd, xsum, out, resid));
     return QMA_CUDA_OK;
 }
 
