@@ -305,8 +305,13 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     for (int t = 0; t < T; t++) {
         const int buf = t & 1;
         const float *co = conv_out + size_t(t) * CONV_DIM;
-        // q (threads 0..127) and k (128..255) with their L2 norms
+        // the token's inputs in one round trip: the q (threads 0..127) or k
+        // (128..255) lane, the head's beta / alpha logits, and v_j
         const float val = tid < SSTATE ? co[qh * SSTATE + tid] : co[KEY_DIM + qh * SSTATE + tid - SSTATE];
+        const float braw = proj[size_t(t) * proj_ld + beta_off + h];
+        const float araw = proj[size_t(t) * proj_ld + alpha_off + h];
+        const float vj = co[2 * KEY_DIM + h * SSTATE + j];
+        // q and k with their L2 norms
         double sq = double(val) * double(val);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
@@ -325,9 +330,8 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
             kq = warp_sum(kq);
             if (lane == 0) kqred[buf][warp] = kq;
         }
-        const float braw = proj[size_t(t) * proj_ld + beta_off + h];
         const float b = 1.0f / (1.0f + expf(-braw));
-        const float a = proj[size_t(t) * proj_ld + alpha_off + h] + dth;
+        const float a = araw + dth;
         const float sp = a > 20.0f ? a : log1pf(expf(a));
         const float g = __fmul_rn(sp, ah);
         const float expg = expf(g);
@@ -344,7 +348,6 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
         }
         __syncthreads();
         const float kq = (kqred[buf][0] + kqred[buf][1]) + (kqred[buf][2] + kqred[buf][3]);
-        const float vj = co[2 * KEY_DIM + h * SSTATE + j];
         const float delta = __fmul_rn(__fsub_rn(vj, __fmul_rn(expg, dk)), b);
 #pragma unroll
         for (int i = 0; i < 16; i++)
