@@ -561,6 +561,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float *__restric
     }
     pdl_trigger();
     pdl_wait();
+    // the query heads of this KV head (the upstream output), issued before
+    // the late records so that both are in flight together: qt = dim tid of
+    // head k, qv = dims lane + 32 k of head `warp`
+    float qt[8], qv[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        qt[k] = qr[(size_t(kh) * 8) * HEAD_DIM + tid + HEAD_DIM * k];
+        qv[k] = qr[(size_t(kh) * 8 + warp) * HEAD_DIM + lane + 32 * k];
+    }
     __syncthreads();
     for (int idx = tid; idx < bn * 10; idx += 256) {
         const int i = idx / 10, wq = idx % 10;
@@ -575,18 +584,12 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float *__restric
     }
     __syncthreads();
     if (tid < bn) S.isq2[tid] &= 1;
-    for (int i = tid; i < 8 * HEAD_DIM; i += 256) {
-        const int h = i / HEAD_DIM, e = i % HEAD_DIM;
-        S.qT[qrow(e)][h] = qr[(size_t(kh) * 8) * HEAD_DIM + i];
-    }
-    {   // warp h: sub-block sums of query head h
-        const float *q = qr + (size_t(kh) * 8 + warp) * HEAD_DIM;
-        float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) v[k] = q[lane + 32 * k];
+    for (int k = 0; k < 8; k++) S.qT[qrow(tid)][k] = qt[k];
+    {   // warp h: sub-block sums of query head h
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const float x4 = warp_sum(v[k]);
+            const float x4 = warp_sum(qv[k]);
             if (lane == 0) S.X4[warp][k] = x4;
         }
         __syncwarp();
@@ -760,13 +763,18 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float *__restri
     }
     __shared__ float wred[8], wsum[8];
     __shared__ __align__(16) float y[HEAD_DIM];
-    pdl_trigger();
-    pdl_wait();
-    const StepParams sp = *spp;
+    const StepParams sp = *spp;                  // written before this step began
     const int nc = (nk_of(sp, t) + span - 1) / span;
     const size_t base = (size_t(t) * NHEAD + h) * nchunk;
-    float m = -INFINITY;
-    for (int c = tid; c < nc; c += 256) m = fmaxf(m, mpart[base + c]);
+    pdl_trigger();
+    pdl_wait();
+    // one round trip for the gate lane and the first chunk's maximum and sum
+    // of this thread (chunks past 256 are read in the loops)
+    const float g = z[size_t(t) * WO_DIM + h * HEAD_DIM + tid];
+    const float m0 = tid < nc ? mpart[base + tid] : -INFINITY;
+    const float l0 = tid < nc ? lpart[base + tid] : 0.0f;
+    float m = m0;
+    for (int c = tid + 256; c < nc; c += 256) m = fmaxf(m, mpart[base + c]);
     m = warp_max(m);
     if (lane == 0) wred[warp] = m;
     __syncthreads();
@@ -775,9 +783,9 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float *__restri
     for (int w = 1; w < 8; w++) m = fmaxf(m, wred[w]);
     float l = 0.0f;
     for (int c = tid; c < nc; c += 256) {
-        const float f = expf(mpart[base + c] - m);
+        const float f = expf((c == tid ? m0 : mpart[base + c]) - m);
         fsh[c] = f;
-        l = __fadd_rn(l, __fmul_rn(f, lpart[base + c]));
+        l = __fadd_rn(l, __fmul_rn(f, c == tid ? l0 : lpart[base + c]));
     }
     l = warp_sum(l);
     if (lane == 0) wsum[warp] = l;
@@ -791,7 +799,6 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float *__restri
     float o = 0.0f;
     for (int c = 0; c < nc; c++) o = __fadd_rn(o, __fmul_rn(fsh[c], op[size_t(c) * HEAD_DIM]));
     o = __fmul_rn(o, 1.0f / l);
-    const float g = z[size_t(t) * WO_DIM + h * HEAD_DIM + tid];
     y[tid] = __fmul_rn(o, 1.0f / (1.0f + expf(-g)));
     __syncthreads();
     if (warp == 0) {

@@ -301,7 +301,12 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     }
     const float scale = 1.0f / sqrtf(float(SSTATE));
     const float dth = dt[h], ah = av[h];
+    // the gated norm's weight and gate lane for this thread, should this CTA
+    // be its head pair's last (one token): read with the other inputs
+    const int pair = h >> 1, hh = pair * 2 + (tid >> 7), hi = tid & (SSTATE - 1);
+    const float gw = gn.cnt ? __ldg(gn.w + hi) : 0.0f;
     pdl_wait();
+    const float gz = gn.cnt ? gn.z[hh * SSTATE + hi] : 0.0f;
     for (int t = 0; t < T; t++) {
         const int buf = t & 1;
         const float *co = conv_out + size_t(t) * CONV_DIM;
@@ -366,7 +371,6 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     __shared__ int is_last;
     __shared__ double hss[8];
     __shared__ float hmax[8];
-    const int pair = h >> 1;
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -375,7 +379,7 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    const int hh = pair * 2 + (tid >> 7), i = tid & (SSTATE - 1);   // thread = lane of the block
+    const int i = hi;                   // thread = lane hh * 128 + i of the pair's block
     const float v = __ldcg(o + hh * SSTATE + i);
     const double sq = warp_sum_d(double(v) * double(v));
     if (lane == 0) hss[warp] = sq;
@@ -383,8 +387,8 @@ __global__ void __launch_bounds__(256) gdn_kernel(const float *__restrict__ conv
     const int w0 = (tid >> 7) * 4;
     const double tot = (hss[w0] + hss[w0 + 1]) + (hss[w0 + 2] + hss[w0 + 3]);
     const float r = 1.0f / sqrtf(float(tot / SSTATE) + 1e-6f);
-    const float zz = gn.z[hh * SSTATE + i];
-    const float normed = __fmul_rn(v, __fmul_rn(r, gn.w[i]));
+    const float zz = gz;
+    const float normed = __fmul_rn(v, __fmul_rn(r, gw));
     const float y = __fmul_rn(normed, zz / (1.0f + expf(-zz)));
     const float am = warp_max(fabsf(y));
     if (lane == 0) hmax[warp] = am;

@@ -394,13 +394,19 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
         gisv[0] = g0.x; gisv[1] = g0.y; gisv[2] = g0.z; gisv[3] = g0.w;
         gisv[4] = g1.x; gisv[5] = g1.y; gisv[6] = g1.z; gisv[7] = g1.w;
     }
+    // the norm weights and this warp's router bias: constants, read before
+    // the wait too
+    constexpr int XPT = MOE_EMBD / RTHREADS;
+    float pn[XPT];
+#pragma unroll
+    for (int k = 0; k < XPT; k++) pn[k] = __ldg(post_norm + tid + RTHREADS * k);
+    const float bias_e = bias ? __ldg(bias + e0) : 0.0f;
     QMA_TRACE_MARK(TK_ROUTER, 1);
     pdl_trigger();
     pdl_wait();
     QMA_TRACE_MARK(TK_ROUTER, 2);
     // ---- xn = rms_norm(x2) * post_norm ------------------------------------
     const float *x = x2 + size_t(t) * MOE_EMBD;
-    constexpr int XPT = MOE_EMBD / RTHREADS;
     float xv[XPT];
     double ss = 0.0;
 #pragma unroll
@@ -418,7 +424,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
 #pragma unroll
     for (int k = 0; k < XPT; k++) {
         const int i = tid + RTHREADS * k;
-        xn[xn_idx(i)] = __fmul_rn(__fmul_rn(xv[k], r), post_norm[i]);
+        xn[xn_idx(i)] = __fmul_rn(__fmul_rn(xv[k], r), pn[k]);
     }
     __syncthreads();
     QMA_TRACE_MARK(TK_ROUTER, 3);
@@ -432,7 +438,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_kernel(const float *__
     {
         double S0, B0;
         router_logit(rrows + size_t(warp) * MOE_EMBD, xn, lane, S0, B0);
-        if (bias) bias_interval(S0, B0, __ldg(bias + e0));
+        if (bias) bias_interval(S0, B0, bias_e);
         if (lane == 0) {
             st_cluster_f64(cluster_map(&sS[e0], 0), S0);
             st_cluster_f64(cluster_map(&sB[e0], 0), B0);
@@ -602,10 +608,16 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_multi_kernel(const flo
         gisv[0] = g0.x; gisv[1] = g0.y; gisv[2] = g0.z; gisv[3] = g0.w;
         gisv[4] = g1.x; gisv[5] = g1.y; gisv[6] = g1.z; gisv[7] = g1.w;
     }
+    // the norm weights and this warp's router bias: constants, read before
+    // the wait too
+    constexpr int XPT = MOE_EMBD / RTHREADS;
+    float pn[XPT];
+#pragma unroll
+    for (int k = 0; k < XPT; k++) pn[k] = __ldg(post_norm + tid + RTHREADS * k);
+    const float bias_e = bias ? __ldg(bias + e0) : 0.0f;
     pdl_trigger();
     pdl_wait();
     // ---- xn of each token (rms_norm_m, nn.c:348-357) ---------------------------
-    constexpr int XPT = MOE_EMBD / RTHREADS;
     float xv[RTPC][XPT];
 #pragma unroll
     for (int u = 0; u < RTPC; u++) {
@@ -628,7 +640,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_multi_kernel(const flo
 #pragma unroll
         for (int k = 0; k < XPT; k++) {
             const int i = tid + RTHREADS * k;
-            R.xn[u][i] = __fmul_rn(__fmul_rn(xv[u][k], r), post_norm[i]);
+            R.xn[u][i] = __fmul_rn(__fmul_rn(xv[u][k], r), pn[k]);
         }
     }
     __syncthreads();
@@ -641,7 +653,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) moe_router_multi_kernel(const flo
     for (int u = 0; u < nt; u++) {
         double S0, B0;
         router_logit(&R.rows[warp][0], R.xn[u], lane, S0, B0);
-        if (bias) bias_interval(S0, B0, __ldg(bias + e0));
+        if (bias) bias_interval(S0, B0, bias_e);
         if (lane == 0) {
             st_cluster_f64(cluster_map(&R.S[u][e0], 0), S0);
             st_cluster_f64(cluster_map(&R.B[u][e0], 0), B0);
