@@ -105,6 +105,8 @@ struct qma_cuda_state {
     std::vector<int> pin_pos;
     int live_n = 0, n4 = 0, n_ring_q4 = 0, rebuilt_at = 0, next_rebuild = HCM_REBUILD_INIT;
     float *h_sal = nullptr, *h_qf = nullptr, *h_pin_sal = nullptr;   // pinned, the rebuild's reads
+    int *h_tok = nullptr;               // pinned, a greedy decode's tokens (h_tok_cap of them)
+    int h_tok_cap = 0;
     // decode graph
     cudaGraphExec_t graph = nullptr;
     int graph_nk = -1;
@@ -1167,6 +1169,18 @@ static int decode_greedy(qma_cuda_state *s, int token, int n_steps, int *tokens_
         set_error("decode: %d + %d positions exceed this state's ring of %d", s->n_pos, n_steps, s->n_ctx);
         return QMA_CUDA_ERR_UNSUPPORTED;
     }
+    // the tokens land in pinned memory (an asynchronous copy per step, so the
+    // host runs ahead of the device instead of waiting on every step) and
+    // reach tokens_out after the last step
+    if (tokens_out && n_steps > s->h_tok_cap) {
+        const int cap = std::max(n_steps, std::max(1024, 2 * s->h_tok_cap));
+        QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+        if (s->h_tok) QMA_CHECK_CUDA(cudaFreeHost(s->h_tok));
+        s->h_tok = nullptr;
+        s->h_tok_cap = 0;
+        QMA_CHECK_CUDA(cudaMallocHost(&s->h_tok, sizeof(int) * size_t(cap)));
+        s->h_tok_cap = cap;
+    }
     int rc;
     int cur = token;
     for (int i = 0; i < n_steps; i++) {
@@ -1189,9 +1203,9 @@ static int decode_greedy(qma_cuda_state *s, int token, int n_steps, int *tokens_
         s->tier[hcm_slot(pos, s->n_ctx)] = 2;
         QMA_CHECK_CUDA(cudaGraphLaunch(s->graph, st));
         if (tokens_out) {
-            if (i == 0) tokens_out[0] = cur;
+            if (i == 0) s->h_tok[0] = cur;
             if (i + 1 < n_steps)
-                QMA_CHECK_CUDA(cudaMemcpyAsync(tokens_out + i + 1, s->argmax_dev, sizeof(int),
+                QMA_CHECK_CUDA(cudaMemcpyAsync(s->h_tok + i + 1, s->argmax_dev, sizeof(int),
                                                cudaMemcpyDeviceToHost, st));
         }
         s->n_pos += 1;
@@ -1200,6 +1214,7 @@ static int decode_greedy(qma_cuda_state *s, int token, int n_steps, int *tokens_
         QMA_CHECK_CUDA(cudaMemcpyAsync(logits, s->logits, sizeof(float) * m->n_vocab,
                                        cudaMemcpyDeviceToHost, st));
     QMA_CHECK_CUDA(cudaStreamSynchronize(st));
+    if (tokens_out) memcpy(tokens_out, s->h_tok, sizeof(int) * size_t(n_steps));
     return check_wait_timeouts();
 }
 
@@ -1365,6 +1380,7 @@ int qma_cuda_state_free(qma_cuda_state *s) {
     cudaStreamSynchronize(s->st);
     if (s->sp_host) cudaFreeHost(s->sp_host);
     for (float *p : {s->h_sal, s->h_qf, s->h_pin_sal}) if (p) cudaFreeHost(p);
+    if (s->h_tok) cudaFreeHost(s->h_tok);
     cudaStreamSynchronize(s->side);
     cudaEventDestroy(s->ev_fork);
     cudaEventDestroy(s->ev_join);
