@@ -29,50 +29,87 @@ constexpr int GR = 64;          // rows per CTA: 4 warps x 16
 constexpr int NSHARED = MOE_NEXP;   // group index of the shared expert
 
 // 1. ---------------------------------------------------------------- lists --
-// One CTA: thread e counts expert e's pairs, an exclusive scan gives the
-// offsets, then thread e lists its pairs in token order; the experts that
-// have pairs are also listed compactly (goff[257] = their number, then
-// their ids ascending) so that the expert kernels launch no CTA for the
-// others.
+// One CTA over the chunk's T x 8 (token, expert) pairs, one pair per thread
+// at a time: shared-memory atomics count each expert's pairs, an exclusive
+// scan (thread e = expert e) gives the offsets, then the pairs are placed in
+// rounds of 256 in token order -- a pair's rank among the earlier pairs of
+// its expert is the expert's count in earlier rounds, plus its count in the
+// lower warps of this round, plus the pair's rank among the matching lanes
+// of its own warp (__match_any_sync).  The experts that have pairs are also
+// listed compactly (goff[257] = their number, then their ids ascending) so
+// that the expert kernels launch no CTA for the others.  A pair with no
+// expert (-1: the padding of an expert-parallel exchange) is not listed.
 __global__ void __launch_bounds__(256) moe_lists_kernel(const int *__restrict__ sel, int T, int *goff,
                                                         int *plist) {
     __shared__ int ssel[MOE_GROUPED_MAX_T * MOE_TOPK];
-    __shared__ int wsum[8];
+    __shared__ int cnt[MOE_NEXP], run[MOE_NEXP];
+    __shared__ int wc[8][MOE_NEXP];     // this round's count of expert e in warp w
+    __shared__ int wsum[8], wact[8];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    cnt[tid] = 0;
+    run[tid] = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) wc[w][tid] = 0;
     pdl_trigger();
     pdl_wait();
     const int np = T * MOE_TOPK;
-    for (int p = tid; p < np; p += 256) ssel[p] = sel[p];
     __syncthreads();
-    int cnt = 0;
-    for (int p = 0; p < np; p++) cnt += ssel[p] == tid;
+    for (int p = tid; p < np; p += 256) ssel[p] = sel[p];   // loads all in flight
+    __syncthreads();
+    for (int p = tid; p < np; p += 256) {
+        const int e = ssel[p];
+        if (e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    const int c = cnt[tid];
     // exclusive scan of the 256 counts
-    int incl = cnt;
+    int incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
     }
     if (lane == 31) wsum[warp] = incl;
-    __syncthreads();
-    int base = 0;
-    for (int w = 0; w < warp; w++) base += wsum[w];
-    const int off = base + incl - cnt;
-    goff[tid] = off;
-    if (tid == 255) goff[256] = off + cnt;
-    // the active experts, ascending: the rank of e among them
-    __shared__ int wact[8];
-    const unsigned am = __ballot_sync(0xffffffffu, cnt > 0);
+    const unsigned am = __ballot_sync(0xffffffffu, c > 0);
     if (lane == 0) wact[warp] = __popc(am);
     __syncthreads();
-    int abase = 0;
-    for (int w = 0; w < warp; w++) abase += wact[w];
+    int base = 0, abase = 0;
+    for (int w = 0; w < warp; w++) {
+        base += wsum[w];
+        abase += wact[w];
+    }
+    const int off = base + incl - c;
+    goff[tid] = off;
+    if (tid == 255) goff[256] = off + c;
+    // the active experts, ascending: the rank of e among them
     int *act = goff + MOE_NEXP + 1;
-    if (cnt > 0) act[1 + abase + __popc(am & ((1u << lane) - 1u))] = tid;
+    if (c > 0) act[1 + abase + __popc(am & ((1u << lane) - 1u))] = tid;
     if (tid == 255) act[0] = abase + __popc(am);
-    int i = off;
-    for (int p = 0; p < np; p++)
-        if (ssel[p] == tid) plist[i++] = p;
+    cnt[tid] = off;                     // from here on: the offsets
+    __syncthreads();
+    for (int p0 = 0; p0 < np; p0 += 256) {
+        const int p = p0 + tid;
+        const int e = p < np ? ssel[p] : -1;
+        // lanes without an expert match nothing (a key of their own)
+        const unsigned m = __match_any_sync(0xffffffffu, e >= 0 ? e : -1 - lane);
+        const int lr = __popc(m & ((1u << lane) - 1u));
+        if (e >= 0 && lr == 0) wc[warp][e] = __popc(m);
+        __syncthreads();
+        if (e >= 0) {
+            int pre = run[e];
+            for (int w = 0; w < warp; w++) pre += wc[w][e];
+            plist[cnt[e] + pre + lr] = p;
+        }
+        __syncthreads();
+        int add = 0;
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            add += wc[w][tid];
+            wc[w][tid] = 0;
+        }
+        run[tid] += add;
+        __syncthreads();
+    }
 }
 
 // The group of grid row y of an expert kernel: rows below nyr take the
