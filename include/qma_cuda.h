@@ -219,7 +219,9 @@ int qma_cuda_eval(qma_cuda_model *m, qma_cuda_state *s, const int *tokens, int n
  * tokens_out[i] (host, optional) and the last step's logits to logits
  * (host, optional).  Each step is one replay of a captured CUDA graph; the
  * host intervenes only when the HCM live index is rebuilt (every 128
- * positions, nn.c:2074-2088). */
+ * positions, nn.c:2074-2088).  The tokens are staged in pinned memory the
+ * state owns and reach tokens_out when the call returns, so tokens_out may
+ * be ordinary (pageable) memory without making the steps wait on the host. */
 int qma_cuda_decode_greedy(qma_cuda_model *m, qma_cuda_state *s, int token, int n_steps,
                            int *tokens_out, float *logits);
 
