@@ -26,6 +26,41 @@ def assert_close(got, want, rtol, what=""):
     return worst
 
 
+def underflow_router(W):
+    """Rows 1..4 copy row 0 and rows 5..8 hold row 0's values permuted, all
+    scaled up: the aligned input gives experts 0..4 logits ~100 above every
+    other expert, so the reference's expf(l - max) underflows to exactly 0
+    for all the rest and they tie at probability 0 (ranked by expert id)."""
+    rng = np.random.default_rng(3)
+    W[0] *= 6.0
+    for e in range(1, 5):
+        W[e] = W[0]
+    for e in range(5, 9):
+        W[e] = W[0][rng.permutation(2048)]
+
+
+def near_tie_router(W):
+    """Rows 1..4 copy row 0 (exact logit ties, ranked by id); rows 5..8 are
+    row 0 with one weight nudged by a few ulps (logits distinct in fp32 but
+    far inside the summation-error bound), so only the reference-order
+    recompute can rank them."""
+    for e in range(1, 9):
+        W[e] = W[0]
+    for e in range(5, 9):
+        i = 100 + 13 * e
+        v = W[e, i]
+        for _ in range(e - 4):
+            v = np.nextafter(v, np.float32(np.inf) if e % 2 else np.float32(-np.inf))
+        W[e, i] = v
+
+
+def aligned_inputs(W0, T, scale, seed):
+    """T tokens of N(0, 1) noise plus scale * sign(router row 0): inputs whose
+    top experts are the crafted rows."""
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((T, 2048)) + scale * np.sign(W0)[None, :]).astype(np.float32)
+
+
 MOE_TENSORS = ("post_attention_norm.weight", "ffn_gate_inp.weight", "ffn_gate_exps.weight",
                "ffn_up_exps.weight", "ffn_down_exps.weight", "ffn_gate_inp_shexp.weight",
                "ffn_gate_shexp.weight", "ffn_up_shexp.weight", "ffn_down_shexp.weight")

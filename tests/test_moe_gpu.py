@@ -8,7 +8,7 @@ Bars: selected expert ids identical in order for every token; outputs within
 import numpy as np
 import pytest
 
-from helpers import MoeLayer, assert_close
+from helpers import MoeLayer, aligned_inputs, assert_close, near_tie_router, underflow_router
 
 pytestmark = pytest.mark.gpu
 
@@ -50,43 +50,14 @@ def test_moe_repeat_calls_reuse_scratch(layer):
     assert np.array_equal(a, b)
 
 
-def _underflow_router(W):
-    """Rows 1..4 copy row 0 and rows 5..8 hold row 0's values permuted, all
-    scaled up: the aligned input gives experts 0..4 logits ~100 above every
-    other expert, so the reference's expf(l - max) underflows to exactly 0
-    for all the rest and they tie at probability 0 (ranked by expert id)."""
-    rng = np.random.default_rng(3)
-    W[0] *= 6.0
-    for e in range(1, 5):
-        W[e] = W[0]
-    for e in range(5, 9):
-        W[e] = W[0][rng.permutation(2048)]
-
-
-def _near_tie_router(W):
-    """Rows 1..4 copy row 0 (exact logit ties, ranked by id); rows 5..8 are
-    row 0 with one weight nudged by a few ulps (logits distinct in fp32 but
-    far inside the summation-error bound), so only the reference-order
-    recompute can rank them."""
-    for e in range(1, 9):
-        W[e] = W[0]
-    for e in range(5, 9):
-        i = 100 + 13 * e
-        v = W[e, i]
-        for _ in range(e - 4):
-            v = np.nextafter(v, np.float32(np.inf) if e % 2 else np.float32(-np.inf))
-        W[e, i] = v
-
-
 def _aligned_inputs(L, T, scale, seed):
-    rng = np.random.default_rng(seed)
     tr = L.t["ffn_gate_inp.weight"]
     W0 = L.blob[tr.off:tr.off + tr.nbytes].view(np.float32).reshape(256, 2048)[0]
-    return (rng.standard_normal((T, 2048)) + scale * np.sign(W0)[None, :]).astype(np.float32)
+    return aligned_inputs(W0, T, scale, seed)
 
 
 @pytest.mark.parametrize("T", [6, 13], ids=["per_token_router", "multi_token_router"])
-@pytest.mark.parametrize("edit,scale", [(_near_tie_router, 0.3), (_underflow_router, 3.0)],
+@pytest.mark.parametrize("edit,scale", [(near_tie_router, 0.3), (underflow_router, 3.0)],
                          ids=["near_ties", "underflow_ties"])
 def test_moe_exact_fallback_on_ties(cuda, edit, scale, T):
     """T = 6 runs the one-token-per-cluster router, T = 13 the router of 4

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from helpers import aligned_inputs, near_tie_router, underflow_router
 
 
 def p(a):
@@ -117,6 +118,46 @@ def test_gdn_layer_and_state_bit_exact(layer0, ref_lib, rng):
     finally:
         L.qo_state_free(os_)
         ref_lib.qr_state_free(rs)
+
+
+@pytest.mark.parametrize("edit,scale", [(near_tie_router, 0.3), (underflow_router, 3.0)],
+                         ids=["near_ties", "underflow_ties"])
+def test_moe_crafted_router_ties_bit_exact(ref_lib, edit, scale):
+    """Layer 0 with its router rewritten so that logits tie exactly, differ
+    by a few ulps, or leave probabilities that underflow to 0: the oracle's
+    experts and output equal the reference's token by token (one token per
+    call, as the reference reports the last token's experts) and for all
+    tokens in one call.  These are the routers the engine's exact fallback
+    is tested on against the oracle."""
+    arr, n, size = O.synth_layout(embd_type=O.Q6_K, out_type=O.Q6_K)
+    names = {arr[i].name.decode() for i in range(n) if arr[i].name.decode().startswith("blk.0.")}
+    blob = O.synth_blob(arr, n, size, seed=0, names=names)
+    t = next(arr[i] for i in range(n) if arr[i].name.decode() == "blk.0.ffn_gate_inp.weight")
+    W = blob[t.off:t.off + t.nbytes].view(np.float32).reshape(256, 2048)
+    edit(W)                             # in place, in the blob
+    om = O.lib().qo_model_new(arr, n, p(blob), O.N_VOCAB)
+    rm = ref_lib.qr_model_new(arr, n, p(blob), size)
+    assert om and rm
+    try:
+        T = 6
+        x = aligned_inputs(W[0].copy(), T, scale, seed=11)
+        o1, o2 = np.zeros((T, 2048), np.float32), np.zeros((T, 2048), np.float32)
+        sel, w, rsel = np.zeros((T, 8), np.int32), np.zeros((T, 8), np.float32), np.zeros(8, np.int32)
+        for k in range(T):
+            xt = np.ascontiguousarray(x[k:k + 1])
+            O.lib().qo_moe_ffn(om, 0, p(xt), 1, p(o1[k:k + 1]), p(sel[k:k + 1]), p(w[k:k + 1]))
+            ref_lib.qr_moe_ffn(rm, 0, p(xt), 1, p(o2[k:k + 1]), p(rsel))
+            assert np.array_equal(sel[k], rsel), (k, sel[k], rsel)
+        assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+        assert set(range(5)) <= set(sel[:, :5].ravel())      # the crafted rows lead the selection
+        a1, a2 = np.zeros((T, 2048), np.float32), np.zeros((T, 2048), np.float32)
+        O.lib().qo_moe_ffn(om, 0, p(x), T, p(a1), p(sel), p(w))
+        ref_lib.qr_moe_ffn(rm, 0, p(x), T, p(a2), p(rsel))
+        assert np.array_equal(a1.view(np.uint32), a2.view(np.uint32))
+        assert np.array_equal(sel[-1], rsel)
+    finally:
+        O.lib().qo_model_free(om)
+        ref_lib.qr_model_free(rm)
 
 
 def test_zero_router_bias_is_the_unbiased_block(layer0, rng):
