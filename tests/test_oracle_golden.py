@@ -99,3 +99,41 @@ def test_gdn_mixer_and_states_match_the_reference_answers(golden, layer0):
             t0 += T
     finally:
         L.qo_state_free(s)
+
+
+def test_fixture_is_the_references_own_output(golden, ref_lib):
+    """Where the reference is built here, it reproduces the committed answers
+    from the committed inputs (so the fixture is the reference's output, not
+    the restatement's)."""
+    R = ref_lib
+    for t in range(len(golden["q8k_x"])):
+        x = np.ascontiguousarray(golden["q8k_x"][t])
+        xq, xd, xs = np.zeros(4096, np.int8), np.zeros(16, np.float32), np.zeros(256, np.int16)
+        R.qma_q8k_quant(p(x), 4096, p(xq), p(xd), p(xs))
+        assert np.array_equal(xq, golden["q8k_xq"][t]) and np.array_equal(bits(xd), bits(golden["q8k_xd"][t]))
+    arr, n, size = O.synth_layout(embd_type=O.Q6_K, out_type=O.Q6_K)
+    names = {arr[i].name.decode() for i in range(n) if arr[i].name.decode().startswith("blk.0.")}
+    blob = O.synth_blob(arr, n, size, seed=int(golden["blob_seed"]), names=names)
+    rm = R.qr_model_new(arr, n, p(blob), size)
+    assert rm
+    try:
+        x = np.ascontiguousarray(golden["moe_x"])
+        out, sel = np.zeros_like(x), np.zeros(8, np.int32)
+        R.qr_moe_ffn(rm, 0, p(x), x.shape[0], p(out), p(sel))
+        assert np.array_equal(bits(out), bits(golden["moe_out"])) and np.array_equal(sel, golden["moe_sel_last"])
+        rs = R.qr_state_new(256)
+        try:
+            t0 = 0
+            for k, T in enumerate(golden["gdn_calls"]):
+                T = int(T)
+                xg = np.ascontiguousarray(golden["gdn_x"][t0:t0 + T])
+                og = np.zeros_like(xg)
+                R.qr_gdn_layer(rm, rs, 0, p(xg), T, p(og))
+                assert np.array_equal(bits(og), bits(golden["gdn_out"][t0:t0 + T])), k
+                ssm = np.ctypeslib.as_array(R.qr_state_ssm(rs, 0), (32 * 128 * 128,))
+                assert np.array_equal(digest(ssm), golden["gdn_ssm_sha256"][k]), k
+                t0 += T
+        finally:
+            R.qr_state_free(rs)
+    finally:
+        R.qr_model_free(rm)
